@@ -1,0 +1,109 @@
+"""ctypes binding of libdgxm_sp.so (the C ABI declared in include/dgxm_sp.h).
+
+This is the binding a maintainer of the reference would add: plain pointers,
+sizes and a stream handle, int status codes turned into Python exceptions.
+The library must be built (``python -m dgx_monarch_b200._build``); there is
+no fallback when it is missing.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+
+from ._build import LIB_PATH
+
+DGXM_OK = 0
+DGXM_ERR_INVALID = 1
+DGXM_ERR_UNSUPPORTED = 2
+DGXM_ERR_CUDA = 3
+DGXM_ERR_TIMEOUT = 4
+DGXM_ERR_STATE = 5
+
+DTYPE_BF16 = 0
+DTYPE_F16 = 1
+DTYPE_E4M3 = 2
+DTYPE_F32 = 3
+
+ATTN_SAFE_ORDER = 1
+
+
+class DgxmError(RuntimeError):
+    """A C-ABI call returned a non-zero status."""
+
+    def __init__(self, code: int, func: str, message: str) -> None:
+        super().__init__(f"{func} failed with status {code}: {message}")
+        self.code = code
+        self.func = func
+
+
+class AttnDesc(ctypes.Structure):
+    _fields_ = [
+        ("batch", ctypes.c_int32),
+        ("q_len", ctypes.c_int32),
+        ("kv_len", ctypes.c_int32),
+        ("q_heads", ctypes.c_int32),
+        ("kv_heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("in_dtype", ctypes.c_int32),
+        ("out_dtype", ctypes.c_int32),
+        ("q_stride", ctypes.c_int64 * 3),
+        ("k_stride", ctypes.c_int64 * 3),
+        ("v_stride", ctypes.c_int64 * 3),
+        ("o_stride", ctypes.c_int64 * 3),
+        ("lse_stride", ctypes.c_int64 * 3),
+        ("softmax_scale", ctypes.c_float),
+        ("flags", ctypes.c_int32),
+    ]
+
+
+# Every symbol include/dgxm_sp.h declares, with its ctypes signature.
+_P = ctypes.c_void_p
+_I32 = ctypes.c_int32
+SIGNATURES: dict[str, tuple[object, list[object]]] = {
+    "dgxm_abi_version": (ctypes.c_int, []),
+    "dgxm_last_error_message": (ctypes.c_char_p, []),
+    "dgxm_device_error": (ctypes.c_int, [ctypes.c_int]),
+    "dgxm_attn_fwd": (ctypes.c_int, [ctypes.POINTER(AttnDesc), _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "dgxm_lse_merge": (ctypes.c_int, [_I32, _I32, _I32, _I32, _I32, ctypes.POINTER(_P), _I32,
+                                      ctypes.POINTER(_P), _P, _I32, _P, _P]),
+}
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+def load(path=None) -> ctypes.CDLL:
+    """Load the library once and attach the declared signatures."""
+    global _lib
+    with _lock:
+        if _lib is not None and path is None:
+            return _lib
+        target = str(path or LIB_PATH)
+        try:
+            lib = ctypes.CDLL(target)
+        except OSError as exc:
+            raise RuntimeError(
+                f"libdgxm_sp.so could not be loaded from {target}: {exc}. Build it with "
+                "`python -m dgx_monarch_b200._build` (nvcc, sm_100a); the attention path has "
+                "no CPU fallback.") from exc
+        for name, (restype, argtypes) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = restype
+            fn.argtypes = argtypes
+        if path is None:
+            _lib = lib
+        return lib
+
+
+def check(code: int, func: str) -> None:
+    if code != DGXM_OK:
+        msg = load().dgxm_last_error_message()
+        raise DgxmError(code, func, msg.decode(errors="replace") if msg else "")
+
+
+def device_error(clear: bool = True) -> int:
+    """The device error word (bounded waits that expired); 0 when clean."""
+    value = load().dgxm_device_error(1 if clear else 0)
+    if value < 0:
+        check(-value, "dgxm_device_error")
+    return value

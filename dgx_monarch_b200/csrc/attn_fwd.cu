@@ -1,0 +1,543 @@
+// Non-causal attention forward for sm_100a (B200): tcgen05 MMAs with TMEM
+// accumulators, TMA-staged Q/K/V tiles, warp-specialised online softmax.
+//
+// One CTA owns 256 query rows of one (batch, head): two 128-row Q tiles that
+// ping-pong on the tensor core.  While the softmax warpgroup of tile 0 turns
+// S0 = Q0 K_j^T into probabilities, the tensor core computes P1 V_{j-1} and
+// S1 = Q1 K_j^T, and vice versa, so the exponentials overlap the MMAs.
+//
+// Warp roles (10 warps, 320 threads):
+//   warps 0-3  softmax + output correction + epilogue for Q tile 0
+//   warps 4-7  the same for Q tile 1
+//   warp  8    TMA producer (Q once, then K_j / V_j through a stage ring)
+//   warp  9    TMEM allocator and single-thread MMA issuer
+//
+// Tensor memory (512 columns x 128 lanes x 32 bit):
+//   [  0,128) S0 (fp32 logits); P0 overwrites its first columns (bf16 pairs
+//             or e4m3 quads) once the softmax has read S0
+//   [128,256) S1 / P1
+//   [256,384) O0 (fp32 output accumulator)
+//   [384,512) O1
+//
+// Shared memory: Q tiles (2 x 128 rows x 128 cols) then a ring of K/V stages,
+// every tile stored as 128-byte rows with the 128-byte swizzle that both TMA
+// and the MMA shared-memory descriptors use.
+//
+// The math follows the per-block contract of the reference's ring processor
+// (adapters/cudnn_ring_attention.py:61-89): out = softmax(scale * Q K^T) V and
+// the fp32 natural-log LSE of the scaled logits, per (batch, head, row).
+#include "common.h"
+#include "device_error.cuh"
+#include "ptx.cuh"
+
+namespace dgxm {
+
+constexpr int kAttnThreads = 320;
+constexpr int kTileRows = 128;   // rows per Q tile and per K/V tile
+constexpr int kHeadDim = 128;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+template <bool FP8>
+struct AttnCfg {
+  static constexpr int kEltBytes = FP8 ? 1 : 2;
+  static constexpr int kBoxCols = 128 / kEltBytes;          // elements in one 128-byte row
+  static constexpr int kBoxes = kHeadDim / kBoxCols;        // 128-byte column blocks per tile
+  static constexpr int kBoxBytes = kTileRows * 128;         // 16 KB
+  static constexpr int kTileBytes = kBoxes * kBoxBytes;     // one 128 x 128 tile
+  static constexpr int kStages = FP8 ? 8 : 4;
+  static constexpr int kMmaK = FP8 ? 32 : 16;               // K extent of one MMA
+  static constexpr int kKSteps = kHeadDim / kMmaK;          // MMAs per 128-deep product
+  static constexpr int kPCols = kTileRows * kEltBytes / 4;  // TMEM columns holding P
+  // Stale-max threshold (log2 units) below which the running max is kept and
+  // O is not rescaled; P values then stay below 2^kThr.
+  static constexpr float kThr = FP8 ? 4.0f : 8.0f;
+  // e4m3 probabilities are stored scaled by 2^4 so typical values sit in the
+  // normal range; the epilogue divides the factor back out.
+  static constexpr float kPScale = FP8 ? 16.0f : 1.0f;
+  static constexpr uint32_t kIdescQK = idesc_make(128, 128, FP8 ? 0u : 1u, false);
+  static constexpr uint32_t kIdescPV = idesc_make(128, 128, FP8 ? 0u : 1u, true);
+  static constexpr int kSmemBytes = 1024 /*align slack*/ + 2 * kTileBytes + kStages * kTileBytes +
+                                    256 /*barriers + slots*/;
+};
+
+struct __align__(64) AttnParams {
+  CUtensorMap tmap_q;  // dims (D, H, L, B), box (128 bytes, 1, 128, 1)
+  CUtensorMap tmap_k;
+  CUtensorMap tmap_v;
+  void* o;
+  float* lse;
+  const float* q_descale;
+  const float* k_descale;
+  const float* v_descale;
+  int64_t o_sb, o_sl, o_sh;
+  int64_t lse_sb, lse_sh, lse_sl;
+  int q_len, kv_len, q_heads, kv_heads;
+  int n_kv_tiles;
+  float scale_log2;
+  int flags;
+};
+
+// Barrier slots inside the control block.
+template <int kStages>
+struct Bars {
+  static constexpr int kQ = 0;
+  static constexpr int kKvFull = 1;
+  static constexpr int kKvEmpty = kKvFull + kStages;
+  static constexpr int kSFull = kKvEmpty + kStages;  // 2
+  static constexpr int kPFull = kSFull + 2;          // 2
+  static constexpr int kOFull = kPFull + 2;          // 2
+  static constexpr int kPvDone = kOFull + 2;         // 2
+  static constexpr int kDrain = kPvDone + 2;
+  static constexpr int kCount = kDrain + 1;
+};
+
+template <bool FP8>
+__device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t sq, uint32_t sk) {
+  using C = AttnCfg<FP8>;
+#pragma unroll
+  for (int kk = 0; kk < C::kKSteps; ++kk) {
+    const uint32_t byte = kk * 32;  // each MMA consumes 32 bytes of the head dimension
+    const uint32_t off = (byte / 128) * C::kBoxBytes + (byte % 128);
+    const uint64_t a = sdesc_sw128(sq + off, 16, 1024);
+    const uint64_t b = sdesc_sw128(sk + off, 16, 1024);
+    if constexpr (FP8)
+      umma_f8_ss(d_tmem, a, b, C::kIdescQK, kk > 0 ? 1u : 0u);
+    else
+      umma_f16_ss(d_tmem, a, b, C::kIdescQK, kk > 0 ? 1u : 0u);
+  }
+}
+
+template <bool FP8>
+__device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint32_t sv,
+                                         bool accumulate) {
+  using C = AttnCfg<FP8>;
+#pragma unroll
+  for (int kk = 0; kk < C::kKSteps; ++kk) {
+    // B = V viewed MN-major: head_dim along the 128-byte rows, keys down the
+    // rows; the second 128-byte column block (bf16) sits kBoxBytes further.
+    const uint64_t b = sdesc_sw128(sv + kk * C::kMmaK * 128, C::kBoxBytes, 1024);
+    const uint32_t a = p_tmem + kk * (C::kMmaK * C::kEltBytes / 4);
+    const uint32_t acc = (accumulate || kk > 0) ? 1u : 0u;
+    if constexpr (FP8)
+      umma_f8_ts(d_tmem, a, b, C::kIdescPV, acc);
+    else
+      umma_f16_ts(d_tmem, a, b, C::kIdescPV, acc);
+  }
+}
+
+__device__ __forceinline__ void raise_abort(volatile int* abort_flag, int bits) {
+  report_device_error(bits);
+  *abort_flag = 1;
+}
+
+template <bool FP8, bool OUT_F32>
+__global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_constant__ AttnParams p) {
+  using C = AttnCfg<FP8>;
+  using B = Bars<C::kStages>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base - raw);
+  const uint32_t sQ = base;
+  const uint32_t sKV = base + 2 * C::kTileBytes;
+  uint8_t* ctrl = smem + 2 * C::kTileBytes + C::kStages * C::kTileBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ctrl);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ctrl + B::kCount * 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  auto bar = [&](int i) { return smem_u32(&bars[i]); };
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar(B::kQ), 1);
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(bar(B::kKvFull + s), 1);
+      mbar_init(bar(B::kKvEmpty + s), 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(bar(B::kSFull + t), 1);
+      mbar_init(bar(B::kPFull + t), 128);
+      mbar_init(bar(B::kOFull + t), 1);
+      mbar_init(bar(B::kPvDone + t), 1);
+    }
+    mbar_init(bar(B::kDrain), 1);
+    *abort_flag = 0;
+    mbar_fence_init();
+  }
+  if (warp == 8 && lane == 0) {
+    tma_prefetch_desc(&p.tmap_q);
+    tma_prefetch_desc(&p.tmap_k);
+    tma_prefetch_desc(&p.tmap_v);
+  }
+  if (warp == 9) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  const int qtile = blockIdx.x;
+  const int h = blockIdx.y;
+  const int b = blockIdx.z;
+  const int hk = h / (p.q_heads / p.kv_heads);
+  const int row0 = qtile * 2 * kTileRows;
+  const int nkv = p.n_kv_tiles;
+  const bool safe_order = (p.flags & DGXM_ATTN_SAFE_ORDER) != 0;
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int issued[C::kStages];
+#pragma unroll
+      for (int s = 0; s < C::kStages; ++s) issued[s] = -1;
+      bool ok = true;
+      const uint64_t keep = l2_policy_evict_last();   // K/V are re-read by every Q tile
+      const uint64_t once = l2_policy_evict_first();  // Q is read by this CTA only
+      mbar_expect_tx(bar(B::kQ), 2 * C::kTileBytes);
+      for (int t = 0; t < 2; ++t)
+        for (int c = 0; c < C::kBoxes; ++c)
+          tma_load_4d_hint(sQ + t * C::kTileBytes + c * C::kBoxBytes, &p.tmap_q, bar(B::kQ),
+                           c * C::kBoxCols, h, row0 + t * kTileRows, b, once);
+      for (int idx = 0; idx < 2 * nkv; ++idx) {
+        const int s = idx % C::kStages;
+        const int ph = (idx / C::kStages) & 1;
+        if (!mbar_wait(bar(B::kKvEmpty + s), ph ^ 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        mbar_expect_tx(bar(B::kKvFull + s), C::kTileBytes);
+        const void* map = (idx & 1) ? static_cast<const void*>(&p.tmap_v)
+                                    : static_cast<const void*>(&p.tmap_k);
+        for (int c = 0; c < C::kBoxes; ++c)
+          tma_load_4d_hint(sKV + s * C::kTileBytes + c * C::kBoxBytes, map,
+                           bar(B::kKvFull + s), c * C::kBoxCols, hk, (idx >> 1) * kTileRows, b,
+                           keep);
+        issued[s] = ph;
+      }
+      if (!ok) {
+        raise_abort(abort_flag, kErrProducerTimeout);
+        // Let the copies already in flight land before the CTA can exit.
+        mbar_wait(bar(B::kQ), 0, nullptr);
+        for (int s = 0; s < C::kStages; ++s)
+          if (issued[s] >= 0) mbar_wait(bar(B::kKvFull + s), issued[s], nullptr);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t tS0 = tmem, tS1 = tmem + 128, tO0 = tmem + 256, tO1 = tmem + 384;
+      bool ok = mbar_wait(bar(B::kQ), 0, abort_flag);
+      tc_fence_after();
+      for (int j = 0; ok && j < nkv; ++j) {
+        const int ki = 2 * j;
+        const int ks = ki % C::kStages;
+        if (!(ok = mbar_wait(bar(B::kKvFull + ks), (ki / C::kStages) & 1, abort_flag))) break;
+        tc_fence_after();
+        // S0 = Q0 K_j^T
+        if (safe_order && j > 0) {
+          if (!(ok = mbar_wait(bar(B::kPvDone + 0), (j - 1) & 1, abort_flag))) break;
+          tc_fence_after();
+        }
+        issue_qk<FP8>(tS0, sQ, sKV + ks * C::kTileBytes);
+        umma_commit(bar(B::kSFull + 0));
+        // O1 += P1 V_{j-1}
+        if (j > 0) {
+          const int vs = (2 * j - 1) % C::kStages;
+          if (!(ok = mbar_wait(bar(B::kPFull + 1), (j - 1) & 1, abort_flag))) break;
+          tc_fence_after();
+          issue_pv<FP8>(tO1, tS1, sKV + vs * C::kTileBytes, j - 1 > 0);
+          umma_commit(bar(B::kKvEmpty + vs));
+          if (safe_order) {
+            umma_commit(bar(B::kPvDone + 1));
+            if (!(ok = mbar_wait(bar(B::kPvDone + 1), (j - 1) & 1, abort_flag))) break;
+            tc_fence_after();
+          }
+        }
+        // S1 = Q1 K_j^T
+        issue_qk<FP8>(tS1, sQ + C::kTileBytes, sKV + ks * C::kTileBytes);
+        umma_commit(bar(B::kSFull + 1));
+        umma_commit(bar(B::kKvEmpty + ks));
+        // O0 += P0 V_j
+        const int vi = 2 * j + 1;
+        const int vs = vi % C::kStages;
+        if (!(ok = mbar_wait(bar(B::kKvFull + vs), (vi / C::kStages) & 1, abort_flag))) break;
+        if (!(ok = mbar_wait(bar(B::kPFull + 0), j & 1, abort_flag))) break;
+        tc_fence_after();
+        issue_pv<FP8>(tO0, tS0, sKV + vs * C::kTileBytes, j > 0);
+        if (safe_order) umma_commit(bar(B::kPvDone + 0));
+        if (j == nkv - 1) umma_commit(bar(B::kOFull + 0));
+      }
+      if (ok) {
+        // O1 += P1 V_{n-1}
+        const int vs = (2 * nkv - 1) % C::kStages;
+        ok = mbar_wait(bar(B::kPFull + 1), (nkv - 1) & 1, abort_flag);
+        if (ok) {
+          tc_fence_after();
+          issue_pv<FP8>(tO1, tS1, sKV + vs * C::kTileBytes, nkv - 1 > 0);
+          umma_commit(bar(B::kKvEmpty + vs));
+          umma_commit(bar(B::kOFull + 1));
+        }
+      }
+      if (!ok) {
+        raise_abort(abort_flag, kErrMmaTimeout);
+        // Wait for the MMAs already issued before TMEM is released.
+        umma_commit(bar(B::kDrain));
+        mbar_wait(bar(B::kDrain), 0, nullptr);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int t = warp >> 2;    // Q tile of this warpgroup
+    const int sub = warp & 3;   // TMEM lane quarter this warp may access
+    const int r = sub * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
+    const uint32_t tS = tmem + lane_off + t * 128;
+    const uint32_t tO = tmem + lane_off + 256 + t * 128;
+    float sl2 = p.scale_log2;
+    if constexpr (FP8) sl2 *= p.q_descale[h] * p.k_descale[hk];
+    float m_run = -INFINITY;  // running max of the scaled logits, log2 units
+    float l_run = 0.f;        // running sum of exp2(s * sl2 - m_run)
+    bool ok = true;
+    for (int j = 0; j < nkv; ++j) {
+      ok = __all_sync(0xffffffffu, mbar_wait(bar(B::kSFull + t), j & 1, abort_flag));
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t sr[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, sr[c]);
+      tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < 4; ++c) reg_fence32(sr[c]);
+      float s[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(sr[c][i]);
+      const int valid = p.kv_len - j * kTileRows;
+      if (valid < kTileRows) {
+#pragma unroll
+        for (int i = 0; i < 128; ++i)
+          if (i >= valid) s[i] = -INFINITY;
+      }
+      float mx0 = s[0], mx1 = s[1], mx2 = s[2], mx3 = s[3];
+#pragma unroll
+      for (int i = 4; i < 128; i += 4) {
+        mx0 = fmaxf(mx0, s[i]);
+        mx1 = fmaxf(mx1, s[i + 1]);
+        mx2 = fmaxf(mx2, s[i + 2]);
+        mx3 = fmaxf(mx3, s[i + 3]);
+      }
+      const float m_cand = fmaxf(m_run, fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2);
+      const bool grow = m_cand > m_run + C::kThr;
+      float alpha = 1.f;
+      bool rescale = false;
+      if (__any_sync(0xffffffffu, grow)) {
+        alpha = ex2_approx(m_run - m_cand);  // 0 on the first block (m_run = -inf)
+        m_run = m_cand;
+        rescale = j > 0;
+      }
+      l_run *= alpha;
+      const float neg_m = -m_run;
+      float sum0 = 0.f, sum1 = 0.f;
+#pragma unroll
+      for (int i = 0; i < 128; i += 2) {
+        s[i] = ex2_approx(fmaf(s[i], sl2, neg_m));
+        s[i + 1] = ex2_approx(fmaf(s[i + 1], sl2, neg_m));
+        sum0 += s[i];
+        sum1 += s[i + 1];
+      }
+      l_run += sum0 + sum1;
+      if constexpr (FP8) {
+        uint32_t pk[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          pk[i] = pack_e4m3x4(s[4 * i] * C::kPScale, s[4 * i + 1] * C::kPScale,
+                              s[4 * i + 2] * C::kPScale, s[4 * i + 3] * C::kPScale);
+        tmem_st32(tS, pk);
+      } else {
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint32_t pk[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) pk[i] = pack_bf16x2(s[64 * c + 2 * i], s[64 * c + 2 * i + 1]);
+          tmem_st32(tS + c * 32, pk);
+        }
+      }
+      if (rescale) {
+        // O_t is quiescent here: the commit behind this S_t also covered the
+        // previous P_t V product.
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tO + c * 32, o);
+          tmem_wait_ld();
+          reg_fence32(o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(tO + c * 32, o);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(bar(B::kPFull + t));
+    }
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar(B::kOFull + t), 0, abort_flag));
+    if (!ok) {
+      raise_abort(abort_flag, kErrSoftmaxTimeout);
+    } else {
+      tc_fence_after();
+      const int grow = row0 + t * kTileRows + r;
+      const bool row_ok = grow < p.q_len;
+      float inv = 1.f / (l_run * C::kPScale);
+      if constexpr (FP8) inv *= p.v_descale[hk];
+      char* orow = static_cast<char*>(p.o) +
+                   (static_cast<int64_t>(b) * p.o_sb + static_cast<int64_t>(grow) * p.o_sl +
+                    static_cast<int64_t>(h) * p.o_sh) *
+                       (OUT_F32 ? 4 : 2);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[32];
+        tmem_ld32(tO + c * 32, o);
+        tmem_wait_ld();
+        reg_fence32(o);
+        if (row_ok) {
+          if constexpr (OUT_F32) {
+            float4* dst = reinterpret_cast<float4*>(orow + c * 128);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              dst[i] = make_float4(__uint_as_float(o[4 * i]) * inv, __uint_as_float(o[4 * i + 1]) * inv,
+                                   __uint_as_float(o[4 * i + 2]) * inv,
+                                   __uint_as_float(o[4 * i + 3]) * inv);
+          } else {
+            uint4* dst = reinterpret_cast<uint4*>(orow + c * 64);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              uint4 w;
+              w.x = pack_bf16x2(__uint_as_float(o[8 * i + 0]) * inv, __uint_as_float(o[8 * i + 1]) * inv);
+              w.y = pack_bf16x2(__uint_as_float(o[8 * i + 2]) * inv, __uint_as_float(o[8 * i + 3]) * inv);
+              w.z = pack_bf16x2(__uint_as_float(o[8 * i + 4]) * inv, __uint_as_float(o[8 * i + 5]) * inv);
+              w.w = pack_bf16x2(__uint_as_float(o[8 * i + 6]) * inv, __uint_as_float(o[8 * i + 7]) * inv);
+              dst[i] = w;
+            }
+          }
+        }
+      }
+      if (row_ok && p.lse != nullptr) {
+        p.lse[static_cast<int64_t>(b) * p.lse_sb + static_cast<int64_t>(h) * p.lse_sh +
+              static_cast<int64_t>(grow) * p.lse_sl] = (m_run + log2f(l_run)) * kLn2;
+      }
+    }
+  }
+
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <bool FP8, bool OUT_F32>
+static int launch_attn(const AttnParams& prm, dim3 grid, cudaStream_t stream) {
+  using C = AttnCfg<FP8>;
+  static uint64_t configured = 0;  // one bit per device ordinal
+  auto kern = attn_fwd_kernel<FP8, OUT_F32>;
+  int dev = 0;
+  DGXM_CUDA_TRY(cudaGetDevice(&dev));
+  const uint64_t bit = uint64_t(1) << (dev & 63);
+  if (!(configured & bit)) {
+    DGXM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       C::kSmemBytes));
+    configured |= bit;
+  }
+  kern<<<grid, kAttnThreads, C::kSmemBytes, stream>>>(prm);
+  DGXM_CUDA_TRY(cudaGetLastError());
+  return DGXM_OK;
+}
+
+static bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
+
+}  // namespace dgxm
+
+extern "C" int dgxm_attn_fwd(const dgxm_attn_desc* d, const void* q, const void* k, const void* v,
+                             const float* q_descale, const float* k_descale,
+                             const float* v_descale, void* o, float* lse, void* stream) {
+  using namespace dgxm;
+  if (d == nullptr) return fail(DGXM_ERR_INVALID, "attention descriptor is NULL");
+  if (d->batch < 0 || d->q_len < 0 || d->kv_len < 0 || d->q_heads <= 0 || d->kv_heads <= 0)
+    return fail(DGXM_ERR_INVALID, "negative or zero attention extent (batch=%d q_len=%d kv_len=%d "
+                "q_heads=%d kv_heads=%d)", d->batch, d->q_len, d->kv_len, d->q_heads, d->kv_heads);
+  if (d->head_dim != kHeadDim)
+    return fail(DGXM_ERR_UNSUPPORTED, "head_dim %d is not supported (this build runs 128)",
+                d->head_dim);
+  if (d->q_heads % d->kv_heads != 0)
+    return fail(DGXM_ERR_INVALID, "query heads (%d) must be divisible by key/value heads (%d)",
+                d->q_heads, d->kv_heads);
+  if (d->batch == 0 || d->q_len == 0) return DGXM_OK;
+  if (d->kv_len == 0)
+    return fail(DGXM_ERR_INVALID, "attention over an empty key axis has no defined output");
+  if (d->batch > 65535 || d->q_heads > 65535)
+    return fail(DGXM_ERR_UNSUPPORTED, "batch %d or heads %d exceed the launch grid", d->batch,
+                d->q_heads);
+  const bool fp8 = d->in_dtype == DGXM_DTYPE_E4M3;
+  if (!fp8 && d->in_dtype != DGXM_DTYPE_BF16)
+    return fail(DGXM_ERR_UNSUPPORTED, "input dtype %d is not supported (bf16 or e4m3)",
+                d->in_dtype);
+  const bool out_f32 = d->out_dtype == DGXM_DTYPE_F32;
+  if (!out_f32 && d->out_dtype != DGXM_DTYPE_BF16)
+    return fail(DGXM_ERR_UNSUPPORTED, "output dtype %d is not supported (bf16 or f32)",
+                d->out_dtype);
+  if (q == nullptr || k == nullptr || v == nullptr || o == nullptr)
+    return fail(DGXM_ERR_INVALID, "q, k, v and o must be non-NULL");
+  if (fp8 && (q_descale == nullptr || k_descale == nullptr || v_descale == nullptr))
+    return fail(DGXM_ERR_INVALID, "e4m3 attention needs q, k and v descale arrays");
+  const int out_bytes = out_f32 ? 4 : 2;
+  if (!aligned16(o) || (d->o_stride[1] * out_bytes) % 16 != 0 ||
+      (d->o_stride[2] * out_bytes) % 16 != 0 || (d->o_stride[0] * out_bytes) % 16 != 0)
+    return fail(DGXM_ERR_INVALID, "output base and strides must be 16-byte aligned");
+
+  AttnParams prm;
+  memset(&prm, 0, sizeof(prm));
+  const CUtensorMapDataType dt = fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const int eb = fp8 ? 1 : 2;
+  const int box_cols = 128 / eb;
+  int rc;
+  if ((rc = encode_map_4d(&prm.tmap_q, q, dt, eb, kHeadDim, d->q_heads, d->q_len, d->batch,
+                          d->q_stride[2], d->q_stride[1], d->q_stride[0], box_cols, kTileRows)))
+    return rc;
+  if ((rc = encode_map_4d(&prm.tmap_k, k, dt, eb, kHeadDim, d->kv_heads, d->kv_len, d->batch,
+                          d->k_stride[2], d->k_stride[1], d->k_stride[0], box_cols, kTileRows)))
+    return rc;
+  if ((rc = encode_map_4d(&prm.tmap_v, v, dt, eb, kHeadDim, d->kv_heads, d->kv_len, d->batch,
+                          d->v_stride[2], d->v_stride[1], d->v_stride[0], box_cols, kTileRows)))
+    return rc;
+  prm.o = o;
+  prm.lse = lse;
+  prm.q_descale = q_descale;
+  prm.k_descale = k_descale;
+  prm.v_descale = v_descale;
+  prm.o_sb = d->o_stride[0];
+  prm.o_sl = d->o_stride[1];
+  prm.o_sh = d->o_stride[2];
+  prm.lse_sb = d->lse_stride[0];
+  prm.lse_sh = d->lse_stride[1];
+  prm.lse_sl = d->lse_stride[2];
+  prm.q_len = d->q_len;
+  prm.kv_len = d->kv_len;
+  prm.q_heads = d->q_heads;
+  prm.kv_heads = d->kv_heads;
+  prm.n_kv_tiles = (d->kv_len + kTileRows - 1) / kTileRows;
+  const float scale = d->softmax_scale > 0.f ? d->softmax_scale : 1.0f / sqrtf((float)d->head_dim);
+  prm.scale_log2 = scale * kLog2e;
+  prm.flags = d->flags;
+
+  dim3 grid((d->q_len + 2 * kTileRows - 1) / (2 * kTileRows), d->q_heads, d->batch);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (fp8) return out_f32 ? launch_attn<true, true>(prm, grid, st) : launch_attn<true, false>(prm, grid, st);
+  return out_f32 ? launch_attn<false, true>(prm, grid, st) : launch_attn<false, false>(prm, grid, st);
+}

@@ -1,0 +1,9 @@
+// Single translation unit of libdgxm_sp.so.  The kernels share one device
+// error word (device_error.cuh), so the library is built as one unit rather
+// than with relocatable device code.
+#include <math.h>
+#include <string.h>
+
+#include "capi.cu"
+#include "attn_fwd.cu"
+#include "lse_merge.cu"

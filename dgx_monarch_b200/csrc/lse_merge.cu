@@ -1,0 +1,138 @@
+// Log-sum-exp merge of partial attention results over disjoint key blocks.
+//
+// For every (batch, row, head):
+//   lse = log(sum_i exp(lse_i))
+//   out = sum_i exp(lse_i - lse) * out_i
+// computed in fp32.  This is the combine step of ring attention: each ring
+// step attends the local queries to one rotating key/value block and leaves
+// (out_i, lse_i); the merge folds them into the exact full-axis result.
+//
+// HBM-bound: one warp per (batch, row, head) row of head_dim = 128 values;
+// each lane owns four consecutive values, so every part's row is read with one
+// fully coalesced 256-byte (bf16) or 512-byte (fp32) warp access.
+#include "common.h"
+#include "ptx.cuh"
+
+namespace dgxm {
+
+constexpr int kMaxMergeParts = 16;
+
+struct MergeParams {
+  const void* out[kMaxMergeParts];
+  const float* lse[kMaxMergeParts];
+  void* dst;
+  float* dst_lse;
+  int n;
+  int batch, rows, heads;
+};
+
+template <bool PART_F32, bool OUT_F32>
+__global__ void __launch_bounds__(256) lse_merge_kernel(const __grid_constant__ MergeParams p) {
+  const int warps_per_block = blockDim.x >> 5;
+  const int64_t total = static_cast<int64_t>(p.batch) * p.rows * p.heads;
+  const int lane = threadIdx.x & 31;
+  for (int64_t item = static_cast<int64_t>(blockIdx.x) * warps_per_block + (threadIdx.x >> 5);
+       item < total; item += static_cast<int64_t>(gridDim.x) * warps_per_block) {
+    // item enumerates (b, row, h) with h fastest, matching the (B, L, H, D) rows.
+    const int h = static_cast<int>(item % p.heads);
+    const int64_t br = item / p.heads;
+    const int row = static_cast<int>(br % p.rows);
+    const int b = static_cast<int>(br / p.rows);
+    const int64_t lse_idx = (static_cast<int64_t>(b) * p.heads + h) * p.rows + row;
+    float mx = -INFINITY;
+    for (int i = 0; i < p.n; ++i) mx = fmaxf(mx, p.lse[i][lse_idx]);
+    float wsum = 0.f;
+    float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
+    const int64_t elem = item * 128 + lane * 4;
+    for (int i = 0; i < p.n; ++i) {
+      const float li = p.lse[i][lse_idx];
+      // A part with lse = -inf saw no keys for this row and carries no weight.
+      const float w = (li == -INFINITY) ? 0.f : __expf(li - mx);
+      wsum += w;
+      float x0, x1, x2, x3;
+      if constexpr (PART_F32) {
+        const float4 v = *reinterpret_cast<const float4*>(static_cast<const float*>(p.out[i]) + elem);
+        x0 = v.x; x1 = v.y; x2 = v.z; x3 = v.w;
+      } else {
+        const uint2 v = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(p.out[i]) + elem);
+        const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.x));
+        const float2 c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.y));
+        x0 = a.x; x1 = a.y; x2 = c.x; x3 = c.y;
+      }
+      acc0 = fmaf(w, x0, acc0);
+      acc1 = fmaf(w, x1, acc1);
+      acc2 = fmaf(w, x2, acc2);
+      acc3 = fmaf(w, x3, acc3);
+    }
+    const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+    if constexpr (OUT_F32) {
+      *reinterpret_cast<float4*>(static_cast<float*>(p.dst) + elem) =
+          make_float4(acc0 * inv, acc1 * inv, acc2 * inv, acc3 * inv);
+    } else {
+      uint2 w;
+      w.x = pack_bf16x2(acc0 * inv, acc1 * inv);
+      w.y = pack_bf16x2(acc2 * inv, acc3 * inv);
+      *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(p.dst) + elem) = w;
+    }
+    if (lane == 0 && p.dst_lse != nullptr)
+      p.dst_lse[lse_idx] = wsum > 0.f ? mx + __logf(wsum) : -INFINITY;
+  }
+}
+
+}  // namespace dgxm
+
+extern "C" int dgxm_lse_merge(int32_t batch, int32_t rows, int32_t heads, int32_t head_dim,
+                              int32_t n_parts, const void* const* parts_out, int32_t part_dtype,
+                              const float* const* parts_lse, void* out, int32_t out_dtype,
+                              float* lse_out, void* stream) {
+  using namespace dgxm;
+  if (batch < 0 || rows < 0 || heads <= 0)
+    return fail(DGXM_ERR_INVALID, "merge extents must be non-negative (heads positive)");
+  if (head_dim != 128)
+    return fail(DGXM_ERR_UNSUPPORTED, "merge head_dim %d is not supported (128)", head_dim);
+  if (n_parts < 1 || n_parts > kMaxMergeParts)
+    return fail(DGXM_ERR_INVALID, "merge takes 1..%d parts, got %d", kMaxMergeParts, n_parts);
+  const bool part_f32 = part_dtype == DGXM_DTYPE_F32;
+  if (!part_f32 && part_dtype != DGXM_DTYPE_BF16)
+    return fail(DGXM_ERR_UNSUPPORTED, "merge part dtype %d is not supported", part_dtype);
+  const bool out_f32 = out_dtype == DGXM_DTYPE_F32;
+  if (!out_f32 && out_dtype != DGXM_DTYPE_BF16)
+    return fail(DGXM_ERR_UNSUPPORTED, "merge output dtype %d is not supported", out_dtype);
+  if (parts_out == nullptr || parts_lse == nullptr || out == nullptr)
+    return fail(DGXM_ERR_INVALID, "merge pointers must be non-NULL");
+  if (batch == 0 || rows == 0) return DGXM_OK;
+  MergeParams prm;
+  memset(&prm, 0, sizeof(prm));
+  for (int i = 0; i < n_parts; ++i) {
+    if (parts_out[i] == nullptr || parts_lse[i] == nullptr)
+      return fail(DGXM_ERR_INVALID, "merge part %d is NULL", i);
+    if (reinterpret_cast<uintptr_t>(parts_out[i]) % 16 != 0)
+      return fail(DGXM_ERR_INVALID, "merge part %d is not 16-byte aligned", i);
+    prm.out[i] = parts_out[i];
+    prm.lse[i] = parts_lse[i];
+  }
+  if (reinterpret_cast<uintptr_t>(out) % 16 != 0)
+    return fail(DGXM_ERR_INVALID, "merge output is not 16-byte aligned");
+  prm.dst = out;
+  prm.dst_lse = lse_out;
+  prm.n = n_parts;
+  prm.batch = batch;
+  prm.rows = rows;
+  prm.heads = heads;
+  int dev = 0, sms = 148;
+  DGXM_CUDA_TRY(cudaGetDevice(&dev));
+  DGXM_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const int64_t items = static_cast<int64_t>(batch) * rows * heads;
+  const int64_t want = (items + 7) / 8;
+  const int blocks = static_cast<int>(want < int64_t(sms) * 16 ? want : int64_t(sms) * 16);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (part_f32) {
+    if (out_f32) lse_merge_kernel<true, true><<<blocks, 256, 0, st>>>(prm);
+    else lse_merge_kernel<true, false><<<blocks, 256, 0, st>>>(prm);
+  } else {
+    if (out_f32) lse_merge_kernel<false, true><<<blocks, 256, 0, st>>>(prm);
+    else lse_merge_kernel<false, false><<<blocks, 256, 0, st>>>(prm);
+  }
+  DGXM_CUDA_TRY(cudaGetLastError());
+  return DGXM_OK;
+}

@@ -1,0 +1,233 @@
+"""Generate the golden fixtures in this directory from the reference itself.
+
+Run in a container that has the dgx-monarch source tree (read-only) at
+/root/reference:
+
+    python tests/golden/make_golden.py
+
+It imports the reference's own in-repo USP modules (adapters/base.py,
+usp_full_axis.py, usp_pad_exclusion.py, usp_sequence_order.py,
+cfg_parallel.py, cudnn_ring_attention.py) with xfuser / yunchang replaced by
+stubs in sys.modules, exactly where the reference's tests place theirs
+(tests/test_usp_full_axis.py:12-27, tests/test_usp_pad_exact.py:323-360), and
+records inputs and outputs as small fixtures.  Nothing at test time reads the
+reference; the tests compare the oracle (oracle/usp.py) with these files.
+"""
+from __future__ import annotations
+
+import json
+import math
+import sys
+import types
+from pathlib import Path
+
+import numpy as np
+import torch
+
+REF_SRC = Path("/root/reference/src")
+OUT = Path(__file__).resolve().parent
+
+
+def _install_stubs(ring_world=1, gathered=None, world=1, rank=0):
+    """The xfuser / yunchang leaves, as the reference's tests stub them."""
+    calls = []
+
+    class AllToAll:
+        @staticmethod
+        def apply(_group, tensor, scatter, gather):
+            calls.append((scatter, gather, tensor.detach().clone()))
+            if (scatter, gather) == (2, 1) and gathered is not None:
+                return gathered.to(dtype=tensor.dtype)
+            return tensor
+
+    class StubUSP:
+        ulysses_pg = ring_pg = attn_type = attn_processor = None
+        q_descale = k_descale = v_descale = None
+
+        def __init__(self, *args, **kwargs):
+            pass
+
+        def __call__(self, attn, q_l, k_l, v_l, **kwargs):
+            return _attend64(q_l, k_l, v_l)
+
+        @staticmethod
+        def ring_attn_fn(q, k, v, **kwargs):
+            return _attend64(q, k, v)
+
+    mods = {name: types.ModuleType(name) for name in (
+        "xfuser", "xfuser.core", "xfuser.core.distributed", "xfuser.core.long_ctx_attention",
+        "yunchang", "yunchang.kernels", "yunchang.comm", "yunchang.comm.all_to_all")}
+    mods["xfuser.core.distributed"].get_ring_parallel_world_size = lambda: ring_world
+    mods["xfuser.core.distributed"].get_sequence_parallel_world_size = lambda: world
+    mods["xfuser.core.distributed"].get_sequence_parallel_rank = lambda: rank
+    mods["xfuser.core.long_ctx_attention"].xFuserLongContextAttention = StubUSP
+    mods["yunchang.kernels"].AttnType = {"TORCH_FLASH": "TORCH_FLASH"}
+    mods["yunchang.comm.all_to_all"].SeqAllToAll4D = AllToAll
+    sys.modules.update(mods)
+    return calls, StubUSP
+
+
+def _attend64(q, k, v):
+    """float64 softmax(q k^T / sqrt(D)) v in (B, L, H, D), the reference tests' kernel."""
+    qh, kh, vh = (t.transpose(1, 2).double() for t in (q, k, v))
+    scores = qh @ kh.transpose(-1, -2) / math.sqrt(qh.shape[-1])
+    return (torch.softmax(scores, dim=-1) @ vh).transpose(1, 2).to(q.dtype)
+
+
+def main() -> None:
+    sys.path.insert(0, str(REF_SRC))
+    _install_stubs()
+    import dgx_monarch.adapters.base as base
+    from dgx_monarch.adapters import cfg_parallel, cudnn_ring_attention
+    from dgx_monarch.adapters.usp_full_axis import run_full_axis
+    from dgx_monarch.adapters.usp_pad_exclusion import keep_index
+    from dgx_monarch.adapters.usp_sequence_order import RankMajorJointOrder
+
+    golden: dict = {}
+    arrays: dict[str, np.ndarray] = {}
+    rng = np.random.default_rng(2026)
+
+    # a) gathered pad-row coordinates (adapters/base.py:134-149), including the
+    #    hand-computed Krea2 geometries of tests/test_usp_pad_exact.py:28-75.
+    cases = [([(512, 256), (9216, 4608)], 2), ([(512, 256), (8281, 4141)], 2),
+             ([(511, 256), (8281, 4141)], 2), ([(512, 256), (8275, 4139)], 2),
+             ([(510, 128), (8281, 2071)], 4), ([(511, 511), (8281, 8281)], 1),
+             ([(511, 256)], 2), ([(512, 256)], 2)]
+    for _ in range(24):
+        world = int(rng.choice([2, 3, 4, 8]))
+        segs = []
+        for _s in range(int(rng.integers(1, 4))):
+            orig = int(rng.integers(1, 5000))
+            segs.append((orig, -(-orig // world)))
+        cases.append((segs, world))
+    padded = []
+    for segs, world in cases:
+        base.sp_world = (lambda w=world: w)
+        padded.append({"segments": segs, "world": world, "rows": base.padded_row_indices(segs)})
+    golden["padded_row_indices"] = padded
+
+    # b) joint key order (adapters/usp_sequence_order.py:246-309).
+    joint = []
+    for text, image, world in ((1, 1, 2), (3, 5, 2), (128, 2048, 2), (7, 2, 4), (64, 1152, 8),
+                               (2, 4, 2), (5, 3, 3)):
+        order = RankMajorJointOrder(text, image)
+        rows = world * (text + image)
+        perm = order.permutation(rows, torch.device("cpu")).tolist()
+        drop = sorted(set(int(x) for x in rng.integers(0, rows, size=min(4, rows))))
+        kv_drop = sorted(set(int(x) for x in rng.integers(0, rows, size=min(3, rows))))
+        z = torch.zeros(1, rows, 1, 1)
+        _q, _k, _v, qd, kd, _p = order.canonicalize(z, z, z, drop, kv_drop, None)
+        joint.append({"text": text, "image": image, "world": world, "permutation": perm,
+                      "drop": drop, "kv_drop": kv_drop, "canon_drop": qd, "canon_kv_drop": kd})
+    golden["joint_order"] = joint
+
+    # c) keep index (adapters/usp_pad_exclusion.py:79-126).
+    keeps = []
+    for rows, drop in ((6, []), (4, [1]), (14, [5, 13]), (10, [8, 9]), (4, [3]), (9728, [4652, 8793])):
+        idx = keep_index(rows, drop, torch.device("cpu"))
+        keeps.append({"rows": rows, "drop": drop, "kept": None if idx is None else idx.tolist()})
+    golden["keep_index"] = keeps
+
+    # d) the full-axis Ulysses composition with an order descriptor and pads
+    #    (adapters/usp_full_axis.py:9-40), float64, the rank-major gathered axis
+    #    handed in the way tests/test_usp_full_axis.py:67-91 does.
+    full = []
+    for n, (text, image, world, hds, dim, drop, kvdrop) in enumerate(
+            ((2, 2, 2, 2, 3, [3], [7]), (3, 5, 2, 2, 4, [7, 15], [2, 11]), (2, 4, 3, 1, 8, [], []))):
+        rows = world * (text + image)
+        gathered = torch.from_numpy(rng.standard_normal((1, rows, hds, dim)))
+        calls, usp_cls = _install_stubs(gathered=gathered)
+        out = run_full_axis(usp_cls(), gathered[:, :rows // world], gathered[:, :rows // world],
+                            gathered[:, :rows // world], drop, kvdrop, None,
+                            RankMajorJointOrder(text, image), None)
+        arrays[f"full_axis_{n}_in"] = gathered.numpy()
+        arrays[f"full_axis_{n}_sent"] = calls[-1][2].numpy()  # what the inverse all-to-all got
+        arrays[f"full_axis_{n}_out"] = out.numpy()
+        full.append({"index": n, "text": text, "image": image, "world": world,
+                     "drop": drop, "kv_drop": kvdrop})
+    golden["full_axis"] = full
+
+    # e) the usp_attention callable at world 1 (adapters/base.py:216-326):
+    #    reshape surfaces, GQA repeat_interleave, pad-row exclusion.
+    _install_stubs()
+    attn = base._make_usp_attention_callable(sys.modules["xfuser.core.long_ctx_attention"]
+                                             .xFuserLongContextAttention())
+    callable_cases = []
+    specs = [
+        dict(b=1, l=10, h=4, hkv=4, d=8, skip=False, gqa=False, drop=None),
+        dict(b=2, l=7, h=4, hkv=2, d=8, skip=False, gqa=True, drop=None),
+        dict(b=1, l=14, h=4, hkv=4, d=8, skip=True, gqa=False, drop=[5, 13]),
+        dict(b=1, l=9, h=2, hkv=1, d=16, skip=True, gqa=True, drop=[8]),
+    ]
+    for n, s in enumerate(specs):
+        q = torch.from_numpy(rng.standard_normal((s["b"], s["l"], s["h"], s["d"])))
+        k = torch.from_numpy(rng.standard_normal((s["b"], s["l"], s["hkv"], s["d"])))
+        v = torch.from_numpy(rng.standard_normal((s["b"], s["l"], s["hkv"], s["d"])))
+        if s["skip"]:
+            out = attn(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), heads=s["h"],
+                       skip_reshape=True, skip_output_reshape=True, enable_gqa=s["gqa"],
+                       drop_rows=s["drop"]).transpose(1, 2)
+        else:
+            out = attn(q.reshape(s["b"], s["l"], -1), k.reshape(s["b"], s["l"], -1),
+                       v.reshape(s["b"], s["l"], -1), heads=s["h"], enable_gqa=s["gqa"],
+                       drop_rows=s["drop"]).reshape(s["b"], s["l"], s["h"], s["d"])
+        for name, t in (("q", q), ("k", k), ("v", v), ("out", out)):
+            arrays[f"callable_{n}_{name}"] = t.numpy()
+        callable_cases.append({"index": n, **s})
+    golden["usp_callable"] = callable_cases
+
+    # f) the CFG batch slice (adapters/cfg_parallel.py:71-87).
+    x = rng.standard_normal((4, 3, 2))
+    bcast = rng.standard_normal((1, 3))
+    tree = {"x": torch.from_numpy(x), "nested": [torch.from_numpy(x[:, 0]), torch.from_numpy(bcast)]}
+    slices = []
+    for world in (2, 4):
+        for rank in range(world):
+            sl = cfg_parallel._take_slice(tree, 4, world, rank)
+            arrays[f"cfg_{world}_{rank}_x"] = sl["x"].numpy()
+            arrays[f"cfg_{world}_{rank}_n0"] = sl["nested"][0].numpy()
+            arrays[f"cfg_{world}_{rank}_n1"] = sl["nested"][1].numpy()
+            slices.append({"world": world, "rank": rank})
+    arrays["cfg_in_x"], arrays["cfg_in_bcast"] = x, bcast
+    golden["cfg_slice"] = slices
+
+    # g) shard_seq chunks (adapters/base.py:91-123).
+    t = rng.standard_normal((1, 7, 3))
+    shards = []
+    for world in (2, 3, 4):
+        for rank in range(world):
+            base.sp_world = (lambda w=world: w)
+            base.sp_rank = (lambda r=rank: r)
+            local, orig = base.shard_seq(torch.from_numpy(t))
+            arrays[f"shard_{world}_{rank}"] = local.numpy()
+            shards.append({"world": world, "rank": rank, "orig": orig})
+    arrays["shard_in"] = t
+    golden["shard_seq"] = shards
+
+    # h) the dyadic known-answer probe of the cuDNN ring processor
+    #    (adapters/cudnn_ring_attention.py:106-135): record its inputs and the
+    #    expected (out, lse) its own formula computes, in fp32 on the CPU.
+    seen = []
+
+    def recorder(q, k, v, softmax_scale=None):
+        qh, kh, vh = (value.transpose(1, 2).float() for value in (q, k, v))
+        scores = torch.matmul(qh, kh.transpose(-1, -2)) * softmax_scale
+        lse = torch.logsumexp(scores, dim=-1)
+        out = torch.matmul(torch.softmax(scores, dim=-1), vh).transpose(1, 2).to(q.dtype)
+        seen.append((q.clone(), k.clone(), v.clone(), out.clone(), lse.clone(), softmax_scale))
+        return out, lse
+
+    cudnn_ring_attention._probe_native(recorder, device=torch.device("cpu"))
+    for n, (q, k, v, out, lse, scale) in enumerate(seen):
+        for name, tt in (("q", q), ("k", k), ("v", v), ("out", out)):
+            arrays[f"probe_{n}_{name}"] = tt.float().numpy()
+        arrays[f"probe_{n}_lse"] = lse.numpy()
+    golden["probe"] = [{"index": n, "dtype": str(s[0].dtype), "scale": s[5]} for n, s in enumerate(seen)]
+
+    (OUT / "golden.json").write_text(json.dumps(golden, indent=1))
+    np.savez_compressed(OUT / "golden_arrays.npz", **arrays)
+    print("wrote", OUT / "golden.json", OUT / "golden_arrays.npz")
+
+
+if __name__ == "__main__":
+    main()

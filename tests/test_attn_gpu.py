@@ -1,0 +1,166 @@
+"""Parity of the tcgen05 attention kernel against an fp32 torch reference.
+
+Tolerances are the ones the path is held to: bf16 output max-abs <= 2e-2 and
+rel-L2 <= 5e-3 against fp32 softmax(QK^T/sqrt(D))V; FP8-e4m3 rel-L2 <= 3e-2;
+LSE (natural log, fp32) within 2e-3 absolute.
+"""
+from __future__ import annotations
+
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+BF16_MAX_ABS = 2e-2
+BF16_REL_L2 = 5e-3
+FP8_REL_L2 = 3e-2
+LSE_ABS = 2e-3
+
+
+def reference_attention(q, k, v, scale=None, chunk=2048):
+    """fp32 softmax(scale * q k^T) v and natural-log LSE, (B,L,H,D) layout."""
+    b, lq, h, d = q.shape
+    hkv = k.shape[2]
+    scale = scale or 1.0 / math.sqrt(d)
+    rep = h // hkv
+    kf = k.float().repeat_interleave(rep, dim=2).permute(0, 2, 3, 1)  # B H D Lk
+    vf = v.float().repeat_interleave(rep, dim=2).permute(0, 2, 1, 3)  # B H Lk D
+    outs, lses = [], []
+    for s in range(0, lq, chunk):
+        qc = q[:, s:s + chunk].float().permute(0, 2, 1, 3)  # B H c D
+        logits = torch.matmul(qc, kf) * scale
+        lse = torch.logsumexp(logits, dim=-1)
+        p = torch.softmax(logits, dim=-1)
+        outs.append(torch.matmul(p, vf).permute(0, 2, 1, 3))
+        lses.append(lse)
+    return torch.cat(outs, dim=1), torch.cat(lses, dim=2)
+
+
+def rel_l2(a, b):
+    return ((a.float() - b.float()).norm() / b.float().norm()).item()
+
+
+SHAPES = [
+    # (batch, q_len, kv_len, q_heads, kv_heads)
+    (1, 256, 256, 1, 1),
+    (1, 128, 128, 2, 2),
+    (2, 300, 77, 3, 1),
+    (1, 1000, 1000, 4, 4),
+    (1, 513, 2049, 2, 2),
+    (1, 4096, 4096, 2, 2),
+]
+
+
+@pytest.mark.parametrize("shape", SHAPES)
+def test_bf16_matches_fp32_reference(lib, shape):
+    from dgx_monarch_b200.ops import attention_fwd
+
+    b, lq, lk, h, hkv = shape
+    g = torch.Generator(device="cuda").manual_seed(0)
+    q = torch.randn(b, lq, h, 128, device="cuda", generator=g).bfloat16()
+    k = torch.randn(b, lk, hkv, 128, device="cuda", generator=g).bfloat16()
+    v = torch.randn(b, lk, hkv, 128, device="cuda", generator=g).bfloat16()
+    out, lse = attention_fwd(q, k, v)
+    torch.cuda.synchronize()
+    ref, ref_lse = reference_attention(q, k, v)
+    assert torch.isfinite(out.float()).all()
+    assert (out.float() - ref).abs().max().item() <= BF16_MAX_ABS
+    assert rel_l2(out, ref) <= BF16_REL_L2
+    assert (lse - ref_lse).abs().max().item() <= LSE_ABS
+
+
+def test_fast_and_safe_mma_orders_agree_bitwise(lib):
+    """The fast issue order reuses S tensor memory right behind the P.V that
+    reads P from it; the safe order drains first.  Same math, same bits."""
+    from dgx_monarch_b200.ops import attention_fwd
+
+    g = torch.Generator(device="cuda").manual_seed(1)
+    q, k, v = (torch.randn(1, 2048, 4, 128, device="cuda", generator=g).bfloat16() for _ in range(3))
+    fast, fast_lse = attention_fwd(q, k, v)
+    safe, safe_lse = attention_fwd(q, k, v, safe_order=True)
+    torch.cuda.synchronize()
+    assert torch.equal(fast, safe)
+    assert torch.equal(fast_lse, safe_lse)
+
+
+def test_fp32_output_and_strided_inputs(lib):
+    from dgx_monarch_b200.ops import attention_fwd
+
+    g = torch.Generator(device="cuda").manual_seed(2)
+    # q/k/v as views into one packed (B, L, 3, H, D) projection output.
+    qkv = torch.randn(1, 700, 3, 4, 128, device="cuda", generator=g).bfloat16()
+    q, k, v = qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2]
+    out, lse = attention_fwd(q, k, v, out_dtype=torch.float32, softmax_scale=0.05)
+    torch.cuda.synchronize()
+    ref, ref_lse = reference_attention(q, k, v, scale=0.05)
+    assert out.dtype == torch.float32
+    assert rel_l2(out, ref) <= BF16_REL_L2
+    assert (lse - ref_lse).abs().max().item() <= LSE_ABS
+
+
+def quantize_e4m3_per_head(x):
+    """Per-head fp32 absmax scale (amax/448) and e4m3 values, (B,L,H,D)."""
+    amax = x.float().abs().amax(dim=(0, 1, 3)).clamp_min(1e-12)
+    scale = (amax / 448.0).contiguous()
+    q8 = (x.float() / scale.view(1, 1, -1, 1)).to(torch.float8_e4m3fn)
+    return q8, scale
+
+
+@pytest.mark.parametrize("shape", [(1, 256, 256, 2, 2), (2, 4608, 4608, 3, 3), (1, 1000, 333, 4, 2)])
+def test_fp8_matches_sdpa_within_3e2(lib, shape):
+    from dgx_monarch_b200.ops import attention_fwd
+
+    b, lq, lk, h, hkv = shape
+    g = torch.Generator(device="cuda").manual_seed(3)
+    q = torch.randn(b, lq, h, 128, device="cuda", generator=g).bfloat16()
+    k = torch.randn(b, lk, hkv, 128, device="cuda", generator=g).bfloat16()
+    v = torch.randn(b, lk, hkv, 128, device="cuda", generator=g).bfloat16()
+    q8, qs = quantize_e4m3_per_head(q)
+    k8, ks = quantize_e4m3_per_head(k)
+    v8, vs = quantize_e4m3_per_head(v)
+    out, lse = attention_fwd(q8, k8, v8, q_descale=qs, k_descale=ks, v_descale=vs)
+    torch.cuda.synchronize()
+    # The contract: SDPA over the same e4m3 inputs (dequantized with their
+    # per-head scales) -- the kernel's own error, P quantization included.
+    deq = [x.float() * s.view(1, 1, -1, 1) for x, s in ((q8, qs), (k8, ks), (v8, vs))]
+    ref, ref_lse = reference_attention(*deq)
+    assert out.dtype == torch.bfloat16
+    assert rel_l2(out, ref) <= FP8_REL_L2
+    assert (lse - ref_lse).abs().max().item() <= 5 * LSE_ABS
+    # Against the unquantized bf16 activations the input quantization adds
+    # about 5% for N(0,1) data (3 mantissa bits on q, k and v).
+    ref_bf16, _ = reference_attention(q, k, v)
+    assert rel_l2(out, ref_bf16) <= 8e-2
+
+
+def test_lse_merge_reconstructs_full_attention(lib):
+    """Attention over four key blocks, merged, equals attention over all keys."""
+    from dgx_monarch_b200.ops import attention_fwd, lse_merge
+
+    g = torch.Generator(device="cuda").manual_seed(4)
+    q = torch.randn(1, 1000, 3, 128, device="cuda", generator=g).bfloat16()
+    k = torch.randn(1, 4 * 384, 3, 128, device="cuda", generator=g).bfloat16()
+    v = torch.randn(1, 4 * 384, 3, 128, device="cuda", generator=g).bfloat16()
+    parts = [attention_fwd(q, k[:, i * 384:(i + 1) * 384].contiguous(),
+                           v[:, i * 384:(i + 1) * 384].contiguous(), out_dtype=torch.float32)
+             for i in range(4)]
+    out, lse = lse_merge([p[0] for p in parts], [p[1] for p in parts])
+    torch.cuda.synchronize()
+    ref, ref_lse = reference_attention(q, k, v)
+    assert rel_l2(out, ref) <= BF16_REL_L2
+    assert (lse - ref_lse).abs().max().item() <= LSE_ABS
+
+
+def test_invalid_arguments_raise_before_launch(lib):
+    from dgx_monarch_b200._lib import DgxmError
+    from dgx_monarch_b200.ops import attention_fwd
+
+    q = torch.randn(1, 64, 2, 64, device="cuda").bfloat16()
+    with pytest.raises(DgxmError, match="head_dim"):
+        attention_fwd(q, q, q)
+    q = torch.randn(1, 64, 3, 128, device="cuda").bfloat16()
+    k = torch.randn(1, 64, 2, 128, device="cuda").bfloat16()
+    with pytest.raises(DgxmError, match="divisible"):
+        attention_fwd(q, k, k)
