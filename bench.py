@@ -1,0 +1,315 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 sequence-parallel attention path.
+
+Workload (one "step"): the Wan-style video DiT self-attention layer --
+75,600 tokens (1280x720, 81 frames -> 21x90x160 latent, (1,2,2) patches),
+40 heads x 128, bf16, non-causal, Q/K/V ~ N(0,1) seeded.  At N GPUs it runs
+as Ulysses-N: each rank holds 75,600/N tokens of all 40 heads, the sequence->
+head all-to-all hands every rank 40/N heads of the whole sequence, the rank
+attends them, and the inverse all-to-all returns its own rows.
+
+Metric: attention TFLOP/s for the whole job (4*B*H*S*S*D per step divided by
+the max over ranks of the device time), plus tokens/s of the layer.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 is launched with torch.distributed.run (one process per GPU).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "attn TFLOP/s + DiT-layer tokens/s at 1/2/4/8 B200; % of roofline"
+SEQ, HEADS, DIM, BATCH = 75600, 40, 128, 1
+WORKLOAD = ("Wan-style video DiT self-attention: 75,600 tokens (21x90x160 latent, (1,2,2) "
+            "patches), 40 heads x 128, bf16, non-causal, Q/K/V ~ N(0,1)")
+
+
+def attn_flops(b=BATCH, h=HEADS, s=SEQ, d=DIM) -> float:
+    return 4.0 * b * h * s * s * d
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--cpu-budget", type=float, default=12.0,
+                   help="seconds of CPU work for the CPU baseline sample")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+# ----------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples of this GPU's clocks during the timed region."""
+
+    FIELDS = ("pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, bus_id: str) -> None:
+        self.bus_id = bus_id.lower()
+        self.rows: list[list[str]] = []
+        self.proc = None
+        self.thread = None
+
+    def start(self) -> None:
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self) -> None:
+        for line in self.proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9 and parts[0].lower().endswith(self.bus_id[-12:]):
+                self.rows.append(parts)
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=5)
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        loaded = [s for s in sm if s > 0.5 * (max(mx) if mx else 1)] or sm
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            for name, val in zip(names, r[5:9]):
+                if val.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(loaded) if loaded else None,
+                "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(self.rows)}
+
+
+def bus_id_of(device_index: int) -> str:
+    import torch
+
+    p = torch.cuda.get_device_properties(device_index)
+    return f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+
+
+# ----------------------------------------------------------------- peaks / traffic
+def measured_peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        d = json.loads(path.read_text())
+        return {"bf16_tflops": d["bf16_tflops"], "bf16_sustained": d["bf16_tflops_sustained"],
+                "hbm_gbs": d["hbm_gbs"], "source": "measured"}
+    return {"bf16_tflops": 1590.0, "bf16_sustained": 1400.0, "hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def profiled_traffic(kernel: str, workload: str):
+    """DRAM bytes per launch from the committed ncu summary, if one exists."""
+    path = ROOT / "profiles" / "traffic.json"
+    if not path.exists():
+        return None
+    table = json.loads(path.read_text())
+    entry = table.get(f"{kernel}:{workload}")
+    return None if entry is None else entry.get("bytes_per_launch")
+
+
+# ----------------------------------------------------------------- reference arm
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle.cpu_baseline import time_sdpa_sample
+
+    budget = max(3.0, min(args.cpu_budget, 60.0 / max(1, args.steps + args.warmup)))
+    samples = []
+    for i in range(args.warmup + args.steps):
+        r = time_sdpa_sample(SEQ, HEADS // args.gpus, DIM, budget_s=budget, seed=i)
+        if i >= args.warmup:
+            samples.append(r)
+    value = statistics.mean(s["value"] for s in samples)
+    # Whole-job time for the workload at the sampled rate.
+    ms = attn_flops() / (value * 1e12) * 1e3
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": WORKLOAD, "seq_len": SEQ, "heads": HEADS, "head_dim": DIM,
+                   "batch": BATCH, "parallelism": f"ulysses{args.gpus}"},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": samples[-1]["cores"],
+                         "kind": "port", "sample": samples[-1]["sample"]},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------- our arm
+def main() -> None:
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be at least 3")
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+
+    from dgx_monarch_b200 import _lib
+    from dgx_monarch_b200.ulysses import UlyssesAttention
+
+    if SEQ % world or HEADS % world:
+        raise SystemExit(f"{world} GPUs do not tile {SEQ} tokens x {HEADS} heads")
+    ls = SEQ // world
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    q, k, v = (torch.randn(BATCH, ls, HEADS, DIM, device=dev, generator=g, dtype=torch.bfloat16)
+               for _ in range(3))
+    uly = UlyssesAttention(world=world, rank=rank, batch=BATCH, seq_local=ls, heads=HEADS,
+                           head_dim=DIM, device=dev)
+    out = torch.empty(BATCH, ls, HEADS, DIM, device=dev, dtype=torch.bfloat16)
+
+    def step():
+        uly.forward(q, k, v, out=out)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(bus_id_of(local_rank))
+    clocks.start()
+    time.sleep(0.3)
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    ms_local = e0.elapsed_time(e1) / args.steps
+    # The attention kernel alone, timed on its own stream (roofline numerator).
+    attn_ms_local = uly.time_attention_kernel(args.steps)
+    t = torch.tensor([ms_local, attn_ms_local], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, attn_ms = t.tolist()
+    launches = args.steps * uly.launches_per_step
+
+    # End to end through the public call with host buffers: pinned host Q/K/V in,
+    # output back to pinned host memory, every step.
+    hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
+    hout = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+
+    def e2e_step():
+        dq, dk, dv = (x.to(dev, non_blocking=True) for x in (hq, hk, hv))
+        uly.forward(dq, dk, dv, out=out)
+        hout.copy_(out, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    e2e_steps = max(2, args.steps // 2)
+    for _ in range(e2e_steps):
+        e2e_step()
+    f1.record(stream)
+    torch.cuda.synchronize()
+    te = torch.tensor([f0.elapsed_time(f1) / e2e_steps], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_ms = te.item()
+    dev_err = _lib.device_error()
+
+    if rank == 0:
+        peaks = measured_peaks()
+        flops = attn_flops()
+        value = flops / (ms * 1e-3) / 1e12
+        per_rank_flops = flops / world
+        achieved = per_rank_flops / (attn_ms * 1e-3) / 1e12
+        traffic = profiled_traffic("attn_fwd_bf16", f"s{SEQ}_h{HEADS // world}")
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": "TFLOP/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms,
+            "higher_is_better": True,
+            "scaling": "weak" if world == 1 else "strong",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (Q/K/V ~ N(0,1), seeded)",
+            "config": {"workload": WORKLOAD, "seq_len": SEQ, "heads": HEADS, "head_dim": DIM,
+                       "batch": BATCH, "parallelism": f"ulysses{world}",
+                       "l2": "inputs larger than L2 (Q/K/V 2.3 GB)"},
+            "tokens_per_s": BATCH * SEQ / (ms * 1e-3),
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
+                         "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
+                         "traffic": traffic, "peak_source": peaks["source"] + " burst bf16",
+                         "kernel": "attn_fwd_kernel<bf16>"},
+            "e2e": {"value": flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": 3 * q.numel() * q.element_size(),
+                    "d2h_bytes_per_step": out.numel() * out.element_size(),
+                    "ms_per_step": e2e_ms},
+            "gpu_launches": launches,
+            "clocks": clk,
+            "device_error": dev_err,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            from oracle.cpu_baseline import time_sdpa_sample
+
+            cpu = time_sdpa_sample(SEQ, HEADS, DIM, budget_s=args.cpu_budget)
+            line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "sample")}
+            line["cpu_baseline"]["kind"] = "port"
+        print(json.dumps(line), flush=True)
+    uly.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -56,6 +56,24 @@ class AttnDesc(ctypes.Structure):
     ]
 
 
+MAX_WORLD = 8
+IPC_HANDLE_BYTES = 64
+
+
+class A2ADesc(ctypes.Structure):
+    _fields_ = [
+        ("n_tensors", ctypes.c_int32),
+        ("world", ctypes.c_int32),
+        ("rank", ctypes.c_int32),
+        ("batch", ctypes.c_int32),
+        ("seq_local", ctypes.c_int32),
+        ("heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+        ("src_stride", (ctypes.c_int64 * 3) * 3),
+    ]
+
+
 # Every symbol include/dgxm_sp.h declares, with its ctypes signature.
 _P = ctypes.c_void_p
 _I32 = ctypes.c_int32
@@ -66,6 +84,20 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "dgxm_attn_fwd": (ctypes.c_int, [ctypes.POINTER(AttnDesc), _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "dgxm_lse_merge": (ctypes.c_int, [_I32, _I32, _I32, _I32, _I32, ctypes.POINTER(_P), _I32,
                                       ctypes.POINTER(_P), _P, _I32, _P, _P]),
+    "dgxm_comm_create": (ctypes.c_int, [_I32, _I32, ctypes.c_int64, ctypes.c_uint64,
+                                        ctypes.POINTER(_P)]),
+    "dgxm_comm_export": (ctypes.c_int, [_P, _P]),
+    "dgxm_comm_import": (ctypes.c_int, [_P, _P]),
+    "dgxm_comm_window": (ctypes.c_int, [_P, _I32, ctypes.POINTER(_P)]),
+    "dgxm_comm_bytes": (ctypes.c_int64, [_P]),
+    "dgxm_comm_generation": (ctypes.c_uint64, [_P]),
+    "dgxm_comm_barrier": (ctypes.c_int, [_P, _P]),
+    "dgxm_comm_destroy": (ctypes.c_int, [_P]),
+    "dgxm_ulysses_scatter": (ctypes.c_int, [ctypes.POINTER(A2ADesc), ctypes.POINTER(_P),
+                                            ctypes.POINTER(_P), _P]),
+    "dgxm_ulysses_gather": (ctypes.c_int, [ctypes.POINTER(A2ADesc), _P, ctypes.POINTER(_P), _P]),
+    "dgxm_attn_fwd_routed": (ctypes.c_int, [ctypes.POINTER(AttnDesc), _P, _P, _P, _P, _P, _P,
+                                            ctypes.POINTER(_P), _I32, _I32, _I32, _P, _P]),
 }
 
 _lock = threading.Lock()

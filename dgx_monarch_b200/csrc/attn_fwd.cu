@@ -76,6 +76,11 @@ struct __align__(64) AttnParams {
   int n_kv_tiles;
   float scale_log2;
   int flags;
+  // Fused inverse all-to-all: when o_rows > 0, query row i goes to
+  // o_peer[i / o_rows] at row i % o_rows and head o_head_off + h.
+  void* o_peer[DGXM_MAX_WORLD];
+  int o_rows;
+  int o_head_off;
 };
 
 // Barrier slots inside the control block.
@@ -396,9 +401,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
       const bool row_ok = grow < p.q_len;
       float inv = 1.f / (l_run * C::kPScale);
       if constexpr (FP8) inv *= p.v_descale[hk];
-      char* orow = static_cast<char*>(p.o) +
-                   (static_cast<int64_t>(b) * p.o_sb + static_cast<int64_t>(grow) * p.o_sl +
-                    static_cast<int64_t>(h) * p.o_sh) *
+      void* obase = p.o;
+      int orow_idx = grow;
+      int ohead = h;
+      if (p.o_rows > 0) {
+        const int peer = row_ok ? grow / p.o_rows : 0;
+        obase = p.o_peer[peer];
+        orow_idx = grow - peer * p.o_rows;
+        ohead = p.o_head_off + h;
+      }
+      char* orow = static_cast<char*>(obase) +
+                   (static_cast<int64_t>(b) * p.o_sb + static_cast<int64_t>(orow_idx) * p.o_sl +
+                    static_cast<int64_t>(ohead) * p.o_sh) *
                        (OUT_F32 ? 4 : 2);
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
@@ -464,10 +478,13 @@ static bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 1
 
 }  // namespace dgxm
 
-extern "C" int dgxm_attn_fwd(const dgxm_attn_desc* d, const void* q, const void* k, const void* v,
-                             const float* q_descale, const float* k_descale,
-                             const float* v_descale, void* o, float* lse, void* stream) {
-  using namespace dgxm;
+namespace dgxm {
+
+// Validate the descriptor and fill the kernel parameters (everything but
+// the output routing, which the caller sets).
+static int prepare_attn(const dgxm_attn_desc* d, const void* q, const void* k, const void* v,
+                        const float* q_descale, const float* k_descale, const float* v_descale,
+                        void* o, float* lse, AttnParams* out_prm, dim3* out_grid, bool* skip) {
   if (d == nullptr) return fail(DGXM_ERR_INVALID, "attention descriptor is NULL");
   if (d->batch < 0 || d->q_len < 0 || d->kv_len < 0 || d->q_heads <= 0 || d->kv_heads <= 0)
     return fail(DGXM_ERR_INVALID, "negative or zero attention extent (batch=%d q_len=%d kv_len=%d "
@@ -478,7 +495,11 @@ extern "C" int dgxm_attn_fwd(const dgxm_attn_desc* d, const void* q, const void*
   if (d->q_heads % d->kv_heads != 0)
     return fail(DGXM_ERR_INVALID, "query heads (%d) must be divisible by key/value heads (%d)",
                 d->q_heads, d->kv_heads);
-  if (d->batch == 0 || d->q_len == 0) return DGXM_OK;
+  *skip = false;
+  if (d->batch == 0 || d->q_len == 0) {
+    *skip = true;
+    return DGXM_OK;
+  }
   if (d->kv_len == 0)
     return fail(DGXM_ERR_INVALID, "attention over an empty key axis has no defined output");
   if (d->batch > 65535 || d->q_heads > 65535)
@@ -501,7 +522,7 @@ extern "C" int dgxm_attn_fwd(const dgxm_attn_desc* d, const void* q, const void*
       (d->o_stride[2] * out_bytes) % 16 != 0 || (d->o_stride[0] * out_bytes) % 16 != 0)
     return fail(DGXM_ERR_INVALID, "output base and strides must be 16-byte aligned");
 
-  AttnParams prm;
+  AttnParams& prm = *out_prm;
   memset(&prm, 0, sizeof(prm));
   const CUtensorMapDataType dt = fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const int eb = fp8 ? 1 : 2;
@@ -536,8 +557,55 @@ extern "C" int dgxm_attn_fwd(const dgxm_attn_desc* d, const void* q, const void*
   prm.scale_log2 = scale * kLog2e;
   prm.flags = d->flags;
 
-  dim3 grid((d->q_len + 2 * kTileRows - 1) / (2 * kTileRows), d->q_heads, d->batch);
+  *out_grid = dim3((d->q_len + 2 * kTileRows - 1) / (2 * kTileRows), d->q_heads, d->batch);
+  return DGXM_OK;
+}
+
+static int dispatch_attn(const dgxm_attn_desc* d, const AttnParams& prm, dim3 grid, void* stream) {
+  const bool fp8 = d->in_dtype == DGXM_DTYPE_E4M3;
+  const bool out_f32 = d->out_dtype == DGXM_DTYPE_F32;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (fp8) return out_f32 ? launch_attn<true, true>(prm, grid, st) : launch_attn<true, false>(prm, grid, st);
   return out_f32 ? launch_attn<false, true>(prm, grid, st) : launch_attn<false, false>(prm, grid, st);
+}
+
+}  // namespace dgxm
+
+extern "C" int dgxm_attn_fwd(const dgxm_attn_desc* d, const void* q, const void* k, const void* v,
+                             const float* q_descale, const float* k_descale,
+                             const float* v_descale, void* o, float* lse, void* stream) {
+  using namespace dgxm;
+  AttnParams prm;
+  dim3 grid;
+  bool skip = false;
+  int rc = prepare_attn(d, q, k, v, q_descale, k_descale, v_descale, o, lse, &prm, &grid, &skip);
+  if (rc != DGXM_OK || skip) return rc;
+  return dispatch_attn(d, prm, grid, stream);
+}
+
+extern "C" int dgxm_attn_fwd_routed(const dgxm_attn_desc* d, const void* q, const void* k,
+                                    const void* v, const float* q_descale, const float* k_descale,
+                                    const float* v_descale, void* const* o_peers, int32_t world,
+                                    int32_t rank, int32_t seq_local, float* lse, void* stream) {
+  using namespace dgxm;
+  if (o_peers == nullptr) return fail(DGXM_ERR_INVALID, "o_peers is NULL");
+  if (world < 1 || world > DGXM_MAX_WORLD || rank < 0 || rank >= world)
+    return fail(DGXM_ERR_INVALID, "rank %d / world %d out of range", rank, world);
+  if (d == nullptr) return fail(DGXM_ERR_INVALID, "attention descriptor is NULL");
+  if (seq_local <= 0 || static_cast<int64_t>(seq_local) * world != d->q_len)
+    return fail(DGXM_ERR_INVALID, "seq_local %d x world %d does not cover q_len %d", seq_local,
+                world, d->q_len);
+  for (int r = 0; r < world; ++r)
+    if (o_peers[r] == nullptr || reinterpret_cast<uintptr_t>(o_peers[r]) % 16)
+      return fail(DGXM_ERR_INVALID, "output peer %d is NULL or not 16-byte aligned", r);
+  AttnParams prm;
+  dim3 grid;
+  bool skip = false;
+  int rc = prepare_attn(d, q, k, v, q_descale, k_descale, v_descale, o_peers[0], lse, &prm,
+                        &grid, &skip);
+  if (rc != DGXM_OK || skip) return rc;
+  for (int r = 0; r < world; ++r) prm.o_peer[r] = o_peers[r];
+  prm.o_rows = seq_local;
+  prm.o_head_off = rank * d->q_heads;
+  return dispatch_attn(d, prm, grid, stream);
 }

@@ -1,0 +1,354 @@
+// Peer windows over NVLink, the Ulysses all-to-all as direct peer stores, and
+// a bounded device-side barrier.
+//
+// Each rank cudaMallocs one window in its own HBM and exports a CUDA IPC
+// handle; every other rank maps it (plain peer mapping, no multicast object),
+// so a kernel on rank s can store straight into rank r's window over NVLink.
+// The first 4 KB of a window hold barrier flags: slot i is written by rank i.
+//
+// Replaces yunchang's SeqAllToAll4D (reached from adapters/usp_full_axis.py:
+// 27-29,40 and inside xfuser's USP call at adapters/base.py:320), which the
+// reference runs as an NCCL all_to_all plus permute copies.
+#include "common.h"
+#include "device_error.cuh"
+#include "ptx.cuh"
+
+struct dgxm_comm {
+  int rank;
+  int world;
+  int device;
+  uint64_t generation;
+  int64_t bytes;       // usable bytes after the flag area
+  char* local;         // this rank's window base (cudaMalloc)
+  char* peers[DGXM_MAX_WORLD];  // window bases as seen by this process
+  bool opened[DGXM_MAX_WORLD];
+  uint32_t epoch;      // barriers issued so far
+};
+
+namespace dgxm {
+
+constexpr int64_t kFlagBytes = 4096;
+
+// ------------------------------------------------------------------ barrier
+struct BarrierParams {
+  int* peer_flags[DGXM_MAX_WORLD];  // flag area of each rank's window
+  int* my_flags;
+  int rank, world;
+  int epoch;
+};
+
+__global__ void comm_barrier_kernel(const __grid_constant__ BarrierParams p) {
+  const int i = threadIdx.x;
+  if (i >= p.world) return;
+  // Everything this rank wrote before this kernel (earlier kernels in the
+  // stream) is performed before the flag below becomes visible.
+  __threadfence_system();
+  int* slot = p.peer_flags[i] + p.rank;
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(slot), "r"(p.epoch) : "memory");
+  const int* mine = p.my_flags + i;
+  const long long start = clock64();
+  while (true) {
+    int seen;
+    asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(seen) : "l"(mine) : "memory");
+    if (seen - p.epoch >= 0) break;  // wrap-safe monotonic compare
+    if (clock64() - start > kWaitBudgetCycles) {
+      report_device_error(kErrPeerTimeout);
+      break;
+    }
+    __nanosleep(64);
+  }
+  __threadfence_system();
+}
+
+// ------------------------------------------------------------------ all-to-all
+struct ScatterParams {
+  const char* src[3];                      // (B, Ls, H, D) per tensor
+  char* dst[3][DGXM_MAX_WORLD];            // (B, world*Ls, H/world, D) on each rank
+  int64_t s_sb[3], s_sl[3], s_sh[3];       // source strides, bytes
+  int n_tensors, world, rank;
+  int batch, seq_local, heads, head_bytes; // head_bytes = D * elt
+};
+
+// Sequence -> head: this rank's rows, head slice of rank r -> rank r's
+// gathered axis at rows [rank*Ls, (rank+1)*Ls).  One thread moves 16 bytes;
+// a warp moves two consecutive 256-byte head rows, so loads and peer stores
+// are both coalesced.
+__global__ void __launch_bounds__(256) ulysses_scatter_kernel(const __grid_constant__ ScatterParams p) {
+  const int chunks_per_head = p.head_bytes / 16;
+  const int hl = p.heads / p.world;
+  const int64_t per_tensor = static_cast<int64_t>(p.batch) * p.seq_local * p.heads * chunks_per_head;
+  const int64_t total = per_tensor * p.n_tensors;
+  const int64_t seq_full = static_cast<int64_t>(p.seq_local) * p.world;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int t = static_cast<int>(i / per_tensor);
+    int64_t rem = i - t * per_tensor;
+    const int part = static_cast<int>(rem % chunks_per_head);
+    rem /= chunks_per_head;
+    const int h = static_cast<int>(rem % p.heads);
+    rem /= p.heads;
+    const int l = static_cast<int>(rem % p.seq_local);
+    const int b = static_cast<int>(rem / p.seq_local);
+    const uint4 val = __ldg(reinterpret_cast<const uint4*>(
+        p.src[t] + b * p.s_sb[t] + l * p.s_sl[t] + h * p.s_sh[t]) + part);
+    const int r = h / hl;
+    const int hh = h - r * hl;
+    const int64_t row = static_cast<int64_t>(b) * seq_full + static_cast<int64_t>(p.rank) * p.seq_local + l;
+    char* dst = p.dst[t][r] + (row * hl + hh) * p.head_bytes;
+    reinterpret_cast<uint4*>(dst)[part] = val;
+  }
+}
+
+// Head -> sequence (the inverse): this rank's (B, S, Hl, D) rows go back to
+// the rank owning each sequence chunk, into head slice [rank*Hl, (rank+1)*Hl)
+// of its (B, Ls, H, D) tensor.
+struct GatherParams {
+  const char* src;                     // (B, S, Hl, D), strides below
+  char* dst[DGXM_MAX_WORLD];           // (B, Ls, H, D) contiguous on each rank
+  int64_t s_sb, s_sl, s_sh;
+  int world, rank;
+  int batch, seq_local, heads, head_bytes;
+};
+
+__global__ void __launch_bounds__(256) ulysses_gather_kernel(const __grid_constant__ GatherParams p) {
+  const int chunks_per_head = p.head_bytes / 16;
+  const int hl = p.heads / p.world;
+  const int64_t seq_full = static_cast<int64_t>(p.seq_local) * p.world;
+  const int64_t total = static_cast<int64_t>(p.batch) * seq_full * hl * chunks_per_head;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    int64_t rem = i;
+    const int part = static_cast<int>(rem % chunks_per_head);
+    rem /= chunks_per_head;
+    const int hh = static_cast<int>(rem % hl);
+    rem /= hl;
+    const int64_t l = rem % seq_full;
+    const int b = static_cast<int>(rem / seq_full);
+    const uint4 val = __ldg(reinterpret_cast<const uint4*>(p.src + b * p.s_sb + l * p.s_sl + hh * p.s_sh) + part);
+    const int r = static_cast<int>(l / p.seq_local);
+    const int64_t lr = l - static_cast<int64_t>(r) * p.seq_local;
+    const int64_t row = static_cast<int64_t>(b) * p.seq_local + lr;
+    char* dst = p.dst[r] + (row * p.heads + static_cast<int64_t>(p.rank) * hl + hh) * p.head_bytes;
+    reinterpret_cast<uint4*>(dst)[part] = val;
+  }
+}
+
+static int grid_for(int64_t work_items, int threads) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t want = (work_items + threads - 1) / threads;
+  const int64_t cap = static_cast<int64_t>(sms) * 8;
+  return static_cast<int>(want < cap ? (want > 0 ? want : 1) : cap);
+}
+
+static int elt_bytes(int dtype) {
+  switch (dtype) {
+    case DGXM_DTYPE_BF16:
+    case DGXM_DTYPE_F16: return 2;
+    case DGXM_DTYPE_E4M3: return 1;
+    case DGXM_DTYPE_F32: return 4;
+    default: return 0;
+  }
+}
+
+}  // namespace dgxm
+
+// ------------------------------------------------------------------ C ABI
+extern "C" int dgxm_comm_create(int32_t rank, int32_t world, int64_t bytes, uint64_t generation,
+                                dgxm_comm** out) {
+  using namespace dgxm;
+  if (out == nullptr) return fail(DGXM_ERR_INVALID, "out handle pointer is NULL");
+  *out = nullptr;
+  if (world < 1 || world > DGXM_MAX_WORLD || rank < 0 || rank >= world)
+    return fail(DGXM_ERR_INVALID, "rank %d / world %d out of range (world <= %d)", rank, world,
+                DGXM_MAX_WORLD);
+  if (bytes < 0) return fail(DGXM_ERR_INVALID, "window size %lld is negative", (long long)bytes);
+  dgxm_comm* c = new dgxm_comm();
+  memset(c, 0, sizeof(*c));
+  c->rank = rank;
+  c->world = world;
+  c->generation = generation;
+  c->bytes = (bytes + 255) / 256 * 256;
+  cudaError_t e = cudaGetDevice(&c->device);
+  if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&c->local), kFlagBytes + c->bytes);
+  if (e == cudaSuccess) e = cudaMemset(c->local, 0, kFlagBytes);
+  if (e != cudaSuccess) {
+    if (c->local) cudaFree(c->local);
+    delete c;
+    return cuda_fail(e, "dgxm_comm_create window allocation");
+  }
+  c->peers[rank] = c->local;
+  c->opened[rank] = false;
+  *out = c;
+  return DGXM_OK;
+}
+
+extern "C" int dgxm_comm_export(dgxm_comm* c, void* handle) {
+  using namespace dgxm;
+  if (c == nullptr || handle == nullptr) return fail(DGXM_ERR_INVALID, "NULL comm or handle buffer");
+  cudaIpcMemHandle_t h;
+  DGXM_CUDA_TRY(cudaIpcGetMemHandle(&h, c->local));
+  memcpy(handle, &h, sizeof(h));
+  return DGXM_OK;
+}
+
+extern "C" int dgxm_comm_import(dgxm_comm* c, const void* handles) {
+  using namespace dgxm;
+  if (c == nullptr || handles == nullptr) return fail(DGXM_ERR_INVALID, "NULL comm or handles");
+  for (int r = 0; r < c->world; ++r) {
+    if (r == c->rank || c->opened[r]) continue;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, static_cast<const char*>(handles) + r * DGXM_IPC_HANDLE_BYTES, sizeof(h));
+    void* p = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+    c->peers[r] = static_cast<char*>(p);
+    c->opened[r] = true;
+  }
+  return DGXM_OK;
+}
+
+extern "C" int dgxm_comm_window(dgxm_comm* c, int32_t peer, void** ptr) {
+  using namespace dgxm;
+  if (c == nullptr || ptr == nullptr) return fail(DGXM_ERR_INVALID, "NULL comm or output pointer");
+  if (peer < 0 || peer >= c->world) return fail(DGXM_ERR_INVALID, "peer %d out of range", peer);
+  if (c->peers[peer] == nullptr)
+    return fail(DGXM_ERR_STATE, "peer %d window is not mapped (call dgxm_comm_import)", peer);
+  *ptr = c->peers[peer] + kFlagBytes;
+  return DGXM_OK;
+}
+
+extern "C" int64_t dgxm_comm_bytes(dgxm_comm* c) { return c == nullptr ? -1 : c->bytes; }
+
+extern "C" uint64_t dgxm_comm_generation(dgxm_comm* c) { return c == nullptr ? 0 : c->generation; }
+
+extern "C" int dgxm_comm_barrier(dgxm_comm* c, void* stream) {
+  using namespace dgxm;
+  if (c == nullptr) return fail(DGXM_ERR_INVALID, "NULL comm");
+  if (c->world == 1) return DGXM_OK;
+  BarrierParams p;
+  memset(&p, 0, sizeof(p));
+  for (int r = 0; r < c->world; ++r) {
+    if (c->peers[r] == nullptr)
+      return fail(DGXM_ERR_STATE, "peer %d window is not mapped (call dgxm_comm_import)", r);
+    p.peer_flags[r] = reinterpret_cast<int*>(c->peers[r]);
+  }
+  p.my_flags = reinterpret_cast<int*>(c->local);
+  p.rank = c->rank;
+  p.world = c->world;
+  c->epoch += 1;
+  p.epoch = static_cast<int>(c->epoch);
+  comm_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  DGXM_CUDA_TRY(cudaGetLastError());
+  return DGXM_OK;
+}
+
+extern "C" int dgxm_comm_destroy(dgxm_comm* c) {
+  using namespace dgxm;
+  if (c == nullptr) return DGXM_OK;
+  int prev = -1;
+  cudaGetDevice(&prev);
+  cudaSetDevice(c->device);
+  cudaDeviceSynchronize();
+  for (int r = 0; r < c->world; ++r)
+    if (c->opened[r]) cudaIpcCloseMemHandle(c->peers[r]);
+  cudaError_t e = cudaFree(c->local);
+  if (prev >= 0) cudaSetDevice(prev);
+  delete c;
+  if (e != cudaSuccess) return cuda_fail(e, "dgxm_comm_destroy cudaFree");
+  return DGXM_OK;
+}
+
+extern "C" int dgxm_ulysses_scatter(const dgxm_a2a_desc* d, const void* const* src,
+                                    void* const* dst, void* stream) {
+  using namespace dgxm;
+  if (d == nullptr || src == nullptr || dst == nullptr)
+    return fail(DGXM_ERR_INVALID, "NULL all-to-all argument");
+  if (d->n_tensors < 1 || d->n_tensors > 3)
+    return fail(DGXM_ERR_INVALID, "all-to-all moves 1..3 tensors, got %d", d->n_tensors);
+  if (d->world < 1 || d->world > DGXM_MAX_WORLD || d->rank < 0 || d->rank >= d->world)
+    return fail(DGXM_ERR_INVALID, "rank %d / world %d out of range", d->rank, d->world);
+  if (d->heads <= 0 || d->heads % d->world)
+    return fail(DGXM_ERR_INVALID, "%d heads are not divisible by the Ulysses degree %d", d->heads,
+                d->world);
+  const int eb = elt_bytes(d->dtype);
+  if (eb == 0) return fail(DGXM_ERR_UNSUPPORTED, "dtype %d is not supported", d->dtype);
+  const int head_bytes = d->head_dim * eb;
+  if (d->head_dim <= 0 || head_bytes % 16)
+    return fail(DGXM_ERR_INVALID, "head row of %d bytes is not a multiple of 16", head_bytes);
+  if (d->batch < 0 || d->seq_local < 0)
+    return fail(DGXM_ERR_INVALID, "negative batch or sequence length");
+  if (d->batch == 0 || d->seq_local == 0) return DGXM_OK;
+  ScatterParams p;
+  memset(&p, 0, sizeof(p));
+  for (int t = 0; t < d->n_tensors; ++t) {
+    if (src[t] == nullptr || reinterpret_cast<uintptr_t>(src[t]) % 16)
+      return fail(DGXM_ERR_INVALID, "source tensor %d is NULL or not 16-byte aligned", t);
+    p.src[t] = static_cast<const char*>(src[t]);
+    p.s_sb[t] = d->src_stride[t][0] * eb;
+    p.s_sl[t] = d->src_stride[t][1] * eb;
+    p.s_sh[t] = d->src_stride[t][2] * eb;
+    if (p.s_sb[t] % 16 || p.s_sl[t] % 16 || p.s_sh[t] % 16)
+      return fail(DGXM_ERR_INVALID, "source tensor %d strides are not 16-byte multiples", t);
+    for (int r = 0; r < d->world; ++r) {
+      void* q = dst[t * d->world + r];
+      if (q == nullptr || reinterpret_cast<uintptr_t>(q) % 16)
+        return fail(DGXM_ERR_INVALID, "destination %d of tensor %d is NULL or misaligned", r, t);
+      p.dst[t][r] = static_cast<char*>(q);
+    }
+  }
+  p.n_tensors = d->n_tensors;
+  p.world = d->world;
+  p.rank = d->rank;
+  p.batch = d->batch;
+  p.seq_local = d->seq_local;
+  p.heads = d->heads;
+  p.head_bytes = head_bytes;
+  const int64_t work = static_cast<int64_t>(d->n_tensors) * d->batch * d->seq_local * d->heads * (head_bytes / 16);
+  ulysses_scatter_kernel<<<grid_for(work, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  DGXM_CUDA_TRY(cudaGetLastError());
+  return DGXM_OK;
+}
+
+extern "C" int dgxm_ulysses_gather(const dgxm_a2a_desc* d, const void* src, void* const* dst,
+                                   void* stream) {
+  using namespace dgxm;
+  if (d == nullptr || src == nullptr || dst == nullptr)
+    return fail(DGXM_ERR_INVALID, "NULL all-to-all argument");
+  if (d->world < 1 || d->world > DGXM_MAX_WORLD || d->rank < 0 || d->rank >= d->world)
+    return fail(DGXM_ERR_INVALID, "rank %d / world %d out of range", d->rank, d->world);
+  if (d->heads <= 0 || d->heads % d->world)
+    return fail(DGXM_ERR_INVALID, "%d heads are not divisible by the Ulysses degree %d", d->heads,
+                d->world);
+  const int eb = elt_bytes(d->dtype);
+  if (eb == 0) return fail(DGXM_ERR_UNSUPPORTED, "dtype %d is not supported", d->dtype);
+  const int head_bytes = d->head_dim * eb;
+  if (d->head_dim <= 0 || head_bytes % 16)
+    return fail(DGXM_ERR_INVALID, "head row of %d bytes is not a multiple of 16", head_bytes);
+  if (d->batch == 0 || d->seq_local == 0) return DGXM_OK;
+  GatherParams p;
+  memset(&p, 0, sizeof(p));
+  if (reinterpret_cast<uintptr_t>(src) % 16) return fail(DGXM_ERR_INVALID, "source misaligned");
+  p.src = static_cast<const char*>(src);
+  p.s_sb = d->src_stride[0][0] * eb;
+  p.s_sl = d->src_stride[0][1] * eb;
+  p.s_sh = d->src_stride[0][2] * eb;
+  if (p.s_sb % 16 || p.s_sl % 16 || p.s_sh % 16)
+    return fail(DGXM_ERR_INVALID, "source strides are not 16-byte multiples");
+  for (int r = 0; r < d->world; ++r) {
+    if (dst[r] == nullptr || reinterpret_cast<uintptr_t>(dst[r]) % 16)
+      return fail(DGXM_ERR_INVALID, "destination %d is NULL or misaligned", r);
+    p.dst[r] = static_cast<char*>(dst[r]);
+  }
+  p.world = d->world;
+  p.rank = d->rank;
+  p.batch = d->batch;
+  p.seq_local = d->seq_local;
+  p.heads = d->heads;
+  p.head_bytes = head_bytes;
+  const int64_t work = static_cast<int64_t>(d->batch) * d->seq_local * d->heads * (head_bytes / 16);
+  ulysses_gather_kernel<<<grid_for(work, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  DGXM_CUDA_TRY(cudaGetLastError());
+  return DGXM_OK;
+}

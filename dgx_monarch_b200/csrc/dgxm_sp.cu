@@ -7,3 +7,4 @@
 #include "capi.cu"
 #include "attn_fwd.cu"
 #include "lse_merge.cu"
+#include "comm.cu"

@@ -1,0 +1,169 @@
+"""Ulysses sequence-parallel attention on NVLink peer windows.
+
+One step, per rank (P ranks, local rows Ls = S/P, local heads Hl = H/P):
+  1. dgxm_ulysses_scatter: this rank's (B, Ls, H, D) q/k/v rows are stored
+     head-slice by head-slice straight into every peer's receive tensors
+     (B, S, Hl, D) -- the rank-major gathered axis of yunchang's
+     SeqAllToAll4D(pg, x, 2, 1) (adapters/usp_full_axis.py:27-29);
+  2. dgxm_comm_barrier;
+  3. dgxm_attn_fwd_routed: attention over the whole axis for the local heads,
+     whose epilogue stores each output row into the (B, Ls, H, D) output of
+     the rank owning that row -- the inverse SeqAllToAll4D(pg, out, 1, 2)
+     (adapters/usp_full_axis.py:40) with no separate kernel;
+  4. dgxm_comm_barrier.
+At P = 1 the step is the attention kernel alone.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from . import _lib
+from .comm import PeerWindows
+from .ops import _dtype_code, _ptr, attention_fwd
+
+
+def a2a_desc(n_tensors, world, rank, batch, seq_local, heads, head_dim, dtype, strides):
+    d = _lib.A2ADesc()
+    d.n_tensors, d.world, d.rank = n_tensors, world, rank
+    d.batch, d.seq_local, d.heads, d.head_dim = batch, seq_local, heads, head_dim
+    d.dtype = _dtype_code(dtype)
+    for t, st in enumerate(strides):
+        d.src_stride[t][0], d.src_stride[t][1], d.src_stride[t][2] = st
+    return d
+
+
+def ulysses_scatter(tensors: list[torch.Tensor], dst_ptrs: list[list[int]], *, world: int,
+                    rank: int, stream=None) -> None:
+    """Store head slices of this rank's (B, Ls, H, D) tensors into dst_ptrs[t][r]."""
+    b, ls, h, d = tensors[0].shape
+    for t in tensors:
+        if t.shape != tensors[0].shape or t.dtype != tensors[0].dtype or t.stride(3) != 1:
+            raise ValueError("all-to-all tensors must share shape/dtype with contiguous head_dim")
+    desc = a2a_desc(len(tensors), world, rank, b, ls, h, d, tensors[0].dtype,
+                    [(t.stride(0), t.stride(1), t.stride(2)) for t in tensors])
+    n = len(tensors)
+    src = (ctypes.c_void_p * n)(*[t.data_ptr() for t in tensors])
+    dst = (ctypes.c_void_p * (n * world))(*[p for row in dst_ptrs for p in row])
+    stream = stream or torch.cuda.current_stream(tensors[0].device)
+    _lib.check(_lib.load().dgxm_ulysses_scatter(ctypes.byref(desc), src, dst, stream.cuda_stream),
+               "dgxm_ulysses_scatter")
+
+
+def ulysses_gather(src: torch.Tensor, dst_ptrs: list[int], *, world: int, rank: int,
+                   seq_local: int, heads: int, stream=None) -> None:
+    """Return (B, S, Hl, D) rows to the owning ranks' (B, Ls, H, D) tensors."""
+    b, s, hl, d = src.shape
+    if s != seq_local * world or hl * world != heads or src.stride(3) != 1:
+        raise ValueError("gather source must be (B, world*seq_local, heads/world, D)")
+    desc = a2a_desc(1, world, rank, b, seq_local, heads, d, src.dtype,
+                    [(src.stride(0), src.stride(1), src.stride(2))])
+    dst = (ctypes.c_void_p * world)(*dst_ptrs)
+    stream = stream or torch.cuda.current_stream(src.device)
+    _lib.check(_lib.load().dgxm_ulysses_gather(ctypes.byref(desc), src.data_ptr(), dst,
+                                               stream.cuda_stream), "dgxm_ulysses_gather")
+
+
+def attention_routed(q, k, v, out_ptrs: list[int], out_strides, *, world: int, rank: int,
+                     seq_local: int, lse: torch.Tensor | None = None, softmax_scale=None,
+                     q_descale=None, k_descale=None, v_descale=None, stream=None) -> None:
+    """Attention whose epilogue writes row i to rank i // seq_local's output."""
+    b, lq, hl, d = q.shape
+    _, lk, hkv, _ = k.shape
+    desc = _lib.AttnDesc()
+    desc.batch, desc.q_len, desc.kv_len = b, lq, lk
+    desc.q_heads, desc.kv_heads, desc.head_dim = hl, hkv, d
+    desc.in_dtype = _dtype_code(q.dtype)
+    desc.out_dtype = _lib.DTYPE_BF16
+    desc.q_stride[:] = [q.stride(0), q.stride(1), q.stride(2)]
+    desc.k_stride[:] = [k.stride(0), k.stride(1), k.stride(2)]
+    desc.v_stride[:] = [v.stride(0), v.stride(1), v.stride(2)]
+    desc.o_stride[:] = list(out_strides)
+    if lse is not None:
+        desc.lse_stride[:] = [lse.stride(0), lse.stride(1), lse.stride(2)]
+    desc.softmax_scale = float(softmax_scale) if softmax_scale else 1.0 / math.sqrt(d)
+    peers = (ctypes.c_void_p * world)(*out_ptrs)
+    stream = stream or torch.cuda.current_stream(q.device)
+    _lib.check(_lib.load().dgxm_attn_fwd_routed(
+        ctypes.byref(desc), q.data_ptr(), k.data_ptr(), v.data_ptr(), _ptr(q_descale),
+        _ptr(k_descale), _ptr(v_descale), peers, world, rank, seq_local, _ptr(lse),
+        stream.cuda_stream), "dgxm_attn_fwd_routed")
+
+
+class UlyssesAttention:
+    """Ulysses-P attention for fixed (B, Ls, H, D) bf16 shapes on one rank."""
+
+    def __init__(self, *, world: int, rank: int, batch: int, seq_local: int, heads: int,
+                 head_dim: int, device: torch.device, group=None, generation: int = 0,
+                 dtype: torch.dtype = torch.bfloat16) -> None:
+        if heads % world:
+            raise ValueError(f"{heads} heads do not divide the Ulysses degree {world}")
+        self.world, self.rank, self.device = world, rank, device
+        self.b, self.ls, self.h, self.d = batch, seq_local, heads, head_dim
+        self.hl = heads // world
+        self.s = seq_local * world
+        self.dtype = dtype
+        self.windows = None
+        if world == 1:
+            self.launches_per_step = 1
+            return
+        elt = torch.empty((), dtype=dtype).element_size()
+        recv_bytes = batch * self.s * self.hl * head_dim * elt
+        out_bytes = batch * seq_local * heads * head_dim * elt
+        self.windows = PeerWindows(3 * recv_bytes + out_bytes + 4 * 256, device=device, group=group,
+                                   rank=rank, world=world, generation=generation)
+        self.off_recv = [self.windows.carve(recv_bytes) for _ in range(3)]
+        self.off_out = self.windows.carve(out_bytes)
+        self.recv = [self.windows.local_tensor(o, (batch, self.s, self.hl, head_dim), dtype)
+                     for o in self.off_recv]
+        self.out_local = self.windows.local_tensor(self.off_out, (batch, seq_local, heads, head_dim), dtype)
+        self.out_strides = (seq_local * heads * head_dim, heads * head_dim, head_dim)
+        self.lse = torch.empty(batch, self.hl, self.s, device=device, dtype=torch.float32)
+        self.launches_per_step = 4
+
+    def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+        if self.world == 1:
+            res, _ = attention_fwd(q, k, v, out=out, return_lse=False)
+            return res
+        w = self.windows
+        ulysses_scatter([q, k, v], [[w.peer_ptr(r, off) for r in range(self.world)]
+                                    for off in self.off_recv], world=self.world, rank=self.rank)
+        w.barrier()
+        attention_routed(self.recv[0], self.recv[1], self.recv[2],
+                         [w.peer_ptr(r, self.off_out) for r in range(self.world)], self.out_strides,
+                         world=self.world, rank=self.rank, seq_local=self.ls, lse=self.lse)
+        w.barrier()
+        if out is None:
+            return self.out_local
+        out.copy_(self.out_local)
+        return out
+
+    def time_attention_kernel(self, steps: int) -> float:
+        """Mean ms of the attention kernel alone over this rank's full-axis heads."""
+        if self.world == 1:
+            g = torch.Generator(device=self.device).manual_seed(7)
+            q, k, v = (torch.randn(self.b, self.s, self.h, self.d, device=self.device, generator=g,
+                                   dtype=self.dtype) for _ in range(3))
+        else:
+            q, k, v = self.recv
+        out = torch.empty(q.shape, device=self.device, dtype=self.dtype)
+        for _ in range(2):
+            attention_fwd(q, k, v, out=out, return_lse=False)
+        stream = torch.cuda.current_stream(self.device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(steps):
+            attention_fwd(q, k, v, out=out, return_lse=False)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    def close(self) -> None:
+        if self.windows is not None:
+            torch.cuda.synchronize(self.device)
+            self.windows.close()
+            self.windows = None

@@ -110,6 +110,92 @@ int dgxm_lse_merge(int32_t batch, int32_t rows, int32_t heads, int32_t head_dim,
                    const float* const* parts_lse, void* out, int32_t out_dtype, float* lse_out,
                    void* stream);
 
+/* ------------------------------------------------------------ communicator */
+#define DGXM_MAX_WORLD 8
+#define DGXM_IPC_HANDLE_BYTES 64
+
+/* One rank's NVLink window: device memory on the current device that every
+ * peer maps through a CUDA IPC handle (a plain peer mapping; no multicast
+ * object is created).  Bound to one setup generation: a handle from a retired
+ * generation is destroyed, never reused.
+ *
+ * Stands in for the process groups the reference builds in
+ * actor/worker_env.py:313-327 (init_process_group("nccl") + xfuser
+ * initialize_model_parallel) as far as the data path needs them; bootstrap
+ * (handle exchange) still rides torch.distributed. */
+typedef struct dgxm_comm dgxm_comm;
+
+/* Allocate `bytes` (plus a 4 KB flag area) on the current device. */
+int dgxm_comm_create(int32_t rank, int32_t world, int64_t bytes, uint64_t generation,
+                     dgxm_comm** out);
+/* Write this rank's DGXM_IPC_HANDLE_BYTES-byte window handle into `handle`. */
+int dgxm_comm_export(dgxm_comm* comm, void* handle);
+/* Map every peer window; `handles` holds world handles in rank order. */
+int dgxm_comm_import(dgxm_comm* comm, const void* handles);
+/* Base of `peer`'s usable window as addressable from this process. */
+int dgxm_comm_window(dgxm_comm* comm, int32_t peer, void** ptr);
+int64_t dgxm_comm_bytes(dgxm_comm* comm);
+uint64_t dgxm_comm_generation(dgxm_comm* comm);
+/* Stream-ordered barrier over all ranks of the comm: each rank releases a
+ * flag in every peer window and waits (bounded, about one second) for every
+ * peer's flag.  A wait that expires sets the device error word instead of
+ * hanging.  Replaces the implicit synchronisation of the reference's NCCL
+ * all_to_all. */
+int dgxm_comm_barrier(dgxm_comm* comm, void* stream);
+/* Synchronise the device, unmap peers, free the window. */
+int dgxm_comm_destroy(dgxm_comm* comm);
+
+/* ------------------------------------------------------------ Ulysses all-to-all */
+typedef struct dgxm_a2a_desc {
+  int32_t n_tensors;  /* 1..3 tensors moved in one launch (q, k, v) */
+  int32_t world;
+  int32_t rank;
+  int32_t batch;
+  int32_t seq_local;  /* rows this rank holds before the scatter */
+  int32_t heads;      /* all heads; heads % world == 0 */
+  int32_t head_dim;
+  int32_t dtype;
+  int64_t src_stride[3][3]; /* per tensor: batch, row, head (elements) */
+} dgxm_a2a_desc;
+
+/*
+ * Sequence -> head all-to-all as direct peer stores.  src[t] is this rank's
+ * (batch, seq_local, heads, head_dim) tensor t; dst[t*world + r] is rank r's
+ * contiguous (batch, world*seq_local, heads/world, head_dim) receive tensor,
+ * addressable from this rank (a comm window).  This rank writes head slice
+ * [r*H/P, (r+1)*H/P) of its rows into rows [rank*seq_local, (rank+1)*seq_local)
+ * of dst[t*world + r]: the rank-major gathered axis.  Follow with
+ * dgxm_comm_barrier before any rank reads its receive tensors.
+ *
+ * Replaces yunchang SeqAllToAll4D.apply(pg, x, 2, 1) at
+ * adapters/usp_full_axis.py:27-29 (and inside xfuser's call at
+ * adapters/base.py:320).
+ */
+int dgxm_ulysses_scatter(const dgxm_a2a_desc* desc, const void* const* src, void* const* dst,
+                         void* stream);
+
+/*
+ * Head -> sequence (the inverse).  src is this rank's (batch, world*seq_local,
+ * heads/world, head_dim) tensor (strides in desc->src_stride[0]); dst[r] is
+ * rank r's contiguous (batch, seq_local, heads, head_dim) output.  Replaces
+ * SeqAllToAll4D.apply(pg, out, 1, 2) at adapters/usp_full_axis.py:40.
+ */
+int dgxm_ulysses_gather(const dgxm_a2a_desc* desc, const void* src, void* const* dst,
+                        void* stream);
+
+/*
+ * Attention whose epilogue performs the inverse all-to-all: output row i of
+ * query head h goes to rank i / seq_local, row i % seq_local, head
+ * rank*q_heads + h of that rank's (batch, seq_local, world*q_heads, head_dim)
+ * tensor o_peers[i / seq_local] (strides desc->o_stride).  Everything else is
+ * dgxm_attn_fwd; lse stays local.  No separate all-to-all kernel or permute
+ * runs for the output.
+ */
+int dgxm_attn_fwd_routed(const dgxm_attn_desc* desc, const void* q, const void* k, const void* v,
+                         const float* q_descale, const float* k_descale,
+                         const float* v_descale, void* const* o_peers, int32_t world,
+                         int32_t rank, int32_t seq_local, float* lse, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
