@@ -1,11 +1,12 @@
-"""Drive one attention shape three times (for ncu captures): argv = seq heads."""
+"""Run one attention shape three times, for profiler captures.
+
+    python -m dgx_monarch_b200.profile_case SEQ HEADS
+"""
 import sys
-from pathlib import Path
 
-sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
-import torch  # noqa: E402
+import torch
 
-from dgx_monarch_b200.ops import attention_fwd  # noqa: E402
+from dgx_monarch_b200.ops import attention_fwd
 
 seq, heads = (int(sys.argv[1]), int(sys.argv[2])) if len(sys.argv) > 2 else (32768, 8)
 g = torch.Generator(device="cuda").manual_seed(0)
