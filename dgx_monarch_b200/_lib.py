@@ -71,6 +71,7 @@ class A2ADesc(ctypes.Structure):
         ("head_dim", ctypes.c_int32),
         ("dtype", ctypes.c_int32),
         ("src_stride", (ctypes.c_int64 * 3) * 3),
+        ("seg0", ctypes.c_int32),
     ]
 
 
@@ -92,12 +93,17 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "dgxm_comm_bytes": (ctypes.c_int64, [_P]),
     "dgxm_comm_generation": (ctypes.c_uint64, [_P]),
     "dgxm_comm_barrier": (ctypes.c_int, [_P, _P]),
+    "dgxm_comm_set_timeout": (ctypes.c_int, [_P, _I32]),
     "dgxm_comm_destroy": (ctypes.c_int, [_P]),
     "dgxm_ulysses_scatter": (ctypes.c_int, [ctypes.POINTER(A2ADesc), ctypes.POINTER(_P),
                                             ctypes.POINTER(_P), _P]),
     "dgxm_ulysses_gather": (ctypes.c_int, [ctypes.POINTER(A2ADesc), _P, ctypes.POINTER(_P), _P]),
     "dgxm_attn_fwd_routed": (ctypes.c_int, [ctypes.POINTER(AttnDesc), _P, _P, _P, _P, _P, _P,
-                                            ctypes.POINTER(_P), _I32, _I32, _I32, _P, _P]),
+                                            ctypes.POINTER(_P), _I32, _I32, _I32, _I32, _P, _P]),
+    "dgxm_ring_window_bytes": (ctypes.c_int64, [ctypes.POINTER(AttnDesc)]),
+    "dgxm_ring_workspace_bytes": (ctypes.c_int64, [ctypes.POINTER(AttnDesc), _I32]),
+    "dgxm_ring_attn_fwd": (ctypes.c_int, [_P, ctypes.POINTER(AttnDesc), _P, _P, _P, _P, _P, _P,
+                                          ctypes.c_int64, _P]),
 }
 
 _lock = threading.Lock()

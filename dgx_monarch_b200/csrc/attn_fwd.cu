@@ -81,6 +81,8 @@ struct __align__(64) AttnParams {
   void* o_peer[DGXM_MAX_WORLD];
   int o_rows;
   int o_head_off;
+  int o_world;
+  int o_seg0;  // joint order of the gathered axis (0 = rank-major)
 };
 
 // Barrier slots inside the control block.
@@ -405,9 +407,23 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
       int orow_idx = grow;
       int ohead = h;
       if (p.o_rows > 0) {
-        const int peer = row_ok ? grow / p.o_rows : 0;
+        int peer = 0, lrow = 0;
+        if (row_ok) {
+          if (p.o_seg0 == 0) {
+            peer = grow / p.o_rows;
+            lrow = grow - peer * p.o_rows;
+          } else if (grow < p.o_world * p.o_seg0) {
+            peer = grow / p.o_seg0;
+            lrow = grow - peer * p.o_seg0;
+          } else {
+            const int seg1 = p.o_rows - p.o_seg0;
+            const int t2 = grow - p.o_world * p.o_seg0;
+            peer = t2 / seg1;
+            lrow = p.o_seg0 + (t2 - peer * seg1);
+          }
+        }
         obase = p.o_peer[peer];
-        orow_idx = grow - peer * p.o_rows;
+        orow_idx = lrow;
         ohead = p.o_head_off + h;
       }
       char* orow = static_cast<char*>(obase) +
@@ -586,7 +602,8 @@ extern "C" int dgxm_attn_fwd(const dgxm_attn_desc* d, const void* q, const void*
 extern "C" int dgxm_attn_fwd_routed(const dgxm_attn_desc* d, const void* q, const void* k,
                                     const void* v, const float* q_descale, const float* k_descale,
                                     const float* v_descale, void* const* o_peers, int32_t world,
-                                    int32_t rank, int32_t seq_local, float* lse, void* stream) {
+                                    int32_t rank, int32_t seq_local, int32_t seg0, float* lse,
+                                    void* stream) {
   using namespace dgxm;
   if (o_peers == nullptr) return fail(DGXM_ERR_INVALID, "o_peers is NULL");
   if (world < 1 || world > DGXM_MAX_WORLD || rank < 0 || rank >= world)
@@ -605,7 +622,12 @@ extern "C" int dgxm_attn_fwd_routed(const dgxm_attn_desc* d, const void* q, cons
                         &grid, &skip);
   if (rc != DGXM_OK || skip) return rc;
   for (int r = 0; r < world; ++r) prm.o_peer[r] = o_peers[r];
+  if (seg0 < 0 || seg0 >= seq_local)
+    return fail(DGXM_ERR_INVALID, "joint segment of %d rows does not split %d local rows", seg0,
+                seq_local);
   prm.o_rows = seq_local;
   prm.o_head_off = rank * d->q_heads;
+  prm.o_world = world;
+  prm.o_seg0 = seg0;
   return dispatch_attn(d, prm, grid, stream);
 }

@@ -23,6 +23,9 @@ struct dgxm_comm {
   char* peers[DGXM_MAX_WORLD];  // window bases as seen by this process
   bool opened[DGXM_MAX_WORLD];
   uint32_t epoch;      // barriers issued so far
+  long long wait_cycles;  // barrier wait budget in SM clock cycles
+  cudaStream_t side;      // ring: copy-engine stream (created on first use)
+  cudaEvent_t ev_main, ev_side;
 };
 
 namespace dgxm {
@@ -35,6 +38,7 @@ struct BarrierParams {
   int* my_flags;
   int rank, world;
   int epoch;
+  long long wait_cycles;
 };
 
 __global__ void comm_barrier_kernel(const __grid_constant__ BarrierParams p) {
@@ -51,7 +55,7 @@ __global__ void comm_barrier_kernel(const __grid_constant__ BarrierParams p) {
     int seen;
     asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(seen) : "l"(mine) : "memory");
     if (seen - p.epoch >= 0) break;  // wrap-safe monotonic compare
-    if (clock64() - start > kWaitBudgetCycles) {
+    if (clock64() - start > p.wait_cycles) {
       report_device_error(kErrPeerTimeout);
       break;
     }
@@ -67,7 +71,20 @@ struct ScatterParams {
   int64_t s_sb[3], s_sl[3], s_sh[3];       // source strides, bytes
   int n_tensors, world, rank;
   int batch, seq_local, heads, head_bytes; // head_bytes = D * elt
+  int seg0;                                // joint order: leading rows per rank (0 = rank-major)
 };
+
+// Position on the gathered axis of local row l of rank r.  With seg0 == 0
+// this is the rank-major concat [r*Ls + l]; with a two-segment local layout
+// [seg0 rows | Ls - seg0 rows] it is the canonical order that lists every
+// rank's first segment before every rank's second
+// (adapters/usp_sequence_order.py:246-255).
+__device__ __forceinline__ int64_t gathered_row(int r, int l, int seq_local, int world, int seg0) {
+  if (seg0 == 0) return static_cast<int64_t>(r) * seq_local + l;
+  if (l < seg0) return static_cast<int64_t>(r) * seg0 + l;
+  const int seg1 = seq_local - seg0;
+  return static_cast<int64_t>(world) * seg0 + static_cast<int64_t>(r) * seg1 + (l - seg0);
+}
 
 // Sequence -> head: this rank's rows, head slice of rank r -> rank r's
 // gathered axis at rows [rank*Ls, (rank+1)*Ls).  One thread moves 16 bytes;
@@ -93,7 +110,7 @@ __global__ void __launch_bounds__(256) ulysses_scatter_kernel(const __grid_const
         p.src[t] + b * p.s_sb[t] + l * p.s_sl[t] + h * p.s_sh[t]) + part);
     const int r = h / hl;
     const int hh = h - r * hl;
-    const int64_t row = static_cast<int64_t>(b) * seq_full + static_cast<int64_t>(p.rank) * p.seq_local + l;
+    const int64_t row = static_cast<int64_t>(b) * seq_full + gathered_row(p.rank, l, p.seq_local, p.world, p.seg0);
     char* dst = p.dst[t][r] + (row * hl + hh) * p.head_bytes;
     reinterpret_cast<uint4*>(dst)[part] = val;
   }
@@ -108,7 +125,28 @@ struct GatherParams {
   int64_t s_sb, s_sl, s_sh;
   int world, rank;
   int batch, seq_local, heads, head_bytes;
+  int seg0;
 };
+
+// Inverse of gathered_row: (owner rank, local row) of gathered row g.
+__device__ __forceinline__ void owner_of_row(int64_t g, int seq_local, int world, int seg0, int* r,
+                                             int* l) {
+  if (seg0 == 0) {
+    *r = static_cast<int>(g / seq_local);
+    *l = static_cast<int>(g - static_cast<int64_t>(*r) * seq_local);
+    return;
+  }
+  const int64_t head = static_cast<int64_t>(world) * seg0;
+  if (g < head) {
+    *r = static_cast<int>(g / seg0);
+    *l = static_cast<int>(g - static_cast<int64_t>(*r) * seg0);
+  } else {
+    const int seg1 = seq_local - seg0;
+    const int64_t t = g - head;
+    *r = static_cast<int>(t / seg1);
+    *l = seg0 + static_cast<int>(t - static_cast<int64_t>(*r) * seg1);
+  }
+}
 
 __global__ void __launch_bounds__(256) ulysses_gather_kernel(const __grid_constant__ GatherParams p) {
   const int chunks_per_head = p.head_bytes / 16;
@@ -125,8 +163,8 @@ __global__ void __launch_bounds__(256) ulysses_gather_kernel(const __grid_consta
     const int64_t l = rem % seq_full;
     const int b = static_cast<int>(rem / seq_full);
     const uint4 val = __ldg(reinterpret_cast<const uint4*>(p.src + b * p.s_sb + l * p.s_sl + hh * p.s_sh) + part);
-    const int r = static_cast<int>(l / p.seq_local);
-    const int64_t lr = l - static_cast<int64_t>(r) * p.seq_local;
+    int r, lr;
+    owner_of_row(l, p.seq_local, p.world, p.seg0, &r, &lr);
     const int64_t row = static_cast<int64_t>(b) * p.seq_local + lr;
     char* dst = p.dst[r] + (row * p.heads + static_cast<int64_t>(p.rank) * hl + hh) * p.head_bytes;
     reinterpret_cast<uint4*>(dst)[part] = val;
@@ -180,7 +218,19 @@ extern "C" int dgxm_comm_create(int32_t rank, int32_t world, int64_t bytes, uint
   }
   c->peers[rank] = c->local;
   c->opened[rank] = false;
+  c->wait_cycles = kWaitBudgetCycles;
   *out = c;
+  return DGXM_OK;
+}
+
+extern "C" int dgxm_comm_set_timeout(dgxm_comm* c, int32_t timeout_ms) {
+  using namespace dgxm;
+  if (c == nullptr || timeout_ms <= 0) return fail(DGXM_ERR_INVALID, "NULL comm or non-positive timeout");
+  int khz = 0;
+  DGXM_CUDA_TRY(cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, c->device));
+  // Budget at the highest clock, so the wall-clock limit is never shorter
+  // than asked.
+  c->wait_cycles = static_cast<long long>(timeout_ms) * (khz > 0 ? khz : 2000000);
   return DGXM_OK;
 }
 
@@ -239,6 +289,7 @@ extern "C" int dgxm_comm_barrier(dgxm_comm* c, void* stream) {
   p.world = c->world;
   c->epoch += 1;
   p.epoch = static_cast<int>(c->epoch);
+  p.wait_cycles = c->wait_cycles;
   comm_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(p);
   DGXM_CUDA_TRY(cudaGetLastError());
   return DGXM_OK;
@@ -251,6 +302,11 @@ extern "C" int dgxm_comm_destroy(dgxm_comm* c) {
   cudaGetDevice(&prev);
   cudaSetDevice(c->device);
   cudaDeviceSynchronize();
+  if (c->side != nullptr) {
+    cudaEventDestroy(c->ev_main);
+    cudaEventDestroy(c->ev_side);
+    cudaStreamDestroy(c->side);
+  }
   for (int r = 0; r < c->world; ++r)
     if (c->opened[r]) cudaIpcCloseMemHandle(c->peers[r]);
   cudaError_t e = cudaFree(c->local);
@@ -305,6 +361,10 @@ extern "C" int dgxm_ulysses_scatter(const dgxm_a2a_desc* d, const void* const* s
   p.seq_local = d->seq_local;
   p.heads = d->heads;
   p.head_bytes = head_bytes;
+  if (d->seg0 < 0 || d->seg0 >= d->seq_local || (d->seg0 > 0 && d->seq_local - d->seg0 < 1))
+    return fail(DGXM_ERR_INVALID, "joint segment of %d rows does not split %d local rows", d->seg0,
+                d->seq_local);
+  p.seg0 = d->seg0;
   const int64_t work = static_cast<int64_t>(d->n_tensors) * d->batch * d->seq_local * d->heads * (head_bytes / 16);
   ulysses_scatter_kernel<<<grid_for(work, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
   DGXM_CUDA_TRY(cudaGetLastError());
@@ -347,6 +407,10 @@ extern "C" int dgxm_ulysses_gather(const dgxm_a2a_desc* d, const void* src, void
   p.seq_local = d->seq_local;
   p.heads = d->heads;
   p.head_bytes = head_bytes;
+  if (d->seg0 < 0 || d->seg0 >= d->seq_local)
+    return fail(DGXM_ERR_INVALID, "joint segment of %d rows does not split %d local rows", d->seg0,
+                d->seq_local);
+  p.seg0 = d->seg0;
   const int64_t work = static_cast<int64_t>(d->batch) * d->seq_local * d->heads * (head_bytes / 16);
   ulysses_gather_kernel<<<grid_for(work, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
   DGXM_CUDA_TRY(cudaGetLastError());

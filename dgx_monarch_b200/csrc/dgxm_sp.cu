@@ -8,3 +8,4 @@
 #include "attn_fwd.cu"
 #include "lse_merge.cu"
 #include "comm.cu"
+#include "ring.cu"

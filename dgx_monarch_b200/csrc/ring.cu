@@ -1,0 +1,141 @@
+// Ring attention over the ranks of one comm: K/V blocks rotate over NVLink
+// while the attention of the current block runs, then the per-block partial
+// results are merged by log-sum-exp.
+//
+// Step t on rank r (R ranks, next = r+1 mod R):
+//   side stream : copy the block r holds (its own at t = 0, else the one
+//                 received at t-1) into next's window buffer t % 2 -- a
+//                 copy-engine peer copy, so it uses no SMs;
+//   main stream : attention(Q, block) -> fp32 partial out_t and lse_t;
+//   join, then dgxm_comm_barrier: every rank's copy has landed and every
+//   rank finished step t, so buffer (t+1) % 2 may be overwritten next.
+// After R steps the LSE merge writes the output.  The block a rank attends
+// at step t came from rank (r - t) mod R, the oracle's ring order.
+//
+// Replaces the ring loop of xfuser/yunchang reached from
+// adapters/base.py:320 (usp_attn with ring degree > 1), with the per-block
+// contract of adapters/cudnn_ring_attention.py:61-89 and an fp32 merge (the
+// reason the reference carries a cuDNN ring processor at all,
+// adapters/wan_ring_attention.py:1-9).
+
+namespace dgxm {
+
+static int64_t ring_block_bytes(const dgxm_attn_desc* d) {
+  const int64_t eb = d->in_dtype == DGXM_DTYPE_E4M3 ? 1 : 2;
+  return static_cast<int64_t>(d->batch) * d->kv_len * d->kv_heads * d->head_dim * eb;
+}
+
+static int64_t round256(int64_t x) { return (x + 255) / 256 * 256; }
+
+static int64_t ring_part_bytes(const dgxm_attn_desc* d) {
+  return round256(static_cast<int64_t>(d->batch) * d->q_len * d->q_heads * d->head_dim * 4);
+}
+
+static int64_t ring_lse_bytes(const dgxm_attn_desc* d) {
+  return round256(static_cast<int64_t>(d->batch) * d->q_heads * d->q_len * 4);
+}
+
+static int ring_prepare_streams(dgxm_comm* c) {
+  if (c->side != nullptr) return DGXM_OK;
+  DGXM_CUDA_TRY(cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking));
+  DGXM_CUDA_TRY(cudaEventCreateWithFlags(&c->ev_main, cudaEventDisableTiming));
+  DGXM_CUDA_TRY(cudaEventCreateWithFlags(&c->ev_side, cudaEventDisableTiming));
+  return DGXM_OK;
+}
+
+static bool contiguous_bhld(const int64_t* s, const dgxm_attn_desc* d, int heads, int len) {
+  return s[2] == d->head_dim && s[1] == static_cast<int64_t>(heads) * d->head_dim &&
+         (d->batch == 1 || s[0] == static_cast<int64_t>(len) * heads * d->head_dim);
+}
+
+}  // namespace dgxm
+
+extern "C" int64_t dgxm_ring_window_bytes(const dgxm_attn_desc* d) {
+  if (d == nullptr) return -1;
+  return 4 * dgxm::round256(dgxm::ring_block_bytes(d));
+}
+
+extern "C" int64_t dgxm_ring_workspace_bytes(const dgxm_attn_desc* d, int32_t ring_world) {
+  if (d == nullptr || ring_world < 1) return -1;
+  return static_cast<int64_t>(ring_world) * (dgxm::ring_part_bytes(d) + dgxm::ring_lse_bytes(d));
+}
+
+extern "C" int dgxm_ring_attn_fwd(dgxm_comm* c, const dgxm_attn_desc* d, const void* q,
+                                  const void* k, const void* v, void* o, float* lse,
+                                  void* workspace, int64_t workspace_bytes, void* stream) {
+  using namespace dgxm;
+  if (c == nullptr || d == nullptr) return fail(DGXM_ERR_INVALID, "NULL comm or descriptor");
+  const int world = c->world;
+  if (world > kMaxMergeParts)
+    return fail(DGXM_ERR_UNSUPPORTED, "ring degree %d exceeds %d", world, kMaxMergeParts);
+  if (world == 1) return dgxm_attn_fwd(d, q, k, v, nullptr, nullptr, nullptr, o, lse, stream);
+  if (d->in_dtype != DGXM_DTYPE_BF16)
+    return fail(DGXM_ERR_UNSUPPORTED, "ring attention runs bf16 inputs");
+  if (!contiguous_bhld(d->k_stride, d, d->kv_heads, d->kv_len) ||
+      !contiguous_bhld(d->v_stride, d, d->kv_heads, d->kv_len))
+    return fail(DGXM_ERR_INVALID, "ring attention needs contiguous (B, L, H, D) keys and values");
+  if (!contiguous_bhld(d->o_stride, d, d->q_heads, d->q_len))
+    return fail(DGXM_ERR_INVALID, "ring attention needs a contiguous (B, L, H, D) output");
+  const int64_t block = ring_block_bytes(d);
+  const int64_t slot = round256(block);
+  if (4 * slot > c->bytes)
+    return fail(DGXM_ERR_INVALID, "comm window of %lld bytes is smaller than the %lld the ring needs",
+                (long long)c->bytes, (long long)(4 * slot));
+  const int64_t need = dgxm_ring_workspace_bytes(d, world);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(DGXM_ERR_INVALID, "ring workspace of %lld bytes is smaller than %lld",
+                (long long)workspace_bytes, (long long)need);
+  if (reinterpret_cast<uintptr_t>(workspace) % 256)
+    return fail(DGXM_ERR_INVALID, "ring workspace must be 256-byte aligned");
+  for (int r = 0; r < world; ++r)
+    if (c->peers[r] == nullptr) return fail(DGXM_ERR_STATE, "peer %d window is not mapped", r);
+  int rc = ring_prepare_streams(c);
+  if (rc) return rc;
+  cudaStream_t main = static_cast<cudaStream_t>(stream);
+  const int next = (c->rank + 1) % world;
+  char* mine = c->local + kFlagBytes;
+  char* theirs = c->peers[next] + kFlagBytes;
+  char* parts_out = static_cast<char*>(workspace);
+  char* parts_lse = parts_out + world * ring_part_bytes(d);
+  const void* outs[kMaxMergeParts];
+  const float* lses[kMaxMergeParts];
+
+  dgxm_attn_desc step = *d;
+  step.out_dtype = DGXM_DTYPE_F32;
+  step.o_stride[0] = static_cast<int64_t>(d->q_len) * d->q_heads * d->head_dim;
+  step.o_stride[1] = static_cast<int64_t>(d->q_heads) * d->head_dim;
+  step.o_stride[2] = d->head_dim;
+  step.lse_stride[0] = static_cast<int64_t>(d->q_heads) * d->q_len;
+  step.lse_stride[1] = d->q_len;
+  step.lse_stride[2] = 1;
+
+  const char* cur_k = static_cast<const char*>(k);
+  const char* cur_v = static_cast<const char*>(v);
+  DGXM_CUDA_TRY(cudaEventRecord(c->ev_main, main));
+  for (int t = 0; t < world; ++t) {
+    const bool send = t < world - 1;
+    const int buf = t % 2;
+    if (send) {
+      DGXM_CUDA_TRY(cudaStreamWaitEvent(c->side, c->ev_main, 0));
+      DGXM_CUDA_TRY(cudaMemcpyAsync(theirs + (2 * buf) * slot, cur_k, block, cudaMemcpyDefault, c->side));
+      DGXM_CUDA_TRY(cudaMemcpyAsync(theirs + (2 * buf + 1) * slot, cur_v, block, cudaMemcpyDefault, c->side));
+      DGXM_CUDA_TRY(cudaEventRecord(c->ev_side, c->side));
+    }
+    void* po = parts_out + t * ring_part_bytes(d);
+    float* pl = reinterpret_cast<float*>(parts_lse + t * ring_lse_bytes(d));
+    outs[t] = po;
+    lses[t] = pl;
+    rc = dgxm_attn_fwd(&step, q, cur_k, cur_v, nullptr, nullptr, nullptr, po, pl, main);
+    if (rc) return rc;
+    if (send) {
+      DGXM_CUDA_TRY(cudaStreamWaitEvent(main, c->ev_side, 0));
+      rc = dgxm_comm_barrier(c, main);
+      if (rc) return rc;
+      DGXM_CUDA_TRY(cudaEventRecord(c->ev_main, main));
+      cur_k = mine + (2 * buf) * slot;
+      cur_v = mine + (2 * buf + 1) * slot;
+    }
+  }
+  return dgxm_lse_merge(d->batch, d->q_len, d->q_heads, d->head_dim, world, outs, DGXM_DTYPE_F32,
+                        lses, o, d->out_dtype, lse, stream);
+}

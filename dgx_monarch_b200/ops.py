@@ -42,6 +42,28 @@ def _require_cuda(*tensors: torch.Tensor) -> torch.device:
     return dev
 
 
+def attn_desc(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor,
+              lse: torch.Tensor | None, softmax_scale: float | None = None,
+              safe_order: bool = False) -> _lib.AttnDesc:
+    """The C descriptor of one attention call over (B, L, H, D) tensors."""
+    b, lq, h, d = q.shape
+    _, lk, hkv, _ = k.shape
+    desc = _lib.AttnDesc()
+    desc.batch, desc.q_len, desc.kv_len = b, lq, lk
+    desc.q_heads, desc.kv_heads, desc.head_dim = h, hkv, d
+    desc.in_dtype = _dtype_code(q.dtype)
+    desc.out_dtype = _dtype_code(out.dtype)
+    desc.q_stride[:] = [q.stride(0), q.stride(1), q.stride(2)]
+    desc.k_stride[:] = [k.stride(0), k.stride(1), k.stride(2)]
+    desc.v_stride[:] = [v.stride(0), v.stride(1), v.stride(2)]
+    desc.o_stride[:] = [out.stride(0), out.stride(1), out.stride(2)]
+    if lse is not None:
+        desc.lse_stride[:] = [lse.stride(0), lse.stride(1), lse.stride(2)]
+    desc.softmax_scale = float(softmax_scale) if softmax_scale else 1.0 / math.sqrt(d)
+    desc.flags = _lib.ATTN_SAFE_ORDER if safe_order else 0
+    return desc
+
+
 def attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
                   softmax_scale: float | None = None,
                   out_dtype: torch.dtype = torch.bfloat16,
@@ -75,19 +97,7 @@ def attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
         out = torch.empty((b, lq, h, d), device=dev, dtype=out_dtype)
     if lse is None and return_lse:
         lse = torch.empty((b, h, lq), device=dev, dtype=torch.float32)
-    desc = _lib.AttnDesc()
-    desc.batch, desc.q_len, desc.kv_len = b, lq, lk
-    desc.q_heads, desc.kv_heads, desc.head_dim = h, hkv, d
-    desc.in_dtype = _dtype_code(q.dtype)
-    desc.out_dtype = _dtype_code(out.dtype)
-    desc.q_stride[:] = [q.stride(0), q.stride(1), q.stride(2)]
-    desc.k_stride[:] = [k.stride(0), k.stride(1), k.stride(2)]
-    desc.v_stride[:] = [v.stride(0), v.stride(1), v.stride(2)]
-    desc.o_stride[:] = [out.stride(0), out.stride(1), out.stride(2)]
-    if lse is not None:
-        desc.lse_stride[:] = [lse.stride(0), lse.stride(1), lse.stride(2)]
-    desc.softmax_scale = float(softmax_scale) if softmax_scale else 1.0 / math.sqrt(d)
-    desc.flags = _lib.ATTN_SAFE_ORDER if safe_order else 0
+    desc = attn_desc(q, k, v, out, lse, softmax_scale, safe_order)
     lib = _lib.load()
     with torch.cuda.device(dev):
         stream = torch.cuda.current_stream(dev).cuda_stream

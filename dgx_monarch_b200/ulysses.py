@@ -25,8 +25,9 @@ from .comm import PeerWindows
 from .ops import _dtype_code, _ptr, attention_fwd
 
 
-def a2a_desc(n_tensors, world, rank, batch, seq_local, heads, head_dim, dtype, strides):
+def a2a_desc(n_tensors, world, rank, batch, seq_local, heads, head_dim, dtype, strides, seg0=0):
     d = _lib.A2ADesc()
+    d.seg0 = int(seg0)
     d.n_tensors, d.world, d.rank = n_tensors, world, rank
     d.batch, d.seq_local, d.heads, d.head_dim = batch, seq_local, heads, head_dim
     d.dtype = _dtype_code(dtype)
@@ -36,14 +37,18 @@ def a2a_desc(n_tensors, world, rank, batch, seq_local, heads, head_dim, dtype, s
 
 
 def ulysses_scatter(tensors: list[torch.Tensor], dst_ptrs: list[list[int]], *, world: int,
-                    rank: int, stream=None) -> None:
-    """Store head slices of this rank's (B, Ls, H, D) tensors into dst_ptrs[t][r]."""
+                    rank: int, seg0: int = 0, stream=None) -> None:
+    """Store head slices of this rank's (B, Ls, H, D) tensors into dst_ptrs[t][r].
+
+    seg0 > 0 writes the joint (text-first canonical) order of a two-segment
+    local layout instead of the rank-major concat.
+    """
     b, ls, h, d = tensors[0].shape
     for t in tensors:
         if t.shape != tensors[0].shape or t.dtype != tensors[0].dtype or t.stride(3) != 1:
             raise ValueError("all-to-all tensors must share shape/dtype with contiguous head_dim")
     desc = a2a_desc(len(tensors), world, rank, b, ls, h, d, tensors[0].dtype,
-                    [(t.stride(0), t.stride(1), t.stride(2)) for t in tensors])
+                    [(t.stride(0), t.stride(1), t.stride(2)) for t in tensors], seg0)
     n = len(tensors)
     src = (ctypes.c_void_p * n)(*[t.data_ptr() for t in tensors])
     dst = (ctypes.c_void_p * (n * world))(*[p for row in dst_ptrs for p in row])
@@ -53,13 +58,13 @@ def ulysses_scatter(tensors: list[torch.Tensor], dst_ptrs: list[list[int]], *, w
 
 
 def ulysses_gather(src: torch.Tensor, dst_ptrs: list[int], *, world: int, rank: int,
-                   seq_local: int, heads: int, stream=None) -> None:
+                   seq_local: int, heads: int, seg0: int = 0, stream=None) -> None:
     """Return (B, S, Hl, D) rows to the owning ranks' (B, Ls, H, D) tensors."""
     b, s, hl, d = src.shape
     if s != seq_local * world or hl * world != heads or src.stride(3) != 1:
         raise ValueError("gather source must be (B, world*seq_local, heads/world, D)")
     desc = a2a_desc(1, world, rank, b, seq_local, heads, d, src.dtype,
-                    [(src.stride(0), src.stride(1), src.stride(2))])
+                    [(src.stride(0), src.stride(1), src.stride(2))], seg0)
     dst = (ctypes.c_void_p * world)(*dst_ptrs)
     stream = stream or torch.cuda.current_stream(src.device)
     _lib.check(_lib.load().dgxm_ulysses_gather(ctypes.byref(desc), src.data_ptr(), dst,
@@ -67,7 +72,8 @@ def ulysses_gather(src: torch.Tensor, dst_ptrs: list[int], *, world: int, rank: 
 
 
 def attention_routed(q, k, v, out_ptrs: list[int], out_strides, *, world: int, rank: int,
-                     seq_local: int, lse: torch.Tensor | None = None, softmax_scale=None,
+                     seq_local: int, seg0: int = 0, lse: torch.Tensor | None = None,
+                     softmax_scale=None,
                      q_descale=None, k_descale=None, v_descale=None, stream=None) -> None:
     """Attention whose epilogue writes row i to rank i // seq_local's output."""
     b, lq, hl, d = q.shape
@@ -88,7 +94,7 @@ def attention_routed(q, k, v, out_ptrs: list[int], out_strides, *, world: int, r
     stream = stream or torch.cuda.current_stream(q.device)
     _lib.check(_lib.load().dgxm_attn_fwd_routed(
         ctypes.byref(desc), q.data_ptr(), k.data_ptr(), v.data_ptr(), _ptr(q_descale),
-        _ptr(k_descale), _ptr(v_descale), peers, world, rank, seq_local, _ptr(lse),
+        _ptr(k_descale), _ptr(v_descale), peers, world, rank, seq_local, seg0, _ptr(lse),
         stream.cuda_stream), "dgxm_attn_fwd_routed")
 
 

@@ -5,9 +5,9 @@
  * (passed as void*), returns an int status (DGXM_OK == 0), never aborts the
  * process, and waits on the device only for a bounded time.  A failed call
  * leaves a human-readable reason in dgxm_last_error_message() for the calling
- * thread.  Nothing here allocates device memory except dgxm_comm_create and
- * the ring entry point (which owns its rotation buffers through the comm
- * handle).
+ * thread.  Nothing here allocates device memory except dgxm_comm_create;
+ * the ring entry point keeps its rotating blocks in the comm window and its
+ * partial results in a caller-provided workspace.
  *
  * The reference (dgx-monarch) is pure Python; these functions replace the
  * third-party library calls its attention seam makes.  Each declaration names
@@ -142,6 +142,8 @@ uint64_t dgxm_comm_generation(dgxm_comm* comm);
  * hanging.  Replaces the implicit synchronisation of the reference's NCCL
  * all_to_all. */
 int dgxm_comm_barrier(dgxm_comm* comm, void* stream);
+/* Wall-clock budget of one barrier wait (default about one second). */
+int dgxm_comm_set_timeout(dgxm_comm* comm, int32_t timeout_ms);
 /* Synchronise the device, unmap peers, free the window. */
 int dgxm_comm_destroy(dgxm_comm* comm);
 
@@ -156,6 +158,13 @@ typedef struct dgxm_a2a_desc {
   int32_t head_dim;
   int32_t dtype;
   int64_t src_stride[3][3]; /* per tensor: batch, row, head (elements) */
+  /* Joint order.  0: the gathered axis is the rank-major concat of the local
+   * rows.  seg0 > 0: each rank's local rows are [seg0 rows | seq_local - seg0
+   * rows] (text then image) and the gathered axis lists every rank's first
+   * segment, then every rank's second -- the stock key order that
+   * adapters/usp_sequence_order.py:209-322 (RankMajorJointOrder) restores
+   * with index copies; here the all-to-all writes rows straight there. */
+  int32_t seg0;
 } dgxm_a2a_desc;
 
 /*
@@ -185,16 +194,40 @@ int dgxm_ulysses_gather(const dgxm_a2a_desc* desc, const void* src, void* const*
 
 /*
  * Attention whose epilogue performs the inverse all-to-all: output row i of
- * query head h goes to rank i / seq_local, row i % seq_local, head
+ * query head h goes to the rank owning gathered row i (rank-major, or the
+ * joint order when seg0 > 0, see dgxm_a2a_desc), at that rank's local row,
+ * head
  * rank*q_heads + h of that rank's (batch, seq_local, world*q_heads, head_dim)
- * tensor o_peers[i / seq_local] (strides desc->o_stride).  Everything else is
+ * tensor o_peers[owner] (strides desc->o_stride).  Everything else is
  * dgxm_attn_fwd; lse stays local.  No separate all-to-all kernel or permute
  * runs for the output.
  */
 int dgxm_attn_fwd_routed(const dgxm_attn_desc* desc, const void* q, const void* k, const void* v,
                          const float* q_descale, const float* k_descale,
                          const float* v_descale, void* const* o_peers, int32_t world,
-                         int32_t rank, int32_t seq_local, float* lse, void* stream);
+                         int32_t rank, int32_t seq_local, int32_t seg0, float* lse,
+                         void* stream);
+
+/* ------------------------------------------------------------ ring attention */
+/*
+ * Ring attention over the ranks of `comm` (the ring group): every rank holds
+ * its own query rows and one key/value block; the blocks rotate over NVLink
+ * (copy-engine peer copies into the next rank's window, overlapped with the
+ * attention of the current block) and the R partial results are merged by
+ * LSE in fp32.  Keys/values and the output must be contiguous (B, L, H, D);
+ * lse (may be NULL) is contiguous fp32 (B, H, Lq).  The comm window needs
+ * dgxm_ring_window_bytes(desc); `workspace` (scratch owned by the caller,
+ * 256-byte aligned) needs dgxm_ring_workspace_bytes(desc, R).  bf16 inputs.
+ *
+ * Replaces the ring loop of xfuser/yunchang that adapters/base.py:320 reaches
+ * when the ring degree exceeds one (block contract:
+ * adapters/cudnn_ring_attention.py:61-89).
+ */
+int64_t dgxm_ring_window_bytes(const dgxm_attn_desc* desc);
+int64_t dgxm_ring_workspace_bytes(const dgxm_attn_desc* desc, int32_t ring_world);
+int dgxm_ring_attn_fwd(dgxm_comm* comm, const dgxm_attn_desc* desc, const void* q, const void* k,
+                       const void* v, void* o, float* lse, void* workspace,
+                       int64_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

@@ -114,3 +114,87 @@ def test_routed_epilogue_equals_attention_then_gather(lib, world, seq_local, hea
     got = torch.cat(routed, dim=1)
     assert (got.float() - ref).abs().max().item() <= BF16_MAX_ABS
     assert rel_l2(got, ref) <= BF16_REL_L2
+
+
+@pytest.mark.parametrize("world,text,image,heads", [(2, 3, 5, 4), (4, 16, 48, 8), (8, 64, 1152 // 8, 24)])
+def test_joint_order_scatter_is_canonical_bit_exact(lib, world, text, image, heads):
+    """seg0 > 0 writes the stock [t0,t1,...,i0,i1,...] order that
+    RankMajorJointOrder.canonicalize (adapters/usp_sequence_order.py:282-309)
+    produces from the rank-major gathered axis."""
+    from dgx_monarch_b200.ulysses import ulysses_gather, ulysses_scatter
+
+    g = torch.Generator(device="cuda").manual_seed(17)
+    ls = text + image
+    local = [torch.randn(1, ls, heads, 128, device="cuda", generator=g).bfloat16() for _ in range(world)]
+    hl = heads // world
+    recv = [torch.zeros(1, ls * world, hl, 128, device="cuda", dtype=torch.bfloat16) for _ in range(world)]
+    for src in range(world):
+        ulysses_scatter([local[src]], [[recv[r].data_ptr() for r in range(world)]], world=world,
+                        rank=src, seg0=text)
+    torch.cuda.synchronize()
+    rank_major = usp.seq_all_to_all_4d([_bits(t) for t in local], 2, 1)
+    order = usp.RankMajorJointOrder(text, image)
+    for r in range(world):
+        canon, _, _, _, _, _ = order.canonicalize(rank_major[r], rank_major[r], rank_major[r], None, None)
+        assert np.array_equal(_bits(recv[r]), canon)
+    # The inverse with the same row map returns every rank's own rows.
+    back = [torch.zeros_like(x) for x in local]
+    for src in range(world):
+        ulysses_gather(recv[src], [b.data_ptr() for b in back], world=world, rank=src,
+                       seq_local=ls, heads=heads, seg0=text)
+    torch.cuda.synchronize()
+    for r in range(world):
+        assert torch.equal(back[r], local[r])
+
+
+def test_joint_order_routed_epilogue_matches_gather(lib):
+    from dgx_monarch_b200.ops import attention_fwd
+    from dgx_monarch_b200.ulysses import attention_routed, ulysses_gather, ulysses_scatter
+
+    world, text, image, heads = 2, 64, 192, 4
+    ls = text + image
+    g = torch.Generator(device="cuda").manual_seed(19)
+    local = [[torch.randn(1, ls, heads, 128, device="cuda", generator=g).bfloat16() for _ in range(3)]
+             for _ in range(world)]
+    hl = heads // world
+    recv = [[torch.empty(1, ls * world, hl, 128, device="cuda", dtype=torch.bfloat16) for _ in range(world)]
+            for _ in range(3)]
+    for src in range(world):
+        ulysses_scatter(local[src], [[recv[t][r].data_ptr() for r in range(world)] for t in range(3)],
+                        world=world, rank=src, seg0=text)
+    routed = [torch.zeros(1, ls, heads, 128, device="cuda", dtype=torch.bfloat16) for _ in range(world)]
+    gathered = [torch.zeros_like(x) for x in routed]
+    for r in range(world):
+        attention_routed(recv[0][r], recv[1][r], recv[2][r], [o.data_ptr() for o in routed],
+                         (ls * heads * 128, heads * 128, 128), world=world, rank=r, seq_local=ls, seg0=text)
+        full, _ = attention_fwd(recv[0][r], recv[1][r], recv[2][r])
+        ulysses_gather(full, [o.data_ptr() for o in gathered], world=world, rank=r, seq_local=ls,
+                       heads=heads, seg0=text)
+    torch.cuda.synchronize()
+    for r in range(world):
+        assert torch.equal(routed[r], gathered[r])
+    # And the composition is joint attention over the whole [text, image] sequence.
+    q, k, v = (torch.cat([local[r][t] for r in range(world)], dim=1) for t in range(3))
+    ref, _ = reference_attention(q, k, v)
+    got = torch.cat(routed, dim=1)
+    assert rel_l2(got, ref) <= BF16_REL_L2
+
+
+def test_emulated_ring_merge_equals_full_attention(lib):
+    """Ring order of oracle.usp.ring_attention on one GPU: rank r attends the
+    block of rank (r - t) mod R at step t; the LSE merge of the R partial
+    results equals attention over the whole key axis."""
+    from dgx_monarch_b200.ops import attention_fwd, lse_merge
+
+    world, rows = 4, 300
+    g = torch.Generator(device="cuda").manual_seed(23)
+    q, k, v = (torch.randn(1, rows * world, 3, 128, device="cuda", generator=g).bfloat16() for _ in range(3))
+    blk = lambda t, r: t[:, r * rows:(r + 1) * rows].contiguous()
+    ref, ref_lse = reference_attention(q, k, v)
+    for r in range(world):
+        parts = [attention_fwd(blk(q, r), blk(k, (r - t) % world), blk(v, (r - t) % world),
+                               out_dtype=torch.float32) for t in range(world)]
+        out, lse = lse_merge([p[0] for p in parts], [p[1] for p in parts])
+        torch.cuda.synchronize()
+        assert rel_l2(out, ref[:, r * rows:(r + 1) * rows]) <= BF16_REL_L2
+        assert (lse - ref_lse[:, :, r * rows:(r + 1) * rows]).abs().max().item() <= 2e-3
