@@ -75,6 +75,25 @@ class A2ADesc(ctypes.Structure):
     ]
 
 
+NORM_NONE, NORM_HIDDEN, NORM_HEAD = 0, 1, 2
+
+
+class PrologueDesc(ctypes.Structure):
+    _fields_ = [
+        ("world", ctypes.c_int32),
+        ("rank", ctypes.c_int32),
+        ("batch", ctypes.c_int32),
+        ("seq_local", ctypes.c_int32),
+        ("heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("norm_mode", ctypes.c_int32),
+        ("eps", ctypes.c_float),
+        ("src_stride", (ctypes.c_int64 * 3) * 3),
+        ("rope_batch_stride", ctypes.c_int64),
+        ("seg0", ctypes.c_int32),
+    ]
+
+
 # Every symbol include/dgxm_sp.h declares, with its ctypes signature.
 _P = ctypes.c_void_p
 _I32 = ctypes.c_int32
@@ -94,12 +113,17 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "dgxm_comm_generation": (ctypes.c_uint64, [_P]),
     "dgxm_comm_barrier": (ctypes.c_int, [_P, _P]),
     "dgxm_comm_set_timeout": (ctypes.c_int, [_P, _I32]),
+    "dgxm_comm_allgather": (ctypes.c_int, [_P, _P, ctypes.c_int64, ctypes.c_int64, _P]),
     "dgxm_comm_destroy": (ctypes.c_int, [_P]),
     "dgxm_ulysses_scatter": (ctypes.c_int, [ctypes.POINTER(A2ADesc), ctypes.POINTER(_P),
                                             ctypes.POINTER(_P), _P]),
     "dgxm_ulysses_gather": (ctypes.c_int, [ctypes.POINTER(A2ADesc), _P, ctypes.POINTER(_P), _P]),
     "dgxm_attn_fwd_routed": (ctypes.c_int, [ctypes.POINTER(AttnDesc), _P, _P, _P, _P, _P, _P,
                                             ctypes.POINTER(_P), _I32, _I32, _I32, _I32, _P, _P]),
+    "dgxm_qkv_prologue_scatter": (ctypes.c_int, [ctypes.POINTER(PrologueDesc), ctypes.POINTER(_P),
+                                                 _P, _P, _P, ctypes.POINTER(_P), _P]),
+    "dgxm_quantize_e4m3_per_head": (ctypes.c_int, [_I32, _I32, _I32, _I32, _P,
+                                                   ctypes.POINTER(ctypes.c_int64), _P, _P, _P]),
     "dgxm_ring_window_bytes": (ctypes.c_int64, [ctypes.POINTER(AttnDesc)]),
     "dgxm_ring_workspace_bytes": (ctypes.c_int64, [ctypes.POINTER(AttnDesc), _I32]),
     "dgxm_ring_attn_fwd": (ctypes.c_int, [_P, ctypes.POINTER(AttnDesc), _P, _P, _P, _P, _P, _P,

@@ -316,6 +316,27 @@ extern "C" int dgxm_comm_destroy(dgxm_comm* c) {
   return DGXM_OK;
 }
 
+extern "C" int dgxm_comm_allgather(dgxm_comm* c, const void* src, int64_t bytes,
+                                   int64_t window_offset, void* stream) {
+  using namespace dgxm;
+  if (c == nullptr || src == nullptr) return fail(DGXM_ERR_INVALID, "NULL comm or source");
+  if (bytes < 0 || window_offset < 0 || window_offset % 16)
+    return fail(DGXM_ERR_INVALID, "negative size or misaligned window offset");
+  if (window_offset + bytes * c->world > c->bytes)
+    return fail(DGXM_ERR_INVALID, "all-gather of %d x %lld bytes at offset %lld overflows the "
+                "%lld-byte window", c->world, (long long)bytes, (long long)window_offset,
+                (long long)c->bytes);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  for (int i = 0; i < c->world; ++i) {
+    // Start with the next peer so the copies of all ranks spread over links.
+    const int r = (c->rank + i) % c->world;
+    if (c->peers[r] == nullptr) return fail(DGXM_ERR_STATE, "peer %d window is not mapped", r);
+    char* dst = c->peers[r] + kFlagBytes + window_offset + static_cast<int64_t>(c->rank) * bytes;
+    if (bytes > 0) DGXM_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, st));
+  }
+  return dgxm_comm_barrier(c, stream);
+}
+
 extern "C" int dgxm_ulysses_scatter(const dgxm_a2a_desc* d, const void* const* src,
                                     void* const* dst, void* stream) {
   using namespace dgxm;

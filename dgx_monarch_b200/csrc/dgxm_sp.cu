@@ -9,3 +9,4 @@
 #include "lse_merge.cu"
 #include "comm.cu"
 #include "ring.cu"
+#include "prologue.cu"

@@ -1,0 +1,308 @@
+// Fused Ulysses prologue and FP8 quantisation.
+//
+// qkv_prologue_scatter_kernel: Q/K RMSNorm and multi-axis RoPE applied to a
+// rank's rows while they are scattered head-slice by head-slice into the
+// peers' receive tensors -- the sequence->head all-to-all of
+// dgxm_ulysses_scatter with the per-token math the family forwards run just
+// before the attention seam folded in (Wan: norm_q/norm_k over the whole
+// hidden size then RoPE, adapters/wan_family.py:70-73; Flux/Krea2: per-head
+// QKNorm then RoPE inside the blocks).  V is moved unchanged.
+//
+// Rounding follows the separate ops it fuses: the norm's output is rounded
+// to bf16 (the module's output dtype), RoPE then rotates that in fp32 and
+// rounds once more.
+//
+// quantize kernels: per-head absmax (fp32) and e4m3 values x / (amax / 448),
+// the FP8 inputs of the attention's kind::f8f6f4 path.
+#include "common.h"
+#include "ptx.cuh"
+
+namespace dgxm {
+
+struct PrologueParams {
+  const char* src[3];
+  int64_t s_sb[3], s_sl[3], s_sh[3];  // bytes
+  char* dst[3][DGXM_MAX_WORLD];
+  const __nv_bfloat16* norm_w[2];     // q, k weights (may be NULL)
+  const float* rope;                  // (rows, D/2, 2) cos/sin per local row, or NULL
+  int64_t rope_sb;                    // elements between batch items (0: shared)
+  int norm_mode;                      // DGXM_NORM_*
+  float eps;
+  int world, rank, batch, seq_local, heads, seg0;
+};
+
+__device__ __forceinline__ int64_t gathered_row_p(int r, int l, int seq_local, int world, int seg0) {
+  if (seg0 == 0) return static_cast<int64_t>(r) * seq_local + l;
+  if (l < seg0) return static_cast<int64_t>(r) * seg0 + l;
+  return static_cast<int64_t>(world) * seg0 + static_cast<int64_t>(r) * (seq_local - seg0) + (l - seg0);
+}
+
+constexpr int kPrologueThreads = 256;
+constexpr int kPrologueMaxHidden = 6144;  // H * D of one row (static shared memory bound)
+
+__global__ void __launch_bounds__(kPrologueThreads) qkv_prologue_scatter_kernel(const __grid_constant__ PrologueParams p) {
+  __shared__ float buf[kPrologueMaxHidden];
+  __shared__ __align__(16) __nv_bfloat16 obuf[kPrologueMaxHidden];
+  __shared__ float red[kPrologueThreads / 32];
+  __shared__ float head_scale[kPrologueMaxHidden / 128];
+  const int hid = p.heads * 128;
+  const int hl = p.heads / p.world;
+  const int64_t seq_full = static_cast<int64_t>(p.seq_local) * p.world;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int64_t item = blockIdx.x; item < static_cast<int64_t>(p.batch) * p.seq_local; item += gridDim.x) {
+    const int b = static_cast<int>(item / p.seq_local);
+    const int l = static_cast<int>(item - static_cast<int64_t>(b) * p.seq_local);
+    const int64_t grow = static_cast<int64_t>(b) * seq_full + gathered_row_p(p.rank, l, p.seq_local, p.world, p.seg0);
+    for (int t = 0; t < 3; ++t) {
+      const char* row = p.src[t] + b * p.s_sb[t] + static_cast<int64_t>(l) * p.s_sl[t];
+      const bool math = t < 2 && (p.norm_mode != DGXM_NORM_NONE || p.rope != nullptr);
+      if (math) {
+        // Load the row (all heads) as fp32.
+        for (int v = threadIdx.x; v < hid / 8; v += blockDim.x) {
+          const int h = v / 16, part = v % 16;
+          const uint4 raw = __ldg(reinterpret_cast<const uint4*>(row + h * p.s_sh[t]) + part);
+          const __nv_bfloat162* pr = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = __bfloat1622float2(pr[i]);
+            buf[v * 8 + 2 * i] = f.x;
+            buf[v * 8 + 2 * i + 1] = f.y;
+          }
+        }
+        __syncthreads();
+        if (p.norm_mode == DGXM_NORM_HIDDEN) {
+          float ss = 0.f;
+          for (int i = threadIdx.x; i < hid; i += blockDim.x) ss = fmaf(buf[i], buf[i], ss);
+          for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+          if (lane == 0) red[warp] = ss;
+          __syncthreads();
+          if (threadIdx.x == 0) {
+            float tot = 0.f;
+            for (int w = 0; w < kPrologueThreads / 32; ++w) tot += red[w];
+            head_scale[0] = rsqrtf(tot / hid + p.eps);
+          }
+          __syncthreads();
+        } else if (p.norm_mode == DGXM_NORM_HEAD) {
+          for (int h = warp; h < p.heads; h += kPrologueThreads / 32) {
+            float ss = 0.f;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float x = buf[h * 128 + lane * 4 + i];
+              ss = fmaf(x, x, ss);
+            }
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            if (lane == 0) head_scale[h] = rsqrtf(ss / 128.f + p.eps);
+          }
+          __syncthreads();
+        }
+        const __nv_bfloat16* w = p.norm_w[t];
+        const float* rope_row = p.rope == nullptr ? nullptr : p.rope + b * p.rope_sb + static_cast<int64_t>(l) * 128;
+        for (int pr = threadIdx.x; pr < hid / 2; pr += blockDim.x) {
+          const int e = 2 * pr;
+          float x0 = buf[e], x1 = buf[e + 1];
+          if (p.norm_mode != DGXM_NORM_NONE) {
+            const float sc = p.norm_mode == DGXM_NORM_HIDDEN ? head_scale[0] : head_scale[e / 128];
+            // the norm module's output: bf16(x * rsqrt(mean + eps)) * weight, rounded
+            const int wi = p.norm_mode == DGXM_NORM_HIDDEN ? e : (e % 128);
+            float n0 = __bfloat162float(__float2bfloat16(x0 * sc));
+            float n1 = __bfloat162float(__float2bfloat16(x1 * sc));
+            if (w != nullptr) {
+              n0 = __bfloat162float(__float2bfloat16(n0 * __bfloat162float(w[wi])));
+              n1 = __bfloat162float(__float2bfloat16(n1 * __bfloat162float(w[wi + 1])));
+            }
+            x0 = n0;
+            x1 = n1;
+          }
+          if (rope_row != nullptr) {
+            const int i = (e % 128) / 2;
+            const float c = rope_row[2 * i], s = rope_row[2 * i + 1];
+            const float y0 = fmaf(-s, x1, c * x0);
+            const float y1 = fmaf(c, x1, s * x0);
+            x0 = y0;
+            x1 = y1;
+          }
+          reinterpret_cast<__nv_bfloat162*>(obuf)[pr] = __floats2bfloat162_rn(x0, x1);
+        }
+        __syncthreads();
+        for (int v = threadIdx.x; v < hid / 8; v += blockDim.x) {
+          const int h = v / 16, part = v % 16;
+          const int r = h / hl, hh = h - r * hl;
+          char* dst = p.dst[t][r] + (grow * hl + hh) * 256;
+          reinterpret_cast<uint4*>(dst)[part] = reinterpret_cast<const uint4*>(obuf)[v];
+        }
+        __syncthreads();
+      } else {
+        for (int v = threadIdx.x; v < hid / 8; v += blockDim.x) {
+          const int h = v / 16, part = v % 16;
+          const uint4 raw = __ldg(reinterpret_cast<const uint4*>(row + h * p.s_sh[t]) + part);
+          const int r = h / hl, hh = h - r * hl;
+          char* dst = p.dst[t][r] + (grow * hl + hh) * 256;
+          reinterpret_cast<uint4*>(dst)[part] = raw;
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------- FP8
+struct QuantParams {
+  const char* x;
+  int64_t sb, sl, sh;  // bytes
+  uint8_t* out;        // contiguous (B, L, H, D) e4m3
+  float* amax;         // per head: accumulated absmax, then rewritten as descale
+  int batch, rows, heads;
+};
+
+__global__ void __launch_bounds__(256) absmax_kernel(const __grid_constant__ QuantParams p) {
+  const int64_t vecs = static_cast<int64_t>(p.batch) * p.rows * p.heads * 16;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < vecs;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int part = static_cast<int>(i % 16);
+    int64_t rem = i / 16;
+    const int h = static_cast<int>(rem % p.heads);
+    rem /= p.heads;
+    const int l = static_cast<int>(rem % p.rows);
+    const int b = static_cast<int>(rem / p.rows);
+    const uint4 raw = __ldg(reinterpret_cast<const uint4*>(p.x + b * p.sb + l * p.sl + h * p.sh) + part);
+    const __nv_bfloat162* pr = reinterpret_cast<const __nv_bfloat162*>(&raw);
+    float m = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 f = __bfloat1622float2(pr[k]);
+      m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
+    }
+    // Non-negative floats order like their bit patterns.
+    atomicMax(reinterpret_cast<unsigned int*>(p.amax) + h, __float_as_uint(m));
+  }
+}
+
+__global__ void __launch_bounds__(256) quantize_e4m3_kernel(const __grid_constant__ QuantParams p) {
+  const int64_t vecs = static_cast<int64_t>(p.batch) * p.rows * p.heads * 16;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < vecs;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int part = static_cast<int>(i % 16);
+    int64_t rem = i / 16;
+    const int h = static_cast<int>(rem % p.heads);
+    rem /= p.heads;
+    const int l = static_cast<int>(rem % p.rows);
+    const int b = static_cast<int>(rem / p.rows);
+    const uint4 raw = __ldg(reinterpret_cast<const uint4*>(p.x + b * p.sb + l * p.sl + h * p.sh) + part);
+    const __nv_bfloat162* pr = reinterpret_cast<const __nv_bfloat162*>(&raw);
+    const float amax = fmaxf(p.amax[h], 1e-12f);
+    const float scale = amax / 448.f;
+    uint32_t w[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const float2 a = __bfloat1622float2(pr[2 * k]);
+      const float2 c = __bfloat1622float2(pr[2 * k + 1]);
+      w[k] = pack_e4m3x4(__fdiv_rn(a.x, scale), __fdiv_rn(a.y, scale), __fdiv_rn(c.x, scale),
+                         __fdiv_rn(c.y, scale));
+    }
+    const int64_t o = ((static_cast<int64_t>(b) * p.rows + l) * p.heads + h) * 128 + part * 8;
+    *reinterpret_cast<uint2*>(p.out + o) = make_uint2(w[0], w[1]);
+  }
+}
+
+__global__ void descale_kernel(float* amax, int heads) {
+  const int h = blockIdx.x * blockDim.x + threadIdx.x;
+  if (h < heads) amax[h] = fmaxf(amax[h], 1e-12f) / 448.f;
+}
+
+}  // namespace dgxm
+
+extern "C" int dgxm_qkv_prologue_scatter(const dgxm_prologue_desc* d, const void* const* src,
+                                         const void* norm_q_w, const void* norm_k_w,
+                                         const float* rope, void* const* dst, void* stream) {
+  using namespace dgxm;
+  if (d == nullptr || src == nullptr || dst == nullptr)
+    return fail(DGXM_ERR_INVALID, "NULL prologue argument");
+  if (d->world < 1 || d->world > DGXM_MAX_WORLD || d->rank < 0 || d->rank >= d->world)
+    return fail(DGXM_ERR_INVALID, "rank %d / world %d out of range", d->rank, d->world);
+  if (d->head_dim != 128) return fail(DGXM_ERR_UNSUPPORTED, "prologue head_dim must be 128");
+  if (d->heads <= 0 || d->heads % d->world || d->heads * 128 > kPrologueMaxHidden)
+    return fail(DGXM_ERR_INVALID, "%d heads: not divisible by %d or above %d hidden", d->heads,
+                d->world, kPrologueMaxHidden);
+  if (d->norm_mode < DGXM_NORM_NONE || d->norm_mode > DGXM_NORM_HEAD)
+    return fail(DGXM_ERR_INVALID, "unknown norm mode %d", d->norm_mode);
+  if (d->seg0 < 0 || d->seg0 >= d->seq_local)
+    return fail(DGXM_ERR_INVALID, "joint segment of %d rows does not split %d local rows", d->seg0,
+                d->seq_local);
+  if (d->batch <= 0 || d->seq_local <= 0) return DGXM_OK;
+  PrologueParams p;
+  memset(&p, 0, sizeof(p));
+  for (int t = 0; t < 3; ++t) {
+    if (src[t] == nullptr || reinterpret_cast<uintptr_t>(src[t]) % 16)
+      return fail(DGXM_ERR_INVALID, "source %d is NULL or misaligned", t);
+    p.src[t] = static_cast<const char*>(src[t]);
+    p.s_sb[t] = d->src_stride[t][0] * 2;
+    p.s_sl[t] = d->src_stride[t][1] * 2;
+    p.s_sh[t] = d->src_stride[t][2] * 2;
+    if (p.s_sb[t] % 16 || p.s_sl[t] % 16 || p.s_sh[t] % 16)
+      return fail(DGXM_ERR_INVALID, "source %d strides are not 16-byte multiples", t);
+    for (int r = 0; r < d->world; ++r) {
+      void* q = dst[t * d->world + r];
+      if (q == nullptr || reinterpret_cast<uintptr_t>(q) % 16)
+        return fail(DGXM_ERR_INVALID, "destination %d of tensor %d is NULL or misaligned", r, t);
+      p.dst[t][r] = static_cast<char*>(q);
+    }
+  }
+  if (d->norm_mode != DGXM_NORM_NONE && (norm_q_w == nullptr) != (norm_k_w == nullptr))
+    return fail(DGXM_ERR_INVALID, "give both norm weights or neither");
+  p.norm_w[0] = static_cast<const __nv_bfloat16*>(norm_q_w);
+  p.norm_w[1] = static_cast<const __nv_bfloat16*>(norm_k_w);
+  p.rope = rope;
+  p.rope_sb = d->rope_batch_stride;
+  p.norm_mode = d->norm_mode;
+  p.eps = d->eps;
+  p.world = d->world;
+  p.rank = d->rank;
+  p.batch = d->batch;
+  p.seq_local = d->seq_local;
+  p.heads = d->heads;
+  p.seg0 = d->seg0;
+  int dev = 0, sms = 148;
+  DGXM_CUDA_TRY(cudaGetDevice(&dev));
+  DGXM_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const int64_t rows = static_cast<int64_t>(d->batch) * d->seq_local;
+  const int blocks = static_cast<int>(rows < int64_t(sms) * 8 ? rows : int64_t(sms) * 8);
+  qkv_prologue_scatter_kernel<<<blocks, kPrologueThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  DGXM_CUDA_TRY(cudaGetLastError());
+  return DGXM_OK;
+}
+
+extern "C" int dgxm_quantize_e4m3_per_head(int32_t batch, int32_t rows, int32_t heads,
+                                           int32_t head_dim, const void* x, const int64_t* stride,
+                                           void* out, float* descale, void* stream) {
+  using namespace dgxm;
+  if (x == nullptr || out == nullptr || descale == nullptr || stride == nullptr)
+    return fail(DGXM_ERR_INVALID, "NULL quantisation argument");
+  if (head_dim != 128) return fail(DGXM_ERR_UNSUPPORTED, "quantisation head_dim must be 128");
+  if (batch < 0 || rows < 0 || heads <= 0) return fail(DGXM_ERR_INVALID, "bad extents");
+  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(out) % 16 ||
+      (stride[0] * 2) % 16 || (stride[1] * 2) % 16 || (stride[2] * 2) % 16)
+    return fail(DGXM_ERR_INVALID, "quantisation tensors must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  DGXM_CUDA_TRY(cudaMemsetAsync(descale, 0, sizeof(float) * heads, st));
+  if (batch == 0 || rows == 0) return DGXM_OK;
+  QuantParams p;
+  p.x = static_cast<const char*>(x);
+  p.sb = stride[0] * 2;
+  p.sl = stride[1] * 2;
+  p.sh = stride[2] * 2;
+  p.out = static_cast<uint8_t*>(out);
+  p.amax = descale;
+  p.batch = batch;
+  p.rows = rows;
+  p.heads = heads;
+  int dev = 0, sms = 148;
+  DGXM_CUDA_TRY(cudaGetDevice(&dev));
+  DGXM_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const int64_t vecs = static_cast<int64_t>(batch) * rows * heads * 16;
+  const int64_t want = (vecs + 255) / 256;
+  const int blocks = static_cast<int>(want < int64_t(sms) * 8 ? want : int64_t(sms) * 8);
+  absmax_kernel<<<blocks, 256, 0, st>>>(p);
+  quantize_e4m3_kernel<<<blocks, 256, 0, st>>>(p);
+  descale_kernel<<<(heads + 127) / 128, 128, 0, st>>>(descale, heads);
+  DGXM_CUDA_TRY(cudaGetLastError());
+  return DGXM_OK;
+}

@@ -144,6 +144,13 @@ uint64_t dgxm_comm_generation(dgxm_comm* comm);
 int dgxm_comm_barrier(dgxm_comm* comm, void* stream);
 /* Wall-clock budget of one barrier wait (default about one second). */
 int dgxm_comm_set_timeout(dgxm_comm* comm, int32_t timeout_ms);
+/* All-gather as peer stores: `bytes` from src land in every rank's window at
+ * window_offset + rank*bytes (copy-engine peer copies), followed by a
+ * barrier, so on return (stream order) every window holds all world slices
+ * in rank order.  Replaces the cfg-group all_gather of the CFG split,
+ * adapters/cfg_parallel.py:293-301 (and actor/dual_model_cfg.py:84). */
+int dgxm_comm_allgather(dgxm_comm* comm, const void* src, int64_t bytes, int64_t window_offset,
+                        void* stream);
 /* Synchronise the device, unmap peers, free the window. */
 int dgxm_comm_destroy(dgxm_comm* comm);
 
@@ -207,6 +214,52 @@ int dgxm_attn_fwd_routed(const dgxm_attn_desc* desc, const void* q, const void* 
                          const float* v_descale, void* const* o_peers, int32_t world,
                          int32_t rank, int32_t seq_local, int32_t seg0, float* lse,
                          void* stream);
+
+/* ------------------------------------------------------------ fused prologue */
+#define DGXM_NORM_NONE 0
+#define DGXM_NORM_HIDDEN 1 /* RMSNorm over all heads of a row (Wan norm_q / norm_k)   */
+#define DGXM_NORM_HEAD 2   /* RMSNorm over each head's 128 values (Flux/Krea2 QKNorm) */
+
+typedef struct dgxm_prologue_desc {
+  int32_t world;
+  int32_t rank;
+  int32_t batch;
+  int32_t seq_local;
+  int32_t heads;    /* heads * 128 <= 6144 */
+  int32_t head_dim; /* 128 */
+  int32_t norm_mode;
+  float eps;
+  int64_t src_stride[3][3];  /* q, k, v: batch, row, head (elements), bf16 */
+  int64_t rope_batch_stride; /* elements between batch items of the rope table; 0 = shared */
+  int32_t seg0;              /* joint order, as in dgxm_a2a_desc */
+} dgxm_prologue_desc;
+
+/*
+ * The Ulysses scatter with the per-token math the family forwards run right
+ * before the attention seam fused in: RMSNorm of q and k (weights bf16, NULL
+ * for none), then RoPE from `rope` -- fp32 (rows, head_dim/2, 2) cos/sin per
+ * local row, rotating consecutive pairs (x0 c - x1 s, x0 s + x1 c) -- and the
+ * head-sliced peer stores of dgxm_ulysses_scatter (dst as there).  V moves
+ * unchanged.  Replaces the separate norm / apply_rope1 / all-to-all / permute
+ * ops of adapters/wan_family.py:70-73 followed by
+ * adapters/usp_full_axis.py:27-29.
+ */
+int dgxm_qkv_prologue_scatter(const dgxm_prologue_desc* desc, const void* const* src,
+                              const void* norm_q_w, const void* norm_k_w, const float* rope,
+                              void* const* dst, void* stream);
+
+/* ------------------------------------------------------------ FP8 inputs */
+/*
+ * Per-head e4m3 quantisation of a bf16 (batch, rows, heads, 128) tensor
+ * (strides in elements): descale[h] = absmax over head h / 448 (fp32) and
+ * out = e4m3(x / descale[h]), contiguous.  The inputs of dgxm_attn_fwd's
+ * e4m3 path (FP8 config: per-head fp32 absmax scales).  After a Ulysses
+ * scatter every head lives whole on one rank, so the scale needs no
+ * cross-rank reduction.
+ */
+int dgxm_quantize_e4m3_per_head(int32_t batch, int32_t rows, int32_t heads, int32_t head_dim,
+                                const void* x, const int64_t* stride, void* out, float* descale,
+                                void* stream);
 
 /* ------------------------------------------------------------ ring attention */
 /*

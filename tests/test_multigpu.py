@@ -88,3 +88,93 @@ def _ulysses_case(rank, world, dev):
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
 def test_ulysses_across_gpus_matches_unsharded_attention():
     _spawn(_ulysses_case, min(torch.cuda.device_count(), 4))
+
+
+def _ring_case(rank, world, dev):
+    from dgx_monarch_b200 import _lib
+    from dgx_monarch_b200.ring import RingAttention
+    from tests.test_attn_gpu import BF16_REL_L2, reference_attention, rel_l2
+
+    rows, heads = 500, 3
+    g = torch.Generator(device=dev).manual_seed(7)
+    q, k, v = (torch.randn(1, rows * world, heads, 128, device=dev, generator=g).bfloat16() for _ in range(3))
+    sl = slice(rank * rows, (rank + 1) * rows)
+    ring = RingAttention(world=world, rank=rank, batch=1, q_len=rows, kv_len=rows, heads=heads,
+                         kv_heads=heads, head_dim=128, device=dev, generation=2)
+    lse = torch.empty(1, heads, rows, device=dev, dtype=torch.float32)
+    for _ in range(3):
+        out, _ = ring.forward(q[:, sl].contiguous(), k[:, sl].contiguous(), v[:, sl].contiguous(), lse=lse)
+    torch.cuda.synchronize()
+    ref, ref_lse = reference_attention(q, k, v)
+    assert rel_l2(out, ref[:, sl]) <= BF16_REL_L2
+    assert (lse - ref_lse[:, :, sl]).abs().max().item() <= 2e-3
+    assert _lib.device_error() == 0
+    ring.close()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
+def test_ring_across_gpus_matches_unsharded_attention():
+    _spawn(_ring_case, min(torch.cuda.device_count(), 4))
+
+
+def _callable_case(rank, world, dev):
+    """The drop-in usp_attention on a Ulysses group: plain, joint order with
+    pad rows, and native GQA, against unsharded attention."""
+    import torch.distributed as dist
+
+    from dgx_monarch_b200 import _lib
+    from dgx_monarch_b200.usp import make_b200_usp_attention
+    from oracle import usp as oracle_usp
+    from tests.test_attn_gpu import BF16_MAX_ABS, BF16_REL_L2, reference_attention, rel_l2
+
+    group = dist.new_group(list(range(world)))
+    attn = make_b200_usp_attention(ulysses_group=group, generation=3, device=dev)
+    heads, d = 2 * world, 128
+    # 1) plain Ulysses, comfy (B, L, H*D) layout
+    ls = 256
+    g = torch.Generator(device=dev).manual_seed(31)
+    q, k, v = (torch.randn(1, ls * world, heads, d, device=dev, generator=g).bfloat16() for _ in range(3))
+    sl = slice(rank * ls, (rank + 1) * ls)
+    out = attn(*(t[:, sl].reshape(1, ls, -1) for t in (q, k, v)), heads=heads)
+    ref, _ = reference_attention(q, k, v)
+    assert rel_l2(out.reshape(1, ls, heads, d), ref[:, sl]) <= BF16_REL_L2
+    # 2) joint [text, image] order with one image pad row on the last rank
+    text, image = 32, 96
+    ls2 = text + image
+    txt = [torch.randn(1, text * world, heads, d, device=dev, generator=g).bfloat16() for _ in range(3)]
+    img = [torch.randn(1, image * world, heads, d, device=dev, generator=g).bfloat16() for _ in range(3)]
+    for t in img:
+        t[:, -1] = 0  # the synthetic pad shard_seq appends
+    local = [torch.cat((tt[:, rank * text:(rank + 1) * text], ii[:, rank * image:(rank + 1) * image]), dim=1)
+             for tt, ii in zip(txt, img)]
+    pad = [(world - 1) * ls2 + ls2 - 1]  # rank-major coordinate of the last image row
+    order = oracle_usp.RankMajorJointOrder(text, image)
+    out2 = attn(*(t.transpose(1, 2) for t in local), heads=heads, skip_reshape=True,
+                skip_output_reshape=True, drop_rows=pad, sequence_order=order).transpose(1, 2)
+    full = [torch.cat((tt, ii[:, :-1]), dim=1) for tt, ii in zip(txt, img)]  # stock order, pad dropped
+    ref2, _ = reference_attention(*full)
+    want_txt = ref2[:, rank * text:(rank + 1) * text]
+    img_rows = ref2[:, text * world:]
+    want_img = img_rows[:, rank * image:(rank + 1) * image]
+    got_img = out2[:, text:]
+    if rank == world - 1:
+        assert torch.equal(got_img[:, -1], torch.zeros_like(got_img[:, -1]))
+        got_img = got_img[:, :-1]
+    assert (out2[:, :text].float() - want_txt).abs().max().item() <= BF16_MAX_ABS
+    assert (got_img.float() - want_img).abs().max().item() <= BF16_MAX_ABS
+    # 3) native GQA: K/V heads split by the Ulysses degree
+    hkv = world
+    qg = torch.randn(1, ls * world, heads, d, device=dev, generator=g).bfloat16()
+    kg, vg = (torch.randn(1, ls * world, hkv, d, device=dev, generator=g).bfloat16() for _ in range(2))
+    out3 = attn(qg[:, sl].reshape(1, ls, -1), kg[:, sl].reshape(1, ls, -1), vg[:, sl].reshape(1, ls, -1),
+                heads=heads, enable_gqa=True)
+    ref3, _ = reference_attention(qg, kg, vg)
+    assert rel_l2(out3.reshape(1, ls, heads, d), ref3[:, sl]) <= BF16_REL_L2
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    attn.impl.invalidate()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
+def test_usp_callable_across_gpus():
+    _spawn(_callable_case, min(torch.cuda.device_count(), 4))
