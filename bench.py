@@ -165,6 +165,84 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------- DiT layer
+DIT = {"hidden": 3072, "heads": 24, "img": 9216, "txt": 512, "latent": (96, 96)}
+DIT_WORKLOAD = ("Flux/Krea2-style joint-attention DiT double block (attention sub-layer): "
+                "1536x1536 image -> 96x96 patch grid = 9216 tokens + 512 text tokens, hidden 3072, "
+                "24 heads x 128, bf16, random-init weights N(0, 0.02); QKV and out projections, "
+                "per-head RMSNorm on Q/K, 2-axis RoPE, joint [text, image] attention")
+
+
+def dit_layer_flops() -> float:
+    s, hid = DIT["img"] + DIT["txt"], DIT["hidden"]
+    return 2.0 * s * hid * 3 * hid + 2.0 * s * hid * hid + attn_flops(1, DIT["heads"], s, DIM)
+
+
+def run_dit_layer(world: int, rank: int, dev, steps: int, warmup: int, group=None) -> dict:
+    """One C2 double-block attention sub-layer per step, Ulysses over `world`."""
+    import torch
+
+    from dgx_monarch_b200 import _lib
+    from dgx_monarch_b200.comm import PeerWindows
+    from dgx_monarch_b200.prologue import qkv_prologue_scatter, rope_table
+    from dgx_monarch_b200.ulysses import attention_routed
+
+    hid, h = DIT["hidden"], DIT["heads"]
+    t_loc, i_loc = DIT["txt"] // world, DIT["img"] // world
+    ls = t_loc + i_loc
+    s = ls * world
+    hl = h // world
+    g = torch.Generator(device=dev).manual_seed(77 + rank)
+    w = lambda *shape: (0.02 * torch.randn(*shape, device=dev, generator=g)).bfloat16()
+    x_txt, x_img = w(1, t_loc, hid) * 50, w(1, i_loc, hid) * 50
+    w_qkv_txt, w_qkv_img = w(hid, 3 * hid), w(hid, 3 * hid)
+    w_o_txt, w_o_img = w(hid, hid), w(hid, hid)
+    nq, nk = (1 + w(128)).contiguous(), (1 + w(128)).contiguous()
+    # Positions: text tokens at 0, image tokens at (0, row, col) of the 96x96 grid.
+    img_ids = torch.arange(rank * i_loc, (rank + 1) * i_loc, device=dev)
+    pos = torch.cat((torch.zeros(t_loc, 3, device=dev, dtype=torch.long),
+                     torch.stack((torch.zeros_like(img_ids), img_ids // 96, img_ids % 96), dim=1)))
+    table = rope_table(pos, [16, 56, 56])
+    qkv = torch.empty(1, ls, 3, h, DIM, device=dev, dtype=torch.bfloat16)
+    elt = 2
+    recv_bytes = s * hl * DIM * elt
+    out_bytes = ls * h * DIM * elt
+    win = PeerWindows(3 * recv_bytes + out_bytes + 1024, device=dev, group=group, rank=rank,
+                      world=world, generation=11)
+    offs = [win.carve(recv_bytes) for _ in range(3)] + [win.carve(out_bytes)]
+    recv = [win.local_tensor(o, (1, s, hl, DIM), torch.bfloat16) for o in offs[:3]]
+    out_local = win.local_tensor(offs[3], (1, ls, h, DIM), torch.bfloat16)
+    y = torch.empty(1, ls, hid, device=dev, dtype=torch.bfloat16)
+
+    def step():
+        torch.matmul(x_txt, w_qkv_txt, out=qkv[:, :t_loc].view(1, t_loc, 3 * hid))
+        torch.matmul(x_img, w_qkv_img, out=qkv[:, t_loc:].view(1, i_loc, 3 * hid))
+        qkv_prologue_scatter(qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2],
+                             [[win.peer_ptr(r, o) for r in range(world)] for o in offs[:3]],
+                             world=world, rank=rank, norm_mode=_lib.NORM_HEAD, norm_q_w=nq,
+                             norm_k_w=nk, rope=table, seg0=t_loc)
+        win.barrier()
+        attention_routed(recv[0], recv[1], recv[2], [win.peer_ptr(r, offs[3]) for r in range(world)],
+                         (ls * h * DIM, h * DIM, DIM), world=world, rank=rank, seq_local=ls, seg0=t_loc)
+        win.barrier()
+        o = out_local.view(1, ls, hid)
+        torch.matmul(o[:, :t_loc], w_o_txt, out=y[:, :t_loc])
+        torch.matmul(o[:, t_loc:], w_o_img, out=y[:, t_loc:])
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    win.close()
+    return {"ms": ms, "my_launches": 4 if world > 1 else 2}
+
+
 # ----------------------------------------------------------------- our arm
 def main() -> None:
     args = parse_args()
@@ -260,6 +338,11 @@ def main() -> None:
     if world > 1:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_ms = te.item()
+    dit = run_dit_layer(world, rank, dev, max(5, args.steps), args.warmup)
+    td = torch.tensor([dit["ms"]], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(td, op=dist.ReduceOp.MAX)
+    dit_ms = td.item()
     dev_err = _lib.device_error()
 
     if rank == 0:
@@ -294,6 +377,10 @@ def main() -> None:
                     "h2d_bytes_per_step": 3 * q.numel() * q.element_size(),
                     "d2h_bytes_per_step": out.numel() * out.element_size(),
                     "ms_per_step": e2e_ms},
+            "dit_layer": {"workload": DIT_WORKLOAD, "tokens_per_s": (DIT["img"] + DIT["txt"]) / (dit_ms * 1e-3),
+                          "ms_per_layer": dit_ms, "tflops": dit_layer_flops() / (dit_ms * 1e-3) / 1e12,
+                          "frac_of_bf16_peak": dit_layer_flops() / (dit_ms * 1e-3) / 1e12 / peaks["bf16_tflops"],
+                          "parallelism": f"ulysses{world}"},
             "gpu_launches": launches,
             "clocks": clk,
             "device_error": dev_err,

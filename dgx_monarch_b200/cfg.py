@@ -68,6 +68,10 @@ class CfgGather:
 
     def __init__(self, nbytes_per_rank: int, *, device: torch.device, group=None, rank: int = 0,
                  world: int = 1, generation: int = 0) -> None:
+        import torch.distributed as dist
+
+        if group is not None or (world > 1 and dist.is_initialized()):
+            world = dist.get_world_size(group)
         self.windows = PeerWindows(nbytes_per_rank * max(world, 1) + 256, device=device,
                                    group=group, rank=rank, world=world, generation=generation)
         self.world, self.rank, self.device = self.windows.world, self.windows.rank, device

@@ -6,11 +6,13 @@
 // S0 = Q0 K_j^T into probabilities, the tensor core computes P1 V_{j-1} and
 // S1 = Q1 K_j^T, and vice versa, so the exponentials overlap the MMAs.
 //
-// Warp roles (10 warps, 320 threads):
-//   warps 0-3  softmax + output correction + epilogue for Q tile 0
-//   warps 4-7  the same for Q tile 1
-//   warp  8    TMA producer (Q once, then K_j / V_j through a stage ring)
-//   warp  9    TMEM allocator and single-thread MMA issuer
+// Warp roles (18 warps, 576 threads):
+//   warps 0-7   softmax + output correction + epilogue for Q tile 0: two
+//               threads per row, warps 0-3 own key columns 0-63 of the
+//               tile's rows, warps 4-7 columns 64-127
+//   warps 8-15  the same for Q tile 1
+//   warp  16    TMA producer (Q once, then K_j / V_j through a stage ring)
+//   warp  17    TMEM allocator and single-thread MMA issuer
 //
 // Tensor memory (512 columns x 128 lanes x 32 bit):
 //   [  0,128) S0 (fp32 logits); P0 overwrites its first columns (bf16 pairs
@@ -30,9 +32,24 @@
 #include "device_error.cuh"
 #include "ptx.cuh"
 
+// Softmax instruction choices (all compute the same function):
+//   DGXM_SM_MAX3      three-input max for the row reduction
+//   DGXM_SM_POLY_MOD  every N-th pair of exponentials on the FMA pipe
+//                     (exp2_poly2) instead of MUFU; 0 disables
+#ifndef DGXM_SM_MAX3
+#define DGXM_SM_MAX3 1
+#endif
+#ifndef DGXM_SM_POLY_MOD
+#define DGXM_SM_POLY_MOD 8
+#endif
+
 namespace dgxm {
 
-constexpr int kAttnThreads = 320;
+constexpr int kSoftmaxWarps = 16;  // 2 tiles x 2 column halves x 4 lane quarters
+constexpr int kProducerWarp = 16;
+constexpr int kMmaWarp = 17;        // allocates TMEM and issues every MMA (one thread)
+constexpr int kAttnThreads = 18 * 32;
+constexpr int kCtrlXmaxOffset = 1024;  // row-max / row-sum exchange area inside the control block
 constexpr int kTileRows = 128;   // rows per Q tile and per K/V tile
 constexpr int kHeadDim = 128;
 constexpr float kLog2e = 1.4426950408889634f;
@@ -55,10 +72,11 @@ struct AttnCfg {
   // e4m3 probabilities are stored scaled by 2^4 so typical values sit in the
   // normal range; the epilogue divides the factor back out.
   static constexpr float kPScale = FP8 ? 16.0f : 1.0f;
+  static constexpr float kPScaleLog2 = FP8 ? 4.0f : 0.0f;
   static constexpr uint32_t kIdescQK = idesc_make(128, 128, FP8 ? 0u : 1u, false);
   static constexpr uint32_t kIdescPV = idesc_make(128, 128, FP8 ? 0u : 1u, true);
   static constexpr int kSmemBytes = 1024 /*align slack*/ + 2 * kTileBytes + kStages * kTileBytes +
-                                    256 /*barriers + slots*/;
+                                    1024 /*barriers + slots*/ + 12 * 128 * 4 /*row exchange*/;
 };
 
 struct __align__(64) AttnParams {
@@ -99,15 +117,38 @@ struct Bars {
   static constexpr int kCount = kDrain + 1;
 };
 
+// Shared-memory descriptors split into a low word (start address in 16-byte
+// units | leading byte offset) and a constant high word (stride byte offset,
+// sm100 version, 128-byte swizzle).  The MMA issuer keeps one low word per
+// tile and adds compile-time offsets, so each MMA costs one integer add per
+// operand: the issuing thread shares its SM sub-partition with softmax warps
+// and must not spend its issue slots on descriptor arithmetic.
+__host__ __device__ constexpr uint32_t sdesc_hi(uint32_t sbo_bytes) {
+  return ((sbo_bytes >> 4) & 0x3FFFu) | (1u << 14) | (2u << 29);
+}
+
+__device__ __forceinline__ uint32_t sdesc_lo(uint32_t saddr, uint32_t lbo_bytes) {
+  return ((saddr >> 4) & 0x3FFFu) | (((lbo_bytes >> 4) & 0x3FFFu) << 16);
+}
+
+__device__ __forceinline__ uint64_t sdesc_join(uint32_t lo, uint32_t hi) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "r"(lo), "r"(hi));
+  return d;
+}
+
+// S = Q K^T: both operands K-major, one 128-byte swizzle atom per 64 (bf16)
+// or 128 (e4m3) head-dim columns.  q_lo / k_lo are the tiles' low words.
 template <bool FP8>
-__device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t sq, uint32_t sk) {
+__device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_lo, uint32_t k_lo) {
   using C = AttnCfg<FP8>;
+  constexpr uint32_t hi = sdesc_hi(1024);
 #pragma unroll
   for (int kk = 0; kk < C::kKSteps; ++kk) {
     const uint32_t byte = kk * 32;  // each MMA consumes 32 bytes of the head dimension
-    const uint32_t off = (byte / 128) * C::kBoxBytes + (byte % 128);
-    const uint64_t a = sdesc_sw128(sq + off, 16, 1024);
-    const uint64_t b = sdesc_sw128(sk + off, 16, 1024);
+    const uint32_t off = ((byte / 128) * C::kBoxBytes + (byte % 128)) >> 4;
+    const uint64_t a = sdesc_join(q_lo + off, hi);
+    const uint64_t b = sdesc_join(k_lo + off, hi);
     if constexpr (FP8)
       umma_f8_ss(d_tmem, a, b, C::kIdescQK, kk > 0 ? 1u : 0u);
     else
@@ -115,15 +156,17 @@ __device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t sq, uint32_t 
   }
 }
 
+// O += P V: P from tensor memory, V MN-major (head_dim along the 128-byte
+// rows, keys down the rows; the second 128-byte column block of bf16 sits
+// kBoxBytes further, the leading byte offset).
 template <bool FP8>
-__device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint32_t sv,
+__device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_lo,
                                          bool accumulate) {
   using C = AttnCfg<FP8>;
+  constexpr uint32_t hi = sdesc_hi(1024);
 #pragma unroll
   for (int kk = 0; kk < C::kKSteps; ++kk) {
-    // B = V viewed MN-major: head_dim along the 128-byte rows, keys down the
-    // rows; the second 128-byte column block (bf16) sits kBoxBytes further.
-    const uint64_t b = sdesc_sw128(sv + kk * C::kMmaK * 128, C::kBoxBytes, 1024);
+    const uint64_t b = sdesc_join(v_lo + ((kk * C::kMmaK * 128) >> 4), hi);
     const uint32_t a = p_tmem + kk * (C::kMmaK * C::kEltBytes / 4);
     const uint32_t acc = (accumulate || kk > 0) ? 1u : 0u;
     if constexpr (FP8)
@@ -165,7 +208,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(bar(B::kSFull + t), 1);
-      mbar_init(bar(B::kPFull + t), 128);
+      mbar_init(bar(B::kPFull + t), 256);
       mbar_init(bar(B::kOFull + t), 1);
       mbar_init(bar(B::kPvDone + t), 1);
     }
@@ -173,12 +216,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
     *abort_flag = 0;
     mbar_fence_init();
   }
-  if (warp == 8 && lane == 0) {
+  if (warp == kProducerWarp && lane == 0) {
     tma_prefetch_desc(&p.tmap_q);
     tma_prefetch_desc(&p.tmap_k);
     tma_prefetch_desc(&p.tmap_v);
   }
-  if (warp == 9) {
+  if (warp == kMmaWarp) {
     tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
   }
@@ -195,12 +238,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
   const int nkv = p.n_kv_tiles;
   const bool safe_order = (p.flags & DGXM_ATTN_SAFE_ORDER) != 0;
 
-  if (warp == 8) {
+  if (warp == kProducerWarp) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      int issued[C::kStages];
-#pragma unroll
-      for (int s = 0; s < C::kStages; ++s) issued[s] = -1;
+      int issued_count = 0;  // loads issued into the K/V ring so far
       bool ok = true;
       const uint64_t keep = l2_policy_evict_last();   // K/V are re-read by every Q tile
       const uint64_t once = l2_policy_evict_first();  // Q is read by this CTA only
@@ -223,21 +264,32 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
           tma_load_4d_hint(sKV + s * C::kTileBytes + c * C::kBoxBytes, map,
                            bar(B::kKvFull + s), c * C::kBoxCols, hk, (idx >> 1) * kTileRows, b,
                            keep);
-        issued[s] = ph;
+        issued_count = idx + 1;
       }
       if (!ok) {
         raise_abort(abort_flag, kErrProducerTimeout);
         // Let the copies already in flight land before the CTA can exit.
         mbar_wait(bar(B::kQ), 0, nullptr);
-        for (int s = 0; s < C::kStages; ++s)
-          if (issued[s] >= 0) mbar_wait(bar(B::kKvFull + s), issued[s], nullptr);
+        const int first = issued_count > C::kStages ? issued_count - C::kStages : 0;
+        for (int idx = first; idx < issued_count; ++idx)
+          mbar_wait(bar(B::kKvFull + idx % C::kStages), (idx / C::kStages) & 1, nullptr);
       }
     }
     __syncwarp();
-  } else if (warp == 9) {
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
+    // One thread issues both tiles' products in the order
+    //   S0_j = Q0 K_j^T, O1 += P1_{j-1} V_{j-1}, S1_j = Q1 K_j^T, O0 += P0_j V_j
+    // so each softmax group's exponentials overlap the other tile's two
+    // products.  P_t sits in S_t's tensor memory, so S_t of the next block is
+    // issued only after the P_t V that reads it (tcgen05 operations of one
+    // thread execute in issue order; DGXM_ATTN_SAFE_ORDER drains instead).
     if (lane == 0) {
       const uint32_t tS0 = tmem, tS1 = tmem + 128, tO0 = tmem + 256, tO1 = tmem + 384;
+      const uint32_t q0_lo = sdesc_lo(sQ, 16), q1_lo = sdesc_lo(sQ + C::kTileBytes, 16);
+      const uint32_t kv_lo_k = sdesc_lo(sKV, 16);             // stage 0, K-major view
+      const uint32_t kv_lo_v = sdesc_lo(sKV, C::kBoxBytes);   // stage 0, MN-major view
+      constexpr uint32_t kStageLo = C::kTileBytes >> 4;       // low-word step per stage
       bool ok = mbar_wait(bar(B::kQ), 0, abort_flag);
       tc_fence_after();
       for (int j = 0; ok && j < nkv; ++j) {
@@ -250,14 +302,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
           if (!(ok = mbar_wait(bar(B::kPvDone + 0), (j - 1) & 1, abort_flag))) break;
           tc_fence_after();
         }
-        issue_qk<FP8>(tS0, sQ, sKV + ks * C::kTileBytes);
+        issue_qk<FP8>(tS0, q0_lo, kv_lo_k + ks * kStageLo);
         umma_commit(bar(B::kSFull + 0));
         // O1 += P1 V_{j-1}
         if (j > 0) {
           const int vs = (2 * j - 1) % C::kStages;
           if (!(ok = mbar_wait(bar(B::kPFull + 1), (j - 1) & 1, abort_flag))) break;
           tc_fence_after();
-          issue_pv<FP8>(tO1, tS1, sKV + vs * C::kTileBytes, j - 1 > 0);
+          issue_pv<FP8>(tO1, tS1, kv_lo_v + vs * kStageLo, j - 1 > 0);
           umma_commit(bar(B::kKvEmpty + vs));
           if (safe_order) {
             umma_commit(bar(B::kPvDone + 1));
@@ -266,7 +318,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
           }
         }
         // S1 = Q1 K_j^T
-        issue_qk<FP8>(tS1, sQ + C::kTileBytes, sKV + ks * C::kTileBytes);
+        issue_qk<FP8>(tS1, q1_lo, kv_lo_k + ks * kStageLo);
         umma_commit(bar(B::kSFull + 1));
         umma_commit(bar(B::kKvEmpty + ks));
         // O0 += P0 V_j
@@ -275,7 +327,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
         if (!(ok = mbar_wait(bar(B::kKvFull + vs), (vi / C::kStages) & 1, abort_flag))) break;
         if (!(ok = mbar_wait(bar(B::kPFull + 0), j & 1, abort_flag))) break;
         tc_fence_after();
-        issue_pv<FP8>(tO0, tS0, sKV + vs * C::kTileBytes, j > 0);
+        issue_pv<FP8>(tO0, tS0, kv_lo_v + vs * kStageLo, j > 0);
         if (safe_order) umma_commit(bar(B::kPvDone + 0));
         if (j == nkv - 1) umma_commit(bar(B::kOFull + 0));
       }
@@ -285,7 +337,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
         ok = mbar_wait(bar(B::kPFull + 1), (nkv - 1) & 1, abort_flag);
         if (ok) {
           tc_fence_after();
-          issue_pv<FP8>(tO1, tS1, sKV + vs * C::kTileBytes, nkv - 1 > 0);
+          issue_pv<FP8>(tO1, tS1, kv_lo_v + vs * kStageLo, nkv - 1 > 0);
           umma_commit(bar(B::kKvEmpty + vs));
           umma_commit(bar(B::kOFull + 1));
         }
@@ -300,47 +352,87 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
     __syncwarp();
   } else {
     // ------------------------------------------------------------ softmax
-    const int t = warp >> 2;    // Q tile of this warpgroup
-    const int sub = warp & 3;   // TMEM lane quarter this warp may access
-    const int r = sub * 32 + lane;
+    // Two threads per query row: warps 4c..4c+3 of a tile's group own the
+    // key columns [64c, 64c+64) of every row of their TMEM lane quarter.
+    // The halves exchange row maxima through shared memory behind a named
+    // barrier, so both apply the same running max; each keeps a partial row
+    // sum and rescales / writes its own half of the output columns.
+    const int t = warp / 8;          // Q tile of this group
+    const int c = (warp / 4) & 1;    // column half
+    const int sub = warp & 3;        // TMEM lane quarter this warp may access
+    const int r = sub * 32 + lane;   // row within the tile
     const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
-    const uint32_t tS = tmem + lane_off + t * 128;
-    const uint32_t tO = tmem + lane_off + 256 + t * 128;
+    const uint32_t tS = tmem + lane_off + t * 128 + c * 64;
+    const uint32_t tP = tmem + lane_off + t * 128 + c * (C::kPCols / 2);
+    const uint32_t tO = tmem + lane_off + 256 + t * 128 + c * 64;
+    float* xmax = reinterpret_cast<float*>(ctrl + kCtrlXmaxOffset);  // [2 parity][2 tile][2 half][128]
     float sl2 = p.scale_log2;
     if constexpr (FP8) sl2 *= p.q_descale[h] * p.k_descale[hk];
     float m_run = -INFINITY;  // running max of the scaled logits, log2 units
-    float l_run = 0.f;        // running sum of exp2(s * sl2 - m_run)
+    float l_run = 0.f;        // this half's running sum of exp2(s * sl2 - m_run)
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
-      ok = __all_sync(0xffffffffu, mbar_wait(bar(B::kSFull + t), j & 1, abort_flag));
-      if (!ok) break;
-      tc_fence_after();
-      uint32_t sr[4][32];
+      const bool got = __all_sync(0xffffffffu, mbar_wait(bar(B::kSFull + t), j & 1, abort_flag));
+      if (!got) raise_abort(abort_flag, kErrSoftmaxTimeout);
+      uint32_t sr[2][32];
+      if (got) {
+        tc_fence_after();
+        tmem_ld32(tS, sr[0]);
+        tmem_ld32(tS + 32, sr[1]);
+        tmem_wait_ld();
+      } else {
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, sr[c]);
-      tmem_wait_ld();
+        for (int i = 0; i < 32; ++i) sr[0][i] = sr[1][i] = 0u;
+      }
+      reg_fence32(sr[0]);
+      reg_fence32(sr[1]);
+      float s[64];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) reg_fence32(sr[c]);
-      float s[128];
+      for (int h2 = 0; h2 < 2; ++h2)
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
+        for (int i = 0; i < 32; ++i) s[h2 * 32 + i] = __uint_as_float(sr[h2][i]);
+      const int valid = p.kv_len - j * kTileRows - c * 64;
+      if (valid < 64) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(sr[c][i]);
-      const int valid = p.kv_len - j * kTileRows;
-      if (valid < kTileRows) {
-#pragma unroll
-        for (int i = 0; i < 128; ++i)
+        for (int i = 0; i < 64; ++i)
           if (i >= valid) s[i] = -INFINITY;
       }
+#if DGXM_SM_MAX3
+      float mx0 = fmax3(s[0], s[1], s[2]), mx1 = fmax3(s[3], s[4], s[5]);
+      float mx2 = fmax3(s[6], s[7], s[8]), mx3 = fmax3(s[9], s[10], s[11]);
+#pragma unroll
+      for (int i = 12; i < 60; i += 8) {
+        mx0 = fmax3(mx0, s[i], s[i + 1]);
+        mx1 = fmax3(mx1, s[i + 2], s[i + 3]);
+        mx2 = fmax3(mx2, s[i + 4], s[i + 5]);
+        mx3 = fmax3(mx3, s[i + 6], s[i + 7]);
+      }
+      const float half_max = fmaxf(fmax3(mx0, mx1, fmax3(s[60], s[61], s[62])), fmax3(mx2, mx3, s[63]));
+#else
       float mx0 = s[0], mx1 = s[1], mx2 = s[2], mx3 = s[3];
 #pragma unroll
-      for (int i = 4; i < 128; i += 4) {
+      for (int i = 4; i < 64; i += 4) {
         mx0 = fmaxf(mx0, s[i]);
         mx1 = fmaxf(mx1, s[i + 1]);
         mx2 = fmaxf(mx2, s[i + 2]);
         mx3 = fmaxf(mx3, s[i + 3]);
       }
-      const float m_cand = fmaxf(m_run, fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2);
+      const float half_max = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+#endif
+      // Exchange with the other half of the row.  Double-buffered by
+      // iteration parity: a buffer is rewritten two barriers after it was read.
+      float* xm = xmax + ((j & 1) * 4 + t * 2) * 128;
+      xm[c * 128 + r] = half_max;
+      // Every warp of the group arrives here exactly once per iteration, and
+      // all of them take the same stop decision, so the barrier counts of
+      // later iterations can never mismatch.
+      if (named_barrier_or(1 + t, 256, !got || *abort_flag != 0)) {
+        ok = false;
+        break;
+      }
+      const float row_max = fmaxf(half_max, xm[(c ^ 1) * 128 + r]);
+      const float m_cand = fmaxf(m_run, row_max * sl2);
+      // Both halves of a row see the same maximum, so their warp votes agree.
       const bool grow = m_cand > m_run + C::kThr;
       float alpha = 1.f;
       bool rescale = false;
@@ -350,44 +442,59 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
         rescale = j > 0;
       }
       l_run *= alpha;
-      const float neg_m = -m_run;
-      float sum0 = 0.f, sum1 = 0.f;
+      // p = 2^(s * sl2 - m) (times kPScale for e4m3, folded into the exponent).
+      const float bias = -m_run + C::kPScaleLog2;
+      const uint64_t sl2x2 = pk2(sl2, sl2), biasx2 = pk2(bias, bias);
+      uint64_t sum_a = pk2(0.f, 0.f), sum_b = pk2(0.f, 0.f);
+      uint32_t pk[32];
 #pragma unroll
-      for (int i = 0; i < 128; i += 2) {
-        s[i] = ex2_approx(fmaf(s[i], sl2, neg_m));
-        s[i + 1] = ex2_approx(fmaf(s[i + 1], sl2, neg_m));
-        sum0 += s[i];
-        sum1 += s[i + 1];
-      }
-      l_run += sum0 + sum1;
-      if constexpr (FP8) {
-        uint32_t pk[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          pk[i] = pack_e4m3x4(s[4 * i] * C::kPScale, s[4 * i + 1] * C::kPScale,
-                              s[4 * i + 2] * C::kPScale, s[4 * i + 3] * C::kPScale);
-        tmem_st32(tS, pk);
-      } else {
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          uint32_t pk[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) pk[i] = pack_bf16x2(s[64 * c + 2 * i], s[64 * c + 2 * i + 1]);
-          tmem_st32(tS + c * 32, pk);
+      for (int i = 0; i < 32; ++i) {
+        uint64_t x = ffma2(pk2(s[2 * i], s[2 * i + 1]), sl2x2, biasx2);
+        float p0, p1;
+        if (DGXM_SM_POLY_MOD > 0 && (i % (DGXM_SM_POLY_MOD > 0 ? DGXM_SM_POLY_MOD : 1)) == 0) {
+          x = exp2_poly2(x);
+          upk2(x, p0, p1);
+        } else {
+          upk2(x, p0, p1);
+          p0 = ex2_approx(p0);
+          p1 = ex2_approx(p1);
+          x = pk2(p0, p1);
         }
+        if (i & 1) sum_b = fadd2(sum_b, x); else sum_a = fadd2(sum_a, x);
+        if constexpr (FP8) {
+          s[2 * i] = p0;
+          s[2 * i + 1] = p1;
+        } else {
+          pk[i] = pack_bf16x2(p0, p1);
+        }
+      }
+      {
+        float a0, a1, b0, b1;
+        upk2(sum_a, a0, a1);
+        upk2(sum_b, b0, b1);
+        l_run += ((a0 + a1) + (b0 + b1)) * (1.0f / C::kPScale);
+      }
+      if constexpr (FP8) {
+        uint32_t q8[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          q8[i] = pack_e4m3x4(s[4 * i], s[4 * i + 1], s[4 * i + 2], s[4 * i + 3]);
+        tmem_st16(tP, q8);
+      } else {
+        tmem_st32(tP, pk);
       }
       if (rescale) {
         // O_t is quiescent here: the commit behind this S_t also covered the
         // previous P_t V product.
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int h2 = 0; h2 < 2; ++h2) {
           uint32_t o[32];
-          tmem_ld32(tO + c * 32, o);
+          tmem_ld32(tO + h2 * 32, o);
           tmem_wait_ld();
           reg_fence32(o);
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st32(tO + c * 32, o);
+          tmem_st32(tO + h2 * 32, o);
         }
       }
       tmem_wait_st();
@@ -395,13 +502,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
       mbar_arrive(bar(B::kPFull + t));
     }
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar(B::kOFull + t), 0, abort_flag));
+    // Combine the two halves' row sums (all threads of the group take part,
+    // so the barrier is reached even when a wait above gave up).
+    float* lsum = xmax + (8 + t * 2) * 128;
+    lsum[c * 128 + r] = l_run;
+    named_barrier_sync(1 + t, 256);
+    const float l_row = l_run + lsum[(c ^ 1) * 128 + r];
     if (!ok) {
       raise_abort(abort_flag, kErrSoftmaxTimeout);
     } else {
       tc_fence_after();
       const int grow = row0 + t * kTileRows + r;
       const bool row_ok = grow < p.q_len;
-      float inv = 1.f / (l_run * C::kPScale);
+      float inv = 1.f / (l_row * C::kPScale);
       if constexpr (FP8) inv *= p.v_descale[hk];
       void* obase = p.o;
       int orow_idx = grow;
@@ -429,23 +542,24 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
       char* orow = static_cast<char*>(obase) +
                    (static_cast<int64_t>(b) * p.o_sb + static_cast<int64_t>(orow_idx) * p.o_sl +
                     static_cast<int64_t>(ohead) * p.o_sh) *
-                       (OUT_F32 ? 4 : 2);
+                       (OUT_F32 ? 4 : 2) +
+                   c * 64 * (OUT_F32 ? 4 : 2);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int h2 = 0; h2 < 2; ++h2) {
         uint32_t o[32];
-        tmem_ld32(tO + c * 32, o);
+        tmem_ld32(tO + h2 * 32, o);
         tmem_wait_ld();
         reg_fence32(o);
         if (row_ok) {
           if constexpr (OUT_F32) {
-            float4* dst = reinterpret_cast<float4*>(orow + c * 128);
+            float4* dst = reinterpret_cast<float4*>(orow + h2 * 128);
 #pragma unroll
             for (int i = 0; i < 8; ++i)
               dst[i] = make_float4(__uint_as_float(o[4 * i]) * inv, __uint_as_float(o[4 * i + 1]) * inv,
                                    __uint_as_float(o[4 * i + 2]) * inv,
                                    __uint_as_float(o[4 * i + 3]) * inv);
           } else {
-            uint4* dst = reinterpret_cast<uint4*>(orow + c * 64);
+            uint4* dst = reinterpret_cast<uint4*>(orow + h2 * 64);
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
               uint4 w;
@@ -458,15 +572,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
           }
         }
       }
-      if (row_ok && p.lse != nullptr) {
+      if (c == 0 && row_ok && p.lse != nullptr) {
         p.lse[static_cast<int64_t>(b) * p.lse_sb + static_cast<int64_t>(h) * p.lse_sh +
-              static_cast<int64_t>(grow) * p.lse_sl] = (m_run + log2f(l_run)) * kLn2;
+              static_cast<int64_t>(grow) * p.lse_sl] = (m_run + log2f(l_row)) * kLn2;
       }
     }
   }
-
   __syncthreads();
-  if (warp == 9) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }

@@ -251,11 +251,101 @@ __device__ __forceinline__ void reg_fence32(uint32_t (&r)[32]) {
                  "+r"(r[30]), "+r"(r[31]));
 }
 
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
+      : "memory");
+}
+
+// ---------------------------------------------------------------- named barriers
+// Named barrier over `nthreads` threads (a multiple of 32); id 0 is
+// __syncthreads'.
+__device__ __forceinline__ void named_barrier_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// Named barrier that also ORs a predicate over every arriving thread, so a
+// group can take one uniform decision (stop or go) at the barrier.
+__device__ __forceinline__ bool named_barrier_or(int id, int nthreads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %3, 0;\n\t"
+      "bar.red.or.pred q, %1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}\n"
+      : "=r"(r)
+      : "r"(id), "r"(nthreads), "r"(pred ? 1u : 0u)
+      : "memory");
+  return r != 0;
+}
+
 // ---------------------------------------------------------------- math
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Packed pairs of fp32 (sm_100 f32x2 arithmetic): one instruction, two lanes.
+__device__ __forceinline__ uint64_t pk2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+
+__device__ __forceinline__ void upk2(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x for a pair of inputs on the FMA pipe instead of MUFU.
+// Method (Cody-Waite range reduction): x = j + f with j = round(x) taken from
+// the low mantissa bits of x + 1.5*2^23 and f in [-1/2, 1/2]; 2^f from a
+// degree-3 polynomial fitted here by iteratively reweighted least squares on
+// Chebyshev nodes (max relative error 7.5e-5, far below the bf16 rounding of
+// P); 2^j is added straight into the exponent field.  Inputs are clamped at
+// -125 so the result stays a normal number; anything that small is zero to
+// the attention.
+__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  float x0, x1;
+  upk2(x, x0, x1);
+  x = pk2(fmaxf(x0, -125.f), fmaxf(x1, -125.f));
+  const uint64_t t = fadd2(x, pk2(kMagic, kMagic));
+  const uint64_t jf = fadd2(t, pk2(-kMagic, -kMagic));
+  const uint64_t f = ffma2(jf, pk2(-1.f, -1.f), x);
+  uint64_t p = ffma2(f, pk2(0.05517394095659256f, 0.05517394095659256f),
+                     pk2(0.24261131882667542f, 0.24261131882667542f));
+  p = ffma2(p, f, pk2(0.6932605504989624f, 0.6932605504989624f));
+  p = ffma2(p, f, pk2(0.9999280571937561f, 0.9999280571937561f));
+  float p0, p1, t0, t1;
+  upk2(p, p0, p1);
+  upk2(t, t0, t1);
+  // (bits(t) - bits(1.5*2^23)) << 23 == bits(t) << 23 modulo 2^32.
+  const float r0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
+  const float r1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
+  return pk2(r0, r1);
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {

@@ -1,0 +1,77 @@
+"""Torch-facing wrappers: fused Q/K norm + RoPE + Ulysses scatter, RoPE
+tables, and per-head e4m3 quantisation."""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+
+def rope_table(positions: torch.Tensor, axes_dim: list[int], theta: float = 10000.0) -> torch.Tensor:
+    """(rows, 64, 2) fp32 cos/sin table for multi-axis RoPE over head_dim 128.
+
+    positions: (rows, n_axes) coordinates of each local token (e.g. (t, h, w)
+    for video, (0, h, w) / (0, 0, 0) for Flux image / text tokens); axis a owns
+    axes_dim[a] / 2 consecutive rotation pairs with frequencies
+    theta^(-2i / axes_dim[a]).  The angle is computed in float64 and rounded
+    once (the standard N-D rotary embedding).
+    """
+    if sum(axes_dim) != 128:
+        raise ValueError(f"axes_dim {axes_dim} must sum to the head dimension 128")
+    cols = []
+    pos = positions.to(torch.float64)
+    for a, dim in enumerate(axes_dim):
+        omega = 1.0 / (theta ** (torch.arange(0, dim, 2, dtype=torch.float64, device=pos.device) / dim))
+        cols.append(pos[:, a:a + 1] * omega[None, :])
+    ang = torch.cat(cols, dim=1)
+    return torch.stack((torch.cos(ang), torch.sin(ang)), dim=-1).to(torch.float32).contiguous()
+
+
+def qkv_prologue_scatter(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, dst_ptrs: list[list[int]],
+                         *, world: int, rank: int, norm_mode: int = _lib.NORM_NONE,
+                         norm_q_w: torch.Tensor | None = None, norm_k_w: torch.Tensor | None = None,
+                         eps: float = 1e-6, rope: torch.Tensor | None = None, seg0: int = 0,
+                         stream=None) -> None:
+    """Norm + RoPE this rank's (B, Ls, H, 128) q/k rows and scatter q/k/v
+    head slices to dst_ptrs[t][r] (rank-major, or joint order with seg0)."""
+    b, ls, h, d = q.shape
+    for t in (q, k, v):
+        if t.shape != q.shape or t.dtype != torch.bfloat16 or t.stride(3) != 1:
+            raise ValueError("prologue tensors must be bf16 (B, Ls, H, 128) with contiguous head_dim")
+    if rope is not None and (rope.dtype != torch.float32 or not rope.is_contiguous()
+                             or rope.shape[-2:] != (64, 2) or rope.shape[-3] != ls):
+        raise ValueError("rope must be a contiguous fp32 (Ls, 64, 2) or (B, Ls, 64, 2) table")
+    desc = _lib.PrologueDesc()
+    desc.world, desc.rank, desc.batch, desc.seq_local = world, rank, b, ls
+    desc.heads, desc.head_dim, desc.norm_mode, desc.eps = h, d, norm_mode, eps
+    for i, t in enumerate((q, k, v)):
+        desc.src_stride[i][0], desc.src_stride[i][1], desc.src_stride[i][2] = t.stride(0), t.stride(1), t.stride(2)
+    desc.rope_batch_stride = 0 if rope is None or rope.ndim == 3 else rope.stride(0)
+    desc.seg0 = seg0
+    src = (ctypes.c_void_p * 3)(q.data_ptr(), k.data_ptr(), v.data_ptr())
+    dst = (ctypes.c_void_p * (3 * world))(*[p for row in dst_ptrs for p in row])
+    stream = stream or torch.cuda.current_stream(q.device)
+    ptr = lambda t: None if t is None else t.data_ptr()
+    _lib.check(_lib.load().dgxm_qkv_prologue_scatter(ctypes.byref(desc), src, ptr(norm_q_w), ptr(norm_k_w),
+                                                     ptr(rope), dst, stream.cuda_stream),
+               "dgxm_qkv_prologue_scatter")
+
+
+def quantize_e4m3_per_head(x: torch.Tensor, out: torch.Tensor | None = None,
+                           descale: torch.Tensor | None = None, stream=None):
+    """(e4m3 values, fp32 per-head descale = absmax / 448) of a bf16 (B, L, H, 128) tensor."""
+    b, l, h, d = x.shape
+    if x.dtype != torch.bfloat16 or x.stride(3) != 1:
+        raise ValueError("quantisation input must be bf16 with contiguous head_dim")
+    if out is None:
+        out = torch.empty(b, l, h, d, device=x.device, dtype=torch.float8_e4m3fn)
+    if descale is None:
+        descale = torch.empty(h, device=x.device, dtype=torch.float32)
+    stride = (ctypes.c_int64 * 3)(x.stride(0), x.stride(1), x.stride(2))
+    stream = stream or torch.cuda.current_stream(x.device)
+    _lib.check(_lib.load().dgxm_quantize_e4m3_per_head(b, l, h, d, x.data_ptr(), stride, out.data_ptr(),
+                                                       descale.data_ptr(), stream.cuda_stream),
+               "dgxm_quantize_e4m3_per_head")
+    return out, descale

@@ -75,8 +75,9 @@ class B200SequenceParallelAttention:
     """Setup-generation-bound implementation behind the callable."""
 
     def __init__(self, *, ulysses_group=None, ring_group=None, generation: int = 1,
-                 device: torch.device | None = None) -> None:
+                 device: torch.device | None = None, fp8: bool = False) -> None:
         self.groups = _Groups(ulysses_group, ring_group)
+        self.fp8 = fp8
         self.generation = generation
         self.device = device or torch.device("cuda", torch.cuda.current_device())
         self._plans: dict = {}
@@ -105,6 +106,16 @@ class B200SequenceParallelAttention:
                      win.local_tensor(offs[2], (b, s, hkv // p, d), dtype)],
             "out": win.local_tensor(offs[3], (b, ls, h, d), dtype),
         }
+        if self.fp8:
+            # e4m3 copies of the gathered heads and their per-head descales;
+            # after the scatter each head is whole on this rank, so the absmax
+            # needs no cross-rank reduction.
+            plan["q8"] = torch.empty(b, s, h // p, d, device=self.device, dtype=torch.float8_e4m3fn)
+            plan["k8"] = torch.empty(b, s, hkv // p, d, device=self.device, dtype=torch.float8_e4m3fn)
+            plan["v8"] = torch.empty(b, s, hkv // p, d, device=self.device, dtype=torch.float8_e4m3fn)
+            plan["ds"] = [torch.empty(h // p, device=self.device, dtype=torch.float32),
+                          torch.empty(hkv // p, device=self.device, dtype=torch.float32),
+                          torch.empty(hkv // p, device=self.device, dtype=torch.float32)]
         self._plans[key] = plan
         return plan
 
@@ -146,8 +157,12 @@ class B200SequenceParallelAttention:
                 inv = _joint_inverse(text, image, p)
                 drop_rows = sorted(inv[r] for r in drop_rows) if drop_rows else drop_rows
                 kv_drop_rows = sorted(inv[r] for r in kv_drop_rows) if kv_drop_rows else kv_drop_rows
-        if p == 1 and g.ring_world == 1:
+        if p == 1 and g.ring_world == 1 and not self.fp8:
             return self._local(q_l, k_l, v_l, drop_rows, kv_drop_rows)
+        if self.fp8 and (g.ring_world > 1 or drop_rows or kv_drop_rows):
+            raise UnsupportedModelError(
+                "the B200 FP8 attention path runs pure Ulysses without pad rows; use the bf16 "
+                "kernel for ring topologies or padded sequences")
         if g.ring_world > 1:
             return self._hybrid(q_l, k_l, v_l)
         plan = self._ulysses_plan(b, ls, h, hkv, d, q_l.dtype)
@@ -163,7 +178,15 @@ class B200SequenceParallelAttention:
         win.barrier()
         qg, kg, vg = plan["recv"]
         out_ptrs = [win.peer_ptr(r, offs[3]) for r in range(p)]
-        if not drop_rows and not kv_drop_rows:
+        if self.fp8:
+            from .prologue import quantize_e4m3_per_head
+
+            for src, dst, ds in zip((qg, kg, vg), (plan["q8"], plan["k8"], plan["v8"]), plan["ds"]):
+                quantize_e4m3_per_head(src, out=dst, descale=ds)
+            attention_routed(plan["q8"], plan["k8"], plan["v8"], out_ptrs, (ls * h * d, h * d, d),
+                             world=p, rank=g.uly_rank, seq_local=ls, seg0=seg0,
+                             q_descale=plan["ds"][0], k_descale=plan["ds"][1], v_descale=plan["ds"][2])
+        elif not drop_rows and not kv_drop_rows:
             attention_routed(qg, kg, vg, out_ptrs, (ls * h * d, h * d, d), world=p, rank=g.uly_rank,
                              seq_local=ls, seg0=seg0)
         else:
@@ -250,11 +273,13 @@ def _joint_inverse(text: int, image: int, world: int) -> list[int]:
 
 
 def make_b200_usp_attention(*, ulysses_group=None, ring_group=None, generation: int = 1,
-                            device: torch.device | None = None):
+                            device: torch.device | None = None, fp8: bool = False):
     """A callable with the reference's usp_attention contract
-    (adapters/base.py:216-326) on the B200 kernels."""
+    (adapters/base.py:216-326) on the B200 kernels.  fp8=True quantises the
+    gathered heads to e4m3 with per-head absmax scales and runs the FP8
+    tensor-core path (output bf16)."""
     impl = B200SequenceParallelAttention(ulysses_group=ulysses_group, ring_group=ring_group,
-                                         generation=generation, device=device)
+                                         generation=generation, device=device, fp8=fp8)
 
     def usp_attention(q, k, v, heads, mask=None, attn_precision=None,
                       skip_reshape=False, skip_output_reshape=False,

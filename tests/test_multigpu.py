@@ -178,3 +178,41 @@ def _callable_case(rank, world, dev):
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
 def test_usp_callable_across_gpus():
     _spawn(_callable_case, min(torch.cuda.device_count(), 4))
+
+
+def _cfg_fp8_case(rank, world, dev):
+    """CFG split across GPUs with FP8 attention (the C3 shape family, small):
+    batch 2 (cond, uncond) -> one row per cfg rank -> e4m3 attention ->
+    peer-store all-gather of the predictions, in rank order."""
+    import torch.distributed as dist
+
+    from dgx_monarch_b200 import _lib
+    from dgx_monarch_b200.cfg import CfgGather, cfg_parallel_call
+    from dgx_monarch_b200.usp import make_b200_usp_attention
+    from tests.test_attn_gpu import reference_attention, rel_l2
+
+    cfg_group = dist.new_group(list(range(world)))
+    attn = make_b200_usp_attention(generation=4, device=dev, fp8=True)  # Ulysses degree 1 per cfg rank
+    batch, l, heads = world, 640, 4
+    g = torch.Generator(device=dev).manual_seed(53)
+    x = torch.randn(batch, l, 3, heads, 128, device=dev, generator=g).bfloat16()
+
+    def forward(x):
+        q, k, v = (x[:, :, i].reshape(x.shape[0], l, -1) for i in range(3))
+        return attn(q, k, v, heads=heads)
+
+    gather = CfgGather(l * heads * 128 * 2, device=dev, group=cfg_group, generation=4)
+    full = cfg_parallel_call(forward, x, group=cfg_group, gather=gather).reshape(batch, l, heads, 128)
+    torch.cuda.synchronize()
+    ref, _ = reference_attention(x[:, :, 0], x[:, :, 1], x[:, :, 2])
+    assert full.shape == (batch, l, heads, 128)
+    for bi in range(batch):
+        assert rel_l2(full[bi], ref[bi]) <= 8e-2  # e4m3 inputs vs bf16 activations
+    assert _lib.device_error() == 0
+    gather.close()
+    attn.impl.invalidate()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
+def test_cfg_split_fp8_across_gpus():
+    _spawn(_cfg_fp8_case, 2)

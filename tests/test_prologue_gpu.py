@@ -1,0 +1,144 @@
+"""Fused Q/K norm + RoPE + Ulysses scatter, and per-head e4m3 quantisation.
+
+The prologue is checked against the separate ops it replaces, composed in
+torch with the same rounding points (norm output rounded to bf16, weight
+product rounded, RoPE in fp32 then rounded), and its layout against the
+oracle's all-to-all: values within one bf16 ulp (the norm's sum order and
+rsqrt differ), V bit-exact.  Quantisation is bit-exact against torch.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import usp
+
+pytestmark = pytest.mark.gpu
+
+
+def _ref_norm_rope(x, w, mode, eps, table):
+    """The unfused composition in torch: (B, L, H, D) bf16 -> bf16."""
+    xf = x.float()
+    b, l, h, d = x.shape
+    if mode == "hidden":
+        flat = xf.reshape(b, l, h * d)
+        sc = torch.rsqrt(flat.pow(2).mean(-1, keepdim=True) + eps)
+        n = (flat * sc).bfloat16()
+        n = (n.float() * w.float()).bfloat16().reshape(b, l, h, d)
+    elif mode == "head":
+        sc = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+        n = (xf * sc).bfloat16()
+        n = (n.float() * w.float()).bfloat16()
+    else:
+        n = x
+    if table is None:
+        return n
+    nf = n.float()
+    c = table[..., 0][None, :, None, :]
+    s = table[..., 1][None, :, None, :]
+    x0, x1 = nf[..., 0::2], nf[..., 1::2]
+    out = torch.empty_like(nf)
+    out[..., 0::2] = x0 * c - x1 * s
+    out[..., 1::2] = x0 * s + x1 * c
+    return out.bfloat16()
+
+
+def _within_one_ulp(got, want):
+    g, w = got.float(), want.float()
+    tol = 2.0 ** -7 * torch.maximum(g.abs(), w.abs()) + 1e-6
+    return bool(((g - w).abs() <= tol).all())
+
+
+def _bits(t):
+    return t.contiguous().view(torch.int16).cpu().numpy()
+
+
+@pytest.mark.parametrize("mode,world,heads,axes", [
+    ("hidden", 4, 40, [44, 42, 42]),   # Wan: norm over 5120, 3-axis RoPE
+    ("head", 2, 24, [16, 56, 56]),     # Flux/Krea2: per-head QKNorm, axis 0 unused by images
+    ("none", 2, 8, None),
+])
+def test_prologue_matches_unfused_ops(lib, mode, world, heads, axes):
+    from dgx_monarch_b200 import _lib
+    from dgx_monarch_b200.prologue import qkv_prologue_scatter, rope_table
+
+    ls, eps = 90, 1e-6
+    g = torch.Generator(device="cuda").manual_seed(29)
+    # q/k/v as views of one packed projection output (B, Ls, 3, H, D).
+    packed = [torch.randn(1, ls, 3, heads, 128, device="cuda", generator=g).bfloat16() for _ in range(world)]
+    wdim = heads * 128 if mode == "hidden" else 128
+    wq = (1 + 0.1 * torch.randn(wdim, device="cuda", generator=g)).bfloat16()
+    wk = (1 + 0.1 * torch.randn(wdim, device="cuda", generator=g)).bfloat16()
+    tables = [None] * world
+    if axes is not None:
+        for r in range(world):
+            rows = torch.arange(r * ls, (r + 1) * ls, device="cuda")
+            pos = torch.stack((rows // 100, (rows // 10) % 10, rows % 10), dim=1)
+            tables[r] = rope_table(pos, axes)
+    hl = heads // world
+    recv = [[torch.zeros(1, ls * world, hl, 128, device="cuda", dtype=torch.bfloat16) for _ in range(world)]
+            for _ in range(3)]
+    nmode = {"hidden": _lib.NORM_HIDDEN, "head": _lib.NORM_HEAD, "none": _lib.NORM_NONE}[mode]
+    for src in range(world):
+        q, k, v = (packed[src][:, :, i] for i in range(3))
+        qkv_prologue_scatter(q, k, v, [[recv[t][r].data_ptr() for r in range(world)] for t in range(3)],
+                             world=world, rank=src, norm_mode=nmode,
+                             norm_q_w=wq if mode != "none" else None,
+                             norm_k_w=wk if mode != "none" else None, eps=eps, rope=tables[src])
+    torch.cuda.synchronize()
+    for t, w in ((0, wq), (1, wk), (2, None)):
+        want_local = []
+        for src in range(world):
+            x = packed[src][:, :, t]
+            if t < 2:
+                x = _ref_norm_rope(x, w, mode, eps, tables[src])
+            want_local.append(x.contiguous())
+        want = usp.seq_all_to_all_4d([x.float().cpu().numpy() for x in want_local], 2, 1)
+        for r in range(world):
+            got = recv[t][r]
+            if t == 2:
+                want_bits = usp.seq_all_to_all_4d([_bits(x) for x in want_local], 2, 1)[r]
+                assert np.array_equal(_bits(got), want_bits)
+            else:
+                assert _within_one_ulp(got, torch.from_numpy(want[r]).cuda())
+
+
+def test_prologue_joint_order_matches_canonical_layout(lib):
+    from dgx_monarch_b200.prologue import qkv_prologue_scatter
+
+    world, text, image, heads = 2, 8, 24, 4
+    ls = text + image
+    g = torch.Generator(device="cuda").manual_seed(37)
+    local = [[torch.randn(1, ls, heads, 128, device="cuda", generator=g).bfloat16() for _ in range(3)]
+             for _ in range(world)]
+    recv = [[torch.zeros(1, ls * world, heads // world, 128, device="cuda", dtype=torch.bfloat16)
+             for _ in range(world)] for _ in range(3)]
+    for src in range(world):
+        qkv_prologue_scatter(*local[src], [[recv[t][r].data_ptr() for r in range(world)] for t in range(3)],
+                             world=world, rank=src, seg0=text)
+    torch.cuda.synchronize()
+    order = usp.RankMajorJointOrder(text, image)
+    for t in range(3):
+        rank_major = usp.seq_all_to_all_4d([_bits(local[s][t]) for s in range(world)], 2, 1)
+        for r in range(world):
+            canon = order.canonicalize(rank_major[r], rank_major[r], rank_major[r], None, None)[0]
+            assert np.array_equal(_bits(recv[t][r]), canon)
+
+
+@pytest.mark.parametrize("shape", [(1, 333, 3), (2, 4608, 24)])
+def test_quantize_is_bit_exact_against_torch(lib, shape):
+    from dgx_monarch_b200.prologue import quantize_e4m3_per_head
+
+    b, l, h = shape
+    g = torch.Generator(device="cuda").manual_seed(41)
+    x = torch.randn(b, l, h, 128, device="cuda", generator=g).bfloat16()
+    q8, descale = quantize_e4m3_per_head(x)
+    torch.cuda.synchronize()
+    amax = x.float().abs().amax(dim=(0, 1, 3))
+    # IEEE division by a tensor (torch divides by a Python scalar through its
+    # reciprocal, which rounds differently).
+    want_scale = amax / torch.full_like(amax, 448.0)
+    want = (x.float() / want_scale.view(1, 1, -1, 1)).to(torch.float8_e4m3fn)
+    assert torch.equal(descale, want_scale)
+    assert torch.equal(q8.view(torch.uint8), want.view(torch.uint8))
