@@ -128,6 +128,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "dgxm_ring_workspace_bytes": (ctypes.c_int64, [ctypes.POINTER(AttnDesc), _I32]),
     "dgxm_ring_attn_fwd": (ctypes.c_int, [_P, ctypes.POINTER(AttnDesc), _P, _P, _P, _P, _P, _P,
                                           ctypes.c_int64, _P]),
+    "dgxm_ring_noalloc_max_bytes": (ctypes.c_int64, []),
+    "dgxm_ring_attn_fwd_noalloc": (ctypes.c_int, [_P, ctypes.POINTER(AttnDesc), _P, _P, _P, _P, _P,
+                                                  _P]),
 }
 
 _lock = threading.Lock()

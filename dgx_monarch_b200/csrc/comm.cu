@@ -219,6 +219,19 @@ extern "C" int dgxm_comm_create(int32_t rank, int32_t world, int64_t bytes, uint
   c->peers[rank] = c->local;
   c->opened[rank] = false;
   c->wait_cycles = kWaitBudgetCycles;
+  if (world > 1) {
+    // The copy-engine stream and events of ring attention, created with the
+    // comm so that no attention call creates driver objects.
+    e = cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_main, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_side, cudaEventDisableTiming);
+    if (e != cudaSuccess) {
+      if (c->side) cudaStreamDestroy(c->side);
+      cudaFree(c->local);
+      delete c;
+      return cuda_fail(e, "dgxm_comm_create stream/events");
+    }
+  }
   *out = c;
   return DGXM_OK;
 }
@@ -303,8 +316,8 @@ extern "C" int dgxm_comm_destroy(dgxm_comm* c) {
   cudaSetDevice(c->device);
   cudaDeviceSynchronize();
   if (c->side != nullptr) {
-    cudaEventDestroy(c->ev_main);
-    cudaEventDestroy(c->ev_side);
+    if (c->ev_main) cudaEventDestroy(c->ev_main);
+    if (c->ev_side) cudaEventDestroy(c->ev_side);
     cudaStreamDestroy(c->side);
   }
   for (int r = 0; r < c->world; ++r)

@@ -4,6 +4,8 @@
 #include <math.h>
 #include <string.h>
 
+#include <mutex>
+
 #include "capi.cu"
 #include "attn_fwd.cu"
 #include "lse_merge.cu"

@@ -35,14 +35,6 @@ static int64_t ring_lse_bytes(const dgxm_attn_desc* d) {
   return round256(static_cast<int64_t>(d->batch) * d->q_heads * d->q_len * 4);
 }
 
-static int ring_prepare_streams(dgxm_comm* c) {
-  if (c->side != nullptr) return DGXM_OK;
-  DGXM_CUDA_TRY(cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking));
-  DGXM_CUDA_TRY(cudaEventCreateWithFlags(&c->ev_main, cudaEventDisableTiming));
-  DGXM_CUDA_TRY(cudaEventCreateWithFlags(&c->ev_side, cudaEventDisableTiming));
-  return DGXM_OK;
-}
-
 static bool contiguous_bhld(const int64_t* s, const dgxm_attn_desc* d, int heads, int len) {
   return s[2] == d->head_dim && s[1] == static_cast<int64_t>(heads) * d->head_dim &&
          (d->batch == 1 || s[0] == static_cast<int64_t>(len) * heads * d->head_dim);
@@ -60,10 +52,13 @@ extern "C" int64_t dgxm_ring_workspace_bytes(const dgxm_attn_desc* d, int32_t ri
   return static_cast<int64_t>(ring_world) * (dgxm::ring_part_bytes(d) + dgxm::ring_lse_bytes(d));
 }
 
-extern "C" int dgxm_ring_attn_fwd(dgxm_comm* c, const dgxm_attn_desc* d, const void* q,
-                                  const void* k, const void* v, void* o, float* lse,
-                                  void* workspace, int64_t workspace_bytes, void* stream) {
-  using namespace dgxm;
+namespace dgxm {
+
+// The ring loop, partial results in `workspace` (any device memory of at
+// least dgxm_ring_workspace_bytes, 256-byte aligned).
+static int ring_attn_impl(dgxm_comm* c, const dgxm_attn_desc* d, const void* q, const void* k,
+                          const void* v, void* o, float* lse, void* workspace,
+                          int64_t workspace_bytes, void* stream) {
   if (c == nullptr || d == nullptr) return fail(DGXM_ERR_INVALID, "NULL comm or descriptor");
   const int world = c->world;
   if (world > kMaxMergeParts)
@@ -89,8 +84,8 @@ extern "C" int dgxm_ring_attn_fwd(dgxm_comm* c, const dgxm_attn_desc* d, const v
     return fail(DGXM_ERR_INVALID, "ring workspace must be 256-byte aligned");
   for (int r = 0; r < world; ++r)
     if (c->peers[r] == nullptr) return fail(DGXM_ERR_STATE, "peer %d window is not mapped", r);
-  int rc = ring_prepare_streams(c);
-  if (rc) return rc;
+  if (c->side == nullptr) return fail(DGXM_ERR_STATE, "the comm has no copy stream (world 1?)");
+  int rc = DGXM_OK;
   cudaStream_t main = static_cast<cudaStream_t>(stream);
   const int next = (c->rank + 1) % world;
   char* mine = c->local + kFlagBytes;
@@ -138,4 +133,64 @@ extern "C" int dgxm_ring_attn_fwd(dgxm_comm* c, const dgxm_attn_desc* d, const v
   }
   return dgxm_lse_merge(d->batch, d->q_len, d->q_heads, d->head_dim, world, outs, DGXM_DTYPE_F32,
                         lses, o, d->out_dtype, lse, stream);
+}
+
+}  // namespace dgxm
+
+extern "C" int dgxm_ring_attn_fwd(dgxm_comm* c, const dgxm_attn_desc* d, const void* q,
+                                  const void* k, const void* v, void* o, float* lse,
+                                  void* workspace, int64_t workspace_bytes, void* stream) {
+  return dgxm::ring_attn_impl(c, d, q, k, v, o, lse, workspace, workspace_bytes, stream);
+}
+
+// ---------------------------------------------------------------- without allocation
+// Partial results of dgxm_ring_attn_fwd_noalloc live in this module-scope
+// array instead of a caller's workspace.  It is created when the library
+// loads on a device and stays until the process exits; every call shares it.
+namespace dgxm {
+
+constexpr int64_t kRingStaticScratchBytes = int64_t(32) << 20;  // 32 MiB
+static __device__ __align__(256) unsigned char g_ring_static_scratch[kRingStaticScratchBytes];
+
+// The device address of the array on the current device.  In host code the
+// array's name is only a host-side stand-in, so the address comes from
+// cudaGetSymbolAddress, looked up once per device (with that device current)
+// and cached.
+static int ring_static_scratch(void** out) {
+  static std::mutex mu;
+  static void* addr[64] = {};
+  int dev = 0;
+  DGXM_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(DGXM_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_ring_static_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(ring scratch)");
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return DGXM_OK;
+}
+
+}  // namespace dgxm
+
+extern "C" int64_t dgxm_ring_noalloc_max_bytes(void) { return dgxm::kRingStaticScratchBytes; }
+
+extern "C" int dgxm_ring_attn_fwd_noalloc(dgxm_comm* c, const dgxm_attn_desc* d, const void* q,
+                                          const void* k, const void* v, void* o, float* lse,
+                                          void* stream) {
+  using namespace dgxm;
+  if (c == nullptr || d == nullptr) return fail(DGXM_ERR_INVALID, "NULL comm or descriptor");
+  if (c->world == 1) return dgxm_attn_fwd(d, q, k, v, nullptr, nullptr, nullptr, o, lse, stream);
+  const int64_t need = dgxm_ring_workspace_bytes(d, c->world);
+  if (need < 0 || need > kRingStaticScratchBytes)
+    return fail(DGXM_ERR_INVALID,
+                "ring attention of this shape needs %lld bytes of scratch; the allocation-free "
+                "entry point holds at most %lld (32 MiB). Use dgxm_ring_attn_fwd with a workspace.",
+                (long long)need, (long long)kRingStaticScratchBytes);
+  void* scratch = nullptr;
+  const int rc = ring_static_scratch(&scratch);
+  if (rc != DGXM_OK) return rc;
+  return ring_attn_impl(c, d, q, k, v, o, lse, scratch, kRingStaticScratchBytes, stream);
 }

@@ -282,6 +282,29 @@ int dgxm_ring_attn_fwd(dgxm_comm* comm, const dgxm_attn_desc* desc, const void* 
                        const void* v, void* o, float* lse, void* workspace,
                        int64_t workspace_bytes, void* stream);
 
+/*
+ * Ring attention that allocates nothing, for callers that cannot call
+ * cudaMalloc at attention time: a host runtime whose device memory is all
+ * owned by another allocator with a fixed budget (a request outside it
+ * would break the budget or fail), or a caller on a latency-critical path
+ * where cudaMalloc would synchronise the device.  It has no counterpart in
+ * the reference (which always allocates through torch).
+ *
+ * Same contract as dgxm_ring_attn_fwd, except that the per-step partial
+ * results live in one 32 MiB array of module memory on each device that
+ * loads this library (held until the process exits) instead of a caller
+ * workspace: shapes needing more than dgxm_ring_noalloc_max_bytes() of
+ * scratch are refused with DGXM_ERR_INVALID.  The first call on a device
+ * looks up the array's device address (cudaGetSymbolAddress); make that first
+ * call before any stream capture.  Every call on a device shares the array,
+ * so calls whose work overlaps on the GPU race; nothing in it needs clearing,
+ * since every step rewrites its whole partial result.  The comm (created
+ * earlier with dgxm_comm_create) supplies the rotation buffers and streams.
+ */
+int64_t dgxm_ring_noalloc_max_bytes(void);
+int dgxm_ring_attn_fwd_noalloc(dgxm_comm* comm, const dgxm_attn_desc* desc, const void* q,
+                               const void* k, const void* v, void* o, float* lse, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
