@@ -243,6 +243,140 @@ def run_dit_layer(world: int, rank: int, dev, steps: int, warmup: int, group=Non
     return {"ms": ms, "my_launches": 4 if world > 1 else 2}
 
 
+# ----------------------------------------------------------------- ring / CFG workloads (N > 1)
+RING = {"seq": 219600, "heads": 24}
+RING_WORKLOAD = ("Long-video hybrid ring x Ulysses attention: 1280x720 at 241 frames -> 61x90x160 "
+                 "latent, (1,2,2) patches = 219,600 tokens, 24 heads x 128, bf16; Ulysses-2 x ring-N/2 "
+                 "(ring-2 at N=2), K/V blocks rotating over NVLink, LSE merge")
+CFG = {"img": 4096, "txt": 512, "heads": 24, "batch": 2}
+CFG_WORKLOAD = ("CFG-parallel + Ulysses image attention: batch 2 (cond/uncond) -> one row per cfg rank, "
+                "1024x1024 image = 4096 tokens + 512 text tokens, 24 heads x 128, Q/K/V in FP8 e4m3 with "
+                "per-head absmax scales, bf16 out; cfg2 x Ulysses-N/2")
+
+
+def _groups(world: int, uly: int, ring: int):
+    """Ulysses / ring process groups in the ulysses-low layout (Ulysses
+    groups are consecutive ranks), every rank creating every group."""
+    import torch.distributed as dist
+
+    from oracle.usp import hybrid_groups
+
+    ug, rg = hybrid_groups(world, uly, ring)
+    rank = dist.get_rank()
+    mine_u = mine_r = None
+    for ranks in ug:
+        g = dist.new_group(ranks)
+        if rank in ranks:
+            mine_u = g
+    for ranks in rg:
+        g = dist.new_group(ranks)
+        if rank in ranks:
+            mine_r = g
+    return mine_u, mine_r
+
+
+def run_ring(world: int, rank: int, dev, steps: int, warmup: int) -> dict:
+    import torch
+
+    from dgx_monarch_b200.usp import make_b200_usp_attention
+
+    uly = 2 if world >= 4 else 1
+    ring = world // uly
+    ug, rg = _groups(world, uly, ring)
+    attn = make_b200_usp_attention(ulysses_group=ug if uly > 1 else None, ring_group=rg,
+                                   generation=31, device=dev)
+    seq, h = RING["seq"], RING["heads"]
+    ls = seq // world
+    g = torch.Generator(device=dev).manual_seed(500 + rank)
+    q, k, v = (torch.randn(1, ls, h * DIM, device=dev, generator=g, dtype=torch.bfloat16) for _ in range(3))
+    for _ in range(warmup):
+        attn(q, k, v, heads=h)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        attn(q, k, v, heads=h)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    attn.impl.invalidate()
+    return {"ms": ms, "layout": f"ulysses{uly}xring{ring}"}
+
+
+def run_cfg_fp8(world: int, rank: int, dev, steps: int, warmup: int) -> dict:
+    import torch
+
+    from dgx_monarch_b200.cfg import CfgGather
+    from dgx_monarch_b200.usp import make_b200_usp_attention
+
+    sp = world // 2
+    # sequence parallel fastest, then cfg: ranks r and r + sp form a cond/uncond pair
+    import torch.distributed as dist
+
+    sp_groups = [list(range(c * sp, (c + 1) * sp)) for c in range(2)]
+    cfg_groups = [[r, r + sp] for r in range(sp)]
+    mine_sp = mine_cfg = None
+    for ranks in sp_groups:
+        gsp = dist.new_group(ranks)
+        if rank in ranks:
+            mine_sp = gsp
+    for ranks in cfg_groups:
+        gc = dist.new_group(ranks)
+        if rank in ranks:
+            mine_cfg = gc
+    attn = make_b200_usp_attention(ulysses_group=mine_sp if sp > 1 else None, generation=41,
+                                   device=dev, fp8=True)
+    s = CFG["img"] + CFG["txt"]
+    ls = s // sp
+    h = CFG["heads"]
+    g = torch.Generator(device=dev).manual_seed(700 + rank)
+    q, k, v = (torch.randn(1, ls, h * DIM, device=dev, generator=g, dtype=torch.bfloat16) for _ in range(3))
+    gather = CfgGather(ls * h * DIM * 2, device=dev, group=mine_cfg, generation=41)
+
+    def step():
+        out = attn(q, k, v, heads=h)          # this cfg rank's batch row, its sequence shard
+        return gather(out)                    # predictions of the pair, in cfg-rank order
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    gather.close()
+    attn.impl.invalidate()
+    return {"ms": ms, "layout": f"cfg2xulysses{sp}"}
+
+
+def time_scatter(uly, steps: int = 5) -> dict:
+    """Device time of the Ulysses scatter alone (q, k, v peer stores)."""
+    import torch
+
+    from dgx_monarch_b200.ulysses import ulysses_scatter
+
+    w = uly.windows
+    q = torch.zeros(uly.b, uly.ls, uly.h, uly.d, device=uly.device, dtype=uly.dtype)
+    ptrs = [[w.peer_ptr(r, off) for r in range(uly.world)] for off in uly.off_recv]
+    ulysses_scatter([q, q, q], ptrs, world=uly.world, rank=uly.rank)
+    w.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        ulysses_scatter([q, q, q], ptrs, world=uly.world, rank=uly.rank)
+    e1.record()
+    torch.cuda.synchronize()
+    w.barrier()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    remote = 3 * q.numel() * q.element_size() * (uly.world - 1) / uly.world
+    return {"ms": ms, "nvlink_bytes_per_rank": remote, "gbs_per_direction": remote / (ms * 1e-3) / 1e9}
+
+
 # ----------------------------------------------------------------- our arm
 def main() -> None:
     args = parse_args()
@@ -339,10 +473,21 @@ def main() -> None:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_ms = te.item()
     dit = run_dit_layer(world, rank, dev, max(5, args.steps), args.warmup)
-    td = torch.tensor([dit["ms"]], device=dev, dtype=torch.float64)
+    extra = [dit["ms"], 0.0, 0.0, 0.0, 0.0]
+    a2a = ring_res = cfg_res = None
+    if world > 1:
+        a2a = time_scatter(uly)
+        ring_res = run_ring(world, rank, dev, 2, 1)
+        cfg_res = run_cfg_fp8(world, rank, dev, 5, 3)
+        extra[1:] = [a2a["ms"], ring_res["ms"], cfg_res["ms"], a2a["gbs_per_direction"]]
+    td = torch.tensor(extra, device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(td, op=dist.ReduceOp.MAX)
-    dit_ms = td.item()
+        # the slowest rank's link rate
+        tmin = torch.tensor([extra[4]], device=dev, dtype=torch.float64)
+        dist.all_reduce(tmin, op=dist.ReduceOp.MIN)
+        td[4] = tmin[0]
+    dit_ms, a2a_ms, ring_ms, cfg_ms, a2a_gbs = td.tolist()
     dev_err = _lib.device_error()
 
     if rank == 0:
@@ -379,12 +524,27 @@ def main() -> None:
                     "ms_per_step": e2e_ms},
             "dit_layer": {"workload": DIT_WORKLOAD, "tokens_per_s": (DIT["img"] + DIT["txt"]) / (dit_ms * 1e-3),
                           "ms_per_layer": dit_ms, "tflops": dit_layer_flops() / (dit_ms * 1e-3) / 1e12,
-                          "frac_of_bf16_peak": dit_layer_flops() / (dit_ms * 1e-3) / 1e12 / peaks["bf16_tflops"],
+                          "frac_of_bf16_peak": dit_layer_flops() / (dit_ms * 1e-3) / 1e12 / (world * peaks["bf16_tflops"]),
                           "parallelism": f"ulysses{world}"},
             "gpu_launches": launches,
+            "roofline_sustained": {"peak": peaks["bf16_sustained"], "frac": achieved / peaks["bf16_sustained"],
+                                   "note": "measured cuBLAS bf16 GEMM held for seconds under the 1 kW cap"},
             "clocks": clk,
             "device_error": dev_err,
         }
+        if world > 1:
+            line["all_to_all"] = {"kernel": "ulysses_scatter_kernel", "ms": a2a_ms,
+                                  "nvlink_bytes_per_rank": a2a["nvlink_bytes_per_rank"],
+                                  "gbs_per_direction": a2a_gbs, "peak_gbs": 770.0,
+                                  "frac": a2a_gbs / 770.0,
+                                  "peak_note": "measured peer copy per direction on this pool"}
+            rflops = attn_flops(1, RING["heads"], RING["seq"], DIM)
+            line["ring"] = {"workload": RING_WORKLOAD, "layout": ring_res["layout"], "ms_per_layer": ring_ms,
+                            "tflops": rflops / (ring_ms * 1e-3) / 1e12,
+                            "tokens_per_s": RING["seq"] / (ring_ms * 1e-3)}
+            cflops = attn_flops(CFG["batch"], CFG["heads"], CFG["img"] + CFG["txt"], DIM)
+            line["cfg_fp8"] = {"workload": CFG_WORKLOAD, "layout": cfg_res["layout"], "ms_per_step": cfg_ms,
+                               "tflops": cflops / (cfg_ms * 1e-3) / 1e12}
         if world == 1 and not args.no_cpu_baseline:
             from oracle.cpu_baseline import time_sdpa_sample
 

@@ -153,27 +153,33 @@ struct QuantParams {
   int batch, rows, heads;
 };
 
-__global__ void __launch_bounds__(256) absmax_kernel(const __grid_constant__ QuantParams p) {
-  const int64_t vecs = static_cast<int64_t>(p.batch) * p.rows * p.heads * 16;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < vecs;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int part = static_cast<int>(i % 16);
-    int64_t rem = i / 16;
-    const int h = static_cast<int>(rem % p.heads);
-    rem /= p.heads;
-    const int l = static_cast<int>(rem % p.rows);
-    const int b = static_cast<int>(rem / p.rows);
-    const uint4 raw = __ldg(reinterpret_cast<const uint4*>(p.x + b * p.sb + l * p.sl + h * p.sh) + part);
-    const __nv_bfloat162* pr = reinterpret_cast<const __nv_bfloat162*>(&raw);
-    float m = 0.f;
+// Per-head absmax.  Thread (h, part) of a block owns 16 bytes of head h in
+// every row the block visits, keeps a running max in a register, reduces it
+// over the head's 16 lanes with shuffles, and issues one atomicMax per head
+// per block -- not one per 16 bytes, which would serialise on 'heads'
+// addresses.  Non-negative floats order like their bit patterns.
+__global__ void __launch_bounds__(1024) absmax_kernel(const __grid_constant__ QuantParams p) {
+  const int slot = threadIdx.x;         // h * 16 + part
+  const int h = slot / 16, part = slot % 16;
+  float m = 0.f;
+  if (h < p.heads) {
+    const int64_t rows = static_cast<int64_t>(p.batch) * p.rows;
+    for (int64_t br = blockIdx.x; br < rows; br += gridDim.x) {
+      const int b = static_cast<int>(br / p.rows);
+      const int l = static_cast<int>(br - static_cast<int64_t>(b) * p.rows);
+      const uint4 raw = __ldg(reinterpret_cast<const uint4*>(p.x + b * p.sb + l * p.sl + h * p.sh) + part);
+      const __nv_bfloat162* pr = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const float2 f = __bfloat1622float2(pr[k]);
-      m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __bfloat1622float2(pr[k]);
+        m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
+      }
     }
-    // Non-negative floats order like their bit patterns.
-    atomicMax(reinterpret_cast<unsigned int*>(p.amax) + h, __float_as_uint(m));
   }
+  // The 16 lanes of one head are 16 consecutive lanes of a warp.
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (part == 0 && h < p.heads) atomicMax(reinterpret_cast<unsigned int*>(p.amax) + h, __float_as_uint(m));
 }
 
 __global__ void __launch_bounds__(256) quantize_e4m3_kernel(const __grid_constant__ QuantParams p) {
@@ -297,10 +303,14 @@ extern "C" int dgxm_quantize_e4m3_per_head(int32_t batch, int32_t rows, int32_t 
   int dev = 0, sms = 148;
   DGXM_CUDA_TRY(cudaGetDevice(&dev));
   DGXM_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  if (heads > 64) return fail(DGXM_ERR_UNSUPPORTED, "quantisation supports up to 64 heads, got %d", heads);
   const int64_t vecs = static_cast<int64_t>(batch) * rows * heads * 16;
   const int64_t want = (vecs + 255) / 256;
   const int blocks = static_cast<int>(want < int64_t(sms) * 8 ? want : int64_t(sms) * 8);
-  absmax_kernel<<<blocks, 256, 0, st>>>(p);
+  const int64_t nrows = static_cast<int64_t>(batch) * rows;
+  const int amax_blocks = static_cast<int>(nrows < int64_t(sms) * 4 ? nrows : int64_t(sms) * 4);
+  const int amax_threads = (heads * 16 + 31) / 32 * 32;
+  absmax_kernel<<<amax_blocks, amax_threads, 0, st>>>(p);
   quantize_e4m3_kernel<<<blocks, 256, 0, st>>>(p);
   descale_kernel<<<(heads + 127) / 128, 128, 0, st>>>(descale, heads);
   DGXM_CUDA_TRY(cudaGetLastError());
