@@ -75,6 +75,34 @@ class A2ADesc(ctypes.Structure):
     ]
 
 
+MAX_BIAS_GROUPS = 8
+
+
+class AttnExtras(ctypes.Structure):
+    _fields_ = [
+        ("key_keep", ctypes.c_void_p),
+        ("key_keep_batch_stride", ctypes.c_int64),
+        ("query_keep", ctypes.c_void_p),
+        ("query_keep_batch_stride", ctypes.c_int64),
+        ("n_bias_groups", ctypes.c_int32),
+        ("bias_row_begin", ctypes.c_int32 * MAX_BIAS_GROUPS),
+        ("bias_row_end", ctypes.c_int32 * MAX_BIAS_GROUPS),
+        ("bias", ctypes.c_void_p * MAX_BIAS_GROUPS),
+        ("bias_stride", (ctypes.c_int64 * 3) * MAX_BIAS_GROUPS),
+        ("bias_keys", ctypes.c_int32 * MAX_BIAS_GROUPS),
+    ]
+
+
+class AttnRoute(ctypes.Structure):
+    _fields_ = [
+        ("o_peers", ctypes.c_void_p * 8),
+        ("world", ctypes.c_int32),
+        ("rank", ctypes.c_int32),
+        ("seq_local", ctypes.c_int32),
+        ("seg0", ctypes.c_int32),
+    ]
+
+
 NORM_NONE, NORM_HIDDEN, NORM_HEAD = 0, 1, 2
 
 
@@ -118,6 +146,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "dgxm_ulysses_scatter": (ctypes.c_int, [ctypes.POINTER(A2ADesc), ctypes.POINTER(_P),
                                             ctypes.POINTER(_P), _P]),
     "dgxm_ulysses_gather": (ctypes.c_int, [ctypes.POINTER(A2ADesc), _P, ctypes.POINTER(_P), _P]),
+    "dgxm_attn_fwd_ext": (ctypes.c_int, [ctypes.POINTER(AttnDesc), ctypes.POINTER(AttnExtras),
+                                         ctypes.POINTER(AttnRoute), _P, _P, _P, _P, _P, _P, _P, _P,
+                                         _P]),
     "dgxm_attn_fwd_routed": (ctypes.c_int, [ctypes.POINTER(AttnDesc), _P, _P, _P, _P, _P, _P,
                                             ctypes.POINTER(_P), _I32, _I32, _I32, _I32, _P, _P]),
     "dgxm_qkv_prologue_scatter": (ctypes.c_int, [ctypes.POINTER(PrologueDesc), ctypes.POINTER(_P),

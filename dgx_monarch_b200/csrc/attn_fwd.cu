@@ -101,6 +101,20 @@ struct __align__(64) AttnParams {
   int o_head_off;
   int o_world;
   int o_seg0;  // joint order of the gathered axis (0 = rank-major)
+  // Extras (the EXTRA kernel variant only): keep bits over keys (0 excludes
+  // the key) and over query rows (0 writes a zero output row), and additive
+  // biases for query-row groups, added to the scaled logits.
+  const uint32_t* kmask;
+  int64_t kmask_sb;  // words
+  int kmask_words;
+  const uint32_t* qmask;
+  int64_t qmask_sb;
+  int n_bias;
+  int bias_q0[DGXM_MAX_BIAS_GROUPS], bias_q1[DGXM_MAX_BIAS_GROUPS];
+  const float* bias[DGXM_MAX_BIAS_GROUPS];
+  int64_t bias_sb[DGXM_MAX_BIAS_GROUPS], bias_sh[DGXM_MAX_BIAS_GROUPS], bias_sq[DGXM_MAX_BIAS_GROUPS];
+  int bias_len[DGXM_MAX_BIAS_GROUPS];
+  float inv_scale;
 };
 
 // Barrier slots inside the control block.
@@ -181,7 +195,7 @@ __device__ __forceinline__ void raise_abort(volatile int* abort_flag, int bits) 
   *abort_flag = 1;
 }
 
-template <bool FP8, bool OUT_F32>
+template <bool FP8, bool OUT_F32, bool EXTRA>
 __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_constant__ AttnParams p) {
   using C = AttnCfg<FP8>;
   using B = Bars<C::kStages>;
@@ -370,6 +384,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
     if constexpr (FP8) sl2 *= p.q_descale[h] * p.k_descale[hk];
     float m_run = -INFINITY;  // running max of the scaled logits, log2 units
     float l_run = 0.f;        // this half's running sum of exp2(s * sl2 - m_run)
+    // EXTRA: this row's bias group (if any).
+    const float* bias_row = nullptr;
+    int bias_len = 0;
+    if constexpr (EXTRA) {
+      const int qrow = row0 + t * kTileRows + r;
+      for (int g = 0; g < p.n_bias; ++g) {
+        if (qrow >= p.bias_q0[g] && qrow < p.bias_q1[g] && p.bias[g] != nullptr) {
+          bias_row = p.bias[g] + static_cast<int64_t>(b) * p.bias_sb[g] +
+                     static_cast<int64_t>(h) * p.bias_sh[g] +
+                     static_cast<int64_t>(qrow - p.bias_q0[g]) * p.bias_sq[g];
+          bias_len = p.bias_len[g];
+        }
+      }
+    }
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
       const bool got = __all_sync(0xffffffffu, mbar_wait(bar(B::kSFull + t), j & 1, abort_flag));
@@ -392,6 +420,25 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
 #pragma unroll
         for (int i = 0; i < 32; ++i) s[h2 * 32 + i] = __uint_as_float(sr[h2][i]);
       const int valid = p.kv_len - j * kTileRows - c * 64;
+      if constexpr (EXTRA) {
+        const int key0 = j * kTileRows + c * 64;
+        if (bias_row != nullptr) {
+#pragma unroll
+          for (int i = 0; i < 64; ++i)
+            if (key0 + i < bias_len) s[i] += __ldg(bias_row + key0 + i) * p.inv_scale;
+        }
+        if (p.kmask != nullptr) {
+          const uint32_t* km = p.kmask + static_cast<int64_t>(b) * p.kmask_sb;
+          const int w = key0 >> 5;
+          const uint32_t m0 = w < p.kmask_words ? __ldg(km + w) : 0u;
+          const uint32_t m1 = w + 1 < p.kmask_words ? __ldg(km + w + 1) : 0u;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            if (!((m0 >> i) & 1u)) s[i] = -INFINITY;
+            if (!((m1 >> i) & 1u)) s[32 + i] = -INFINITY;
+          }
+        }
+      }
       if (valid < 64) {
 #pragma unroll
         for (int i = 0; i < 64; ++i)
@@ -437,13 +484,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
       float alpha = 1.f;
       bool rescale = false;
       if (__any_sync(0xffffffffu, grow)) {
-        alpha = ex2_approx(m_run - m_cand);  // 0 on the first block (m_run = -inf)
+        // 0 on the first block (m_run = -inf).  With extras a row can see
+        // only excluded keys while another row of the warp grows; its
+        // m_run = m_cand = -inf, and -inf - -inf must give 1, not NaN.
+        alpha = ex2_approx((EXTRA && m_cand == -INFINITY) ? 0.f : m_run - m_cand);
         m_run = m_cand;
         rescale = j > 0;
       }
       l_run *= alpha;
       // p = 2^(s * sl2 - m) (times kPScale for e4m3, folded into the exponent).
-      const float bias = -m_run + C::kPScaleLog2;
+      // A row whose keys so far were all excluded keeps m = -inf and p = 0.
+      const float bias = -(EXTRA && m_run == -INFINITY ? 0.f : m_run) + C::kPScaleLog2;
       const uint64_t sl2x2 = pk2(sl2, sl2), biasx2 = pk2(bias, bias);
       uint64_t sum_a = pk2(0.f, 0.f), sum_b = pk2(0.f, 0.f);
       uint32_t pk[32];
@@ -516,6 +567,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
       const bool row_ok = grow < p.q_len;
       float inv = 1.f / (l_row * C::kPScale);
       if constexpr (FP8) inv *= p.v_descale[hk];
+      bool row_empty = false;
+      if constexpr (EXTRA) {
+        bool row_dropped = false;
+        if (p.qmask != nullptr && row_ok) {
+          const uint32_t wq = __ldg(p.qmask + static_cast<int64_t>(b) * p.qmask_sb + (grow >> 5));
+          row_dropped = !((wq >> (grow & 31)) & 1u);
+        }
+        // A dropped row, or one that saw no key at all (its maximum never
+        // left -inf; the exp2 polynomial floors excluded keys at 2^-125, so
+        // the sum alone cannot tell), is written as zeros with LSE -inf.
+        row_empty = row_dropped || m_run == -INFINITY || !(l_row > 0.f);
+        if (row_empty) inv = 0.f;
+      }
       void* obase = p.o;
       int orow_idx = grow;
       int ohead = h;
@@ -574,7 +638,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
       }
       if (c == 0 && row_ok && p.lse != nullptr) {
         p.lse[static_cast<int64_t>(b) * p.lse_sb + static_cast<int64_t>(h) * p.lse_sh +
-              static_cast<int64_t>(grow) * p.lse_sl] = (m_run + log2f(l_row)) * kLn2;
+              static_cast<int64_t>(grow) * p.lse_sl] =
+            row_empty ? -INFINITY : (m_run + log2f(l_row)) * kLn2;
       }
     }
   }
@@ -585,11 +650,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
   }
 }
 
-template <bool FP8, bool OUT_F32>
+template <bool FP8, bool OUT_F32, bool EXTRA>
 static int launch_attn(const AttnParams& prm, dim3 grid, cudaStream_t stream) {
   using C = AttnCfg<FP8>;
   static uint64_t configured = 0;  // one bit per device ordinal
-  auto kern = attn_fwd_kernel<FP8, OUT_F32>;
+  auto kern = attn_fwd_kernel<FP8, OUT_F32, EXTRA>;
   int dev = 0;
   DGXM_CUDA_TRY(cudaGetDevice(&dev));
   const uint64_t bit = uint64_t(1) << (dev & 63);
@@ -690,12 +755,75 @@ static int prepare_attn(const dgxm_attn_desc* d, const void* q, const void* k, c
   return DGXM_OK;
 }
 
-static int dispatch_attn(const dgxm_attn_desc* d, const AttnParams& prm, dim3 grid, void* stream) {
+template <bool EXTRA>
+static int dispatch_attn_t(const dgxm_attn_desc* d, const AttnParams& prm, dim3 grid, cudaStream_t st) {
   const bool fp8 = d->in_dtype == DGXM_DTYPE_E4M3;
   const bool out_f32 = d->out_dtype == DGXM_DTYPE_F32;
+  if (fp8)
+    return out_f32 ? launch_attn<true, true, EXTRA>(prm, grid, st)
+                   : launch_attn<true, false, EXTRA>(prm, grid, st);
+  return out_f32 ? launch_attn<false, true, EXTRA>(prm, grid, st)
+                 : launch_attn<false, false, EXTRA>(prm, grid, st);
+}
+
+static int dispatch_attn(const dgxm_attn_desc* d, const AttnParams& prm, dim3 grid, void* stream) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (fp8) return out_f32 ? launch_attn<true, true>(prm, grid, st) : launch_attn<true, false>(prm, grid, st);
-  return out_f32 ? launch_attn<false, true>(prm, grid, st) : launch_attn<false, false>(prm, grid, st);
+  const bool extra = prm.kmask != nullptr || prm.qmask != nullptr || prm.n_bias > 0;
+  return extra ? dispatch_attn_t<true>(d, prm, grid, st) : dispatch_attn_t<false>(d, prm, grid, st);
+}
+
+// Fill the output routing of the fused inverse all-to-all.
+static int set_route(const dgxm_attn_desc* d, const dgxm_attn_route* rt, AttnParams* prm) {
+  if (rt->world < 1 || rt->world > DGXM_MAX_WORLD || rt->rank < 0 || rt->rank >= rt->world)
+    return fail(DGXM_ERR_INVALID, "rank %d / world %d out of range", rt->rank, rt->world);
+  if (rt->seq_local <= 0 || static_cast<int64_t>(rt->seq_local) * rt->world != d->q_len)
+    return fail(DGXM_ERR_INVALID, "seq_local %d x world %d does not cover q_len %d", rt->seq_local,
+                rt->world, d->q_len);
+  if (rt->seg0 < 0 || rt->seg0 >= rt->seq_local)
+    return fail(DGXM_ERR_INVALID, "joint segment of %d rows does not split %d local rows", rt->seg0,
+                rt->seq_local);
+  for (int r = 0; r < rt->world; ++r) {
+    if (rt->o_peers[r] == nullptr || reinterpret_cast<uintptr_t>(rt->o_peers[r]) % 16)
+      return fail(DGXM_ERR_INVALID, "output peer %d is NULL or not 16-byte aligned", r);
+    prm->o_peer[r] = rt->o_peers[r];
+  }
+  prm->o_rows = rt->seq_local;
+  prm->o_head_off = rt->rank * d->q_heads;
+  prm->o_world = rt->world;
+  prm->o_seg0 = rt->seg0;
+  return DGXM_OK;
+}
+
+// Fill the keep masks and query-group biases.
+static int set_extras(const dgxm_attn_desc* d, const dgxm_attn_extras* ex, AttnParams* prm) {
+  prm->kmask = ex->key_keep;
+  prm->kmask_sb = ex->key_keep_batch_stride;
+  prm->kmask_words = (d->kv_len + 31) / 32;
+  prm->qmask = ex->query_keep;
+  prm->qmask_sb = ex->query_keep_batch_stride;
+  if (ex->n_bias_groups < 0 || ex->n_bias_groups > DGXM_MAX_BIAS_GROUPS)
+    return fail(DGXM_ERR_INVALID, "%d bias groups (at most %d)", ex->n_bias_groups,
+                DGXM_MAX_BIAS_GROUPS);
+  prm->n_bias = ex->n_bias_groups;
+  for (int g = 0; g < ex->n_bias_groups; ++g) {
+    if (ex->bias_row_begin[g] < 0 || ex->bias_row_end[g] < ex->bias_row_begin[g] ||
+        ex->bias_row_end[g] > d->q_len)
+      return fail(DGXM_ERR_INVALID, "bias group %d rows [%d, %d) outside [0, %d)", g,
+                  ex->bias_row_begin[g], ex->bias_row_end[g], d->q_len);
+    if (ex->bias_keys[g] < 0 || ex->bias_keys[g] > d->kv_len)
+      return fail(DGXM_ERR_INVALID, "bias group %d declares %d keys over %d", g, ex->bias_keys[g],
+                  d->kv_len);
+    prm->bias_q0[g] = ex->bias_row_begin[g];
+    prm->bias_q1[g] = ex->bias_row_end[g];
+    prm->bias[g] = ex->bias[g];
+    prm->bias_sb[g] = ex->bias_stride[g][0];
+    prm->bias_sh[g] = ex->bias_stride[g][1];
+    prm->bias_sq[g] = ex->bias_stride[g][2];
+    prm->bias_len[g] = ex->bias_keys[g];
+  }
+  const float scale = d->softmax_scale > 0.f ? d->softmax_scale : 1.0f / sqrtf((float)d->head_dim);
+  prm->inv_scale = 1.0f / scale;
+  return DGXM_OK;
 }
 
 }  // namespace dgxm
@@ -734,13 +862,35 @@ extern "C" int dgxm_attn_fwd_routed(const dgxm_attn_desc* d, const void* q, cons
   int rc = prepare_attn(d, q, k, v, q_descale, k_descale, v_descale, o_peers[0], lse, &prm,
                         &grid, &skip);
   if (rc != DGXM_OK || skip) return rc;
-  for (int r = 0; r < world; ++r) prm.o_peer[r] = o_peers[r];
-  if (seg0 < 0 || seg0 >= seq_local)
-    return fail(DGXM_ERR_INVALID, "joint segment of %d rows does not split %d local rows", seg0,
-                seq_local);
-  prm.o_rows = seq_local;
-  prm.o_head_off = rank * d->q_heads;
-  prm.o_world = world;
-  prm.o_seg0 = seg0;
+  dgxm_attn_route rt;
+  memset(&rt, 0, sizeof(rt));
+  for (int r = 0; r < world; ++r) rt.o_peers[r] = o_peers[r];
+  rt.world = world;
+  rt.rank = rank;
+  rt.seq_local = seq_local;
+  rt.seg0 = seg0;
+  if ((rc = set_route(d, &rt, &prm))) return rc;
+  return dispatch_attn(d, prm, grid, stream);
+}
+
+extern "C" int dgxm_attn_fwd_ext(const dgxm_attn_desc* d, const dgxm_attn_extras* extras,
+                                 const dgxm_attn_route* route, const void* q, const void* k,
+                                 const void* v, const float* q_descale, const float* k_descale,
+                                 const float* v_descale, void* o, float* lse, void* stream) {
+  using namespace dgxm;
+  if (d == nullptr) return fail(DGXM_ERR_INVALID, "attention descriptor is NULL");
+  void* o0 = o;
+  if (route != nullptr) {
+    if (route->world < 1 || route->world > DGXM_MAX_WORLD)
+      return fail(DGXM_ERR_INVALID, "route world %d out of range", route->world);
+    o0 = route->o_peers[0];
+  }
+  AttnParams prm;
+  dim3 grid;
+  bool skip = false;
+  int rc = prepare_attn(d, q, k, v, q_descale, k_descale, v_descale, o0, lse, &prm, &grid, &skip);
+  if (rc != DGXM_OK || skip) return rc;
+  if (route != nullptr && (rc = set_route(d, route, &prm))) return rc;
+  if (extras != nullptr && (rc = set_extras(d, extras, &prm))) return rc;
   return dispatch_attn(d, prm, grid, stream);
 }

@@ -108,6 +108,107 @@ def attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
     return out, lse
 
 
+_KEEP_BITS: dict = {}
+
+
+def keep_bits(rows: int, drop_rows, device: torch.device) -> torch.Tensor | None:
+    """Packed keep bits (int32 words, bit i of word i//32) of `rows` rows with
+    `drop_rows` cleared; None when nothing drops.  Cached per layout, like the
+    reference's keep index (adapters/usp_pad_exclusion.py:93-126), and range
+    checked before any device work."""
+    if not drop_rows:
+        return None
+    key = (rows, tuple(sorted(set(drop_rows))), str(device))
+    found = _KEEP_BITS.get(key)
+    if found is not None:
+        return found
+    drop = key[1]
+    if drop[-1] >= rows or drop[0] < 0:
+        raise ValueError(f"a pad row at index {drop[-1]} was handed to an attention whose axis "
+                         f"carries {rows} rows")
+    words = (rows + 31) // 32
+    bits = [0xFFFFFFFF] * words
+    if rows % 32:
+        bits[-1] = (1 << (rows % 32)) - 1
+    for r in drop:
+        bits[r // 32] &= ~(1 << (r % 32)) & 0xFFFFFFFF
+    t = torch.tensor([b - (1 << 32) if b >= (1 << 31) else b for b in bits], dtype=torch.int32,
+                     device=device)
+    if len(_KEEP_BITS) > 64:
+        _KEEP_BITS.clear()
+    _KEEP_BITS[key] = t
+    return t
+
+
+def attention_fwd_ext(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
+                      key_keep: torch.Tensor | None = None,
+                      query_keep: torch.Tensor | None = None,
+                      bias_groups=None,
+                      route: dict | None = None,
+                      out: torch.Tensor | None = None,
+                      out_strides=None,
+                      lse: torch.Tensor | None = None,
+                      softmax_scale: float | None = None,
+                      q_descale=None, k_descale=None, v_descale=None):
+    """Attention with keep masks, query-group biases and/or output routing.
+
+    bias_groups: [(row_begin, row_end, bias fp32 (B|1, H|1, Q|1, K') or None)],
+    Q the group's row count;
+    route: {"o_peers": [ptr...], "world", "rank", "seq_local", "seg0"} with
+    out_strides describing the peers' (B, Ls, H_total, D) tensors.
+    """
+    dev = _require_cuda(q, k, v)
+    b, lq, h, d = q.shape
+    keep = []
+    if out is None and route is None:
+        out = torch.empty((b, lq, h, d), device=dev, dtype=torch.bfloat16)
+    probe_out = out if out is not None else torch.empty((1, 1, 1, d), device="meta", dtype=torch.bfloat16)
+    desc = attn_desc(q, k, v, probe_out, lse, softmax_scale)
+    if out_strides is not None:
+        desc.o_stride[:] = list(out_strides)
+    ex = _lib.AttnExtras()
+    if key_keep is not None:
+        ex.key_keep = key_keep.data_ptr()
+        ex.key_keep_batch_stride = key_keep.stride(0) if key_keep.ndim == 2 else 0
+    if query_keep is not None:
+        ex.query_keep = query_keep.data_ptr()
+        ex.query_keep_batch_stride = query_keep.stride(0) if query_keep.ndim == 2 else 0
+    groups = [g for g in (bias_groups or []) if g[2] is not None]
+    if len(groups) > _lib.MAX_BIAS_GROUPS:
+        raise ValueError(f"at most {_lib.MAX_BIAS_GROUPS} biased query groups")
+    ex.n_bias_groups = len(groups)
+    for i, (start, end, bias) in enumerate(groups):
+        if bias.dtype != torch.float32 or bias.ndim != 4 or bias.stride(3) != 1:
+            raise ValueError("a group bias must be fp32 (B|1, H|1, Q|1, K) with contiguous keys")
+        if bias.shape[2] not in (1, end - start):
+            raise ValueError(f"a group bias of {bias.shape[2]} query rows over a group of "
+                             f"{end - start}")
+        keep.append(bias)
+        ex.bias_row_begin[i], ex.bias_row_end[i] = int(start), int(end)
+        ex.bias[i] = bias.data_ptr()
+        ex.bias_stride[i][0] = 0 if bias.shape[0] == 1 else bias.stride(0)
+        ex.bias_stride[i][1] = 0 if bias.shape[1] == 1 else bias.stride(1)
+        ex.bias_stride[i][2] = 0 if bias.shape[2] == 1 else bias.stride(2)
+        ex.bias_keys[i] = bias.shape[3]
+    rt = None
+    if route is not None:
+        rt = _lib.AttnRoute()
+        for i, ptr in enumerate(route["o_peers"]):
+            rt.o_peers[i] = ptr
+        rt.world, rt.rank = route["world"], route["rank"]
+        rt.seq_local, rt.seg0 = route["seq_local"], route.get("seg0", 0)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        rc = lib.dgxm_attn_fwd_ext(ctypes.byref(desc), ctypes.byref(ex),
+                                   ctypes.byref(rt) if rt is not None else None,
+                                   q.data_ptr(), k.data_ptr(), v.data_ptr(), _ptr(q_descale),
+                                   _ptr(k_descale), _ptr(v_descale),
+                                   out.data_ptr() if out is not None else None, _ptr(lse), stream)
+    _lib.check(rc, "dgxm_attn_fwd_ext")
+    return out, lse
+
+
 def lse_merge(parts_out: list[torch.Tensor], parts_lse: list[torch.Tensor], *,
               out_dtype: torch.dtype = torch.bfloat16,
               out: torch.Tensor | None = None,

@@ -9,9 +9,12 @@ the reference's `_AttentionDispatch.configure` (actor/attention_dispatch.py:
   the inverse all-to-all in its epilogue -> barrier; a joint-order
   descriptor (adapters/usp_sequence_order.py) is applied by the scatter and
   the epilogue row maps, never by index copies;
-- pad rows (adapters/usp_pad_exclusion.py:152-177): scatter, keep-index
-  compaction at the full-axis point, attention, zero-restore, inverse
-  all-to-all kernel;
+- pad rows (adapters/usp_pad_exclusion.py:152-177): the same fused path,
+  with keep bits over keys and query rows applied inside the attention
+  kernel (excluded keys never enter a softmax, dropped rows are written as
+  zeros) instead of index_select / zero-restore copies;
+- query-group biases (adapters/usp_query_bias.py:109-130), key rows or
+  per-query rectangles, added to the scaled logits inside the kernel;
 - Ulysses x ring: Ulysses scatter inside the Ulysses group, ring attention
   over the ring group, inverse all-to-all kernel.
 
@@ -21,12 +24,12 @@ collectives require, so the window exchange on first use stays collective.
 """
 from __future__ import annotations
 
-import math
 
 import torch
 
+from ._lib import MAX_BIAS_GROUPS
 from .comm import PeerWindows
-from .ops import attention_fwd
+from .ops import attention_fwd, attention_fwd_ext, keep_bits
 from .ring import RingAttention
 from .ulysses import attention_routed, ulysses_gather, ulysses_scatter
 
@@ -42,19 +45,16 @@ def _mask_is_noop(mask) -> bool:
     return not bool(mask.any())
 
 
-def _kept_rows(rows: int, drop_rows, device) -> torch.Tensor | None:
-    """Ascending kept indices, built on the device; refuses out-of-range rows
-    before any device scatter (adapters/usp_pad_exclusion.py:79-126)."""
+def _check_pad_rows(rows: int, drop_rows) -> None:
+    """Refuse pad rows outside the gathered axis before any device work
+    (adapters/usp_pad_exclusion.py:93-108)."""
     if not drop_rows:
-        return None
+        return
     highest = max(drop_rows)
     if highest >= rows or min(drop_rows) < 0:
         raise UnsupportedModelError(
             f"a divisibility pad row at index {highest} was handed to an attention whose axis "
             f"carries {rows} rows. This is a dgx-monarch fault, not a workflow setting.")
-    mask = torch.ones(rows, dtype=torch.bool)
-    mask[sorted(set(drop_rows))] = False
-    return torch.nonzero(mask).flatten().to(device)
 
 
 class _Groups:
@@ -131,7 +131,7 @@ class B200SequenceParallelAttention:
         return plan
 
     # ---------------------------------------------------------------- forward
-    def attend(self, q_l, k_l, v_l, drop_rows, kv_drop_rows, sequence_order):
+    def attend(self, q_l, k_l, v_l, drop_rows, kv_drop_rows, sequence_order, bias_groups=None):
         """(B, Ls, H, D) local rows in, (B, Ls, H, D) local rows out."""
         if self.closed:
             raise UnsupportedModelError("this attention implementation belongs to a retired setup "
@@ -157,9 +157,11 @@ class B200SequenceParallelAttention:
                 inv = _joint_inverse(text, image, p)
                 drop_rows = sorted(inv[r] for r in drop_rows) if drop_rows else drop_rows
                 kv_drop_rows = sorted(inv[r] for r in kv_drop_rows) if kv_drop_rows else kv_drop_rows
+        _check_pad_rows(ls * p, drop_rows)
+        _check_pad_rows(k_l.shape[1] * p, kv_drop_rows)
         if p == 1 and g.ring_world == 1 and not self.fp8:
-            return self._local(q_l, k_l, v_l, drop_rows, kv_drop_rows)
-        if self.fp8 and (g.ring_world > 1 or drop_rows or kv_drop_rows):
+            return self._local(q_l, k_l, v_l, drop_rows, kv_drop_rows, bias_groups)
+        if self.fp8 and (g.ring_world > 1 or drop_rows or kv_drop_rows or bias_groups):
             raise UnsupportedModelError(
                 "the B200 FP8 attention path runs pure Ulysses without pad rows; use the bf16 "
                 "kernel for ring topologies or padded sequences")
@@ -186,38 +188,31 @@ class B200SequenceParallelAttention:
             attention_routed(plan["q8"], plan["k8"], plan["v8"], out_ptrs, (ls * h * d, h * d, d),
                              world=p, rank=g.uly_rank, seq_local=ls, seg0=seg0,
                              q_descale=plan["ds"][0], k_descale=plan["ds"][1], v_descale=plan["ds"][2])
-        elif not drop_rows and not kv_drop_rows:
+        elif not drop_rows and not kv_drop_rows and not bias_groups:
             attention_routed(qg, kg, vg, out_ptrs, (ls * h * d, h * d, d), world=p, rank=g.uly_rank,
                              seq_local=ls, seg0=seg0)
         else:
-            full = self._exact_without_pads(qg, kg, vg, drop_rows, kv_drop_rows)
-            ulysses_gather(full, out_ptrs, world=p, rank=g.uly_rank, seq_local=ls, heads=h, seg0=seg0)
+            # Pads and biases live on the full axis, which this rank holds for
+            # its heads; the kernel applies both and still routes the output.
+            attention_fwd_ext(qg, kg, vg, key_keep=keep_bits(kg.shape[1], kv_drop_rows, qg.device),
+                              query_keep=keep_bits(qg.shape[1], drop_rows, qg.device),
+                              bias_groups=_rank_bias(bias_groups, g.uly_rank, h // p,
+                                                     kg.shape[1], kv_drop_rows),
+                              route={"o_peers": out_ptrs, "world": p, "rank": g.uly_rank,
+                                     "seq_local": ls, "seg0": seg0},
+                              out_strides=(ls * h * d, h * d, d))
         win.barrier()
         return plan["out"].clone()
 
-    def _local(self, q, k, v, drop_rows, kv_drop_rows):
-        if drop_rows or kv_drop_rows:
-            return self._exact_without_pads(q, k, v, drop_rows, kv_drop_rows)
+    def _local(self, q, k, v, drop_rows, kv_drop_rows, bias_groups=None):
+        if drop_rows or kv_drop_rows or bias_groups:
+            out, _ = attention_fwd_ext(q, k, v, key_keep=keep_bits(k.shape[1], kv_drop_rows, q.device),
+                                       query_keep=keep_bits(q.shape[1], drop_rows, q.device),
+                                       bias_groups=_rank_bias(bias_groups, 0, q.shape[2],
+                                                              k.shape[1], kv_drop_rows))
+            return out
         out, _ = attention_fwd(q, k, v, return_lse=False)
         return out
-
-    def _exact_without_pads(self, q, k, v, drop_rows, kv_drop_rows):
-        """Attend the real rows only and write zeros where pads sat
-        (adapters/usp_pad_exclusion.py:152-177)."""
-        qi = _kept_rows(q.shape[1], drop_rows, q.device)
-        if kv_drop_rows is drop_rows and k.shape[1] == q.shape[1]:
-            ki = qi
-        else:
-            ki = _kept_rows(k.shape[1], kv_drop_rows, k.device)
-        qq = q if qi is None else q.index_select(1, qi)
-        kk = k if ki is None else k.index_select(1, ki)
-        vv = v if ki is None else v.index_select(1, ki)
-        out, _ = attention_fwd(qq, kk, vv, return_lse=False)
-        if qi is None:
-            return out
-        full = q.new_zeros(q.shape)
-        full[:, qi] = out
-        return full
 
     def _hybrid(self, q_l, k_l, v_l):
         """Ulysses inside the Ulysses group, ring across the ring group."""
@@ -254,6 +249,76 @@ class B200SequenceParallelAttention:
                 plan.close()
         self._plans.clear()
         self.closed = True
+
+
+def _rank_bias(groups, rank: int, heads_local: int, keys: int, kv_drop_rows):
+    """This rank's slice of the group biases: (B|1, H|1, Q|1, K') -> fp32
+    (B|1, H_local|1, Q|1, K'') for the heads the rank attends after the scatter.
+
+    A bias names keys by their position among the kept keys
+    (adapters/usp_query_bias.py:95-106 runs after the pads are dropped).  The
+    kernel reads the padded axis, so where a pad key precedes a declared key
+    the bias is spread onto the kept positions; pads at the tail need no
+    change, and a zero column adds nothing where the bias declared no key."""
+    if not groups:
+        return None
+    kept = None
+    if kv_drop_rows:
+        drop = sorted(set(kv_drop_rows))
+        if drop != list(range(keys - len(drop), keys)):
+            dropped = set(drop)
+            kept = [r for r in range(keys) if r not in dropped]
+    out = []
+    for start, end, bias in groups:
+        if bias is None:
+            out.append((start, end, None))
+            continue
+        bb = bias
+        if bb.shape[1] > 1:
+            bb = bb[:, rank * heads_local:(rank + 1) * heads_local]
+        bb = bb.float()
+        if kept is not None:
+            n = bb.shape[3]
+            index = torch.tensor(kept[:n], device=bb.device)
+            spread = bb.new_zeros((*bb.shape[:3], kept[n - 1] + 1 if n else 0))
+            spread.index_copy_(3, index, bb)
+            bb = spread
+        out.append((start, end, bb.contiguous()))
+    return out
+
+
+def validate_bias_groups(groups, queries: int, keys: int, batch: int, heads: int) -> None:
+    """The partition contract of adapters/usp_query_bias.py:64-97, plus the
+    broadcast and group-count limits of the kernel."""
+    cursor = 0
+    for start, end, bias in groups:
+        if start != cursor or end < start or end > queries:
+            raise UnsupportedModelError(
+                f"query bias groups are malformed: group [{start}, {end}) does not continue the "
+                f"partition of [0, {queries}) at row {cursor}")
+        cursor = end
+        if bias is None:
+            continue
+        if bias.ndim != 4 or bias.shape[2] not in (1, end - start):
+            raise UnsupportedModelError(
+                f"query bias groups are malformed: a bias shaped {tuple(bias.shape)} does not "
+                f"broadcast over the {end - start} query rows of its group as (B, H, Q, K)")
+        if bias.shape[3] > keys:
+            raise UnsupportedModelError(
+                f"query bias groups are malformed: a bias declares {bias.shape[3]} keys over a "
+                f"sequence of {keys}")
+        if bias.shape[0] not in (1, batch) or bias.shape[1] not in (1, heads):
+            raise UnsupportedModelError(
+                f"query bias groups are malformed: a bias shaped {tuple(bias.shape)} does not "
+                f"broadcast over batch {batch} and {heads} heads")
+    if cursor != queries:
+        raise UnsupportedModelError(
+            f"query bias groups are malformed: the groups cover {cursor} of {queries} query rows")
+    biased = sum(1 for group in groups if group[2] is not None)
+    if biased > MAX_BIAS_GROUPS:
+        raise UnsupportedModelError(
+            f"the B200 kernel applies at most {MAX_BIAS_GROUPS} biased query groups in one call; "
+            f"this one carries {biased}. Select TORCH_FLASH for it.")
 
 
 def _joint_inverse(text: int, image: int, world: int) -> list[int]:
@@ -338,10 +403,6 @@ def make_b200_usp_attention(*, ulysses_group=None, ring_group=None, generation: 
         if kwargs:
             raise UnsupportedModelError(
                 f"the B200 sequence-parallel kernel cannot apply extra attention arguments {sorted(kwargs)}")
-        if query_bias_groups:
-            raise UnsupportedModelError(
-                "query-group attention bias is not supported by the B200 sequence-parallel kernel; "
-                "select TORCH_FLASH for this family")
         padded = bool(drop_rows) or bool(kv_drop_rows)
         ring_world = impl.groups.ring_world
         if padded and ring_world > 1:
@@ -349,13 +410,35 @@ def make_b200_usp_attention(*, ulysses_group=None, ring_group=None, generation: 
                 "this sequence length needs divisibility padding, and the exact pad exclusion is "
                 "ulysses-only; ring/hybrid attention would attend the synthetic pad rows. Use a "
                 "uly* or single topology (docs/ADAPTERS.md).")
+        if query_bias_groups:
+            if ring_world != 1:
+                raise UnsupportedModelError(
+                    "this render biases attention between token groups, and ring or hybrid "
+                    "attention shards the key axis, so the weights cannot be applied where the "
+                    "kernel reads them. Use a pure-ulysses topology.")
+            if sequence_order is not None:
+                raise UnsupportedModelError(
+                    "joint Ulysses order cannot preserve this attention contract: query-bias group "
+                    "coordinates are present")
+            full_q = q_l.shape[1] * impl.groups.uly_world
+            full_k = k_l.shape[1] * impl.groups.uly_world
+            if drop_rows:
+                tail = list(range(full_q - len(drop_rows), full_q))
+                if list(drop_rows) != tail:
+                    raise UnsupportedModelError(
+                        f"a query-group bias met {len(drop_rows)} divisibility pad row(s) away from "
+                        f"the tail of its {full_q}-row sequence, where the group boundaries stop "
+                        "being exact.")
+            validate_bias_groups(query_bias_groups, full_q - len(drop_rows or ()),
+                                 full_k - len(kv_drop_rows if kv_drop_rows is not None else drop_rows or ()),
+                                 b, h)
         if sequence_order is not None and ring_world != 1:
             sequence_order = None
         if q_l.dtype != torch.bfloat16:
             q_l, k_l, v_l = (t.to(torch.bfloat16) for t in (q_l, k_l, v_l))
         q_l, k_l, v_l = (t if t.stride(-1) == 1 else t.contiguous() for t in (q_l, k_l, v_l))
         kv_rows = drop_rows if kv_drop_rows is None else kv_drop_rows
-        out = impl.attend(q_l, k_l, v_l, drop_rows, kv_rows, sequence_order)
+        out = impl.attend(q_l, k_l, v_l, drop_rows, kv_rows, sequence_order, query_bias_groups)
         out = out.to(q.dtype)
         if skip_output_reshape:
             return out.transpose(1, 2)

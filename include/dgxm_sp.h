@@ -91,6 +91,59 @@ int dgxm_attn_fwd(const dgxm_attn_desc* desc, const void* q, const void* k, cons
                   const float* q_descale, const float* k_descale, const float* v_descale,
                   void* o, float* lse, void* stream);
 
+/* ------------------------------------------------------------ attention extras */
+#define DGXM_MAX_BIAS_GROUPS 8
+
+/*
+ * Optional inputs of dgxm_attn_fwd_ext.
+ *
+ * key_keep / query_keep: bit i of word i/32 keeps key (query row) i; a key
+ * with bit 0 is excluded from every softmax, a query row with bit 0 is
+ * written as zeros (LSE -inf).  This is the exact pad-row exclusion of
+ * adapters/usp_pad_exclusion.py:152-177 (attend the real rows, zero-restore
+ * the pads) done inside the kernel instead of by index_select copies.
+ * NULL keeps everything; a batch stride of 0 shares one mask.
+ *
+ * Query-group bias (adapters/usp_query_bias.py:109-130): query row r in
+ * [bias_row_begin[g], bias_row_end[g]) adds
+ * bias[g][b, h, r - bias_row_begin[g], key] to its scaled logits for keys
+ * < bias_keys[g] (later keys carry no bias, extend_bias_keys at
+ * adapters/usp_query_bias.py:95-106); rows in no group carry none.  fp32,
+ * strides in elements; a stride of 0 broadcasts (a query-row stride of 0 is
+ * one key row shared by the whole group).
+ */
+typedef struct dgxm_attn_extras {
+  const uint32_t* key_keep;
+  int64_t key_keep_batch_stride;   /* words */
+  const uint32_t* query_keep;
+  int64_t query_keep_batch_stride; /* words */
+  int32_t n_bias_groups;
+  int32_t bias_row_begin[DGXM_MAX_BIAS_GROUPS];
+  int32_t bias_row_end[DGXM_MAX_BIAS_GROUPS];
+  const float* bias[DGXM_MAX_BIAS_GROUPS];
+  int64_t bias_stride[DGXM_MAX_BIAS_GROUPS][3]; /* batch, head, query row */
+  int32_t bias_keys[DGXM_MAX_BIAS_GROUPS];
+} dgxm_attn_extras;
+
+/* Output routing of the fused inverse all-to-all (see dgxm_attn_fwd_routed). */
+typedef struct dgxm_attn_route {
+  void* o_peers[8];
+  int32_t world;
+  int32_t rank;
+  int32_t seq_local;
+  int32_t seg0;
+} dgxm_attn_route;
+
+/*
+ * dgxm_attn_fwd with optional extras and optional output routing (either may
+ * be NULL; with a route, `o` is ignored).  The general entry behind the
+ * drop-in's padded and biased calls.
+ */
+int dgxm_attn_fwd_ext(const dgxm_attn_desc* desc, const dgxm_attn_extras* extras,
+                      const dgxm_attn_route* route, const void* q, const void* k, const void* v,
+                      const float* q_descale, const float* k_descale, const float* v_descale,
+                      void* o, float* lse, void* stream);
+
 /* ------------------------------------------------------------ LSE merge */
 /*
  * Merge n_parts partial attention results over disjoint key blocks:

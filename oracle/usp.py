@@ -100,6 +100,74 @@ def attend_without_pads(q, k, v, drop_rows, kv_drop_rows, attend):
     return full
 
 
+# ----------------------------------------------------------------- query-group bias
+def validate_query_bias_groups(groups, queries: int, keys: int) -> None:
+    """Groups must partition [0, queries) in order; each bias broadcasts as
+    (B, H, Q, K) over its group and declares at most `keys` keys
+    (adapters/usp_query_bias.py:64-92)."""
+    cursor = 0
+    for start, end, bias in groups:
+        if start != cursor or end < start or end > queries:
+            raise OracleRefusal(f"group [{start}, {end}) does not continue the partition of "
+                                f"[0, {queries}) at row {cursor}")
+        cursor = end
+        if bias is None:
+            continue
+        if bias.ndim != 4 or bias.shape[2] not in (1, end - start):
+            raise OracleRefusal(f"a bias shaped {bias.shape} does not broadcast over its group")
+        if bias.shape[3] > keys:
+            raise OracleRefusal(f"a bias declares {bias.shape[3]} keys over a sequence of {keys}")
+    if cursor != queries:
+        raise OracleRefusal(f"the groups cover {cursor} of {queries} query rows")
+
+
+def extend_bias_keys(bias: np.ndarray, keys: int) -> np.ndarray:
+    """Zero columns for the keys a bias does not declare
+    (adapters/usp_query_bias.py:95-106)."""
+    short = keys - bias.shape[3]
+    if short <= 0:
+        return bias
+    return np.concatenate([bias, np.zeros((*bias.shape[:3], short), dtype=bias.dtype)], axis=3)
+
+
+def query_group_attention(q, k, v, groups, scale=None):
+    """Each query group attends the whole key axis under its own additive
+    bias, float64 (adapters/usp_query_bias.py:109-130); (B, L, H, D) in/out."""
+    validate_query_bias_groups(groups, q.shape[1], k.shape[1])
+    d = q.shape[-1]
+    scale = 1.0 / math.sqrt(d) if scale is None else scale
+    qh, kh, vh = (np.asarray(t, dtype=np.float64).transpose(0, 2, 1, 3) for t in (q, k, v))
+    out = np.empty_like(qh)
+    for start, end, bias in groups:
+        if end == start:
+            continue
+        logits = qh[:, :, start:end] @ kh.transpose(0, 1, 3, 2) * scale
+        if bias is not None:
+            logits = logits + extend_bias_keys(np.asarray(bias, dtype=np.float64), kh.shape[2])
+        logits = logits - logits.max(axis=-1, keepdims=True)
+        w = np.exp(logits)
+        out[:, :, start:end] = (w / w.sum(axis=-1, keepdims=True)) @ vh
+    return out.transpose(0, 2, 1, 3)
+
+
+def assert_pads_are_a_tail(drop_rows, rows: int) -> None:
+    """A biased stream's pad rows must be the sequence tail, or the group
+    boundaries would slide (adapters/usp_pad_exclusion.py:129-149)."""
+    if drop_rows and list(drop_rows) != list(range(rows - len(drop_rows), rows)):
+        raise OracleRefusal(f"a query-group bias met {len(drop_rows)} divisibility pad row(s) "
+                            f"away from the tail of its {rows}-row sequence")
+
+
+def attend_groups_without_pads(q, k, v, drop_rows, kv_drop_rows, groups):
+    """The pad exclusion with query-bias groups: tail check, drop, grouped
+    attention, zero-restore (adapters/usp_pad_exclusion.py:152-177 with
+    groups, adapters/usp_full_axis.py:14-16)."""
+    if groups:
+        assert_pads_are_a_tail(drop_rows, q.shape[1])
+    return attend_without_pads(q, k, v, drop_rows, kv_drop_rows,
+                               lambda qq, kk, vv: query_group_attention(qq, kk, vv, groups))
+
+
 # ----------------------------------------------------------------- joint order
 @dataclass(frozen=True)
 class RankMajorJointOrder:

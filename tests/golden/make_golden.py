@@ -224,6 +224,64 @@ def main() -> None:
         arrays[f"probe_{n}_lse"] = lse.numpy()
     golden["probe"] = [{"index": n, "dtype": str(s[0].dtype), "scale": s[5]} for n, s in enumerate(seen)]
 
+    # i) query-group biases through the usp_attention callable at world 1
+    #    (adapters/base.py:299-316 -> usp_full_axis.py:14-16 ->
+    #    usp_query_bias.py:109-130), comfy's SDPA wrapper stubbed by torch SDPA
+    #    as tests/test_usp_query_bias.py:26-29 passes it: the LTX guide
+    #    rectangles (one weight, per-token weights with a zero), a Lens-style
+    #    single key-bias group, a per-head bias, and a padded stream whose tail
+    #    pads are dropped (tests/test_usp_query_bias.py:198-223).
+    comfy = types.ModuleType("comfy")
+    comfy_ops = types.ModuleType("comfy.ops")
+    comfy_ops.scaled_dot_product_attention = (
+        lambda q, k, v, attn_mask=None: torch.nn.functional.scaled_dot_product_attention(
+            q, k, v, attn_mask=attn_mask))
+    sys.modules.update({"comfy": comfy, "comfy.ops": comfy_ops})
+    _install_stubs()
+    attn = base._make_usp_attention_callable(sys.modules["xfuser.core.long_ctx_attention"]
+                                             .xFuserLongContextAttention())
+
+    def guide(tokens, guide_start, weights):
+        finfo = torch.finfo(weights.dtype)
+        log_w = torch.full_like(weights, finfo.min)
+        log_w[weights > 0] = torch.log(weights[weights > 0])
+        tracked = weights.shape[0]
+        noisy = torch.zeros((1, 1, 1, tokens), dtype=weights.dtype)
+        noisy[..., guide_start:guide_start + tracked] = log_w.view(1, 1, 1, -1)
+        rect = torch.zeros((1, 1, tracked, tokens), dtype=weights.dtype)
+        rect[..., :guide_start] = log_w.view(1, 1, -1, 1)
+        groups = [(0, guide_start, noisy), (guide_start, guide_start + tracked, rect)]
+        if guide_start + tracked < tokens:
+            groups.append((guide_start + tracked, tokens, None))
+        return groups
+
+    f64 = torch.float64
+    bias_cases = [
+        ("ltx_uniform", 12, 4, guide(12, 8, torch.full((4,), 0.7, dtype=f64)), None),
+        ("ltx_pixel", 14, 4, guide(14, 9, torch.tensor([0.2, 0.8, 0.0, 1.0, 0.55], dtype=f64)), None),
+        ("ltx_partial", 16, 2, guide(16, 9, torch.full((4,), 0.3, dtype=f64)), None),
+        ("lens_key_bias", 11, 2, [(0, 11, torch.from_numpy(rng.standard_normal((1, 1, 1, 9))))], None),
+        ("per_head", 10, 2, [(0, 4, None), (4, 10, torch.from_numpy(rng.standard_normal((1, 2, 1, 10))))],
+         None),
+        ("padded_tail", 14, 4, guide(12, 8, torch.full((4,), 0.7, dtype=f64)), [12, 13]),
+    ]
+    biased = []
+    for name, tokens, hds, groups, drop in bias_cases:
+        q = torch.from_numpy(rng.standard_normal((1, hds, tokens, 8)))
+        k = torch.from_numpy(rng.standard_normal((1, hds, tokens, 8)))
+        v = torch.from_numpy(rng.standard_normal((1, hds, tokens, 8)))
+        out = attn(q, k, v, heads=hds, skip_reshape=True, skip_output_reshape=True,
+                   drop_rows=drop, query_bias_groups=tuple(groups))
+        for key, t in (("q", q), ("k", k), ("v", v), ("out", out)):
+            arrays[f"bias_{name}_{key}"] = t.transpose(1, 2).numpy()
+        spec = []
+        for g, (start, end, bias) in enumerate(groups):
+            if bias is not None:
+                arrays[f"bias_{name}_g{g}"] = bias.numpy()
+            spec.append([start, end, None if bias is None else f"bias_{name}_g{g}"])
+        biased.append({"name": name, "tokens": tokens, "heads": hds, "groups": spec, "drop": drop})
+    golden["query_bias"] = biased
+
     (OUT / "golden.json").write_text(json.dumps(golden, indent=1))
     np.savez_compressed(OUT / "golden_arrays.npz", **arrays)
     print("wrote", OUT / "golden.json", OUT / "golden_arrays.npz")

@@ -164,3 +164,96 @@ def test_invalid_arguments_raise_before_launch(lib):
     k = torch.randn(1, 64, 2, 128, device="cuda").bfloat16()
     with pytest.raises(DgxmError, match="divisible"):
         attention_fwd(q, k, k)
+
+
+def test_keep_masks_exclude_pad_rows_exactly(lib):
+    """In-kernel pad exclusion: attention over the kept rows only, zeros (and
+    LSE -inf) at dropped query rows -- adapters/usp_pad_exclusion.py:152-177."""
+    from dgx_monarch_b200.ops import attention_fwd_ext, keep_bits
+
+    g = torch.Generator(device="cuda").manual_seed(31)
+    rows = 700
+    q, k, v = (torch.randn(1, rows, 3, 128, device="cuda", generator=g).bfloat16() for _ in range(3))
+    drop = [0, 5, 127, 128, 255, 256, 311, 699]
+    kk = keep_bits(rows, drop, q.device)
+    out, lse = attention_fwd_ext(q, k, v, key_keep=kk, query_keep=kk,
+                                 lse=torch.empty(1, 3, rows, device="cuda"))
+    torch.cuda.synchronize()
+    keep = [i for i in range(rows) if i not in drop]
+    ref, ref_lse = reference_attention(q[:, keep], k[:, keep], v[:, keep])
+    assert (out[:, keep].float() - ref).abs().max().item() <= BF16_MAX_ABS
+    assert rel_l2(out[:, keep], ref) <= BF16_REL_L2
+    assert torch.equal(out[:, drop], torch.zeros_like(out[:, drop]))
+    assert (lse[:, :, keep] - ref_lse).abs().max().item() <= LSE_ABS
+    assert torch.isinf(lse[:, :, drop]).all()
+
+
+def test_key_mask_over_whole_blocks_and_cross_attention(lib):
+    """Keys dropped over entire 128-key blocks, and a key side that pads
+    while the query side does not."""
+    from dgx_monarch_b200.ops import attention_fwd_ext, keep_bits
+
+    g = torch.Generator(device="cuda").manual_seed(37)
+    q = torch.randn(1, 300, 2, 128, device="cuda", generator=g).bfloat16()
+    k = torch.randn(1, 600, 2, 128, device="cuda", generator=g).bfloat16()
+    v = torch.randn(1, 600, 2, 128, device="cuda", generator=g).bfloat16()
+    drop = list(range(0, 256)) + [599]
+    out, _ = attention_fwd_ext(q, k, v, key_keep=keep_bits(600, drop, q.device))
+    torch.cuda.synchronize()
+    keep = [i for i in range(600) if i not in drop]
+    ref, _ = reference_attention(q, k[:, keep], v[:, keep])
+    assert rel_l2(out, ref) <= BF16_REL_L2
+
+
+def test_query_group_bias_matches_sdpa_with_additive_mask(lib):
+    """adapters/usp_query_bias.py:109-130: each query group attends the full
+    keys under its own additive bias (zero-extended past its keys): a key row
+    shared over heads, no bias, a per-head key row with -inf keys, and a
+    per-query-row bias (the LTX tracked-guide rectangle)."""
+    from dgx_monarch_b200.ops import attention_fwd_ext
+
+    g = torch.Generator(device="cuda").manual_seed(41)
+    rows, heads = 650, 2
+    q, k, v = (torch.randn(1, rows, heads, 128, device="cuda", generator=g).bfloat16() for _ in range(3))
+    b0 = torch.randn(1, 1, 1, 300, device="cuda", generator=g) * 2.0     # shared over heads, 300 keys
+    b2 = torch.randn(1, heads, 1, rows, device="cuda", generator=g)       # per head, all keys
+    b2[..., 10:20] = float("-inf")
+    b3 = torch.zeros(1, 1, 130, rows, device="cuda")                      # one weight per query row
+    b3[..., :400] = torch.log(torch.rand(1, 1, 130, 1, device="cuda", generator=g) + 0.05)
+    groups = [(0, 100, b0), (100, 260, None), (260, 520, b2), (520, rows, b3)]
+    out, _ = attention_fwd_ext(q, k, v, bias_groups=groups)
+    torch.cuda.synchronize()
+    qf, kf, vf = (t.float().transpose(1, 2) for t in (q, k, v))
+    for start, end, bias in groups:
+        logits = qf[:, :, start:end] @ kf.transpose(-1, -2) / math.sqrt(128)
+        if bias is not None:
+            full = torch.zeros(1, bias.shape[1], bias.shape[2], rows, device="cuda")
+            full[..., :bias.shape[3]] = bias
+            logits = logits + full
+        ref = (torch.softmax(logits, -1) @ vf).transpose(1, 2)
+        assert rel_l2(out[:, start:end], ref) <= BF16_REL_L2
+
+
+def test_row_with_only_excluded_keys_in_leading_blocks(lib):
+    """One query row whose first 384 keys are excluded by its bias, beside
+    rows that see every key: the row must attend the remaining keys (its
+    running maximum stays -inf while the warp's other rows rescale)."""
+    from dgx_monarch_b200.ops import attention_fwd_ext
+
+    g = torch.Generator(device="cuda").manual_seed(43)
+    rows = 600
+    q, k, v = (torch.randn(1, rows, 2, 128, device="cuda", generator=g).bfloat16() for _ in range(3))
+    rect = torch.zeros(1, 1, 64, rows, device="cuda")
+    rect[:, :, 5, :384] = torch.finfo(torch.float32).min
+    rect[:, :, 40, :] = float("-inf")  # a row that sees no key at all: zeros, as an empty softmax
+    out, _ = attention_fwd_ext(q, k, v, bias_groups=[(0, 64, rect)])
+    torch.cuda.synchronize()
+    qf, kf, vf = (t.float().transpose(1, 2) for t in (q, k, v))
+    logits = qf[:, :, :64] @ kf.transpose(-1, -2) / math.sqrt(128) + rect.clamp_min(-1e30)
+    ref = (torch.softmax(logits, -1) @ vf).transpose(1, 2)
+    keep = [i for i in range(64) if i != 40]
+    assert rel_l2(out[:, keep], ref[:, keep]) <= BF16_REL_L2
+    assert (out[:, 5].float() - ref[:, 5]).abs().max().item() <= BF16_MAX_ABS
+    assert torch.equal(out[:, 40], torch.zeros_like(out[:, 40]))
+    rest, _ = reference_attention(q[:, 64:], k, v)
+    assert rel_l2(out[:, 64:], rest) <= BF16_REL_L2

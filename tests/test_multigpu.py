@@ -24,8 +24,12 @@ def _free_port() -> int:
 
 
 def _worker(rank, world, port, case, q):
+    """One rank.  Whatever its case does, every rank ends at the same barrier
+    before reporting, so a failure on one rank never leaves another waiting
+    in a collective it alone entered."""
     import torch.distributed as dist
 
+    err = None
     try:
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
         torch.cuda.set_device(rank)
@@ -35,18 +39,47 @@ def _worker(rank, world, port, case, q):
         dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
                                 timeout=timedelta(seconds=60))
         case(rank, world, dev)
-        dist.barrier()
-        q.put((rank, None))
     except Exception:  # pragma: no cover - reported to the parent
-        q.put((rank, traceback.format_exc()))
-    finally:
-        import torch.distributed as dist
-
+        err = f"rank {rank}:\n{traceback.format_exc()}"
+    try:
         if dist.is_initialized():
-            dist.destroy_process_group()
+            torch.cuda.synchronize()
+            dist.barrier()
+    except Exception:  # pragma: no cover
+        err = (err or "") + f"rank {rank} final barrier:\n{traceback.format_exc()}"
+    q.put((rank, err))
+    q.close()
+    q.join_thread()
+    if dist.is_initialized():
+        dist.destroy_process_group()
 
 
-def _spawn(case, world):
+class Checks:
+    """Deferred assertions: a case records failures and raises them only after
+    its last collective step, so every rank takes the same steps."""
+
+    def __init__(self, rank):
+        self.rank, self.failed = rank, []
+
+    def __call__(self, ok, what):
+        if not ok:
+            self.failed.append(what)
+
+    def le(self, value, bound, what):
+        """Record `what` (with the measured value) unless value <= bound."""
+        value = float(value)
+        if not value <= bound:
+            self.failed.append(f"{what}: {value:.4g} > {bound:.4g}")
+
+    def close(self):
+        if self.failed:
+            raise AssertionError(f"rank {self.rank}: " + "; ".join(self.failed))
+
+
+def _spawn(case, world, limit_s=300):
+    import queue
+    import time
+
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
@@ -55,14 +88,30 @@ def _spawn(case, world):
     procs = [ctx.Process(target=_worker, args=(r, world, port, case, q)) for r in range(world)]
     for p in procs:
         p.start()
-    results = [q.get(timeout=300) for _ in procs]
+    results, deadline = {}, time.monotonic() + limit_s
+    while len(results) < world and time.monotonic() < deadline:
+        try:
+            rank, err = q.get(timeout=5)
+            results[rank] = err
+        except queue.Empty:
+            if all(not p.is_alive() for p in procs) and q.empty():
+                break
     for p in procs:
         p.join(timeout=60)
-    errors = [e for _, e in results if e]
+    for p in procs:  # only the children this call started
+        if p.is_alive():
+            p.terminate()
+            p.join(timeout=30)
+    missing = [r for r in range(world) if r not in results]
+    errors = [e for e in results.values() if e]
+    if missing:
+        errors.append(f"ranks {missing} reported nothing (exit codes "
+                      f"{[procs[r].exitcode for r in missing]})")
     assert not errors, "\n".join(errors)
 
 
 def _ulysses_case(rank, world, dev):
+    check = Checks(rank)
     from dgx_monarch_b200 import _lib
     from dgx_monarch_b200.ulysses import UlyssesAttention
     from tests.test_attn_gpu import BF16_MAX_ABS, BF16_REL_L2, reference_attention, rel_l2
@@ -79,10 +128,11 @@ def _ulysses_case(rank, world, dev):
     torch.cuda.synchronize()
     ref, _ = reference_attention(q, k, v)
     ref = ref[:, rank * ls:(rank + 1) * ls]
-    assert (out.float() - ref).abs().max().item() <= BF16_MAX_ABS
-    assert rel_l2(out, ref) <= BF16_REL_L2
-    assert _lib.device_error() == 0
+    check.le((out.float() - ref).abs().max().item(), BF16_MAX_ABS, "ulysses max abs")
+    check.le(rel_l2(out, ref), BF16_REL_L2, "ulysses rel l2")
+    check(_lib.device_error() == 0, f"device error word {_lib.device_error()}")
     uly.close()
+    check.close()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
@@ -91,6 +141,7 @@ def test_ulysses_across_gpus_matches_unsharded_attention():
 
 
 def _ring_case(rank, world, dev):
+    check = Checks(rank)
     from dgx_monarch_b200 import _lib
     from dgx_monarch_b200.ring import RingAttention
     from tests.test_attn_gpu import BF16_REL_L2, reference_attention, rel_l2
@@ -106,10 +157,11 @@ def _ring_case(rank, world, dev):
         out, _ = ring.forward(q[:, sl].contiguous(), k[:, sl].contiguous(), v[:, sl].contiguous(), lse=lse)
     torch.cuda.synchronize()
     ref, ref_lse = reference_attention(q, k, v)
-    assert rel_l2(out, ref[:, sl]) <= BF16_REL_L2
-    assert (lse - ref_lse[:, :, sl]).abs().max().item() <= 2e-3
-    assert _lib.device_error() == 0
+    check.le(rel_l2(out, ref[:, sl]), BF16_REL_L2, "ring rel l2")
+    check.le((lse - ref_lse[:, :, sl]).abs().max().item(), 2e-3, "ring lse")
+    check(_lib.device_error() == 0, f"device error word {_lib.device_error()}")
     ring.close()
+    check.close()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
@@ -120,6 +172,7 @@ def test_ring_across_gpus_matches_unsharded_attention():
 def _callable_case(rank, world, dev):
     """The drop-in usp_attention on a Ulysses group: plain, joint order with
     pad rows, and native GQA, against unsharded attention."""
+    check = Checks(rank)
     import torch.distributed as dist
 
     from dgx_monarch_b200 import _lib
@@ -137,7 +190,7 @@ def _callable_case(rank, world, dev):
     sl = slice(rank * ls, (rank + 1) * ls)
     out = attn(*(t[:, sl].reshape(1, ls, -1) for t in (q, k, v)), heads=heads)
     ref, _ = reference_attention(q, k, v)
-    assert rel_l2(out.reshape(1, ls, heads, d), ref[:, sl]) <= BF16_REL_L2
+    check.le(rel_l2(out.reshape(1, ls, heads, d), ref[:, sl]), BF16_REL_L2, "plain rel l2")
     # 2) joint [text, image] order with one image pad row on the last rank
     text, image = 32, 96
     ls2 = text + image
@@ -158,10 +211,10 @@ def _callable_case(rank, world, dev):
     want_img = img_rows[:, rank * image:(rank + 1) * image]
     got_img = out2[:, text:]
     if rank == world - 1:
-        assert torch.equal(got_img[:, -1], torch.zeros_like(got_img[:, -1]))
+        check(torch.equal(got_img[:, -1], torch.zeros_like(got_img[:, -1])), "joint pad row not zero")
         got_img = got_img[:, :-1]
-    assert (out2[:, :text].float() - want_txt).abs().max().item() <= BF16_MAX_ABS
-    assert (got_img.float() - want_img).abs().max().item() <= BF16_MAX_ABS
+    check.le((out2[:, :text].float() - want_txt).abs().max().item(), BF16_MAX_ABS, "joint text max abs")
+    check.le((got_img.float() - want_img).abs().max().item(), BF16_MAX_ABS, "joint image max abs")
     # 3) native GQA: K/V heads split by the Ulysses degree
     hkv = world
     qg = torch.randn(1, ls * world, heads, d, device=dev, generator=g).bfloat16()
@@ -169,10 +222,26 @@ def _callable_case(rank, world, dev):
     out3 = attn(qg[:, sl].reshape(1, ls, -1), kg[:, sl].reshape(1, ls, -1), vg[:, sl].reshape(1, ls, -1),
                 heads=heads, enable_gqa=True)
     ref3, _ = reference_attention(qg, kg, vg)
-    assert rel_l2(out3.reshape(1, ls, heads, d), ref3[:, sl]) <= BF16_REL_L2
+    check.le(rel_l2(out3.reshape(1, ls, heads, d), ref3[:, sl]), BF16_REL_L2, "gqa rel l2")
+    # 4) LTX guide biases plus a per-head key bias on a stream with tail pads:
+    #    the kernel applies the groups on the gathered axis and routes rows home
+    from tests.test_usp_callable_gpu import ltx_guide_groups, oracle_grouped
+
+    real = ls * world - 9
+    qb, kb, vb = (torch.randn(1, ls * world, heads, d, device=dev, generator=g).bfloat16() for _ in range(3))
+    weights = torch.rand(100, device=dev, generator=g) + 0.05
+    weights[3] = 0.0
+    groups = ltx_guide_groups(real, real - 180, weights)
+    groups[-1] = (groups[-1][0], groups[-1][1], torch.randn(1, heads, 1, real, device=dev, generator=g))
+    drop = list(range(real, ls * world))
+    out4 = attn(*(t[:, sl].transpose(1, 2) for t in (qb, kb, vb)), heads=heads, skip_reshape=True,
+                skip_output_reshape=True, drop_rows=drop, query_bias_groups=groups).transpose(1, 2)
+    want4 = oracle_grouped(qb, kb, vb, drop, groups)[:, sl]
+    check.le((out4.double() - want4).abs().max().item(), BF16_MAX_ABS, "bias groups max abs")
     torch.cuda.synchronize()
-    assert _lib.device_error() == 0
+    check(_lib.device_error() == 0, f"device error word {_lib.device_error()}")
     attn.impl.invalidate()
+    check.close()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
@@ -184,6 +253,7 @@ def _cfg_fp8_case(rank, world, dev):
     """CFG split across GPUs with FP8 attention (the C3 shape family, small):
     batch 2 (cond, uncond) -> one row per cfg rank -> e4m3 attention ->
     peer-store all-gather of the predictions, in rank order."""
+    check = Checks(rank)
     import torch.distributed as dist
 
     from dgx_monarch_b200 import _lib
@@ -205,12 +275,13 @@ def _cfg_fp8_case(rank, world, dev):
     full = cfg_parallel_call(forward, x, group=cfg_group, gather=gather).reshape(batch, l, heads, 128)
     torch.cuda.synchronize()
     ref, _ = reference_attention(x[:, :, 0], x[:, :, 1], x[:, :, 2])
-    assert full.shape == (batch, l, heads, 128)
+    check(full.shape == (batch, l, heads, 128), f"gathered shape {tuple(full.shape)}")
     for bi in range(batch):
-        assert rel_l2(full[bi], ref[bi]) <= 8e-2  # e4m3 inputs vs bf16 activations
-    assert _lib.device_error() == 0
+        check.le(rel_l2(full[bi], ref[bi]), 8e-2, f"cfg row {bi} rel l2")
+    check(_lib.device_error() == 0, f"device error word {_lib.device_error()}")
     gather.close()
     attn.impl.invalidate()
+    check.close()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")

@@ -176,3 +176,37 @@ def test_hybrid_groups_are_ulysses_low():
     uly, ring = usp.hybrid_groups(8, 2, 4)
     assert uly == [[0, 1], [2, 3], [4, 5], [6, 7]]
     assert ring == [[0, 2, 4, 6], [1, 3, 5, 7]]
+
+
+def _bias_groups(case):
+    return [(start, end, None if name is None else ARR[name]) for start, end, name in case["groups"]]
+
+
+@pytest.mark.parametrize("case", SPEC["query_bias"], ids=lambda c: c["name"])
+def test_query_bias_groups_match_reference(case):
+    """Query-group biases through the reference's callable
+    (adapters/usp_query_bias.py:109-130, with pads adapters/usp_pad_exclusion.py:152-177)."""
+    name = case["name"]
+    q, k, v = (ARR[f"bias_{name}_{x}"] for x in "qkv")
+    drop = case["drop"]
+    out = usp.attend_groups_without_pads(q, k, v, drop, drop, _bias_groups(case))
+    np.testing.assert_allclose(out, ARR[f"bias_{name}_out"], atol=1e-12, rtol=0)
+
+
+@pytest.mark.parametrize("groups,reason", [
+    (((0, 4, None), (6, 10, None)), "gap"),
+    (((0, 6, None), (4, 10, None)), "overlap"),
+    (((0, 6, None),), "short"),
+    (((0, 12, None),), "past the end"),
+    (((0, 10, np.zeros((1, 1, 3, 10))),), "rows"),
+    (((0, 10, np.zeros((1, 1, 1, 40))),), "keys"),
+])
+def test_malformed_bias_groups_refuse(groups, reason):
+    with pytest.raises(usp.OracleRefusal):
+        usp.validate_query_bias_groups(groups, 10, 10)
+
+
+def test_bias_pads_must_be_a_tail():
+    usp.assert_pads_are_a_tail([12, 13], 14)
+    with pytest.raises(usp.OracleRefusal, match="away from the tail"):
+        usp.assert_pads_are_a_tail([3, 13], 14)

@@ -76,8 +76,10 @@ def test_typed_refusals(attn):
         attn(q2, q2, q2, heads=2, mask=mask)
     # A no-op mask is dropped exactly, as in the reference.
     attn(q2, q2, q2, heads=2, mask=torch.zeros(1, 1, 64, 64, device="cuda"))
-    with pytest.raises(UnsupportedModelError, match="query-group"):
-        attn(q2, q2, q2, heads=2, query_bias_groups=[(0, 2)])
+    with pytest.raises(UnsupportedModelError, match="cover 10 of 64"):
+        attn(q2, q2, q2, heads=2, query_bias_groups=[(0, 10, None)])
+    with pytest.raises(UnsupportedModelError, match="does not broadcast"):
+        attn(q2, q2, q2, heads=2, query_bias_groups=[(0, 64, torch.zeros(1, 1, 3, 64, device="cuda"))])
     with pytest.raises(UnsupportedModelError, match="carries 64 rows"):
         attn(*(t.transpose(1, 2) for t in (q, q, q)), heads=2, skip_reshape=True, drop_rows=[64])
 
@@ -89,3 +91,79 @@ def test_invalidate_retires_the_implementation(attn):
     attn.impl.invalidate()
     with pytest.raises(UnsupportedModelError, match="retired"):
         attn(q, q, q, heads=2)
+
+
+def ltx_guide_groups(tokens, guide_start, weights):
+    """The LTX guide layout (tests/test_usp_query_bias.py:51-86 of the
+    reference): log weights as a key row for the noisy queries and as one
+    weight per tracked query row over the noisy keys; finfo.min at weight 0."""
+    finfo = torch.finfo(weights.dtype)
+    log_w = torch.full_like(weights, finfo.min)
+    log_w[weights > 0] = torch.log(weights[weights > 0])
+    tracked = weights.shape[0]
+    noisy = torch.zeros((1, 1, 1, tokens), dtype=weights.dtype, device=weights.device)
+    noisy[..., guide_start:guide_start + tracked] = log_w.view(1, 1, 1, -1)
+    rect = torch.zeros((1, 1, tracked, tokens), dtype=weights.dtype, device=weights.device)
+    rect[..., :guide_start] = log_w.view(1, 1, -1, 1)
+    groups = [(0, guide_start, noisy), (guide_start, guide_start + tracked, rect)]
+    if guide_start + tracked < tokens:
+        groups.append((guide_start + tracked, tokens, None))
+    return groups
+
+
+def oracle_grouped(q, k, v, drop, groups):
+    """The oracle's grouped attention with pad exclusion, float64, as a tensor."""
+    from oracle import usp as oracle_usp
+
+    host = [t.double().cpu().numpy() for t in (q, k, v)]
+    g64 = [(s, e, None if b is None else b.double().cpu().numpy()) for s, e, b in groups]
+    out = oracle_usp.attend_groups_without_pads(*host, drop, drop, g64)
+    return torch.from_numpy(out).to(q.device)
+
+
+def test_query_bias_groups_ltx_guides_and_tail_pads(attn):
+    """LTX guide rectangles (per-token weights, one of them 0) on a stream
+    with tail pads, against the oracle of adapters/usp_query_bias.py."""
+    real, pad, heads = 700, 20, 4
+    q, k, v = _qkv(1, real + pad, heads, heads, 8)
+    g = torch.Generator(device="cuda").manual_seed(9)
+    weights = torch.rand(150, device="cuda", generator=g) + 0.1
+    weights[7] = 0.0
+    weights[8] = 1.0
+    groups = ltx_guide_groups(real, 520, weights)
+    drop = list(range(real, real + pad))
+    out = attn(*(t.transpose(1, 2) for t in (q, k, v)), heads=heads, skip_reshape=True,
+               skip_output_reshape=True, drop_rows=drop, query_bias_groups=groups).transpose(1, 2)
+    want = oracle_grouped(q, k, v, drop, groups)
+    assert (out[:, :real].double() - want[:, :real]).abs().max().item() <= BF16_MAX_ABS
+    assert rel_l2(out[:, :real], want[:, :real].float()) <= BF16_REL_L2
+    assert torch.equal(out[:, real:], torch.zeros_like(out[:, real:]))
+
+
+def test_query_bias_lens_key_row_and_per_head_bias(attn):
+    """One group carrying a key bias narrower than the key axis (the Lens
+    joint-attention form), and a per-head key bias in a later group."""
+    rows, heads = 400, 2
+    q, k, v = _qkv(1, rows, heads, heads, 10)
+    g = torch.Generator(device="cuda").manual_seed(12)
+    lens = [(0, rows, torch.randn(1, 1, 1, 330, device="cuda", generator=g))]
+    out = attn(*(t.reshape(1, rows, -1) for t in (q, k, v)), heads=heads,
+               query_bias_groups=lens).reshape(1, rows, heads, 128)
+    assert rel_l2(out, oracle_grouped(q, k, v, None, lens).float()) <= BF16_REL_L2
+    per_head = [(0, 150, None), (150, rows, torch.randn(1, heads, 1, rows, device="cuda", generator=g))]
+    out = attn(*(t.reshape(1, rows, -1) for t in (q, k, v)), heads=heads,
+               query_bias_groups=per_head).reshape(1, rows, heads, 128)
+    assert rel_l2(out, oracle_grouped(q, k, v, None, per_head).float()) <= BF16_REL_L2
+
+
+def test_query_bias_refusals(attn):
+    from dgx_monarch_b200.usp import UnsupportedModelError
+
+    q, k, v = _qkv(1, 64, 2, 2, 14)
+    qs = [t.transpose(1, 2) for t in (q, k, v)]
+    groups = [(0, 60, torch.zeros(1, 1, 1, 60, device="cuda"))]
+    with pytest.raises(UnsupportedModelError, match="away from the tail"):
+        attn(*qs, heads=2, skip_reshape=True, drop_rows=[3, 63, 62, 61], query_bias_groups=groups)
+    many = [(i, i + 1, torch.zeros(1, 1, 1, 64, device="cuda")) for i in range(64)]
+    with pytest.raises(UnsupportedModelError, match="at most"):
+        attn(*qs, heads=2, skip_reshape=True, query_bias_groups=many)

@@ -18,7 +18,7 @@ import ctypes
 import pytest
 import torch
 
-from tests.test_multigpu import _spawn
+from tests.test_multigpu import Checks, _spawn
 
 pytestmark = pytest.mark.gpu
 
@@ -29,6 +29,7 @@ def _noalloc_case(rank, world, dev):
     from dgx_monarch_b200.ring import RingAttention
     from tests.test_attn_gpu import BF16_MAX_ABS, BF16_REL_L2, LSE_ABS, reference_attention, rel_l2
 
+    check = Checks(rank)
     lib = _lib.load()
     rows, heads = 384, 4
     g = torch.Generator(device=dev).manual_seed(101)
@@ -48,23 +49,24 @@ def _noalloc_case(rank, world, dev):
         rc = lib.dgxm_ring_attn_fwd_noalloc(ring.windows._handle, ctypes.byref(desc), ql.data_ptr(),
                                             kl.data_ptr(), vl.data_ptr(), got.data_ptr(),
                                             got_lse.data_ptr(), stream)
-        _lib.check(rc, "dgxm_ring_attn_fwd_noalloc")
+        check(rc == 0, f"dgxm_ring_attn_fwd_noalloc returned {rc}")
         torch.cuda.synchronize(dev)
-        assert (got.float() - want.float()).abs().max().item() <= BF16_MAX_ABS
-        assert rel_l2(got, want) <= BF16_REL_L2
-        assert (got_lse - want_lse).abs().max().item() <= LSE_ABS
+        check.le((got.float() - want.float()).abs().max().item(), BF16_MAX_ABS, "max abs vs workspace entry")
+        check.le(rel_l2(got, want), BF16_REL_L2, "rel l2 vs workspace entry")
+        check.le((got_lse - want_lse).abs().max().item(), LSE_ABS, "lse vs workspace entry")
     ref, _ = reference_attention(q, k, v)
-    assert rel_l2(got, ref[:, sl]) <= BF16_REL_L2
+    check.le(rel_l2(got, ref[:, sl]), BF16_REL_L2, "rel l2 vs unsharded attention")
     # A shape whose partial results exceed the static array is refused, not truncated.
     big_q = torch.empty(1, 1 << 20, heads, 128, device="meta", dtype=torch.bfloat16)
     desc = attn_desc(big_q, kl, vl, big_q, None)
     rc = lib.dgxm_ring_attn_fwd_noalloc(ring.windows._handle, ctypes.byref(desc), None, None, None,
                                         None, None, stream)
-    assert rc == _lib.DGXM_ERR_INVALID
-    assert b"32 MiB" in lib.dgxm_last_error_message()
-    assert lib.dgxm_ring_noalloc_max_bytes() == 32 << 20
-    assert _lib.device_error() == 0
+    check(rc == _lib.DGXM_ERR_INVALID, f"oversized shape returned {rc}")
+    check(b"32 MiB" in lib.dgxm_last_error_message(), "refusal names the 32 MiB limit")
+    check(lib.dgxm_ring_noalloc_max_bytes() == 32 << 20, "static array size")
+    check(_lib.device_error() == 0, f"device error word {_lib.device_error()}")
     ring.close()
+    check.close()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="ring attention needs two or more GPUs")
