@@ -303,6 +303,39 @@ def run_ring(world: int, rank: int, dev, steps: int, warmup: int) -> dict:
     return {"ms": ms, "layout": f"ulysses{uly}xring{ring}"}
 
 
+def run_full_context(world: int, rank: int, dev, steps: int, warmup: int) -> dict:
+    """The Wan Ring2 full-context path on the C4 layer: ranks in pairs, each
+    pair a pure ring of degree 2 gathering K/V over NVLink and attending
+    local Q against the full 75,600-key axis in one call."""
+    import torch
+    import torch.distributed as dist
+
+    from dgx_monarch_b200.usp import make_b200_usp_attention
+
+    mine = None
+    for first in range(0, world - world % 2, 2):
+        g = dist.new_group([first, first + 1])
+        if rank in (first, first + 1):
+            mine = g
+    attn = make_b200_usp_attention(ring_group=mine, generation=33, device=dev, full_context_ring=True)
+    ls = SEQ // 2
+    g = torch.Generator(device=dev).manual_seed(700 + rank)
+    q, k, v = (torch.randn(1, ls, HEADS * DIM, device=dev, generator=g, dtype=torch.bfloat16)
+               for _ in range(3))
+    for _ in range(warmup):
+        attn(q, k, v, heads=HEADS)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        attn(q, k, v, heads=HEADS)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    attn.impl.invalidate()
+    return {"ms": ms, "pairs": world // 2}
+
+
 def run_cfg_fp8(world: int, rank: int, dev, steps: int, warmup: int) -> dict:
     import torch
 
@@ -473,13 +506,14 @@ def main() -> None:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_ms = te.item()
     dit = run_dit_layer(world, rank, dev, max(5, args.steps), args.warmup)
-    extra = [dit["ms"], 0.0, 0.0, 0.0, 0.0]
-    a2a = ring_res = cfg_res = None
+    extra = [dit["ms"], 0.0, 0.0, 0.0, 0.0, 0.0]
+    a2a = ring_res = cfg_res = fc_res = None
     if world > 1:
         a2a = time_scatter(uly)
         ring_res = run_ring(world, rank, dev, 2, 1)
         cfg_res = run_cfg_fp8(world, rank, dev, 5, 3)
-        extra[1:] = [a2a["ms"], ring_res["ms"], cfg_res["ms"], a2a["gbs_per_direction"]]
+        fc_res = run_full_context(world, rank, dev, 3, 3)
+        extra[1:] = [a2a["ms"], ring_res["ms"], cfg_res["ms"], a2a["gbs_per_direction"], fc_res["ms"]]
     td = torch.tensor(extra, device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(td, op=dist.ReduceOp.MAX)
@@ -487,7 +521,7 @@ def main() -> None:
         tmin = torch.tensor([extra[4]], device=dev, dtype=torch.float64)
         dist.all_reduce(tmin, op=dist.ReduceOp.MIN)
         td[4] = tmin[0]
-    dit_ms, a2a_ms, ring_ms, cfg_ms, a2a_gbs = td.tolist()
+    dit_ms, a2a_ms, ring_ms, cfg_ms, a2a_gbs, fc_ms = td.tolist()
     dev_err = _lib.device_error()
 
     if rank == 0:
@@ -545,6 +579,12 @@ def main() -> None:
             cflops = attn_flops(CFG["batch"], CFG["heads"], CFG["img"] + CFG["txt"], DIM)
             line["cfg_fp8"] = {"workload": CFG_WORKLOAD, "layout": cfg_res["layout"], "ms_per_step": cfg_ms,
                                "tflops": cflops / (cfg_ms * 1e-3) / 1e12}
+            line["wan_ring2_full_context"] = {
+                "workload": WORKLOAD + "; pure ring-2 full context: K/V gathered over NVLink, "
+                            "local Q x full K/V in one call",
+                "layout": f"{fc_res['pairs']} independent ring2 pairs", "ms_per_layer": fc_ms,
+                "tflops_per_pair": flops / (fc_ms * 1e-3) / 1e12,
+                "tflops_total": fc_res["pairs"] * flops / (fc_ms * 1e-3) / 1e12}
         if world == 1 and not args.no_cpu_baseline:
             from oracle.cpu_baseline import time_sdpa_sample
 

@@ -162,6 +162,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "dgxm_ring_noalloc_max_bytes": (ctypes.c_int64, []),
     "dgxm_ring_attn_fwd_noalloc": (ctypes.c_int, [_P, ctypes.POINTER(AttnDesc), _P, _P, _P, _P, _P,
                                                   _P]),
+    "dgxm_full_context_window_bytes": (ctypes.c_int64, [ctypes.POINTER(AttnDesc), _I32]),
+    "dgxm_full_context_attn_fwd": (ctypes.c_int, [_P, ctypes.POINTER(AttnDesc), _P, _P, _P, _P, _P,
+                                                  _P]),
 }
 
 _lock = threading.Lock()

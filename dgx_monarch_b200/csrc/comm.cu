@@ -23,6 +23,7 @@ struct dgxm_comm {
   char* peers[DGXM_MAX_WORLD];  // window bases as seen by this process
   bool opened[DGXM_MAX_WORLD];
   uint32_t epoch;      // barriers issued so far
+  uint32_t fc_calls;   // full-context calls so far (their window buffer alternates)
   long long wait_cycles;  // barrier wait budget in SM clock cycles
   cudaStream_t side;      // ring: copy-engine stream (created on first use)
   cudaEvent_t ev_main, ev_side;

@@ -11,4 +11,5 @@
 #include "lse_merge.cu"
 #include "comm.cu"
 #include "ring.cu"
+#include "full_context.cu"
 #include "prologue.cu"

@@ -64,3 +64,54 @@ class RingAttention:
             torch.cuda.synchronize(self.device)
             self.windows.close()
             self.windows = None
+
+
+class FullContextRingAttention:
+    """Local Q against the whole K/V axis of a ring group, in one kernel call
+    (libdgxm_sp.so: dgxm_full_context_attn_fwd).
+
+    The Wan Ring2 full-context path of the reference
+    (adapters/wan_ring_full_context.py:203-295, :422-449): each rank's K/V
+    block lands in rank-major slots of every rank's peer window (NVLink peer
+    stores, all batch items at once), then one attention call of the local
+    query rows over the gathered axis -- exact, with no LSE merge.
+    """
+
+    def __init__(self, *, world: int, rank: int, batch: int, q_len: int, kv_len: int, heads: int,
+                 kv_heads: int, head_dim: int, device: torch.device, group=None,
+                 generation: int = 0, timeout_ms: int | None = None) -> None:
+        self.world, self.rank, self.device = world, rank, device
+        self.shape = (batch, q_len, kv_len, heads, kv_heads, head_dim)
+        probe_q = torch.empty(batch, q_len, heads, head_dim, device="meta", dtype=torch.bfloat16)
+        probe_k = torch.empty(batch, kv_len, kv_heads, head_dim, device="meta", dtype=torch.bfloat16)
+        desc = attn_desc(probe_q, probe_k, probe_k, probe_q, None)
+        lib = _lib.load()
+        self.window_bytes = int(lib.dgxm_full_context_window_bytes(ctypes.byref(desc), world))
+        self.windows = PeerWindows(self.window_bytes, device=device, group=group, rank=rank,
+                                   world=world, generation=generation)
+        if timeout_ms is not None:
+            _lib.check(lib.dgxm_comm_set_timeout(self.windows._handle, int(timeout_ms)),
+                       "dgxm_comm_set_timeout")
+        self.launches_per_step = 3  # gather, barrier, attention
+
+    def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
+                out: torch.Tensor | None = None, lse: torch.Tensor | None = None,
+                softmax_scale: float | None = None) -> tuple[torch.Tensor, torch.Tensor | None]:
+        b, lq, h, d = q.shape
+        if (b, lq, k.shape[1], h, k.shape[2], d) != self.shape or v.shape != k.shape:
+            raise ValueError(f"full-context ring planned for {self.shape}, called with "
+                             f"q {tuple(q.shape)} k {tuple(k.shape)} v {tuple(v.shape)}")
+        if out is None:
+            out = torch.empty(b, lq, h, d, device=self.device, dtype=q.dtype)
+        desc = attn_desc(q, k, v, out, lse, softmax_scale)
+        stream = torch.cuda.current_stream(self.device)
+        _lib.check(_lib.load().dgxm_full_context_attn_fwd(
+            self.windows._handle, ctypes.byref(desc), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+            out.data_ptr(), _ptr(lse), stream.cuda_stream), "dgxm_full_context_attn_fwd")
+        return out, lse
+
+    def close(self) -> None:
+        if self.windows is not None:
+            torch.cuda.synchronize(self.device)
+            self.windows.close()
+            self.windows = None

@@ -16,7 +16,10 @@ the reference's `_AttentionDispatch.configure` (actor/attention_dispatch.py:
 - query-group biases (adapters/usp_query_bias.py:109-130), key rows or
   per-query rectangles, added to the scaled logits inside the kernel;
 - Ulysses x ring: Ulysses scatter inside the Ulysses group, ring attention
-  over the ring group, inverse all-to-all kernel.
+  over the ring group, inverse all-to-all kernel;
+- pure ring with full_context_ring=True: the Wan Ring2 full-context strategy
+  (adapters/wan_ring_full_context.py:298-449), K/V gathered into rank-major
+  slots over NVLink and one local-Q x full-KV attention call, no merge.
 
 Per-shape plans (peer windows, workspaces) are built on first use.  Every
 rank issues the same calls in the same order, as the reference's
@@ -30,7 +33,7 @@ import torch
 from ._lib import MAX_BIAS_GROUPS
 from .comm import PeerWindows
 from .ops import attention_fwd, attention_fwd_ext, keep_bits
-from .ring import RingAttention
+from .ring import FullContextRingAttention, RingAttention
 from .ulysses import attention_routed, ulysses_gather, ulysses_scatter
 
 
@@ -75,9 +78,11 @@ class B200SequenceParallelAttention:
     """Setup-generation-bound implementation behind the callable."""
 
     def __init__(self, *, ulysses_group=None, ring_group=None, generation: int = 1,
-                 device: torch.device | None = None, fp8: bool = False) -> None:
+                 device: torch.device | None = None, fp8: bool = False,
+                 full_context_ring: bool = False) -> None:
         self.groups = _Groups(ulysses_group, ring_group)
         self.fp8 = fp8
+        self.full_context_ring = full_context_ring
         self.generation = generation
         self.device = device or torch.device("cuda", torch.cuda.current_device())
         self._plans: dict = {}
@@ -124,9 +129,15 @@ class B200SequenceParallelAttention:
         plan = self._plans.get(key)
         if plan is None:
             g = self.groups
-            plan = RingAttention(world=g.ring_world, rank=g.ring_rank, batch=b, q_len=lq, kv_len=lk,
-                                 heads=h, kv_heads=hkv, head_dim=d, device=self.device,
-                                 group=g.ring_group, generation=self.generation, dtype=dtype)
+            if self.full_context_ring and g.uly_world == 1 and dtype == torch.bfloat16:
+                plan = FullContextRingAttention(world=g.ring_world, rank=g.ring_rank, batch=b, q_len=lq,
+                                                kv_len=lk, heads=h, kv_heads=hkv, head_dim=d,
+                                                device=self.device, group=g.ring_group,
+                                                generation=self.generation)
+            else:
+                plan = RingAttention(world=g.ring_world, rank=g.ring_rank, batch=b, q_len=lq, kv_len=lk,
+                                     heads=h, kv_heads=hkv, head_dim=d, device=self.device,
+                                     group=g.ring_group, generation=self.generation, dtype=dtype)
             self._plans[key] = plan
         return plan
 
@@ -338,13 +349,17 @@ def _joint_inverse(text: int, image: int, world: int) -> list[int]:
 
 
 def make_b200_usp_attention(*, ulysses_group=None, ring_group=None, generation: int = 1,
-                            device: torch.device | None = None, fp8: bool = False):
+                            device: torch.device | None = None, fp8: bool = False,
+                            full_context_ring: bool = False):
     """A callable with the reference's usp_attention contract
     (adapters/base.py:216-326) on the B200 kernels.  fp8=True quantises the
     gathered heads to e4m3 with per-head absmax scales and runs the FP8
-    tensor-core path (output bf16)."""
+    tensor-core path (output bf16).  full_context_ring=True runs pure ring
+    topologies as the Wan Ring2 full-context path (one attention call over
+    the gathered K/V) instead of the rotating ring with an LSE merge."""
     impl = B200SequenceParallelAttention(ulysses_group=ulysses_group, ring_group=ring_group,
-                                         generation=generation, device=device, fp8=fp8)
+                                         generation=generation, device=device, fp8=fp8,
+                                         full_context_ring=full_context_ring)
 
     def usp_attention(q, k, v, heads, mask=None, attn_precision=None,
                       skip_reshape=False, skip_output_reshape=False,

@@ -358,6 +358,23 @@ int64_t dgxm_ring_noalloc_max_bytes(void);
 int dgxm_ring_attn_fwd_noalloc(dgxm_comm* comm, const dgxm_attn_desc* desc, const void* q,
                                const void* k, const void* v, void* o, float* lse, void* stream);
 
+/* ------------------------------------------------------------ full-context ring */
+/*
+ * The Wan Ring2 full-context path (adapters/wan_ring_full_context.py:203-295
+ * gather, :422-449 local-Q x full-KV flash call): each rank's K/V block
+ * (B, L, H_kv, D) is stored over NVLink into rank-major slots
+ * [rank*L, (rank+1)*L) of every rank's window, then this rank's Q attends the
+ * whole (B, R*L) key axis in one call -- exact, no LSE merge.  desc describes
+ * the LOCAL shapes (kv_len = L); o and lse are this rank's (B, Lq, H, D) and
+ * (B, H, Lq).  bf16 inputs; any ring degree R = comm world <= 8.  The window
+ * must hold dgxm_full_context_window_bytes(desc, R) (two alternating buffers,
+ * so one barrier per call suffices).  Collective: every rank of the comm
+ * calls it in the same order with the same shapes.
+ */
+int64_t dgxm_full_context_window_bytes(const dgxm_attn_desc* desc, int32_t world);
+int dgxm_full_context_attn_fwd(dgxm_comm* comm, const dgxm_attn_desc* desc, const void* q,
+                               const void* k, const void* v, void* o, float* lse, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -312,6 +312,19 @@ def ring_attention(q_local: list[np.ndarray], k_local: list[np.ndarray], v_local
     return results
 
 
+def full_context_gather(blocks: list[np.ndarray]) -> np.ndarray:
+    """Every rank's (B, L, H, D) block in rank-major slots [r*L, (r+1)*L) of the
+    gathered axis (adapters/wan_ring_full_context.py:238-251)."""
+    return np.concatenate(blocks, axis=1)
+
+
+def full_context_ring_attention(q_local, k_local, v_local, scale=None):
+    """Local Q of each rank against the gathered K/V in one softmax, no merge
+    (adapters/wan_ring_full_context.py:422-449)."""
+    k_full, v_full = full_context_gather(k_local), full_context_gather(v_local)
+    return [attention_lse(q, k_full, v_full, scale) for q in q_local]
+
+
 def ulysses_attention(q_local, k_local, v_local, scale=None):
     """Pure Ulysses: head scatter, full-axis attention, inverse all-to-all
     (adapters/usp_full_axis.py:27-40 at ring world 1)."""

@@ -74,6 +74,56 @@ def _attend64(q, k, v):
     return (torch.softmax(scores, dim=-1) @ vh).transpose(1, 2).to(q.dtype)
 
 
+def _full_context_rank(rank, port, k, v, out_q):
+    """One gloo rank running the reference's Ring2 K/V gather
+    (adapters/wan_ring_full_context.py:203-295)."""
+    import os
+
+    import torch.distributed as dist
+
+    sys.path.insert(0, str(REF_SRC))
+    _install_stubs()
+    from dgx_monarch.adapters.wan_ring_full_context import _materialize_full_kv_batch
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=2)
+    full_k, full_v = _materialize_full_kv_batch(k[rank], v[rank], group=None, world=2, rank=rank,
+                                                global_ranks=(0, 1))
+    out_q.put((rank, full_k.numpy(), full_v.numpy()))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _full_context_golden(rng, arrays) -> list:
+    """Run the reference's full-context gather on a world-2 gloo group."""
+    import socket
+
+    import torch.multiprocessing as mp
+
+    cases = []
+    for n, (length, heads, dim) in enumerate(((5, 2, 4), (3, 1, 8))):
+        k = [torch.from_numpy(rng.standard_normal((1, length, heads, dim))) for _ in range(2)]
+        v = [torch.from_numpy(rng.standard_normal((1, length, heads, dim))) for _ in range(2)]
+        with socket.socket() as sock:
+            sock.bind(("127.0.0.1", 0))
+            port = sock.getsockname()[1]
+        ctx = mp.get_context("spawn")
+        out_q = ctx.Queue()
+        procs = [ctx.Process(target=_full_context_rank, args=(r, port, k, v, out_q)) for r in range(2)]
+        for proc in procs:
+            proc.start()
+        got = dict((r, (fk, fv)) for r, fk, fv in (out_q.get(timeout=120) for _ in range(2)))
+        for proc in procs:
+            proc.join(timeout=60)
+        for r in range(2):
+            arrays[f"fullctx_{n}_k{r}"] = k[r].numpy()
+            arrays[f"fullctx_{n}_v{r}"] = v[r].numpy()
+            arrays[f"fullctx_{n}_fullk{r}"] = got[r][0]
+            arrays[f"fullctx_{n}_fullv{r}"] = got[r][1]
+        cases.append({"index": n, "length": length, "heads": heads, "dim": dim})
+    return cases
+
+
 def main() -> None:
     sys.path.insert(0, str(REF_SRC))
     _install_stubs()
@@ -281,6 +331,10 @@ def main() -> None:
             spec.append([start, end, None if bias is None else f"bias_{name}_g{g}"])
         biased.append({"name": name, "tokens": tokens, "heads": hds, "groups": spec, "drop": drop})
     golden["query_bias"] = biased
+
+    # j) the Wan Ring2 full-context K/V gather on a world-2 gloo group: the
+    #    rank-major slots every rank's local-Q x full-KV call reads.
+    golden["full_context"] = _full_context_golden(rng, arrays)
 
     (OUT / "golden.json").write_text(json.dumps(golden, indent=1))
     np.savez_compressed(OUT / "golden_arrays.npz", **arrays)

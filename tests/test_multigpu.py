@@ -287,3 +287,72 @@ def _cfg_fp8_case(rank, world, dev):
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
 def test_cfg_split_fp8_across_gpus():
     _spawn(_cfg_fp8_case, 2)
+
+
+def _full_context_case(rank, world, dev):
+    """The Wan Ring2 full-context path (adapters/wan_ring_full_context.py):
+    the class at any ring degree, then the reference-signature function and
+    the drop-in's full_context_ring option at ring degree 2."""
+    import torch.distributed as dist
+
+    from dgx_monarch_b200 import _lib
+    from dgx_monarch_b200.ring import FullContextRingAttention
+    from dgx_monarch_b200.usp import UnsupportedModelError, make_b200_usp_attention
+    from tests.test_attn_gpu import BF16_MAX_ABS, BF16_REL_L2, LSE_ABS, reference_attention, rel_l2
+
+    check = Checks(rank)
+    rows, heads = 300, 3
+    g = torch.Generator(device=dev).manual_seed(61)
+    q, k, v = (torch.randn(2, rows * world, heads, 128, device=dev, generator=g).bfloat16() for _ in range(3))
+    sl = slice(rank * rows, (rank + 1) * rows)
+    ref, ref_lse = reference_attention(q, k, v)
+    fc = FullContextRingAttention(world=world, rank=rank, batch=2, q_len=rows, kv_len=rows, heads=heads,
+                                  kv_heads=heads, head_dim=128, device=dev, generation=8)
+    lse = torch.empty(2, heads, rows, device=dev, dtype=torch.float32)
+    for step in range(3):  # alternating window buffers
+        ql, kl, vl = (t[:, sl].contiguous() for t in (q, k, v))
+        if step == 2:  # strided views of a packed layout are gathered as well
+            packed = torch.stack((q[:, sl], k[:, sl], v[:, sl]), dim=2)
+            ql, kl, vl = packed[:, :, 0], packed[:, :, 1], packed[:, :, 2]
+        out, _ = fc.forward(ql, kl, vl, lse=lse)
+        torch.cuda.synchronize()
+        check.le((out.float() - ref[:, sl]).abs().max().item(), BF16_MAX_ABS, f"class step {step} max abs")
+        check.le(rel_l2(out, ref[:, sl]), BF16_REL_L2, f"class step {step} rel l2")
+        check.le((lse - ref_lse[:, :, sl]).abs().max().item(), LSE_ABS, f"class step {step} lse")
+    fc.close()
+    if world == 2:
+        from dgx_monarch_b200.full_context import make_full_context_ring_attention
+
+        group = dist.new_group([0, 1])
+        fn = make_full_context_ring_attention(ring_group=group, generation=9, device=dev)
+        ql, kl, vl = (t[:, sl].contiguous() for t in (q, k, v))
+        refused = 0
+        for kwargs in ({"causal": True}, {"dropout_p": 0.1}, {"window_size": (4, 4)},
+                       {"softmax_scale": 0.5}, {"q_descale": torch.ones(1)}):
+            try:
+                fn(ql, kl, vl, **kwargs)
+            except UnsupportedModelError:
+                refused += 1
+        check(refused == 5, f"{refused} of 5 unsupported surfaces refused")
+        try:
+            fn(ql.half(), kl.half(), vl.half())
+            check(False, "fp16 accepted")
+        except UnsupportedModelError:
+            pass
+        out = fn(ql, kl, vl, group=group)
+        check.le(rel_l2(out, ref[:, sl]), BF16_REL_L2, "reference-signature function rel l2")
+        fn.invalidate()
+        attn = make_b200_usp_attention(ring_group=group, generation=10, device=dev, full_context_ring=True)
+        out = attn(*(t.reshape(2, rows, -1) for t in (ql, kl, vl)), heads=heads)
+        check.le(rel_l2(out.reshape(2, rows, heads, 128), ref[:, sl]), BF16_REL_L2, "drop-in rel l2")
+        attn.impl.invalidate()
+    torch.cuda.synchronize()
+    check(_lib.device_error() == 0, f"device error word {_lib.device_error()}")
+    check.close()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
+def test_full_context_ring_across_gpus():
+    _spawn(_full_context_case, 2)
+    if torch.cuda.device_count() >= 4:
+        _spawn(_full_context_case, 4)

@@ -210,3 +210,27 @@ def test_bias_pads_must_be_a_tail():
     usp.assert_pads_are_a_tail([12, 13], 14)
     with pytest.raises(usp.OracleRefusal, match="away from the tail"):
         usp.assert_pads_are_a_tail([3, 13], 14)
+
+
+@pytest.mark.parametrize("case", SPEC["full_context"], ids=lambda c: str(c["index"]))
+def test_full_context_gather_matches_reference(case):
+    """The reference's Ring2 K/V gather on a gloo world-2 group
+    (adapters/wan_ring_full_context.py:203-295): rank-major slots, the same
+    gathered axis on both ranks."""
+    n = case["index"]
+    for name in "kv":
+        blocks = [ARR[f"fullctx_{n}_{name}{r}"] for r in range(2)]
+        want = usp.full_context_gather(blocks)
+        for r in range(2):
+            np.testing.assert_array_equal(ARR[f"fullctx_{n}_full{name}{r}"], want)
+
+
+def test_full_context_equals_ring_merge():
+    """Local-Q x full-KV in one softmax equals the ring's per-block merge."""
+    rng = np.random.default_rng(11)
+    q, k, v = ([rng.standard_normal((1, 6, 2, 8)) for _ in range(3)] for _ in range(3))
+    full = usp.full_context_ring_attention(q, k, v)
+    ring = usp.ring_attention(q, k, v)
+    for (o1, l1), (o2, l2) in zip(full, ring):
+        np.testing.assert_allclose(o1, o2, atol=1e-12, rtol=0)
+        np.testing.assert_allclose(l1, l2, atol=1e-12, rtol=0)
