@@ -103,6 +103,17 @@ class AttnRoute(ctypes.Structure):
     ]
 
 
+class SeqGatherDesc(ctypes.Structure):
+    _fields_ = [
+        ("batch", ctypes.c_int32),
+        ("seq_local", ctypes.c_int32),
+        ("orig_len", ctypes.c_int32),
+        ("row_bytes", ctypes.c_int32),
+        ("src_batch_stride", ctypes.c_int64),
+        ("src_row_stride", ctypes.c_int64),
+    ]
+
+
 NORM_NONE, NORM_HIDDEN, NORM_HEAD = 0, 1, 2
 
 
@@ -163,6 +174,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "dgxm_ring_attn_fwd_noalloc": (ctypes.c_int, [_P, ctypes.POINTER(AttnDesc), _P, _P, _P, _P, _P,
                                                   _P]),
     "dgxm_full_context_window_bytes": (ctypes.c_int64, [ctypes.POINTER(AttnDesc), _I32]),
+    "dgxm_seq_allgather": (ctypes.c_int, [_P, ctypes.POINTER(SeqGatherDesc), _P, ctypes.c_int64, _P]),
+    "dgxm_shared_amax_scale": (ctypes.c_int, [_P, _P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                              _I32, ctypes.c_float, _P, _P, _P]),
     "dgxm_full_context_attn_fwd": (ctypes.c_int, [_P, ctypes.POINTER(AttnDesc), _P, _P, _P, _P, _P,
                                                   _P]),
 }

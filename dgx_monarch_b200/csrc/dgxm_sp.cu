@@ -12,4 +12,5 @@
 #include "comm.cu"
 #include "ring.cu"
 #include "full_context.cu"
+#include "shard.cu"
 #include "prologue.cu"

@@ -375,6 +375,43 @@ int64_t dgxm_full_context_window_bytes(const dgxm_attn_desc* desc, int32_t world
 int dgxm_full_context_attn_fwd(dgxm_comm* comm, const dgxm_attn_desc* desc, const void* q,
                                const void* k, const void* v, void* o, float* lse, void* stream);
 
+/* ------------------------------------------------------------ sequence-shard collectives */
+/*
+ * sp_gather (adapters/base.py:126-131): every rank's contiguous chunk of
+ * seq_local rows (rank r holds gathered rows [r*seq_local, (r+1)*seq_local))
+ * is stored over NVLink into every rank's window at window_offset, as the
+ * trimmed (batch, orig_len, row_bytes) tensor; rows at or past orig_len (the
+ * divisibility pad of shard_seq, adapters/base.py:91-123) are not sent.  A
+ * flag barrier follows, so on return (in stream order) each rank's own
+ * window holds the whole trimmed tensor.  Rows, strides and the source are
+ * 16-byte aligned.  Collective over the comm.
+ */
+typedef struct dgxm_seq_gather_desc {
+  int32_t batch;
+  int32_t seq_local;
+  int32_t orig_len;
+  int32_t row_bytes;
+  int64_t src_batch_stride; /* bytes */
+  int64_t src_row_stride;   /* bytes */
+} dgxm_seq_gather_desc;
+
+int dgxm_seq_allgather(dgxm_comm* comm, const dgxm_seq_gather_desc* desc, const void* src,
+                       int64_t window_offset, void* stream);
+
+/*
+ * The shared NVFP4 activation scale (adapters/quant_activation_scale.py:
+ * 222-246): amax(|x|) over this rank's (rows, cols) shard (row_stride in
+ * elements), max-reduced over every rank of the comm (the sequence x CFG
+ * ranks of one model call), written as fp32 to amax_out (may be NULL) and as
+ * dtype(dtype(amax) * (1 / divisor)) to scale_out -- the divide in the
+ * activation dtype, as comfy orders it.  dtype: DGXM_DTYPE_BF16, _F16 or
+ * _F32.  NaN propagates; a barrier that gives up writes NaN and sets the
+ * device error word.  Collective over the comm.
+ */
+int dgxm_shared_amax_scale(dgxm_comm* comm, const void* x, int64_t rows, int64_t cols,
+                           int64_t row_stride, int32_t dtype, float divisor, void* scale_out,
+                           float* amax_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

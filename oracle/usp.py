@@ -168,6 +168,33 @@ def attend_groups_without_pads(q, k, v, drop_rows, kv_drop_rows, groups):
                                lambda qq, kk, vv: query_group_attention(qq, kk, vv, groups))
 
 
+# ----------------------------------------------------------------- NVFP4 activation scale
+def round_to_bf16(x) -> np.ndarray:
+    """fp32 -> bf16 (round to nearest even), returned as fp32 values; NaN kept."""
+    f = np.asarray(x, dtype=np.float32)
+    bits = f.view(np.uint32).astype(np.uint64)
+    rounded = ((bits + 0x7FFF + ((bits >> 16) & 1)) >> 16) << 16
+    out = rounded.astype(np.uint32).view(np.float32)
+    return np.where(np.isnan(f), f, out)
+
+
+def _to_dtype(x, dtype: str) -> np.ndarray:
+    if dtype == "bfloat16":
+        return round_to_bf16(x)
+    if dtype == "float16":
+        return np.asarray(x, dtype=np.float32).astype(np.float16).astype(np.float32)
+    return np.asarray(x, dtype=np.float32)
+
+
+def shared_activation_scale(shards: list[np.ndarray], divisor: float, dtype: str) -> float:
+    """The scale one GPU takes over the whole tensor, from its shards: the max
+    over shards of amax|x| (fp32), cast to the activation dtype, divided by
+    `divisor` in that dtype (adapters/quant_activation_scale.py:222-246)."""
+    amax = np.float32(max((float(np.max(np.abs(s))) if s.size else 0.0) for s in shards))
+    cast = _to_dtype(amax, dtype)
+    return float(_to_dtype(np.float32(cast) / np.float32(divisor), dtype))
+
+
 # ----------------------------------------------------------------- joint order
 @dataclass(frozen=True)
 class RankMajorJointOrder:

@@ -336,6 +336,31 @@ def main() -> None:
     #    rank-major slots every rank's local-Q x full-KV call reads.
     golden["full_context"] = _full_context_golden(rng, arrays)
 
+    # k) the shared NVFP4 activation scale (adapters/quant_activation_scale.py:
+    #    222-246) with a replay reducer standing in for the max all-reduce, as
+    #    tests/test_nvfp4_shard_scale.py:165-178 runs it: every shard of one
+    #    tensor must get the scale one GPU takes over the whole tensor.
+    from dgx_monarch.adapters import quant_activation_scale as qas
+
+    scales = []
+    for n, (dtype, world, rows, cols, outlier) in enumerate((
+            (torch.bfloat16, 2, 64, 64, 30.0), (torch.bfloat16, 4, 96, 40, -7.25),
+            (torch.float16, 2, 32, 48, 11.0), (torch.float32, 3, 30, 20, 5.5),
+            (torch.bfloat16, 8, 128, 256, 0.0))):
+        x = torch.from_numpy(rng.standard_normal((rows, cols)).astype(np.float32)).to(dtype)
+        if outlier:
+            x[rows - 3, cols // 2] = outlier
+        shards = torch.chunk(x, world, dim=0)
+        local = [sh.abs().amax().to(torch.float32).reshape(1) for sh in shards]
+        shared = torch.stack(local).amax(dim=0)
+        plan = qas.SharedScalePlan((("sp", lambda t, m=shared: torch.maximum(t, m)),))
+        got = [qas.shared_activation_scale(sh, plan, qas.NVFP4_SCALE_DIVISOR) for sh in shards]
+        arrays[f"scale_{n}_x"] = x.to(torch.float32).numpy()
+        arrays[f"scale_{n}_out"] = torch.stack([g.to(torch.float32) for g in got]).numpy()
+        scales.append({"index": n, "dtype": str(dtype).replace("torch.", ""), "world": world,
+                       "divisor": qas.NVFP4_SCALE_DIVISOR})
+    golden["shared_scale"] = scales
+
     (OUT / "golden.json").write_text(json.dumps(golden, indent=1))
     np.savez_compressed(OUT / "golden_arrays.npz", **arrays)
     print("wrote", OUT / "golden.json", OUT / "golden_arrays.npz")

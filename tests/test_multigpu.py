@@ -356,3 +356,54 @@ def test_full_context_ring_across_gpus():
     _spawn(_full_context_case, 2)
     if torch.cuda.device_count() >= 4:
         _spawn(_full_context_case, 4)
+
+
+def _shard_case(rank, world, dev):
+    """sp_gather over NVLink (adapters/base.py:126-131) and the shared NVFP4
+    activation scale (adapters/quant_activation_scale.py:222-246)."""
+    from dgx_monarch_b200 import _lib
+    from dgx_monarch_b200.shard import NVFP4_SCALE_DIVISOR, SequenceGather, SharedActivationScale, shard_seq
+
+    check = Checks(rank)
+    gather = SequenceGather(device=dev, generation=12)
+    g = torch.Generator(device=dev).manual_seed(71)
+    cases = [
+        torch.randn(2, 1001, 3072, device=dev, generator=g).bfloat16(),  # pads on the last rank
+        torch.randn(1, 4, 37, 128, device=dev, generator=g),            # fp32, gathered on dim 2
+        torch.randn(3, 50, 3, device=dev, generator=g).half(),           # 6-byte rows
+        torch.randn(2, 1001, 3072, device=dev, generator=g).bfloat16(),  # the first shape again
+    ]
+    for n, x in enumerate(cases):
+        dim = 2 if x.ndim == 4 else 1
+        local, orig = shard_seq(x, world, rank, dim=dim)
+        got = gather(local, orig, dim=dim)
+        torch.cuda.synchronize()
+        check(got.shape == x.shape and torch.equal(got, x), f"sp_gather case {n} differs")
+    gather.close()
+
+    scale = SharedActivationScale(device=dev, generation=13)
+    for n, (dtype, rows, cols) in enumerate(((torch.bfloat16, 256, 3072), (torch.float16, 64, 40),
+                                             (torch.float32, 96, 520), (torch.bfloat16, 8, 7))):
+        x = torch.randn(rows, cols, device=dev, generator=g).to(dtype)
+        x[rows - 1, cols // 2] = 37.5  # the outlier sits on the last rank's rows
+        local, _ = shard_seq(x, world, rank, dim=0)
+        trace: list = []
+        got = scale(local, trace=trace)
+        want = x.abs().amax().to(torch.float32).reshape(()).to(dtype) / NVFP4_SCALE_DIVISOR
+        torch.cuda.synchronize()
+        check(got.dtype == dtype and torch.equal(got, want), f"scale case {n}: {got.item()} vs {want.item()}")
+        check(trace[1].item() == 37.5, f"reduced amax case {n}: {trace[1].item()}")
+    nan = torch.zeros(4, 16, device=dev, dtype=torch.bfloat16)
+    if rank == 0:
+        nan[1, 3] = float("nan")
+    got = scale(nan)
+    torch.cuda.synchronize()
+    check(torch.isnan(got).item(), "a NaN on one rank must reach every rank's scale")
+    scale.close()
+    check(_lib.device_error() == 0, f"device error word {_lib.device_error()}")
+    check.close()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
+def test_sequence_gather_and_shared_scale_across_gpus():
+    _spawn(_shard_case, min(torch.cuda.device_count(), 4))

@@ -234,3 +234,24 @@ def test_full_context_equals_ring_merge():
     for (o1, l1), (o2, l2) in zip(full, ring):
         np.testing.assert_allclose(o1, o2, atol=1e-12, rtol=0)
         np.testing.assert_allclose(l1, l2, atol=1e-12, rtol=0)
+
+
+@pytest.mark.parametrize("case", SPEC["shared_scale"], ids=lambda c: f"{c['dtype']}-w{c['world']}")
+def test_shared_activation_scale_matches_reference(case):
+    """The reference's shared NVFP4 scale with a replay reducer
+    (adapters/quant_activation_scale.py:222-246): every shard gets the
+    one-GPU scale of the whole tensor."""
+    n = case["index"]
+    x = ARR[f"scale_{n}_x"]
+    shards = np.array_split(x, case["world"], axis=0)
+    want = usp.shared_activation_scale(shards, case["divisor"], case["dtype"])
+    for got in ARR[f"scale_{n}_out"]:
+        assert np.float32(got) == np.float32(want)
+
+
+def test_round_to_bf16_is_nearest_even():
+    vals = np.array([1.0, 1.00390625, 1.01171875, 3.0e38, -2.5e-3, np.inf, np.nan], dtype=np.float32)
+    got = usp.round_to_bf16(vals)
+    assert got[1] == 1.0                      # a tie rounds to the even mantissa
+    assert got[2] == np.float32(1.015625)     # a tie rounds up to the even neighbour
+    assert np.isinf(got[5]) and np.isnan(got[6])
