@@ -64,35 +64,106 @@ def cfg_rank_layout(world: int, sp: int, cfg: int) -> list[tuple[int, int]]:
 
 
 class CfgGather:
-    """Peer-store all-gather of fixed-size predictions over one cfg group."""
+    """Peer-store all-gather of fixed-size predictions over one cfg group.
+
+    Two window buffers alternate by call: a rank copies into buffer
+    (n+1) % 2 only after passing the barrier of call n, which every peer
+    reaches after reading its call n-1 result out of that buffer."""
 
     def __init__(self, nbytes_per_rank: int, *, device: torch.device, group=None, rank: int = 0,
                  world: int = 1, generation: int = 0) -> None:
         import torch.distributed as dist
 
-        if group is not None or (world > 1 and dist.is_initialized()):
-            world = dist.get_world_size(group)
-        self.windows = PeerWindows(nbytes_per_rank * max(world, 1) + 256, device=device,
-                                   group=group, rank=rank, world=world, generation=generation)
+        if dist.is_available() and dist.is_initialized():
+            # The named group, or the default group when none is given.
+            rank, world = dist.get_rank(group), dist.get_world_size(group)
+        span = (nbytes_per_rank * max(world, 1) + 255) // 256 * 256
+        self.windows = PeerWindows(2 * span + 256, device=device, group=group, rank=rank, world=world,
+                                   generation=generation)
         self.world, self.rank, self.device = self.windows.world, self.windows.rank, device
         self.slice_bytes = nbytes_per_rank
-        self.offset = self.windows.carve(nbytes_per_rank * self.world)
+        self.offsets = (self.windows.carve(span), self.windows.carve(span))
+        self.calls = 0
 
-    def __call__(self, local: torch.Tensor) -> torch.Tensor:
+    def gather_in_window(self, local: torch.Tensor) -> torch.Tensor:
+        """Gather into this call's window buffer and return a view of it, valid
+        until the call after next."""
         local = local.contiguous()
         nbytes = local.numel() * local.element_size()
         if nbytes != self.slice_bytes:
             raise ValueError(f"gather planned for {self.slice_bytes} bytes per rank, got {nbytes}")
+        offset = self.offsets[self.calls % 2]
+        self.calls += 1
         stream = torch.cuda.current_stream(self.device)
         _lib.check(_lib.load().dgxm_comm_allgather(self.windows._handle, local.data_ptr(), nbytes,
-                                                    self.offset, stream.cuda_stream),
+                                                    offset, stream.cuda_stream),
                    "dgxm_comm_allgather")
-        full = self.windows.local_tensor(self.offset, (self.world * local.shape[0], *local.shape[1:]),
+        return self.windows.local_tensor(offset, (self.world * local.shape[0], *local.shape[1:]),
                                          local.dtype)
-        return full.clone()
+
+    def __call__(self, local: torch.Tensor) -> torch.Tensor:
+        return self.gather_in_window(local).clone()
 
     def close(self) -> None:
+        torch.cuda.synchronize(self.device)
         self.windows.close()
+
+
+_PRED_DTYPES = {torch.float32: _lib.DTYPE_F32, torch.bfloat16: _lib.DTYPE_BF16,
+                torch.float16: _lib.DTYPE_F16}
+
+
+def cfg_combine(cond: torch.Tensor, uncond: torch.Tensor, cfg: float,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """uncond + (cond - uncond) * cfg, rounded per operation as torch does
+    (comfy's default cfg_function), in one kernel (dgxm_cfg_combine)."""
+    if cond.shape != uncond.shape or cond.dtype != uncond.dtype or cond.dtype not in _PRED_DTYPES:
+        raise ValueError("cond and uncond must share shape and a float dtype")
+    # The kernel moves 16-byte vectors; a view at an unaligned offset (a
+    # prediction whose byte size is not a multiple of 16, sliced out of the
+    # gathered pair) is copied to an aligned buffer first.
+    cond, uncond = (t.contiguous() if t.data_ptr() % 16 == 0 else t.clone() for t in (cond, uncond))
+    if out is None:
+        out = torch.empty_like(cond)
+    stream = torch.cuda.current_stream(cond.device)
+    _lib.check(_lib.load().dgxm_cfg_combine(cond.data_ptr(), uncond.data_ptr(), cond.numel(),
+                                            _PRED_DTYPES[cond.dtype], float(cfg), out.data_ptr(),
+                                            stream.cuda_stream), "dgxm_cfg_combine")
+    return out
+
+
+class DualModelCfg:
+    """The dm-cfg2 exchange (actor/dual_model_cfg.py:75-94): cfg rank 0 runs
+    the conditional model, rank 1 the unconditional one; each step both
+    predictions cross NVLink into both ranks' windows (cond first, the
+    all-gather's rank order) and both ranks combine them with the same
+    fp32 formula, so the samplers evolve identically."""
+
+    def __init__(self, pred_bytes: int, cfg: float, *, device: torch.device, group=None,
+                 generation: int = 0) -> None:
+        import math
+
+        if math.isclose(float(cfg), 1.0):
+            # actor/dual_model_cfg.py:122-130: at cfg 1.0 the unconditional
+            # rank would have no work and skip the exchange its peer waits in.
+            raise UnsupportedModelError(
+                "dual-model cfg-parallel (cfg2) needs a guider cfg above 1: at cfg 1.0 the "
+                "unconditional rank has no guidance work and would skip the per-step exchange, "
+                "hanging its peer. Raise the guider cfg above 1, or run this render at cfg 1.0 "
+                "on topology uly2 instead.")
+        self.cfg = float(cfg)
+        self.gather = CfgGather(pred_bytes, device=device, group=group, generation=generation)
+        if self.gather.world != 2:
+            raise UnsupportedModelError(
+                f"dual-model cfg splits across a cfg group of 2 ranks, not {self.gather.world}")
+
+    def __call__(self, local_pred: torch.Tensor) -> torch.Tensor:
+        both = self.gather.gather_in_window(local_pred)
+        n = local_pred.shape[0]
+        return cfg_combine(both[:n], both[n:2 * n], self.cfg)
+
+    def close(self) -> None:
+        self.gather.close()
 
 
 def cfg_parallel_call(forward, *args, batch_arg: str = "x", group=None, gather: CfgGather | None = None,

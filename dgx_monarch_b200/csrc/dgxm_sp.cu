@@ -13,4 +13,5 @@
 #include "ring.cu"
 #include "full_context.cu"
 #include "shard.cu"
+#include "cfg.cu"
 #include "prologue.cu"

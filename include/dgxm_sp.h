@@ -412,6 +412,17 @@ int dgxm_shared_amax_scale(dgxm_comm* comm, const void* x, int64_t rows, int64_t
                            int64_t row_stride, int32_t dtype, float divisor, void* scale_out,
                            float* amax_out, void* stream);
 
+/* ------------------------------------------------------------ CFG combine */
+/*
+ * out = uncond + (cond - uncond) * cfg_scale over n contiguous elements of
+ * dtype (DGXM_DTYPE_F32, _BF16 or _F16), each operation rounded to dtype with
+ * the scale taken as fp32 -- comfy's default cfg_function as the dual-model
+ * CFG split runs it after its all-gather (actor/dual_model_cfg.py:75-94).
+ * The three pointers are 16-byte aligned; out may alias cond or uncond.
+ */
+int dgxm_cfg_combine(const void* cond, const void* uncond, int64_t n, int32_t dtype,
+                     double cfg_scale, void* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -195,6 +195,18 @@ def shared_activation_scale(shards: list[np.ndarray], divisor: float, dtype: str
     return float(_to_dtype(np.float32(cast) / np.float32(divisor), dtype))
 
 
+def cfg_combine(cond: np.ndarray, uncond: np.ndarray, cfg: float, dtype: str) -> np.ndarray:
+    """uncond + (cond - uncond) * cfg with each operation rounded to the
+    prediction dtype and the scale taken as fp32: the default combine the
+    dual-model CFG split runs after its all-gather
+    (actor/dual_model_cfg.py:84-92)."""
+    c = _to_dtype(np.asarray(cond, dtype=np.float32), dtype)
+    u = _to_dtype(np.asarray(uncond, dtype=np.float32), dtype)
+    d = _to_dtype(c - u, dtype)
+    m = _to_dtype(d * np.float32(cfg), dtype)
+    return _to_dtype(u + m, dtype)
+
+
 # ----------------------------------------------------------------- joint order
 @dataclass(frozen=True)
 class RankMajorJointOrder:

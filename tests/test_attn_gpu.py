@@ -257,3 +257,19 @@ def test_row_with_only_excluded_keys_in_leading_blocks(lib):
     assert torch.equal(out[:, 40], torch.zeros_like(out[:, 40]))
     rest, _ = reference_attention(q[:, 64:], k, v)
     assert rel_l2(out[:, 64:], rest) <= BF16_REL_L2
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_cfg_combine_is_bit_exact_against_torch(lib, dtype):
+    """uncond + (cond - uncond) * cfg (comfy's default cfg_function, as the
+    dual-model CFG split runs it) against torch's unfused expression, with a
+    tail that does not fill a 16-byte vector and an output aliasing cond."""
+    from dgx_monarch_b200.cfg import cfg_combine
+
+    g = torch.Generator(device="cuda").manual_seed(47)
+    for n in (16 * 128 * 128, 1003):
+        c = torch.randn(n, device="cuda", generator=g).to(dtype)
+        u = torch.randn(n, device="cuda", generator=g).to(dtype)
+        want = u + (c - u) * 5.5
+        assert torch.equal(cfg_combine(c, u, 5.5), want)
+        assert torch.equal(cfg_combine(c, u, 5.5, out=c), want)

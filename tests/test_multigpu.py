@@ -7,6 +7,7 @@ handle exchange; NVLS stays off.
 """
 from __future__ import annotations
 
+import math
 import os
 import socket
 import traceback
@@ -407,3 +408,30 @@ def _shard_case(rank, world, dev):
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
 def test_sequence_gather_and_shared_scale_across_gpus():
     _spawn(_shard_case, min(torch.cuda.device_count(), 4))
+
+
+def _dual_cfg_case(rank, world, dev):
+    """dm-cfg2 (actor/dual_model_cfg.py:75-94): rank 0 holds the conditional
+    prediction, rank 1 the unconditional; both must end with the identical
+    combined prediction, step after step."""
+    from dgx_monarch_b200 import _lib
+    from dgx_monarch_b200.cfg import DualModelCfg
+
+    check = Checks(rank)
+    shape = (1, 16, 128, 128)
+    split = DualModelCfg(math.prod(shape) * 4, 4.0, device=dev, generation=14)
+    for step in range(3):  # alternating window buffers
+        g = torch.Generator(device=dev).manual_seed(80 + step)
+        cond = torch.randn(shape, device=dev, generator=g)
+        uncond = torch.randn(shape, device=dev, generator=g)
+        got = split(cond if rank == 0 else uncond)
+        torch.cuda.synchronize()
+        check(torch.equal(got, uncond + (cond - uncond) * 4.0), f"step {step}: combined prediction differs")
+    split.close()
+    check(_lib.device_error() == 0, f"device error word {_lib.device_error()}")
+    check.close()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
+def test_dual_model_cfg_split_across_gpus():
+    _spawn(_dual_cfg_case, 2)

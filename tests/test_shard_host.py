@@ -39,3 +39,21 @@ def test_indivisible_stream_that_must_not_pad_is_refused():
     assert shard_seq(None, 4, 0) == (None, 0)
     padded, orig = pad_seq_to_multiple(x, 4)
     assert padded.shape == (1, 12, 2) and orig == 10
+
+
+def test_dual_model_cfg_refuses_a_guidance_scale_of_one():
+    """actor/dual_model_cfg.py:122-130: at cfg 1.0 the unconditional rank would
+    skip the exchange, so the split is refused before any window exists."""
+    from dgx_monarch_b200.cfg import DualModelCfg, UnsupportedModelError
+
+    with pytest.raises(UnsupportedModelError, match="cfg above 1"):
+        DualModelCfg(1024, 1.0, device=torch.device("cpu"))
+
+
+def test_oracle_cfg_combine_rounds_each_operation():
+    """The oracle's combine against torch's unfused expression on the CPU for
+    fp32 (each operation rounded to fp32)."""
+    g = torch.Generator().manual_seed(3)
+    c, u = torch.randn(1000, generator=g), torch.randn(1000, generator=g)
+    want = (u + (c - u) * 4.5).numpy()
+    np.testing.assert_array_equal(usp.cfg_combine(c.numpy(), u.numpy(), 4.5, "float32"), want)
