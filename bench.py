@@ -173,6 +173,34 @@ DIT_WORKLOAD = ("Flux/Krea2-style joint-attention DiT double block (attention su
                 "per-head RMSNorm on Q/K, 2-axis RoPE, joint [text, image] attention")
 
 
+def time_steps(step, steps: int, warmup: int, graph: bool = False) -> float:
+    """Mean device ms per step over `steps` timed steps, eagerly or as a
+    replayed CUDA graph of one step (captured after the warm-up; every rank
+    captures and replays the same sequence)."""
+    import torch
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    run, captured = step, None
+    if graph:
+        captured = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(captured):
+            step()
+        run = captured.replay
+        for _ in range(warmup):
+            run()
+        torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    del captured
+    return e0.elapsed_time(e1) / steps
+
+
 def dit_layer_flops() -> float:
     s, hid = DIT["img"] + DIT["txt"], DIT["hidden"]
     return 2.0 * s * hid * 3 * hid + 2.0 * s * hid * hid + attn_flops(1, DIT["heads"], s, DIM)
@@ -229,18 +257,10 @@ def run_dit_layer(world: int, rank: int, dev, steps: int, warmup: int, group=Non
         torch.matmul(o[:, :t_loc], w_o_txt, out=y[:, :t_loc])
         torch.matmul(o[:, t_loc:], w_o_img, out=y[:, t_loc:])
 
-    for _ in range(warmup):
-        step()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(steps):
-        step()
-    e1.record()
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / steps
+    ms_eager = time_steps(step, steps, warmup)
+    ms = time_steps(step, steps, warmup, graph=True)  # the same work, launched from one graph
     win.close()
-    return {"ms": ms, "my_launches": 4 if world > 1 else 2}
+    return {"ms": ms, "ms_eager": ms_eager, "my_launches": 4 if world > 1 else 2}
 
 
 # ----------------------------------------------------------------- ring / CFG workloads (N > 1)
@@ -370,19 +390,11 @@ def run_cfg_fp8(world: int, rank: int, dev, steps: int, warmup: int) -> dict:
         out = attn(q, k, v, heads=h)          # this cfg rank's batch row, its sequence shard
         return gather(out)                    # predictions of the pair, in cfg-rank order
 
-    for _ in range(warmup):
-        step()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(steps):
-        step()
-    e1.record()
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / steps
+    ms_eager = time_steps(step, steps, warmup)
+    ms = time_steps(step, steps, warmup, graph=True)
     gather.close()
     attn.impl.invalidate()
-    return {"ms": ms, "layout": f"cfg2xulysses{sp}"}
+    return {"ms": ms, "ms_eager": ms_eager, "layout": f"cfg2xulysses{sp}"}
 
 
 def time_scatter(uly, steps: int = 5) -> dict:
@@ -506,14 +518,15 @@ def main() -> None:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_ms = te.item()
     dit = run_dit_layer(world, rank, dev, max(5, args.steps), args.warmup)
-    extra = [dit["ms"], 0.0, 0.0, 0.0, 0.0, 0.0]
+    extra = [dit["ms"], 0.0, 0.0, 0.0, 0.0, 0.0, dit["ms_eager"], 0.0]
     a2a = ring_res = cfg_res = fc_res = None
     if world > 1:
         a2a = time_scatter(uly)
         ring_res = run_ring(world, rank, dev, 2, 1)
         cfg_res = run_cfg_fp8(world, rank, dev, 5, 3)
         fc_res = run_full_context(world, rank, dev, 3, 3)
-        extra[1:] = [a2a["ms"], ring_res["ms"], cfg_res["ms"], a2a["gbs_per_direction"], fc_res["ms"]]
+        extra[1:6] = [a2a["ms"], ring_res["ms"], cfg_res["ms"], a2a["gbs_per_direction"], fc_res["ms"]]
+        extra[7] = cfg_res["ms_eager"]
     td = torch.tensor(extra, device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(td, op=dist.ReduceOp.MAX)
@@ -521,7 +534,7 @@ def main() -> None:
         tmin = torch.tensor([extra[4]], device=dev, dtype=torch.float64)
         dist.all_reduce(tmin, op=dist.ReduceOp.MIN)
         td[4] = tmin[0]
-    dit_ms, a2a_ms, ring_ms, cfg_ms, a2a_gbs, fc_ms = td.tolist()
+    dit_ms, a2a_ms, ring_ms, cfg_ms, a2a_gbs, fc_ms, dit_ms_eager, cfg_ms_eager = td.tolist()
     dev_err = _lib.device_error()
 
     if rank == 0:
@@ -557,7 +570,9 @@ def main() -> None:
                     "d2h_bytes_per_step": out.numel() * out.element_size(),
                     "ms_per_step": e2e_ms},
             "dit_layer": {"workload": DIT_WORKLOAD, "tokens_per_s": (DIT["img"] + DIT["txt"]) / (dit_ms * 1e-3),
-                          "ms_per_layer": dit_ms, "tflops": dit_layer_flops() / (dit_ms * 1e-3) / 1e12,
+                          "ms_per_layer": dit_ms, "ms_per_layer_eager": dit_ms_eager,
+                          "launch": "one CUDA graph per layer (ms_per_layer_eager: the same calls from Python)",
+                          "tflops": dit_layer_flops() / (dit_ms * 1e-3) / 1e12,
                           "frac_of_bf16_peak": dit_layer_flops() / (dit_ms * 1e-3) / 1e12 / (world * peaks["bf16_tflops"]),
                           "parallelism": f"ulysses{world}"},
             "gpu_launches": launches,
@@ -578,6 +593,8 @@ def main() -> None:
                             "tokens_per_s": RING["seq"] / (ring_ms * 1e-3)}
             cflops = attn_flops(CFG["batch"], CFG["heads"], CFG["img"] + CFG["txt"], DIM)
             line["cfg_fp8"] = {"workload": CFG_WORKLOAD, "layout": cfg_res["layout"], "ms_per_step": cfg_ms,
+                               "ms_per_step_eager": cfg_ms_eager,
+                               "launch": "one CUDA graph per step (ms_per_step_eager: the same calls from Python)",
                                "tflops": cflops / (cfg_ms * 1e-3) / 1e12}
             line["wan_ring2_full_context"] = {
                 "workload": WORKLOAD + "; pure ring-2 full context: K/V gathered over NVLink, "

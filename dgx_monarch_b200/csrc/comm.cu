@@ -22,7 +22,6 @@ struct dgxm_comm {
   char* local;         // this rank's window base (cudaMalloc)
   char* peers[DGXM_MAX_WORLD];  // window bases as seen by this process
   bool opened[DGXM_MAX_WORLD];
-  uint32_t epoch;      // barriers issued so far
   uint32_t fc_calls;   // full-context calls so far (their window buffer alternates)
   long long wait_cycles;  // barrier wait budget in SM clock cycles
   cudaStream_t side;      // ring: copy-engine stream (created on first use)
@@ -32,37 +31,51 @@ struct dgxm_comm {
 namespace dgxm {
 
 constexpr int64_t kFlagBytes = 4096;
+// This rank's barrier count, in its own flag area: every barrier-type kernel
+// reads it, uses count + 1 as its epoch and stores that back, so the epochs
+// live on the device and a captured CUDA graph advances them on each replay.
+constexpr int64_t kEpochCounter = 3584;
+
+__device__ __forceinline__ int next_epoch(const char* my_flag_area) {
+  return *reinterpret_cast<const volatile int*>(my_flag_area + kEpochCounter) + 1;
+}
 
 // ------------------------------------------------------------------ barrier
 struct BarrierParams {
   int* peer_flags[DGXM_MAX_WORLD];  // flag area of each rank's window
   int* my_flags;
   int rank, world;
-  int epoch;
   long long wait_cycles;
 };
 
+// One warp; lane i < world does this rank's half of the handshake with rank
+// i: release the epoch into rank i's slot for this rank, acquire rank i's
+// epoch from this rank's slot for it.
 __global__ void comm_barrier_kernel(const __grid_constant__ BarrierParams p) {
   const int i = threadIdx.x;
-  if (i >= p.world) return;
-  // Everything this rank wrote before this kernel (earlier kernels in the
-  // stream) is performed before the flag below becomes visible.
-  __threadfence_system();
-  int* slot = p.peer_flags[i] + p.rank;
-  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(slot), "r"(p.epoch) : "memory");
-  const int* mine = p.my_flags + i;
-  const long long start = clock64();
-  while (true) {
-    int seen;
-    asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(seen) : "l"(mine) : "memory");
-    if (seen - p.epoch >= 0) break;  // wrap-safe monotonic compare
-    if (clock64() - start > p.wait_cycles) {
-      report_device_error(kErrPeerTimeout);
-      break;
+  const int epoch = next_epoch(reinterpret_cast<const char*>(p.my_flags));
+  if (i < p.world) {
+    // Everything this rank wrote before this kernel (earlier kernels in the
+    // stream) is performed before the flag below becomes visible.
+    __threadfence_system();
+    int* slot = p.peer_flags[i] + p.rank;
+    asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(slot), "r"(epoch) : "memory");
+    const int* mine = p.my_flags + i;
+    const long long start = clock64();
+    while (true) {
+      int seen;
+      asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(seen) : "l"(mine) : "memory");
+      if (seen - epoch >= 0) break;  // wrap-safe monotonic compare
+      if (clock64() - start > p.wait_cycles) {
+        report_device_error(kErrPeerTimeout);
+        break;
+      }
+      __nanosleep(64);
     }
-    __nanosleep(64);
+    __threadfence_system();
   }
-  __threadfence_system();
+  __syncwarp();  // every lane has read the count before it advances
+  if (i == 0) *reinterpret_cast<volatile int*>(reinterpret_cast<char*>(p.my_flags) + kEpochCounter) = epoch;
 }
 
 // ------------------------------------------------------------------ all-to-all
@@ -301,8 +314,6 @@ extern "C" int dgxm_comm_barrier(dgxm_comm* c, void* stream) {
   p.my_flags = reinterpret_cast<int*>(c->local);
   p.rank = c->rank;
   p.world = c->world;
-  c->epoch += 1;
-  p.epoch = static_cast<int>(c->epoch);
   p.wait_cycles = c->wait_cycles;
   comm_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(p);
   DGXM_CUDA_TRY(cudaGetLastError());

@@ -13,15 +13,18 @@
 // 448 * 6.  Here: one grid kernel takes the local amax (float bits,
 // atomicMax), and one single-warp kernel publishes it into every rank's
 // window, runs the flag barrier inline, and reduces the slots it received.
-// The slots alternate by call parity: a rank publishes call n+1 only after
-// passing barrier n, and every peer read its call n-1 slots inside the
-// kernel that arrived at barrier n, so a slot is never overwritten unread.
+// The slots alternate by barrier-epoch parity: a rank publishes at epoch e
+// only after passing barrier e-1, and every peer read its epoch e-2 slots
+// inside the kernel that ran before it arrived at barrier e-1, so a slot is
+// never overwritten unread.  The epoch comes from the device counter, so the
+// exchange replays correctly inside a captured CUDA graph.
 
 namespace dgxm {
 
 // Flag-area layout (the first kFlagBytes of every window): barrier flags at
 // byte 0 (one int per rank), amax slots at kAmaxSlots (two parities x 8
-// ranks of fp32), this rank's local amax accumulator at kAmaxLocal.
+// ranks of fp32), this rank's local amax accumulator at kAmaxLocal, the
+// barrier count at kEpochCounter.
 constexpr int64_t kAmaxSlots = 2048;
 constexpr int64_t kAmaxLocal = 3072;
 
@@ -119,7 +122,7 @@ __global__ void __launch_bounds__(256) amax_local_kernel(const __grid_constant__
 struct AmaxExchangeParams {
   char* peer_flag_area[DGXM_MAX_WORLD];  // every rank's flag area as seen here
   char* my_flag_area;
-  int rank, world, epoch, parity;
+  int rank, world;
   long long wait_cycles;
   float inv_divisor;   // 1 / divisor, fp32 (the activation dtype's divide by a scalar)
   int dtype;           // output scale dtype
@@ -132,21 +135,23 @@ struct AmaxExchangeParams {
 // acquire the flag rank i left here), then reads the slot rank i filled here.
 __global__ void amax_exchange_kernel(const __grid_constant__ AmaxExchangeParams p) {
   const int i = threadIdx.x;
+  const int epoch = next_epoch(p.my_flag_area);
+  const int parity = epoch & 1;
   float v = 0.f;
   bool ok = true;
   if (i < p.world) {
     const float mine = __uint_as_float(*reinterpret_cast<const unsigned int*>(p.my_flag_area + kAmaxLocal));
-    float* slot = reinterpret_cast<float*>(p.peer_flag_area[i] + kAmaxSlots) + p.parity * DGXM_MAX_WORLD + p.rank;
+    float* slot = reinterpret_cast<float*>(p.peer_flag_area[i] + kAmaxSlots) + parity * DGXM_MAX_WORLD + p.rank;
     *reinterpret_cast<volatile float*>(slot) = mine;
     __threadfence_system();
     int* flag = reinterpret_cast<int*>(p.peer_flag_area[i]) + p.rank;
-    asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(flag), "r"(p.epoch) : "memory");
+    asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(flag), "r"(epoch) : "memory");
     const int* seen_at = reinterpret_cast<const int*>(p.my_flag_area) + i;
     const long long start = clock64();
     while (true) {
       int seen;
       asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(seen) : "l"(seen_at) : "memory");
-      if (seen - p.epoch >= 0) break;
+      if (seen - epoch >= 0) break;
       if (clock64() - start > p.wait_cycles) {
         report_device_error(kErrPeerTimeout);
         ok = false;
@@ -154,7 +159,7 @@ __global__ void amax_exchange_kernel(const __grid_constant__ AmaxExchangeParams 
       }
       __nanosleep(64);
     }
-    const float* got = reinterpret_cast<const float*>(p.my_flag_area + kAmaxSlots) + p.parity * DGXM_MAX_WORLD + i;
+    const float* got = reinterpret_cast<const float*>(p.my_flag_area + kAmaxSlots) + parity * DGXM_MAX_WORLD + i;
     v = *reinterpret_cast<const volatile float*>(got);
   }
   unsigned int m = __float_as_uint(v);
@@ -163,8 +168,9 @@ __global__ void amax_exchange_kernel(const __grid_constant__ AmaxExchangeParams 
     const unsigned int other = __shfl_xor_sync(0xffffffffu, m, o);
     m = other > m ? other : m;
   }
-  const bool all_ok = __all_sync(0xffffffffu, ok);
+  const bool all_ok = __all_sync(0xffffffffu, ok);  // every lane has read the count
   if (i == 0) {
+    *reinterpret_cast<volatile int*>(p.my_flag_area + kEpochCounter) = epoch;
     // A barrier that gave up leaves NaN, never a plausible scale.
     const float amax = all_ok ? __uint_as_float(m) : __int_as_float(0x7FC00000);
     if (p.amax_out != nullptr) *p.amax_out = amax;
@@ -270,9 +276,6 @@ extern "C" int dgxm_shared_amax_scale(dgxm_comm* c, const void* x, int64_t rows,
   e.my_flag_area = c->local;
   e.rank = c->rank;
   e.world = c->world;
-  c->epoch += 1;
-  e.epoch = static_cast<int>(c->epoch);
-  e.parity = static_cast<int>(c->epoch & 1u);
   e.wait_cycles = c->wait_cycles;
   e.inv_divisor = 1.0f / divisor;
   e.dtype = dtype;

@@ -193,7 +193,12 @@ uint64_t dgxm_comm_generation(dgxm_comm* comm);
  * flag in every peer window and waits (bounded, about one second) for every
  * peer's flag.  A wait that expires sets the device error word instead of
  * hanging.  Replaces the implicit synchronisation of the reference's NCCL
- * all_to_all. */
+ * all_to_all.  The barrier count lives in device memory, so the barrier --
+ * and the Ulysses step built on it (scatter, barrier, routed attention,
+ * barrier) and dgxm_shared_amax_scale -- may be captured in a CUDA graph and
+ * replayed; every rank must replay the same sequence.  The entries that
+ * alternate window buffers on the host (ring, full-context, sequence gather)
+ * are not for capture. */
 int dgxm_comm_barrier(dgxm_comm* comm, void* stream);
 /* Wall-clock budget of one barrier wait (default about one second). */
 int dgxm_comm_set_timeout(dgxm_comm* comm, int32_t timeout_ms);

@@ -435,3 +435,42 @@ def _dual_cfg_case(rank, world, dev):
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
 def test_dual_model_cfg_split_across_gpus():
     _spawn(_dual_cfg_case, 2)
+
+
+def _graph_case(rank, world, dev):
+    """A Ulysses step (scatter, barrier, routed attention, barrier) captured in
+    a CUDA graph and replayed with new inputs: the barrier epochs advance on
+    the device, so every replay synchronises afresh."""
+    from dgx_monarch_b200 import _lib
+    from dgx_monarch_b200.ulysses import UlyssesAttention
+    from tests.test_attn_gpu import BF16_REL_L2, reference_attention, rel_l2
+
+    check = Checks(rank)
+    heads, ls = 2 * world, 256
+    uly = UlyssesAttention(world=world, rank=rank, batch=1, seq_local=ls, heads=heads, head_dim=128,
+                           device=dev, generation=15)
+    bufs = [torch.zeros(1, ls, heads, 128, device=dev, dtype=torch.bfloat16) for _ in range(3)]
+    out = torch.zeros(1, ls, heads, 128, device=dev, dtype=torch.bfloat16)
+    uly.forward(*bufs)  # warm-up outside the capture (kernel attributes, plans)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out.copy_(uly.forward(*bufs))
+    for step in range(3):
+        g = torch.Generator(device=dev).manual_seed(90 + step)  # the same full tensors on every rank
+        q, k, v = (torch.randn(1, ls * world, heads, 128, device=dev, generator=g).bfloat16() for _ in range(3))
+        for buf, full in zip(bufs, (q, k, v)):
+            buf.copy_(full[:, rank * ls:(rank + 1) * ls])
+        graph.replay()
+        torch.cuda.synchronize()
+        ref, _ = reference_attention(q, k, v)
+        check.le(rel_l2(out, ref[:, rank * ls:(rank + 1) * ls]), BF16_REL_L2, f"replay {step} rel l2")
+    del graph
+    uly.close()
+    check(_lib.device_error() == 0, f"device error word {_lib.device_error()}")
+    check.close()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
+def test_captured_ulysses_step_replays_across_gpus():
+    _spawn(_graph_case, 2)
