@@ -169,8 +169,10 @@ def run_reference(args) -> None:
 DIT = {"hidden": 3072, "heads": 24, "img": 9216, "txt": 512, "latent": (96, 96)}
 DIT_WORKLOAD = ("Flux/Krea2-style joint-attention DiT double block (attention sub-layer): "
                 "1536x1536 image -> 96x96 patch grid = 9216 tokens + 512 text tokens, hidden 3072, "
-                "24 heads x 128, bf16, random-init weights N(0, 0.02); QKV and out projections, "
-                "per-head RMSNorm on Q/K, 2-axis RoPE, joint [text, image] attention")
+                "24 heads x 128, bf16, random-init weights N(0, 0.02); QKV projection with bias (cuBLAS), "
+                "per-head RMSNorm on Q/K + 2-axis RoPE + sequence->head scatter in one kernel, joint "
+                "[text, image] attention with the inverse all-to-all in its epilogue, out projection "
+                "(cuBLAS)")
 
 
 def time_steps(step, steps: int, warmup: int, graph: bool = False) -> float:
@@ -212,7 +214,7 @@ def run_dit_layer(world: int, rank: int, dev, steps: int, warmup: int, group=Non
 
     from dgx_monarch_b200 import _lib
     from dgx_monarch_b200.comm import PeerWindows
-    from dgx_monarch_b200.prologue import qkv_prologue_scatter, rope_table
+    from dgx_monarch_b200.prologue import qkv_gemm_prologue_scatter, qkv_prologue_scatter, rope_table
     from dgx_monarch_b200.ulysses import attention_routed
 
     hid, h = DIT["hidden"], DIT["heads"]
@@ -223,7 +225,10 @@ def run_dit_layer(world: int, rank: int, dev, steps: int, warmup: int, group=Non
     g = torch.Generator(device=dev).manual_seed(77 + rank)
     w = lambda *shape: (0.02 * torch.randn(*shape, device=dev, generator=g)).bfloat16()
     x_txt, x_img = w(1, t_loc, hid) * 50, w(1, i_loc, hid) * 50
-    w_qkv_txt, w_qkv_img = w(hid, 3 * hid), w(hid, 3 * hid)
+    # Linear weights (out, in), as the block's modules hold them, and their biases.
+    w_qkv_txt, w_qkv_img = w(3 * hid, hid), w(3 * hid, hid)
+    b_qkv_txt, b_qkv_img = w(3 * hid), w(3 * hid)
+    qkv = torch.empty(1, ls, 3, h, DIM, device=dev, dtype=torch.bfloat16)
     w_o_txt, w_o_img = w(hid, hid), w(hid, hid)
     nq, nk = (1 + w(128)).contiguous(), (1 + w(128)).contiguous()
     # Positions: text tokens at 0, image tokens at (0, row, col) of the 96x96 grid.
@@ -231,7 +236,6 @@ def run_dit_layer(world: int, rank: int, dev, steps: int, warmup: int, group=Non
     pos = torch.cat((torch.zeros(t_loc, 3, device=dev, dtype=torch.long),
                      torch.stack((torch.zeros_like(img_ids), img_ids // 96, img_ids % 96), dim=1)))
     table = rope_table(pos, [16, 56, 56])
-    qkv = torch.empty(1, ls, 3, h, DIM, device=dev, dtype=torch.bfloat16)
     elt = 2
     recv_bytes = s * hl * DIM * elt
     out_bytes = ls * h * DIM * elt
@@ -242,13 +246,24 @@ def run_dit_layer(world: int, rank: int, dev, steps: int, warmup: int, group=Non
     out_local = win.local_tensor(offs[3], (1, ls, h, DIM), torch.bfloat16)
     y = torch.empty(1, ls, hid, device=dev, dtype=torch.bfloat16)
 
+    dst = [[win.peer_ptr(r, o) for r in range(world)] for o in offs[:3]]
+
+    def qkv_fused():
+        # QKV Linear + QKNorm + RoPE + sequence->head scatter, one kernel per stream.
+        for x, wq, bq, row0 in ((x_txt, w_qkv_txt, b_qkv_txt, 0), (x_img, w_qkv_img, b_qkv_img, t_loc)):
+            qkv_gemm_prologue_scatter(x, wq, dst, world=world, rank=rank, seq_local=ls, row0=row0,
+                                      seg0=t_loc, bias=bq, norm_mode=_lib.NORM_HEAD, norm_q_w=nq,
+                                      norm_k_w=nk, rope=table)
+
+    def qkv_split():
+        # cuBLAS QKV Linear per stream, then the fused norm + RoPE + scatter kernel.
+        torch.addmm(b_qkv_txt, x_txt[0], w_qkv_txt.t(), out=qkv[0, :t_loc].view(t_loc, 3 * hid))
+        torch.addmm(b_qkv_img, x_img[0], w_qkv_img.t(), out=qkv[0, t_loc:].view(i_loc, 3 * hid))
+        qkv_prologue_scatter(qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2], dst, world=world, rank=rank,
+                             norm_mode=_lib.NORM_HEAD, norm_q_w=nq, norm_k_w=nk, rope=table, seg0=t_loc)
+
     def step():
-        torch.matmul(x_txt, w_qkv_txt, out=qkv[:, :t_loc].view(1, t_loc, 3 * hid))
-        torch.matmul(x_img, w_qkv_img, out=qkv[:, t_loc:].view(1, i_loc, 3 * hid))
-        qkv_prologue_scatter(qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2],
-                             [[win.peer_ptr(r, o) for r in range(world)] for o in offs[:3]],
-                             world=world, rank=rank, norm_mode=_lib.NORM_HEAD, norm_q_w=nq,
-                             norm_k_w=nk, rope=table, seg0=t_loc)
+        qkv_split()
         win.barrier()
         attention_routed(recv[0], recv[1], recv[2], [win.peer_ptr(r, offs[3]) for r in range(world)],
                          (ls * h * DIM, h * DIM, DIM), world=world, rank=rank, seq_local=ls, seg0=t_loc)
@@ -259,8 +274,15 @@ def run_dit_layer(world: int, rank: int, dev, steps: int, warmup: int, group=Non
 
     ms_eager = time_steps(step, steps, warmup)
     ms = time_steps(step, steps, warmup, graph=True)  # the same work, launched from one graph
+    # The QKV stage alone, both ways (rank-local work; peers are not waited for).
+    ms_split = time_steps(qkv_split, steps, warmup, graph=True)
+    ms_fused = time_steps(qkv_fused, steps, warmup, graph=True)
+    if world > 1:
+        win.barrier()
+        torch.cuda.synchronize()
     win.close()
-    return {"ms": ms, "ms_eager": ms_eager, "my_launches": 4 if world > 1 else 2}
+    return {"ms": ms, "ms_eager": ms_eager, "ms_qkv_split": ms_split, "ms_qkv_fused": ms_fused,
+            "my_launches": 6 if world > 1 else 4}
 
 
 # ----------------------------------------------------------------- ring / CFG workloads (N > 1)
@@ -518,7 +540,7 @@ def main() -> None:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_ms = te.item()
     dit = run_dit_layer(world, rank, dev, max(5, args.steps), args.warmup)
-    extra = [dit["ms"], 0.0, 0.0, 0.0, 0.0, 0.0, dit["ms_eager"], 0.0]
+    extra = [dit["ms"], 0.0, 0.0, 0.0, 0.0, 0.0, dit["ms_eager"], 0.0, dit["ms_qkv_split"], dit["ms_qkv_fused"]]
     a2a = ring_res = cfg_res = fc_res = None
     if world > 1:
         a2a = time_scatter(uly)
@@ -534,7 +556,7 @@ def main() -> None:
         tmin = torch.tensor([extra[4]], device=dev, dtype=torch.float64)
         dist.all_reduce(tmin, op=dist.ReduceOp.MIN)
         td[4] = tmin[0]
-    dit_ms, a2a_ms, ring_ms, cfg_ms, a2a_gbs, fc_ms, dit_ms_eager, cfg_ms_eager = td.tolist()
+    dit_ms, a2a_ms, ring_ms, cfg_ms, a2a_gbs, fc_ms, dit_ms_eager, cfg_ms_eager, qkv_split_ms, qkv_fused_ms = td.tolist()
     dev_err = _lib.device_error()
 
     if rank == 0:
@@ -572,6 +594,9 @@ def main() -> None:
             "dit_layer": {"workload": DIT_WORKLOAD, "tokens_per_s": (DIT["img"] + DIT["txt"]) / (dit_ms * 1e-3),
                           "ms_per_layer": dit_ms, "ms_per_layer_eager": dit_ms_eager,
                           "launch": "one CUDA graph per layer (ms_per_layer_eager: the same calls from Python)",
+                          "qkv_stage_ms": {"cublas_addmm_plus_prologue_scatter": qkv_split_ms,
+                                           "fused_tcgen05_gemm_prologue_scatter": qkv_fused_ms,
+                                           "in_layer": "cublas_addmm_plus_prologue_scatter"},
                           "tflops": dit_layer_flops() / (dit_ms * 1e-3) / 1e12,
                           "frac_of_bf16_peak": dit_layer_flops() / (dit_ms * 1e-3) / 1e12 / (world * peaks["bf16_tflops"]),
                           "parallelism": f"ulysses{world}"},

@@ -114,6 +114,22 @@ class SeqGatherDesc(ctypes.Structure):
     ]
 
 
+class QkvGemmDesc(ctypes.Structure):
+    _fields_ = [
+        ("world", ctypes.c_int32),
+        ("rank", ctypes.c_int32),
+        ("m", ctypes.c_int32),
+        ("k", ctypes.c_int32),
+        ("heads", ctypes.c_int32),
+        ("seq_local", ctypes.c_int32),
+        ("row0", ctypes.c_int32),
+        ("seg0", ctypes.c_int32),
+        ("norm_mode", ctypes.c_int32),
+        ("eps", ctypes.c_float),
+        ("x_row_stride", ctypes.c_int64),
+    ]
+
+
 NORM_NONE, NORM_HIDDEN, NORM_HEAD = 0, 1, 2
 
 
@@ -174,6 +190,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "dgxm_ring_attn_fwd_noalloc": (ctypes.c_int, [_P, ctypes.POINTER(AttnDesc), _P, _P, _P, _P, _P,
                                                   _P]),
     "dgxm_full_context_window_bytes": (ctypes.c_int64, [ctypes.POINTER(AttnDesc), _I32]),
+    "dgxm_qkv_gemm_prologue_scatter": (ctypes.c_int, [ctypes.POINTER(QkvGemmDesc), _P, _P, _P, _P, _P, _P,
+                                                      _P, _P]),
     "dgxm_cfg_combine": (ctypes.c_int, [_P, _P, ctypes.c_int64, _I32, ctypes.c_double, _P, _P]),
     "dgxm_seq_allgather": (ctypes.c_int, [_P, ctypes.POINTER(SeqGatherDesc), _P, ctypes.c_int64, _P]),
     "dgxm_shared_amax_scale": (ctypes.c_int, [_P, _P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,

@@ -42,6 +42,12 @@
 #ifndef DGXM_SM_POLY_MOD
 #define DGXM_SM_POLY_MOD 8
 #endif
+#ifndef DGXM_SM_PAIR_BARRIER
+#define DGXM_SM_PAIR_BARRIER 1  // exchange row halves over a 64-thread barrier per warp pair
+#endif
+#ifndef DGXM_SM_THR_BF16
+#define DGXM_SM_THR_BF16 8.0f  // stale-max threshold of the bf16 kernel (log2 units)
+#endif
 
 namespace dgxm {
 
@@ -68,7 +74,7 @@ struct AttnCfg {
   static constexpr int kPCols = kTileRows * kEltBytes / 4;  // TMEM columns holding P
   // Stale-max threshold (log2 units) below which the running max is kept and
   // O is not rescaled; P values then stay below 2^kThr.
-  static constexpr float kThr = FP8 ? 4.0f : 8.0f;
+  static constexpr float kThr = FP8 ? 4.0f : DGXM_SM_THR_BF16;
   // e4m3 probabilities are stored scaled by 2^4 so typical values sit in the
   // normal range; the epilogue divides the factor back out.
   static constexpr float kPScale = FP8 ? 16.0f : 1.0f;
@@ -376,6 +382,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
     const int sub = warp & 3;        // TMEM lane quarter this warp may access
     const int r = sub * 32 + lane;   // row within the tile
     const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
+    // The two threads of a row sit in warps sub and sub + 4 of the group; they
+    // meet on a barrier of their own warp pair, or of the whole group.
+    const int xbar_id = DGXM_SM_PAIR_BARRIER ? 1 + t * 4 + sub : 1 + t;
+    const int xbar_threads = DGXM_SM_PAIR_BARRIER ? 64 : 256;
     const uint32_t tS = tmem + lane_off + t * 128 + c * 64;
     const uint32_t tP = tmem + lane_off + t * 128 + c * (C::kPCols / 2);
     const uint32_t tO = tmem + lane_off + 256 + t * 128 + c * 64;
@@ -473,7 +483,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
       // Every warp of the group arrives here exactly once per iteration, and
       // all of them take the same stop decision, so the barrier counts of
       // later iterations can never mismatch.
-      if (named_barrier_or(1 + t, 256, !got || *abort_flag != 0)) {
+      if (named_barrier_or(xbar_id, xbar_threads, !got || *abort_flag != 0)) {
         ok = false;
         break;
       }
@@ -557,7 +567,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
     // so the barrier is reached even when a wait above gave up).
     float* lsum = xmax + (8 + t * 2) * 128;
     lsum[c * 128 + r] = l_run;
-    named_barrier_sync(1 + t, 256);
+    named_barrier_sync(xbar_id, xbar_threads);
     const float l_row = l_run + lsum[(c ^ 1) * 128 + r];
     if (!ok) {
       raise_abort(abort_flag, kErrSoftmaxTimeout);

@@ -14,4 +14,5 @@
 #include "full_context.cu"
 #include "shard.cu"
 #include "cfg.cu"
+#include "qkv_gemm.cu"
 #include "prologue.cu"

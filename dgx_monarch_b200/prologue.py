@@ -59,6 +59,43 @@ def qkv_prologue_scatter(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, dst_
                "dgxm_qkv_prologue_scatter")
 
 
+def qkv_gemm_prologue_scatter(x: torch.Tensor, w_qkv: torch.Tensor, dst_ptrs: list[list[int]], *,
+                              world: int, rank: int, seq_local: int, row0: int = 0, seg0: int = 0,
+                              bias: torch.Tensor | None = None, norm_mode: int = _lib.NORM_NONE,
+                              norm_q_w: torch.Tensor | None = None, norm_k_w: torch.Tensor | None = None,
+                              eps: float = 1e-6, rope: torch.Tensor | None = None, stream=None) -> None:
+    """The QKV Linear of one token stream fused with per-head Q/K RMSNorm,
+    RoPE and the sequence->head scatter (dgxm_qkv_gemm_prologue_scatter).
+
+    x: (m, k) or (1, m, k) bf16 rows, contiguous features; w_qkv: the Linear
+    weight (3 * heads * 128, k); dst_ptrs[t][r]: rank r's (world * seq_local,
+    heads / world, 128) receive tensor t; rope: (seq_local, 64, 2) fp32."""
+    x2 = x.reshape(-1, x.shape[-1]) if x.ndim == 3 else x
+    if x.ndim == 3 and x.shape[0] != 1:
+        raise ValueError("the fused QKV kernel takes one batch item per call")
+    m, k = x2.shape
+    n = w_qkv.shape[0]
+    if x2.dtype != torch.bfloat16 or w_qkv.dtype != torch.bfloat16 or x2.stride(1) != 1 or not w_qkv.is_contiguous():
+        raise ValueError("x and w_qkv must be bf16 with contiguous features")
+    if w_qkv.shape[1] != k or n % 384:
+        raise ValueError(f"w_qkv {tuple(w_qkv.shape)} is not a (3 * heads * 128, {k}) Linear weight")
+    if rope is not None and (rope.dtype != torch.float32 or not rope.is_contiguous()
+                             or tuple(rope.shape) != (seq_local, 64, 2)):
+        raise ValueError("rope must be a contiguous fp32 (seq_local, 64, 2) table")
+    if bias is not None and (bias.dtype != torch.bfloat16 or bias.numel() != n or not bias.is_contiguous()):
+        raise ValueError("bias must be a contiguous bf16 vector of the Linear's outputs")
+    desc = _lib.QkvGemmDesc()
+    desc.world, desc.rank, desc.m, desc.k = world, rank, m, k
+    desc.heads, desc.seq_local, desc.row0, desc.seg0 = n // 384, seq_local, row0, seg0
+    desc.norm_mode, desc.eps, desc.x_row_stride = norm_mode, eps, x2.stride(0)
+    dst = (ctypes.c_void_p * (3 * world))(*[p for row in dst_ptrs for p in row])
+    stream = stream or torch.cuda.current_stream(x.device)
+    ptr = lambda t: None if t is None else t.data_ptr()
+    _lib.check(_lib.load().dgxm_qkv_gemm_prologue_scatter(
+        ctypes.byref(desc), x2.data_ptr(), w_qkv.data_ptr(), ptr(bias), ptr(norm_q_w), ptr(norm_k_w),
+        ptr(rope), dst, stream.cuda_stream), "dgxm_qkv_gemm_prologue_scatter")
+
+
 def quantize_e4m3_per_head(x: torch.Tensor, out: torch.Tensor | None = None,
                            descale: torch.Tensor | None = None, stream=None):
     """(e4m3 values, fp32 per-head descale = absmax / 448) of a bf16 (B, L, H, 128) tensor."""

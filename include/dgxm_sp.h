@@ -417,6 +417,42 @@ int dgxm_shared_amax_scale(dgxm_comm* comm, const void* x, int64_t rows, int64_t
                            int64_t row_stride, int32_t dtype, float divisor, void* scale_out,
                            float* amax_out, void* stream);
 
+/* ------------------------------------------------------------ fused QKV projection */
+/*
+ * y = x W^T + bias for one token stream of this rank (x: m rows of k bf16
+ * features, row stride x_row_stride elements; W: the Linear weight,
+ * (3 * heads * 128, k) bf16 row-major; bias: 3 * heads * 128 bf16 or NULL),
+ * rounded to bf16, then per head: q and k through the per-head RMSNorm
+ * (norm_mode DGXM_NORM_HEAD: bf16(y * rsqrt(mean(y^2) + eps)) then
+ * bf16(n * w), weights of 128 bf16 or NULL) and RoPE (rope: (seq_local, 64, 2)
+ * fp32 cos/sin by local row, or NULL), and every 128-wide head row stored into
+ * dst[t * world + r] -- rank r's contiguous (world * seq_local, heads/world,
+ * 128) bf16 receive tensor t (0 q, 1 k, 2 v) -- at the gathered row of local
+ * row row0 + i (joint order seg0 as in dgxm_a2a_desc).  One tcgen05 kernel:
+ * the QKV Linear, the QKNorm and RoPE of the Flux/Krea2 blocks and the
+ * sequence->head all-to-all (adapters/usp_full_axis.py:27-29).  Batch 1 per
+ * call; the text and image streams of a joint block are two calls with their
+ * own weights and row0.  Follow with dgxm_comm_barrier before any rank reads
+ * its receive tensors.
+ */
+typedef struct dgxm_qkv_gemm_desc {
+  int32_t world;
+  int32_t rank;
+  int32_t m;          /* rows of x in this call */
+  int32_t k;          /* input features; a multiple of 8 */
+  int32_t heads;      /* query heads (== key/value heads); heads % world == 0 */
+  int32_t seq_local;  /* rows this rank holds over all streams */
+  int32_t row0;       /* local row of x's first row */
+  int32_t seg0;       /* joint order: leading rows per rank (0 = rank-major) */
+  int32_t norm_mode;  /* DGXM_NORM_NONE or DGXM_NORM_HEAD */
+  float eps;
+  int64_t x_row_stride; /* elements; a multiple of 8 */
+} dgxm_qkv_gemm_desc;
+
+int dgxm_qkv_gemm_prologue_scatter(const dgxm_qkv_gemm_desc* desc, const void* x, const void* w_qkv,
+                                   const void* bias, const void* norm_q_w, const void* norm_k_w,
+                                   const float* rope, void* const* dst, void* stream);
+
 /* ------------------------------------------------------------ CFG combine */
 /*
  * out = uncond + (cond - uncond) * cfg_scale over n contiguous elements of

@@ -142,3 +142,89 @@ def test_quantize_is_bit_exact_against_torch(lib, shape):
     want = (x.float() / want_scale.view(1, 1, -1, 1)).to(torch.float8_e4m3fn)
     assert torch.equal(descale, want_scale)
     assert torch.equal(q8.view(torch.uint8), want.view(torch.uint8))
+
+
+def _within_ulps(got, want, ulps):
+    g, w = got.float(), want.float()
+    tol = ulps * 2.0 ** -7 * torch.maximum(g.abs(), w.abs()) + 1e-5
+    return ((g - w).abs() > tol).float().mean().item()
+
+
+@pytest.mark.parametrize("hidden,heads,t_loc,i_loc,rope,bias", [
+    (512, 4, 40, 300, True, True),       # tails below and above one 128-row tile
+    (3072, 24, 64, 300, True, False),    # the C2 block width: 216 tiles over 148 SMs, 48-stage ring wrap
+    (512, 4, 0, 129, False, True),       # image stream only, no RoPE
+])
+def test_fused_qkv_gemm_prologue_matches_separate_ops(lib, hidden, heads, t_loc, i_loc, rope, bias):
+    """The QKV Linear + per-head QKNorm + RoPE + sequence->head scatter in one
+    tcgen05 kernel, against the separate ops in torch (fp32 GEMM rounded to
+    bf16, then the unfused norm / RoPE) and the oracle's all-to-all layout,
+    two ranks emulated on one GPU in the joint [text, image] order.  The GEMM
+    sums in a different order from torch, so a value may land one bf16 ulp
+    away; the fraction of such values is bounded, V's rows differ only there."""
+    from dgx_monarch_b200 import _lib
+    from dgx_monarch_b200.prologue import qkv_gemm_prologue_scatter, rope_table
+
+    world, eps = 2, 1e-6
+    ls = t_loc + i_loc
+    g = torch.Generator(device="cuda").manual_seed(51)
+    w = lambda *shape, s=0.02: (s * torch.randn(*shape, device="cuda", generator=g)).bfloat16()
+    n = 3 * heads * 128
+    w_txt, w_img = w(n, hidden), w(n, hidden)
+    b_txt = w(n, s=0.5) if bias else None
+    b_img = w(n, s=0.5) if bias else None
+    nq_t, nk_t, nq_i, nk_i = ((1 + w(128, s=0.1)).contiguous() for _ in range(4))
+    xs = [(w(t_loc, hidden, s=1.0), w(i_loc, hidden, s=1.0)) for _ in range(world)]
+    tables = []
+    for r in range(world):
+        rows = torch.arange(r * ls, (r + 1) * ls, device="cuda")
+        pos = torch.stack((rows // 100, (rows // 10) % 10, rows % 10), dim=1)
+        tables.append(rope_table(pos, [16, 56, 56]) if rope else None)
+    hl = heads // world
+    recv = [[torch.zeros(world * ls, hl, 128, device="cuda", dtype=torch.bfloat16) for _ in range(world)]
+            for _ in range(3)]
+    ptrs = [[recv[t][r].data_ptr() for r in range(world)] for t in range(3)]
+    for r in range(world):
+        x_t, x_i = xs[r]
+        for x, wq, bb, row0, nq, nk in ((x_t, w_txt, b_txt, 0, nq_t, nk_t), (x_i, w_img, b_img, t_loc, nq_i, nk_i)):
+            if x.shape[0] == 0:
+                continue
+            qkv_gemm_prologue_scatter(x, wq, ptrs, world=world, rank=r, seq_local=ls, row0=row0, seg0=t_loc,
+                                      bias=bb, norm_mode=_lib.NORM_HEAD, norm_q_w=nq, norm_k_w=nk, eps=eps,
+                                      rope=tables[r])
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    # The separate ops: Linear per stream (fp32 sum, bf16 output), then norm + RoPE.
+    want_local = [[None] * world for _ in range(3)]
+    for r in range(world):
+        x_t, x_i = xs[r]
+        parts = []
+        for x, wq, bb, nq, nk in ((x_t, w_txt, b_txt, nq_t, nk_t), (x_i, w_img, b_img, nq_i, nk_i)):
+            y = x.double() @ wq.double().T
+            if bb is not None:
+                y = y + bb.double()
+            y = y.float().bfloat16().reshape(1, x.shape[0], 3, heads, 128)
+            parts.append((y, nq, nk))
+        for t in range(3):
+            rows = []
+            for y, nq, nk in parts:
+                tab = None
+                if tables[r] is not None:
+                    tab = tables[r][:t_loc] if y is parts[0][0] and t_loc else tables[r][t_loc:]
+                v = y[:, :, t]
+                rows.append(_ref_norm_rope(v, (nq, nk)[t], "head", eps, tab) if t < 2 else v)
+            want_local[t][r] = torch.cat(rows, dim=1)
+    order = usp.RankMajorJointOrder(t_loc, i_loc)
+    for t in range(3):
+        # Stock order on the gathered axis: every rank's text rows, then every rank's image rows.
+        gathered = [x[0].float().cpu().numpy() for x in want_local[t]]
+        full = np.concatenate([np.concatenate([g_[:t_loc] for g_ in gathered]),
+                               np.concatenate([g_[t_loc:] for g_ in gathered])])
+        for r in range(world):
+            want = torch.from_numpy(full[:, r * hl:(r + 1) * hl]).cuda()
+            frac = _within_ulps(recv[t][r], want, 2 if t < 2 else 1)
+            assert frac <= 2e-3, f"tensor {t} rank {r}: {frac:.2e} of values beyond the ulp bound"
+            # No value is further off than two ulps of the largest magnitude.
+            diff = (recv[t][r].float() - want).abs().max().item()
+            assert diff <= 2.0 ** -6 * want.abs().max().item() + 1e-3, f"tensor {t} rank {r}: max-abs {diff}"
+    assert order.text_rows == t_loc
