@@ -9,7 +9,9 @@
 //
 // HBM-bound: one warp per (batch, row, head) row of head_dim = 128 values;
 // each lane owns four consecutive values, so every part's row is read with one
-// fully coalesced 256-byte (bf16) or 512-byte (fp32) warp access.
+// fully coalesced 256-byte (bf16) or 512-byte (fp32) warp access.  The common
+// part counts (the ring degrees) are compiled in, so all of a row's loads are
+// in flight at once.
 #include "common.h"
 #include "ptx.cuh"
 
@@ -26,8 +28,24 @@ struct MergeParams {
   int batch, rows, heads;
 };
 
-template <bool PART_F32, bool OUT_F32>
+template <bool PART_F32>
+__device__ __forceinline__ float4 load_part(const void* base, int64_t elem) {
+  if constexpr (PART_F32) {
+    return *reinterpret_cast<const float4*>(static_cast<const float*>(base) + elem);
+  } else {
+    const uint2 v = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(base) + elem);
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.x));
+    const float2 c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.y));
+    return make_float4(a.x, a.y, c.x, c.y);
+  }
+}
+
+// NP > 0 fixes the part count at compile time: every part's row and LSE is
+// loaded before the first is used, so a warp keeps NP loads in flight
+// instead of one (NP == 0 loops over p.n parts).
+template <bool PART_F32, bool OUT_F32, int NP>
 __global__ void __launch_bounds__(256) lse_merge_kernel(const __grid_constant__ MergeParams p) {
+  constexpr int kSlots = NP > 0 ? NP : 1;
   const int warps_per_block = blockDim.x >> 5;
   const int64_t total = static_cast<int64_t>(p.batch) * p.rows * p.heads;
   const int lane = threadIdx.x & 31;
@@ -39,43 +57,66 @@ __global__ void __launch_bounds__(256) lse_merge_kernel(const __grid_constant__ 
     const int row = static_cast<int>(br % p.rows);
     const int b = static_cast<int>(br / p.rows);
     const int64_t lse_idx = (static_cast<int64_t>(b) * p.heads + h) * p.rows + row;
-    float mx = -INFINITY;
-    for (int i = 0; i < p.n; ++i) mx = fmaxf(mx, p.lse[i][lse_idx]);
-    float wsum = 0.f;
-    float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
     const int64_t elem = item * 128 + lane * 4;
-    for (int i = 0; i < p.n; ++i) {
-      const float li = p.lse[i][lse_idx];
-      // A part with lse = -inf saw no keys for this row and carries no weight.
-      const float w = (li == -INFINITY) ? 0.f : __expf(li - mx);
-      wsum += w;
-      float x0, x1, x2, x3;
-      if constexpr (PART_F32) {
-        const float4 v = *reinterpret_cast<const float4*>(static_cast<const float*>(p.out[i]) + elem);
-        x0 = v.x; x1 = v.y; x2 = v.z; x3 = v.w;
-      } else {
-        const uint2 v = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(p.out[i]) + elem);
-        const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.x));
-        const float2 c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.y));
-        x0 = a.x; x1 = a.y; x2 = c.x; x3 = c.y;
+    float mx = -INFINITY, wsum = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if constexpr (NP > 0) {
+      float li[kSlots];
+      float4 xv[kSlots];
+#pragma unroll
+      for (int i = 0; i < NP; ++i) {
+        li[i] = p.lse[i][lse_idx];
+        xv[i] = load_part<PART_F32>(p.out[i], elem);
       }
-      acc0 = fmaf(w, x0, acc0);
-      acc1 = fmaf(w, x1, acc1);
-      acc2 = fmaf(w, x2, acc2);
-      acc3 = fmaf(w, x3, acc3);
+#pragma unroll
+      for (int i = 0; i < NP; ++i) mx = fmaxf(mx, li[i]);
+#pragma unroll
+      for (int i = 0; i < NP; ++i) {
+        // A part with lse = -inf saw no keys for this row and carries no weight.
+        const float w = (li[i] == -INFINITY) ? 0.f : __expf(li[i] - mx);
+        wsum += w;
+        acc.x = fmaf(w, xv[i].x, acc.x);
+        acc.y = fmaf(w, xv[i].y, acc.y);
+        acc.z = fmaf(w, xv[i].z, acc.z);
+        acc.w = fmaf(w, xv[i].w, acc.w);
+      }
+    } else {
+      for (int i = 0; i < p.n; ++i) mx = fmaxf(mx, p.lse[i][lse_idx]);
+      for (int i = 0; i < p.n; ++i) {
+        const float li = p.lse[i][lse_idx];
+        const float w = (li == -INFINITY) ? 0.f : __expf(li - mx);
+        wsum += w;
+        const float4 x = load_part<PART_F32>(p.out[i], elem);
+        acc.x = fmaf(w, x.x, acc.x);
+        acc.y = fmaf(w, x.y, acc.y);
+        acc.z = fmaf(w, x.z, acc.z);
+        acc.w = fmaf(w, x.w, acc.w);
+      }
     }
     const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
     if constexpr (OUT_F32) {
       *reinterpret_cast<float4*>(static_cast<float*>(p.dst) + elem) =
-          make_float4(acc0 * inv, acc1 * inv, acc2 * inv, acc3 * inv);
+          make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
     } else {
       uint2 w;
-      w.x = pack_bf16x2(acc0 * inv, acc1 * inv);
-      w.y = pack_bf16x2(acc2 * inv, acc3 * inv);
+      w.x = pack_bf16x2(acc.x * inv, acc.y * inv);
+      w.y = pack_bf16x2(acc.z * inv, acc.w * inv);
       *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(p.dst) + elem) = w;
     }
     if (lane == 0 && p.dst_lse != nullptr)
       p.dst_lse[lse_idx] = wsum > 0.f ? mx + __logf(wsum) : -INFINITY;
+  }
+}
+
+template <bool PART_F32, bool OUT_F32>
+static void launch_merge(const MergeParams& prm, int blocks, cudaStream_t st) {
+  switch (prm.n) {
+    case 1: lse_merge_kernel<PART_F32, OUT_F32, 1><<<blocks, 256, 0, st>>>(prm); break;
+    case 2: lse_merge_kernel<PART_F32, OUT_F32, 2><<<blocks, 256, 0, st>>>(prm); break;
+    case 3: lse_merge_kernel<PART_F32, OUT_F32, 3><<<blocks, 256, 0, st>>>(prm); break;
+    case 4: lse_merge_kernel<PART_F32, OUT_F32, 4><<<blocks, 256, 0, st>>>(prm); break;
+    case 8: lse_merge_kernel<PART_F32, OUT_F32, 8><<<blocks, 256, 0, st>>>(prm); break;
+    default: lse_merge_kernel<PART_F32, OUT_F32, 0><<<blocks, 256, 0, st>>>(prm); break;
   }
 }
 
@@ -127,11 +168,11 @@ extern "C" int dgxm_lse_merge(int32_t batch, int32_t rows, int32_t heads, int32_
   const int blocks = static_cast<int>(want < int64_t(sms) * 16 ? want : int64_t(sms) * 16);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (part_f32) {
-    if (out_f32) lse_merge_kernel<true, true><<<blocks, 256, 0, st>>>(prm);
-    else lse_merge_kernel<true, false><<<blocks, 256, 0, st>>>(prm);
+    if (out_f32) launch_merge<true, true>(prm, blocks, st);
+    else launch_merge<true, false>(prm, blocks, st);
   } else {
-    if (out_f32) lse_merge_kernel<false, true><<<blocks, 256, 0, st>>>(prm);
-    else lse_merge_kernel<false, false><<<blocks, 256, 0, st>>>(prm);
+    if (out_f32) launch_merge<false, true>(prm, blocks, st);
+    else launch_merge<false, false>(prm, blocks, st);
   }
   DGXM_CUDA_TRY(cudaGetLastError());
   return DGXM_OK;

@@ -144,6 +144,108 @@ __global__ void __launch_bounds__(kPrologueThreads) qkv_prologue_scatter_kernel(
   }
 }
 
+// Per-head norm (or none): one warp per (row, tensor, head).  Lane l owns
+// values [4l, 4l + 4) of the head row -- two RoPE pairs -- and the head's sum
+// of squares is the lane sums reduced by the same xor shuffle as the
+// row-per-block kernel above, so both give identical bits.  Loads and the
+// 256-byte peer store of a head row are one coalesced warp access each, and
+// no block barrier is needed.
+// Per-head norm (or none): each half-warp owns one (tensor, head) row of a
+// token -- sub-lane s holds values [8s, 8s + 8), four RoPE pairs -- so a warp
+// reads and writes two 256-byte head rows per access, and every half-warp has
+// two rows in flight before it uses either.  The head's sum of squares is the
+// sub-lane sums reduced over the half-warp; no block barrier is needed.
+__device__ __forceinline__ uint4 prologue_head_math(const PrologueParams& p, uint4 raw, int t, int sub,
+                                                   const float* rope_row) {
+  float x[8];
+  const __nv_bfloat162* pr = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(pr[i]);
+    x[2 * i] = f.x;
+    x[2 * i + 1] = f.y;
+  }
+  // The reduction runs on every lane whatever row it holds (the norm mode is
+  // uniform over the kernel), so a warp whose halves hold a k row and a v row
+  // still meets every shuffle.
+  float ss = 0.f;
+  if (p.norm_mode == DGXM_NORM_HEAD) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss = fmaf(x[i], x[i], ss);
+    for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  }
+  if (t == 2 || (p.norm_mode != DGXM_NORM_HEAD && rope_row == nullptr)) return raw;
+  if (p.norm_mode == DGXM_NORM_HEAD) {
+    const float sc = rsqrtf(ss / 128.f + p.eps);
+    const __nv_bfloat16* w = p.norm_w[t];
+    uint4 wv = make_uint4(0u, 0u, 0u, 0u);
+    if (w != nullptr) wv = __ldg(reinterpret_cast<const uint4*>(w) + sub);  // this lane's 8 weights
+    const __nv_bfloat16* wl = reinterpret_cast<const __nv_bfloat16*>(&wv);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float n = __bfloat162float(__float2bfloat16(x[i] * sc));
+      if (w != nullptr) n = __bfloat162float(__float2bfloat16(n * __bfloat162float(wl[i])));
+      x[i] = n;
+    }
+  }
+  if (rope_row != nullptr) {
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const float4 cs = __ldg(reinterpret_cast<const float4*>(rope_row) + 2 * sub + q);
+      float* y = x + 4 * q;
+      const float y0 = fmaf(-cs.y, y[1], cs.x * y[0]), y1 = fmaf(cs.x, y[1], cs.y * y[0]);
+      const float y2 = fmaf(-cs.w, y[3], cs.z * y[2]), y3 = fmaf(cs.z, y[3], cs.w * y[2]);
+      y[0] = y0; y[1] = y1; y[2] = y2; y[3] = y3;
+    }
+  }
+  uint4 out;
+  uint32_t* o = reinterpret_cast<uint32_t*>(&out);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
+    o[i] = *reinterpret_cast<uint32_t*>(&v);
+  }
+  return out;
+}
+
+__global__ void __launch_bounds__(256) qkv_prologue_head_kernel(const __grid_constant__ PrologueParams p) {
+  const int hl = p.heads / p.world;
+  const int items = 3 * p.heads;  // (tensor, head) rows of one token
+  const int lane = threadIdx.x & 31, sub = lane & 15;
+  const int worker = threadIdx.x >> 4, workers = blockDim.x >> 4;  // half-warps
+  const int64_t seq_full = static_cast<int64_t>(p.seq_local) * p.world;
+  for (int64_t token = blockIdx.x; token < static_cast<int64_t>(p.batch) * p.seq_local; token += gridDim.x) {
+    const int b = static_cast<int>(token / p.seq_local);
+    const int l = static_cast<int>(token - static_cast<int64_t>(b) * p.seq_local);
+    const int64_t grow = static_cast<int64_t>(b) * seq_full + gathered_row_p(p.rank, l, p.seq_local, p.world, p.seg0);
+    const float* rope_row = p.rope == nullptr ? nullptr : p.rope + b * p.rope_sb + static_cast<int64_t>(l) * 128;
+    // Both half-warps of a warp run the same trip count, so the shuffles of
+    // the norm always see full warps.
+    const int rounds = (items + 2 * workers - 1) / (2 * workers);
+    for (int k = 0; k < rounds; ++k) {
+      const int i0 = worker + 2 * workers * k, i1 = i0 + workers;
+      const bool v0 = i0 < items, v1 = i1 < items;
+      const int c0 = v0 ? i0 : 0, c1 = v1 ? i1 : 0;
+      const int t0 = c0 / p.heads, h0 = c0 - t0 * p.heads;
+      const int t1 = c1 / p.heads, h1 = c1 - t1 * p.heads;
+      const uint4 r0 = __ldg(reinterpret_cast<const uint4*>(p.src[t0] + b * p.s_sb[t0] + static_cast<int64_t>(l) * p.s_sl[t0] +
+                                                            h0 * p.s_sh[t0]) + sub);
+      const uint4 r1 = __ldg(reinterpret_cast<const uint4*>(p.src[t1] + b * p.s_sb[t1] + static_cast<int64_t>(l) * p.s_sl[t1] +
+                                                            h1 * p.s_sh[t1]) + sub);
+      const uint4 o0 = prologue_head_math(p, r0, t0, sub, t0 < 2 ? rope_row : nullptr);
+      const uint4 o1 = prologue_head_math(p, r1, t1, sub, t1 < 2 ? rope_row : nullptr);
+      if (v0) {
+        const int own = h0 / hl;
+        reinterpret_cast<uint4*>(p.dst[t0][own] + (grow * hl + (h0 - own * hl)) * 256)[sub] = o0;
+      }
+      if (v1) {
+        const int own = h1 / hl;
+        reinterpret_cast<uint4*>(p.dst[t1][own] + (grow * hl + (h1 - own * hl)) * 256)[sub] = o1;
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------- FP8
 struct QuantParams {
   const char* x;
@@ -254,6 +356,8 @@ extern "C" int dgxm_qkv_prologue_scatter(const dgxm_prologue_desc* d, const void
   }
   if (d->norm_mode != DGXM_NORM_NONE && (norm_q_w == nullptr) != (norm_k_w == nullptr))
     return fail(DGXM_ERR_INVALID, "give both norm weights or neither");
+  if ((reinterpret_cast<uintptr_t>(norm_q_w) | reinterpret_cast<uintptr_t>(norm_k_w)) % 16)
+    return fail(DGXM_ERR_INVALID, "norm weights must be 16-byte aligned");
   p.norm_w[0] = static_cast<const __nv_bfloat16*>(norm_q_w);
   p.norm_w[1] = static_cast<const __nv_bfloat16*>(norm_k_w);
   p.rope = rope;
@@ -270,6 +374,13 @@ extern "C" int dgxm_qkv_prologue_scatter(const dgxm_prologue_desc* d, const void
   DGXM_CUDA_TRY(cudaGetDevice(&dev));
   DGXM_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   const int64_t rows = static_cast<int64_t>(d->batch) * d->seq_local;
+  if (d->norm_mode != DGXM_NORM_HIDDEN) {
+    // Per-head norm or none: nothing couples the heads of a row.
+    const int blocks = static_cast<int>(rows < int64_t(sms) * 16 ? rows : int64_t(sms) * 16);
+    qkv_prologue_head_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+    DGXM_CUDA_TRY(cudaGetLastError());
+    return DGXM_OK;
+  }
   const int blocks = static_cast<int>(rows < int64_t(sms) * 8 ? rows : int64_t(sms) * 8);
   qkv_prologue_scatter_kernel<<<blocks, kPrologueThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
   DGXM_CUDA_TRY(cudaGetLastError());

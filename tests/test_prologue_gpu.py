@@ -58,6 +58,8 @@ def _bits(t):
     ("hidden", 4, 40, [44, 42, 42]),   # Wan: norm over 5120, 3-axis RoPE
     ("head", 2, 24, [16, 56, 56]),     # Flux/Krea2: per-head QKNorm, axis 0 unused by images
     ("none", 2, 8, None),
+    ("head", 1, 5, [16, 56, 56]),      # an odd head count: a warp's halves straddle the k / v rows
+    ("head", 3, 9, [16, 56, 56]),
 ])
 def test_prologue_matches_unfused_ops(lib, mode, world, heads, axes):
     from dgx_monarch_b200 import _lib
