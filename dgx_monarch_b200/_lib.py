@@ -192,6 +192,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "dgxm_full_context_window_bytes": (ctypes.c_int64, [ctypes.POINTER(AttnDesc), _I32]),
     "dgxm_qkv_gemm_prologue_scatter": (ctypes.c_int, [ctypes.POINTER(QkvGemmDesc), _P, _P, _P, _P, _P, _P,
                                                       _P, _P]),
+    "dgxm_copy_2d": (ctypes.c_int, [_P, ctypes.c_int64, _P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _P]),
     "dgxm_cfg_combine": (ctypes.c_int, [_P, _P, ctypes.c_int64, _I32, ctypes.c_double, _P, _P]),
     "dgxm_seq_allgather": (ctypes.c_int, [_P, ctypes.POINTER(SeqGatherDesc), _P, ctypes.c_int64, _P]),
     "dgxm_shared_amax_scale": (ctypes.c_int, [_P, _P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,

@@ -89,3 +89,20 @@ extern "C" int dgxm_device_error(int clear) {
   }
   return value;
 }
+
+// A strided copy between host and device memory (or within either): `height`
+// rows of `width` bytes, row pitches `dpitch` / `spitch`.  One copy-engine
+// transfer; the head-group slices of a (B, L, H, D) tensor are such copies.
+extern "C" int dgxm_copy_2d(void* dst, int64_t dpitch, const void* src, int64_t spitch, int64_t width,
+                            int64_t height, void* stream) {
+  using namespace dgxm;
+  if (width < 0 || height < 0 || dpitch < width || spitch < width)
+    return fail(DGXM_ERR_INVALID, "2-D copy of %lld x %lld bytes with pitches %lld / %lld", (long long)height,
+                (long long)width, (long long)dpitch, (long long)spitch);
+  if (width == 0 || height == 0) return DGXM_OK;
+  if (dst == nullptr || src == nullptr) return fail(DGXM_ERR_INVALID, "NULL 2-D copy pointer");
+  DGXM_CUDA_TRY(cudaMemcpy2DAsync(dst, static_cast<size_t>(dpitch), src, static_cast<size_t>(spitch),
+                                  static_cast<size_t>(width), static_cast<size_t>(height), cudaMemcpyDefault,
+                                  static_cast<cudaStream_t>(stream)));
+  return DGXM_OK;
+}

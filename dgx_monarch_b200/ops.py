@@ -237,3 +237,78 @@ def lse_merge(parts_out: list[torch.Tensor], parts_lse: list[torch.Tensor], *,
                                 out.data_ptr(), _dtype_code(out.dtype), lse_out.data_ptr(), stream)
     _lib.check(rc, "dgxm_lse_merge")
     return out, lse_out
+
+
+def copy_2d(dst: int, dpitch: int, src: int, spitch: int, width: int, height: int, stream) -> None:
+    """One strided copy-engine transfer (dgxm_copy_2d): height rows of width bytes."""
+    _lib.check(_lib.load().dgxm_copy_2d(dst, dpitch, src, spitch, width, height, stream.cuda_stream),
+               "dgxm_copy_2d")
+
+
+class HostStreamedAttention:
+    """Attention whose inputs and output live in pinned host memory, streamed
+    through the device one head group at a time.
+
+    Heads are independent, so the host->device copy of group g + 1 and the
+    device->host copy of group g - 1 (copy engines, one stream each way) run
+    while the tensor cores attend group g.  Each group's slice of a
+    (B, L, H, D) tensor is one strided copy per tensor.  The result is the
+    same bits as one attention_fwd call over the whole tensors.
+    """
+
+    def __init__(self, batch: int, q_len: int, kv_len: int, heads: int, kv_heads: int | None = None,
+                 head_dim: int = 128, *, device: torch.device, groups: int = 8) -> None:
+        kv_heads = heads if kv_heads is None else kv_heads
+        if heads % groups or kv_heads % groups:
+            raise ValueError(f"{groups} head groups do not split {heads} query / {kv_heads} key-value heads")
+        self.shape = (batch, q_len, kv_len, heads, kv_heads, head_dim)
+        self.groups, self.device = groups, device
+        dt = torch.bfloat16
+        self.q = torch.empty(batch, q_len, heads, head_dim, device=device, dtype=dt)
+        self.k = torch.empty(batch, kv_len, kv_heads, head_dim, device=device, dtype=dt)
+        self.v = torch.empty(batch, kv_len, kv_heads, head_dim, device=device, dtype=dt)
+        self.out = torch.empty(batch, q_len, heads, head_dim, device=device, dtype=dt)
+        self.copy_in = torch.cuda.Stream(device)
+        self.copy_out = torch.cuda.Stream(device)
+        self.launches_per_call = groups
+
+    def _slice(self, dst: torch.Tensor, src: torch.Tensor, g: int, stream) -> None:
+        """Head group g of a (B, L, H, D) tensor: B * L rows of (H / groups) heads."""
+        b, l, h, d = src.shape
+        hg = h // self.groups
+        elt = src.element_size()
+        off = g * hg * d * elt
+        copy_2d(dst.data_ptr() + off, h * d * elt, src.data_ptr() + off, h * d * elt, hg * d * elt, b * l, stream)
+
+    def __call__(self, q_host: torch.Tensor, k_host: torch.Tensor, v_host: torch.Tensor,
+                 out_host: torch.Tensor) -> torch.Tensor:
+        b, lq, lk, h, hkv, d = self.shape
+        for t, want in ((q_host, (b, lq, h, d)), (k_host, (b, lk, hkv, d)), (v_host, (b, lk, hkv, d)),
+                        (out_host, (b, lq, h, d))):
+            if tuple(t.shape) != want or not t.is_contiguous() or t.dtype != torch.bfloat16:
+                raise ValueError(f"host tensor {tuple(t.shape)} is not a contiguous bf16 {want}")
+        main = torch.cuda.current_stream(self.device)
+        self.copy_in.wait_stream(main)   # the device buffers are free once earlier work is done
+        self.copy_out.wait_stream(main)
+        hg, kg = h // self.groups, hkv // self.groups
+        loaded, done = [], []
+        for g in range(self.groups):
+            with torch.cuda.stream(self.copy_in):
+                for dst, src in ((self.q, q_host), (self.k, k_host), (self.v, v_host)):
+                    self._slice(dst, src, g, self.copy_in)
+                ev = torch.cuda.Event()
+                ev.record(self.copy_in)
+                loaded.append(ev)
+        for g in range(self.groups):
+            main.wait_event(loaded[g])
+            attention_fwd(self.q[:, :, g * hg:(g + 1) * hg], self.k[:, :, g * kg:(g + 1) * kg],
+                          self.v[:, :, g * kg:(g + 1) * kg], out=self.out[:, :, g * hg:(g + 1) * hg],
+                          return_lse=False)
+            ev = torch.cuda.Event()
+            ev.record(main)
+            self.copy_out.wait_event(ev)
+            self._slice(out_host, self.out, g, self.copy_out)
+        fin = torch.cuda.Event()
+        fin.record(self.copy_out)
+        main.wait_event(fin)
+        return out_host

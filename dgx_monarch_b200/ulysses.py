@@ -173,3 +173,69 @@ class UlyssesAttention:
             torch.cuda.synchronize(self.device)
             self.windows.close()
             self.windows = None
+
+
+class HostStreamedUlysses:
+    """Ulysses attention whose inputs and output live in pinned host memory,
+    streamed one head group at a time.
+
+    Each group of heads is a Ulysses step of its own (its heads divide the
+    Ulysses degree), so the host->device copy of group g + 1 and the
+    device->host copy of group g - 1 run on copy engines while group g is
+    scattered, attended and gathered.  Each group's output is first copied out
+    of the peer window on the compute stream, before any rank's next step can
+    write into that window.
+    """
+
+    def __init__(self, *, world: int, rank: int, batch: int, seq_local: int, heads: int, head_dim: int,
+                 device: torch.device, groups: int, group=None, generation: int = 0) -> None:
+        if heads % groups or (heads // groups) % world:
+            raise ValueError(f"{groups} head groups of {heads} heads do not split over {world} ranks")
+        self.groups, self.device = groups, device
+        self.shape = (batch, seq_local, heads, head_dim)
+        self.uly = UlyssesAttention(world=world, rank=rank, batch=batch, seq_local=seq_local,
+                                    heads=heads // groups, head_dim=head_dim, device=device, group=group,
+                                    generation=generation)
+        dt = torch.bfloat16
+        self.q, self.k, self.v, self.out = (torch.empty(batch, seq_local, heads, head_dim, device=device, dtype=dt)
+                                            for _ in range(4))
+        self.copy_in = torch.cuda.Stream(device)
+        self.copy_out = torch.cuda.Stream(device)
+        self.launches_per_call = groups * self.uly.launches_per_step
+
+    def __call__(self, q_host, k_host, v_host, out_host):
+        from .ops import copy_2d
+
+        b, ls, h, d = self.shape
+        for t in (q_host, k_host, v_host, out_host):
+            if tuple(t.shape) != self.shape or not t.is_contiguous() or t.dtype != torch.bfloat16:
+                raise ValueError(f"host tensor {tuple(t.shape)} is not a contiguous bf16 {self.shape}")
+        hg = h // self.groups
+        pitch, width, rows = h * d * 2, hg * d * 2, b * ls
+        main = torch.cuda.current_stream(self.device)
+        self.copy_in.wait_stream(main)
+        self.copy_out.wait_stream(main)
+        loaded = []
+        for g in range(self.groups):
+            off = g * width
+            for dst, src in ((self.q, q_host), (self.k, k_host), (self.v, v_host)):
+                copy_2d(dst.data_ptr() + off, pitch, src.data_ptr() + off, pitch, width, rows, self.copy_in)
+            ev = torch.cuda.Event()
+            ev.record(self.copy_in)
+            loaded.append(ev)
+        for g in range(self.groups):
+            sl = slice(g * hg, (g + 1) * hg)
+            main.wait_event(loaded[g])
+            self.uly.forward(self.q[:, :, sl], self.k[:, :, sl], self.v[:, :, sl], out=self.out[:, :, sl])
+            ev = torch.cuda.Event()
+            ev.record(main)
+            self.copy_out.wait_event(ev)
+            copy_2d(out_host.data_ptr() + g * width, pitch, self.out.data_ptr() + g * width, pitch, width, rows,
+                    self.copy_out)
+        fin = torch.cuda.Event()
+        fin.record(self.copy_out)
+        main.wait_event(fin)
+        return out_host
+
+    def close(self) -> None:
+        self.uly.close()

@@ -48,6 +48,12 @@ int dgxm_abi_version(void);
 /* Message describing the last failed call made on this thread ("" if none). */
 const char* dgxm_last_error_message(void);
 
+/* A strided copy (host <-> device or within either): height rows of width
+ * bytes with row pitches dpitch / spitch, one copy-engine transfer on the
+ * stream.  The head-group slices of a (B, L, H, D) tensor are such copies. */
+int dgxm_copy_2d(void* dst, int64_t dpitch, const void* src, int64_t spitch, int64_t width,
+                 int64_t height, void* stream);
+
 /* Read (and optionally clear) the device-side error word that bounded waits
  * set when they expire.  Synchronises the current device.  Returns 0 when no
  * kernel has reported a problem. */

@@ -273,3 +273,23 @@ def test_cfg_combine_is_bit_exact_against_torch(lib, dtype):
         want = u + (c - u) * 5.5
         assert torch.equal(cfg_combine(c, u, 5.5), want)
         assert torch.equal(cfg_combine(c, u, 5.5, out=c), want)
+
+
+@pytest.mark.parametrize("heads,kv_heads,groups", [(8, 8, 4), (8, 4, 2), (6, 6, 3)])
+def test_host_streamed_attention_equals_one_device_call(lib, heads, kv_heads, groups):
+    """Pinned host tensors streamed through the device by head groups give the
+    same bits as one attention call over the whole device tensors."""
+    from dgx_monarch_b200.ops import HostStreamedAttention, attention_fwd
+
+    g = torch.Generator(device="cuda").manual_seed(57)
+    q = torch.randn(2, 1000, heads, 128, device="cuda", generator=g).bfloat16()
+    k = torch.randn(2, 1300, kv_heads, 128, device="cuda", generator=g).bfloat16()
+    v = torch.randn(2, 1300, kv_heads, 128, device="cuda", generator=g).bfloat16()
+    want, _ = attention_fwd(q, k, v, return_lse=False)
+    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+    hout = torch.full(q.shape, float("nan"), dtype=torch.bfloat16).pin_memory()
+    streamed = HostStreamedAttention(2, 1000, 1300, heads, kv_heads, device=q.device, groups=groups)
+    for _ in range(2):  # a second call reuses the device buffers and streams
+        streamed(hq, hk, hv, hout)
+        torch.cuda.synchronize()
+        assert torch.equal(hout.cuda(), want)

@@ -474,3 +474,36 @@ def _graph_case(rank, world, dev):
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
 def test_captured_ulysses_step_replays_across_gpus():
     _spawn(_graph_case, 2)
+
+
+def _streamed_case(rank, world, dev):
+    """Ulysses attention over pinned host tensors streamed by head groups, each
+    group its own Ulysses step, against unsharded attention."""
+    from dgx_monarch_b200 import _lib
+    from dgx_monarch_b200.ulysses import HostStreamedUlysses
+    from tests.test_attn_gpu import BF16_MAX_ABS, BF16_REL_L2, reference_attention, rel_l2
+
+    check = Checks(rank)
+    heads, ls = 4 * world, 300
+    g = torch.Generator(device=dev).manual_seed(97)
+    q, k, v = (torch.randn(1, ls * world, heads, 128, device=dev, generator=g).bfloat16() for _ in range(3))
+    sl = slice(rank * ls, (rank + 1) * ls)
+    hq, hk, hv = (t[:, sl].contiguous().cpu().pin_memory() for t in (q, k, v))
+    hout = torch.full((1, ls, heads, 128), float("nan"), dtype=torch.bfloat16).pin_memory()
+    streamed = HostStreamedUlysses(world=world, rank=rank, batch=1, seq_local=ls, heads=heads, head_dim=128,
+                                   device=dev, groups=2, generation=16)
+    ref, _ = reference_attention(q, k, v)
+    for step in range(2):
+        streamed(hq, hk, hv, hout)
+        torch.cuda.synchronize()
+        got = hout.to(dev)
+        check.le((got.float() - ref[:, sl]).abs().max().item(), BF16_MAX_ABS, f"call {step} max abs")
+        check.le(rel_l2(got, ref[:, sl]), BF16_REL_L2, f"call {step} rel l2")
+    streamed.close()
+    check(_lib.device_error() == 0, f"device error word {_lib.device_error()}")
+    check.close()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
+def test_host_streamed_ulysses_across_gpus():
+    _spawn(_streamed_case, 2)
