@@ -284,16 +284,15 @@ __global__ void __launch_bounds__(1024) absmax_kernel(const __grid_constant__ Qu
   if (part == 0 && h < p.heads) atomicMax(reinterpret_cast<unsigned int*>(p.amax) + h, __float_as_uint(m));
 }
 
+// Blocks stride over (batch, row); threads over the row's (head, 16-byte
+// part) vectors, so the index math is a shift and a mask per vector.
 __global__ void __launch_bounds__(256) quantize_e4m3_kernel(const __grid_constant__ QuantParams p) {
-  const int64_t vecs = static_cast<int64_t>(p.batch) * p.rows * p.heads * 16;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < vecs;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int part = static_cast<int>(i % 16);
-    int64_t rem = i / 16;
-    const int h = static_cast<int>(rem % p.heads);
-    rem /= p.heads;
-    const int l = static_cast<int>(rem % p.rows);
-    const int b = static_cast<int>(rem / p.rows);
+  const int per_row = p.heads * 16;
+  for (int64_t row = blockIdx.x; row < static_cast<int64_t>(p.batch) * p.rows; row += gridDim.x) {
+    const int b = static_cast<int>(row / p.rows);
+    const int l = static_cast<int>(row - static_cast<int64_t>(b) * p.rows);
+    for (int v = threadIdx.x; v < per_row; v += blockDim.x) {
+    const int h = v >> 4, part = v & 15;
     const uint4 raw = __ldg(reinterpret_cast<const uint4*>(p.x + b * p.sb + l * p.sl + h * p.sh) + part);
     const __nv_bfloat162* pr = reinterpret_cast<const __nv_bfloat162*>(&raw);
     const float amax = fmaxf(p.amax[h], 1e-12f);
@@ -306,8 +305,9 @@ __global__ void __launch_bounds__(256) quantize_e4m3_kernel(const __grid_constan
       w[k] = pack_e4m3x4(__fdiv_rn(a.x, scale), __fdiv_rn(a.y, scale), __fdiv_rn(c.x, scale),
                          __fdiv_rn(c.y, scale));
     }
-    const int64_t o = ((static_cast<int64_t>(b) * p.rows + l) * p.heads + h) * 128 + part * 8;
+    const int64_t o = (row * p.heads + h) * 128 + part * 8;
     *reinterpret_cast<uint2*>(p.out + o) = make_uint2(w[0], w[1]);
+    }
   }
 }
 
@@ -415,14 +415,12 @@ extern "C" int dgxm_quantize_e4m3_per_head(int32_t batch, int32_t rows, int32_t 
   DGXM_CUDA_TRY(cudaGetDevice(&dev));
   DGXM_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   if (heads > 64) return fail(DGXM_ERR_UNSUPPORTED, "quantisation supports up to 64 heads, got %d", heads);
-  const int64_t vecs = static_cast<int64_t>(batch) * rows * heads * 16;
-  const int64_t want = (vecs + 255) / 256;
-  const int blocks = static_cast<int>(want < int64_t(sms) * 8 ? want : int64_t(sms) * 8);
   const int64_t nrows = static_cast<int64_t>(batch) * rows;
   const int amax_blocks = static_cast<int>(nrows < int64_t(sms) * 4 ? nrows : int64_t(sms) * 4);
   const int amax_threads = (heads * 16 + 31) / 32 * 32;
   absmax_kernel<<<amax_blocks, amax_threads, 0, st>>>(p);
-  quantize_e4m3_kernel<<<blocks, 256, 0, st>>>(p);
+  const int qblocks = static_cast<int>(nrows < int64_t(sms) * 8 ? nrows : int64_t(sms) * 8);
+  quantize_e4m3_kernel<<<qblocks, 256, 0, st>>>(p);
   descale_kernel<<<(heads + 127) / 128, 128, 0, st>>>(descale, heads);
   DGXM_CUDA_TRY(cudaGetLastError());
   return DGXM_OK;

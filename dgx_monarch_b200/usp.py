@@ -172,6 +172,8 @@ class B200SequenceParallelAttention:
         _check_pad_rows(k_l.shape[1] * p, kv_drop_rows)
         if p == 1 and g.ring_world == 1 and not self.fp8:
             return self._local(q_l, k_l, v_l, drop_rows, kv_drop_rows, bias_groups)
+        if p == 1 and g.ring_world == 1 and not (drop_rows or kv_drop_rows or bias_groups):
+            return self._local_fp8(q_l, k_l, v_l)
         if self.fp8 and (g.ring_world > 1 or drop_rows or kv_drop_rows or bias_groups):
             raise UnsupportedModelError(
                 "the B200 FP8 attention path runs pure Ulysses without pad rows; use the bf16 "
@@ -225,6 +227,26 @@ class B200SequenceParallelAttention:
         out, _ = attention_fwd(q, k, v, return_lse=False)
         return out
 
+    def _local_fp8(self, q, k, v):
+        """One rank, e4m3: quantise the caller's heads in place of a scatter
+        and attend into a fresh output (no window copy, no barrier)."""
+        from .prologue import quantize_e4m3_per_head
+
+        b, ls, h, d = q.shape
+        key = ("fp8_local", b, ls, k.shape[1], h, k.shape[2], d)
+        bufs = self._plans.get(key)
+        if bufs is None:
+            bufs = {"q8": torch.empty(q.shape, device=self.device, dtype=torch.float8_e4m3fn),
+                    "k8": torch.empty(k.shape, device=self.device, dtype=torch.float8_e4m3fn),
+                    "v8": torch.empty(v.shape, device=self.device, dtype=torch.float8_e4m3fn),
+                    "ds": [torch.empty(x.shape[2], device=self.device, dtype=torch.float32) for x in (q, k, v)]}
+            self._plans[key] = bufs
+        for src, dst, ds in zip((q, k, v), (bufs["q8"], bufs["k8"], bufs["v8"]), bufs["ds"]):
+            quantize_e4m3_per_head(src, out=dst, descale=ds)
+        out, _ = attention_fwd(bufs["q8"], bufs["k8"], bufs["v8"], q_descale=bufs["ds"][0],
+                               k_descale=bufs["ds"][1], v_descale=bufs["ds"][2], return_lse=False)
+        return out
+
     def _hybrid(self, q_l, k_l, v_l):
         """Ulysses inside the Ulysses group, ring across the ring group."""
         g = self.groups
@@ -255,7 +277,8 @@ class B200SequenceParallelAttention:
         (actor/attention_dispatch.py:383-401)."""
         for plan in self._plans.values():
             if isinstance(plan, dict):
-                plan["win"].close()
+                if "win" in plan:
+                    plan["win"].close()
             else:
                 plan.close()
         self._plans.clear()

@@ -167,3 +167,17 @@ def test_query_bias_refusals(attn):
     many = [(i, i + 1, torch.zeros(1, 1, 1, 64, device="cuda")) for i in range(64)]
     with pytest.raises(UnsupportedModelError, match="at most"):
         attn(*qs, heads=2, skip_reshape=True, query_bias_groups=many)
+
+
+def test_fp8_callable_on_one_rank(lib):
+    """The FP8 drop-in at Ulysses degree 1 quantises the caller's heads in
+    place of a scatter (per-head e4m3 scales) and attends them."""
+    from dgx_monarch_b200.usp import make_b200_usp_attention
+
+    attn = make_b200_usp_attention(fp8=True)
+    q, k, v = _qkv(2, 640, 4, 4, 21)
+    for _ in range(2):  # the second call reuses the e4m3 buffers
+        out = attn(*(t.reshape(2, 640, -1) for t in (q, k, v)), heads=4).reshape(2, 640, 4, 128)
+    ref, _ = reference_attention(q, k, v)
+    assert rel_l2(out, ref) <= 8e-2  # e4m3 inputs against bf16 activations
+    attn.impl.invalidate()
