@@ -1,12 +1,15 @@
 // Fused Ulysses prologue and FP8 quantisation.
 //
-// qkv_prologue_scatter_kernel: Q/K RMSNorm and multi-axis RoPE applied to a
-// rank's rows while they are scattered head-slice by head-slice into the
-// peers' receive tensors -- the sequence->head all-to-all of
-// dgxm_ulysses_scatter with the per-token math the family forwards run just
-// before the attention seam folded in (Wan: norm_q/norm_k over the whole
-// hidden size then RoPE, adapters/wan_family.py:70-73; Flux/Krea2: per-head
-// QKNorm then RoPE inside the blocks).  V is moved unchanged.
+// Q/K RMSNorm and multi-axis RoPE applied to a rank's rows while they are
+// scattered head-slice by head-slice into the peers' receive tensors -- the
+// sequence->head all-to-all of dgxm_ulysses_scatter with the per-token math
+// the family forwards run just before the attention seam folded in.  V is
+// moved unchanged.  Two kernels:
+//   qkv_prologue_scatter_kernel  one block per token row, for the Wan
+//                                norm_q/norm_k over the whole hidden size
+//                                (adapters/wan_family.py:70-73);
+//   qkv_prologue_head_kernel     one half-warp per head row, for the
+//                                Flux/Krea2 per-head QKNorm or no norm.
 //
 // Rounding follows the separate ops it fuses: the norm's output is rounded
 // to bf16 (the module's output dtype), RoPE then rotates that in fp32 and
@@ -44,7 +47,7 @@ __global__ void __launch_bounds__(kPrologueThreads) qkv_prologue_scatter_kernel(
   __shared__ float buf[kPrologueMaxHidden];
   __shared__ __align__(16) __nv_bfloat16 obuf[kPrologueMaxHidden];
   __shared__ float red[kPrologueThreads / 32];
-  __shared__ float head_scale[kPrologueMaxHidden / 128];
+  __shared__ float row_scale;
   const int hid = p.heads * 128;
   const int hl = p.heads / p.world;
   const int64_t seq_full = static_cast<int64_t>(p.seq_local) * p.world;
@@ -79,19 +82,7 @@ __global__ void __launch_bounds__(kPrologueThreads) qkv_prologue_scatter_kernel(
           if (threadIdx.x == 0) {
             float tot = 0.f;
             for (int w = 0; w < kPrologueThreads / 32; ++w) tot += red[w];
-            head_scale[0] = rsqrtf(tot / hid + p.eps);
-          }
-          __syncthreads();
-        } else if (p.norm_mode == DGXM_NORM_HEAD) {
-          for (int h = warp; h < p.heads; h += kPrologueThreads / 32) {
-            float ss = 0.f;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const float x = buf[h * 128 + lane * 4 + i];
-              ss = fmaf(x, x, ss);
-            }
-            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-            if (lane == 0) head_scale[h] = rsqrtf(ss / 128.f + p.eps);
+            row_scale = rsqrtf(tot / hid + p.eps);
           }
           __syncthreads();
         }
@@ -100,10 +91,10 @@ __global__ void __launch_bounds__(kPrologueThreads) qkv_prologue_scatter_kernel(
         for (int pr = threadIdx.x; pr < hid / 2; pr += blockDim.x) {
           const int e = 2 * pr;
           float x0 = buf[e], x1 = buf[e + 1];
-          if (p.norm_mode != DGXM_NORM_NONE) {
-            const float sc = p.norm_mode == DGXM_NORM_HIDDEN ? head_scale[0] : head_scale[e / 128];
+          if (p.norm_mode == DGXM_NORM_HIDDEN) {
+            const float sc = row_scale;
             // the norm module's output: bf16(x * rsqrt(mean + eps)) * weight, rounded
-            const int wi = p.norm_mode == DGXM_NORM_HIDDEN ? e : (e % 128);
+            const int wi = e;
             float n0 = __bfloat162float(__float2bfloat16(x0 * sc));
             float n1 = __bfloat162float(__float2bfloat16(x1 * sc));
             if (w != nullptr) {
@@ -144,12 +135,6 @@ __global__ void __launch_bounds__(kPrologueThreads) qkv_prologue_scatter_kernel(
   }
 }
 
-// Per-head norm (or none): one warp per (row, tensor, head).  Lane l owns
-// values [4l, 4l + 4) of the head row -- two RoPE pairs -- and the head's sum
-// of squares is the lane sums reduced by the same xor shuffle as the
-// row-per-block kernel above, so both give identical bits.  Loads and the
-// 256-byte peer store of a head row are one coalesced warp access each, and
-// no block barrier is needed.
 // Per-head norm (or none): each half-warp owns one (tensor, head) row of a
 // token -- sub-lane s holds values [8s, 8s + 8), four RoPE pairs -- so a warp
 // reads and writes two 256-byte head rows per access, and every half-warp has
