@@ -234,6 +234,10 @@ def check(code: int, func: str) -> None:
         raise DgxmError(code, func, msg.decode(errors="replace") if msg else "")
 
 
+# Bits of the device error word (csrc/common.h).
+ERR_PRODUCER_TIMEOUT, ERR_MMA_TIMEOUT, ERR_SOFTMAX_TIMEOUT, ERR_EPILOGUE_TIMEOUT, ERR_PEER_TIMEOUT = 1, 2, 4, 8, 16
+
+
 def device_error(clear: bool = True) -> int:
     """The device error word (bounded waits that expired); 0 when clean."""
     value = load().dgxm_device_error(1 if clear else 0)

@@ -102,6 +102,11 @@ class PeerWindows:
         return raw.view(dtype).view(*shape)
 
     # ---------------------------------------------------------------- sync
+    def set_timeout(self, milliseconds: int) -> None:
+        """Bound every barrier wait of these windows to about `milliseconds`;
+        a wait that runs out sets the device error word and returns."""
+        _lib.check(self._lib.dgxm_comm_set_timeout(self._handle, int(milliseconds)), "dgxm_comm_set_timeout")
+
     def barrier(self, stream: torch.cuda.Stream | None = None) -> None:
         stream = stream or torch.cuda.current_stream(self.device)
         _lib.check(self._lib.dgxm_comm_barrier(self._handle, stream.cuda_stream), "dgxm_comm_barrier")

@@ -507,3 +507,44 @@ def _streamed_case(rank, world, dev):
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
 def test_host_streamed_ulysses_across_gpus():
     _spawn(_streamed_case, 2)
+
+
+def _peer_timeout_case(rank, world, dev):
+    """Failure detection without a GPU fault: rank 1 never arrives at a
+    barrier (the failure is made on the host), rank 0's barrier kernel gives up
+    after its 200 ms budget, sets the peer-timeout bit of the device error word
+    and returns, and the context stays usable for the next kernel."""
+    import torch.distributed as dist
+
+    from dgx_monarch_b200 import _lib
+    from dgx_monarch_b200.comm import PeerWindows
+    from dgx_monarch_b200.ops import attention_fwd
+    from tests.test_attn_gpu import BF16_REL_L2, reference_attention, rel_l2
+
+    check = Checks(rank)
+    win = PeerWindows(1 << 20, device=dev, rank=rank, world=world, generation=18)
+    win.set_timeout(200)
+    win.barrier()                      # both ranks: a barrier that completes
+    torch.cuda.synchronize()
+    check(_lib.device_error() == 0, "the completed barrier reported an error")
+    dist.barrier()
+    if rank == 0:
+        win.barrier()                  # rank 1 never arrives at this one
+        torch.cuda.synchronize()
+        word = _lib.device_error()     # read and clear
+        check(word & _lib.ERR_PEER_TIMEOUT != 0, f"device error word {word} lacks the peer-timeout bit")
+        g = torch.Generator(device=dev).manual_seed(3)
+        q, k, v = (torch.randn(1, 300, 2, 128, device=dev, generator=g).bfloat16() for _ in range(3))
+        out, _ = attention_fwd(q, k, v, return_lse=False)
+        ref, _ = reference_attention(q, k, v)
+        torch.cuda.synchronize()
+        check.le(rel_l2(out, ref), BF16_REL_L2, "attention after the expired wait")
+        check(_lib.device_error() == 0, "the context reported errors after recovery")
+    dist.barrier()                     # the host learns of the missing rank; both retire the windows
+    win.close()
+    check.close()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
+def test_expired_barrier_reports_and_the_context_recovers():
+    _spawn(_peer_timeout_case, 2)
