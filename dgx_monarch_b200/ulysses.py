@@ -239,3 +239,100 @@ class HostStreamedUlysses:
 
     def close(self) -> None:
         self.uly.close()
+
+
+class OverlappedUlysses:
+    """A Ulysses step whose sequence->head scatter is hidden behind attention.
+
+    Heads go in `groups` groups (a group's heads divide the Ulysses degree).
+    Group g + 1 is scattered on a side stream into one of two receive slots
+    while the tensor cores attend group g from the other.  Each group's routed
+    epilogue writes its own head columns of the owners' outputs (the peer
+    base pointers are offset by the group), so the inverse all-to-all stays
+    fused.
+
+    Ordering: a rank refills a slot in its peers' windows only after a
+    barrier that every rank reaches after its own attention from that slot,
+    so no peer is still reading it.  All barriers of the windows are ordered
+    through the two streams' events, as their shared epoch counter requires.
+    The result is bit-identical to UlyssesAttention.forward.
+    """
+
+    def __init__(self, *, world: int, rank: int, batch: int, seq_local: int, heads: int, head_dim: int,
+                 device: torch.device, groups: int, group=None, generation: int = 0,
+                 dtype: torch.dtype = torch.bfloat16) -> None:
+        if world < 2:
+            raise ValueError("the overlapped step needs a Ulysses degree of 2 or more")
+        if heads % groups or (heads // groups) % world:
+            raise ValueError(f"{groups} head groups of {heads} heads do not split over {world} ranks")
+        self.world, self.rank, self.device, self.groups = world, rank, device, groups
+        self.b, self.ls, self.h, self.d = batch, seq_local, heads, head_dim
+        self.hg = heads // groups               # heads per group
+        self.hgl = self.hg // world             # heads per group on one rank after the scatter
+        s = seq_local * world
+        elt = torch.empty((), dtype=dtype).element_size()
+        slot_bytes = batch * s * self.hgl * head_dim * elt
+        out_bytes = batch * seq_local * heads * head_dim * elt
+        self.windows = PeerWindows(6 * slot_bytes + out_bytes + 8 * 256, device=device, group=group,
+                                   rank=rank, world=world, generation=generation)
+        self.off_recv = [[self.windows.carve(slot_bytes) for _ in range(3)] for _ in range(2)]
+        self.off_out = self.windows.carve(out_bytes)
+        self.recv = [[self.windows.local_tensor(o, (batch, s, self.hgl, head_dim), dtype) for o in slot]
+                     for slot in self.off_recv]
+        self.out_local = self.windows.local_tensor(self.off_out, (batch, seq_local, heads, head_dim), dtype)
+        self.out_strides = (seq_local * heads * head_dim, heads * head_dim, head_dim)
+        self.group_bytes = self.hg * head_dim * elt  # head-column offset of one group in the outputs
+        self.side = torch.cuda.Stream(device)
+        # per group a scatter, a barrier and an attention; one more barrier per
+        # group after the first two (slot reuse); the final barrier
+        self.launches_per_step = 3 * groups + max(0, groups - 2) + 1
+
+    def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+        w, side = self.windows, self.side
+        main = torch.cuda.current_stream(self.device)
+        start = torch.cuda.Event()
+        start.record(main)
+        side.wait_event(start)       # inputs written, the previous step finished
+        ready: list = [None] * self.groups
+        freed: list = [None, None]
+
+        def scatter(g: int) -> None:
+            slot = g % 2
+            if g >= 2:
+                side.wait_event(freed[slot])   # this rank attended group g - 2 from the slot
+                w.barrier(side)                 # ... and so has every other rank
+            sl = slice(g * self.hg, (g + 1) * self.hg)
+            ulysses_scatter([q[:, :, sl], k[:, :, sl], v[:, :, sl]],
+                            [[w.peer_ptr(r, off) for r in range(self.world)] for off in self.off_recv[slot]],
+                            world=self.world, rank=self.rank, stream=side)
+            w.barrier(side)                     # every rank's rows of group g have landed
+            ev = torch.cuda.Event()
+            ev.record(side)
+            ready[g] = ev
+
+        for g in range(min(2, self.groups)):
+            scatter(g)
+        for g in range(self.groups):
+            slot = g % 2
+            main.wait_event(ready[g])
+            qg, kg, vg = self.recv[slot]
+            attention_routed(qg, kg, vg,
+                             [w.peer_ptr(r, self.off_out) + g * self.group_bytes for r in range(self.world)],
+                             self.out_strides, world=self.world, rank=self.rank, seq_local=self.ls)
+            ev = torch.cuda.Event()
+            ev.record(main)
+            freed[slot] = ev
+            if g + 2 < self.groups:
+                scatter(g + 2)
+        w.barrier(main)                         # every routed row of every group has landed
+        if out is None:
+            return self.out_local
+        out.copy_(self.out_local)
+        return out
+
+    def close(self) -> None:
+        if self.windows is not None:
+            torch.cuda.synchronize(self.device)
+            self.windows.close()
+            self.windows = None

@@ -548,3 +548,34 @@ def _peer_timeout_case(rank, world, dev):
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
 def test_expired_barrier_reports_and_the_context_recovers():
     _spawn(_peer_timeout_case, 2)
+
+
+def _overlapped_case(rank, world, dev):
+    """The overlapped Ulysses step (group scatters hidden behind attention,
+    two receive slots) gives the same bits as the plain step, call after call."""
+    from dgx_monarch_b200 import _lib
+    from dgx_monarch_b200.ulysses import OverlappedUlysses, UlyssesAttention
+
+    check = Checks(rank)
+    heads, ls = 4 * world, 300
+    plain = UlyssesAttention(world=world, rank=rank, batch=1, seq_local=ls, heads=heads, head_dim=128,
+                             device=dev, generation=19)
+    for groups in (4, 2):
+        over = OverlappedUlysses(world=world, rank=rank, batch=1, seq_local=ls, heads=heads, head_dim=128,
+                                 device=dev, groups=groups, generation=20 + groups)
+        for step in range(3):
+            g = torch.Generator(device=dev).manual_seed(110 + step + rank)
+            q, k, v = (torch.randn(1, ls, heads, 128, device=dev, generator=g).bfloat16() for _ in range(3))
+            want = plain.forward(q, k, v).clone()
+            got = over.forward(q, k, v).clone()
+            torch.cuda.synchronize()
+            check(torch.equal(got, want), f"{groups} groups, call {step}: differs from the plain step")
+        over.close()
+    plain.close()
+    check(_lib.device_error() == 0, f"device error word {_lib.device_error()}")
+    check.close()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
+def test_overlapped_ulysses_equals_plain_step():
+    _spawn(_overlapped_case, min(torch.cuda.device_count(), 4))
