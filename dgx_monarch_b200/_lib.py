@@ -100,6 +100,9 @@ class AttnRoute(ctypes.Structure):
         ("rank", ctypes.c_int32),
         ("seq_local", ctypes.c_int32),
         ("seg0", ctypes.c_int32),
+        ("txt_rows", ctypes.c_int32),
+        ("txt_front", ctypes.c_int32),
+        ("txt_peers", ctypes.c_void_p * 8),
     ]
 
 
@@ -172,6 +175,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "dgxm_comm_destroy": (ctypes.c_int, [_P]),
     "dgxm_ulysses_scatter": (ctypes.c_int, [ctypes.POINTER(A2ADesc), ctypes.POINTER(_P),
                                             ctypes.POINTER(_P), _P]),
+    "dgxm_ulysses_scatter_joint": (ctypes.c_int, [ctypes.POINTER(A2ADesc), ctypes.c_int32, ctypes.c_int32,
+                                                  ctypes.POINTER(_P), ctypes.POINTER(ctypes.c_int64),
+                                                  ctypes.POINTER(_P), ctypes.POINTER(_P), _P]),
     "dgxm_ulysses_gather": (ctypes.c_int, [ctypes.POINTER(A2ADesc), _P, ctypes.POINTER(_P), _P]),
     "dgxm_attn_fwd_ext": (ctypes.c_int, [ctypes.POINTER(AttnDesc), ctypes.POINTER(AttnExtras),
                                          ctypes.POINTER(AttnRoute), _P, _P, _P, _P, _P, _P, _P, _P,

@@ -18,6 +18,7 @@ import torch
 
 from . import _lib
 from .comm import PeerWindows
+from .ops import _require_cuda, _require_on
 
 
 class UnsupportedModelError(RuntimeError):
@@ -88,6 +89,7 @@ class CfgGather:
     def gather_in_window(self, local: torch.Tensor) -> torch.Tensor:
         """Gather into this call's window buffer and return a view of it, valid
         until the call after next."""
+        _require_on(self.device, local)
         local = local.contiguous()
         nbytes = local.numel() * local.element_size()
         if nbytes != self.slice_bytes:
@@ -119,6 +121,10 @@ def cfg_combine(cond: torch.Tensor, uncond: torch.Tensor, cfg: float,
     (comfy's default cfg_function), in one kernel (dgxm_cfg_combine)."""
     if cond.shape != uncond.shape or cond.dtype != uncond.dtype or cond.dtype not in _PRED_DTYPES:
         raise ValueError("cond and uncond must share shape and a float dtype")
+    _require_cuda(cond, uncond, out)
+    if out is not None and (out.shape != cond.shape or out.dtype != cond.dtype or not out.is_contiguous()
+                            or out.data_ptr() % 16):
+        raise ValueError("out must be a contiguous, 16-byte aligned tensor of the predictions' shape and dtype")
     # The kernel moves 16-byte vectors; a view at an unaligned offset (a
     # prediction whose byte size is not a multiple of 16, sliced out of the
     # gathered pair) is copied to an aligned buffer first.

@@ -107,6 +107,11 @@ struct __align__(64) AttnParams {
   int o_head_off;
   int o_world;
   int o_seg0;  // joint order of the gathered axis (0 = rank-major)
+  // Replicated text: o_txt rows before (o_txt_front) or after the o_img_rows
+  // image rows; a text row goes to every rank's o_txt_peer tensor.
+  int o_txt, o_txt_front, o_img_rows;
+  int64_t o_txt_sb;
+  void* o_txt_peer[DGXM_MAX_WORLD];
   // Extras (the EXTRA kernel variant only): keep bits over keys (0 excludes
   // the key) and over query rows (0 writes a zero output row), and additive
   // biases for query-row groups, added to the scaled logits.
@@ -593,31 +598,47 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
       void* obase = p.o;
       int orow_idx = grow;
       int ohead = h;
+      int64_t osb = p.o_sb;
+      int n_dst = 1;  // a replicated text row is stored to every rank
       if (p.o_rows > 0) {
         int peer = 0, lrow = 0;
+        bool txt = false;
         if (row_ok) {
-          if (p.o_seg0 == 0) {
-            peer = grow / p.o_rows;
-            lrow = grow - peer * p.o_rows;
-          } else if (grow < p.o_world * p.o_seg0) {
-            peer = grow / p.o_seg0;
-            lrow = grow - peer * p.o_seg0;
+          int g = grow;
+          if (p.o_txt > 0) {
+            if (p.o_txt_front) {
+              txt = g < p.o_txt;
+              if (!txt) g -= p.o_txt;
+            } else {
+              txt = g >= p.o_img_rows;
+              if (txt) g -= p.o_img_rows;
+            }
+          }
+          if (txt) {
+            n_dst = p.o_world;
+            lrow = g;
+          } else if (p.o_seg0 == 0) {
+            peer = g / p.o_rows;
+            lrow = g - peer * p.o_rows;
+          } else if (g < p.o_world * p.o_seg0) {
+            peer = g / p.o_seg0;
+            lrow = g - peer * p.o_seg0;
           } else {
             const int seg1 = p.o_rows - p.o_seg0;
-            const int t2 = grow - p.o_world * p.o_seg0;
+            const int t2 = g - p.o_world * p.o_seg0;
             peer = t2 / seg1;
             lrow = p.o_seg0 + (t2 - peer * seg1);
           }
         }
-        obase = p.o_peer[peer];
+        obase = txt ? p.o_txt_peer[0] : p.o_peer[peer];
+        osb = txt ? p.o_txt_sb : p.o_sb;
         orow_idx = lrow;
         ohead = p.o_head_off + h;
       }
-      char* orow = static_cast<char*>(obase) +
-                   (static_cast<int64_t>(b) * p.o_sb + static_cast<int64_t>(orow_idx) * p.o_sl +
-                    static_cast<int64_t>(ohead) * p.o_sh) *
-                       (OUT_F32 ? 4 : 2) +
-                   c * 64 * (OUT_F32 ? 4 : 2);
+      const int64_t ooff = (static_cast<int64_t>(b) * osb + static_cast<int64_t>(orow_idx) * p.o_sl +
+                            static_cast<int64_t>(ohead) * p.o_sh) *
+                               (OUT_F32 ? 4 : 2) +
+                           c * 64 * (OUT_F32 ? 4 : 2);
 #pragma unroll
       for (int h2 = 0; h2 < 2; ++h2) {
         uint32_t o[32];
@@ -626,22 +647,31 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
         reg_fence32(o);
         if (row_ok) {
           if constexpr (OUT_F32) {
-            float4* dst = reinterpret_cast<float4*>(orow + h2 * 128);
+            float4 f[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i)
-              dst[i] = make_float4(__uint_as_float(o[4 * i]) * inv, __uint_as_float(o[4 * i + 1]) * inv,
-                                   __uint_as_float(o[4 * i + 2]) * inv,
-                                   __uint_as_float(o[4 * i + 3]) * inv);
+              f[i] = make_float4(__uint_as_float(o[4 * i]) * inv, __uint_as_float(o[4 * i + 1]) * inv,
+                                 __uint_as_float(o[4 * i + 2]) * inv, __uint_as_float(o[4 * i + 3]) * inv);
+            for (int dd = 0; dd < n_dst; ++dd) {
+              float4* dst = reinterpret_cast<float4*>(
+                  static_cast<char*>(dd == 0 ? obase : p.o_txt_peer[dd]) + ooff + h2 * 128);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) dst[i] = f[i];
+            }
           } else {
-            uint4* dst = reinterpret_cast<uint4*>(orow + h2 * 64);
+            uint4 w[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-              uint4 w;
-              w.x = pack_bf16x2(__uint_as_float(o[8 * i + 0]) * inv, __uint_as_float(o[8 * i + 1]) * inv);
-              w.y = pack_bf16x2(__uint_as_float(o[8 * i + 2]) * inv, __uint_as_float(o[8 * i + 3]) * inv);
-              w.z = pack_bf16x2(__uint_as_float(o[8 * i + 4]) * inv, __uint_as_float(o[8 * i + 5]) * inv);
-              w.w = pack_bf16x2(__uint_as_float(o[8 * i + 6]) * inv, __uint_as_float(o[8 * i + 7]) * inv);
-              dst[i] = w;
+              w[i].x = pack_bf16x2(__uint_as_float(o[8 * i + 0]) * inv, __uint_as_float(o[8 * i + 1]) * inv);
+              w[i].y = pack_bf16x2(__uint_as_float(o[8 * i + 2]) * inv, __uint_as_float(o[8 * i + 3]) * inv);
+              w[i].z = pack_bf16x2(__uint_as_float(o[8 * i + 4]) * inv, __uint_as_float(o[8 * i + 5]) * inv);
+              w[i].w = pack_bf16x2(__uint_as_float(o[8 * i + 6]) * inv, __uint_as_float(o[8 * i + 7]) * inv);
+            }
+            for (int dd = 0; dd < n_dst; ++dd) {
+              uint4* dst = reinterpret_cast<uint4*>(
+                  static_cast<char*>(dd == 0 ? obase : p.o_txt_peer[dd]) + ooff + h2 * 64);
+#pragma unroll
+              for (int i = 0; i < 4; ++i) dst[i] = w[i];
             }
           }
         }
@@ -786,9 +816,15 @@ static int dispatch_attn(const dgxm_attn_desc* d, const AttnParams& prm, dim3 gr
 static int set_route(const dgxm_attn_desc* d, const dgxm_attn_route* rt, AttnParams* prm) {
   if (rt->world < 1 || rt->world > DGXM_MAX_WORLD || rt->rank < 0 || rt->rank >= rt->world)
     return fail(DGXM_ERR_INVALID, "rank %d / world %d out of range", rt->rank, rt->world);
-  if (rt->seq_local <= 0 || static_cast<int64_t>(rt->seq_local) * rt->world != d->q_len)
-    return fail(DGXM_ERR_INVALID, "seq_local %d x world %d does not cover q_len %d", rt->seq_local,
-                rt->world, d->q_len);
+  if (rt->txt_rows < 0 || (rt->txt_front != 0 && rt->txt_front != 1))
+    return fail(DGXM_ERR_INVALID, "text rows %d / front flag %d out of range", rt->txt_rows,
+                rt->txt_front);
+  if (rt->txt_rows > 0 && rt->seg0 != 0)
+    return fail(DGXM_ERR_INVALID, "replicated text needs the rank-major image order (seg0 = 0)");
+  if (rt->seq_local <= 0 ||
+      static_cast<int64_t>(rt->seq_local) * rt->world + rt->txt_rows != d->q_len)
+    return fail(DGXM_ERR_INVALID, "seq_local %d x world %d + %d text rows does not cover q_len %d",
+                rt->seq_local, rt->world, rt->txt_rows, d->q_len);
   if (rt->seg0 < 0 || rt->seg0 >= rt->seq_local)
     return fail(DGXM_ERR_INVALID, "joint segment of %d rows does not split %d local rows", rt->seg0,
                 rt->seq_local);
@@ -796,11 +832,20 @@ static int set_route(const dgxm_attn_desc* d, const dgxm_attn_route* rt, AttnPar
     if (rt->o_peers[r] == nullptr || reinterpret_cast<uintptr_t>(rt->o_peers[r]) % 16)
       return fail(DGXM_ERR_INVALID, "output peer %d is NULL or not 16-byte aligned", r);
     prm->o_peer[r] = rt->o_peers[r];
+    if (rt->txt_rows > 0) {
+      if (rt->txt_peers[r] == nullptr || reinterpret_cast<uintptr_t>(rt->txt_peers[r]) % 16)
+        return fail(DGXM_ERR_INVALID, "text output peer %d is NULL or not 16-byte aligned", r);
+      prm->o_txt_peer[r] = rt->txt_peers[r];
+    }
   }
   prm->o_rows = rt->seq_local;
   prm->o_head_off = rt->rank * d->q_heads;
   prm->o_world = rt->world;
   prm->o_seg0 = rt->seg0;
+  prm->o_txt = rt->txt_rows;
+  prm->o_txt_front = rt->txt_front;
+  prm->o_img_rows = rt->seq_local * rt->world;
+  prm->o_txt_sb = static_cast<int64_t>(rt->txt_rows) * d->o_stride[1];
   return DGXM_OK;
 }
 

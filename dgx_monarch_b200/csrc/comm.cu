@@ -86,6 +86,8 @@ struct ScatterParams {
   int n_tensors, world, rank;
   int batch, seq_local, heads, head_bytes; // head_bytes = D * elt
   int seg0;                                // joint order: leading rows per rank (0 = rank-major)
+  int64_t seq_full;                        // rows of each receive tensor
+  int row_off;                             // first image row in it (after replicated text)
 };
 
 // Position on the gathered axis of local row l of rank r.  With seg0 == 0
@@ -109,7 +111,7 @@ __global__ void __launch_bounds__(256) ulysses_scatter_kernel(const __grid_const
   const int hl = p.heads / p.world;
   const int64_t per_tensor = static_cast<int64_t>(p.batch) * p.seq_local * p.heads * chunks_per_head;
   const int64_t total = per_tensor * p.n_tensors;
-  const int64_t seq_full = static_cast<int64_t>(p.seq_local) * p.world;
+  const int64_t seq_full = p.seq_full;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int t = static_cast<int>(i / per_tensor);
@@ -124,8 +126,41 @@ __global__ void __launch_bounds__(256) ulysses_scatter_kernel(const __grid_const
         p.src[t] + b * p.s_sb[t] + l * p.s_sl[t] + h * p.s_sh[t]) + part);
     const int r = h / hl;
     const int hh = h - r * hl;
-    const int64_t row = static_cast<int64_t>(b) * seq_full + gathered_row(p.rank, l, p.seq_local, p.world, p.seg0);
+    const int64_t row = static_cast<int64_t>(b) * seq_full + p.row_off +
+                        gathered_row(p.rank, l, p.seq_local, p.world, p.seg0);
     char* dst = p.dst[t][r] + (row * hl + hh) * p.head_bytes;
+    reinterpret_cast<uint4*>(dst)[part] = val;
+  }
+}
+
+// Replicated text: this rank's head slice [head0, head0 + hl) of its own
+// whole (B, T, H, D) text goes into its own receive tensors at rows
+// [row_off, row_off + T).  Local HBM to HBM, 16 bytes per thread.
+struct TextSliceParams {
+  const char* src[3];
+  char* dst[3];
+  int64_t s_sb[3], s_sl[3], s_sh[3];  // bytes
+  int64_t d_sb;                       // bytes between batch items of a receive tensor
+  int n_tensors, batch, rows, hl, head0, head_bytes, row_off;
+};
+
+__global__ void __launch_bounds__(256) text_head_slice_kernel(const __grid_constant__ TextSliceParams p) {
+  const int chunks = p.head_bytes / 16;
+  const int64_t per_tensor = static_cast<int64_t>(p.batch) * p.rows * p.hl * chunks;
+  const int64_t total = per_tensor * p.n_tensors;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int t = static_cast<int>(i / per_tensor);
+    int64_t rem = i - t * per_tensor;
+    const int part = static_cast<int>(rem % chunks);
+    rem /= chunks;
+    const int hh = static_cast<int>(rem % p.hl);
+    rem /= p.hl;
+    const int l = static_cast<int>(rem % p.rows);
+    const int b = static_cast<int>(rem / p.rows);
+    const uint4 val = __ldg(reinterpret_cast<const uint4*>(
+        p.src[t] + b * p.s_sb[t] + l * p.s_sl[t] + (p.head0 + hh) * p.s_sh[t]) + part);
+    char* dst = p.dst[t] + b * p.d_sb + ((static_cast<int64_t>(p.row_off) + l) * p.hl + hh) * p.head_bytes;
     reinterpret_cast<uint4*>(dst)[part] = val;
   }
 }
@@ -362,9 +397,14 @@ extern "C" int dgxm_comm_allgather(dgxm_comm* c, const void* src, int64_t bytes,
   return dgxm_comm_barrier(c, stream);
 }
 
-extern "C" int dgxm_ulysses_scatter(const dgxm_a2a_desc* d, const void* const* src,
-                                    void* const* dst, void* stream) {
-  using namespace dgxm;
+namespace dgxm {
+
+// Checks an all-to-all descriptor and fills the scatter parameters (the
+// receive tensor holds world*seq_local rows, image rows from row 0).  The
+// pointers are checked only when there are rows to move, as an empty shard
+// may carry NULL tensors.
+static int build_scatter(const dgxm_a2a_desc* d, const void* const* src, void* const* dst,
+                         ScatterParams* p) {
   if (d == nullptr || src == nullptr || dst == nullptr)
     return fail(DGXM_ERR_INVALID, "NULL all-to-all argument");
   if (d->n_tensors < 1 || d->n_tensors > 3)
@@ -381,38 +421,103 @@ extern "C" int dgxm_ulysses_scatter(const dgxm_a2a_desc* d, const void* const* s
     return fail(DGXM_ERR_INVALID, "head row of %d bytes is not a multiple of 16", head_bytes);
   if (d->batch < 0 || d->seq_local < 0)
     return fail(DGXM_ERR_INVALID, "negative batch or sequence length");
-  if (d->batch == 0 || d->seq_local == 0) return DGXM_OK;
-  ScatterParams p;
-  memset(&p, 0, sizeof(p));
-  for (int t = 0; t < d->n_tensors; ++t) {
+  memset(p, 0, sizeof(*p));
+  const bool rows = d->batch > 0 && d->seq_local > 0;
+  for (int t = 0; t < d->n_tensors && rows; ++t) {
     if (src[t] == nullptr || reinterpret_cast<uintptr_t>(src[t]) % 16)
       return fail(DGXM_ERR_INVALID, "source tensor %d is NULL or not 16-byte aligned", t);
-    p.src[t] = static_cast<const char*>(src[t]);
-    p.s_sb[t] = d->src_stride[t][0] * eb;
-    p.s_sl[t] = d->src_stride[t][1] * eb;
-    p.s_sh[t] = d->src_stride[t][2] * eb;
-    if (p.s_sb[t] % 16 || p.s_sl[t] % 16 || p.s_sh[t] % 16)
+    p->src[t] = static_cast<const char*>(src[t]);
+    p->s_sb[t] = d->src_stride[t][0] * eb;
+    p->s_sl[t] = d->src_stride[t][1] * eb;
+    p->s_sh[t] = d->src_stride[t][2] * eb;
+    if (p->s_sb[t] % 16 || p->s_sl[t] % 16 || p->s_sh[t] % 16)
       return fail(DGXM_ERR_INVALID, "source tensor %d strides are not 16-byte multiples", t);
     for (int r = 0; r < d->world; ++r) {
       void* q = dst[t * d->world + r];
       if (q == nullptr || reinterpret_cast<uintptr_t>(q) % 16)
         return fail(DGXM_ERR_INVALID, "destination %d of tensor %d is NULL or misaligned", r, t);
-      p.dst[t][r] = static_cast<char*>(q);
+      p->dst[t][r] = static_cast<char*>(q);
     }
   }
-  p.n_tensors = d->n_tensors;
-  p.world = d->world;
-  p.rank = d->rank;
-  p.batch = d->batch;
-  p.seq_local = d->seq_local;
-  p.heads = d->heads;
-  p.head_bytes = head_bytes;
-  if (d->seg0 < 0 || d->seg0 >= d->seq_local || (d->seg0 > 0 && d->seq_local - d->seg0 < 1))
+  p->n_tensors = d->n_tensors;
+  p->world = d->world;
+  p->rank = d->rank;
+  p->batch = d->batch;
+  p->seq_local = d->seq_local;
+  p->heads = d->heads;
+  p->head_bytes = head_bytes;
+  if (d->seq_local > 0 &&
+      (d->seg0 < 0 || d->seg0 >= d->seq_local || (d->seg0 > 0 && d->seq_local - d->seg0 < 1)))
     return fail(DGXM_ERR_INVALID, "joint segment of %d rows does not split %d local rows", d->seg0,
                 d->seq_local);
-  p.seg0 = d->seg0;
-  const int64_t work = static_cast<int64_t>(d->n_tensors) * d->batch * d->seq_local * d->heads * (head_bytes / 16);
+  p->seg0 = d->seg0;
+  p->seq_full = static_cast<int64_t>(d->seq_local) * d->world;
+  p->row_off = 0;
+  return DGXM_OK;
+}
+
+static int launch_scatter(const dgxm_a2a_desc* d, const ScatterParams& p, void* stream) {
+  if (d->batch == 0 || d->seq_local == 0) return DGXM_OK;
+  const int64_t work = static_cast<int64_t>(d->n_tensors) * d->batch * d->seq_local * d->heads * (p.head_bytes / 16);
   ulysses_scatter_kernel<<<grid_for(work, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  DGXM_CUDA_TRY(cudaGetLastError());
+  return DGXM_OK;
+}
+
+}  // namespace dgxm
+
+extern "C" int dgxm_ulysses_scatter(const dgxm_a2a_desc* d, const void* const* src,
+                                    void* const* dst, void* stream) {
+  using namespace dgxm;
+  ScatterParams p;
+  int rc = build_scatter(d, src, dst, &p);
+  if (rc) return rc;
+  return launch_scatter(d, p, stream);
+}
+
+extern "C" int dgxm_ulysses_scatter_joint(const dgxm_a2a_desc* d, int32_t txt_rows, int32_t txt_front,
+                                          const void* const* txt, const int64_t* txt_stride,
+                                          const void* const* src, void* const* dst, void* stream) {
+  using namespace dgxm;
+  ScatterParams p;
+  int rc = build_scatter(d, src, dst, &p);
+  if (rc) return rc;
+  if (d->seg0 != 0)
+    return fail(DGXM_ERR_INVALID, "replicated text needs the rank-major image order (seg0 = 0)");
+  if (txt_rows < 0 || (txt_front != 0 && txt_front != 1))
+    return fail(DGXM_ERR_INVALID, "text rows %d / front flag %d out of range", txt_rows, txt_front);
+  p.seq_full = static_cast<int64_t>(d->seq_local) * d->world + txt_rows;
+  p.row_off = txt_front ? txt_rows : 0;
+  if ((rc = launch_scatter(d, p, stream))) return rc;
+  if (txt_rows == 0 || d->batch == 0) return DGXM_OK;
+  if (txt == nullptr || txt_stride == nullptr) return fail(DGXM_ERR_INVALID, "NULL text argument");
+  const int eb = p.head_bytes / d->head_dim;
+  TextSliceParams tp;
+  memset(&tp, 0, sizeof(tp));
+  for (int t = 0; t < d->n_tensors; ++t) {
+    if (txt[t] == nullptr || reinterpret_cast<uintptr_t>(txt[t]) % 16)
+      return fail(DGXM_ERR_INVALID, "text tensor %d is NULL or not 16-byte aligned", t);
+    void* own = dst[t * d->world + d->rank];
+    if (own == nullptr || reinterpret_cast<uintptr_t>(own) % 16)
+      return fail(DGXM_ERR_INVALID, "receive tensor %d of this rank is NULL or misaligned", t);
+    tp.src[t] = static_cast<const char*>(txt[t]);
+    tp.s_sb[t] = txt_stride[3 * t] * eb;
+    tp.s_sl[t] = txt_stride[3 * t + 1] * eb;
+    tp.s_sh[t] = txt_stride[3 * t + 2] * eb;
+    if (tp.s_sb[t] % 16 || tp.s_sl[t] % 16 || tp.s_sh[t] % 16)
+      return fail(DGXM_ERR_INVALID, "text tensor %d strides are not 16-byte multiples", t);
+    tp.dst[t] = static_cast<char*>(own);
+  }
+  tp.n_tensors = d->n_tensors;
+  tp.batch = d->batch;
+  tp.rows = txt_rows;
+  tp.hl = d->heads / d->world;
+  tp.head0 = d->rank * tp.hl;
+  tp.head_bytes = p.head_bytes;
+  tp.d_sb = p.seq_full * tp.hl * p.head_bytes;
+  tp.row_off = txt_front ? 0 : d->seq_local * d->world;
+  const int64_t work = static_cast<int64_t>(d->n_tensors) * d->batch * txt_rows * tp.hl * (p.head_bytes / 16);
+  text_head_slice_kernel<<<grid_for(work, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(tp);
   DGXM_CUDA_TRY(cudaGetLastError());
   return DGXM_OK;
 }

@@ -31,15 +31,53 @@ def _ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
-def _require_cuda(*tensors: torch.Tensor) -> torch.device:
-    dev = tensors[0].device
-    for t in tensors:
+def _require_cuda(*tensors: torch.Tensor | None) -> torch.device | None:
+    """All given tensors (None skipped) are CUDA tensors on one device, which
+    is returned (None when no tensor is given): no host pointer, nor another
+    GPU's, ever reaches a kernel."""
+    given = [t for t in tensors if t is not None]
+    if not given:
+        return None
+    dev = given[0].device
+    for t in given:
         if t.device.type != "cuda":
             raise RuntimeError("the B200 attention path runs on CUDA tensors only "
                                f"(got a tensor on {t.device}); there is no CPU fallback")
         if t.device != dev:
             raise RuntimeError("all tensors of one call must live on the same CUDA device")
     return dev
+
+
+def _require_on(device: torch.device, *tensors: torch.Tensor | None) -> None:
+    """Like _require_cuda, and the device is the one the operation was built for."""
+    dev = _require_cuda(*tensors)
+    if dev is None:
+        return
+    device = torch.device(device)
+    want = device.index if device.index is not None else torch.cuda.current_device()
+    if dev.index != want:
+        raise RuntimeError(f"a tensor on {dev} was passed to an operation set up on cuda:{want}")
+
+
+def check_attn_buffers(q: torch.Tensor, k: torch.Tensor, *, out: torch.Tensor | None = None,
+                       lse: torch.Tensor | None = None, q_descale: torch.Tensor | None = None,
+                       k_descale: torch.Tensor | None = None,
+                       v_descale: torch.Tensor | None = None) -> None:
+    """Caller-given buffers of one attention call cover what the kernel touches:
+    out (B, Lq, H, D) with a contiguous head_dim, lse fp32 (B, H, Lq), one fp32
+    descale per query head (q) or key/value head (k, v), all on q's device."""
+    b, lq, h, d = q.shape
+    hkv = k.shape[2]
+    _require_on(q.device, out, lse, q_descale, k_descale, v_descale)
+    if out is not None and (tuple(out.shape) != (b, lq, h, d) or out.stride(3) != 1):
+        raise ValueError(f"out {tuple(out.shape)} is not a {(b, lq, h, d)} tensor with contiguous head_dim")
+    if lse is not None and (tuple(lse.shape) != (b, h, lq) or lse.dtype != torch.float32):
+        raise ValueError(f"lse {tuple(lse.shape)} {lse.dtype} is not an fp32 {(b, h, lq)} tensor")
+    for name, scale, n in (("q_descale", q_descale, h), ("k_descale", k_descale, hkv),
+                           ("v_descale", v_descale, hkv)):
+        if scale is not None and (scale.dtype != torch.float32 or scale.numel() != n
+                                  or not scale.is_contiguous()):
+            raise ValueError(f"{name} must be a contiguous fp32 vector of {n} heads")
 
 
 def attn_desc(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor,
@@ -93,6 +131,7 @@ def attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
     for name, t in (("q", q), ("k", k), ("v", v)):
         if t.stride(3) != 1:
             raise ValueError(f"{name} must have a contiguous head_dim")
+    check_attn_buffers(q, k, out=out, lse=lse, q_descale=q_descale, k_descale=k_descale, v_descale=v_descale)
     if out is None:
         out = torch.empty((b, lq, h, d), device=dev, dtype=out_dtype)
     if lse is None and return_lse:
@@ -155,10 +194,15 @@ def attention_fwd_ext(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
     bias_groups: [(row_begin, row_end, bias fp32 (B|1, H|1, Q|1, K') or None)],
     Q the group's row count;
     route: {"o_peers": [ptr...], "world", "rank", "seq_local", "seg0"} with
-    out_strides describing the peers' (B, Ls, H_total, D) tensors.
+    out_strides describing the peers' (B, Ls, H_total, D) tensors; optional
+    "txt_rows", "txt_front", "txt_peers" route replicated text rows to every
+    rank's (B, T, H_total, D) text output (dgxm_attn_route).
     """
     dev = _require_cuda(q, k, v)
     b, lq, h, d = q.shape
+    check_attn_buffers(q, k, out=out if route is None else None, lse=lse, q_descale=q_descale,
+                       k_descale=k_descale, v_descale=v_descale)
+    _require_on(dev, key_keep, query_keep, *[g[2] for g in (bias_groups or [])])
     keep = []
     if out is None and route is None:
         out = torch.empty((b, lq, h, d), device=dev, dtype=torch.bfloat16)
@@ -197,6 +241,9 @@ def attention_fwd_ext(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
             rt.o_peers[i] = ptr
         rt.world, rt.rank = route["world"], route["rank"]
         rt.seq_local, rt.seg0 = route["seq_local"], route.get("seg0", 0)
+        rt.txt_rows, rt.txt_front = route.get("txt_rows", 0), int(route.get("txt_front", 1))
+        for i, ptr in enumerate(route.get("txt_peers", ())):
+            rt.txt_peers[i] = ptr
     lib = _lib.load()
     with torch.cuda.device(dev):
         stream = torch.cuda.current_stream(dev).cuda_stream

@@ -7,6 +7,7 @@ import ctypes
 import torch
 
 from . import _lib
+from .ops import _require_cuda
 
 
 def rope_table(positions: torch.Tensor, axes_dim: list[int], theta: float = 10000.0) -> torch.Tensor:
@@ -36,6 +37,7 @@ def qkv_prologue_scatter(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, dst_
                          stream=None) -> None:
     """Norm + RoPE this rank's (B, Ls, H, 128) q/k rows and scatter q/k/v
     head slices to dst_ptrs[t][r] (rank-major, or joint order with seg0)."""
+    _require_cuda(q, k, v, norm_q_w, norm_k_w, rope)
     b, ls, h, d = q.shape
     for t in (q, k, v):
         if t.shape != q.shape or t.dtype != torch.bfloat16 or t.stride(3) != 1:
@@ -70,6 +72,7 @@ def qkv_gemm_prologue_scatter(x: torch.Tensor, w_qkv: torch.Tensor, dst_ptrs: li
     x: (m, k) or (1, m, k) bf16 rows, contiguous features; w_qkv: the Linear
     weight (3 * heads * 128, k); dst_ptrs[t][r]: rank r's (world * seq_local,
     heads / world, 128) receive tensor t; rope: (seq_local, 64, 2) fp32."""
+    _require_cuda(x, w_qkv, bias, norm_q_w, norm_k_w, rope)
     x2 = x.reshape(-1, x.shape[-1]) if x.ndim == 3 else x
     if x.ndim == 3 and x.shape[0] != 1:
         raise ValueError("the fused QKV kernel takes one batch item per call")
@@ -99,13 +102,18 @@ def qkv_gemm_prologue_scatter(x: torch.Tensor, w_qkv: torch.Tensor, dst_ptrs: li
 def quantize_e4m3_per_head(x: torch.Tensor, out: torch.Tensor | None = None,
                            descale: torch.Tensor | None = None, stream=None):
     """(e4m3 values, fp32 per-head descale = absmax / 448) of a bf16 (B, L, H, 128) tensor."""
+    _require_cuda(x, out, descale)
     b, l, h, d = x.shape
     if x.dtype != torch.bfloat16 or x.stride(3) != 1:
         raise ValueError("quantisation input must be bf16 with contiguous head_dim")
     if out is None:
         out = torch.empty(b, l, h, d, device=x.device, dtype=torch.float8_e4m3fn)
+    elif tuple(out.shape) != (b, l, h, d) or out.dtype != torch.float8_e4m3fn or not out.is_contiguous():
+        raise ValueError(f"out must be a contiguous float8_e4m3fn tensor of shape {(b, l, h, d)}")
     if descale is None:
         descale = torch.empty(h, device=x.device, dtype=torch.float32)
+    elif descale.numel() != h or descale.dtype != torch.float32 or not descale.is_contiguous():
+        raise ValueError(f"descale must be a contiguous fp32 vector of {h} heads")
     stride = (ctypes.c_int64 * 3)(x.stride(0), x.stride(1), x.stride(2))
     stream = stream or torch.cuda.current_stream(x.device)
     _lib.check(_lib.load().dgxm_quantize_e4m3_per_head(b, l, h, d, x.data_ptr(), stride, out.data_ptr(),

@@ -16,7 +16,7 @@ import torch
 
 from . import _lib
 from .comm import PeerWindows
-from .ops import _ptr, attn_desc
+from .ops import _ptr, _require_on, attn_desc, check_attn_buffers
 
 
 class RingAttention:
@@ -46,8 +46,10 @@ class RingAttention:
                 out: torch.Tensor | None = None, lse: torch.Tensor | None = None,
                 softmax_scale: float | None = None) -> tuple[torch.Tensor, torch.Tensor | None]:
         b, lq, h, d = q.shape
-        if (b, lq, k.shape[1], h, k.shape[2], d) != self.shape:
+        if (b, lq, k.shape[1], h, k.shape[2], d) != self.shape or v.shape != k.shape:
             raise ValueError(f"ring planned for {self.shape}, called with q {tuple(q.shape)} k {tuple(k.shape)}")
+        _require_on(self.device, q, k, v)
+        check_attn_buffers(q, k, out=out, lse=lse)
         k, v = k.contiguous(), v.contiguous()
         if out is None:
             out = torch.empty(b, lq, h, d, device=self.device, dtype=q.dtype)
@@ -101,6 +103,8 @@ class FullContextRingAttention:
         if (b, lq, k.shape[1], h, k.shape[2], d) != self.shape or v.shape != k.shape:
             raise ValueError(f"full-context ring planned for {self.shape}, called with "
                              f"q {tuple(q.shape)} k {tuple(k.shape)} v {tuple(v.shape)}")
+        _require_on(self.device, q, k, v)
+        check_attn_buffers(q, k, out=out, lse=lse)
         if out is None:
             out = torch.empty(b, lq, h, d, device=self.device, dtype=q.dtype)
         desc = attn_desc(q, k, v, out, lse, softmax_scale)

@@ -25,6 +25,7 @@ import torch
 
 from . import _lib
 from .comm import PeerWindows
+from .ops import _require_on
 
 NVFP4_SCALE_DIVISOR = 448.0 * 6.0  # F8_E4M3_MAX * F4_E2M1_MAX (adapters/quant_activation_scale.py:91-100)
 
@@ -108,6 +109,7 @@ class SequenceGather:
     def __call__(self, t: torch.Tensor, orig_len: int, dim: int = 1) -> torch.Tensor:
         if self.closed:
             raise RuntimeError("this sequence gather belongs to a retired setup generation")
+        _require_on(self.device, t)
         dim = dim % t.ndim
         t = t.contiguous()
         lead = math.prod(t.shape[:dim])
@@ -156,6 +158,7 @@ class SharedActivationScale:
         """0-d scale in input's dtype: dtype(max over ranks of amax|x|) / divisor."""
         if input.dtype not in _ACT_DTYPES:
             raise ValueError(f"activation dtype {input.dtype} has no NVFP4 activation scale")
+        _require_on(self.device, input)
         flat = input.reshape(-1, input.shape[-1]) if input.ndim >= 1 and input.numel() else input.reshape(0, 1)
         if flat.stride(-1) != 1:
             flat = flat.contiguous()

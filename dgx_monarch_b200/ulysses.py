@@ -22,7 +22,7 @@ import torch
 
 from . import _lib
 from .comm import PeerWindows
-from .ops import _dtype_code, _ptr, attention_fwd
+from .ops import _dtype_code, _ptr, _require_cuda, attention_fwd
 
 
 def a2a_desc(n_tensors, world, rank, batch, seq_local, heads, head_dim, dtype, strides, seg0=0):
@@ -43,6 +43,7 @@ def ulysses_scatter(tensors: list[torch.Tensor], dst_ptrs: list[list[int]], *, w
     seg0 > 0 writes the joint (text-first canonical) order of a two-segment
     local layout instead of the rank-major concat.
     """
+    _require_cuda(*tensors)
     b, ls, h, d = tensors[0].shape
     for t in tensors:
         if t.shape != tensors[0].shape or t.dtype != tensors[0].dtype or t.stride(3) != 1:
@@ -60,6 +61,7 @@ def ulysses_scatter(tensors: list[torch.Tensor], dst_ptrs: list[list[int]], *, w
 def ulysses_gather(src: torch.Tensor, dst_ptrs: list[int], *, world: int, rank: int,
                    seq_local: int, heads: int, seg0: int = 0, stream=None) -> None:
     """Return (B, S, Hl, D) rows to the owning ranks' (B, Ls, H, D) tensors."""
+    _require_cuda(src)
     b, s, hl, d = src.shape
     if s != seq_local * world or hl * world != heads or src.stride(3) != 1:
         raise ValueError("gather source must be (B, world*seq_local, heads/world, D)")
@@ -76,6 +78,7 @@ def attention_routed(q, k, v, out_ptrs: list[int], out_strides, *, world: int, r
                      softmax_scale=None,
                      q_descale=None, k_descale=None, v_descale=None, stream=None) -> None:
     """Attention whose epilogue writes row i to rank i // seq_local's output."""
+    _require_cuda(q, k, v)
     b, lq, hl, d = q.shape
     _, lk, hkv, _ = k.shape
     desc = _lib.AttnDesc()
@@ -167,6 +170,158 @@ class UlyssesAttention:
         e1.record(stream)
         torch.cuda.synchronize()
         return e0.elapsed_time(e1) / steps
+
+    def close(self) -> None:
+        if self.windows is not None:
+            torch.cuda.synchronize(self.device)
+            self.windows.close()
+            self.windows = None
+
+
+def ulysses_scatter_joint(tensors: list[torch.Tensor], texts: list[torch.Tensor] | None,
+                          dst_ptrs: list[list[int]], *, world: int, rank: int,
+                          text_first: bool = True, stream=None) -> None:
+    """The scatter of joint attention with replicated text.
+
+    tensors[t] is this rank's (B, Ls, H, D) image rows and texts[t] its whole
+    (B, T, H, D) text (None: no text); dst_ptrs[t][r] is rank r's
+    (B, T + world*Ls, H/world, D) receive tensor.  The image rows land
+    rank-major after (text_first) or before the text rows; this rank's head
+    slice of its own text goes into its own receive tensor only.
+    """
+    texts = list(texts or [])
+    _require_cuda(*tensors, *texts)
+    b, ls, h, d = tensors[0].shape
+    for x in tensors:
+        if x.shape != tensors[0].shape or x.dtype != tensors[0].dtype or x.stride(3) != 1:
+            raise ValueError("image tensors must share shape/dtype with contiguous head_dim")
+    tr = texts[0].shape[1] if texts else 0
+    if texts and len(texts) != len(tensors):
+        raise ValueError("one text tensor per image tensor")
+    for x in texts:
+        if (tuple(x.shape) != (b, tr, h, d) or x.dtype != tensors[0].dtype or x.stride(3) != 1):
+            raise ValueError("text tensors must be (B, T, H, D) of the image dtype with contiguous head_dim")
+    if tr == 0:
+        texts = tensors  # never read: the library ignores text pointers without text rows
+    desc = a2a_desc(len(tensors), world, rank, b, ls, h, d, tensors[0].dtype,
+                    [(x.stride(0), x.stride(1), x.stride(2)) for x in tensors])
+    n = len(tensors)
+    src = (ctypes.c_void_p * n)(*[x.data_ptr() for x in tensors])
+    txt = (ctypes.c_void_p * n)(*[x.data_ptr() for x in texts])
+    strides = (ctypes.c_int64 * (3 * n))(*[s for x in texts for s in (x.stride(0), x.stride(1), x.stride(2))])
+    dst = (ctypes.c_void_p * (n * world))(*[q for row in dst_ptrs for q in row])
+    stream = stream or torch.cuda.current_stream(tensors[0].device)
+    _lib.check(_lib.load().dgxm_ulysses_scatter_joint(ctypes.byref(desc), tr, 1 if text_first else 0, txt,
+                                                      strides, src, dst, stream.cuda_stream),
+               "dgxm_ulysses_scatter_joint")
+
+
+class JointUlyssesAttention:
+    """Ulysses joint image+text attention whose text every rank holds in full.
+
+    The image rows are split by sequence over the P ranks and the text rows
+    are replicated.  One step, per rank:
+      1. dgxm_ulysses_scatter_joint: the image rows go head slice by head
+         slice into every rank's receive tensors (rank-major), and this rank
+         copies its head slice of its own text next to them -- no text
+         crosses NVLink;
+      2. dgxm_comm_barrier;
+      3. attention over [text | image] ([image | text] when not text_first)
+         for the local heads; the epilogue stores image rows to their owners
+         and text rows to every rank at this rank's head columns, the
+         all-gather of the text output over heads;
+      4. dgxm_comm_barrier.
+    The result is one-process attention over the unsharded concatenation:
+    (image output (B, Ls, H, D) of this rank's rows, text output (B, T, H, D),
+    the same on every rank).
+
+    Inputs of any float dtype are computed in bf16 and returned in their own
+    dtype.  A head_dim below 128 (a multiple of 8) runs zero-padded to 128:
+    the padded columns add exact zeros to every logit and give zero output
+    columns, which are dropped; the softmax scale stays 1/sqrt(head_dim).
+    """
+
+    KERNEL_HEAD_DIM = 128
+
+    def __init__(self, *, world: int, rank: int, batch: int, seq_local: int, txt_rows: int,
+                 heads: int, head_dim: int, device: torch.device, text_first: bool = True,
+                 group=None, generation: int = 0, softmax_scale: float | None = None) -> None:
+        if heads % world:
+            raise ValueError(f"{heads} heads do not divide the Ulysses degree {world}")
+        if head_dim > self.KERNEL_HEAD_DIM or head_dim % 8:
+            raise ValueError(f"head_dim {head_dim} is not a multiple of 8 up to {self.KERNEL_HEAD_DIM}")
+        if seq_local < 1 or txt_rows < 0:
+            raise ValueError("each rank needs at least one image row and a non-negative text length")
+        device = torch.device(device)
+        if device.type == "cuda" and device.index is None:
+            device = torch.device("cuda", torch.cuda.current_device())
+        self.world, self.rank, self.device = world, rank, device
+        self.b, self.ls, self.t, self.h, self.d = batch, seq_local, txt_rows, heads, head_dim
+        self.hl = heads // world
+        self.text_first = text_first
+        self.scale = softmax_scale or 1.0 / math.sqrt(head_dim)
+        dk = self.KERNEL_HEAD_DIM
+        self.rows = txt_rows + world * seq_local
+        dt = torch.bfloat16
+        recv_bytes = batch * self.rows * self.hl * dk * 2
+        img_bytes = batch * seq_local * heads * dk * 2
+        txt_bytes = batch * max(txt_rows, 1) * heads * dk * 2
+        self.windows = PeerWindows(3 * recv_bytes + img_bytes + txt_bytes + 6 * 256, device=device,
+                                   group=group, rank=rank, world=world, generation=generation)
+        w = self.windows
+        self.off_recv = [w.carve(recv_bytes) for _ in range(3)]
+        self.off_img = w.carve(img_bytes)
+        self.off_txt = w.carve(txt_bytes)
+        self.recv = [w.local_tensor(o, (batch, self.rows, self.hl, dk), dt) for o in self.off_recv]
+        self.img_out = w.local_tensor(self.off_img, (batch, seq_local, heads, dk), dt)
+        self.txt_out = (w.local_tensor(self.off_txt, (batch, txt_rows, heads, dk), dt) if txt_rows > 0
+                        else None)
+        self.padded = head_dim != dk
+        if self.padded:
+            self.stage_img = [torch.zeros(batch, seq_local, heads, dk, device=device, dtype=dt) for _ in range(3)]
+            self.stage_txt = [torch.zeros(batch, max(txt_rows, 1), heads, dk, device=device, dtype=dt)[:, :txt_rows]
+                              for _ in range(3)]
+        self.launches_per_step = 4 + (1 if txt_rows > 0 else 0)
+
+    def _stage(self, xs, stage):
+        if self.padded:
+            for x, s in zip(xs, stage):
+                s[..., :self.d].copy_(x)
+            return stage
+        return [x if x.device == self.device and x.dtype == torch.bfloat16 and x.stride(3) == 1 else
+                x.to(device=self.device, dtype=torch.bfloat16).contiguous() for x in xs]
+
+    def forward(self, q_img, k_img, v_img, q_txt, k_txt, v_txt):
+        for x in (q_img, k_img, v_img):
+            if tuple(x.shape) != (self.b, self.ls, self.h, self.d):
+                raise ValueError(f"image tensor {tuple(x.shape)} is not {(self.b, self.ls, self.h, self.d)}")
+        for x in (q_txt, k_txt, v_txt):
+            if tuple(x.shape) != (self.b, self.t, self.h, self.d):
+                raise ValueError(f"text tensor {tuple(x.shape)} is not {(self.b, self.t, self.h, self.d)}")
+        imgs = self._stage((q_img, k_img, v_img), self.stage_img if self.padded else None)
+        txts = self._stage((q_txt, k_txt, v_txt), self.stage_txt if self.padded else None)
+        w, p = self.windows, self.world
+        ulysses_scatter_joint(list(imgs), list(txts) if self.t > 0 else None,
+                              [[w.peer_ptr(r, off) for r in range(p)] for off in self.off_recv],
+                              world=p, rank=self.rank, text_first=self.text_first)
+        w.barrier()
+        from .ops import attention_fwd_ext
+
+        dk = self.KERNEL_HEAD_DIM
+        route = {"o_peers": [w.peer_ptr(r, self.off_img) for r in range(p)], "world": p,
+                 "rank": self.rank, "seq_local": self.ls,
+                 "txt_rows": self.t, "txt_front": self.text_first,
+                 "txt_peers": [w.peer_ptr(r, self.off_txt) for r in range(p)]}
+        attention_fwd_ext(self.recv[0], self.recv[1], self.recv[2], route=route,
+                          out_strides=(self.ls * self.h * dk, self.h * dk, dk),
+                          softmax_scale=self.scale)
+        w.barrier()
+        img = self.img_out[..., :self.d].to(q_img.dtype, copy=True)
+        if self.txt_out is None:
+            return img, torch.empty(self.b, 0, self.h, self.d, device=self.device, dtype=q_img.dtype)
+        return img, self.txt_out[..., :self.d].to(q_img.dtype, copy=True)
+
+    __call__ = forward
 
     def close(self) -> None:
         if self.windows is not None:

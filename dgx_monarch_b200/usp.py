@@ -422,6 +422,10 @@ def make_b200_usp_attention(*, ulysses_group=None, ring_group=None, generation: 
             q_l = q.reshape(b, -1, h, d)
             k_l = _reshape(k, "key")
             v_l = _reshape(v, "value")
+        if q_l.shape[-1] != 128:
+            raise UnsupportedModelError(
+                f"head_dim {q_l.shape[-1]}: the B200 sequence-parallel kernels run head_dim 128 "
+                "(JointUlyssesAttention zero-pads smaller heads)")
         kv_heads = k_l.shape[2]
         if v_l.shape[2] != kv_heads:
             raise UnsupportedModelError(f"key/value head counts differ ({kv_heads} vs {v_l.shape[2]})")

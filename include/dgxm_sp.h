@@ -131,13 +131,26 @@ typedef struct dgxm_attn_extras {
   int32_t bias_keys[DGXM_MAX_BIAS_GROUPS];
 } dgxm_attn_extras;
 
-/* Output routing of the fused inverse all-to-all (see dgxm_attn_fwd_routed). */
+/* Output routing of the fused inverse all-to-all (see dgxm_attn_fwd_routed).
+ *
+ * Replicated text (txt_rows > 0): the gathered axis holds txt_rows text rows
+ * -- every rank holds the whole text and attends its own head slice of it --
+ * before (txt_front = 1) or after (txt_front = 0) the world*seq_local image
+ * rows, so q_len = txt_rows + world*seq_local.  Image rows route as above
+ * (rank-major, seg0 must be 0).  Text output row i of query head h goes to
+ * EVERY rank r: row i, head rank*q_heads + h of txt_peers[r], a (batch,
+ * txt_rows, world*q_heads, head_dim) tensor with the row and head strides of
+ * desc->o_stride and batch stride txt_rows * o_stride[1] -- the all-gather
+ * over heads of the text output, done by the epilogue's stores. */
 typedef struct dgxm_attn_route {
   void* o_peers[8];
   int32_t world;
   int32_t rank;
   int32_t seq_local;
   int32_t seg0;
+  int32_t txt_rows;
+  int32_t txt_front;
+  void* txt_peers[8];
 } dgxm_attn_route;
 
 /*
@@ -253,6 +266,29 @@ typedef struct dgxm_a2a_desc {
  */
 int dgxm_ulysses_scatter(const dgxm_a2a_desc* desc, const void* const* src, void* const* dst,
                          void* stream);
+
+/*
+ * The scatter of the joint image+text attention whose text every rank holds
+ * in full (replicated, not sharded).  desc and src are the image rows, as for
+ * dgxm_ulysses_scatter (seg0 must be 0).  txt[t] is this rank's whole
+ * (batch, txt_rows, heads, head_dim) text tensor t, strides txt_stride[3*t ..
+ * 3*t+2] (batch, row, head; elements).  dst[t*world + r] is rank r's
+ * contiguous (batch, txt_rows + world*seq_local, heads/world, head_dim)
+ * receive tensor: this rank's image rows land rank-major after
+ * (txt_front = 1) or before (txt_front = 0) the text rows, and this rank
+ * copies head slice [rank*H/P, (rank+1)*H/P) of its own text into its own
+ * receive tensor, so no text crosses NVLink.  Follow with dgxm_comm_barrier.
+ *
+ * The key order is the unsharded [text | image] (or [image | text])
+ * concatenation, the order of the single-process attention this replaces:
+ * the joint attention of the CPU/gloo Ulysses case, image rows split by
+ * sequence, text replicated, checked against one-process SDPA (the
+ * SeqAllToAll4D call sites at adapters/usp_full_axis.py:27-29,40 around the
+ * inner kernel of adapters/wan_ring_full_context.py:160-167).
+ */
+int dgxm_ulysses_scatter_joint(const dgxm_a2a_desc* desc, int32_t txt_rows, int32_t txt_front,
+                               const void* const* txt, const int64_t* txt_stride,
+                               const void* const* src, void* const* dst, void* stream);
 
 /*
  * Head -> sequence (the inverse).  src is this rank's (batch, world*seq_local,

@@ -293,3 +293,34 @@ def test_host_streamed_attention_equals_one_device_call(lib, heads, kv_heads, gr
         streamed(hq, hk, hv, hout)
         torch.cuda.synchronize()
         assert torch.equal(hout.cuda(), want)
+
+
+def test_buffers_that_do_not_cover_the_launch_are_refused(lib):
+    """A caller-given output, LSE or descale that the kernel would overrun, or a
+    host tensor, is refused before anything launches."""
+    from dgx_monarch_b200.cfg import cfg_combine
+    from dgx_monarch_b200.ops import attention_fwd, attention_fwd_ext
+    from dgx_monarch_b200.prologue import quantize_e4m3_per_head
+
+    q, k, v = (torch.randn(1, 64, 2, 128, device="cuda").bfloat16() for _ in range(3))
+    bf16 = {"device": "cuda", "dtype": torch.bfloat16}
+    with pytest.raises(ValueError, match="out"):
+        attention_fwd(q, k, v, out=torch.empty(1, 32, 2, 128, **bf16))
+    with pytest.raises(ValueError, match="lse"):
+        attention_fwd(q, k, v, lse=torch.empty(1, 2, 32, device="cuda"))
+    with pytest.raises(ValueError, match="lse"):
+        attention_fwd_ext(q, k, v, lse=torch.empty(1, 64, 2, device="cuda"))
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        attention_fwd(q, k, v, out=torch.empty(1, 64, 2, 128, dtype=torch.bfloat16))
+    q8 = torch.empty(1, 64, 2, 128, device="cuda", dtype=torch.float8_e4m3fn)
+    with pytest.raises(ValueError, match="k_descale"):
+        attention_fwd(q8, q8, q8, q_descale=torch.ones(2, device="cuda"), k_descale=torch.ones(1, device="cuda"),
+                      v_descale=torch.ones(2, device="cuda"))
+    with pytest.raises(ValueError, match="out"):
+        quantize_e4m3_per_head(q, out=q8[:, :32])
+    with pytest.raises(ValueError, match="descale"):
+        quantize_e4m3_per_head(q, descale=torch.empty(1, device="cuda"))
+    c = torch.randn(1000, device="cuda")
+    with pytest.raises(ValueError, match="out"):
+        cfg_combine(c, c, 3.0, out=torch.empty(500, device="cuda"))
+    torch.cuda.synchronize()

@@ -579,3 +579,58 @@ def _overlapped_case(rank, world, dev):
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
 def test_overlapped_ulysses_equals_plain_step():
     _spawn(_overlapped_case, min(torch.cuda.device_count(), 4))
+
+
+def _joint_case(rank, world, dev):
+    """Joint image+text attention with the text replicated: 1024 image rows
+    split by sequence, 256 text rows on every rank, 8 heads of 64, fp32 in and
+    out.  Every rank's text output is the same bytes; both outputs are the
+    one-rank result bit for bit, and within the bf16 bound of fp32 attention
+    over the unsharded [text | image] concatenation."""
+    import torch.distributed as dist
+
+    from dgx_monarch_b200 import _lib
+    from dgx_monarch_b200.ulysses import JointUlyssesAttention
+    from tests.test_attn_gpu import BF16_MAX_ABS, BF16_REL_L2, reference_attention, rel_l2
+
+    check = Checks(rank)
+    heads, d, image, text = 8, 64, 1024, 256
+    ls = image // world
+    g = torch.Generator(device=dev).manual_seed(2024)
+    img = [torch.randn(1, image, heads, d, device=dev, generator=g) for _ in range(3)]
+    txt = [torch.randn(1, text, heads, d, device=dev, generator=g) for _ in range(3)]
+    mine = [x[:, rank * ls:(rank + 1) * ls].contiguous() for x in img]
+    for text_first in (True, False):
+        joint = JointUlyssesAttention(world=world, rank=rank, batch=1, seq_local=ls, txt_rows=text,
+                                      heads=heads, head_dim=d, device=dev, text_first=text_first,
+                                      generation=31 + int(text_first))
+        out_img, out_txt = joint(*mine, *txt)
+        torch.cuda.synchronize()
+        joint.close()
+        alone = JointUlyssesAttention(world=1, rank=0, batch=1, seq_local=image, txt_rows=text, heads=heads,
+                                      head_dim=d, device=dev, text_first=text_first)
+        one_img, one_txt = alone(*img, *txt)
+        torch.cuda.synchronize()
+        alone.close()
+        tag = "text first" if text_first else "text last"
+        check(out_img.dtype == torch.float32 and out_txt.dtype == torch.float32, f"{tag}: output dtype")
+        check(torch.equal(out_img, one_img[:, rank * ls:(rank + 1) * ls]), f"{tag}: image rows differ from one rank")
+        check(torch.equal(out_txt, one_txt), f"{tag}: text differs from one rank")
+        every = [torch.empty_like(out_txt) for _ in range(world)]
+        dist.all_gather(every, out_txt)
+        check(all(torch.equal(e, every[0]) for e in every), f"{tag}: ranks hold different text outputs")
+        q, k, v = (torch.cat([a, b] if text_first else [b, a], dim=1).bfloat16() for a, b in zip(txt, img))
+        ref, _ = reference_attention(q, k, v)
+        ref_txt, ref_img = (ref[:, :text], ref[:, text:]) if text_first else (ref[:, image:], ref[:, :image])
+        for got, want, what in ((out_img, ref_img[:, rank * ls:(rank + 1) * ls], "image"), (out_txt, ref_txt, "text")):
+            check.le((got - want).abs().max().item(), BF16_MAX_ABS, f"{tag}: {what} max-abs")
+            check.le(rel_l2(got, want), BF16_REL_L2, f"{tag}: {what} rel-L2")
+    check(_lib.device_error() == 0, f"device error word {_lib.device_error()}")
+    check.close()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
+def test_joint_attention_with_replicated_text_across_gpus():
+    _spawn(_joint_case, 2)
+    if torch.cuda.device_count() >= 4:
+        _spawn(_joint_case, 4)

@@ -198,3 +198,120 @@ def test_emulated_ring_merge_equals_full_attention(lib):
         torch.cuda.synchronize()
         assert rel_l2(out, ref[:, r * rows:(r + 1) * rows]) <= BF16_REL_L2
         assert (lse - ref_lse[:, :, r * rows:(r + 1) * rows]).abs().max().item() <= 2e-3
+
+
+@pytest.mark.parametrize("world,batch,image_local,text,heads,text_first", [
+    (2, 1, 512, 256, 8, True),     # 1024 image + 256 text rows, 8 heads, split 2-way
+    (4, 2, 75, 77, 8, False),      # ragged tiles, text after the image
+    (8, 1, 40, 13, 16, True),
+    (1, 1, 300, 33, 4, True)])
+def test_replicated_text_joint_emulated_ranks(lib, world, batch, image_local, text, heads, text_first):
+    """Joint attention with the image split by sequence and the text replicated.
+
+    - Every receive tensor holds this rank's head slice of the text next to the
+      rank-major image rows (bit-exact).
+    - The routed epilogue stores exactly what per-rank attention over the
+      receive tensor computes: image rows at their owners, text rows at every
+      rank (bit-exact), so all ranks hold the same text output.
+    - The result matches one-process attention over the unsharded concatenation.
+    """
+    from dgx_monarch_b200.ops import attention_fwd, attention_fwd_ext
+    from dgx_monarch_b200.ulysses import ulysses_scatter_joint
+
+    g = torch.Generator(device="cuda").manual_seed(100 + world)
+    ls, hl, d = image_local, heads // world, 128
+    s_img = ls * world
+    rows = text + s_img
+    img = [torch.randn(batch, s_img, heads, d, device="cuda", generator=g).bfloat16() for _ in range(3)]
+    txt = [torch.randn(batch, text, heads, d, device="cuda", generator=g).bfloat16() for _ in range(3)]
+    nan = float("nan")
+    recv = [[torch.full((batch, rows, hl, d), nan, device="cuda", dtype=torch.bfloat16) for _ in range(world)]
+            for _ in range(3)]
+    for src in range(world):
+        local = [x[:, src * ls:(src + 1) * ls].contiguous() for x in img]
+        ulysses_scatter_joint(local, txt, [[recv[t][r].data_ptr() for r in range(world)] for t in range(3)],
+                              world=world, rank=src, text_first=text_first)
+    torch.cuda.synchronize()
+    for t in range(3):
+        for r in range(world):
+            heads_r = slice(r * hl, (r + 1) * hl)
+            parts = [txt[t][:, :, heads_r], img[t][:, :, heads_r]]
+            want = torch.cat(parts if text_first else parts[::-1], dim=1)
+            assert torch.equal(recv[t][r], want)
+
+    img_out = [torch.full((batch, ls, heads, d), nan, device="cuda", dtype=torch.bfloat16) for _ in range(world)]
+    txt_out = [torch.full((batch, text, heads, d), nan, device="cuda", dtype=torch.bfloat16) for _ in range(world)]
+    for r in range(world):
+        attention_fwd_ext(recv[0][r], recv[1][r], recv[2][r],
+                          route={"o_peers": [o.data_ptr() for o in img_out], "world": world, "rank": r,
+                                 "seq_local": ls, "txt_rows": text, "txt_front": text_first,
+                                 "txt_peers": [o.data_ptr() for o in txt_out]},
+                          out_strides=(ls * heads * d, heads * d, d))
+    torch.cuda.synchronize()
+    for r in range(world):
+        full, _ = attention_fwd(recv[0][r], recv[1][r], recv[2][r], return_lse=False)
+        f_txt, f_img = (full[:, :text], full[:, text:]) if text_first else (full[:, s_img:], full[:, :s_img])
+        heads_r = slice(r * hl, (r + 1) * hl)
+        for owner in range(world):
+            assert torch.equal(img_out[owner][:, :, heads_r], f_img[:, owner * ls:(owner + 1) * ls])
+            assert torch.equal(txt_out[owner][:, :, heads_r], f_txt)
+    q, k, v = (torch.cat([a, b] if text_first else [b, a], dim=1) for a, b in zip(txt, img))
+    ref, _ = reference_attention(q, k, v)
+    ref_txt, ref_img = (ref[:, :text], ref[:, text:]) if text_first else (ref[:, s_img:], ref[:, :s_img])
+    got_img = torch.cat(img_out, dim=1)
+    for got, want in ((got_img, ref_img), (txt_out[0], ref_txt)):
+        assert (got.float() - want).abs().max().item() <= BF16_MAX_ABS
+        assert rel_l2(got, want) <= BF16_REL_L2
+
+
+@pytest.mark.parametrize("head_dim,dtype,text_first", [
+    (64, torch.float32, True),     # the fp32, head_dim 64 CPU/gloo joint case's data
+    (64, torch.float32, False),
+    (96, torch.float16, True),
+    (128, torch.bfloat16, True)])
+def test_joint_ulysses_class_one_rank(lib, head_dim, dtype, text_first):
+    """JointUlyssesAttention on one rank: any float dtype in and out (bf16
+    compute), head_dim below 128 zero-padded with the softmax scale of the real
+    head_dim; 1024 image + 256 text rows, 8 heads."""
+    from dgx_monarch_b200.ulysses import JointUlyssesAttention
+
+    dev = torch.device("cuda")
+    g = torch.Generator(device="cuda").manual_seed(head_dim)
+    img = [torch.randn(1, 1024, 8, head_dim, device=dev, generator=g).to(dtype) for _ in range(3)]
+    txt = [torch.randn(1, 256, 8, head_dim, device=dev, generator=g).to(dtype) for _ in range(3)]
+    joint = JointUlyssesAttention(world=1, rank=0, batch=1, seq_local=1024, txt_rows=256, heads=8,
+                                  head_dim=head_dim, device=dev, text_first=text_first)
+    try:
+        out_img, out_txt = joint(*img, *txt)
+        again_img, again_txt = joint(*img, *txt)
+    finally:
+        joint.close()
+    assert out_img.dtype == dtype and out_txt.dtype == dtype
+    assert out_img.shape == (1, 1024, 8, head_dim) and out_txt.shape == (1, 256, 8, head_dim)
+    assert torch.equal(out_img, again_img) and torch.equal(out_txt, again_txt)
+    q, k, v = (torch.cat([a, b] if text_first else [b, a], dim=1).bfloat16() for a, b in zip(txt, img))
+    ref, _ = reference_attention(q, k, v)
+    ref_txt, ref_img = (ref[:, :256], ref[:, 256:]) if text_first else (ref[:, 1024:], ref[:, :1024])
+    for got, want in ((out_img, ref_img), (out_txt, ref_txt)):
+        assert (got.float() - want).abs().max().item() <= BF16_MAX_ABS
+        assert rel_l2(got, want) <= BF16_REL_L2
+
+
+def test_joint_ulysses_without_text_is_plain_attention(lib):
+    """No text rows: the joint step is bit-identical to the attention kernel."""
+    from dgx_monarch_b200.ops import attention_fwd
+    from dgx_monarch_b200.ulysses import JointUlyssesAttention
+
+    dev = torch.device("cuda")
+    g = torch.Generator(device="cuda").manual_seed(3)
+    q, k, v = (torch.randn(2, 200, 4, 128, device=dev, generator=g).bfloat16() for _ in range(3))
+    joint = JointUlyssesAttention(world=1, rank=0, batch=2, seq_local=200, txt_rows=0, heads=4, head_dim=128,
+                                  device=dev)
+    empty = torch.empty(2, 0, 4, 128, device=dev, dtype=torch.bfloat16)
+    try:
+        out, out_txt = joint(q, k, v, empty, empty, empty)
+    finally:
+        joint.close()
+    want, _ = attention_fwd(q, k, v, return_lse=False)
+    assert out_txt.shape == (2, 0, 4, 128)
+    assert torch.equal(out, want)
