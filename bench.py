@@ -50,6 +50,9 @@ def parse_args():
     p.add_argument("--cpu-budget", type=float, default=12.0,
                    help="seconds of CPU work for the CPU baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--p-chunks", type=int, choices=[0, 1, 2, 4], default=0,
+                   help="release each block's probabilities to the tensor core in this many "
+                        "chunks (0: the library default)")
     return p.parse_args()
 
 
@@ -470,6 +473,10 @@ def main() -> None:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
+    if args.p_chunks:
+        from dgx_monarch_b200.ops import set_p_chunks
+
+        set_p_chunks(args.p_chunks)
     if world > 1:
         from datetime import timedelta
 
@@ -623,7 +630,8 @@ def main() -> None:
             "data": "synthetic (Q/K/V ~ N(0,1), seeded)",
             "config": {"workload": WORKLOAD, "seq_len": SEQ, "heads": HEADS, "head_dim": DIM,
                        "batch": BATCH, "parallelism": f"ulysses{world}",
-                       "l2": "inputs larger than L2 (Q/K/V 2.3 GB)"},
+                       "l2": "inputs larger than L2 (Q/K/V 2.3 GB)",
+                       "p_chunks": args.p_chunks or "library default (1)"},
             "tokens_per_s": BATCH * SEQ / (ms * 1e-3),
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
                          "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],

@@ -48,6 +48,16 @@
 #ifndef DGXM_SM_THR_BF16
 #define DGXM_SM_THR_BF16 8.0f  // stale-max threshold of the bf16 kernel (log2 units)
 #endif
+// P is released to the tensor core in 1, 2 or 4 chunks per block (at most 2
+// for e4m3), chosen per call (DGXM_ATTN_P_CHUNKS in the descriptor flags;
+// this default when the flags leave it 0).  With more than one, each softmax
+// thread stores and signals a chunk of its probabilities as soon as they are
+// computed, and the MMA issuer starts the P.V steps of that chunk while the
+// rest is still in the exponential loop: the softmax -> P.V dependency that
+// bounds the block time shrinks by the later chunks' share of the loop.
+#ifndef DGXM_SM_P_CHUNKS
+#define DGXM_SM_P_CHUNKS 1
+#endif
 
 namespace dgxm {
 
@@ -84,6 +94,14 @@ struct AttnCfg {
   static constexpr int kSmemBytes = 1024 /*align slack*/ + 2 * kTileBytes + kStages * kTileBytes +
                                     1024 /*barriers + slots*/ + 12 * 128 * 4 /*row exchange*/;
 };
+
+// P chunks of a kernel built for NCH: e4m3 blocks hold whole 32-key MMA
+// steps per column half only up to two chunks.
+template <bool FP8, int NCH>
+__host__ __device__ constexpr int p_chunks() {
+  static_assert(NCH == 1 || NCH == 2 || NCH == 4, "P chunks: 1, 2 or 4");
+  return (FP8 && NCH > 2) ? 2 : NCH;
+}
 
 struct __align__(64) AttnParams {
   CUtensorMap tmap_q;  // dims (D, H, L, B), box (128 bytes, 1, 128, 1)
@@ -129,14 +147,14 @@ struct __align__(64) AttnParams {
 };
 
 // Barrier slots inside the control block.
-template <int kStages>
+template <int kStages, int kPChunks>
 struct Bars {
   static constexpr int kQ = 0;
   static constexpr int kKvFull = 1;
   static constexpr int kKvEmpty = kKvFull + kStages;
   static constexpr int kSFull = kKvEmpty + kStages;  // 2
-  static constexpr int kPFull = kSFull + 2;          // 2
-  static constexpr int kOFull = kPFull + 2;          // 2
+  static constexpr int kPFull = kSFull + 2;          // 2 tiles x kPChunks, tile-major
+  static constexpr int kOFull = kPFull + 2 * kPChunks;  // 2
   static constexpr int kPvDone = kOFull + 2;         // 2
   static constexpr int kDrain = kPvDone + 2;
   static constexpr int kCount = kDrain + 1;
@@ -201,15 +219,59 @@ __device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint3
   }
 }
 
+// The P V steps of one P chunk: the keys [64 c + ch K, 64 c + (ch + 1) K) of
+// both column halves c, K = 64 / kPChunks -- the probabilities one chunk of
+// every softmax thread has stored.  The first step of chunk 0 starts the
+// accumulation when `accumulate` is false.
+template <bool FP8, int kPChunks>
+__device__ __forceinline__ void issue_pv_chunk(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_lo,
+                                               bool accumulate, int ch) {
+  using C = AttnCfg<FP8>;
+  constexpr uint32_t hi = sdesc_hi(1024);
+  constexpr int kKeys = 64 / kPChunks;         // keys of one column half in one chunk
+  constexpr int kSteps = kKeys / C::kMmaK;     // MMAs per column half per chunk
+  static_assert(kSteps >= 1 && kKeys % C::kMmaK == 0, "a chunk holds whole MMA K steps");
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+#pragma unroll
+    for (int q = 0; q < kSteps; ++q) {
+      const int kk = (c * 64 + ch * kKeys) / C::kMmaK + q;
+      const uint64_t b = sdesc_join(v_lo + ((kk * C::kMmaK * 128) >> 4), hi);
+      const uint32_t a = p_tmem + kk * (C::kMmaK * C::kEltBytes / 4);
+      const uint32_t acc = (accumulate || ch > 0 || c > 0 || q > 0) ? 1u : 0u;
+      if constexpr (FP8)
+        umma_f8_ts(d_tmem, a, b, C::kIdescPV, acc);
+      else
+        umma_f16_ts(d_tmem, a, b, C::kIdescPV, acc);
+    }
+  }
+}
+
+// O += P V of one tile, chunk by chunk as the softmax releases P: each chunk
+// waits for its own barrier.  Returns false when a wait gave up.
+template <bool FP8, int kPChunks, int kBarPFull>
+__device__ __forceinline__ bool issue_pv_chunks(uint64_t* bars, uint32_t d_tmem, uint32_t p_tmem,
+                                                uint32_t v_lo, bool accumulate, int parity,
+                                                volatile int* abort_flag) {
+#pragma unroll
+  for (int ch = 0; ch < kPChunks; ++ch) {
+    if (!mbar_wait(smem_u32(&bars[kBarPFull + ch]), parity, abort_flag)) return false;
+    tc_fence_after();
+    issue_pv_chunk<FP8, kPChunks>(d_tmem, p_tmem, v_lo, accumulate, ch);
+  }
+  return true;
+}
+
 __device__ __forceinline__ void raise_abort(volatile int* abort_flag, int bits) {
   report_device_error(bits);
   *abort_flag = 1;
 }
 
-template <bool FP8, bool OUT_F32, bool EXTRA>
+template <bool FP8, bool OUT_F32, bool EXTRA, int NCH>
 __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_constant__ AttnParams p) {
   using C = AttnCfg<FP8>;
-  using B = Bars<C::kStages>;
+  constexpr int kPChunks = p_chunks<FP8, NCH>();
+  using B = Bars<C::kStages, kPChunks>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -233,7 +295,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(bar(B::kSFull + t), 1);
-      mbar_init(bar(B::kPFull + t), 256);
+      for (int ch = 0; ch < kPChunks; ++ch) mbar_init(bar(B::kPFull + t * kPChunks + ch), 256);
       mbar_init(bar(B::kOFull + t), 1);
       mbar_init(bar(B::kPvDone + t), 1);
     }
@@ -332,9 +394,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
         // O1 += P1 V_{j-1}
         if (j > 0) {
           const int vs = (2 * j - 1) % C::kStages;
-          if (!(ok = mbar_wait(bar(B::kPFull + 1), (j - 1) & 1, abort_flag))) break;
-          tc_fence_after();
-          issue_pv<FP8>(tO1, tS1, kv_lo_v + vs * kStageLo, j - 1 > 0);
+          if constexpr (kPChunks > 1) {
+            if (!(ok = issue_pv_chunks<FP8, kPChunks, B::kPFull + kPChunks>(
+                      bars, tO1, tS1, kv_lo_v + vs * kStageLo, j - 1 > 0, (j - 1) & 1, abort_flag)))
+              break;
+          } else {
+            if (!(ok = mbar_wait(bar(B::kPFull + 1), (j - 1) & 1, abort_flag))) break;
+            tc_fence_after();
+            issue_pv<FP8>(tO1, tS1, kv_lo_v + vs * kStageLo, j - 1 > 0);
+          }
           umma_commit(bar(B::kKvEmpty + vs));
           if (safe_order) {
             umma_commit(bar(B::kPvDone + 1));
@@ -350,19 +418,32 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
         const int vi = 2 * j + 1;
         const int vs = vi % C::kStages;
         if (!(ok = mbar_wait(bar(B::kKvFull + vs), (vi / C::kStages) & 1, abort_flag))) break;
-        if (!(ok = mbar_wait(bar(B::kPFull + 0), j & 1, abort_flag))) break;
-        tc_fence_after();
-        issue_pv<FP8>(tO0, tS0, kv_lo_v + vs * kStageLo, j > 0);
+        if constexpr (kPChunks > 1) {
+          if (!(ok = issue_pv_chunks<FP8, kPChunks, B::kPFull>(bars, tO0, tS0, kv_lo_v + vs * kStageLo, j > 0,
+                                                     j & 1, abort_flag)))
+            break;
+        } else {
+          if (!(ok = mbar_wait(bar(B::kPFull + 0), j & 1, abort_flag))) break;
+          tc_fence_after();
+          issue_pv<FP8>(tO0, tS0, kv_lo_v + vs * kStageLo, j > 0);
+        }
         if (safe_order) umma_commit(bar(B::kPvDone + 0));
         if (j == nkv - 1) umma_commit(bar(B::kOFull + 0));
       }
       if (ok) {
         // O1 += P1 V_{n-1}
         const int vs = (2 * nkv - 1) % C::kStages;
-        ok = mbar_wait(bar(B::kPFull + 1), (nkv - 1) & 1, abort_flag);
+        if constexpr (kPChunks > 1) {
+          ok = issue_pv_chunks<FP8, kPChunks, B::kPFull + kPChunks>(bars, tO1, tS1, kv_lo_v + vs * kStageLo,
+                                                            nkv - 1 > 0, (nkv - 1) & 1, abort_flag);
+        } else {
+          ok = mbar_wait(bar(B::kPFull + 1), (nkv - 1) & 1, abort_flag);
+          if (ok) {
+            tc_fence_after();
+            issue_pv<FP8>(tO1, tS1, kv_lo_v + vs * kStageLo, nkv - 1 > 0);
+          }
+        }
         if (ok) {
-          tc_fence_after();
-          issue_pv<FP8>(tO1, tS1, kv_lo_v + vs * kStageLo, nkv - 1 > 0);
           umma_commit(bar(B::kKvEmpty + vs));
           umma_commit(bar(B::kOFull + 1));
         }
@@ -510,62 +591,130 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
       // p = 2^(s * sl2 - m) (times kPScale for e4m3, folded into the exponent).
       // A row whose keys so far were all excluded keeps m = -inf and p = 0.
       const float bias = -(EXTRA && m_run == -INFINITY ? 0.f : m_run) + C::kPScaleLog2;
-      const uint64_t sl2x2 = pk2(sl2, sl2), biasx2 = pk2(bias, bias);
-      uint64_t sum_a = pk2(0.f, 0.f), sum_b = pk2(0.f, 0.f);
-      uint32_t pk[32];
+      if constexpr (kPChunks > 1) {
+        const uint64_t sl2x2 = pk2(sl2, sl2), biasx2 = pk2(bias, bias);
+        uint64_t sum_a = pk2(0.f, 0.f), sum_b = pk2(0.f, 0.f);
+        constexpr int kPairs = 32 / kPChunks;  // exponential pairs per chunk
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        uint64_t x = ffma2(pk2(s[2 * i], s[2 * i + 1]), sl2x2, biasx2);
-        float p0, p1;
-        if (DGXM_SM_POLY_MOD > 0 && (i % (DGXM_SM_POLY_MOD > 0 ? DGXM_SM_POLY_MOD : 1)) == 0) {
-          x = exp2_poly2(x);
-          upk2(x, p0, p1);
-        } else {
-          upk2(x, p0, p1);
-          p0 = ex2_approx(p0);
-          p1 = ex2_approx(p1);
-          x = pk2(p0, p1);
+        for (int ch = 0; ch < kPChunks; ++ch) {
+          uint32_t pk[kPairs];
+#pragma unroll
+          for (int q = 0; q < kPairs; ++q) {
+            const int i = ch * kPairs + q;
+            uint64_t x = ffma2(pk2(s[2 * i], s[2 * i + 1]), sl2x2, biasx2);
+            float p0, p1;
+            if (DGXM_SM_POLY_MOD > 0 && (i % (DGXM_SM_POLY_MOD > 0 ? DGXM_SM_POLY_MOD : 1)) == 0) {
+              x = exp2_poly2(x);
+              upk2(x, p0, p1);
+            } else {
+              upk2(x, p0, p1);
+              p0 = ex2_approx(p0);
+              p1 = ex2_approx(p1);
+              x = pk2(p0, p1);
+            }
+            if (i & 1) sum_b = fadd2(sum_b, x); else sum_a = fadd2(sum_a, x);
+            if constexpr (FP8) {
+              s[2 * i] = p0;
+              s[2 * i + 1] = p1;
+            } else {
+              pk[q] = pack_bf16x2(p0, p1);
+            }
+          }
+          if constexpr (FP8) {
+            // 2 kPairs keys of this chunk, four per column.
+            uint32_t q8[kPairs / 2];
+#pragma unroll
+            for (int k = 0; k < kPairs / 2; ++k) {
+              const int e = 2 * ch * kPairs + 4 * k;
+              q8[k] = pack_e4m3x4(s[e], s[e + 1], s[e + 2], s[e + 3]);
+            }
+            tmem_st_n<kPairs / 2>(tP + ch * (kPairs / 2), q8);
+          } else {
+            tmem_st_n<kPairs>(tP + ch * kPairs, pk);
+          }
+          if (ch == 0 && rescale) {
+            // O is rescaled before the first chunk is released, since the
+            // P V of this block starts with that chunk.  O_t is quiescent
+            // here: the commit behind this S_t also covered the previous
+            // P_t V product.  Eight columns at a time, because the later
+            // chunks' logits are still held in registers.
+#pragma unroll
+            for (int h8 = 0; h8 < 8; ++h8) {
+              uint32_t o[8];
+              tmem_ld8(tO + h8 * 8, o);
+              tmem_wait_ld();
+              reg_fence8(o);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+              tmem_st8(tO + h8 * 8, o);
+            }
+          }
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(bar(B::kPFull + t * kPChunks + ch));
         }
-        if (i & 1) sum_b = fadd2(sum_b, x); else sum_a = fadd2(sum_a, x);
-        if constexpr (FP8) {
-          s[2 * i] = p0;
-          s[2 * i + 1] = p1;
-        } else {
-          pk[i] = pack_bf16x2(p0, p1);
-        }
-      }
-      {
         float a0, a1, b0, b1;
         upk2(sum_a, a0, a1);
         upk2(sum_b, b0, b1);
         l_run += ((a0 + a1) + (b0 + b1)) * (1.0f / C::kPScale);
-      }
-      if constexpr (FP8) {
-        uint32_t q8[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i)
-          q8[i] = pack_e4m3x4(s[4 * i], s[4 * i + 1], s[4 * i + 2], s[4 * i + 3]);
-        tmem_st16(tP, q8);
       } else {
-        tmem_st32(tP, pk);
-      }
-      if (rescale) {
-        // O_t is quiescent here: the commit behind this S_t also covered the
-        // previous P_t V product.
+        const uint64_t sl2x2 = pk2(sl2, sl2), biasx2 = pk2(bias, bias);
+        uint64_t sum_a = pk2(0.f, 0.f), sum_b = pk2(0.f, 0.f);
+        uint32_t pk[32];
 #pragma unroll
-        for (int h2 = 0; h2 < 2; ++h2) {
-          uint32_t o[32];
-          tmem_ld32(tO + h2 * 32, o);
-          tmem_wait_ld();
-          reg_fence32(o);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st32(tO + h2 * 32, o);
+        for (int i = 0; i < 32; ++i) {
+          uint64_t x = ffma2(pk2(s[2 * i], s[2 * i + 1]), sl2x2, biasx2);
+          float p0, p1;
+          if (DGXM_SM_POLY_MOD > 0 && (i % (DGXM_SM_POLY_MOD > 0 ? DGXM_SM_POLY_MOD : 1)) == 0) {
+            x = exp2_poly2(x);
+            upk2(x, p0, p1);
+          } else {
+            upk2(x, p0, p1);
+            p0 = ex2_approx(p0);
+            p1 = ex2_approx(p1);
+            x = pk2(p0, p1);
+          }
+          if (i & 1) sum_b = fadd2(sum_b, x); else sum_a = fadd2(sum_a, x);
+          if constexpr (FP8) {
+            s[2 * i] = p0;
+            s[2 * i + 1] = p1;
+          } else {
+            pk[i] = pack_bf16x2(p0, p1);
+          }
         }
+        {
+          float a0, a1, b0, b1;
+          upk2(sum_a, a0, a1);
+          upk2(sum_b, b0, b1);
+          l_run += ((a0 + a1) + (b0 + b1)) * (1.0f / C::kPScale);
+        }
+        if constexpr (FP8) {
+          uint32_t q8[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            q8[i] = pack_e4m3x4(s[4 * i], s[4 * i + 1], s[4 * i + 2], s[4 * i + 3]);
+          tmem_st16(tP, q8);
+        } else {
+          tmem_st32(tP, pk);
+        }
+        if (rescale) {
+          // O_t is quiescent here: the commit behind this S_t also covered the
+          // previous P_t V product.
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2) {
+            uint32_t o[32];
+            tmem_ld32(tO + h2 * 32, o);
+            tmem_wait_ld();
+            reg_fence32(o);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(tO + h2 * 32, o);
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(bar(B::kPFull + t));
       }
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(bar(B::kPFull + t));
     }
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar(B::kOFull + t), 0, abort_flag));
     // Combine the two halves' row sums (all threads of the group take part,
@@ -690,11 +839,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
   }
 }
 
-template <bool FP8, bool OUT_F32, bool EXTRA>
+template <bool FP8, bool OUT_F32, bool EXTRA, int NCH>
 static int launch_attn(const AttnParams& prm, dim3 grid, cudaStream_t stream) {
   using C = AttnCfg<FP8>;
   static uint64_t configured = 0;  // one bit per device ordinal
-  auto kern = attn_fwd_kernel<FP8, OUT_F32, EXTRA>;
+  auto kern = attn_fwd_kernel<FP8, OUT_F32, EXTRA, NCH>;
   int dev = 0;
   DGXM_CUDA_TRY(cudaGetDevice(&dev));
   const uint64_t bit = uint64_t(1) << (dev & 63);
@@ -795,15 +944,28 @@ static int prepare_attn(const dgxm_attn_desc* d, const void* q, const void* k, c
   return DGXM_OK;
 }
 
-template <bool EXTRA>
-static int dispatch_attn_t(const dgxm_attn_desc* d, const AttnParams& prm, dim3 grid, cudaStream_t st) {
+template <bool EXTRA, int NCH>
+static int dispatch_attn_n(const dgxm_attn_desc* d, const AttnParams& prm, dim3 grid, cudaStream_t st) {
   const bool fp8 = d->in_dtype == DGXM_DTYPE_E4M3;
   const bool out_f32 = d->out_dtype == DGXM_DTYPE_F32;
+  constexpr int kFp8Chunks = p_chunks<true, NCH>();  // 4 runs as 2: one instantiation
   if (fp8)
-    return out_f32 ? launch_attn<true, true, EXTRA>(prm, grid, st)
-                   : launch_attn<true, false, EXTRA>(prm, grid, st);
-  return out_f32 ? launch_attn<false, true, EXTRA>(prm, grid, st)
-                 : launch_attn<false, false, EXTRA>(prm, grid, st);
+    return out_f32 ? launch_attn<true, true, EXTRA, kFp8Chunks>(prm, grid, st)
+                   : launch_attn<true, false, EXTRA, kFp8Chunks>(prm, grid, st);
+  return out_f32 ? launch_attn<false, true, EXTRA, NCH>(prm, grid, st)
+                 : launch_attn<false, false, EXTRA, NCH>(prm, grid, st);
+}
+
+template <bool EXTRA>
+static int dispatch_attn_t(const dgxm_attn_desc* d, const AttnParams& prm, dim3 grid, cudaStream_t st) {
+  int nch = (d->flags & DGXM_ATTN_P_CHUNKS_MASK) >> DGXM_ATTN_P_CHUNKS_SHIFT;
+  if (nch == 0) nch = DGXM_SM_P_CHUNKS;
+  switch (nch) {
+    case 1: return dispatch_attn_n<EXTRA, 1>(d, prm, grid, st);
+    case 2: return dispatch_attn_n<EXTRA, 2>(d, prm, grid, st);
+    case 4: return dispatch_attn_n<EXTRA, 4>(d, prm, grid, st);
+    default: return fail(DGXM_ERR_INVALID, "%d P chunks per block (1, 2 or 4)", nch);
+  }
 }
 
 static int dispatch_attn(const dgxm_attn_desc* d, const AttnParams& prm, dim3 grid, void* stream) {

@@ -80,6 +80,24 @@ def check_attn_buffers(q: torch.Tensor, k: torch.Tensor, *, out: torch.Tensor | 
             raise ValueError(f"{name} must be a contiguous fp32 vector of {n} heads")
 
 
+_P_CHUNKS = 0  # 0: the library's default release of P per 128-key block
+
+
+def set_p_chunks(chunks: int) -> None:
+    """Release each block's probabilities to the tensor core in `chunks` parts
+    (1, 2 or 4; 0 restores the library default) in every attention call this
+    process makes from now on (DGXM_ATTN_P_CHUNKS)."""
+    global _P_CHUNKS
+    if chunks not in (0, 1, 2, 4):
+        raise ValueError(f"P is released in 1, 2 or 4 chunks, not {chunks}")
+    _P_CHUNKS = chunks
+
+
+def attn_flags(safe_order: bool = False) -> int:
+    """The descriptor flags of one attention call."""
+    return (_lib.ATTN_SAFE_ORDER if safe_order else 0) | (_P_CHUNKS << _lib.ATTN_P_CHUNKS_SHIFT)
+
+
 def attn_desc(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor,
               lse: torch.Tensor | None, softmax_scale: float | None = None,
               safe_order: bool = False) -> _lib.AttnDesc:
@@ -98,7 +116,7 @@ def attn_desc(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tens
     if lse is not None:
         desc.lse_stride[:] = [lse.stride(0), lse.stride(1), lse.stride(2)]
     desc.softmax_scale = float(softmax_scale) if softmax_scale else 1.0 / math.sqrt(d)
-    desc.flags = _lib.ATTN_SAFE_ORDER if safe_order else 0
+    desc.flags = attn_flags(safe_order)
     return desc
 
 

@@ -22,7 +22,7 @@ import torch
 
 from . import _lib
 from .comm import PeerWindows
-from .ops import _dtype_code, _ptr, _require_cuda, attention_fwd
+from .ops import _dtype_code, _ptr, _require_cuda, attention_fwd, attn_flags
 
 
 def a2a_desc(n_tensors, world, rank, batch, seq_local, heads, head_dim, dtype, strides, seg0=0):
@@ -93,6 +93,7 @@ def attention_routed(q, k, v, out_ptrs: list[int], out_strides, *, world: int, r
     if lse is not None:
         desc.lse_stride[:] = [lse.stride(0), lse.stride(1), lse.stride(2)]
     desc.softmax_scale = float(softmax_scale) if softmax_scale else 1.0 / math.sqrt(d)
+    desc.flags = attn_flags()
     peers = (ctypes.c_void_p * world)(*out_ptrs)
     stream = stream or torch.cuda.current_stream(q.device)
     _lib.check(_lib.load().dgxm_attn_fwd_routed(

@@ -41,6 +41,14 @@ extern "C" {
 /* Drain each P.V product before the next Q.K^T product reuses its tensor
  * memory columns (slower; kept as a cross-check of the fast ordering). */
 #define DGXM_ATTN_SAFE_ORDER 1
+/* Release the probabilities of each 128-key block to the tensor core in 1, 2
+ * or 4 chunks (e4m3: 4 runs as 2), so P.V starts on the first chunk while the
+ * softmax computes the rest.  0 keeps the library's default.  Results agree
+ * within the attention tolerance across chunk counts (the P.V steps
+ * accumulate in another order). */
+#define DGXM_ATTN_P_CHUNKS_SHIFT 4
+#define DGXM_ATTN_P_CHUNKS_MASK (7 << DGXM_ATTN_P_CHUNKS_SHIFT)
+#define DGXM_ATTN_P_CHUNKS(n) ((n) << DGXM_ATTN_P_CHUNKS_SHIFT)
 
 /* Version of this ABI; bumped on any incompatible change. */
 int dgxm_abi_version(void);
