@@ -842,16 +842,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
 template <bool FP8, bool OUT_F32, bool EXTRA, int NCH>
 static int launch_attn(const AttnParams& prm, dim3 grid, cudaStream_t stream) {
   using C = AttnCfg<FP8>;
-  static uint64_t configured = 0;  // one bit per device ordinal
+  static std::atomic<uint64_t> configured{0};  // one bit per device ordinal
   auto kern = attn_fwd_kernel<FP8, OUT_F32, EXTRA, NCH>;
-  int dev = 0;
-  DGXM_CUDA_TRY(cudaGetDevice(&dev));
-  const uint64_t bit = uint64_t(1) << (dev & 63);
-  if (!(configured & bit)) {
-    DGXM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       C::kSmemBytes));
-    configured |= bit;
-  }
+  DGXM_CUDA_TRY(set_smem_limit_once(kern, C::kSmemBytes, configured));
   kern<<<grid, kAttnThreads, C::kSmemBytes, stream>>>(prm);
   DGXM_CUDA_TRY(cudaGetLastError());
   return DGXM_OK;

@@ -4,6 +4,7 @@
 
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <atomic>
 #include <stdarg.h>
 #include <stdint.h>
 #include <stdio.h>
@@ -23,6 +24,21 @@ int cuda_fail(cudaError_t e, const char* what);
     cudaError_t _e = (expr);                                 \
     if (_e != cudaSuccess) return ::dgxm::cuda_fail(_e, #expr); \
   } while (0)
+
+// Raise `kern`'s dynamic shared-memory limit to `bytes` on the current device,
+// once per device: `done` keeps one bit per device ordinal below 64 (others
+// are set on every call).  Safe to call from several host threads.
+template <typename Kernel>
+cudaError_t set_smem_limit_once(Kernel kern, int bytes, std::atomic<uint64_t>& done) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = dev < 64 ? uint64_t(1) << dev : 0;
+  if (bit != 0 && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && bit != 0) done.fetch_or(bit, std::memory_order_acq_rel);
+  return e;
+}
 
 // Encode a 4-D tiled tensor map over a (batch, row, head, col) tensor whose
 // innermost dimension `cols` is contiguous.  Strides are in elements.

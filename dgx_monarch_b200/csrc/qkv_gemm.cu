@@ -311,12 +311,8 @@ extern "C" int dgxm_qkv_gemm_prologue_scatter(const dgxm_qkv_gemm_desc* d, const
   int dev = 0, sms = 148;
   DGXM_CUDA_TRY(cudaGetDevice(&dev));
   DGXM_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-  static unsigned configured = 0;  // bit per device
-  if (dev < 32 && !(configured & (1u << dev))) {
-    DGXM_CUDA_TRY(cudaFuncSetAttribute(qkv_gemm_prologue_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       kQkvSmemBytes));
-    configured |= 1u << dev;
-  }
+  static std::atomic<uint64_t> configured{0};  // bit per device
+  DGXM_CUDA_TRY(set_smem_limit_once(qkv_gemm_prologue_kernel, kQkvSmemBytes, configured));
   const int tiles = p.m_tiles * p.n_tiles;
   const int grid = tiles < sms ? tiles : sms;
   qkv_gemm_prologue_kernel<<<grid, kQkvThreads, kQkvSmemBytes, static_cast<cudaStream_t>(stream)>>>(p);
