@@ -27,6 +27,7 @@ collectives require, so the window exchange on first use stays collective.
 """
 from __future__ import annotations
 
+import math
 
 import torch
 
@@ -35,6 +36,11 @@ from .comm import PeerWindows
 from .ops import attention_fwd, attention_fwd_ext, keep_bits
 from .ring import FullContextRingAttention, RingAttention
 from .ulysses import attention_routed, ulysses_gather, ulysses_scatter
+
+
+# The head dimension the kernels run; smaller heads (multiples of 8) are
+# zero-padded to it, as the capability table's limit of 128 promises.
+KERNEL_HEAD_DIM = 128
 
 
 class UnsupportedModelError(RuntimeError):
@@ -142,8 +148,10 @@ class B200SequenceParallelAttention:
         return plan
 
     # ---------------------------------------------------------------- forward
-    def attend(self, q_l, k_l, v_l, drop_rows, kv_drop_rows, sequence_order, bias_groups=None):
-        """(B, Ls, H, D) local rows in, (B, Ls, H, D) local rows out."""
+    def attend(self, q_l, k_l, v_l, drop_rows, kv_drop_rows, sequence_order, bias_groups=None,
+               softmax_scale=None):
+        """(B, Ls, H, D) local rows in, (B, Ls, H, D) local rows out.  softmax_scale
+        None is 1/sqrt(D)."""
         if self.closed:
             raise UnsupportedModelError("this attention implementation belongs to a retired setup "
                                         "generation and cannot run")
@@ -171,15 +179,15 @@ class B200SequenceParallelAttention:
         _check_pad_rows(ls * p, drop_rows)
         _check_pad_rows(k_l.shape[1] * p, kv_drop_rows)
         if p == 1 and g.ring_world == 1 and not self.fp8:
-            return self._local(q_l, k_l, v_l, drop_rows, kv_drop_rows, bias_groups)
+            return self._local(q_l, k_l, v_l, drop_rows, kv_drop_rows, bias_groups, softmax_scale)
         if p == 1 and g.ring_world == 1 and not (drop_rows or kv_drop_rows or bias_groups):
-            return self._local_fp8(q_l, k_l, v_l)
+            return self._local_fp8(q_l, k_l, v_l, softmax_scale)
         if self.fp8 and (g.ring_world > 1 or drop_rows or kv_drop_rows or bias_groups):
             raise UnsupportedModelError(
                 "the B200 FP8 attention path runs pure Ulysses without pad rows; use the bf16 "
                 "kernel for ring topologies or padded sequences")
         if g.ring_world > 1:
-            return self._hybrid(q_l, k_l, v_l)
+            return self._hybrid(q_l, k_l, v_l, softmax_scale)
         plan = self._ulysses_plan(b, ls, h, hkv, d, q_l.dtype)
         win, offs = plan["win"], plan["offs"]
         if hkv == h:
@@ -200,10 +208,11 @@ class B200SequenceParallelAttention:
                 quantize_e4m3_per_head(src, out=dst, descale=ds)
             attention_routed(plan["q8"], plan["k8"], plan["v8"], out_ptrs, (ls * h * d, h * d, d),
                              world=p, rank=g.uly_rank, seq_local=ls, seg0=seg0,
-                             q_descale=plan["ds"][0], k_descale=plan["ds"][1], v_descale=plan["ds"][2])
+                             q_descale=plan["ds"][0], k_descale=plan["ds"][1], v_descale=plan["ds"][2],
+                             softmax_scale=softmax_scale)
         elif not drop_rows and not kv_drop_rows and not bias_groups:
             attention_routed(qg, kg, vg, out_ptrs, (ls * h * d, h * d, d), world=p, rank=g.uly_rank,
-                             seq_local=ls, seg0=seg0)
+                             seq_local=ls, seg0=seg0, softmax_scale=softmax_scale)
         else:
             # Pads and biases live on the full axis, which this rank holds for
             # its heads; the kernel applies both and still routes the output.
@@ -213,21 +222,22 @@ class B200SequenceParallelAttention:
                                                      kg.shape[1], kv_drop_rows),
                               route={"o_peers": out_ptrs, "world": p, "rank": g.uly_rank,
                                      "seq_local": ls, "seg0": seg0},
-                              out_strides=(ls * h * d, h * d, d))
+                              out_strides=(ls * h * d, h * d, d), softmax_scale=softmax_scale)
         win.barrier()
         return plan["out"].clone()
 
-    def _local(self, q, k, v, drop_rows, kv_drop_rows, bias_groups=None):
+    def _local(self, q, k, v, drop_rows, kv_drop_rows, bias_groups=None, softmax_scale=None):
         if drop_rows or kv_drop_rows or bias_groups:
             out, _ = attention_fwd_ext(q, k, v, key_keep=keep_bits(k.shape[1], kv_drop_rows, q.device),
                                        query_keep=keep_bits(q.shape[1], drop_rows, q.device),
                                        bias_groups=_rank_bias(bias_groups, 0, q.shape[2],
-                                                              k.shape[1], kv_drop_rows))
+                                                              k.shape[1], kv_drop_rows),
+                                       softmax_scale=softmax_scale)
             return out
-        out, _ = attention_fwd(q, k, v, return_lse=False)
+        out, _ = attention_fwd(q, k, v, return_lse=False, softmax_scale=softmax_scale)
         return out
 
-    def _local_fp8(self, q, k, v):
+    def _local_fp8(self, q, k, v, softmax_scale=None):
         """One rank, e4m3: quantise the caller's heads in place of a scatter
         and attend into a fresh output (no window copy, no barrier)."""
         from .prologue import quantize_e4m3_per_head
@@ -244,10 +254,11 @@ class B200SequenceParallelAttention:
         for src, dst, ds in zip((q, k, v), (bufs["q8"], bufs["k8"], bufs["v8"]), bufs["ds"]):
             quantize_e4m3_per_head(src, out=dst, descale=ds)
         out, _ = attention_fwd(bufs["q8"], bufs["k8"], bufs["v8"], q_descale=bufs["ds"][0],
-                               k_descale=bufs["ds"][1], v_descale=bufs["ds"][2], return_lse=False)
+                               k_descale=bufs["ds"][1], v_descale=bufs["ds"][2], return_lse=False,
+                               softmax_scale=softmax_scale)
         return out
 
-    def _hybrid(self, q_l, k_l, v_l):
+    def _hybrid(self, q_l, k_l, v_l, softmax_scale=None):
         """Ulysses inside the Ulysses group, ring across the ring group."""
         g = self.groups
         b, ls, h, d = q_l.shape
@@ -264,7 +275,7 @@ class B200SequenceParallelAttention:
         else:
             qg, kg, vg = q_l, k_l, v_l
         ring = self._ring_plan(b, qg.shape[1], kg.shape[1], qg.shape[2], kg.shape[2], d, q_l.dtype)
-        out_g, _ = ring.forward(qg, kg, vg)
+        out_g, _ = ring.forward(qg, kg, vg, softmax_scale=softmax_scale)
         if p == 1:
             return out_g
         ulysses_gather(out_g, [win.peer_ptr(r, offs[3]) for r in range(p)], world=p, rank=g.uly_rank,
@@ -422,10 +433,11 @@ def make_b200_usp_attention(*, ulysses_group=None, ring_group=None, generation: 
             q_l = q.reshape(b, -1, h, d)
             k_l = _reshape(k, "key")
             v_l = _reshape(v, "value")
-        if q_l.shape[-1] != 128:
+        head_dim = q_l.shape[-1]
+        if head_dim > KERNEL_HEAD_DIM or head_dim % 8:
             raise UnsupportedModelError(
-                f"head_dim {q_l.shape[-1]}: the B200 sequence-parallel kernels run head_dim 128 "
-                "(JointUlyssesAttention zero-pads smaller heads)")
+                f"head_dim {head_dim}: the B200 sequence-parallel kernels carry head dimensions up "
+                f"to {KERNEL_HEAD_DIM} in multiples of 8")
         kv_heads = k_l.shape[2]
         if v_l.shape[2] != kv_heads:
             raise UnsupportedModelError(f"key/value head counts differ ({kv_heads} vs {v_l.shape[2]})")
@@ -478,9 +490,17 @@ def make_b200_usp_attention(*, ulysses_group=None, ring_group=None, generation: 
             sequence_order = None
         if q_l.dtype != torch.bfloat16:
             q_l, k_l, v_l = (t.to(torch.bfloat16) for t in (q_l, k_l, v_l))
+        if head_dim < KERNEL_HEAD_DIM:
+            # Zero columns add exact zeros to every logit and give zero output
+            # columns; the scale stays that of the real head dimension.
+            q_l, k_l, v_l = (torch.nn.functional.pad(t, (0, KERNEL_HEAD_DIM - head_dim))
+                             for t in (q_l, k_l, v_l))
         q_l, k_l, v_l = (t if t.stride(-1) == 1 else t.contiguous() for t in (q_l, k_l, v_l))
         kv_rows = drop_rows if kv_drop_rows is None else kv_drop_rows
-        out = impl.attend(q_l, k_l, v_l, drop_rows, kv_rows, sequence_order, query_bias_groups)
+        out = impl.attend(q_l, k_l, v_l, drop_rows, kv_rows, sequence_order, query_bias_groups,
+                          softmax_scale=1.0 / math.sqrt(head_dim))
+        if head_dim < KERNEL_HEAD_DIM:
+            out = out[..., :head_dim]
         out = out.to(q.dtype)
         if skip_output_reshape:
             return out.transpose(1, 2)

@@ -4,12 +4,10 @@ P.V steps of a chunk start while the rest is computed.  Same contract as the
 one-chunk kernel: bf16 output max-abs <= 2e-2 and rel-L2 <= 5e-3, LSE within
 2e-3 of fp32 attention; e4m3 rel-L2 <= 3e-2; masks and routing unchanged.
 
-The chunked kernels run only when DGXM_TEST_P_CHUNKS=1 is set, so their
-first run on a B200 is a deliberate one; the library default stays one chunk.
+These tests carry the first_run marker (tests/conftest.py): the chunked
+kernels have not yet run on a B200, and the library default stays one chunk.
 """
 from __future__ import annotations
-
-import os
 
 import pytest
 import torch
@@ -17,9 +15,7 @@ import torch
 from tests.test_attn_gpu import (BF16_MAX_ABS, BF16_REL_L2, FP8_REL_L2, LSE_ABS, SHAPES,
                                  quantize_e4m3_per_head, reference_attention, rel_l2)
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("DGXM_TEST_P_CHUNKS") != "1",
-                                 reason="the chunked P release runs when DGXM_TEST_P_CHUNKS=1")]
+pytestmark = [pytest.mark.gpu, pytest.mark.first_run]
 
 
 @pytest.fixture

@@ -181,3 +181,30 @@ def test_fp8_callable_on_one_rank(lib):
     ref, _ = reference_attention(q, k, v)
     assert rel_l2(out, ref) <= 8e-2  # e4m3 inputs against bf16 activations
     attn.impl.invalidate()
+
+
+@pytest.mark.first_run
+@pytest.mark.parametrize("head_dim", [64, 96])
+def test_small_head_dims_run_zero_padded(attn, head_dim):
+    """Heads below 128 (LTX-Video's 64) run zero-padded with the scale of their
+    own head dimension: plain, and with LTX guide biases on tail pads."""
+    real, pad, heads = 700, 20, 4
+    g = torch.Generator(device="cuda").manual_seed(head_dim)
+    q, k, v = (torch.randn(1, real + pad, heads, head_dim, device="cuda", generator=g).bfloat16()
+               for _ in range(3))
+    out = attn(*(t.reshape(1, real + pad, -1) for t in (q, k, v)), heads=heads)
+    assert out.shape == (1, real + pad, heads * head_dim)
+    ref, _ = reference_attention(q, k, v)
+    got = out.reshape(1, real + pad, heads, head_dim)
+    assert (got.float() - ref).abs().max().item() <= BF16_MAX_ABS
+    assert rel_l2(got, ref) <= BF16_REL_L2
+
+    weights = torch.rand(150, device="cuda", generator=g) + 0.1
+    groups = ltx_guide_groups(real, 520, weights)
+    drop = list(range(real, real + pad))
+    out = attn(*(t.transpose(1, 2) for t in (q, k, v)), heads=heads, skip_reshape=True,
+               skip_output_reshape=True, drop_rows=drop, query_bias_groups=groups).transpose(1, 2)
+    want = oracle_grouped(q, k, v, drop, groups)
+    assert out.shape == (1, real + pad, heads, head_dim)
+    assert (out[:, :real].double() - want[:, :real]).abs().max().item() <= BF16_MAX_ABS
+    assert torch.equal(out[:, real:], torch.zeros_like(out[:, real:]))

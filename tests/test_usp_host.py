@@ -1,0 +1,69 @@
+"""Host logic of the usp_attention drop-in, on the CPU: head dimensions below
+the kernels' 128 are zero-padded with the softmax scale of the real head
+dimension, and the output is trimmed back; unsupported head dimensions are
+refused before any device work.  The implementation's `attend` is replaced by
+the float64 oracle, so only the callable's own reshapes, padding, scale and
+trimming are under test here (the kernels are tested on the GPU)."""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import usp as oracle
+
+
+def _callable_with_oracle_attend(seen, head_dim):
+    """A CPU callable whose attend records its arguments and runs the oracle."""
+    from dgx_monarch_b200.usp import make_b200_usp_attention
+
+    attn = make_b200_usp_attention(device=torch.device("cpu"))
+
+    def attend(q, k, v, drop_rows, kv_rows, order, groups, softmax_scale=None):
+        seen.append({"shape": tuple(q.shape), "kv_shape": tuple(k.shape), "scale": softmax_scale,
+                     "dtype": q.dtype,
+                     "pad_max": max(float(t[..., head_dim:].abs().max()) if t.shape[-1] > head_dim else 0.0
+                                    for t in (q, k, v))})
+        out, _ = oracle.attention_lse(q.double().numpy(), k.double().numpy(), v.double().numpy(),
+                                      scale=softmax_scale)
+        return torch.from_numpy(out).to(torch.bfloat16)
+
+    attn.impl.attend = attend
+    return attn
+
+
+@pytest.mark.parametrize("head_dim,heads,kv_heads", [(64, 4, 4), (72, 3, 3), (96, 4, 2), (128, 2, 2)])
+def test_small_heads_are_padded_with_their_own_scale(head_dim, heads, kv_heads):
+    seen = []
+    attn = _callable_with_oracle_attend(seen, head_dim)
+    g = torch.Generator().manual_seed(head_dim)
+    q = torch.randn(1, 40, heads * head_dim, generator=g)
+    k = torch.randn(1, 40, kv_heads * head_dim, generator=g)
+    v = torch.randn(1, 40, kv_heads * head_dim, generator=g)
+    out = attn(q, k, v, heads=heads, enable_gqa=kv_heads != heads)
+    (call,) = seen
+    assert call["shape"] == (1, 40, heads, 128)
+    assert call["kv_shape"][-1] == 128
+    assert call["dtype"] == torch.bfloat16
+    assert call["pad_max"] == 0.0
+    assert call["scale"] == pytest.approx(1.0 / math.sqrt(head_dim))
+    assert out.shape == q.shape and out.dtype == q.dtype
+    # One-process attention over the bf16-rounded, unpadded inputs.
+    qb, kb, vb = (t.bfloat16().double().reshape(1, 40, -1, head_dim).numpy() for t in (q, k, v))
+    want, _ = oracle.attention_lse(qb, kb, vb)
+    got = out.reshape(1, 40, heads, head_dim).double().numpy()
+    assert np.abs(got - want).max() <= 2e-2
+
+
+@pytest.mark.parametrize("head_dim", [130, 256, 60, 4])
+def test_unsupported_head_dims_are_refused(head_dim):
+    from dgx_monarch_b200.usp import UnsupportedModelError
+
+    seen = []
+    attn = _callable_with_oracle_attend(seen, head_dim)
+    x = torch.zeros(1, 8, 2 * head_dim)
+    with pytest.raises(UnsupportedModelError, match=f"head_dim {head_dim}"):
+        attn(x, x, x, heads=2)
+    assert not seen
