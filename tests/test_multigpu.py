@@ -634,3 +634,49 @@ def test_joint_attention_with_replicated_text_across_gpus():
     _spawn(_joint_case, 2)
     if torch.cuda.device_count() >= 4:
         _spawn(_joint_case, 4)
+
+
+def _hybrid_case(rank, world, dev):
+    """Ulysses inside runs of consecutive ranks and ring across them (the
+    ulysses-low layout of oracle.usp.hybrid_groups): each rank holds one
+    sequence chunk in rank order, and its output rows equal unsharded
+    attention over the whole sequence."""
+    import torch.distributed as dist
+
+    from dgx_monarch_b200 import _lib
+    from dgx_monarch_b200.usp import make_b200_usp_attention
+    from oracle.usp import hybrid_groups
+    from tests.test_attn_gpu import BF16_MAX_ABS, BF16_REL_L2, reference_attention, rel_l2
+
+    check = Checks(rank)
+    uly, ring = 2, world // 2
+    ulysses_groups, ring_groups = hybrid_groups(world, uly, ring)
+    mine_u = mine_r = None
+    for ranks in ulysses_groups:
+        grp = dist.new_group(ranks)
+        if rank in ranks:
+            mine_u = grp
+    for ranks in ring_groups:
+        grp = dist.new_group(ranks)
+        if rank in ranks:
+            mine_r = grp
+    attn = make_b200_usp_attention(ulysses_group=mine_u, ring_group=mine_r, generation=41, device=dev)
+    heads, ls = 4, 300
+    g = torch.Generator(device=dev).manual_seed(77)
+    q, k, v = (torch.randn(1, ls * world, heads, 128, device=dev, generator=g).bfloat16() for _ in range(3))
+    rows = slice(rank * ls, (rank + 1) * ls)
+    for step in range(2):
+        out = attn(*(t[:, rows].reshape(1, ls, -1) for t in (q, k, v)), heads=heads)
+        torch.cuda.synchronize()
+        ref, _ = reference_attention(q, k, v)
+        got = out.reshape(1, ls, heads, 128)
+        check.le((got.float() - ref[:, rows]).abs().max().item(), BF16_MAX_ABS, f"call {step} max abs")
+        check.le(rel_l2(got, ref[:, rows]), BF16_REL_L2, f"call {step} rel l2")
+    check(_lib.device_error() == 0, f"device error word {_lib.device_error()}")
+    attn.impl.invalidate()
+    check.close()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 4, reason="needs four or more GPUs")
+def test_hybrid_ulysses_ring_across_gpus():
+    _spawn(_hybrid_case, 4)
