@@ -67,3 +67,44 @@ def test_unsupported_head_dims_are_refused(head_dim):
     with pytest.raises(UnsupportedModelError, match=f"head_dim {head_dim}"):
         attn(x, x, x, heads=2)
     assert not seen
+
+
+def _unpack(bits: torch.Tensor, rows: int) -> np.ndarray:
+    words = bits.numpy().astype(np.uint32)
+    return np.array([(int(words[i // 32]) >> (i % 32)) & 1 for i in range(rows)], dtype=bool)
+
+
+@pytest.mark.parametrize("rows,drop", [(140, [5, 139]), (64, [0, 31, 32, 63]), (1216, list(range(1200, 1216))),
+                                       (33, [32]), (700, [0, 5, 127, 128, 255, 256, 311, 699])])
+def test_keep_bits_mark_exactly_the_oracle_kept_rows(rows, drop):
+    """Bit i of word i // 32 is set exactly for the rows the oracle keeps
+    (adapters/usp_pad_exclusion.py:79-126); bits past the axis stay clear."""
+    from dgx_monarch_b200.ops import keep_bits
+
+    bits = keep_bits(rows, drop, torch.device("cpu"))
+    assert bits.dtype == torch.int32 and bits.numel() == (rows + 31) // 32
+    kept = np.zeros(rows, dtype=bool)
+    kept[oracle.kept_rows(rows, drop)] = True
+    np.testing.assert_array_equal(_unpack(bits, rows), kept)
+    tail = int(bits[-1].item()) & 0xFFFFFFFF
+    assert tail >> (rows % 32 or 32) == 0
+
+
+def test_keep_bits_are_cached_per_layout_and_device():
+    """Built once per (rows, drop set, device) from host integers -- nothing is
+    read back from a device -- and a cached entry equals a fresh build, as
+    tests/test_usp_pad_index_cache.py pins for the reference's keep index."""
+    from dgx_monarch_b200 import ops
+
+    ops._KEEP_BITS.clear()
+    first = ops.keep_bits(300, [7, 299], torch.device("cpu"))
+    assert ops.keep_bits(300, [299, 7, 7], torch.device("cpu")) is first
+    other = ops.keep_bits(301, [7, 299], torch.device("cpu"))
+    assert other is not first
+    ops._KEEP_BITS.clear()
+    assert torch.equal(ops.keep_bits(300, [7, 299], torch.device("cpu")), first)
+    assert ops.keep_bits(300, [], torch.device("cpu")) is None
+    with pytest.raises(ValueError, match="carries 300 rows"):
+        ops.keep_bits(300, [300], torch.device("cpu"))
+    with pytest.raises(ValueError):
+        ops.keep_bits(300, [-1], torch.device("cpu"))
