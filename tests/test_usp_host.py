@@ -108,3 +108,84 @@ def test_keep_bits_are_cached_per_layout_and_device():
         ops.keep_bits(300, [300], torch.device("cpu"))
     with pytest.raises(ValueError):
         ops.keep_bits(300, [-1], torch.device("cpu"))
+
+
+_GROUP_CASES = [
+    ((0, 4, None), (4, 10, None)),
+    ((0, 4, None), (6, 10, None)),
+    ((0, 6, None), (4, 10, None)),
+    ((0, 6, None),),
+    ((0, 12, None),),
+    ((0, 10, np.zeros((1, 1, 3, 10))),),
+    ((0, 10, np.zeros((1, 1, 1, 40))),),
+    ((0, 10, np.zeros((1, 1, 1, 10))),),
+    ((0, 3, np.zeros((1, 2, 3, 8))), (3, 10, None)),
+]
+
+
+@pytest.mark.parametrize("groups", _GROUP_CASES)
+def test_bias_group_validation_agrees_with_the_oracle(groups):
+    """The drop-in accepts exactly the partitions the oracle's restatement of
+    adapters/usp_query_bias.py:64-92 accepts (10 queries, 20 keys)."""
+    from dgx_monarch_b200.usp import UnsupportedModelError, validate_bias_groups
+
+    as_torch = [(s, e, None if b is None else torch.from_numpy(b).float()) for s, e, b in groups]
+    try:
+        oracle.validate_query_bias_groups(list(groups), 10, 20)
+        oracle_ok = True
+    except oracle.OracleRefusal:
+        oracle_ok = False
+    try:
+        validate_bias_groups(as_torch, 10, 20, batch=1, heads=2)
+        ours_ok = True
+    except UnsupportedModelError:
+        ours_ok = False
+    assert ours_ok == oracle_ok
+
+
+def test_bias_group_validation_adds_the_kernel_limits():
+    from dgx_monarch_b200.usp import UnsupportedModelError, validate_bias_groups
+
+    with pytest.raises(UnsupportedModelError, match="broadcast over batch"):
+        validate_bias_groups([(0, 4, torch.zeros(3, 1, 1, 4))], 4, 4, batch=2, heads=1)
+    many = [(i, i + 1, torch.zeros(1, 1, 1, 4)) for i in range(9)]
+    with pytest.raises(UnsupportedModelError, match="at most 8"):
+        validate_bias_groups(many, 9, 4, batch=1, heads=1)
+
+
+@pytest.mark.parametrize("drop", [[], [18, 19], [3, 10], [0, 5, 19]])
+def test_rank_bias_slices_heads_and_spreads_past_interior_key_pads(drop):
+    """Each rank gets its own heads of a per-head bias; a bias that names keys
+    by their position among the kept keys lands on those keys of the padded
+    axis (zero at the pads, which the keep bits exclude anyway)."""
+    from dgx_monarch_b200.usp import _rank_bias
+
+    keys, heads, world = 20, 4, 2
+    hl = heads // world
+    g = torch.Generator().manual_seed(len(drop))
+    n_decl = keys - len(drop) - 2                      # declared keys, fewer than the kept ones
+    bias = torch.randn(1, heads, 3, n_decl, generator=g)
+    shared = torch.randn(1, 1, 1, n_decl, generator=g)
+    kept = [r for r in range(keys) if r not in set(drop)]
+    for rank in range(world):
+        out = _rank_bias([(0, 3, bias), (3, 5, None), (5, 6, shared)], rank, hl, keys, drop)
+        assert out[1] == (3, 5, None)
+        for (start, end, got), src in ((out[0], bias[:, rank * hl:(rank + 1) * hl]), (out[2], shared)):
+            assert got.dtype == torch.float32 and got.is_contiguous()
+            if drop and drop != list(range(keys - len(drop), keys)):
+                assert torch.equal(got[..., kept[:n_decl]], src)
+                dropped_inside = [r for r in drop if r < got.shape[-1]]
+                assert torch.count_nonzero(got[..., dropped_inside]) == 0
+            else:
+                assert torch.equal(got, src)
+
+
+@pytest.mark.parametrize("text,image,world", [(3, 5, 2), (64, 1152, 8), (1, 1, 4), (2, 7, 3)])
+def test_joint_inverse_is_the_oracle_inverse_permutation(text, image, world):
+    """rank-major gathered row -> canonical row, the inverse of the oracle's
+    RankMajorJointOrder permutation (adapters/usp_sequence_order.py:246-261)."""
+    from dgx_monarch_b200.usp import _joint_inverse
+
+    order = oracle.RankMajorJointOrder(text, image)
+    perm = order.permutation((text + image) * world)
+    assert _joint_inverse(text, image, world) == list(order.inverse(perm))
