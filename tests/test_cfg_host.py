@@ -67,3 +67,28 @@ def test_leading_batch_finds_the_first_tensor():
     assert leading_batch([None, {"a": 3, "b": torch.zeros(5, 2)}]) == 5
     assert leading_batch({"s": torch.tensor(1.0)}) is None
     assert leading_batch(("no", "tensors")) is None
+
+
+@pytest.mark.parametrize("axes", [[16, 56, 56], [0, 64, 64], [128], [32, 48, 48]])
+def test_rope_table_is_the_oracle_angles_rounded_once(axes):
+    """The fused prologue's (rows, 64, 2) cos/sin table is cos/sin of the
+    oracle's float64 angles rounded once to fp32 (Wan 3-axis, Flux 2-axis and
+    1-axis layouts)."""
+    from dgx_monarch_b200.prologue import rope_table
+
+    g = np.random.default_rng(len(axes))
+    pos = g.integers(0, 90, size=(57, len(axes)))
+    got = rope_table(torch.from_numpy(pos), axes).numpy()
+    ang = oracle.rope_table(pos, axes)
+    assert got.shape == (57, 64, 2) and got.dtype == np.float32
+    # Within one fp32 ulp of 1.0: libm and torch may round the float64 cos/sin
+    # differently in the last bit before the single rounding to fp32.
+    np.testing.assert_allclose(got[..., 0], np.cos(ang), rtol=0, atol=2.0 ** -23)
+    np.testing.assert_allclose(got[..., 1], np.sin(ang), rtol=0, atol=2.0 ** -23)
+
+
+def test_rope_table_refuses_axes_that_do_not_fill_the_head():
+    from dgx_monarch_b200.prologue import rope_table
+
+    with pytest.raises(ValueError, match="sum to the head dimension"):
+        rope_table(torch.zeros(4, 2), [64, 32])
