@@ -28,6 +28,56 @@ REF_SRC = Path("/root/reference/src")
 OUT = Path(__file__).resolve().parent
 
 
+# Kernel options handed to the Wan Ring2 ring function (flash's surface).
+_FLASH_DEFAULTS = {"dropout_p": 0.0, "softmax_scale": None, "causal": False, "window_size": (-1, -1),
+                   "softcap": 0.0, "alibi_slopes": None, "return_softmax": False}
+FLASH_SURFACE_CASES = [dict(_FLASH_DEFAULTS, **change) for change in (
+    {}, {"softmax_scale": 0.125}, {"softmax_scale": 1}, {"dropout_p": 0}, {"softcap": 0},
+    {"dropout_p": 0.1}, {"dropout_p": False}, {"dropout_p": float("nan")}, {"dropout_p": "0"},
+    {"softmax_scale": 0.0}, {"softmax_scale": -1.0}, {"softmax_scale": float("inf")},
+    {"softmax_scale": True}, {"causal": True}, {"causal": 0}, {"window_size": [-1, -1]},
+    {"window_size": (-1, 0)}, {"window_size": (-1, -1, -1)}, {"window_size": (True, -1)},
+    {"softcap": 30.0}, {"softcap": float("-inf")}, {"alibi_slopes": "slopes"},
+    {"return_softmax": True}, {"return_softmax": 0},
+)]
+
+# Local shards: (shape q, shape k, shape v, dtype, requires_grad, layout).
+LOCAL_QKV_CASES = [
+    {"q": [1, 8, 2, 128], "k": [1, 8, 2, 128], "v": [1, 8, 2, 128], "dtype": "bfloat16"},
+    {"q": [1, 8, 2, 128], "k": [1, 8, 2, 128], "v": [1, 8, 2, 128], "dtype": "bfloat16", "grad": True},
+    {"q": [8, 2, 128], "k": [8, 2, 128], "v": [8, 2, 128], "dtype": "bfloat16"},
+    {"q": [1, 8, 2, 128], "k": [1, 8, 2, 128], "v": [1, 9, 2, 128], "dtype": "bfloat16"},
+    {"q": [1, 8, 3, 128], "k": [1, 8, 2, 128], "v": [1, 8, 2, 128], "dtype": "bfloat16"},
+    {"q": [1, 0, 2, 128], "k": [1, 0, 2, 128], "v": [1, 0, 2, 128], "dtype": "bfloat16"},
+    {"q": [1, 8, 2, 128], "k": [1, 8, 2, 128], "v": [1, 8, 2, 128], "dtype": "float32"},
+    {"q": [1, 8, 2, 64], "k": [1, 8, 2, 64], "v": [1, 8, 2, 64], "dtype": "bfloat16"},
+    {"q": [1, 8, 2, 128], "k": [1, 16, 2, 128], "v": [1, 16, 2, 128], "dtype": "bfloat16"},
+]
+
+
+def encode_case(case: dict) -> dict:
+    """JSON form of a kernel-option case: tuples, non-finite floats and the
+    bool/int distinction survive (tests/test_full_context_host.py decodes)."""
+    def enc(x):
+        if isinstance(x, tuple):
+            return {"tuple": [enc(y) for y in x]}
+        if isinstance(x, list):
+            return {"list": [enc(y) for y in x]}
+        if isinstance(x, float) and not math.isfinite(x):
+            return {"float": repr(x)}
+        return x
+    return {key: enc(value) for key, value in case.items()}
+
+
+def build_qkv(case: dict):
+    """CPU tensors of a local-shard case."""
+    dt = getattr(torch, case["dtype"])
+    q, k, v = (torch.zeros(case[n], dtype=dt) for n in "qkv")
+    if case.get("grad"):
+        q.requires_grad_(True)
+    return q, k, v
+
+
 def _install_stubs(ring_world=1, gathered=None, world=1, rank=0):
     """The xfuser / yunchang leaves, as the reference's tests stub them."""
     calls = []
@@ -360,6 +410,29 @@ def main() -> None:
         scales.append({"index": n, "dtype": str(dtype).replace("torch.", ""), "world": world,
                        "divisor": qas.NVFP4_SCALE_DIVISOR})
     golden["shared_scale"] = scales
+
+    # l) the Wan Ring2 full-context refusals (adapters/wan_ring_full_context.py:
+    #    17-117): every kernel option and local-shard case below, with the
+    #    reference's verdict -- accepted, or its refusal message.
+    from dgx_monarch.adapters import wan_ring_full_context as wfc
+
+    def verdict(fn, **kwargs):
+        try:
+            fn(**kwargs)
+            return "ok"
+        except base.UnsupportedModelError as exc:
+            return str(exc)
+
+    surface = []
+    for case in FLASH_SURFACE_CASES:
+        surface.append({"case": encode_case(case),
+                        "verdict": verdict(wfc._validate_flash_surface, **case)})
+    qkv = []
+    for case in LOCAL_QKV_CASES:
+        q, k, v = build_qkv(case)
+        qkv.append({"case": case, "verdict": verdict(wfc._validate_local_qkv, q=q, k=k, v=v)})
+    golden["full_context_surface"] = surface
+    golden["full_context_qkv"] = qkv
 
     (OUT / "golden.json").write_text(json.dumps(golden, indent=1))
     np.savez_compressed(OUT / "golden_arrays.npz", **arrays)
