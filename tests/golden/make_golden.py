@@ -55,6 +55,38 @@ LOCAL_QKV_CASES = [
 ]
 
 
+# Malformed (and two well-formed) usp_attention calls: tensor shapes, the
+# call's keyword arguments, and an optional mask ("effective" or "noop").
+USP_REFUSAL_CASES = [
+    {"q": [1, 8, 64], "k": [1, 8, 64], "v": [1, 8, 64], "kw": {"heads": 4}},
+    {"q": [1, 8, 100], "k": [1, 8, 100], "v": [1, 8, 100], "kw": {"heads": 3}},
+    {"q": [1, 8, 64], "k": [1, 8, 64], "v": [1, 8, 64], "kw": {"heads": 4, "skip_reshape": True}},
+    {"q": [1, 2, 8, 16], "k": [1, 2, 8, 16], "v": [1, 2, 8, 16], "kw": {"heads": 4, "skip_reshape": True}},
+    {"q": [1, 2, 8, 16], "k": [2, 2, 8, 16], "v": [1, 2, 8, 16], "kw": {"heads": 2, "skip_reshape": True}},
+    {"q": [1, 2, 8, 16], "k": [1, 2, 8, 16], "v": [1, 2, 8, 16], "kw": {"heads": 2}},
+    {"q": [1, 8, 32], "k": [2, 8, 32], "v": [1, 8, 32], "kw": {"heads": 2}},
+    {"q": [1, 8, 32], "k": [1, 8, 40], "v": [1, 8, 40], "kw": {"heads": 2}},
+    {"q": [1, 8, 32], "k": [1, 8, 32], "v": [1, 8, 16], "kw": {"heads": 2}},
+    {"q": [1, 8, 64], "k": [1, 8, 32], "v": [1, 8, 32], "kw": {"heads": 4}},
+    {"q": [1, 8, 48], "k": [1, 8, 32], "v": [1, 8, 32], "kw": {"heads": 3, "enable_gqa": True}},
+    {"q": [1, 8, 64], "k": [1, 8, 64], "v": [1, 8, 64], "kw": {"heads": 4}, "mask": "effective"},
+    {"q": [1, 8, 64], "k": [1, 8, 64], "v": [1, 8, 64], "kw": {"heads": 4}, "mask": "noop"},
+]
+
+
+def build_usp_call(case: dict):
+    """CPU tensors and keyword arguments of a usp_attention case."""
+    q, k, v = (torch.zeros(case[n]) for n in "qkv")
+    kwargs = dict(case["kw"])
+    if case.get("mask") == "effective":
+        mask = torch.zeros(1, 1, 8, 8)
+        mask[..., 0] = -1e9
+        kwargs["mask"] = mask
+    elif case.get("mask") == "noop":
+        kwargs["mask"] = torch.zeros(1, 1, 8, 8)
+    return q, k, v, kwargs
+
+
 def encode_case(case: dict) -> dict:
     """JSON form of a kernel-option case: tuples, non-finite floats and the
     bool/int distinction survive (tests/test_full_context_host.py decodes)."""
@@ -433,6 +465,22 @@ def main() -> None:
         qkv.append({"case": case, "verdict": verdict(wfc._validate_local_qkv, q=q, k=k, v=v)})
     golden["full_context_surface"] = surface
     golden["full_context_qkv"] = qkv
+
+    # m) the usp_attention callable's typed refusals (adapters/base.py:216-292):
+    #    each malformed call below with the reference's verdict.
+    _install_stubs()
+    attn = base._make_usp_attention_callable(sys.modules["xfuser.core.long_ctx_attention"]
+                                             .xFuserLongContextAttention())
+    refusals = []
+    for case in USP_REFUSAL_CASES:
+        q, k, v, kwargs = build_usp_call(case)
+        try:
+            attn(q, k, v, **kwargs)
+            said = "ok"
+        except base.UnsupportedModelError as exc:
+            said = str(exc)
+        refusals.append({"case": case, "verdict": said})
+    golden["usp_refusals"] = refusals
 
     (OUT / "golden.json").write_text(json.dumps(golden, indent=1))
     np.savez_compressed(OUT / "golden_arrays.npz", **arrays)

@@ -6,7 +6,9 @@ the float64 oracle, so only the callable's own reshapes, padding, scale and
 trimming are under test here (the kernels are tested on the GPU)."""
 from __future__ import annotations
 
+import json
 import math
+from pathlib import Path
 
 import numpy as np
 import pytest
@@ -189,3 +191,32 @@ def test_joint_inverse_is_the_oracle_inverse_permutation(text, image, world):
     order = oracle.RankMajorJointOrder(text, image)
     perm = order.permutation((text + image) * world)
     assert _joint_inverse(text, image, world) == list(order.inverse(perm))
+
+
+_GOLDEN = json.loads((Path(__file__).resolve().parent / "golden" / "golden.json").read_text())
+
+
+@pytest.mark.parametrize("entry", _GOLDEN["usp_refusals"], ids=lambda e: e["verdict"][:24])
+def test_typed_refusals_match_the_reference(entry):
+    """Malformed calls are refused with the reference's messages
+    (adapters/base.py:216-292, recorded by make_golden.py section (m)); the
+    well-formed ones reach the kernel."""
+    from dgx_monarch_b200.usp import UnsupportedModelError
+
+    case = entry["case"]
+    q, k, v = (torch.zeros(case[n]) for n in "qkv")
+    kwargs = dict(case["kw"])
+    if case.get("mask") == "effective":
+        kwargs["mask"] = torch.zeros(1, 1, 8, 8)
+        kwargs["mask"][..., 0] = -1e9
+    elif case.get("mask") == "noop":
+        kwargs["mask"] = torch.zeros(1, 1, 8, 8)
+    seen = []
+    attn = _callable_with_oracle_attend(seen, q.shape[-1] // kwargs["heads"] if q.ndim == 3 else q.shape[-1])
+    try:
+        attn(q, k, v, **kwargs)
+        said = "ok"
+    except UnsupportedModelError as exc:
+        said = str(exc)
+    assert said == entry["verdict"]
+    assert bool(seen) == (said == "ok")
