@@ -2,7 +2,7 @@
 // a bounded device-side barrier.
 //
 // Each rank cudaMallocs one window in its own HBM and exports a CUDA IPC
-// handle; every other rank maps it (plain peer mapping, no multicast object),
+// handle; every other rank maps it (a plain peer mapping, nothing switch-side),
 // so a kernel on rank s can store straight into rank r's window over NVLink.
 // The first 4 KB of a window hold barrier flags: slot i is written by rank i.
 //

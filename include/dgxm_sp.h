@@ -195,8 +195,8 @@ int dgxm_lse_merge(int32_t batch, int32_t rows, int32_t heads, int32_t head_dim,
 #define DGXM_IPC_HANDLE_BYTES 64
 
 /* One rank's NVLink window: device memory on the current device that every
- * peer maps through a CUDA IPC handle (a plain peer mapping; no multicast
- * object is created).  Bound to one setup generation: a handle from a retired
+ * peer maps through a CUDA IPC handle (a plain peer mapping; no NVSwitch
+ * group object is created).  Bound to one setup generation: a handle from a retired
  * generation is destroyed, never reused.
  *
  * Stands in for the process groups the reference builds in
