@@ -275,6 +275,7 @@ extern "C" int dgxm_comm_create(int32_t rank, int32_t world, int64_t bytes, uint
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_main, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_side, cudaEventDisableTiming);
     if (e != cudaSuccess) {
+      if (c->ev_main) cudaEventDestroy(c->ev_main);
       if (c->side) cudaStreamDestroy(c->side);
       cudaFree(c->local);
       delete c;
