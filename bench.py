@@ -50,6 +50,9 @@ def parse_args():
     p.add_argument("--cpu-budget", type=float, default=12.0,
                    help="seconds of CPU work for the CPU baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--e2e-groups", type=int, default=5,
+                   help="head groups the host-streamed e2e step pipelines (must divide the "
+                        "40 heads, with a multiple of the GPU count per group)")
     p.add_argument("--p-chunks", type=int, choices=[0, 1, 2, 4], default=0,
                    help="release each block's probabilities to the tensor core in this many "
                         "chunks (0: the library default)")
@@ -463,6 +466,9 @@ def main() -> None:
         return
     if args.warmup < 3:
         raise SystemExit("--warmup must be at least 3")
+    if args.e2e_groups < 1 or HEADS % args.e2e_groups or (HEADS // args.e2e_groups) % args.gpus:
+        raise SystemExit(f"--e2e-groups {args.e2e_groups}: groups must divide the {HEADS} heads into "
+                         f"groups whose size is a multiple of {args.gpus} GPUs")
     import torch
     import torch.distributed as dist
 
@@ -561,13 +567,13 @@ def main() -> None:
     hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
     hout = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
 
-    # Five groups of 8 heads, each its own Ulysses step: the PCIe copies of
-    # group g +/- 1 overlap the all-to-all and attention of group g
+    # Groups of heads (5 x 8 by default), each its own Ulysses step: the PCIe
+    # copies of group g +/- 1 overlap the all-to-all and attention of group g
     # (ulysses.HostStreamedUlysses).
     from dgx_monarch_b200.ulysses import HostStreamedUlysses
 
     streamed = HostStreamedUlysses(world=world, rank=rank, batch=BATCH, seq_local=SEQ // world, heads=HEADS,
-                                   head_dim=DIM, device=dev, groups=5, generation=12)
+                                   head_dim=DIM, device=dev, groups=args.e2e_groups, generation=12)
 
     def e2e_step():
         streamed(hq, hk, hv, hout)
@@ -641,9 +647,9 @@ def main() -> None:
                     "h2d_bytes_per_step": 3 * q.numel() * q.element_size(),
                     "d2h_bytes_per_step": out.numel() * out.element_size(),
                     "ms_per_step": e2e_ms,
-                    "method": ("pinned host Q/K/V in, pinned host output back, every step; 5 groups of 8 heads "
-                               "streamed so the PCIe copies of one group overlap the Ulysses step of another "
-                               "(HostStreamedUlysses)")},
+                    "method": (f"pinned host Q/K/V in, pinned host output back, every step; {args.e2e_groups} "
+                               f"groups of {HEADS // args.e2e_groups} heads streamed so the PCIe copies of one "
+                               "group overlap the Ulysses step of another (HostStreamedUlysses)")},
             "dit_layer": {"workload": DIT_WORKLOAD, "tokens_per_s": (DIT["img"] + DIT["txt"]) / (dit_ms * 1e-3),
                           "ms_per_layer": dit_ms, "ms_per_layer_eager": dit_ms_eager,
                           "launch": "one CUDA graph per layer (ms_per_layer_eager: the same calls from Python)",
