@@ -139,9 +139,11 @@ extern "C" int dgxm_lse_merge(int32_t batch, int32_t rows, int32_t heads, int32_
   const bool out_f32 = out_dtype == DGXM_DTYPE_F32;
   if (!out_f32 && out_dtype != DGXM_DTYPE_BF16)
     return fail(DGXM_ERR_UNSUPPORTED, "merge output dtype %d is not supported", out_dtype);
-  if (parts_out == nullptr || parts_lse == nullptr || out == nullptr)
-    return fail(DGXM_ERR_INVALID, "merge pointers must be non-NULL");
+  if (parts_out == nullptr || parts_lse == nullptr)
+    return fail(DGXM_ERR_INVALID, "merge part arrays must be non-NULL");
+  // Nothing to merge: empty tensors may carry NULL data pointers.
   if (batch == 0 || rows == 0) return DGXM_OK;
+  if (out == nullptr) return fail(DGXM_ERR_INVALID, "merge output must be non-NULL");
   MergeParams prm;
   memset(&prm, 0, sizeof(prm));
   for (int i = 0; i < n_parts; ++i) {

@@ -288,10 +288,15 @@ def lse_merge(parts_out: list[torch.Tensor], parts_lse: list[torch.Tensor], *,
             raise ValueError("merge parts must be contiguous and share shape and dtype")
         if l.shape != (b, heads, rows) or l.dtype != torch.float32 or not l.is_contiguous():
             raise ValueError("merge lse parts must be contiguous fp32 (B, H, L)")
+    _require_on(dev, out, lse_out)
     if out is None:
         out = torch.empty((b, rows, heads, d), device=dev, dtype=out_dtype)
+    elif tuple(out.shape) != (b, rows, heads, d) or not out.is_contiguous():
+        raise ValueError(f"merge output {tuple(out.shape)} is not a contiguous {(b, rows, heads, d)} tensor")
     if lse_out is None:
         lse_out = torch.empty((b, heads, rows), device=dev, dtype=torch.float32)
+    elif tuple(lse_out.shape) != (b, heads, rows) or lse_out.dtype != torch.float32 or not lse_out.is_contiguous():
+        raise ValueError(f"merge lse output must be a contiguous fp32 {(b, heads, rows)} tensor")
     n = len(parts_out)
     outs = (ctypes.c_void_p * n)(*[t.data_ptr() for t in parts_out])
     lses = (ctypes.c_void_p * n)(*[t.data_ptr() for t in parts_lse])

@@ -324,3 +324,32 @@ def test_buffers_that_do_not_cover_the_launch_are_refused(lib):
     with pytest.raises(ValueError, match="out"):
         cfg_combine(c, c, 3.0, out=torch.empty(500, device="cuda"))
     torch.cuda.synchronize()
+
+
+def test_empty_inputs_return_without_a_launch(lib):
+    """No query rows or an empty batch give empty results; an empty key axis
+    has no defined output and is refused; an empty merge and an empty
+    scatter do nothing.  None of these reaches a kernel."""
+    from dgx_monarch_b200 import _lib
+    from dgx_monarch_b200.ops import attention_fwd, lse_merge
+    from dgx_monarch_b200.ulysses import ulysses_scatter
+
+    bf16 = {"device": "cuda", "dtype": torch.bfloat16}
+    k = torch.randn(1, 64, 2, 128, device="cuda").bfloat16()
+    out, lse = attention_fwd(torch.empty(1, 0, 2, 128, **bf16), k, k)
+    assert out.shape == (1, 0, 2, 128) and lse.shape == (1, 2, 0)
+    none = torch.empty(0, 16, 2, 128, **bf16)
+    out, _ = attention_fwd(none, none, none)
+    assert out.shape == (0, 16, 2, 128)
+    no_keys = torch.empty(1, 0, 2, 128, **bf16)
+    with pytest.raises(_lib.DgxmError, match="empty key axis"):
+        attention_fwd(torch.randn(1, 16, 2, 128, device="cuda").bfloat16(), no_keys, no_keys)
+    parts = [torch.empty(1, 0, 2, 128, device="cuda") for _ in range(2)]
+    lses = [torch.empty(1, 2, 0, device="cuda") for _ in range(2)]
+    merged, merged_lse = lse_merge(parts, lses)
+    assert merged.shape == (1, 0, 2, 128) and merged_lse.shape == (1, 2, 0)
+    recv = torch.zeros(1, 8, 2, 128, **bf16)
+    ulysses_scatter([torch.empty(1, 0, 4, 128, **bf16)] * 3, [[recv.data_ptr()] * 2] * 3, world=2, rank=0)
+    torch.cuda.synchronize()
+    assert recv.abs().max().item() == 0.0
+    assert _lib.device_error() == 0
