@@ -1,7 +1,10 @@
 """Representative launches of the library's kernels, for profiler captures.
 
-    python -m dgx_monarch_b200.profile_case SEQ HEADS     # attention, three launches
-    python -m dgx_monarch_b200.profile_case kernels       # every other kernel, one GPU
+    python -m dgx_monarch_b200.profile_case SEQ HEADS [CHUNKS]  # bf16 attention, three launches
+    python -m dgx_monarch_b200.profile_case fp8 SEQ HEADS       # e4m3 attention, three launches
+    python -m dgx_monarch_b200.profile_case kernels             # every other kernel, one GPU
+
+CHUNKS selects the release of P in 1, 2 or 4 chunks per block (ops.set_p_chunks).
 
 The `kernels` cases use the C2 (Flux/Krea2 block) and C4 shapes on one rank,
 each input larger than the 126 MB L2 where the kernel is HBM-bound, and a few
@@ -12,14 +15,30 @@ import sys
 import torch
 
 
-def attention(seq: int, heads: int) -> None:
-    from dgx_monarch_b200.ops import attention_fwd
+def attention(seq: int, heads: int, chunks: int = 0) -> None:
+    from dgx_monarch_b200.ops import attention_fwd, set_p_chunks
 
+    set_p_chunks(chunks)
     g = torch.Generator(device="cuda").manual_seed(0)
     q, k, v = (torch.randn(1, seq, heads, 128, device="cuda", generator=g).bfloat16() for _ in range(3))
     out = torch.empty_like(q)
     for _ in range(3):
         attention_fwd(q, k, v, out=out, return_lse=False)
+    torch.cuda.synchronize()
+
+
+def attention_fp8(seq: int, heads: int) -> None:
+    """e4m3 inputs with per-head descales (the C3 path), bf16 output."""
+    from dgx_monarch_b200.ops import attention_fwd
+    from dgx_monarch_b200.prologue import quantize_e4m3_per_head
+
+    g = torch.Generator(device="cuda").manual_seed(0)
+    q8, k8, v8 = (quantize_e4m3_per_head(torch.randn(1, seq, heads, 128, device="cuda", generator=g).bfloat16())
+                  for _ in range(3))
+    out = torch.empty(1, seq, heads, 128, device="cuda", dtype=torch.bfloat16)
+    for _ in range(3):
+        attention_fwd(q8[0], k8[0], v8[0], q_descale=q8[1], k_descale=k8[1], v_descale=v8[1], out=out,
+                      return_lse=False)
     torch.cuda.synchronize()
 
 
@@ -51,6 +70,18 @@ def kernels() -> None:
         qkv_prologue_scatter(qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2], dst, world=1, rank=0,
                              norm_mode=_lib.NORM_HEAD, norm_q_w=nq, norm_k_w=nk, rope=table)
     del qkv
+    # The joint scatter with replicated text (512 text rows, 9216 image rows,
+    # one rank): the image scatter and the text head-slice copy.
+    from dgx_monarch_b200.ulysses import ulysses_scatter_joint
+
+    txt_rows = 512
+    joint = [torch.empty(1, rows, heads, 128, device=dev, dtype=torch.bfloat16)  # text + image rows
+             for _ in range(3)]
+    img = [w(1, rows - txt_rows, heads, 128, sc=1.0) for _ in range(3)]
+    txt = [w(1, txt_rows, heads, 128, sc=1.0) for _ in range(3)]
+    for _ in range(2):
+        ulysses_scatter_joint(img, txt, [[t.data_ptr()] for t in joint], world=1, rank=0)
+    del joint, img, txt
     # FP8 quantisation of one gathered head slab (C3: 4608 tokens x 24 heads).
     xq = torch.randn(1, 32768, 24, 128, device=dev, generator=g).bfloat16()
     for _ in range(2):
@@ -83,6 +114,9 @@ def kernels() -> None:
 if __name__ == "__main__":
     if len(sys.argv) > 1 and sys.argv[1] == "kernels":
         kernels()
+    elif len(sys.argv) > 1 and sys.argv[1] == "fp8":
+        seq, heads = (int(sys.argv[2]), int(sys.argv[3])) if len(sys.argv) > 3 else (32768, 8)
+        attention_fp8(seq, heads)
     else:
         seq, heads = (int(sys.argv[1]), int(sys.argv[2])) if len(sys.argv) > 2 else (32768, 8)
-        attention(seq, heads)
+        attention(seq, heads, int(sys.argv[3]) if len(sys.argv) > 3 else 0)
