@@ -73,6 +73,8 @@ extern "C" int dgxm_cfg_combine(const void* cond, const void* uncond, int64_t n,
                                 double cfg_scale, void* out, void* stream) {
   using namespace dgxm;
   if (n < 0) return fail(DGXM_ERR_INVALID, "negative element count");
+  if (dtype != DGXM_DTYPE_F32 && dtype != DGXM_DTYPE_BF16 && dtype != DGXM_DTYPE_F16)
+    return fail(DGXM_ERR_UNSUPPORTED, "prediction dtype %d is not supported", dtype);
   if (n == 0) return DGXM_OK;
   if (cond == nullptr || uncond == nullptr || out == nullptr)
     return fail(DGXM_ERR_INVALID, "NULL cond, uncond or output");
