@@ -53,6 +53,8 @@ def parse_args():
     p.add_argument("--e2e-groups", type=int, default=5,
                    help="head groups the host-streamed e2e step pipelines (must divide the "
                         "40 heads, with a multiple of the GPU count per group)")
+    p.add_argument("--pingpong", action="store_true",
+                   help="the two query tiles' exponential loops take turns (bf16 kernel)")
     p.add_argument("--p-chunks", type=int, choices=[0, 1, 2, 4], default=0,
                    help="release each block's probabilities to the tensor core in this many "
                         "chunks (0: the library default)")
@@ -479,10 +481,11 @@ def main() -> None:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    if args.p_chunks:
-        from dgx_monarch_b200.ops import set_p_chunks
+    if args.p_chunks or args.pingpong:
+        from dgx_monarch_b200.ops import set_p_chunks, set_pingpong
 
         set_p_chunks(args.p_chunks)
+        set_pingpong(args.pingpong)
     if world > 1:
         from datetime import timedelta
 
@@ -637,7 +640,8 @@ def main() -> None:
             "config": {"workload": WORKLOAD, "seq_len": SEQ, "heads": HEADS, "head_dim": DIM,
                        "batch": BATCH, "parallelism": f"ulysses{world}",
                        "l2": "inputs larger than L2 (Q/K/V 2.3 GB)",
-                       "p_chunks": args.p_chunks or "library default (1)"},
+                       "p_chunks": args.p_chunks or "library default (1)",
+                       "softmax_schedule": "ping-pong" if args.pingpong else "default"},
             "tokens_per_s": BATCH * SEQ / (ms * 1e-3),
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
                          "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],

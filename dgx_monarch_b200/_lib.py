@@ -26,6 +26,7 @@ DTYPE_F32 = 3
 
 ATTN_SAFE_ORDER = 1
 ATTN_P_CHUNKS_SHIFT = 4  # DGXM_ATTN_P_CHUNKS(n) = n << 4
+ATTN_PINGPONG = 1 << 8
 
 
 class DgxmError(RuntimeError):

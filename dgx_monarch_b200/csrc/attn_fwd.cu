@@ -147,7 +147,7 @@ struct __align__(64) AttnParams {
 };
 
 // Barrier slots inside the control block.
-template <int kStages, int kPChunks>
+template <int kStages, int kPChunks, bool kPingPong = false>
 struct Bars {
   static constexpr int kQ = 0;
   static constexpr int kKvFull = 1;
@@ -157,7 +157,8 @@ struct Bars {
   static constexpr int kOFull = kPFull + 2 * kPChunks;  // 2
   static constexpr int kPvDone = kOFull + 2;         // 2
   static constexpr int kDrain = kPvDone + 2;
-  static constexpr int kCount = kDrain + 1;
+  static constexpr int kTurn = kDrain + 1;                  // 2: ping-pong tokens, one per tile
+  static constexpr int kCount = kTurn + (kPingPong ? 2 : 0);
 };
 
 // Shared-memory descriptors split into a low word (start address in 16-byte
@@ -267,11 +268,11 @@ __device__ __forceinline__ void raise_abort(volatile int* abort_flag, int bits) 
   *abort_flag = 1;
 }
 
-template <bool FP8, bool OUT_F32, bool EXTRA, int NCH>
+template <bool FP8, bool OUT_F32, bool EXTRA, int NCH, bool PP>
 __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_constant__ AttnParams p) {
   using C = AttnCfg<FP8>;
   constexpr int kPChunks = p_chunks<FP8, NCH>();
-  using B = Bars<C::kStages, kPChunks>;
+  using B = Bars<C::kStages, kPChunks, PP>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -300,6 +301,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
       mbar_init(bar(B::kPvDone + t), 1);
     }
     mbar_init(bar(B::kDrain), 1);
+    if constexpr (PP) {
+      mbar_init(bar(B::kTurn + 0), 256);
+      mbar_init(bar(B::kTurn + 1), 256);
+    }
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -591,6 +596,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
       // p = 2^(s * sl2 - m) (times kPScale for e4m3, folded into the exponent).
       // A row whose keys so far were all excluded keeps m = -inf and p = 0.
       const float bias = -(EXTRA && m_run == -INFINITY ? 0.f : m_run) + C::kPScaleLog2;
+      if constexpr (PP) {
+        // Ping-pong: the two tiles' exponential loops take turns -- tile 1's
+        // loop of block j follows tile 0's, tile 0's loop of block j + 1
+        // follows tile 1's of block j -- so neither shares the MUFU with the
+        // other.  A wait that gives up raises the abort flag and the group
+        // stops together at its next exchange barrier.
+        if (t == 1 || j > 0) {
+          const int parity = t == 1 ? (j & 1) : ((j - 1) & 1);
+          if (!__all_sync(0xffffffffu, mbar_wait(bar(B::kTurn + (t ^ 1)), parity, abort_flag)))
+            raise_abort(abort_flag, kErrSoftmaxTimeout);
+        }
+      }
       if constexpr (kPChunks > 1) {
         const uint64_t sl2x2 = pk2(sl2, sl2), biasx2 = pk2(bias, bias);
         uint64_t sum_a = pk2(0.f, 0.f), sum_b = pk2(0.f, 0.f);
@@ -619,6 +636,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
             } else {
               pk[q] = pack_bf16x2(p0, p1);
             }
+          }
+          if constexpr (PP) {
+            if (ch == kPChunks - 1) mbar_arrive(bar(B::kTurn + t));  // the other tile's turn
           }
           if constexpr (FP8) {
             // 2 kPairs keys of this chunk, four per column.
@@ -682,6 +702,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
             pk[i] = pack_bf16x2(p0, p1);
           }
         }
+        if constexpr (PP) mbar_arrive(bar(B::kTurn + t));  // the other tile's turn
         {
           float a0, a1, b0, b1;
           upk2(sum_a, a0, a1);
@@ -839,11 +860,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
   }
 }
 
-template <bool FP8, bool OUT_F32, bool EXTRA, int NCH>
+template <bool FP8, bool OUT_F32, bool EXTRA, int NCH, bool PP = false>
 static int launch_attn(const AttnParams& prm, dim3 grid, cudaStream_t stream) {
   using C = AttnCfg<FP8>;
   static std::atomic<uint64_t> configured{0};  // one bit per device ordinal
-  auto kern = attn_fwd_kernel<FP8, OUT_F32, EXTRA, NCH>;
+  auto kern = attn_fwd_kernel<FP8, OUT_F32, EXTRA, NCH, PP>;
   DGXM_CUDA_TRY(set_smem_limit_once(kern, C::kSmemBytes, configured));
   kern<<<grid, kAttnThreads, C::kSmemBytes, stream>>>(prm);
   DGXM_CUDA_TRY(cudaGetLastError());
@@ -953,6 +974,18 @@ template <bool EXTRA>
 static int dispatch_attn_t(const dgxm_attn_desc* d, const AttnParams& prm, dim3 grid, cudaStream_t st) {
   int nch = (d->flags & DGXM_ATTN_P_CHUNKS_MASK) >> DGXM_ATTN_P_CHUNKS_SHIFT;
   if (nch == 0) nch = DGXM_SM_P_CHUNKS;
+  // The ping-pong schedule is built for the bf16 kernel with bf16 output and
+  // no extras; the other instantiations run their usual schedule.
+  const bool pp = (d->flags & DGXM_ATTN_PINGPONG) != 0 && !EXTRA && d->in_dtype == DGXM_DTYPE_BF16 &&
+                  d->out_dtype == DGXM_DTYPE_BF16;
+  if (pp) {
+    switch (nch) {
+      case 1: return launch_attn<false, false, false, 1, true>(prm, grid, st);
+      case 2: return launch_attn<false, false, false, 2, true>(prm, grid, st);
+      case 4: return launch_attn<false, false, false, 4, true>(prm, grid, st);
+      default: return fail(DGXM_ERR_INVALID, "%d P chunks per block (1, 2 or 4)", nch);
+    }
+  }
   switch (nch) {
     case 1: return dispatch_attn_n<EXTRA, 1>(d, prm, grid, st);
     case 2: return dispatch_attn_n<EXTRA, 2>(d, prm, grid, st);

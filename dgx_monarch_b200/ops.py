@@ -93,9 +93,20 @@ def set_p_chunks(chunks: int) -> None:
     _P_CHUNKS = chunks
 
 
+_PINGPONG = False
+
+
+def set_pingpong(on: bool) -> None:
+    """Let the two query tiles' exponential loops take turns in every later
+    bf16 attention call of this process (DGXM_ATTN_PINGPONG); same results."""
+    global _PINGPONG
+    _PINGPONG = bool(on)
+
+
 def attn_flags(safe_order: bool = False) -> int:
     """The descriptor flags of one attention call."""
-    return (_lib.ATTN_SAFE_ORDER if safe_order else 0) | (_P_CHUNKS << _lib.ATTN_P_CHUNKS_SHIFT)
+    return ((_lib.ATTN_SAFE_ORDER if safe_order else 0) | (_P_CHUNKS << _lib.ATTN_P_CHUNKS_SHIFT)
+            | (_lib.ATTN_PINGPONG if _PINGPONG else 0))
 
 
 def attn_desc(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor,

@@ -1,4 +1,5 @@
-"""The chunked release of P (DGXM_ATTN_P_CHUNKS): the softmax hands each
+"""The chunked release of P (DGXM_ATTN_P_CHUNKS) and the ping-pong softmax
+(DGXM_ATTN_PINGPONG).  With chunks, the softmax hands each
 128-key block's probabilities to the tensor core in 2 or 4 chunks, and the
 P.V steps of a chunk start while the rest is computed.  Same contract as the
 one-chunk kernel: bf16 output max-abs <= 2e-2 and rel-L2 <= 5e-3, LSE within
@@ -113,3 +114,27 @@ def test_chunked_keep_masks_and_routing(lib, chunks):
     assert (got[:, keep].float() - ref).abs().max().item() <= BF16_MAX_ABS
     assert rel_l2(got[:, keep], ref) <= BF16_REL_L2
     assert got[:, drop].abs().max().item() == 0.0
+
+
+@pytest.mark.parametrize("chunks", [1, 2, 4], indirect=True)
+@pytest.mark.parametrize("shape", [(1, 256, 256, 1, 1), (2, 300, 77, 3, 1), (1, 4096, 4096, 2, 2)])
+def test_pingpong_schedule_gives_the_same_bits(lib, chunks, shape):
+    """Only the timing changes when the two tiles' exponential loops take
+    turns: the output and LSE equal the same call without ping-pong."""
+    from dgx_monarch_b200.ops import attention_fwd, set_pingpong
+
+    b, lq, lk, h, hkv = shape
+    g = torch.Generator(device="cuda").manual_seed(17)
+    q = torch.randn(b, lq, h, 128, device="cuda", generator=g).bfloat16()
+    k = torch.randn(b, lk, hkv, 128, device="cuda", generator=g).bfloat16()
+    v = torch.randn(b, lk, hkv, 128, device="cuda", generator=g).bfloat16()
+    want, want_lse = attention_fwd(q, k, v)
+    set_pingpong(True)
+    try:
+        got, got_lse = attention_fwd(q, k, v)
+    finally:
+        set_pingpong(False)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want) and torch.equal(got_lse, want_lse)
+    ref, _ = reference_attention(q, k, v)
+    assert rel_l2(got, ref) <= BF16_REL_L2
