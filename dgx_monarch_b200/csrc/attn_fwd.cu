@@ -974,10 +974,17 @@ template <bool EXTRA>
 static int dispatch_attn_t(const dgxm_attn_desc* d, const AttnParams& prm, dim3 grid, cudaStream_t st) {
   int nch = (d->flags & DGXM_ATTN_P_CHUNKS_MASK) >> DGXM_ATTN_P_CHUNKS_SHIFT;
   if (nch == 0) nch = DGXM_SM_P_CHUNKS;
-  // The ping-pong schedule is built for the bf16 kernel with bf16 output and
-  // no extras; the other instantiations run their usual schedule.
-  const bool pp = (d->flags & DGXM_ATTN_PINGPONG) != 0 && !EXTRA && d->in_dtype == DGXM_DTYPE_BF16 &&
-                  d->out_dtype == DGXM_DTYPE_BF16;
+  // The ping-pong schedule is built for bf16 output without extras (bf16 or
+  // e4m3 input); the other instantiations run their usual schedule.
+  const bool pp = (d->flags & DGXM_ATTN_PINGPONG) != 0 && !EXTRA && d->out_dtype == DGXM_DTYPE_BF16;
+  if (pp && d->in_dtype == DGXM_DTYPE_E4M3) {
+    switch (nch) {
+      case 1: return launch_attn<true, false, false, 1, true>(prm, grid, st);
+      case 2:
+      case 4: return launch_attn<true, false, false, 2, true>(prm, grid, st);  // e4m3 runs 4 as 2
+      default: return fail(DGXM_ERR_INVALID, "%d P chunks per block (1, 2 or 4)", nch);
+    }
+  }
   if (pp) {
     switch (nch) {
       case 1: return launch_attn<false, false, false, 1, true>(prm, grid, st);

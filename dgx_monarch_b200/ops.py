@@ -98,7 +98,8 @@ _PINGPONG = False
 
 def set_pingpong(on: bool) -> None:
     """Let the two query tiles' exponential loops take turns in every later
-    bf16 attention call of this process (DGXM_ATTN_PINGPONG); same results."""
+    attention call with bf16 output and no extras (DGXM_ATTN_PINGPONG); same
+    results."""
     global _PINGPONG
     _PINGPONG = bool(on)
 

@@ -50,8 +50,8 @@ extern "C" {
 #define DGXM_ATTN_P_CHUNKS_MASK (7 << DGXM_ATTN_P_CHUNKS_SHIFT)
 #define DGXM_ATTN_P_CHUNKS(n) ((n) << DGXM_ATTN_P_CHUNKS_SHIFT)
 /* Let the two query tiles' exponential loops take turns instead of sharing
- * the special-function units (a ping-pong softmax).  Applies to bf16 input
- * and output without extras; other calls run their usual schedule.  Only the
+ * the special-function units (a ping-pong softmax).  Applies to bf16 output
+ * without extras (bf16 or e4m3 input); other calls run their usual schedule.  Only the
  * timing changes: the output is bit-identical to the same call without it. */
 #define DGXM_ATTN_PINGPONG (1 << 8)
 

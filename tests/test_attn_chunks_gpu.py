@@ -138,3 +138,20 @@ def test_pingpong_schedule_gives_the_same_bits(lib, chunks, shape):
     assert torch.equal(got, want) and torch.equal(got_lse, want_lse)
     ref, _ = reference_attention(q, k, v)
     assert rel_l2(got, ref) <= BF16_REL_L2
+
+
+@pytest.mark.parametrize("chunks", [1, 2], indirect=True)
+def test_pingpong_schedule_gives_the_same_bits_in_e4m3(lib, chunks):
+    from dgx_monarch_b200.ops import attention_fwd, set_pingpong
+
+    g = torch.Generator(device="cuda").manual_seed(23)
+    (q8, qs), (k8, ks), (v8, vs) = (quantize_e4m3_per_head(
+        torch.randn(2, 1000, 3, 128, device="cuda", generator=g).bfloat16()) for _ in range(3))
+    want, want_lse = attention_fwd(q8, k8, v8, q_descale=qs, k_descale=ks, v_descale=vs)
+    set_pingpong(True)
+    try:
+        got, got_lse = attention_fwd(q8, k8, v8, q_descale=qs, k_descale=ks, v_descale=vs)
+    finally:
+        set_pingpong(False)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want) and torch.equal(got_lse, want_lse)
