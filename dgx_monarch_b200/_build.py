@@ -44,12 +44,25 @@ def needs_build() -> bool:
     return any(src.stat().st_mtime > built for src in sources())
 
 
+def tuning_defines() -> list[str]:
+    """Compile-time tuning of the kernels' defaults (the DGXM_SM_* macros of
+    csrc/attn_fwd.cu), from DGXM_NVCC_DEFINES, e.g. "-DDGXM_SM_POLY_MOD=4".
+    Only -D definitions are taken."""
+    defines = os.environ.get("DGXM_NVCC_DEFINES", "").split()
+    bad = [d for d in defines if not d.startswith("-DDGXM_")]
+    if bad:
+        raise ValueError(f"DGXM_NVCC_DEFINES takes -DDGXM_* definitions only, got {bad}")
+    return defines
+
+
 def build_library(force: bool = False, verbose: bool = False) -> Path:
-    """Compile csrc/dgxm_sp.cu into dgx_monarch_b200/libdgxm_sp.so."""
-    if not force and not needs_build():
+    """Compile csrc/dgxm_sp.cu into dgx_monarch_b200/libdgxm_sp.so.  A build
+    with tuning defines is always redone, so the library matches them."""
+    defines = tuning_defines()
+    if not force and not defines and not needs_build():
         return LIB_PATH
     tmp = LIB_PATH.with_suffix(".so.tmp")
-    cmd = [_nvcc(), *NVCC_FLAGS]
+    cmd = [_nvcc(), *NVCC_FLAGS, *defines]
     if verbose:
         cmd += ["-Xptxas", "-v"]
     cmd += ["-o", str(tmp), str(CSRC / "dgxm_sp.cu")]
