@@ -19,7 +19,7 @@ def _coefficients() -> list[float]:
     body = text[text.index("uint64_t exp2_poly2"):]
     body = body[:body.index("\n}\n")]
     found = [float(x) for x in re.findall(r"pk2\(([-0-9.e]+)f, \1f\)", body)]
-    return found
+    return [c for c in found if c > 0]  # the polynomial's; -1 belongs to the range reduction
 
 
 def _fma(a, b, c):
