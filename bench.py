@@ -58,7 +58,113 @@ def parse_args():
     p.add_argument("--p-chunks", type=int, choices=[0, 1, 2, 4], default=0,
                    help="release each block's probabilities to the tensor core in this many "
                         "chunks (0: the library default)")
+    p.add_argument("--profile-case", choices=["attn", "fp8", "f16", "kernels"], default=None,
+                   help="instead of the bench: a few launches of one kernel family on one GPU, "
+                        "sized for a profiler capture (attn / fp8 / f16: three attention launches "
+                        "of --case-seq tokens x --case-heads heads; kernels: every support kernel "
+                        "at the Flux/Krea2 block shapes)")
+    p.add_argument("--case-seq", type=int, default=32768)
+    p.add_argument("--case-heads", type=int, default=8)
+    p.add_argument("--case-batch", type=int, default=1)
     return p.parse_args()
+
+
+# ----------------------------------------------------------------- profiler cases
+def run_profile_case(args) -> None:
+    """Representative launches for an ncu capture: small enough (a few GB on
+    the device, inputs above the 126 MB L2) that a full-set capture of one
+    launch ends in a minute or two."""
+    import torch
+
+    from dgx_monarch_b200.ops import attention_fwd, set_p_chunks, set_pingpong
+
+    set_p_chunks(args.p_chunks)
+    set_pingpong(args.pingpong)
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    shape = (args.case_batch, args.case_seq, args.case_heads, DIM)
+    if args.profile_case == "kernels":
+        profile_support_kernels(dev, g)
+        return
+    if args.profile_case == "fp8":
+        from dgx_monarch_b200.prologue import quantize_e4m3_per_head
+
+        q8, k8, v8 = (quantize_e4m3_per_head(torch.randn(*shape, device=dev, generator=g).bfloat16())
+                      for _ in range(3))
+        out = torch.empty(*shape, device=dev, dtype=torch.bfloat16)
+        for _ in range(3):
+            attention_fwd(q8[0], k8[0], v8[0], q_descale=q8[1], k_descale=k8[1], v_descale=v8[1],
+                          out=out, return_lse=False)
+    else:
+        dt = torch.float16 if args.profile_case == "f16" else torch.bfloat16
+        q, k, v = (torch.randn(*shape, device=dev, generator=g).to(dt) for _ in range(3))
+        out = torch.empty_like(q)
+        for _ in range(3):
+            attention_fwd(q, k, v, out=out, return_lse=False)
+    torch.cuda.synchronize()
+
+
+def profile_support_kernels(dev, g) -> None:
+    """Every support kernel once or twice, at the C2 (Flux/Krea2 block) and C3
+    shapes on one rank, each input larger than the L2 where the kernel is
+    HBM-bound."""
+    import torch
+
+    from dgx_monarch_b200 import _lib
+    from dgx_monarch_b200.cfg import cfg_combine
+    from dgx_monarch_b200.ops import lse_merge
+    from dgx_monarch_b200.prologue import (qkv_gemm_prologue_scatter, qkv_prologue_scatter,
+                                           quantize_e4m3_per_head, rope_table)
+    from dgx_monarch_b200.shard import SequenceGather, SharedActivationScale
+    from dgx_monarch_b200.ulysses import ulysses_scatter_joint
+
+    hid, heads, rows = 3072, 24, 9728
+    w = lambda *s, sc=0.02: (sc * torch.randn(*s, device=dev, generator=g)).bfloat16()
+    x = w(rows, hid, sc=1.0)
+    wq, bq = w(3 * hid, hid), w(3 * hid)
+    nq, nk = (1 + w(128)).contiguous(), (1 + w(128)).contiguous()
+    pos = torch.stack((torch.zeros(rows, device=dev, dtype=torch.long),
+                       torch.arange(rows, device=dev) // 96, torch.arange(rows, device=dev) % 96), dim=1)
+    table = rope_table(pos, [16, 56, 56])
+    recv = [torch.empty(rows, heads, 128, device=dev, dtype=torch.bfloat16) for _ in range(3)]
+    dst = [[t.data_ptr()] for t in recv]
+    for _ in range(2):
+        qkv_gemm_prologue_scatter(x, wq, dst, world=1, rank=0, seq_local=rows, bias=bq,
+                                  norm_mode=_lib.NORM_HEAD, norm_q_w=nq, norm_k_w=nk, rope=table)
+    qkv = (x @ wq.t()).view(1, rows, 3, heads, 128)
+    for _ in range(2):
+        qkv_prologue_scatter(qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2], dst, world=1, rank=0,
+                             norm_mode=_lib.NORM_HEAD, norm_q_w=nq, norm_k_w=nk, rope=table)
+    del qkv
+    txt_rows = 512
+    joint = [torch.empty(1, rows, heads, 128, device=dev, dtype=torch.bfloat16) for _ in range(3)]
+    img = [w(1, rows - txt_rows, heads, 128, sc=1.0) for _ in range(3)]
+    txt = [w(1, txt_rows, heads, 128, sc=1.0) for _ in range(3)]
+    for _ in range(2):
+        ulysses_scatter_joint(img, txt, [[t.data_ptr()] for t in joint], world=1, rank=0)
+    del joint, img, txt
+    xq = torch.randn(1, 32768, 24, 128, device=dev, generator=g).bfloat16()
+    for _ in range(2):
+        quantize_e4m3_per_head(xq)
+    parts = [torch.randn(1, 32768, 8, 128, device=dev, generator=g) for _ in range(2)]
+    lses = [torch.randn(1, 8, 32768, device=dev, generator=g) for _ in range(2)]
+    for _ in range(2):
+        lse_merge(parts, lses)
+    c, u = (torch.randn(64 * 1024 * 1024, device=dev, generator=g) for _ in range(2))
+    for _ in range(2):
+        cfg_combine(c, u, 4.0)
+    del c, u
+    act = w(rows, 3 * hid, sc=1.0)
+    scale = SharedActivationScale(device=dev, generation=90)
+    for _ in range(2):
+        scale(act)
+    scale.close()
+    gather = SequenceGather(device=dev, generation=91)
+    tokens = w(2, rows, hid, sc=1.0)
+    for _ in range(2):
+        gather(tokens, rows)
+    gather.close()
+    torch.cuda.synchronize()
 
 
 # ----------------------------------------------------------------- clocks
@@ -313,24 +419,11 @@ CFG_WORKLOAD = ("CFG-parallel + Ulysses image attention: batch 2 (cond/uncond) -
 
 
 def _groups(world: int, uly: int, ring: int):
-    """Ulysses / ring process groups in the ulysses-low layout (Ulysses
-    groups are consecutive ranks), every rank creating every group."""
-    import torch.distributed as dist
+    """This rank's Ulysses / ring process groups in the ulysses-low layout
+    (Ulysses groups are consecutive ranks), every rank creating every group."""
+    from dgx_monarch_b200.groups import new_hybrid_groups
 
-    from oracle.usp import hybrid_groups
-
-    ug, rg = hybrid_groups(world, uly, ring)
-    rank = dist.get_rank()
-    mine_u = mine_r = None
-    for ranks in ug:
-        g = dist.new_group(ranks)
-        if rank in ranks:
-            mine_u = g
-    for ranks in rg:
-        g = dist.new_group(ranks)
-        if rank in ranks:
-            mine_r = g
-    return mine_u, mine_r
+    return new_hybrid_groups(world, uly, ring)
 
 
 def run_ring(world: int, rank: int, dev, steps: int, warmup: int) -> dict:
@@ -463,6 +556,9 @@ def time_scatter(uly, steps: int = 5) -> dict:
 # ----------------------------------------------------------------- our arm
 def main() -> None:
     args = parse_args()
+    if args.profile_case is not None:
+        run_profile_case(args)
+        return
     if args.impl == "reference":
         run_reference(args)
         return

@@ -4,7 +4,7 @@ The reference splits one batched cond+uncond model call into
 `batch // world` contiguous rows per cfg rank, runs the forward, and
 all-gathers the predictions over the cfg group
 (adapters/cfg_parallel.py:57-87 slicing, :293-301 gather, :304-374 the
-wrapper).  Here the slicing mirrors `_take_slice` exactly and the gather is a
+wrapper).  Here the slice follows the same contract and the gather is a
 peer-store all-gather into NVLink windows (dgxm_comm_allgather): each rank's
 prediction is copied straight into every peer's window, then a bounded flag
 barrier, with no NCCL call on the data path.  CFG pairs map to GPU pairs: with
@@ -25,35 +25,55 @@ class UnsupportedModelError(RuntimeError):
     """Typed refusal (adapters/base.py:37)."""
 
 
+def _children(item) -> list:
+    """The direct members of a forward argument container (dict values in
+    insertion order, list / tuple items); leaves have none."""
+    if isinstance(item, dict):
+        return list(item.values())
+    if isinstance(item, (list, tuple)):
+        return list(item)
+    return []
+
+
+def _rebuild(item, fn):
+    """`item` with `fn` applied to every leaf, containers rebuilt as the same
+    kind (a tuple stays a tuple, a dict keeps its keys)."""
+    if isinstance(item, dict):
+        return {key: _rebuild(member, fn) for key, member in item.items()}
+    if isinstance(item, tuple):
+        return tuple(_rebuild(member, fn) for member in item)
+    if isinstance(item, list):
+        return [_rebuild(member, fn) for member in item]
+    return fn(item)
+
+
 def take_slice(value, batch: int, world: int, rank: int):
-    """This rank's contiguous rows of every tensor whose dim 0 equals the call
-    batch; broadcast tensors and non-tensor leaves pass through; containers
-    recurse (adapters/cfg_parallel.py:71-87)."""
-    if torch.is_tensor(value):
-        if value.ndim > 0 and value.shape[0] == batch:
-            rows = batch // world
-            return value.narrow(0, rank * rows, rows)
-        return value
-    if isinstance(value, dict):
-        return {key: take_slice(item, batch, world, rank) for key, item in value.items()}
-    if isinstance(value, (list, tuple)):
-        sliced = [take_slice(item, batch, world, rank) for item in value]
-        return tuple(sliced) if isinstance(value, tuple) else sliced
-    return value
+    """The cfg rank's share of one batched model call
+    (adapters/cfg_parallel.py:71-87): a tensor whose leading dimension is the
+    whole call batch keeps rows [rank * n, (rank + 1) * n), n = batch // world,
+    as a view; every other leaf (broadcast tensors, scalars, non-tensors)
+    is shared unchanged, and containers are rebuilt around their members."""
+    share = batch // world
+    first = rank * share
+
+    def rows_of(leaf):
+        if torch.is_tensor(leaf) and leaf.dim() > 0 and leaf.size(0) == batch:
+            return leaf[first:first + share]
+        return leaf
+
+    return _rebuild(value, rows_of)
 
 
 def leading_batch(value) -> int | None:
-    """Batch size of the first tensor inside a forward argument
-    (adapters/cfg_parallel.py:57-68)."""
-    queue = [value]
-    while queue:
-        item = queue.pop(0)
-        if torch.is_tensor(item):
-            return int(item.shape[0]) if item.ndim > 0 else None
-        if isinstance(item, dict):
-            queue.extend(item.values())
-        elif isinstance(item, (list, tuple)):
-            queue.extend(item)
+    """Leading dimension of the first tensor found in a forward argument,
+    searching containers level by level (adapters/cfg_parallel.py:57-68);
+    None when that tensor is a scalar or there is no tensor."""
+    level = [value]
+    while level:
+        for item in level:
+            if torch.is_tensor(item):
+                return int(item.size(0)) if item.dim() > 0 else None
+        level = [member for item in level for member in _children(item)]
     return None
 
 

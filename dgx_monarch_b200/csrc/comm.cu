@@ -94,7 +94,7 @@ struct ScatterParams {
 // this is the rank-major concat [r*Ls + l]; with a two-segment local layout
 // [seg0 rows | Ls - seg0 rows] it is the canonical order that lists every
 // rank's first segment before every rank's second
-// (adapters/usp_sequence_order.py:246-255).
+// (adapters/usp_sequence_order.py:69-78).
 __device__ __forceinline__ int64_t gathered_row(int r, int l, int seq_local, int world, int seg0) {
   if (seg0 == 0) return static_cast<int64_t>(r) * seq_local + l;
   if (l < seg0) return static_cast<int64_t>(r) * seg0 + l;

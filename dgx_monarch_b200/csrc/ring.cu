@@ -9,8 +9,10 @@
 //   main stream : attention(Q, block) -> fp32 partial out_t and lse_t;
 //   join, then dgxm_comm_barrier: every rank's copy has landed and every
 //   rank finished step t, so buffer (t+1) % 2 may be overwritten next.
-// After R steps the LSE merge writes the output.  The block a rank attends
-// at step t came from rank (r - t) mod R, the oracle's ring order.
+// After R steps one closing barrier (so the next call's first copy cannot
+// overwrite a block a neighbour still attends), then the LSE merge writes the
+// output.  The block a rank attends at step t came from rank (r - t) mod R,
+// the oracle's ring order.
 //
 // Replaces the ring loop of xfuser/yunchang reached from
 // adapters/base.py:320 (usp_attn with ring degree > 1), with the per-block
@@ -40,6 +42,24 @@ static bool contiguous_bhld(const int64_t* s, const dgxm_attn_desc* d, int heads
          (d->batch == 1 || s[0] == static_cast<int64_t>(len) * heads * d->head_dim);
 }
 
+// The LSE merge writes (B, H, Lq) contiguously, so a strided lse is refused
+// rather than scrambled.
+static bool contiguous_bhl(const int64_t* s, const dgxm_attn_desc* d) {
+  return s[2] == 1 && s[1] == d->q_len &&
+         (d->batch == 1 || s[0] == static_cast<int64_t>(d->q_heads) * d->q_len);
+}
+
+// Every launch of a ring call goes to the current device, and the comm's
+// window and streams live on the device it was created on.
+static int check_comm_device(const dgxm_comm* c) {
+  int dev = -1;
+  DGXM_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev != c->device)
+    return fail(DGXM_ERR_INVALID, "the current device is %d but the comm lives on device %d", dev,
+                c->device);
+  return DGXM_OK;
+}
+
 }  // namespace dgxm
 
 extern "C" int64_t dgxm_ring_window_bytes(const dgxm_attn_desc* d) {
@@ -60,17 +80,22 @@ static int ring_attn_impl(dgxm_comm* c, const dgxm_attn_desc* d, const void* q, 
                           const void* v, void* o, float* lse, void* workspace,
                           int64_t workspace_bytes, void* stream) {
   if (c == nullptr || d == nullptr) return fail(DGXM_ERR_INVALID, "NULL comm or descriptor");
+  if (int rc0 = check_comm_device(c)) return rc0;
   const int world = c->world;
   if (world > kMaxMergeParts)
     return fail(DGXM_ERR_UNSUPPORTED, "ring degree %d exceeds %d", world, kMaxMergeParts);
-  if (world == 1) return dgxm_attn_fwd(d, q, k, v, nullptr, nullptr, nullptr, o, lse, stream);
-  if (d->in_dtype != DGXM_DTYPE_BF16)
-    return fail(DGXM_ERR_UNSUPPORTED, "ring attention runs bf16 inputs");
+  // The layout rules hold at every ring degree, so a call that runs at one
+  // degree runs at all of them.
   if (!contiguous_bhld(d->k_stride, d, d->kv_heads, d->kv_len) ||
       !contiguous_bhld(d->v_stride, d, d->kv_heads, d->kv_len))
     return fail(DGXM_ERR_INVALID, "ring attention needs contiguous (B, L, H, D) keys and values");
   if (!contiguous_bhld(d->o_stride, d, d->q_heads, d->q_len))
     return fail(DGXM_ERR_INVALID, "ring attention needs a contiguous (B, L, H, D) output");
+  if (lse != nullptr && !contiguous_bhl(d->lse_stride, d))
+    return fail(DGXM_ERR_INVALID, "ring attention needs a contiguous (B, H, L) lse");
+  if (world == 1) return dgxm_attn_fwd(d, q, k, v, nullptr, nullptr, nullptr, o, lse, stream);
+  if (d->in_dtype != DGXM_DTYPE_BF16)
+    return fail(DGXM_ERR_UNSUPPORTED, "ring attention runs bf16 inputs");
   const int64_t block = ring_block_bytes(d);
   const int64_t slot = round256(block);
   if (4 * slot > c->bytes)
@@ -131,6 +156,12 @@ static int ring_attn_impl(dgxm_comm* c, const dgxm_attn_desc* d, const void* q, 
       cur_v = mine + (2 * buf + 1) * slot;
     }
   }
+  // The last step attends the block in this rank's buffer (R - 2) % 2, and the
+  // next call's first copy into a neighbour's buffer 0 waits only on that
+  // neighbour's own stream.  A closing barrier orders every rank's last
+  // attention before any rank's next call can overwrite the buffer it reads.
+  rc = dgxm_comm_barrier(c, main);
+  if (rc) return rc;
   return dgxm_lse_merge(d->batch, d->q_len, d->q_heads, d->head_dim, world, outs, DGXM_DTYPE_F32,
                         lses, o, d->out_dtype, lse, stream);
 }
@@ -182,7 +213,9 @@ extern "C" int dgxm_ring_attn_fwd_noalloc(dgxm_comm* c, const dgxm_attn_desc* d,
                                           void* stream) {
   using namespace dgxm;
   if (c == nullptr || d == nullptr) return fail(DGXM_ERR_INVALID, "NULL comm or descriptor");
-  if (c->world == 1) return dgxm_attn_fwd(d, q, k, v, nullptr, nullptr, nullptr, o, lse, stream);
+  if (int rc0 = check_comm_device(c)) return rc0;
+  // One rank attends its own block: no partial results, so no scratch.
+  if (c->world == 1) return ring_attn_impl(c, d, q, k, v, o, lse, nullptr, 0, stream);
   const int64_t need = dgxm_ring_workspace_bytes(d, c->world);
   if (need < 0 || need > kRingStaticScratchBytes)
     return fail(DGXM_ERR_INVALID,

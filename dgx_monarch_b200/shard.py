@@ -1,8 +1,9 @@
 """Sequence shards: pad / chunk, the NVLink all-gather behind sp_gather, and
 the shared NVFP4 activation scale.
 
-- `pad_seq_to_multiple` and `shard_seq` restate adapters/base.py:48-123 on
-  the device tensor (a zero pad and a view of this rank's chunk).
+- `pad_seq_to_multiple` and `shard_seq` give the zero pad and the per-rank
+  chunk of adapters/base.py:48-123 (a view of the stream where the chunk
+  lies inside it; only a chunk reaching into the pad is assembled).
 - `SequenceGather` replaces `sp_gather` (adapters/base.py:126-131), the
   xfuser all-gather of every rank's chunk followed by a trim to the declared
   length: each rank peer-stores its rows into every rank's window in the
@@ -39,30 +40,47 @@ class ShardRefusal(RuntimeError):
 
 
 def pad_seq_to_multiple(t: torch.Tensor, multiple: int, dim: int = 1) -> tuple[torch.Tensor, int]:
-    """Zero-pad `dim` to a multiple of `multiple`; (padded, original length)."""
-    orig = t.size(dim)
-    short = (multiple - orig % multiple) % multiple
-    if short == 0:
-        return t, orig
+    """`t` with zero rows appended along `dim` up to the next multiple of
+    `multiple` (the tensor itself when none are needed), and its original
+    length -- the divisibility pad of adapters/base.py:48-56."""
+    length = t.size(dim)
+    target = -(-length // multiple) * multiple
+    if target == length:
+        return t, length
     shape = list(t.shape)
-    shape[dim] = short
-    return torch.cat([t, t.new_zeros(shape)], dim=dim), orig
+    shape[dim] = target
+    padded = t.new_zeros(shape)
+    padded.narrow(dim, 0, length).copy_(t)
+    return padded, length
 
 
 def shard_seq(t: torch.Tensor | None, world: int, rank: int, dim: int = 1, *,
               allow_padding: bool = True, name: str | None = None):
-    """This rank's contiguous chunk after the zero pad, and the pre-pad length."""
+    """This rank's contiguous chunk of the zero-padded stream and the stream's
+    length before the pad (the contract of adapters/base.py:91-123).
+
+    The padded stream is never built: a chunk that lies inside the stream is
+    a view of it, and only a chunk that reaches past the end is assembled,
+    from its real rows and zeros."""
     if t is None:
         return None, 0
-    orig = t.size(dim)
-    if orig % world:
-        if not allow_padding:
-            subject = f"{name} stream" if name else "sequence"
-            raise ShardRefusal(
-                f"{subject} length {orig} on dim {dim} is not divisible by the sequence-parallel "
-                f"degree {world}, and this adapter requires exact divisibility.")
-        t, _ = pad_seq_to_multiple(t, world, dim=dim)
-    return torch.chunk(t, world, dim=dim)[rank], orig
+    length = t.size(dim)
+    if length % world and not allow_padding:
+        subject = f"{name} stream" if name else "sequence"
+        raise ShardRefusal(
+            f"{subject} length {length} on dim {dim} is not divisible by the sequence-parallel "
+            f"degree {world}, and this adapter requires exact divisibility.")
+    step = -(-length // world)
+    start = rank * step
+    if start + step <= length:
+        return t.narrow(dim, start, step), length
+    shape = list(t.shape)
+    shape[dim] = step
+    chunk = t.new_zeros(shape)
+    real = max(0, length - start)
+    if real:
+        chunk.narrow(dim, 0, real).copy_(t.narrow(dim, start, real))
+    return chunk, length
 
 
 def _rank_world(group) -> tuple[int, int]:

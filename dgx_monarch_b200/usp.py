@@ -9,7 +9,7 @@ the reference's `_AttentionDispatch.configure` (actor/attention_dispatch.py:
   the inverse all-to-all in its epilogue -> barrier; a joint-order
   descriptor (adapters/usp_sequence_order.py) is applied by the scatter and
   the epilogue row maps, never by index copies;
-- pad rows (adapters/usp_pad_exclusion.py:152-177): the same fused path,
+- pad rows (adapters/usp_pad_exclusion.py:112-137): the same fused path,
   with keep bits over keys and query rows applied inside the attention
   kernel (excluded keys never enter a softmax, dropped rows are written as
   zeros) instead of index_select / zero-restore copies;
@@ -367,7 +367,7 @@ def validate_bias_groups(groups, queries: int, keys: int, batch: int, heads: int
 
 
 def _joint_inverse(text: int, image: int, world: int) -> list[int]:
-    """rank-major row -> canonical row (adapters/usp_sequence_order.py:246-261)."""
+    """rank-major row -> canonical row (adapters/usp_sequence_order.py:69-78)."""
     local = text + image
     inv = [0] * (local * world)
     canon = 0

@@ -119,7 +119,7 @@ int dgxm_attn_fwd(const dgxm_attn_desc* desc, const void* q, const void* k, cons
  * key_keep / query_keep: bit i of word i/32 keeps key (query row) i; a key
  * with bit 0 is excluded from every softmax, a query row with bit 0 is
  * written as zeros (LSE -inf).  This is the exact pad-row exclusion of
- * adapters/usp_pad_exclusion.py:152-177 (attend the real rows, zero-restore
+ * adapters/usp_pad_exclusion.py:112-137 (attend the real rows, zero-restore
  * the pads) done inside the kernel instead of by index_select copies.
  * NULL keeps everything; a batch stride of 0 shares one mask.
  *
@@ -259,7 +259,7 @@ typedef struct dgxm_a2a_desc {
    * rows.  seg0 > 0: each rank's local rows are [seg0 rows | seq_local - seg0
    * rows] (text then image) and the gathered axis lists every rank's first
    * segment, then every rank's second -- the stock key order that
-   * adapters/usp_sequence_order.py:209-322 (RankMajorJointOrder) restores
+   * adapters/usp_sequence_order.py:33-146 (RankMajorJointOrder) restores
    * with index copies; here the all-to-all writes rows straight there. */
   int32_t seg0;
 } dgxm_a2a_desc;

@@ -85,7 +85,7 @@ def kept_rows(rows: int, drop_rows) -> np.ndarray | None:
 
 def attend_without_pads(q, k, v, drop_rows, kv_drop_rows, attend):
     """Attend over the real rows and write zeros where pads sat
-    (adapters/usp_pad_exclusion.py:152-177)."""
+    (adapters/usp_pad_exclusion.py:112-137)."""
     qi = kept_rows(q.shape[1], drop_rows)
     if kv_drop_rows is drop_rows and k.shape[1] == q.shape[1]:
         ki = qi
@@ -160,7 +160,7 @@ def assert_pads_are_a_tail(drop_rows, rows: int) -> None:
 
 def attend_groups_without_pads(q, k, v, drop_rows, kv_drop_rows, groups):
     """The pad exclusion with query-bias groups: tail check, drop, grouped
-    attention, zero-restore (adapters/usp_pad_exclusion.py:152-177 with
+    attention, zero-restore (adapters/usp_pad_exclusion.py:112-137 with
     groups, adapters/usp_full_axis.py:14-16)."""
     if groups:
         assert_pads_are_a_tail(drop_rows, q.shape[1])
@@ -211,7 +211,7 @@ def cfg_combine(cond: np.ndarray, uncond: np.ndarray, cfg: float, dtype: str) ->
 @dataclass(frozen=True)
 class RankMajorJointOrder:
     """[t0,i0,t1,i1,...] <-> [t0,t1,...,i0,i1,...] on the gathered axis
-    (adapters/usp_sequence_order.py:209-322)."""
+    (adapters/usp_sequence_order.py:33-146)."""
 
     text_rows: int
     image_rows: int
@@ -226,7 +226,7 @@ class RankMajorJointOrder:
         return world
 
     def permutation(self, rows: int) -> np.ndarray:
-        """canonical index -> rank-major index (usp_sequence_order.py:246-255)."""
+        """canonical index -> rank-major index (usp_sequence_order.py:69-78)."""
         local = self.text_rows + self.image_rows
         starts = np.arange(self.world(rows))[:, None] * local
         text = starts + np.arange(self.text_rows)[None, :]
@@ -240,7 +240,7 @@ class RankMajorJointOrder:
         return inv
 
     def canonicalize(self, q, k, v, drop_rows, kv_drop_rows):
-        """Reorder to stock order and remap pad rows (usp_sequence_order.py:282-309)."""
+        """Reorder to stock order and remap pad rows (usp_sequence_order.py:105-146)."""
         if q.shape != k.shape or q.shape != v.shape:
             raise OracleRefusal("q/k/v are not equal B,L,H,D self-attention tensors")
         rows = q.shape[1]

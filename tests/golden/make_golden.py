@@ -1,9 +1,9 @@
 """Generate the golden fixtures in this directory from the reference itself.
 
-Run in a container that has the dgx-monarch source tree (read-only) at
-/root/reference:
+Run where the dgx-monarch source tree is readable, naming its `src`
+directory by argument or by the DGXM_REFERENCE_SRC environment variable:
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py <dgx-monarch>/src
 
 It imports the reference's own in-repo USP modules (adapters/base.py,
 usp_full_axis.py, usp_pad_exclusion.py, usp_sequence_order.py,
@@ -24,7 +24,22 @@ from pathlib import Path
 import numpy as np
 import torch
 
-REF_SRC = Path("/root/reference/src")
+REF_SRC: Path | None = None  # the dgx-monarch `src` directory, set by main()
+
+
+def _reference_src(argv: list[str]) -> Path:
+    """The reference's `src` directory from the first argument or
+    DGXM_REFERENCE_SRC; it must hold the dgx_monarch package."""
+    import os
+
+    given = argv[1] if len(argv) > 1 else os.environ.get("DGXM_REFERENCE_SRC")
+    if not given:
+        raise SystemExit("usage: make_golden.py <dgx-monarch src directory> "
+                         "(or set DGXM_REFERENCE_SRC)")
+    src = Path(given).resolve()
+    if not (src / "dgx_monarch" / "adapters" / "base.py").exists():
+        raise SystemExit(f"{src} does not hold dgx_monarch/adapters/base.py")
+    return src
 OUT = Path(__file__).resolve().parent
 
 
@@ -156,14 +171,14 @@ def _attend64(q, k, v):
     return (torch.softmax(scores, dim=-1) @ vh).transpose(1, 2).to(q.dtype)
 
 
-def _full_context_rank(rank, port, k, v, out_q):
+def _full_context_rank(rank, port, k, v, out_q, ref_src):
     """One gloo rank running the reference's Ring2 K/V gather
     (adapters/wan_ring_full_context.py:203-295)."""
     import os
 
     import torch.distributed as dist
 
-    sys.path.insert(0, str(REF_SRC))
+    sys.path.insert(0, str(ref_src))
     _install_stubs()
     from dgx_monarch.adapters.wan_ring_full_context import _materialize_full_kv_batch
 
@@ -191,7 +206,7 @@ def _full_context_golden(rng, arrays) -> list:
             port = sock.getsockname()[1]
         ctx = mp.get_context("spawn")
         out_q = ctx.Queue()
-        procs = [ctx.Process(target=_full_context_rank, args=(r, port, k, v, out_q)) for r in range(2)]
+        procs = [ctx.Process(target=_full_context_rank, args=(r, port, k, v, out_q, str(REF_SRC))) for r in range(2)]
         for proc in procs:
             proc.start()
         got = dict((r, (fk, fv)) for r, fk, fv in (out_q.get(timeout=120) for _ in range(2)))
@@ -207,6 +222,8 @@ def _full_context_golden(rng, arrays) -> list:
 
 
 def main() -> None:
+    global REF_SRC
+    REF_SRC = _reference_src(sys.argv)
     sys.path.insert(0, str(REF_SRC))
     _install_stubs()
     import dgx_monarch.adapters.base as base
@@ -238,7 +255,7 @@ def main() -> None:
         padded.append({"segments": segs, "world": world, "rows": base.padded_row_indices(segs)})
     golden["padded_row_indices"] = padded
 
-    # b) joint key order (adapters/usp_sequence_order.py:246-309).
+    # b) joint key order (adapters/usp_sequence_order.py:69-146).
     joint = []
     for text, image, world in ((1, 1, 2), (3, 5, 2), (128, 2048, 2), (7, 2, 4), (64, 1152, 8),
                                (2, 4, 2), (5, 3, 3)):

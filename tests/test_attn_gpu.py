@@ -168,7 +168,7 @@ def test_invalid_arguments_raise_before_launch(lib):
 
 def test_keep_masks_exclude_pad_rows_exactly(lib):
     """In-kernel pad exclusion: attention over the kept rows only, zeros (and
-    LSE -inf) at dropped query rows -- adapters/usp_pad_exclusion.py:152-177."""
+    LSE -inf) at dropped query rows -- adapters/usp_pad_exclusion.py:112-137."""
     from dgx_monarch_b200.ops import attention_fwd_ext, keep_bits
 
     g = torch.Generator(device="cuda").manual_seed(31)

@@ -121,3 +121,42 @@ def _handles_worker(rank, world):
 
 def test_peer_window_handle_exchange_is_rank_ordered():
     spawn(_handles_worker)
+
+
+@pytest.mark.parametrize("world,uly,ring", [(8, 2, 4), (8, 4, 2), (8, 8, 1), (8, 1, 8), (4, 2, 2),
+                                             (16, 2, 4), (6, 3, 2), (2, 1, 2)])
+def test_hybrid_layout_matches_the_oracle(world, uly, ring):
+    """The package's Ulysses x ring group layout is the oracle's ulysses-low
+    restatement, every group a partition of the world."""
+    from dgx_monarch_b200.groups import hybrid_layout
+    from oracle.usp import hybrid_groups
+
+    got = hybrid_layout(world, uly, ring)
+    assert got == hybrid_groups(world, uly, ring)
+    for groups, size in zip(got, (uly, ring)):
+        assert sorted(r for g in groups for r in g) == list(range(world))
+        assert all(len(g) == size for g in groups)
+
+
+def test_hybrid_layout_refuses_a_world_it_does_not_tile():
+    from dgx_monarch_b200.groups import hybrid_layout
+
+    with pytest.raises(ValueError, match="not a multiple"):
+        hybrid_layout(6, 2, 2)
+
+
+def _groups_worker(rank, world):
+    from dgx_monarch_b200.groups import new_hybrid_groups
+
+    for uly, ring in ((2, 1), (1, 2)):
+        ug, rg = new_hybrid_groups(world, uly, ring)
+        assert dist.get_world_size(ug) == uly and dist.get_world_size(rg) == ring
+        # A collective over each group sees exactly that group's ranks.
+        for group, size in ((ug, uly), (rg, ring)):
+            t = torch.tensor([float(rank + 1)])
+            dist.all_reduce(t, group=group)
+            assert t.item() == (3.0 if size == 2 else float(rank + 1))
+
+
+def test_new_hybrid_groups_world2():
+    spawn(_groups_worker, 2)

@@ -185,7 +185,7 @@ def _bias_groups(case):
 @pytest.mark.parametrize("case", SPEC["query_bias"], ids=lambda c: c["name"])
 def test_query_bias_groups_match_reference(case):
     """Query-group biases through the reference's callable
-    (adapters/usp_query_bias.py:109-130, with pads adapters/usp_pad_exclusion.py:152-177)."""
+    (adapters/usp_query_bias.py:109-130, with pads adapters/usp_pad_exclusion.py:112-137)."""
     name = case["name"]
     q, k, v = (ARR[f"bias_{name}_{x}"] for x in "qkv")
     drop = case["drop"]

@@ -119,7 +119,7 @@ def test_routed_epilogue_equals_attention_then_gather(lib, world, seq_local, hea
 @pytest.mark.parametrize("world,text,image,heads", [(2, 3, 5, 4), (4, 16, 48, 8), (8, 64, 1152 // 8, 24)])
 def test_joint_order_scatter_is_canonical_bit_exact(lib, world, text, image, heads):
     """seg0 > 0 writes the stock [t0,t1,...,i0,i1,...] order that
-    RankMajorJointOrder.canonicalize (adapters/usp_sequence_order.py:282-309)
+    RankMajorJointOrder.canonicalize (adapters/usp_sequence_order.py:105-146)
     produces from the rank-major gathered axis."""
     from dgx_monarch_b200.ulysses import ulysses_gather, ulysses_scatter
 

@@ -185,7 +185,7 @@ def test_rank_bias_slices_heads_and_spreads_past_interior_key_pads(drop):
 @pytest.mark.parametrize("text,image,world", [(3, 5, 2), (64, 1152, 8), (1, 1, 4), (2, 7, 3)])
 def test_joint_inverse_is_the_oracle_inverse_permutation(text, image, world):
     """rank-major gathered row -> canonical row, the inverse of the oracle's
-    RankMajorJointOrder permutation (adapters/usp_sequence_order.py:246-261)."""
+    RankMajorJointOrder permutation (adapters/usp_sequence_order.py:69-78)."""
     from dgx_monarch_b200.usp import _joint_inverse
 
     order = oracle.RankMajorJointOrder(text, image)
