@@ -325,6 +325,42 @@ def time_steps(step, steps: int, warmup: int, graph: bool = False) -> float:
     return e0.elapsed_time(e1) / steps
 
 
+def check_sampled_rows(out, world: int, rank: int, dev, ls: int, n_rows: int = 64) -> dict:
+    """The timed step's output on a sample of this rank's query rows (all
+    heads) against fp32 attention over the whole key axis, outside the timed
+    region.  Every rank's seeded inputs are regenerated here (same seeds, same
+    generator), so each rank checks its own rows against every key.  Bounds:
+    bf16 max-abs 2e-2, rel-L2 5e-3; the result is the max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    ks, vs, q_local = [], [], None
+    for r in range(world):
+        g = torch.Generator(device=dev).manual_seed(1234 + r)
+        q_r, k_r, v_r = (torch.randn(BATCH, ls, HEADS, DIM, device=dev, generator=g, dtype=torch.bfloat16)
+                         for _ in range(3))
+        ks.append(k_r)
+        vs.append(v_r)
+        if r == rank:
+            q_local = q_r
+    k, v = torch.cat(ks, dim=1).float(), torch.cat(vs, dim=1).float()
+    del ks, vs
+    g = torch.Generator(device=dev).manual_seed(77 + rank)
+    rows = torch.cat((torch.randint(0, ls, (n_rows - 8,), device=dev, generator=g),
+                      torch.arange(ls - 8, ls, device=dev)))
+    qs = q_local[:, rows].float().permute(0, 2, 1, 3)                    # B H n D
+    logits = torch.matmul(qs, k.permute(0, 2, 3, 1)) / math.sqrt(DIM)    # B H n S
+    ref = torch.matmul(torch.softmax(logits, dim=-1), v.permute(0, 2, 1, 3)).permute(0, 2, 1, 3)
+    got = out[:, rows].float()
+    err = torch.tensor([(got - ref).abs().max().item(),
+                        ((got - ref).norm() / ref.norm()).item()], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(err, op=dist.ReduceOp.MAX)
+    max_abs, rel = err.tolist()
+    return {"rows_per_rank": n_rows, "heads": HEADS, "against": "fp32 attention over all keys",
+            "max_abs": max_abs, "rel_l2": rel, "ok": bool(max_abs <= 2e-2 and rel <= 5e-3)}
+
+
 def dit_layer_flops() -> float:
     s, hid = DIT["img"] + DIT["txt"], DIT["hidden"]
     return 2.0 * s * hid * 3 * hid + 2.0 * s * hid * hid + attn_flops(1, DIT["heads"], s, DIM)
@@ -660,6 +696,7 @@ def main() -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, attn_ms = t.tolist()
     launches = args.steps * runner.launches_per_step
+    check = check_sampled_rows(out, world, rank, dev, ls)
 
     # End to end through the public call with host buffers: pinned host Q/K/V in,
     # output back to pinned host memory, every step.
@@ -770,6 +807,7 @@ def main() -> None:
                                    "note": "measured cuBLAS bf16 GEMM held for seconds under the 1 kW cap"},
             "clocks": clk,
             "device_error": dev_err,
+            "check": check,
         }
         if world > 1:
             line["all_to_all"] = {"kernel": "ulysses_scatter_kernel", "ms": a2a_ms,
@@ -800,6 +838,8 @@ def main() -> None:
             line["cpu_baseline"]["kind"] = "port"
         print(json.dumps(line), flush=True)
     streamed.close()
+    if not check["ok"]:
+        raise SystemExit(f"the timed step's output failed its sampled fp32 check: {check}")
     if over is not None:
         over.close()
     uly.close()

@@ -71,7 +71,7 @@ constexpr int kHeadDim = 128;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
-template <bool FP8>
+template <bool FP8, bool F16 = false>
 struct AttnCfg {
   static constexpr int kEltBytes = FP8 ? 1 : 2;
   static constexpr int kBoxCols = 128 / kEltBytes;          // elements in one 128-byte row
@@ -89,8 +89,11 @@ struct AttnCfg {
   // normal range; the epilogue divides the factor back out.
   static constexpr float kPScale = FP8 ? 16.0f : 1.0f;
   static constexpr float kPScaleLog2 = FP8 ? 4.0f : 0.0f;
-  static constexpr uint32_t kIdescQK = idesc_make(128, 128, FP8 ? 0u : 1u, false);
-  static constexpr uint32_t kIdescPV = idesc_make(128, 128, FP8 ? 0u : 1u, true);
+  // Operand format: e4m3 (kind::f8f6f4) 0; under kind::f16, f16 0 and bf16 1.
+  // P takes the inputs' 16-bit format, so A and B of P.V always match.
+  static constexpr uint32_t kFmt = FP8 ? 0u : (F16 ? 0u : 1u);
+  static constexpr uint32_t kIdescQK = idesc_make(128, 128, kFmt, false);
+  static constexpr uint32_t kIdescPV = idesc_make(128, 128, kFmt, true);
   static constexpr int kSmemBytes = 1024 /*align slack*/ + 2 * kTileBytes + kStages * kTileBytes +
                                     1024 /*barriers + slots*/ + 12 * 128 * 4 /*row exchange*/;
 };
@@ -183,9 +186,9 @@ __device__ __forceinline__ uint64_t sdesc_join(uint32_t lo, uint32_t hi) {
 
 // S = Q K^T: both operands K-major, one 128-byte swizzle atom per 64 (bf16)
 // or 128 (e4m3) head-dim columns.  q_lo / k_lo are the tiles' low words.
-template <bool FP8>
+template <bool FP8, bool F16>
 __device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_lo, uint32_t k_lo) {
-  using C = AttnCfg<FP8>;
+  using C = AttnCfg<FP8, F16>;
   constexpr uint32_t hi = sdesc_hi(1024);
 #pragma unroll
   for (int kk = 0; kk < C::kKSteps; ++kk) {
@@ -203,10 +206,10 @@ __device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_lo, uint32_
 // O += P V: P from tensor memory, V MN-major (head_dim along the 128-byte
 // rows, keys down the rows; the second 128-byte column block of bf16 sits
 // kBoxBytes further, the leading byte offset).
-template <bool FP8>
+template <bool FP8, bool F16>
 __device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_lo,
                                          bool accumulate) {
-  using C = AttnCfg<FP8>;
+  using C = AttnCfg<FP8, F16>;
   constexpr uint32_t hi = sdesc_hi(1024);
 #pragma unroll
   for (int kk = 0; kk < C::kKSteps; ++kk) {
@@ -224,10 +227,10 @@ __device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint3
 // both column halves c, K = 64 / kPChunks -- the probabilities one chunk of
 // every softmax thread has stored.  The first step of chunk 0 starts the
 // accumulation when `accumulate` is false.
-template <bool FP8, int kPChunks>
+template <bool FP8, bool F16, int kPChunks>
 __device__ __forceinline__ void issue_pv_chunk(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_lo,
                                                bool accumulate, int ch) {
-  using C = AttnCfg<FP8>;
+  using C = AttnCfg<FP8, F16>;
   constexpr uint32_t hi = sdesc_hi(1024);
   constexpr int kKeys = 64 / kPChunks;         // keys of one column half in one chunk
   constexpr int kSteps = kKeys / C::kMmaK;     // MMAs per column half per chunk
@@ -250,7 +253,7 @@ __device__ __forceinline__ void issue_pv_chunk(uint32_t d_tmem, uint32_t p_tmem,
 
 // O += P V of one tile, chunk by chunk as the softmax releases P: each chunk
 // waits for its own barrier.  Returns false when a wait gave up.
-template <bool FP8, int kPChunks, int kBarPFull>
+template <bool FP8, bool F16, int kPChunks, int kBarPFull>
 __device__ __forceinline__ bool issue_pv_chunks(uint64_t* bars, uint32_t d_tmem, uint32_t p_tmem,
                                                 uint32_t v_lo, bool accumulate, int parity,
                                                 volatile int* abort_flag) {
@@ -258,7 +261,7 @@ __device__ __forceinline__ bool issue_pv_chunks(uint64_t* bars, uint32_t d_tmem,
   for (int ch = 0; ch < kPChunks; ++ch) {
     if (!mbar_wait(smem_u32(&bars[kBarPFull + ch]), parity, abort_flag)) return false;
     tc_fence_after();
-    issue_pv_chunk<FP8, kPChunks>(d_tmem, p_tmem, v_lo, accumulate, ch);
+    issue_pv_chunk<FP8, F16, kPChunks>(d_tmem, p_tmem, v_lo, accumulate, ch);
   }
   return true;
 }
@@ -268,9 +271,11 @@ __device__ __forceinline__ void raise_abort(volatile int* abort_flag, int bits) 
   *abort_flag = 1;
 }
 
-template <bool FP8, bool OUT_F32, bool EXTRA, int NCH, bool PP>
+// F16: 16-bit inputs (and P) are fp16 instead of bf16; a 16-bit output is
+// then fp16 too.
+template <bool FP8, bool OUT_F32, bool EXTRA, int NCH, bool PP, bool F16>
 __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_constant__ AttnParams p) {
-  using C = AttnCfg<FP8>;
+  using C = AttnCfg<FP8, F16>;
   constexpr int kPChunks = p_chunks<FP8, NCH>();
   using B = Bars<C::kStages, kPChunks, PP>;
   extern __shared__ uint8_t smem_raw[];
@@ -394,19 +399,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
           if (!(ok = mbar_wait(bar(B::kPvDone + 0), (j - 1) & 1, abort_flag))) break;
           tc_fence_after();
         }
-        issue_qk<FP8>(tS0, q0_lo, kv_lo_k + ks * kStageLo);
+        issue_qk<FP8, F16>(tS0, q0_lo, kv_lo_k + ks * kStageLo);
         umma_commit(bar(B::kSFull + 0));
         // O1 += P1 V_{j-1}
         if (j > 0) {
           const int vs = (2 * j - 1) % C::kStages;
           if constexpr (kPChunks > 1) {
-            if (!(ok = issue_pv_chunks<FP8, kPChunks, B::kPFull + kPChunks>(
+            if (!(ok = issue_pv_chunks<FP8, F16, kPChunks, B::kPFull + kPChunks>(
                       bars, tO1, tS1, kv_lo_v + vs * kStageLo, j - 1 > 0, (j - 1) & 1, abort_flag)))
               break;
           } else {
             if (!(ok = mbar_wait(bar(B::kPFull + 1), (j - 1) & 1, abort_flag))) break;
             tc_fence_after();
-            issue_pv<FP8>(tO1, tS1, kv_lo_v + vs * kStageLo, j - 1 > 0);
+            issue_pv<FP8, F16>(tO1, tS1, kv_lo_v + vs * kStageLo, j - 1 > 0);
           }
           umma_commit(bar(B::kKvEmpty + vs));
           if (safe_order) {
@@ -416,7 +421,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
           }
         }
         // S1 = Q1 K_j^T
-        issue_qk<FP8>(tS1, q1_lo, kv_lo_k + ks * kStageLo);
+        issue_qk<FP8, F16>(tS1, q1_lo, kv_lo_k + ks * kStageLo);
         umma_commit(bar(B::kSFull + 1));
         umma_commit(bar(B::kKvEmpty + ks));
         // O0 += P0 V_j
@@ -424,13 +429,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
         const int vs = vi % C::kStages;
         if (!(ok = mbar_wait(bar(B::kKvFull + vs), (vi / C::kStages) & 1, abort_flag))) break;
         if constexpr (kPChunks > 1) {
-          if (!(ok = issue_pv_chunks<FP8, kPChunks, B::kPFull>(bars, tO0, tS0, kv_lo_v + vs * kStageLo, j > 0,
+          if (!(ok = issue_pv_chunks<FP8, F16, kPChunks, B::kPFull>(bars, tO0, tS0, kv_lo_v + vs * kStageLo, j > 0,
                                                      j & 1, abort_flag)))
             break;
         } else {
           if (!(ok = mbar_wait(bar(B::kPFull + 0), j & 1, abort_flag))) break;
           tc_fence_after();
-          issue_pv<FP8>(tO0, tS0, kv_lo_v + vs * kStageLo, j > 0);
+          issue_pv<FP8, F16>(tO0, tS0, kv_lo_v + vs * kStageLo, j > 0);
         }
         if (safe_order) umma_commit(bar(B::kPvDone + 0));
         if (j == nkv - 1) umma_commit(bar(B::kOFull + 0));
@@ -439,13 +444,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
         // O1 += P1 V_{n-1}
         const int vs = (2 * nkv - 1) % C::kStages;
         if constexpr (kPChunks > 1) {
-          ok = issue_pv_chunks<FP8, kPChunks, B::kPFull + kPChunks>(bars, tO1, tS1, kv_lo_v + vs * kStageLo,
+          ok = issue_pv_chunks<FP8, F16, kPChunks, B::kPFull + kPChunks>(bars, tO1, tS1, kv_lo_v + vs * kStageLo,
                                                             nkv - 1 > 0, (nkv - 1) & 1, abort_flag);
         } else {
           ok = mbar_wait(bar(B::kPFull + 1), (nkv - 1) & 1, abort_flag);
           if (ok) {
             tc_fence_after();
-            issue_pv<FP8>(tO1, tS1, kv_lo_v + vs * kStageLo, nkv - 1 > 0);
+            issue_pv<FP8, F16>(tO1, tS1, kv_lo_v + vs * kStageLo, nkv - 1 > 0);
           }
         }
         if (ok) {
@@ -634,7 +639,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
               s[2 * i] = p0;
               s[2 * i + 1] = p1;
             } else {
-              pk[q] = pack_bf16x2(p0, p1);
+              pk[q] = pack16<F16>(p0, p1);
             }
           }
           if constexpr (PP) {
@@ -699,7 +704,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
             s[2 * i] = p0;
             s[2 * i + 1] = p1;
           } else {
-            pk[i] = pack_bf16x2(p0, p1);
+            pk[i] = pack16<F16>(p0, p1);
           }
         }
         if constexpr (PP) mbar_arrive(bar(B::kTurn + t));  // the other tile's turn
@@ -832,10 +837,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
             uint4 w[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-              w[i].x = pack_bf16x2(__uint_as_float(o[8 * i + 0]) * inv, __uint_as_float(o[8 * i + 1]) * inv);
-              w[i].y = pack_bf16x2(__uint_as_float(o[8 * i + 2]) * inv, __uint_as_float(o[8 * i + 3]) * inv);
-              w[i].z = pack_bf16x2(__uint_as_float(o[8 * i + 4]) * inv, __uint_as_float(o[8 * i + 5]) * inv);
-              w[i].w = pack_bf16x2(__uint_as_float(o[8 * i + 6]) * inv, __uint_as_float(o[8 * i + 7]) * inv);
+              w[i].x = pack16<F16>(__uint_as_float(o[8 * i + 0]) * inv, __uint_as_float(o[8 * i + 1]) * inv);
+              w[i].y = pack16<F16>(__uint_as_float(o[8 * i + 2]) * inv, __uint_as_float(o[8 * i + 3]) * inv);
+              w[i].z = pack16<F16>(__uint_as_float(o[8 * i + 4]) * inv, __uint_as_float(o[8 * i + 5]) * inv);
+              w[i].w = pack16<F16>(__uint_as_float(o[8 * i + 6]) * inv, __uint_as_float(o[8 * i + 7]) * inv);
             }
             for (int dd = 0; dd < n_dst; ++dd) {
               uint4* dst = reinterpret_cast<uint4*>(
@@ -860,11 +865,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
   }
 }
 
-template <bool FP8, bool OUT_F32, bool EXTRA, int NCH, bool PP = false>
+template <bool FP8, bool OUT_F32, bool EXTRA, int NCH, bool PP = false, bool F16 = false>
 static int launch_attn(const AttnParams& prm, dim3 grid, cudaStream_t stream) {
-  using C = AttnCfg<FP8>;
+  using C = AttnCfg<FP8, F16>;
   static std::atomic<uint64_t> configured{0};  // one bit per device ordinal
-  auto kern = attn_fwd_kernel<FP8, OUT_F32, EXTRA, NCH, PP>;
+  auto kern = attn_fwd_kernel<FP8, OUT_F32, EXTRA, NCH, PP, F16>;
   DGXM_CUDA_TRY(set_smem_limit_once(kern, C::kSmemBytes, configured));
   kern<<<grid, kAttnThreads, C::kSmemBytes, stream>>>(prm);
   DGXM_CUDA_TRY(cudaGetLastError());
@@ -903,13 +908,17 @@ static int prepare_attn(const dgxm_attn_desc* d, const void* q, const void* k, c
     return fail(DGXM_ERR_UNSUPPORTED, "batch %d or heads %d exceed the launch grid", d->batch,
                 d->q_heads);
   const bool fp8 = d->in_dtype == DGXM_DTYPE_E4M3;
-  if (!fp8 && d->in_dtype != DGXM_DTYPE_BF16)
-    return fail(DGXM_ERR_UNSUPPORTED, "input dtype %d is not supported (bf16 or e4m3)",
+  const bool f16 = d->in_dtype == DGXM_DTYPE_F16;
+  if (!fp8 && !f16 && d->in_dtype != DGXM_DTYPE_BF16)
+    return fail(DGXM_ERR_UNSUPPORTED, "input dtype %d is not supported (bf16, f16 or e4m3)",
                 d->in_dtype);
+  // A 16-bit output takes the inputs' 16-bit format (bf16 for e4m3 inputs).
   const bool out_f32 = d->out_dtype == DGXM_DTYPE_F32;
-  if (!out_f32 && d->out_dtype != DGXM_DTYPE_BF16)
-    return fail(DGXM_ERR_UNSUPPORTED, "output dtype %d is not supported (bf16 or f32)",
-                d->out_dtype);
+  const int out16 = f16 ? DGXM_DTYPE_F16 : DGXM_DTYPE_BF16;
+  if (!out_f32 && d->out_dtype != out16)
+    return fail(DGXM_ERR_UNSUPPORTED,
+                "output dtype %d is not supported for input dtype %d (f32, or %s)", d->out_dtype,
+                d->in_dtype, f16 ? "f16" : "bf16");
   if (q == nullptr || k == nullptr || v == nullptr || o == nullptr)
     return fail(DGXM_ERR_INVALID, "q, k, v and o must be non-NULL");
   if (fp8 && (q_descale == nullptr || k_descale == nullptr || v_descale == nullptr))
@@ -921,7 +930,8 @@ static int prepare_attn(const dgxm_attn_desc* d, const void* q, const void* k, c
 
   AttnParams& prm = *out_prm;
   memset(&prm, 0, sizeof(prm));
-  const CUtensorMapDataType dt = fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const CUtensorMapDataType dt = fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                : (f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16);
   const int eb = fp8 ? 1 : 2;
   const int box_cols = 128 / eb;
   int rc;
@@ -972,6 +982,13 @@ static int dispatch_attn_n(const dgxm_attn_desc* d, const AttnParams& prm, dim3 
 
 template <bool EXTRA>
 static int dispatch_attn_t(const dgxm_attn_desc* d, const AttnParams& prm, dim3 grid, cudaStream_t st) {
+  if (d->in_dtype == DGXM_DTYPE_F16) {
+    // fp16 inputs run the library's default schedule; the chunk and ping-pong
+    // flags select among the bf16 and e4m3 instantiations only.
+    if (d->out_dtype == DGXM_DTYPE_F32)
+      return launch_attn<false, true, EXTRA, DGXM_SM_P_CHUNKS, false, true>(prm, grid, st);
+    return launch_attn<false, false, EXTRA, DGXM_SM_P_CHUNKS, false, true>(prm, grid, st);
+  }
   int nch = (d->flags & DGXM_ATTN_P_CHUNKS_MASK) >> DGXM_ATTN_P_CHUNKS_SHIFT;
   if (nch == 0) nch = DGXM_SM_P_CHUNKS;
   // The ping-pong schedule is built for bf16 output without extras (bf16 or

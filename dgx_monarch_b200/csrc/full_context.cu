@@ -76,8 +76,8 @@ extern "C" int dgxm_full_context_attn_fwd(dgxm_comm* c, const dgxm_attn_desc* d,
   if (c == nullptr || d == nullptr) return fail(DGXM_ERR_INVALID, "NULL comm or descriptor");
   const int world = c->world;
   if (world == 1) return dgxm_attn_fwd(d, q, k, v, nullptr, nullptr, nullptr, o, lse, stream);
-  if (d->in_dtype != DGXM_DTYPE_BF16)
-    return fail(DGXM_ERR_UNSUPPORTED, "full-context ring attention runs bf16 inputs");
+  if (d->in_dtype != DGXM_DTYPE_BF16 && d->in_dtype != DGXM_DTYPE_F16)
+    return fail(DGXM_ERR_UNSUPPORTED, "full-context ring attention runs bf16 or f16 inputs");
   if (d->head_dim != kHeadDim)
     return fail(DGXM_ERR_UNSUPPORTED, "head_dim %d is not supported (this build runs 128)",
                 d->head_dim);

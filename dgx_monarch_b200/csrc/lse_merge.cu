@@ -9,7 +9,7 @@
 //
 // HBM-bound: one warp per (batch, row, head) row of head_dim = 128 values;
 // each lane owns four consecutive values, so every part's row is read with one
-// fully coalesced 256-byte (bf16) or 512-byte (fp32) warp access.  The common
+// fully coalesced 256-byte (bf16 / fp16) or 512-byte (fp32) warp access.  The common
 // part counts (the ring degrees) are compiled in, so all of a row's loads are
 // in flight at once.
 #include "common.h"
@@ -28,14 +28,21 @@ struct MergeParams {
   int batch, rows, heads;
 };
 
-template <bool PART_F32>
+// Element types of the parts and the output: DGXM_DTYPE_BF16, _F16 or _F32.
+template <int T>
 __device__ __forceinline__ float4 load_part(const void* base, int64_t elem) {
-  if constexpr (PART_F32) {
+  if constexpr (T == DGXM_DTYPE_F32) {
     return *reinterpret_cast<const float4*>(static_cast<const float*>(base) + elem);
   } else {
-    const uint2 v = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(base) + elem);
-    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.x));
-    const float2 c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.y));
+    const uint2 v = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(base) + elem);
+    float2 a, c;
+    if constexpr (T == DGXM_DTYPE_F16) {
+      a = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
+      c = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+    } else {
+      a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.x));
+      c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.y));
+    }
     return make_float4(a.x, a.y, c.x, c.y);
   }
 }
@@ -43,7 +50,7 @@ __device__ __forceinline__ float4 load_part(const void* base, int64_t elem) {
 // NP > 0 fixes the part count at compile time: every part's row and LSE is
 // loaded before the first is used, so a warp keeps NP loads in flight
 // instead of one (NP == 0 loops over p.n parts).
-template <bool PART_F32, bool OUT_F32, int NP>
+template <int PART, int OUT, int NP>
 __global__ void __launch_bounds__(256) lse_merge_kernel(const __grid_constant__ MergeParams p) {
   constexpr int kSlots = NP > 0 ? NP : 1;
   const int warps_per_block = blockDim.x >> 5;
@@ -66,7 +73,7 @@ __global__ void __launch_bounds__(256) lse_merge_kernel(const __grid_constant__ 
 #pragma unroll
       for (int i = 0; i < NP; ++i) {
         li[i] = p.lse[i][lse_idx];
-        xv[i] = load_part<PART_F32>(p.out[i], elem);
+        xv[i] = load_part<PART>(p.out[i], elem);
       }
 #pragma unroll
       for (int i = 0; i < NP; ++i) mx = fmaxf(mx, li[i]);
@@ -86,7 +93,7 @@ __global__ void __launch_bounds__(256) lse_merge_kernel(const __grid_constant__ 
         const float li = p.lse[i][lse_idx];
         const float w = (li == -INFINITY) ? 0.f : __expf(li - mx);
         wsum += w;
-        const float4 x = load_part<PART_F32>(p.out[i], elem);
+        const float4 x = load_part<PART>(p.out[i], elem);
         acc.x = fmaf(w, x.x, acc.x);
         acc.y = fmaf(w, x.y, acc.y);
         acc.z = fmaf(w, x.z, acc.z);
@@ -94,29 +101,30 @@ __global__ void __launch_bounds__(256) lse_merge_kernel(const __grid_constant__ 
       }
     }
     const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
-    if constexpr (OUT_F32) {
+    if constexpr (OUT == DGXM_DTYPE_F32) {
       *reinterpret_cast<float4*>(static_cast<float*>(p.dst) + elem) =
           make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
     } else {
+      constexpr bool kF16 = OUT == DGXM_DTYPE_F16;
       uint2 w;
-      w.x = pack_bf16x2(acc.x * inv, acc.y * inv);
-      w.y = pack_bf16x2(acc.z * inv, acc.w * inv);
-      *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(p.dst) + elem) = w;
+      w.x = pack16<kF16>(acc.x * inv, acc.y * inv);
+      w.y = pack16<kF16>(acc.z * inv, acc.w * inv);
+      *reinterpret_cast<uint2*>(static_cast<uint16_t*>(p.dst) + elem) = w;
     }
     if (lane == 0 && p.dst_lse != nullptr)
       p.dst_lse[lse_idx] = wsum > 0.f ? mx + __logf(wsum) : -INFINITY;
   }
 }
 
-template <bool PART_F32, bool OUT_F32>
+template <int PART, int OUT>
 static void launch_merge(const MergeParams& prm, int blocks, cudaStream_t st) {
   switch (prm.n) {
-    case 1: lse_merge_kernel<PART_F32, OUT_F32, 1><<<blocks, 256, 0, st>>>(prm); break;
-    case 2: lse_merge_kernel<PART_F32, OUT_F32, 2><<<blocks, 256, 0, st>>>(prm); break;
-    case 3: lse_merge_kernel<PART_F32, OUT_F32, 3><<<blocks, 256, 0, st>>>(prm); break;
-    case 4: lse_merge_kernel<PART_F32, OUT_F32, 4><<<blocks, 256, 0, st>>>(prm); break;
-    case 8: lse_merge_kernel<PART_F32, OUT_F32, 8><<<blocks, 256, 0, st>>>(prm); break;
-    default: lse_merge_kernel<PART_F32, OUT_F32, 0><<<blocks, 256, 0, st>>>(prm); break;
+    case 1: lse_merge_kernel<PART, OUT, 1><<<blocks, 256, 0, st>>>(prm); break;
+    case 2: lse_merge_kernel<PART, OUT, 2><<<blocks, 256, 0, st>>>(prm); break;
+    case 3: lse_merge_kernel<PART, OUT, 3><<<blocks, 256, 0, st>>>(prm); break;
+    case 4: lse_merge_kernel<PART, OUT, 4><<<blocks, 256, 0, st>>>(prm); break;
+    case 8: lse_merge_kernel<PART, OUT, 8><<<blocks, 256, 0, st>>>(prm); break;
+    default: lse_merge_kernel<PART, OUT, 0><<<blocks, 256, 0, st>>>(prm); break;
   }
 }
 
@@ -133,12 +141,19 @@ extern "C" int dgxm_lse_merge(int32_t batch, int32_t rows, int32_t heads, int32_
     return fail(DGXM_ERR_UNSUPPORTED, "merge head_dim %d is not supported (128)", head_dim);
   if (n_parts < 1 || n_parts > kMaxMergeParts)
     return fail(DGXM_ERR_INVALID, "merge takes 1..%d parts, got %d", kMaxMergeParts, n_parts);
-  const bool part_f32 = part_dtype == DGXM_DTYPE_F32;
-  if (!part_f32 && part_dtype != DGXM_DTYPE_BF16)
+  auto float_type = [](int t) {
+    return t == DGXM_DTYPE_F32 || t == DGXM_DTYPE_BF16 || t == DGXM_DTYPE_F16;
+  };
+  if (!float_type(part_dtype))
     return fail(DGXM_ERR_UNSUPPORTED, "merge part dtype %d is not supported", part_dtype);
-  const bool out_f32 = out_dtype == DGXM_DTYPE_F32;
-  if (!out_f32 && out_dtype != DGXM_DTYPE_BF16)
+  if (!float_type(out_dtype))
     return fail(DGXM_ERR_UNSUPPORTED, "merge output dtype %d is not supported", out_dtype);
+  // 16-bit parts merge into fp32 or their own 16-bit format.
+  const bool mixed16 = part_dtype != DGXM_DTYPE_F32 && out_dtype != DGXM_DTYPE_F32 &&
+                       part_dtype != out_dtype;
+  if (mixed16)
+    return fail(DGXM_ERR_UNSUPPORTED, "merge of %s parts into a %s output is not supported",
+                part_dtype == DGXM_DTYPE_F16 ? "f16" : "bf16", out_dtype == DGXM_DTYPE_F16 ? "f16" : "bf16");
   if (parts_out == nullptr || parts_lse == nullptr)
     return fail(DGXM_ERR_INVALID, "merge part arrays must be non-NULL");
   // Nothing to merge: empty tensors may carry NULL data pointers.
@@ -169,12 +184,19 @@ extern "C" int dgxm_lse_merge(int32_t batch, int32_t rows, int32_t heads, int32_
   const int64_t want = (items + 7) / 8;
   const int blocks = static_cast<int>(want < int64_t(sms) * 16 ? want : int64_t(sms) * 16);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (part_f32) {
-    if (out_f32) launch_merge<true, true>(prm, blocks, st);
-    else launch_merge<true, false>(prm, blocks, st);
+  // Ring steps hand fp32 parts; 16-bit parts come from callers that merge
+  // blocks they attended themselves.
+  constexpr int F32 = DGXM_DTYPE_F32, BF = DGXM_DTYPE_BF16, H = DGXM_DTYPE_F16;
+  if (part_dtype == F32) {
+    if (out_dtype == F32) launch_merge<F32, F32>(prm, blocks, st);
+    else if (out_dtype == BF) launch_merge<F32, BF>(prm, blocks, st);
+    else launch_merge<F32, H>(prm, blocks, st);
+  } else if (part_dtype == BF) {
+    if (out_dtype == F32) launch_merge<BF, F32>(prm, blocks, st);
+    else launch_merge<BF, BF>(prm, blocks, st);
   } else {
-    if (out_f32) launch_merge<false, true>(prm, blocks, st);
-    else launch_merge<false, false>(prm, blocks, st);
+    if (out_dtype == F32) launch_merge<H, F32>(prm, blocks, st);
+    else launch_merge<H, H>(prm, blocks, st);
   }
   DGXM_CUDA_TRY(cudaGetLastError());
   return DGXM_OK;

@@ -8,6 +8,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_fp8.h>
 #include <stdint.h>
 
@@ -200,7 +201,8 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo_byt
 }
 
 // Instruction descriptor: fp32 accumulator, dense, K-major A.
-//   fmt = 1 selects bf16 inputs under kind::f16, 0 selects e4m3 under kind::f8f6f4.
+//   Under kind::f16, fmt 0 selects f16 and 1 bf16 inputs; under kind::f8f6f4,
+//   0 selects e4m3.  A and B always carry the same format here.
 __host__ __device__ constexpr uint32_t idesc_make(int m, int n, uint32_t fmt, bool b_mn_major) {
   return (1u << 4)                                   // D format: f32
          | (fmt << 7)                                // A format
@@ -387,6 +389,21 @@ __device__ __forceinline__ uint64_t exp2_poly2(uint64_t x) {
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// Two floats -> the 16-bit pair of the kernel's format (fp16 or bf16),
+// round-to-nearest-even, first value in the low half.
+template <bool F16>
+__device__ __forceinline__ uint32_t pack16(float lo, float hi) {
+  if constexpr (F16)
+    return pack_f16x2(lo, hi);
+  else
+    return pack_bf16x2(lo, hi);
 }
 
 // Four floats -> four e4m3 bytes (saturating), first value in the low byte.

@@ -94,8 +94,8 @@ static int ring_attn_impl(dgxm_comm* c, const dgxm_attn_desc* d, const void* q, 
   if (lse != nullptr && !contiguous_bhl(d->lse_stride, d))
     return fail(DGXM_ERR_INVALID, "ring attention needs a contiguous (B, H, L) lse");
   if (world == 1) return dgxm_attn_fwd(d, q, k, v, nullptr, nullptr, nullptr, o, lse, stream);
-  if (d->in_dtype != DGXM_DTYPE_BF16)
-    return fail(DGXM_ERR_UNSUPPORTED, "ring attention runs bf16 inputs");
+  if (d->in_dtype != DGXM_DTYPE_BF16 && d->in_dtype != DGXM_DTYPE_F16)
+    return fail(DGXM_ERR_UNSUPPORTED, "ring attention runs bf16 or f16 inputs");
   const int64_t block = ring_block_bytes(d);
   const int64_t slot = round256(block);
   if (4 * slot > c->bytes)

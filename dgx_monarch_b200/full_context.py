@@ -23,7 +23,7 @@ import torch
 from .ring import FullContextRingAttention
 from .usp import UnsupportedModelError
 
-_SUPPORTED = (torch.bfloat16,)
+_SUPPORTED = (torch.float16, torch.bfloat16)
 
 
 def validate_flash_surface(*, dropout_p, softmax_scale, causal, window_size, softcap,
@@ -54,9 +54,8 @@ def validate_flash_surface(*, dropout_p, softmax_scale, causal, window_size, sof
 
 
 def validate_local_qkv(q, k, v) -> None:
-    """Equal local (B, L, H, 128) shards on one CUDA device, inference only
-    (adapters/wan_ring_full_context.py:17-60).  This kernel runs bf16; the
-    reference's fp16 case is refused by name."""
+    """Equal local (B, L, H, 128) fp16 or bf16 shards on one CUDA device,
+    inference only (adapters/wan_ring_full_context.py:17-60)."""
     if any(not isinstance(t, torch.Tensor) for t in (q, k, v)):
         raise UnsupportedModelError("Wan ring TORCH_FLASH requires tensor q/k/v inputs")
     if any(t.requires_grad for t in (q, k, v)):
@@ -70,8 +69,7 @@ def validate_local_qkv(q, k, v) -> None:
     if any(size < 1 for t in (q, k, v) for size in t.shape):
         raise UnsupportedModelError("Wan ring TORCH_FLASH requires non-empty q/k/v")
     if q.dtype not in _SUPPORTED or any(t.dtype != q.dtype for t in (k, v)):
-        raise UnsupportedModelError(
-            f"the B200 full-context kernel runs matching bf16 q/k/v; got {q.dtype}/{k.dtype}/{v.dtype}")
+        raise UnsupportedModelError("Wan ring TORCH_FLASH is validated for matching FP16/BF16 q/k/v only")
     if q.shape[-1] != 128:
         raise UnsupportedModelError("Wan ring TORCH_FLASH is validated for head dimension 128 only")
     if q.device.type != "cuda" or any(t.device != q.device for t in (k, v)):
@@ -121,12 +119,12 @@ def make_full_context_ring_attention(*, ring_group, generation: int = 1,
         if plans.get("closed"):
             raise UnsupportedModelError("this full-context ring belongs to a retired setup generation")
         b, l, h, d = q.shape
-        key = (b, l, h, k.shape[2], d)
+        key = (b, l, h, k.shape[2], d, q.dtype)
         plan = plans.get(key)
         if plan is None:
             plan = FullContextRingAttention(world=world, rank=rank, batch=b, q_len=l, kv_len=l, heads=h,
                                             kv_heads=k.shape[2], head_dim=d, device=device,
-                                            group=ring_group, generation=generation)
+                                            group=ring_group, generation=generation, dtype=q.dtype)
             plans[key] = plan
         out, _ = plan.forward(q, k, v)
         return out

@@ -20,11 +20,19 @@ _FP8 = getattr(torch, "float8_e4m3fn", None)
 def _dtype_code(dtype: torch.dtype) -> int:
     if dtype == torch.bfloat16:
         return _lib.DTYPE_BF16
+    if dtype == torch.float16:
+        return _lib.DTYPE_F16
     if dtype == torch.float32:
         return _lib.DTYPE_F32
     if _FP8 is not None and dtype == _FP8:
         return _lib.DTYPE_E4M3
     raise TypeError(f"dtype {dtype} is not supported by the B200 attention path")
+
+
+def out16_dtype(in_dtype: torch.dtype) -> torch.dtype:
+    """The 16-bit output format of an attention over `in_dtype` inputs: fp16
+    for fp16, bf16 for bf16 and e4m3."""
+    return torch.float16 if in_dtype == torch.float16 else torch.bfloat16
 
 
 def _ptr(t: torch.Tensor | None) -> int | None:
@@ -134,7 +142,7 @@ def attn_desc(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tens
 
 def attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
                   softmax_scale: float | None = None,
-                  out_dtype: torch.dtype = torch.bfloat16,
+                  out_dtype: torch.dtype | None = None,
                   q_descale: torch.Tensor | None = None,
                   k_descale: torch.Tensor | None = None,
                   v_descale: torch.Tensor | None = None,
@@ -145,9 +153,11 @@ def attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
     """Non-causal attention over (B, L, H, D) tensors; returns (out, lse).
 
     ``lse`` is fp32 (B, H, Lq), the natural-log log-sum-exp of the scaled
-    logits, as the reference's ring processor contract requires.  bf16 inputs
-    run the bf16 tensor-core path; float8_e4m3fn inputs need fp32 descale
-    vectors (one per query head for q, one per key/value head for k and v).
+    logits, as the reference's ring processor contract requires.  bf16 and
+    fp16 inputs run the 16-bit tensor-core path in their own format (P too);
+    float8_e4m3fn inputs need fp32 descale vectors (one per query head for q,
+    one per key/value head for k and v).  out_dtype None is the inputs' 16-bit
+    format (bf16 for e4m3); fp32 is the other choice.
     """
     dev = _require_cuda(q, k, v)
     if q.ndim != 4 or k.ndim != 4 or v.ndim != 4:
@@ -163,7 +173,7 @@ def attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
             raise ValueError(f"{name} must have a contiguous head_dim")
     check_attn_buffers(q, k, out=out, lse=lse, q_descale=q_descale, k_descale=k_descale, v_descale=v_descale)
     if out is None:
-        out = torch.empty((b, lq, h, d), device=dev, dtype=out_dtype)
+        out = torch.empty((b, lq, h, d), device=dev, dtype=out_dtype or out16_dtype(q.dtype))
     if lse is None and return_lse:
         lse = torch.empty((b, h, lq), device=dev, dtype=torch.float32)
     desc = attn_desc(q, k, v, out, lse, softmax_scale, safe_order)
@@ -235,8 +245,9 @@ def attention_fwd_ext(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
     _require_on(dev, key_keep, query_keep, *[g[2] for g in (bias_groups or [])])
     keep = []
     if out is None and route is None:
-        out = torch.empty((b, lq, h, d), device=dev, dtype=torch.bfloat16)
-    probe_out = out if out is not None else torch.empty((1, 1, 1, d), device="meta", dtype=torch.bfloat16)
+        out = torch.empty((b, lq, h, d), device=dev, dtype=out16_dtype(q.dtype))
+    probe_out = out if out is not None else torch.empty((1, 1, 1, d), device="meta",
+                                                        dtype=out16_dtype(q.dtype))
     desc = attn_desc(q, k, v, probe_out, lse, softmax_scale)
     if out_strides is not None:
         desc.o_stride[:] = list(out_strides)

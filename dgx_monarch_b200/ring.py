@@ -81,11 +81,12 @@ class FullContextRingAttention:
 
     def __init__(self, *, world: int, rank: int, batch: int, q_len: int, kv_len: int, heads: int,
                  kv_heads: int, head_dim: int, device: torch.device, group=None,
-                 generation: int = 0, timeout_ms: int | None = None) -> None:
+                 generation: int = 0, timeout_ms: int | None = None,
+                 dtype: torch.dtype = torch.bfloat16) -> None:
         self.world, self.rank, self.device = world, rank, device
         self.shape = (batch, q_len, kv_len, heads, kv_heads, head_dim)
-        probe_q = torch.empty(batch, q_len, heads, head_dim, device="meta", dtype=torch.bfloat16)
-        probe_k = torch.empty(batch, kv_len, kv_heads, head_dim, device="meta", dtype=torch.bfloat16)
+        probe_q = torch.empty(batch, q_len, heads, head_dim, device="meta", dtype=dtype)
+        probe_k = torch.empty(batch, kv_len, kv_heads, head_dim, device="meta", dtype=dtype)
         desc = attn_desc(probe_q, probe_k, probe_k, probe_q, None)
         lib = _lib.load()
         self.window_bytes = int(lib.dgxm_full_context_window_bytes(ctypes.byref(desc), world))

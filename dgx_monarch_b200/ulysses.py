@@ -22,7 +22,7 @@ import torch
 
 from . import _lib
 from .comm import PeerWindows
-from .ops import _dtype_code, _ptr, _require_cuda, attention_fwd, attn_flags
+from .ops import _dtype_code, _ptr, _require_cuda, attention_fwd, attn_flags, out16_dtype
 
 
 def a2a_desc(n_tensors, world, rank, batch, seq_local, heads, head_dim, dtype, strides, seg0=0):
@@ -85,7 +85,7 @@ def attention_routed(q, k, v, out_ptrs: list[int], out_strides, *, world: int, r
     desc.batch, desc.q_len, desc.kv_len = b, lq, lk
     desc.q_heads, desc.kv_heads, desc.head_dim = hl, hkv, d
     desc.in_dtype = _dtype_code(q.dtype)
-    desc.out_dtype = _lib.DTYPE_BF16
+    desc.out_dtype = _dtype_code(out16_dtype(q.dtype))
     desc.q_stride[:] = [q.stride(0), q.stride(1), q.stride(2)]
     desc.k_stride[:] = [k.stride(0), k.stride(1), k.stride(2)]
     desc.v_stride[:] = [v.stride(0), v.stride(1), v.stride(2)]
@@ -236,8 +236,10 @@ class JointUlyssesAttention:
     (image output (B, Ls, H, D) of this rank's rows, text output (B, T, H, D),
     the same on every rank).
 
-    Inputs of any float dtype are computed in bf16 and returned in their own
-    dtype.  A head_dim below 128 (a multiple of 8) runs zero-padded to 128:
+    The step computes in `compute_dtype` (bf16, or fp16 for fp16 models):
+    inputs of any float dtype are rounded to it and the outputs are returned
+    in the inputs' own dtype, so an fp32 caller gets attention over its inputs
+    rounded to bf16.  A head_dim below 128 (a multiple of 8) runs zero-padded to 128:
     the padded columns add exact zeros to every logit and give zero output
     columns, which are dropped; the softmax scale stays 1/sqrt(head_dim).
     """
@@ -246,7 +248,10 @@ class JointUlyssesAttention:
 
     def __init__(self, *, world: int, rank: int, batch: int, seq_local: int, txt_rows: int,
                  heads: int, head_dim: int, device: torch.device, text_first: bool = True,
-                 group=None, generation: int = 0, softmax_scale: float | None = None) -> None:
+                 group=None, generation: int = 0, softmax_scale: float | None = None,
+                 compute_dtype: torch.dtype = torch.bfloat16) -> None:
+        if compute_dtype not in (torch.bfloat16, torch.float16):
+            raise ValueError(f"joint attention computes in bf16 or fp16, not {compute_dtype}")
         if heads % world:
             raise ValueError(f"{heads} heads do not divide the Ulysses degree {world}")
         if head_dim > self.KERNEL_HEAD_DIM or head_dim % 8:
@@ -263,7 +268,7 @@ class JointUlyssesAttention:
         self.scale = softmax_scale or 1.0 / math.sqrt(head_dim)
         dk = self.KERNEL_HEAD_DIM
         self.rows = txt_rows + world * seq_local
-        dt = torch.bfloat16
+        self.dt = dt = compute_dtype
         recv_bytes = batch * self.rows * self.hl * dk * 2
         img_bytes = batch * seq_local * heads * dk * 2
         txt_bytes = batch * max(txt_rows, 1) * heads * dk * 2
@@ -289,8 +294,8 @@ class JointUlyssesAttention:
             for x, s in zip(xs, stage):
                 s[..., :self.d].copy_(x)
             return stage
-        return [x if x.device == self.device and x.dtype == torch.bfloat16 and x.stride(3) == 1 else
-                x.to(device=self.device, dtype=torch.bfloat16).contiguous() for x in xs]
+        return [x if x.device == self.device and x.dtype == self.dt and x.stride(3) == 1 else
+                x.to(device=self.device, dtype=self.dt).contiguous() for x in xs]
 
     def forward(self, q_img, k_img, v_img, q_txt, k_txt, v_txt):
         for x in (q_img, k_img, v_img):

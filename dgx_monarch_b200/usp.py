@@ -135,11 +135,11 @@ class B200SequenceParallelAttention:
         plan = self._plans.get(key)
         if plan is None:
             g = self.groups
-            if self.full_context_ring and g.uly_world == 1 and dtype == torch.bfloat16:
+            if self.full_context_ring and g.uly_world == 1:
                 plan = FullContextRingAttention(world=g.ring_world, rank=g.ring_rank, batch=b, q_len=lq,
                                                 kv_len=lk, heads=h, kv_heads=hkv, head_dim=d,
                                                 device=self.device, group=g.ring_group,
-                                                generation=self.generation)
+                                                generation=self.generation, dtype=dtype)
             else:
                 plan = RingAttention(world=g.ring_world, rank=g.ring_rank, batch=b, q_len=lq, kv_len=lk,
                                      heads=h, kv_heads=hkv, head_dim=d, device=self.device,
@@ -488,8 +488,16 @@ def make_b200_usp_attention(*, ulysses_group=None, ring_group=None, generation: 
                                  b, h)
         if sequence_order is not None and ring_world != 1:
             sequence_order = None
-        if q_l.dtype != torch.bfloat16:
-            q_l, k_l, v_l = (t.to(torch.bfloat16) for t in (q_l, k_l, v_l))
+        # The kernels compute in the caller's 16-bit format: fp16 models stay in
+        # fp16 (the reference's flash path takes fp16 and bf16 alike), bf16 in
+        # bf16.  fp32 callers -- and every caller of the e4m3 path, whose
+        # quantiser reads bf16 -- are rounded to bf16; the output returns in
+        # the caller's dtype.
+        compute = q_l.dtype if q_l.dtype in (torch.float16, torch.bfloat16) else torch.bfloat16
+        if impl.fp8:
+            compute = torch.bfloat16
+        if q_l.dtype != compute or k_l.dtype != compute or v_l.dtype != compute:
+            q_l, k_l, v_l = (t.to(compute) for t in (q_l, k_l, v_l))
         if head_dim < KERNEL_HEAD_DIM:
             # Zero columns add exact zeros to every logit and give zero output
             # columns; the scale stays that of the real head dimension.

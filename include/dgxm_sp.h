@@ -86,8 +86,8 @@ typedef struct dgxm_attn_desc {
   int32_t q_heads;
   int32_t kv_heads;   /* q_heads % kv_heads == 0 (grouped-query attention) */
   int32_t head_dim;   /* 128 */
-  int32_t in_dtype;   /* DGXM_DTYPE_BF16 or DGXM_DTYPE_E4M3 */
-  int32_t out_dtype;  /* DGXM_DTYPE_BF16 or DGXM_DTYPE_F32 */
+  int32_t in_dtype;   /* DGXM_DTYPE_BF16, DGXM_DTYPE_F16 or DGXM_DTYPE_E4M3 */
+  int32_t out_dtype;  /* DGXM_DTYPE_F32, or the inputs' 16-bit format (BF16 for E4M3) */
   int64_t q_stride[3];   /* batch, row, head */
   int64_t k_stride[3];
   int64_t v_stride[3];
@@ -181,9 +181,10 @@ int dgxm_attn_fwd_ext(const dgxm_attn_desc* desc, const dgxm_attn_extras* extras
  * Merge n_parts partial attention results over disjoint key blocks:
  *   lse = log(sum_i exp(lse_i)),  out = sum_i exp(lse_i - lse) * out_i
  * in fp32.  parts_out[i] is (batch, rows, heads, head_dim) of part_dtype
- * (BF16 or F32), contiguous; parts_lse[i] is fp32 (batch, heads, rows),
- * contiguous.  out is written in out_dtype (BF16 or F32) with the same
- * layout; lse_out (may be NULL) is fp32 (batch, heads, rows).
+ * (BF16, F16 or F32), contiguous; parts_lse[i] is fp32 (batch, heads, rows),
+ * contiguous.  out is written in out_dtype (F32, or a 16-bit format: any for
+ * F32 parts, the parts' own for 16-bit parts) with the same layout; lse_out
+ * (may be NULL) is fp32 (batch, heads, rows).
  * parts_out / parts_lse are HOST arrays of device pointers, n_parts <= 16.
  *
  * Replaces the ring merge inside xfuser/yunchang's ring flash attention,
@@ -383,7 +384,8 @@ int dgxm_quantize_e4m3_per_head(int32_t batch, int32_t rows, int32_t heads, int3
  * LSE in fp32.  Keys/values and the output must be contiguous (B, L, H, D);
  * lse (may be NULL) is contiguous fp32 (B, H, Lq).  The comm window needs
  * dgxm_ring_window_bytes(desc); `workspace` (scratch owned by the caller,
- * 256-byte aligned) needs dgxm_ring_workspace_bytes(desc, R).  bf16 inputs.
+ * 256-byte aligned) needs dgxm_ring_workspace_bytes(desc, R).  bf16 or f16
+ * inputs.
  *
  * Replaces the ring loop of xfuser/yunchang that adapters/base.py:320 reaches
  * when the ring degree exceeds one (block contract:
@@ -426,7 +428,7 @@ int dgxm_ring_attn_fwd_noalloc(dgxm_comm* comm, const dgxm_attn_desc* desc, cons
  * [rank*L, (rank+1)*L) of every rank's window, then this rank's Q attends the
  * whole (B, R*L) key axis in one call -- exact, no LSE merge.  desc describes
  * the LOCAL shapes (kv_len = L); o and lse are this rank's (B, Lq, H, D) and
- * (B, H, Lq).  bf16 inputs; any ring degree R = comm world <= 8.  The window
+ * (B, H, Lq).  bf16 or f16 inputs; any ring degree R = comm world <= 8.  The window
  * must hold dgxm_full_context_window_bytes(desc, R) (two alternating buffers,
  * so one barrier per call suffices).  Collective: every rank of the comm
  * calls it in the same order with the same shapes.

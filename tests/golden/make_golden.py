@@ -65,6 +65,7 @@ LOCAL_QKV_CASES = [
     {"q": [1, 8, 3, 128], "k": [1, 8, 2, 128], "v": [1, 8, 2, 128], "dtype": "bfloat16"},
     {"q": [1, 0, 2, 128], "k": [1, 0, 2, 128], "v": [1, 0, 2, 128], "dtype": "bfloat16"},
     {"q": [1, 8, 2, 128], "k": [1, 8, 2, 128], "v": [1, 8, 2, 128], "dtype": "float32"},
+    {"q": [1, 8, 2, 128], "k": [1, 8, 2, 128], "v": [1, 8, 2, 128], "dtype": "float16"},
     {"q": [1, 8, 2, 64], "k": [1, 8, 2, 64], "v": [1, 8, 2, 64], "dtype": "bfloat16"},
     {"q": [1, 8, 2, 128], "k": [1, 16, 2, 128], "v": [1, 16, 2, 128], "dtype": "bfloat16"},
 ]

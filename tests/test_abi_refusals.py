@@ -49,7 +49,9 @@ def _status(lib, rc, code, needle):
     ({"q_heads": 3}, 1, "divisible"),
     ({"kv_len": 0}, 1, "empty key axis"),
     ({"q_len": -1}, 1, "negative"),
-    ({"in_dtype": 1}, 2, "input dtype"),
+    ({"in_dtype": 3}, 2, "input dtype"),
+    ({"in_dtype": 1}, 2, "output dtype 0 is not supported for input dtype 1"),
+    ({"in_dtype": 2, "out_dtype": 1}, 2, "output dtype 1"),
     ({"q_len": 0}, 0, ""),
     ({"batch": 0}, 0, ""),
 ])

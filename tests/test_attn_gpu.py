@@ -353,3 +353,76 @@ def test_empty_inputs_return_without_a_launch(lib):
     torch.cuda.synchronize()
     assert recv.abs().max().item() == 0.0
     assert _lib.device_error() == 0
+
+
+# fp16 runs the 16-bit path in its own format (Q, K, V and P in fp16, fp16 or
+# fp32 output): fp16's 10 mantissa bits hold it well inside the bf16 bounds.
+F16_MAX_ABS = 1e-2
+F16_REL_L2 = 2e-3
+
+
+@pytest.mark.parametrize("shape", [(1, 1000, 1000, 4, 4), (2, 300, 77, 3, 1), (1, 513, 2049, 2, 2)])
+def test_fp16_runs_natively_and_matches_fp32_reference(lib, shape):
+    """The reference's flash path takes fp16 models' q/k/v as they are
+    (adapters/wan_ring_full_context.py:10); so does this kernel."""
+    from dgx_monarch_b200.ops import attention_fwd
+
+    b, lq, lk, h, hkv = shape
+    g = torch.Generator(device="cuda").manual_seed(16)
+    q = torch.randn(b, lq, h, 128, device="cuda", generator=g).half()
+    k = torch.randn(b, lk, hkv, 128, device="cuda", generator=g).half()
+    v = torch.randn(b, lk, hkv, 128, device="cuda", generator=g).half()
+    out, lse = attention_fwd(q, k, v)
+    out32, lse32 = attention_fwd(q, k, v, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert out.dtype == torch.float16 and out32.dtype == torch.float32
+    ref, ref_lse = reference_attention(q, k, v)
+    for got in (out, out32):
+        assert (got.float() - ref).abs().max().item() <= F16_MAX_ABS
+        assert rel_l2(got, ref) <= F16_REL_L2
+    assert (lse - ref_lse).abs().max().item() <= LSE_ABS
+    assert (lse - lse32).abs().max().item() <= 1e-5
+    # Computing in fp16 is closer to the fp16 inputs' exact attention than
+    # rounding them to bf16 first would be.
+    via_bf16, _ = attention_fwd(q.bfloat16(), k.bfloat16(), v.bfloat16())
+    assert rel_l2(out, ref) < rel_l2(via_bf16, ref)
+
+
+def test_fp16_extras_and_merge(lib):
+    """fp16 through the extras kernel (pad keep bits) and the LSE merge of
+    fp16 and fp32 parts."""
+    from dgx_monarch_b200.ops import attention_fwd, attention_fwd_ext, keep_bits, lse_merge
+
+    g = torch.Generator(device="cuda").manual_seed(17)
+    rows = 700
+    q, k, v = (torch.randn(1, rows, 3, 128, device="cuda", generator=g).half() for _ in range(3))
+    drop = [0, 127, 128, 699]
+    kk = keep_bits(rows, drop, q.device)
+    out, _ = attention_fwd_ext(q, k, v, key_keep=kk, query_keep=kk)
+    torch.cuda.synchronize()
+    keep = [i for i in range(rows) if i not in drop]
+    ref, _ = reference_attention(q[:, keep], k[:, keep], v[:, keep])
+    assert out.dtype == torch.float16
+    assert rel_l2(out[:, keep], ref) <= F16_REL_L2
+    assert torch.equal(out[:, drop], torch.zeros_like(out[:, drop]))
+    full_ref, full_lse = reference_attention(q, k, v)
+    for part_dtype in (torch.float16, torch.float32):
+        parts = [attention_fwd(q, k[:, i * 350:(i + 1) * 350].contiguous(), v[:, i * 350:(i + 1) * 350].contiguous(),
+                               out_dtype=part_dtype) for i in range(2)]
+        merged, lse = lse_merge([p[0] for p in parts], [p[1] for p in parts], out_dtype=torch.float16)
+        torch.cuda.synchronize()
+        assert merged.dtype == torch.float16
+        assert rel_l2(merged, full_ref) <= F16_REL_L2
+        assert (lse - full_lse).abs().max().item() <= LSE_ABS
+
+
+def test_mixed_16bit_formats_are_refused(lib):
+    from dgx_monarch_b200._lib import DgxmError
+    from dgx_monarch_b200.ops import attention_fwd, lse_merge
+
+    q = torch.randn(1, 64, 2, 128, device="cuda").half()
+    with pytest.raises(DgxmError, match="output dtype"):
+        attention_fwd(q, q, q, out_dtype=torch.bfloat16)
+    parts = [torch.zeros(1, 64, 2, 128, device="cuda", dtype=torch.float16)]
+    with pytest.raises(DgxmError, match="f16 parts into a bf16"):
+        lse_merge(parts, [torch.zeros(1, 2, 64, device="cuda")], out_dtype=torch.bfloat16)

@@ -2,9 +2,7 @@
 reference's own verdicts (adapters/wan_ring_full_context.py:17-117) recorded
 in tests/golden/ by make_golden.py section (l): every kernel option and local
 shard case is accepted or refused exactly as the reference does, with the
-reference's message.  One deliberate difference: the reference also takes
-fp16 shards, this kernel runs bf16 and refuses other dtypes with its own
-message."""
+reference's message, fp16 and bf16 shards alike."""
 from __future__ import annotations
 
 import json
@@ -55,11 +53,7 @@ def test_local_shards_are_judged_as_the_reference_judges_them(entry):
     q, k, v = (torch.zeros(case[n], dtype=dt) for n in "qkv")
     if case.get("grad"):
         q.requires_grad_(True)
-    got = _verdict(validate_local_qkv, q=q, k=k, v=v)
-    if "FP16/BF16" in entry["verdict"]:
-        assert got != "ok" and "bf16" in got
-    else:
-        assert got == entry["verdict"]
+    assert _verdict(validate_local_qkv, q=q, k=k, v=v) == entry["verdict"]
 
 
 def test_the_cases_cover_every_refusal():

@@ -269,7 +269,7 @@ def test_replicated_text_joint_emulated_ranks(lib, world, batch, image_local, te
     (64, torch.float32, False),
     (96, torch.float16, True),
     (128, torch.bfloat16, True)])
-def test_joint_ulysses_class_one_rank(lib, head_dim, dtype, text_first):
+def test_joint_ulysses_class_one_rank(lib, head_dim, dtype, text_first, record_property):
     """JointUlyssesAttention on one rank: any float dtype in and out (bf16
     compute), head_dim below 128 zero-padded with the softmax scale of the real
     head_dim; 1024 image + 256 text rows, 8 heads."""
@@ -289,12 +289,17 @@ def test_joint_ulysses_class_one_rank(lib, head_dim, dtype, text_first):
     assert out_img.dtype == dtype and out_txt.dtype == dtype
     assert out_img.shape == (1, 1024, 8, head_dim) and out_txt.shape == (1, 256, 8, head_dim)
     assert torch.equal(out_img, again_img) and torch.equal(out_txt, again_txt)
-    q, k, v = (torch.cat([a, b] if text_first else [b, a], dim=1).bfloat16() for a, b in zip(txt, img))
+    # Held against fp32 attention over the caller's own (unrounded) inputs:
+    # the bf16 compute, the rounding of fp32 inputs to it included, stays
+    # within the bf16 bounds.
+    q, k, v = (torch.cat([a, b] if text_first else [b, a], dim=1).float() for a, b in zip(txt, img))
     ref, _ = reference_attention(q, k, v)
     ref_txt, ref_img = (ref[:, :256], ref[:, 256:]) if text_first else (ref[:, 1024:], ref[:, :1024])
     for got, want in ((out_img, ref_img), (out_txt, ref_txt)):
         assert (got.float() - want).abs().max().item() <= BF16_MAX_ABS
         assert rel_l2(got, want) <= BF16_REL_L2
+    record_property("rel_l2_vs_fp32_of_unrounded_inputs",
+                    max(rel_l2(out_img, ref_img), rel_l2(out_txt, ref_txt)))
 
 
 def test_joint_ulysses_without_text_is_plain_attention(lib):
