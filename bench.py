@@ -53,11 +53,9 @@ def parse_args():
     p.add_argument("--e2e-groups", type=int, default=5,
                    help="head groups the host-streamed e2e step pipelines (must divide the "
                         "40 heads, with a multiple of the GPU count per group)")
-    p.add_argument("--pingpong", action="store_true",
-                   help="the two query tiles' exponential loops take turns (bf16 kernel)")
-    p.add_argument("--p-chunks", type=int, choices=[0, 1, 2, 4], default=0,
+    p.add_argument("--p-chunks", type=int, choices=[0, 1, 4], default=0,
                    help="release each block's probabilities to the tensor core in this many "
-                        "chunks (0: the library default)")
+                        "chunks (0: the library default, 4; 1: the single release)")
     p.add_argument("--profile-case", choices=["attn", "fp8", "f16", "kernels"], default=None,
                    help="instead of the bench: a few launches of one kernel family on one GPU, "
                         "sized for a profiler capture (attn / fp8 / f16: three attention launches "
@@ -76,10 +74,9 @@ def run_profile_case(args) -> None:
     launch ends in a minute or two."""
     import torch
 
-    from dgx_monarch_b200.ops import attention_fwd, set_p_chunks, set_pingpong
+    from dgx_monarch_b200.ops import attention_fwd, set_p_chunks
 
     set_p_chunks(args.p_chunks)
-    set_pingpong(args.pingpong)
     dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev).manual_seed(0)
     shape = (args.case_batch, args.case_seq, args.case_heads, DIM)
@@ -613,11 +610,10 @@ def main() -> None:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    if args.p_chunks or args.pingpong:
-        from dgx_monarch_b200.ops import set_p_chunks, set_pingpong
+    if args.p_chunks:
+        from dgx_monarch_b200.ops import set_p_chunks
 
         set_p_chunks(args.p_chunks)
-        set_pingpong(args.pingpong)
     if world > 1:
         from datetime import timedelta
 
@@ -773,8 +769,7 @@ def main() -> None:
             "config": {"workload": WORKLOAD, "seq_len": SEQ, "heads": HEADS, "head_dim": DIM,
                        "batch": BATCH, "parallelism": f"ulysses{world}",
                        "l2": "inputs larger than L2 (Q/K/V 2.3 GB)",
-                       "p_chunks": args.p_chunks or "library default (1)",
-                       "softmax_schedule": "ping-pong" if args.pingpong else "default"},
+                       "p_chunks": args.p_chunks or "library default (4)"},
             "tokens_per_s": BATCH * SEQ / (ms * 1e-3),
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
                          "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],

@@ -26,7 +26,6 @@ DTYPE_F32 = 3
 
 ATTN_SAFE_ORDER = 1
 ATTN_P_CHUNKS_SHIFT = 4  # DGXM_ATTN_P_CHUNKS(n) = n << 4
-ATTN_PINGPONG = 1 << 8
 
 
 class DgxmError(RuntimeError):
@@ -203,6 +202,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "dgxm_copy_2d": (ctypes.c_int, [_P, ctypes.c_int64, _P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _P]),
     "dgxm_cfg_combine": (ctypes.c_int, [_P, _P, ctypes.c_int64, _I32, ctypes.c_double, _P, _P]),
     "dgxm_seq_allgather": (ctypes.c_int, [_P, ctypes.POINTER(SeqGatherDesc), _P, ctypes.c_int64, _P]),
+    "dgxm_seq_gather_store": (ctypes.c_int, [ctypes.POINTER(SeqGatherDesc), _I32, _I32, _P,
+                                             ctypes.POINTER(_P), _P]),
+    "dgxm_kv_gather_store": (ctypes.c_int, [ctypes.POINTER(AttnDesc), _I32, _I32, _P, _P,
+                                            ctypes.POINTER(_P), ctypes.POINTER(_P), _P]),
     "dgxm_shared_amax_scale": (ctypes.c_int, [_P, _P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                               _I32, ctypes.c_float, _P, _P, _P]),
     "dgxm_full_context_attn_fwd": (ctypes.c_int, [_P, ctypes.POINTER(AttnDesc), _P, _P, _P, _P, _P,

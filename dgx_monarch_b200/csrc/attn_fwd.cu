@@ -56,7 +56,7 @@
 // rest is still in the exponential loop: the softmax -> P.V dependency that
 // bounds the block time shrinks by the later chunks' share of the loop.
 #ifndef DGXM_SM_P_CHUNKS
-#define DGXM_SM_P_CHUNKS 1
+#define DGXM_SM_P_CHUNKS 4
 #endif
 
 namespace dgxm {
@@ -150,7 +150,7 @@ struct __align__(64) AttnParams {
 };
 
 // Barrier slots inside the control block.
-template <int kStages, int kPChunks, bool kPingPong = false>
+template <int kStages, int kPChunks>
 struct Bars {
   static constexpr int kQ = 0;
   static constexpr int kKvFull = 1;
@@ -160,8 +160,7 @@ struct Bars {
   static constexpr int kOFull = kPFull + 2 * kPChunks;  // 2
   static constexpr int kPvDone = kOFull + 2;         // 2
   static constexpr int kDrain = kPvDone + 2;
-  static constexpr int kTurn = kDrain + 1;                  // 2: ping-pong tokens, one per tile
-  static constexpr int kCount = kTurn + (kPingPong ? 2 : 0);
+  static constexpr int kCount = kDrain + 1;
 };
 
 // Shared-memory descriptors split into a low word (start address in 16-byte
@@ -273,11 +272,11 @@ __device__ __forceinline__ void raise_abort(volatile int* abort_flag, int bits) 
 
 // F16: 16-bit inputs (and P) are fp16 instead of bf16; a 16-bit output is
 // then fp16 too.
-template <bool FP8, bool OUT_F32, bool EXTRA, int NCH, bool PP, bool F16>
+template <bool FP8, bool OUT_F32, bool EXTRA, int NCH, bool F16>
 __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_constant__ AttnParams p) {
   using C = AttnCfg<FP8, F16>;
   constexpr int kPChunks = p_chunks<FP8, NCH>();
-  using B = Bars<C::kStages, kPChunks, PP>;
+  using B = Bars<C::kStages, kPChunks>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -306,10 +305,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
       mbar_init(bar(B::kPvDone + t), 1);
     }
     mbar_init(bar(B::kDrain), 1);
-    if constexpr (PP) {
-      mbar_init(bar(B::kTurn + 0), 256);
-      mbar_init(bar(B::kTurn + 1), 256);
-    }
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -601,18 +596,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
       // p = 2^(s * sl2 - m) (times kPScale for e4m3, folded into the exponent).
       // A row whose keys so far were all excluded keeps m = -inf and p = 0.
       const float bias = -(EXTRA && m_run == -INFINITY ? 0.f : m_run) + C::kPScaleLog2;
-      if constexpr (PP) {
-        // Ping-pong: the two tiles' exponential loops take turns -- tile 1's
-        // loop of block j follows tile 0's, tile 0's loop of block j + 1
-        // follows tile 1's of block j -- so neither shares the MUFU with the
-        // other.  A wait that gives up raises the abort flag and the group
-        // stops together at its next exchange barrier.
-        if (t == 1 || j > 0) {
-          const int parity = t == 1 ? (j & 1) : ((j - 1) & 1);
-          if (!__all_sync(0xffffffffu, mbar_wait(bar(B::kTurn + (t ^ 1)), parity, abort_flag)))
-            raise_abort(abort_flag, kErrSoftmaxTimeout);
-        }
-      }
       if constexpr (kPChunks > 1) {
         const uint64_t sl2x2 = pk2(sl2, sl2), biasx2 = pk2(bias, bias);
         uint64_t sum_a = pk2(0.f, 0.f), sum_b = pk2(0.f, 0.f);
@@ -641,9 +624,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
             } else {
               pk[q] = pack16<F16>(p0, p1);
             }
-          }
-          if constexpr (PP) {
-            if (ch == kPChunks - 1) mbar_arrive(bar(B::kTurn + t));  // the other tile's turn
           }
           if constexpr (FP8) {
             // 2 kPairs keys of this chunk, four per column.
@@ -707,7 +687,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
             pk[i] = pack16<F16>(p0, p1);
           }
         }
-        if constexpr (PP) mbar_arrive(bar(B::kTurn + t));  // the other tile's turn
         {
           float a0, a1, b0, b1;
           upk2(sum_a, a0, a1);
@@ -865,11 +844,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
   }
 }
 
-template <bool FP8, bool OUT_F32, bool EXTRA, int NCH, bool PP = false, bool F16 = false>
+template <bool FP8, bool OUT_F32, bool EXTRA, int NCH, bool F16 = false>
 static int launch_attn(const AttnParams& prm, dim3 grid, cudaStream_t stream) {
   using C = AttnCfg<FP8, F16>;
   static std::atomic<uint64_t> configured{0};  // one bit per device ordinal
-  auto kern = attn_fwd_kernel<FP8, OUT_F32, EXTRA, NCH, PP, F16>;
+  auto kern = attn_fwd_kernel<FP8, OUT_F32, EXTRA, NCH, F16>;
   DGXM_CUDA_TRY(set_smem_limit_once(kern, C::kSmemBytes, configured));
   kern<<<grid, kAttnThreads, C::kSmemBytes, stream>>>(prm);
   DGXM_CUDA_TRY(cudaGetLastError());
@@ -968,6 +947,8 @@ static int prepare_attn(const dgxm_attn_desc* d, const void* q, const void* k, c
   return DGXM_OK;
 }
 
+// Instantiations: bf16 inputs release P in 4 chunks (the default) or 1; e4m3
+// in 2 (4 runs as 2) or 1; fp16 runs the default.  2 chunks select 4 for bf16.
 template <bool EXTRA, int NCH>
 static int dispatch_attn_n(const dgxm_attn_desc* d, const AttnParams& prm, dim3 grid, cudaStream_t st) {
   const bool fp8 = d->in_dtype == DGXM_DTYPE_E4M3;
@@ -982,40 +963,17 @@ static int dispatch_attn_n(const dgxm_attn_desc* d, const AttnParams& prm, dim3 
 
 template <bool EXTRA>
 static int dispatch_attn_t(const dgxm_attn_desc* d, const AttnParams& prm, dim3 grid, cudaStream_t st) {
-  if (d->in_dtype == DGXM_DTYPE_F16) {
-    // fp16 inputs run the library's default schedule; the chunk and ping-pong
-    // flags select among the bf16 and e4m3 instantiations only.
-    if (d->out_dtype == DGXM_DTYPE_F32)
-      return launch_attn<false, true, EXTRA, DGXM_SM_P_CHUNKS, false, true>(prm, grid, st);
-    return launch_attn<false, false, EXTRA, DGXM_SM_P_CHUNKS, false, true>(prm, grid, st);
-  }
   int nch = (d->flags & DGXM_ATTN_P_CHUNKS_MASK) >> DGXM_ATTN_P_CHUNKS_SHIFT;
-  if (nch == 0) nch = DGXM_SM_P_CHUNKS;
-  // The ping-pong schedule is built for bf16 output without extras (bf16 or
-  // e4m3 input); the other instantiations run their usual schedule.
-  const bool pp = (d->flags & DGXM_ATTN_PINGPONG) != 0 && !EXTRA && d->out_dtype == DGXM_DTYPE_BF16;
-  if (pp && d->in_dtype == DGXM_DTYPE_E4M3) {
-    switch (nch) {
-      case 1: return launch_attn<true, false, false, 1, true>(prm, grid, st);
-      case 2:
-      case 4: return launch_attn<true, false, false, 2, true>(prm, grid, st);  // e4m3 runs 4 as 2
-      default: return fail(DGXM_ERR_INVALID, "%d P chunks per block (1, 2 or 4)", nch);
-    }
+  if (nch != 0 && nch != 1 && nch != 2 && nch != 4)
+    return fail(DGXM_ERR_INVALID, "%d P chunks per block (1, 2 or 4)", nch);
+  if (d->in_dtype == DGXM_DTYPE_F16) {
+    // fp16 inputs run the library's default release of P.
+    if (d->out_dtype == DGXM_DTYPE_F32)
+      return launch_attn<false, true, EXTRA, DGXM_SM_P_CHUNKS, true>(prm, grid, st);
+    return launch_attn<false, false, EXTRA, DGXM_SM_P_CHUNKS, true>(prm, grid, st);
   }
-  if (pp) {
-    switch (nch) {
-      case 1: return launch_attn<false, false, false, 1, true>(prm, grid, st);
-      case 2: return launch_attn<false, false, false, 2, true>(prm, grid, st);
-      case 4: return launch_attn<false, false, false, 4, true>(prm, grid, st);
-      default: return fail(DGXM_ERR_INVALID, "%d P chunks per block (1, 2 or 4)", nch);
-    }
-  }
-  switch (nch) {
-    case 1: return dispatch_attn_n<EXTRA, 1>(d, prm, grid, st);
-    case 2: return dispatch_attn_n<EXTRA, 2>(d, prm, grid, st);
-    case 4: return dispatch_attn_n<EXTRA, 4>(d, prm, grid, st);
-    default: return fail(DGXM_ERR_INVALID, "%d P chunks per block (1, 2 or 4)", nch);
-  }
+  if (nch == 1) return dispatch_attn_n<EXTRA, 1>(d, prm, grid, st);
+  return dispatch_attn_n<EXTRA, DGXM_SM_P_CHUNKS>(d, prm, grid, st);
 }
 
 static int dispatch_attn(const dgxm_attn_desc* d, const AttnParams& prm, dim3 grid, void* stream) {

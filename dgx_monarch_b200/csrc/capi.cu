@@ -72,7 +72,7 @@ int encode_map_4d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, in
 
 }  // namespace dgxm
 
-extern "C" int dgxm_abi_version(void) { return 1; }
+extern "C" int dgxm_abi_version(void) { return 2; }
 
 extern "C" const char* dgxm_last_error_message(void) { return dgxm::g_msg; }
 

@@ -69,13 +69,10 @@ extern "C" int64_t dgxm_full_context_window_bytes(const dgxm_attn_desc* d, int32
   return 4 * dgxm::round256(dgxm::full_kv_bytes(d, world));
 }
 
-extern "C" int dgxm_full_context_attn_fwd(dgxm_comm* c, const dgxm_attn_desc* d, const void* q,
-                                          const void* k, const void* v, void* o, float* lse,
-                                          void* stream) {
-  using namespace dgxm;
-  if (c == nullptr || d == nullptr) return fail(DGXM_ERR_INVALID, "NULL comm or descriptor");
-  const int world = c->world;
-  if (world == 1) return dgxm_attn_fwd(d, q, k, v, nullptr, nullptr, nullptr, o, lse, stream);
+namespace dgxm {
+
+// Checks of the local K/V blocks the gather reads (16-bit elements).
+static int check_kv_block(const dgxm_attn_desc* d, const void* k, const void* v) {
   if (d->in_dtype != DGXM_DTYPE_BF16 && d->in_dtype != DGXM_DTYPE_F16)
     return fail(DGXM_ERR_UNSUPPORTED, "full-context ring attention runs bf16 or f16 inputs");
   if (d->head_dim != kHeadDim)
@@ -85,7 +82,6 @@ extern "C" int dgxm_full_context_attn_fwd(dgxm_comm* c, const dgxm_attn_desc* d,
     return fail(DGXM_ERR_INVALID, "empty key/value block (batch=%d kv_len=%d kv_heads=%d)",
                 d->batch, d->kv_len, d->kv_heads);
   if (k == nullptr || v == nullptr) return fail(DGXM_ERR_INVALID, "k and v must be non-NULL");
-  const int head_bytes = d->head_dim * 2;
   const void* kv[2] = {k, v};
   const int64_t* strides[2] = {d->k_stride, d->v_stride};
   for (int t = 0; t < 2; ++t) {
@@ -95,6 +91,67 @@ extern "C" int dgxm_full_context_attn_fwd(dgxm_comm* c, const dgxm_attn_desc* d,
       if ((strides[t][s] * 2) % 16)
         return fail(DGXM_ERR_INVALID, "%s strides must be multiples of 16 bytes", t ? "v" : "k");
   }
+  return DGXM_OK;
+}
+
+// This rank's K and V blocks into rank-major slots of every rank's full K/V.
+static int launch_kv_gather(const dgxm_attn_desc* d, int world, int rank, const void* k,
+                            const void* v, char* const* dst_k, char* const* dst_v, cudaStream_t st) {
+  const void* kv[2] = {k, v};
+  const int64_t* strides[2] = {d->k_stride, d->v_stride};
+  char* const* dst[2] = {dst_k, dst_v};
+  KvGatherParams p;
+  memset(&p, 0, sizeof(p));
+  for (int t = 0; t < 2; ++t) {
+    p.src[t] = static_cast<const char*>(kv[t]);
+    p.s_sb[t] = strides[t][0] * 2;
+    p.s_sl[t] = strides[t][1] * 2;
+    p.s_sh[t] = strides[t][2] * 2;
+    for (int r = 0; r < world; ++r) p.dst[t][r] = dst[t][r];
+  }
+  p.world = world;
+  p.rank = rank;
+  p.batch = d->batch;
+  p.seq_local = d->kv_len;
+  p.heads = d->kv_heads;
+  p.head_bytes = d->head_dim * 2;
+  const int64_t items = 2 * static_cast<int64_t>(d->batch) * d->kv_len * d->kv_heads * (p.head_bytes / 16);
+  kv_allgather_kernel<<<grid_for(items, 256), 256, 0, st>>>(p);
+  DGXM_CUDA_TRY(cudaGetLastError());
+  return DGXM_OK;
+}
+
+}  // namespace dgxm
+
+extern "C" int dgxm_kv_gather_store(const dgxm_attn_desc* d, int32_t world, int32_t rank,
+                                    const void* k, const void* v, void* const* dst_k,
+                                    void* const* dst_v, void* stream) {
+  using namespace dgxm;
+  if (d == nullptr) return fail(DGXM_ERR_INVALID, "NULL descriptor");
+  if (world < 1 || world > DGXM_MAX_WORLD || rank < 0 || rank >= world)
+    return fail(DGXM_ERR_INVALID, "rank %d / world %d out of range", rank, world);
+  if (int rc = check_kv_block(d, k, v)) return rc;
+  if (dst_k == nullptr || dst_v == nullptr) return fail(DGXM_ERR_INVALID, "destination arrays are NULL");
+  char* bk[DGXM_MAX_WORLD];
+  char* bv[DGXM_MAX_WORLD];
+  for (int r = 0; r < world; ++r) {
+    if (dst_k[r] == nullptr || dst_v[r] == nullptr || reinterpret_cast<uintptr_t>(dst_k[r]) % 16 ||
+        reinterpret_cast<uintptr_t>(dst_v[r]) % 16)
+      return fail(DGXM_ERR_INVALID, "destination %d is NULL or not 16-byte aligned", r);
+    bk[r] = static_cast<char*>(dst_k[r]);
+    bv[r] = static_cast<char*>(dst_v[r]);
+  }
+  return launch_kv_gather(d, world, rank, k, v, bk, bv, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int dgxm_full_context_attn_fwd(dgxm_comm* c, const dgxm_attn_desc* d, const void* q,
+                                          const void* k, const void* v, void* o, float* lse,
+                                          void* stream) {
+  using namespace dgxm;
+  if (c == nullptr || d == nullptr) return fail(DGXM_ERR_INVALID, "NULL comm or descriptor");
+  const int world = c->world;
+  if (world == 1) return dgxm_attn_fwd(d, q, k, v, nullptr, nullptr, nullptr, o, lse, stream);
+  if (int rc = check_kv_block(d, k, v)) return rc;
   const int64_t full = full_kv_bytes(d, world);
   const int64_t slot = round256(full);
   if (4 * slot > c->bytes)
@@ -104,25 +161,14 @@ extern "C" int dgxm_full_context_attn_fwd(dgxm_comm* c, const dgxm_attn_desc* d,
     if (c->peers[r] == nullptr) return fail(DGXM_ERR_STATE, "peer %d window is not mapped", r);
 
   const int buf = static_cast<int>(c->fc_calls & 1u);
-  KvGatherParams p;
-  memset(&p, 0, sizeof(p));
-  for (int t = 0; t < 2; ++t) {
-    p.src[t] = static_cast<const char*>(kv[t]);
-    p.s_sb[t] = strides[t][0] * 2;
-    p.s_sl[t] = strides[t][1] * 2;
-    p.s_sh[t] = strides[t][2] * 2;
-    for (int r = 0; r < world; ++r) p.dst[t][r] = c->peers[r] + kFlagBytes + (2 * buf + t) * slot;
+  char* bk[DGXM_MAX_WORLD];
+  char* bv[DGXM_MAX_WORLD];
+  for (int r = 0; r < world; ++r) {
+    bk[r] = c->peers[r] + kFlagBytes + (2 * buf) * slot;
+    bv[r] = c->peers[r] + kFlagBytes + (2 * buf + 1) * slot;
   }
-  p.world = world;
-  p.rank = c->rank;
-  p.batch = d->batch;
-  p.seq_local = d->kv_len;
-  p.heads = d->kv_heads;
-  p.head_bytes = head_bytes;
-  const int64_t items = 2 * static_cast<int64_t>(d->batch) * d->kv_len * d->kv_heads * (head_bytes / 16);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  kv_allgather_kernel<<<grid_for(items, 256), 256, 0, st>>>(p);
-  DGXM_CUDA_TRY(cudaGetLastError());
+  if (int rc = launch_kv_gather(d, world, c->rank, k, v, bk, bv, st)) return rc;
   c->fc_calls += 1;
   int rc = dgxm_comm_barrier(c, stream);
   if (rc) return rc;

@@ -190,18 +190,66 @@ __global__ void amax_exchange_kernel(const __grid_constant__ AmaxExchangeParams 
 
 }  // namespace dgxm
 
-extern "C" int dgxm_seq_allgather(dgxm_comm* c, const dgxm_seq_gather_desc* d, const void* src,
-                                  int64_t window_offset, void* stream) {
-  using namespace dgxm;
-  if (c == nullptr || d == nullptr || src == nullptr)
-    return fail(DGXM_ERR_INVALID, "NULL comm, descriptor or source");
+namespace dgxm {
+
+// Checks shared by the collective and the store-only entry: 16-byte units.
+static int check_seq_gather(const dgxm_seq_gather_desc* d, int world, const void* src) {
+  if (d == nullptr || src == nullptr) return fail(DGXM_ERR_INVALID, "NULL descriptor or source");
   if (d->batch < 0 || d->seq_local < 0 || d->orig_len < 0 ||
-      static_cast<int64_t>(d->seq_local) * c->world < d->orig_len)
-    return fail(DGXM_ERR_INVALID, "orig_len %d exceeds %d ranks x %d local rows", d->orig_len,
-                c->world, d->seq_local);
+      static_cast<int64_t>(d->seq_local) * world < d->orig_len)
+    return fail(DGXM_ERR_INVALID, "orig_len %d exceeds %d ranks x %d local rows", d->orig_len, world,
+                d->seq_local);
   if (d->row_bytes <= 0 || d->row_bytes % 16 || d->src_batch_stride % 16 || d->src_row_stride % 16 ||
       reinterpret_cast<uintptr_t>(src) % 16)
     return fail(DGXM_ERR_INVALID, "rows, strides and the source must be 16-byte aligned");
+  return DGXM_OK;
+}
+
+// This rank's rows into every rank's trimmed (B, orig_len, row) buffer.
+static int launch_seq_gather(const dgxm_seq_gather_desc* d, int world, int rank, const void* src,
+                             char* const* dst, cudaStream_t st) {
+  if (d->batch == 0 || d->seq_local == 0) return DGXM_OK;
+  SeqGatherParams p;
+  memset(&p, 0, sizeof(p));
+  p.src = static_cast<const char*>(src);
+  p.s_sb = d->src_batch_stride;
+  p.s_sl = d->src_row_stride;
+  for (int r = 0; r < world; ++r) p.dst[r] = dst[r];
+  p.world = world;
+  p.rank = rank;
+  p.batch = d->batch;
+  p.seq_local = d->seq_local;
+  p.orig_len = d->orig_len;
+  p.row_bytes = d->row_bytes;
+  const int64_t items = static_cast<int64_t>(d->batch) * d->seq_local * (d->row_bytes / 16);
+  seq_allgather_kernel<<<grid_for(items, 256), 256, 0, st>>>(p);
+  DGXM_CUDA_TRY(cudaGetLastError());
+  return DGXM_OK;
+}
+
+}  // namespace dgxm
+
+extern "C" int dgxm_seq_gather_store(const dgxm_seq_gather_desc* d, int32_t world, int32_t rank,
+                                     const void* src, void* const* dst, void* stream) {
+  using namespace dgxm;
+  if (world < 1 || world > DGXM_MAX_WORLD || rank < 0 || rank >= world)
+    return fail(DGXM_ERR_INVALID, "rank %d / world %d out of range", rank, world);
+  if (int rc = check_seq_gather(d, world, src)) return rc;
+  if (dst == nullptr) return fail(DGXM_ERR_INVALID, "destination array is NULL");
+  char* bases[DGXM_MAX_WORLD];
+  for (int r = 0; r < world; ++r) {
+    if (dst[r] == nullptr || reinterpret_cast<uintptr_t>(dst[r]) % 16)
+      return fail(DGXM_ERR_INVALID, "destination %d is NULL or not 16-byte aligned", r);
+    bases[r] = static_cast<char*>(dst[r]);
+  }
+  return launch_seq_gather(d, world, rank, src, bases, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int dgxm_seq_allgather(dgxm_comm* c, const dgxm_seq_gather_desc* d, const void* src,
+                                  int64_t window_offset, void* stream) {
+  using namespace dgxm;
+  if (c == nullptr) return fail(DGXM_ERR_INVALID, "NULL comm");
+  if (int rc = check_seq_gather(d, c->world, src)) return rc;
   if (window_offset < 0 || window_offset % 16)
     return fail(DGXM_ERR_INVALID, "window offset %lld is negative or not 16-byte aligned",
                 (long long)window_offset);
@@ -209,25 +257,13 @@ extern "C" int dgxm_seq_allgather(dgxm_comm* c, const dgxm_seq_gather_desc* d, c
   if (window_offset + need > c->bytes)
     return fail(DGXM_ERR_INVALID, "gather of %lld bytes at offset %lld overflows the %lld-byte window",
                 (long long)need, (long long)window_offset, (long long)c->bytes);
-  for (int r = 0; r < c->world; ++r)
+  char* bases[DGXM_MAX_WORLD];
+  for (int r = 0; r < c->world; ++r) {
     if (c->peers[r] == nullptr) return fail(DGXM_ERR_STATE, "peer %d window is not mapped", r);
-  if (d->batch > 0 && d->seq_local > 0) {
-    SeqGatherParams p;
-    memset(&p, 0, sizeof(p));
-    p.src = static_cast<const char*>(src);
-    p.s_sb = d->src_batch_stride;
-    p.s_sl = d->src_row_stride;
-    for (int r = 0; r < c->world; ++r) p.dst[r] = c->peers[r] + kFlagBytes + window_offset;
-    p.world = c->world;
-    p.rank = c->rank;
-    p.batch = d->batch;
-    p.seq_local = d->seq_local;
-    p.orig_len = d->orig_len;
-    p.row_bytes = d->row_bytes;
-    const int64_t items = static_cast<int64_t>(d->batch) * d->seq_local * (d->row_bytes / 16);
-    seq_allgather_kernel<<<grid_for(items, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
-    DGXM_CUDA_TRY(cudaGetLastError());
+    bases[r] = c->peers[r] + kFlagBytes + window_offset;
   }
+  if (int rc = launch_seq_gather(d, c->world, c->rank, src, bases, static_cast<cudaStream_t>(stream)))
+    return rc;
   return dgxm_comm_barrier(c, stream);
 }
 

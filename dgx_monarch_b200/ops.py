@@ -93,29 +93,18 @@ _P_CHUNKS = 0  # 0: the library's default release of P per 128-key block
 
 def set_p_chunks(chunks: int) -> None:
     """Release each block's probabilities to the tensor core in `chunks` parts
-    (1, 2 or 4; 0 restores the library default) in every attention call this
-    process makes from now on (DGXM_ATTN_P_CHUNKS)."""
+    in every attention call this process makes from now on
+    (DGXM_ATTN_P_CHUNKS): 1 is the single release, kept as a cross-check; 0,
+    2 and 4 select the library default (4 chunks; 2 for e4m3 inputs)."""
     global _P_CHUNKS
     if chunks not in (0, 1, 2, 4):
         raise ValueError(f"P is released in 1, 2 or 4 chunks, not {chunks}")
     _P_CHUNKS = chunks
 
 
-_PINGPONG = False
-
-
-def set_pingpong(on: bool) -> None:
-    """Let the two query tiles' exponential loops take turns in every later
-    attention call with bf16 output and no extras (DGXM_ATTN_PINGPONG); same
-    results."""
-    global _PINGPONG
-    _PINGPONG = bool(on)
-
-
 def attn_flags(safe_order: bool = False) -> int:
     """The descriptor flags of one attention call."""
-    return ((_lib.ATTN_SAFE_ORDER if safe_order else 0) | (_P_CHUNKS << _lib.ATTN_P_CHUNKS_SHIFT)
-            | (_lib.ATTN_PINGPONG if _PINGPONG else 0))
+    return (_lib.ATTN_SAFE_ORDER if safe_order else 0) | (_P_CHUNKS << _lib.ATTN_P_CHUNKS_SHIFT)
 
 
 def attn_desc(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor,

@@ -68,6 +68,24 @@ class RingAttention:
             self.windows = None
 
 
+def kv_gather_store(k: torch.Tensor, v: torch.Tensor, dst_k: list[int], dst_v: list[int], *,
+                    world: int, rank: int, stream=None) -> None:
+    """The store half of the full-context gather (dgxm_kv_gather_store): this
+    rank's (B, L, H_kv, 128) K and V blocks (16-bit, any 16-byte strides) go
+    into rows [rank * L, (rank + 1) * L) of every rank's contiguous
+    (B, world * L, H_kv, 128) full K / V at dst_k[r] / dst_v[r]; no barrier."""
+    _require_on(k.device, k, v)
+    if k.shape != v.shape or k.dtype != v.dtype or k.ndim != 4:
+        raise ValueError("k and v are equal (B, L, H_kv, D) blocks of one dtype")
+    if len(dst_k) != world or len(dst_v) != world:
+        raise ValueError(f"destinations for {world} ranks expected")
+    desc = attn_desc(k, k, v, k, None)
+    stream = stream or torch.cuda.current_stream(k.device)
+    _lib.check(_lib.load().dgxm_kv_gather_store(
+        ctypes.byref(desc), world, rank, k.data_ptr(), v.data_ptr(), (ctypes.c_void_p * world)(*dst_k),
+        (ctypes.c_void_p * world)(*dst_v), stream.cuda_stream), "dgxm_kv_gather_store")
+
+
 class FullContextRingAttention:
     """Local Q against the whole K/V axis of a ring group, in one kernel call
     (libdgxm_sp.so: dgxm_full_context_attn_fwd).

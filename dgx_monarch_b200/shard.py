@@ -110,6 +110,29 @@ def _windows_for(cache: dict, nbytes: int, device, group, generation) -> PeerWin
     return win
 
 
+def seq_gather_store(src: torch.Tensor, orig_len: int, dst_ptrs: list[int], *, world: int,
+                     rank: int, stream=None) -> None:
+    """The store half of sp_gather (dgxm_seq_gather_store): this rank's rows of
+    a contiguous (B, L, row) tensor whose rows are whole 16-byte units go into
+    rank r's trimmed (B, orig_len, row) buffer at dst_ptrs[r], gathered rows
+    [rank * L, (rank + 1) * L) below orig_len; no barrier."""
+    _require_on(src.device, src)
+    if src.ndim != 3 or not src.is_contiguous():
+        raise ValueError("the gather source is a contiguous (B, L, row) tensor")
+    if len(dst_ptrs) != world:
+        raise ValueError(f"{len(dst_ptrs)} destinations for {world} ranks")
+    b, seq_local, row = src.shape
+    row_bytes = row * src.element_size()
+    desc = _lib.SeqGatherDesc()
+    desc.batch, desc.seq_local, desc.orig_len, desc.row_bytes = b, seq_local, orig_len, row_bytes
+    desc.src_batch_stride = seq_local * row_bytes
+    desc.src_row_stride = row_bytes
+    dst = (ctypes.c_void_p * world)(*dst_ptrs)
+    stream = stream or torch.cuda.current_stream(src.device)
+    _lib.check(_lib.load().dgxm_seq_gather_store(ctypes.byref(desc), world, rank, src.data_ptr(), dst,
+                                                 stream.cuda_stream), "dgxm_seq_gather_store")
+
+
 class SequenceGather:
     """`sp_gather(t, orig_len, dim)` over NVLink for one sequence group.
 

@@ -41,19 +41,15 @@ extern "C" {
 /* Drain each P.V product before the next Q.K^T product reuses its tensor
  * memory columns (slower; kept as a cross-check of the fast ordering). */
 #define DGXM_ATTN_SAFE_ORDER 1
-/* Release the probabilities of each 128-key block to the tensor core in 1, 2
- * or 4 chunks (e4m3: 4 runs as 2), so P.V starts on the first chunk while the
- * softmax computes the rest.  0 keeps the library's default.  Results agree
- * within the attention tolerance across chunk counts (the P.V steps
- * accumulate in another order). */
+/* Release the probabilities of each 128-key block to the tensor core in
+ * chunks, so P.V starts on the first chunk while the softmax computes the
+ * rest: 0 keeps the library default (4 chunks; 2 for e4m3 inputs, whose
+ * 32-key MMA steps allow no more), as do 2 and 4; 1 releases the whole block
+ * at once (a cross-check).  Results agree within the attention tolerance
+ * across chunk counts (the P.V steps accumulate in another order). */
 #define DGXM_ATTN_P_CHUNKS_SHIFT 4
 #define DGXM_ATTN_P_CHUNKS_MASK (7 << DGXM_ATTN_P_CHUNKS_SHIFT)
 #define DGXM_ATTN_P_CHUNKS(n) ((n) << DGXM_ATTN_P_CHUNKS_SHIFT)
-/* Let the two query tiles' exponential loops take turns instead of sharing
- * the special-function units (a ping-pong softmax).  Applies to bf16 output
- * without extras (bf16 or e4m3 input); other calls run their usual schedule.  Only the
- * timing changes: the output is bit-identical to the same call without it. */
-#define DGXM_ATTN_PINGPONG (1 << 8)
 
 /* Version of this ABI; bumped on any incompatible change. */
 int dgxm_abi_version(void);
@@ -434,6 +430,17 @@ int dgxm_ring_attn_fwd_noalloc(dgxm_comm* comm, const dgxm_attn_desc* desc, cons
  * calls it in the same order with the same shapes.
  */
 int64_t dgxm_full_context_window_bytes(const dgxm_attn_desc* desc, int32_t world);
+/*
+ * The store half of the full-context gather, for callers that own their
+ * destination buffers and order them themselves (no barrier): this rank's
+ * K and V blocks (desc: batch, kv_len, kv_heads, head_dim 128, k/v strides,
+ * in_dtype bf16 or f16) go into rank-major rows [rank*L, (rank+1)*L) of every
+ * rank's contiguous (batch, world*L, kv_heads, head_dim) tensors dst_k[r] /
+ * dst_v[r], all addressable from this rank.  The batch_isend_irecv exchange
+ * of adapters/wan_ring_full_context.py:203-295 as one launch of stores.
+ */
+int dgxm_kv_gather_store(const dgxm_attn_desc* desc, int32_t world, int32_t rank, const void* k,
+                         const void* v, void* const* dst_k, void* const* dst_v, void* stream);
 int dgxm_full_context_attn_fwd(dgxm_comm* comm, const dgxm_attn_desc* desc, const void* q,
                                const void* k, const void* v, void* o, float* lse, void* stream);
 
@@ -459,6 +466,11 @@ typedef struct dgxm_seq_gather_desc {
 
 int dgxm_seq_allgather(dgxm_comm* comm, const dgxm_seq_gather_desc* desc, const void* src,
                        int64_t window_offset, void* stream);
+/* The store half of dgxm_seq_allgather (no barrier), for callers that own the
+ * destinations: this rank's rows into dst[r], rank r's trimmed (batch,
+ * orig_len, row_bytes) buffer, for every r < world (16-byte aligned). */
+int dgxm_seq_gather_store(const dgxm_seq_gather_desc* desc, int32_t world, int32_t rank,
+                          const void* src, void* const* dst, void* stream);
 
 /*
  * The shared NVFP4 activation scale (adapters/quant_activation_scale.py:

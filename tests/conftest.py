@@ -13,9 +13,6 @@ if str(ROOT) not in sys.path:
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a B200 (sm_100a) and the built libdgxm_sp.so")
-    config.addinivalue_line(
-        "markers", "first_run: a GPU path not yet run on a B200; runs only with DGXM_FIRST_RUN=1, "
-        "so its first run on a shared GPU is a deliberate one")
 
 
 def _has_cuda() -> bool:
@@ -28,11 +25,6 @@ def _has_cuda() -> bool:
 
 
 def pytest_collection_modifyitems(config, items):
-    if os.environ.get("DGXM_FIRST_RUN") != "1":
-        first = pytest.mark.skip(reason="first run of this GPU path: set DGXM_FIRST_RUN=1")
-        for item in items:
-            if "first_run" in item.keywords:
-                item.add_marker(first)
     if _has_cuda():
         return
     skip = pytest.mark.skip(reason="no CUDA device in this process")

@@ -66,7 +66,7 @@ def test_bindings_cover_exactly_the_declared_functions():
 
 
 def test_abi_version_without_a_gpu(library):
-    assert library.dgxm_abi_version() == 1
+    assert library.dgxm_abi_version() == 2
     assert isinstance(library.dgxm_last_error_message(), bytes)
 
 

@@ -1,12 +1,9 @@
-"""The chunked release of P (DGXM_ATTN_P_CHUNKS) and the ping-pong softmax
-(DGXM_ATTN_PINGPONG).  With chunks, the softmax hands each
-128-key block's probabilities to the tensor core in 2 or 4 chunks, and the
-P.V steps of a chunk start while the rest is computed.  Same contract as the
-one-chunk kernel: bf16 output max-abs <= 2e-2 and rel-L2 <= 5e-3, LSE within
-2e-3 of fp32 attention; e4m3 rel-L2 <= 3e-2; masks and routing unchanged.
-
-These tests carry the first_run marker (tests/conftest.py): the chunked
-kernels have not yet run on a B200, and the library default stays one chunk.
+"""The release of P in chunks (DGXM_ATTN_P_CHUNKS): the softmax hands each
+128-key block's probabilities to the tensor core in 4 chunks (2 for e4m3),
+the library default, and the P.V steps of a chunk start while the rest is
+computed; one chunk is kept as a cross-check.  Both are held to the same
+contract: bf16 output max-abs <= 2e-2 and rel-L2 <= 5e-3, LSE within 2e-3
+of fp32 attention; e4m3 rel-L2 <= 3e-2; masks and routing unchanged.
 """
 from __future__ import annotations
 
@@ -16,7 +13,7 @@ import torch
 from tests.test_attn_gpu import (BF16_MAX_ABS, BF16_REL_L2, FP8_REL_L2, LSE_ABS, SHAPES,
                                  quantize_e4m3_per_head, reference_attention, rel_l2)
 
-pytestmark = [pytest.mark.gpu, pytest.mark.first_run]
+pytestmark = pytest.mark.gpu
 
 
 @pytest.fixture
@@ -32,7 +29,7 @@ def chunks(request):
     assert _lib.device_error() == 0
 
 
-@pytest.mark.parametrize("chunks", [2, 4], indirect=True)
+@pytest.mark.parametrize("chunks", [1, 4], indirect=True)
 @pytest.mark.parametrize("shape", SHAPES)
 def test_chunked_bf16_matches_fp32_reference(lib, chunks, shape):
     from dgx_monarch_b200.ops import attention_fwd
@@ -51,7 +48,7 @@ def test_chunked_bf16_matches_fp32_reference(lib, chunks, shape):
     assert (lse - ref_lse).abs().max().item() <= LSE_ABS
 
 
-@pytest.mark.parametrize("chunks", [2, 4], indirect=True)
+@pytest.mark.parametrize("chunks", [1, 4], indirect=True)
 def test_chunked_rescales_a_growing_maximum(lib, chunks):
     """Logits that grow block after block force the O rescale, which the
     chunked kernel performs before releasing a block's first chunk."""
@@ -72,7 +69,7 @@ def test_chunked_rescales_a_growing_maximum(lib, chunks):
     assert (lse - ref_lse).abs().max().item() <= LSE_ABS
 
 
-@pytest.mark.parametrize("chunks", [2, 4], indirect=True)
+@pytest.mark.parametrize("chunks", [1, 4], indirect=True)
 @pytest.mark.parametrize("shape", [(1, 256, 256, 2, 2), (2, 4608, 4608, 3, 3), (1, 1000, 333, 4, 2)])
 def test_chunked_fp8_matches_sdpa(lib, chunks, shape):
     from dgx_monarch_b200.ops import attention_fwd
@@ -90,7 +87,7 @@ def test_chunked_fp8_matches_sdpa(lib, chunks, shape):
     assert (lse - ref_lse).abs().max().item() <= 5 * LSE_ABS
 
 
-@pytest.mark.parametrize("chunks", [2, 4], indirect=True)
+@pytest.mark.parametrize("chunks", [1, 4], indirect=True)
 def test_chunked_keep_masks_and_routing(lib, chunks):
     """The extras kernel (keep bits) and the routed epilogue with chunks."""
     from dgx_monarch_b200.ops import attention_fwd_ext, keep_bits
@@ -116,42 +113,24 @@ def test_chunked_keep_masks_and_routing(lib, chunks):
     assert got[:, drop].abs().max().item() == 0.0
 
 
-@pytest.mark.parametrize("chunks", [1, 2, 4], indirect=True)
 @pytest.mark.parametrize("shape", [(1, 256, 256, 1, 1), (2, 300, 77, 3, 1), (1, 4096, 4096, 2, 2)])
-def test_pingpong_schedule_gives_the_same_bits(lib, chunks, shape):
-    """Only the timing changes when the two tiles' exponential loops take
-    turns: the output and LSE equal the same call without ping-pong."""
-    from dgx_monarch_b200.ops import attention_fwd, set_pingpong
+def test_one_and_four_chunks_agree(lib, shape):
+    """The chunked release accumulates the P.V steps in another order than the
+    single release; the two agree within the bf16 bound, and the LSE (computed
+    before any P.V) is the same bits."""
+    from dgx_monarch_b200.ops import attention_fwd, set_p_chunks
 
     b, lq, lk, h, hkv = shape
     g = torch.Generator(device="cuda").manual_seed(17)
     q = torch.randn(b, lq, h, 128, device="cuda", generator=g).bfloat16()
     k = torch.randn(b, lk, hkv, 128, device="cuda", generator=g).bfloat16()
     v = torch.randn(b, lk, hkv, 128, device="cuda", generator=g).bfloat16()
-    want, want_lse = attention_fwd(q, k, v)
-    set_pingpong(True)
+    four, four_lse = attention_fwd(q, k, v)
+    set_p_chunks(1)
     try:
-        got, got_lse = attention_fwd(q, k, v)
+        one, one_lse = attention_fwd(q, k, v)
     finally:
-        set_pingpong(False)
+        set_p_chunks(0)
     torch.cuda.synchronize()
-    assert torch.equal(got, want) and torch.equal(got_lse, want_lse)
-    ref, _ = reference_attention(q, k, v)
-    assert rel_l2(got, ref) <= BF16_REL_L2
-
-
-@pytest.mark.parametrize("chunks", [1, 2], indirect=True)
-def test_pingpong_schedule_gives_the_same_bits_in_e4m3(lib, chunks):
-    from dgx_monarch_b200.ops import attention_fwd, set_pingpong
-
-    g = torch.Generator(device="cuda").manual_seed(23)
-    (q8, qs), (k8, ks), (v8, vs) = (quantize_e4m3_per_head(
-        torch.randn(2, 1000, 3, 128, device="cuda", generator=g).bfloat16()) for _ in range(3))
-    want, want_lse = attention_fwd(q8, k8, v8, q_descale=qs, k_descale=ks, v_descale=vs)
-    set_pingpong(True)
-    try:
-        got, got_lse = attention_fwd(q8, k8, v8, q_descale=qs, k_descale=ks, v_descale=vs)
-    finally:
-        set_pingpong(False)
-    torch.cuda.synchronize()
-    assert torch.equal(got, want) and torch.equal(got_lse, want_lse)
+    assert (four_lse - one_lse).abs().max().item() <= 1e-5
+    assert rel_l2(four, one.float()) <= BF16_REL_L2

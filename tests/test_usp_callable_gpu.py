@@ -183,7 +183,6 @@ def test_fp8_callable_on_one_rank(lib):
     attn.impl.invalidate()
 
 
-@pytest.mark.first_run
 @pytest.mark.parametrize("head_dim", [64, 96])
 def test_small_head_dims_run_zero_padded(attn, head_dim):
     """Heads below 128 (LTX-Video's 64) run zero-padded with the scale of their
