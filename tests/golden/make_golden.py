@@ -71,6 +71,114 @@ LOCAL_QKV_CASES = [
 ]
 
 
+# Ring block-processor calls (adapters/cudnn_ring_attention.py:26-89): kernel
+# options, then q/k/v shapes and dtypes; on CPU tensors a well-formed call
+# ends at the CUDA-device refusal.
+RING_PROCESSOR_CASES = [
+    {"kw": {}},
+    {"kw": {"softmax_scale": 0.125}},
+    {"kw": {"softmax_scale": 1}},
+    {"kw": {"softmax_scale": 0.0}},
+    {"kw": {"softmax_scale": -1.0}},
+    {"kw": {"softmax_scale": {"float": "inf"}}},
+    {"kw": {"softmax_scale": True}},
+    {"kw": {"softmax_scale": "0.1"}},
+    {"kw": {"dropout_p": 0.1}},
+    {"kw": {"causal": True}},
+    {"kw": {"window_size": {"tuple": [0, 0]}}},
+    {"kw": {"alibi_slopes": "slopes"}},
+    {"kw": {"softcap": 1.0}},
+    {"kw": {"return_softmax": True}},
+    {"kw": {"deterministic": True}},
+    {"kw": {"block_mask": None}},
+    {"q": [1, 8, 2, 64], "k": [1, 8, 2, 64], "v": [1, 8, 2, 64], "dtype": "float32"},
+    {"q": [8, 2, 64], "k": [8, 2, 64], "v": [8, 2, 64]},
+    {"q": [1, 0, 2, 64], "k": [1, 8, 2, 64], "v": [1, 8, 2, 64]},
+    {"q": [1, 8, 2, 64], "k": [1, 8, 2, 64], "v": [1, 8, 2, 64], "grad": True},
+    {"q": [1, 8, 3, 64], "k": [1, 8, 2, 64], "v": [1, 8, 2, 64]},
+    {"q": [1, 8, 2, 64], "k": [1, 8, 2, 64], "v": [1, 9, 2, 64]},
+    {"q": [1, 8, 2, 64], "k": [2, 8, 2, 64], "v": [2, 8, 2, 64]},
+    {"q": [1, 5, 2, 64], "k": [1, 8, 2, 64], "v": [1, 8, 2, 64], "dtype": "float16"},
+    {"q": [1, 8, 2, 64], "k": [1, 8, 2, 64], "v": [1, 8, 2, 64], "dtype": "float16", "k_dtype": "bfloat16"},
+]
+
+
+# Per-cond CFG dispatch (adapters/cfg_dispatch.py:92-206): conditioning
+# slots described as lists of entries -- text tokens, an optional batch
+# constant and optional unmodelled keys, hooks or a control object name --
+# built into comfy-like cond objects by build_cond_slots below (the test
+# builds the same objects).
+COND_FOLD_CASES = [
+    {"slots": [[{"tokens": 7}], [{"tokens": 7}]]},
+    {"slots": [[{"tokens": 7}], [{"tokens": 11}]]},
+    {"slots": [[{"tokens": 2}], [{"tokens": 8}]]},
+    {"slots": [[{"tokens": 77}], [{"tokens": 154}]]},
+    {"slots": [[{"tokens": 100}], [{"tokens": 28}]]},
+    {"slots": [[{"tokens": 7, "const": 9}], [{"tokens": 7, "const": 11}]], "key": "num_tokens"},
+    {"slots": [[{"tokens": 7, "const": 9}], [{"tokens": 11, "const": 9}]], "key": "num_tokens"},
+    {"slots": [[{"tokens": 7}], [{"tokens": 11, "area": True}]]},
+    {"slots": [[{"tokens": 7, "hooks": "h"}], [{"tokens": 11}]]},
+    {"slots": [[{"tokens": 7, "control": "a"}], [{"tokens": 11, "control": "b"}]]},
+    {"slots": [[{"tokens": 7}], None]},
+    {"slots": [[{"tokens": 7}], [{"tokens": 11}], [{"tokens": 13}]]},
+    {"slots": [[{"tokens": 7}, {"tokens": 7}], [{"tokens": 7}]]},
+    {"slots": [[{"tokens": 7, "extra": True}], [{"tokens": 7}]]},
+]
+
+
+class _FakeCrossAttn:
+    """A comfy CONDCrossAttn-like object: its length rule decides can_concat."""
+
+    def __init__(self, tokens):
+        self.cond = torch.zeros(1, tokens, 4)
+
+    def process_cond(self, batch_size, area):
+        return self
+
+    def can_concat(self, other):
+        a, b = self.cond.shape[1], other.cond.shape[1]
+        if a == b:
+            return True
+        lo, hi = min(a, b), max(a, b)
+        return lo > 0 and math.lcm(lo, hi) // lo <= 4
+
+
+class _FakeConstant:
+    def __init__(self, value):
+        self.cond = value
+
+    def process_cond(self, batch_size, area):
+        return self
+
+    def can_concat(self, other):
+        return self.cond == other.cond
+
+
+def build_cond_slots(case):
+    controls = {}
+    slots = []
+    for slot in case["slots"]:
+        if slot is None:
+            slots.append(None)
+            continue
+        entries = []
+        for e in slot:
+            conds = {"c_crossattn": _FakeCrossAttn(e["tokens"])}
+            if "const" in e:
+                conds["num_tokens"] = _FakeConstant(e["const"])
+            if e.get("extra"):
+                conds["y"] = object()  # a cond without comfy's methods
+            item = {"model_conds": conds, "control": controls.setdefault(e.get("control"), object())
+                    if e.get("control") else None}
+            if e.get("area"):
+                item["area"] = (1, 1, 0, 0)
+            if e.get("hooks"):
+                item["hooks"] = e["hooks"]
+            entries.append(item)
+        slots.append(entries)
+    return slots
+
+
 # Malformed (and two well-formed) usp_attention calls: tensor shapes, the
 # call's keyword arguments, and an optional mask ("effective" or "noop").
 USP_REFUSAL_CASES = [
@@ -115,6 +223,18 @@ def encode_case(case: dict) -> dict:
             return {"float": repr(x)}
         return x
     return {key: enc(value) for key, value in case.items()}
+
+
+def _decode_case(x):
+    """Inverse of encode_case for one value."""
+    if isinstance(x, dict):
+        if set(x) == {"tuple"}:
+            return tuple(_decode_case(y) for y in x["tuple"])
+        if set(x) == {"list"}:
+            return [_decode_case(y) for y in x["list"]]
+        if set(x) == {"float"}:
+            return float(x["float"])
+    return x
 
 
 def build_qkv(case: dict):
@@ -499,6 +619,40 @@ def main() -> None:
             said = str(exc)
         refusals.append({"case": case, "verdict": said})
     golden["usp_refusals"] = refusals
+
+    # n) the cuDNN ring block processor's verdicts on those calls.
+    processor = cudnn_ring_attention.TorchCudnnRingProcessor()
+    ring_verdicts = []
+    for case in RING_PROCESSOR_CASES:
+        dt = getattr(torch, case.get("dtype", "bfloat16"))
+        shapes = [case.get(n, [1, 8, 2, 64]) for n in "qkv"]
+        q, k, v = (torch.zeros(shape, dtype=dt) for shape in shapes)
+        if "k_dtype" in case:
+            k = k.to(getattr(torch, case["k_dtype"]))
+        if case.get("grad"):
+            q.requires_grad_(True)
+        kwargs = {key: _decode_case(value) for key, value in case.get("kw", {}).items()}
+        try:
+            processor(q, k, v, **kwargs)
+            said = "ok"
+        except base.UnsupportedModelError as exc:
+            said = str(exc)
+        ring_verdicts.append({"case": case, "verdict": said})
+    golden["ring_processor"] = ring_verdicts
+
+    # o) per-cond CFG dispatch: the fold verdicts, the cond groups and the
+    #    cross-attention length rule of adapters/cfg_dispatch.py.
+    from dgx_monarch.adapters import cfg_dispatch
+
+    x_in = torch.zeros(2, 3)
+    golden["cond_fold"] = [{"case": case, "folds": bool(cfg_dispatch.conds_fold(
+        build_cond_slots(case), x_in, case.get("key")))} for case in COND_FOLD_CASES]
+    golden["cond_groups"] = [{"count": c, "world": w, "rank": r,
+                              "bounds": list(cfg_dispatch.cond_group_bounds(c, w, r))}
+                             for c in range(0, 7) for w in (1, 2, 3, 4, 8) for r in range(w)]
+    golden["cross_attn_folds"] = [{"a": a, "b": b, "folds": cfg_dispatch.cross_attn_pair_folds(a, b)}
+                                  for a in (0, 1, 2, 7, 11, 28, 44, 77, 100, 154, 256, 512)
+                                  for b in (0, 1, 2, 8, 11, 44, 77, 154, 300, 512)]
 
     (OUT / "golden.json").write_text(json.dumps(golden, indent=1))
     np.savez_compressed(OUT / "golden_arrays.npz", **arrays)
