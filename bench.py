@@ -630,10 +630,11 @@ def main() -> None:
     uly = UlyssesAttention(world=world, rank=rank, batch=BATCH, seq_local=ls, heads=HEADS,
                            head_dim=DIM, device=dev)
     out = torch.empty(BATCH, ls, HEADS, DIM, device=dev, dtype=torch.bfloat16)
-    # N > 1: five groups of 8 heads, each group's scatter hidden behind the
-    # previous group's attention (the inverse all-to-all is in the epilogue).
+    # N > 1: a first group of one head per rank, whose attention hides the
+    # scatter of the other heads (the inverse all-to-all is in the epilogue).
+    over_groups = [world, HEADS - world]
     over = (OverlappedUlysses(world=world, rank=rank, batch=BATCH, seq_local=ls, heads=HEADS, head_dim=DIM,
-                              device=dev, groups=5, generation=13) if world > 1 else None)
+                              device=dev, groups=over_groups, generation=13) if world > 1 else None)
     stream = torch.cuda.current_stream(dev)
 
     def timed(fn, n):
@@ -792,8 +793,9 @@ def main() -> None:
                           "parallelism": f"ulysses{world}"},
             "gpu_launches": launches,
             "ulysses_step": ({"timed_schedule": "overlapped" if runner is over else "plain",
-                              "overlapped_ms_2_steps": over_ms, "plain_ms_2_steps": plain_ms, "groups": 5,
-                              "note": "overlapped: each 8-head group's scatter runs beside the previous "
+                              "overlapped_ms_2_steps": over_ms, "plain_ms_2_steps": plain_ms,
+                              "head_groups": over_groups,
+                              "note": "overlapped: the second head group's scatter runs beside the first "
                                       "group's attention; plain: scatter, barrier, attention, barrier; "
                                       "both timed after warm-up, the faster one (max over ranks) is timed"}
                              if world > 1 else None),

@@ -405,48 +405,66 @@ class HostStreamedUlysses:
 class OverlappedUlysses:
     """A Ulysses step whose sequence->head scatter is hidden behind attention.
 
-    Heads go in `groups` groups (a group's heads divide the Ulysses degree).
-    Group g + 1 is scattered on a side stream into one of two receive slots
-    while the tensor cores attend group g from the other.  Each group's routed
-    epilogue writes its own head columns of the owners' outputs (the peer
-    base pointers are offset by the group), so the inverse all-to-all stays
-    fused.
+    The heads go in consecutive groups (each group's head count a multiple of
+    the Ulysses degree): `groups` is a count of equal groups or a list of
+    group sizes.  Group g + 1 is scattered on a side stream while the tensor
+    cores attend group g; each group's routed epilogue writes its own head
+    columns of the owners' outputs (the peer base pointers are offset by the
+    group's first head), so the inverse all-to-all stays fused.  A small first
+    group leaves only its own scatter exposed: at Ulysses-8 over 40 heads,
+    [8, 32] exposes 8/40 of the all-to-all behind which one head per rank of
+    attention hides the other 32.
 
-    Ordering: a rank refills a slot in its peers' windows only after a
-    barrier that every rank reaches after its own attention from that slot,
-    so no peer is still reading it.  All barriers of the windows are ordered
-    through the two streams' events, as their shared epoch counter requires.
-    The result is bit-identical to UlyssesAttention.forward.
+    Receive slots: two groups use one slot each.  With more groups two slots
+    alternate, and a rank refills a slot in its peers' windows only after a
+    barrier that every rank reaches after its own attention from that slot, so
+    no peer still reads it.  All barriers of the windows are ordered through
+    the two streams' events, as their shared epoch counter requires.  The
+    result is bit-identical to UlyssesAttention.forward.
     """
 
     def __init__(self, *, world: int, rank: int, batch: int, seq_local: int, heads: int, head_dim: int,
-                 device: torch.device, groups: int, group=None, generation: int = 0,
+                 device: torch.device, groups, group=None, generation: int = 0,
                  dtype: torch.dtype = torch.bfloat16) -> None:
         if world < 2:
             raise ValueError("the overlapped step needs a Ulysses degree of 2 or more")
-        if heads % groups or (heads // groups) % world:
-            raise ValueError(f"{groups} head groups of {heads} heads do not split over {world} ranks")
-        self.world, self.rank, self.device, self.groups = world, rank, device, groups
+        if isinstance(groups, int):
+            if groups < 1 or heads % groups:
+                raise ValueError(f"{groups} groups do not split {heads} heads evenly")
+            sizes = [heads // groups] * groups
+        else:
+            sizes = [int(n) for n in groups]
+        if sum(sizes) != heads or any(n < 1 or n % world for n in sizes):
+            raise ValueError(f"head groups {sizes} do not split {heads} heads into multiples of {world} ranks")
+        self.world, self.rank, self.device = world, rank, device
+        self.sizes = sizes
+        self.groups = len(sizes)
+        self.first = [sum(sizes[:g]) for g in range(self.groups)]   # first head of each group
         self.b, self.ls, self.h, self.d = batch, seq_local, heads, head_dim
-        self.hg = heads // groups               # heads per group
-        self.hgl = self.hg // world             # heads per group on one rank after the scatter
         s = seq_local * world
         elt = torch.empty((), dtype=dtype).element_size()
-        slot_bytes = batch * s * self.hgl * head_dim * elt
+        self.n_slots = min(2, self.groups)
+        # slot i serves groups i, i + 2, ...: sized for the largest of them
+        slot_heads = [max(sizes[i::2]) // world for i in range(self.n_slots)]
+        slot_bytes = [batch * s * hl * head_dim * elt for hl in slot_heads]
         out_bytes = batch * seq_local * heads * head_dim * elt
-        self.windows = PeerWindows(6 * slot_bytes + out_bytes + 8 * 256, device=device, group=group,
+        self.windows = PeerWindows(3 * sum(slot_bytes) + out_bytes + 8 * 256, device=device, group=group,
                                    rank=rank, world=world, generation=generation)
-        self.off_recv = [[self.windows.carve(slot_bytes) for _ in range(3)] for _ in range(2)]
+        self.off_recv = [[self.windows.carve(nb) for _ in range(3)] for nb in slot_bytes]
         self.off_out = self.windows.carve(out_bytes)
-        self.recv = [[self.windows.local_tensor(o, (batch, s, self.hgl, head_dim), dtype) for o in slot]
-                     for slot in self.off_recv]
+        self.s, self.dtype = s, dtype
         self.out_local = self.windows.local_tensor(self.off_out, (batch, seq_local, heads, head_dim), dtype)
         self.out_strides = (seq_local * heads * head_dim, heads * head_dim, head_dim)
-        self.group_bytes = self.hg * head_dim * elt  # head-column offset of one group in the outputs
+        self.head_bytes = head_dim * elt
         self.side = torch.cuda.Stream(device)
-        # per group a scatter, a barrier and an attention; one more barrier per
-        # group after the first two (slot reuse); the final barrier
-        self.launches_per_step = 3 * groups + max(0, groups - 2) + 1
+        # per group a scatter, a barrier and an attention; a slot-reuse barrier
+        # per group after the first two; the final barrier
+        self.launches_per_step = 3 * self.groups + max(0, self.groups - 2) + 1
+
+    def _recv(self, g: int):
+        hl = self.sizes[g] // self.world
+        return [self.windows.local_tensor(off, (self.b, self.s, hl, self.d), self.dtype)
+                for off in self.off_recv[g % 2]]
 
     def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                 out: torch.Tensor | None = None) -> torch.Tensor:
@@ -463,7 +481,7 @@ class OverlappedUlysses:
             if g >= 2:
                 side.wait_event(freed[slot])   # this rank attended group g - 2 from the slot
                 w.barrier(side)                 # ... and so has every other rank
-            sl = slice(g * self.hg, (g + 1) * self.hg)
+            sl = slice(self.first[g], self.first[g] + self.sizes[g])
             ulysses_scatter([q[:, :, sl], k[:, :, sl], v[:, :, sl]],
                             [[w.peer_ptr(r, off) for r in range(self.world)] for off in self.off_recv[slot]],
                             world=self.world, rank=self.rank, stream=side)
@@ -475,15 +493,14 @@ class OverlappedUlysses:
         for g in range(min(2, self.groups)):
             scatter(g)
         for g in range(self.groups):
-            slot = g % 2
             main.wait_event(ready[g])
-            qg, kg, vg = self.recv[slot]
-            attention_routed(qg, kg, vg,
-                             [w.peer_ptr(r, self.off_out) + g * self.group_bytes for r in range(self.world)],
+            qg, kg, vg = self._recv(g)
+            col = self.first[g] * self.head_bytes
+            attention_routed(qg, kg, vg, [w.peer_ptr(r, self.off_out) + col for r in range(self.world)],
                              self.out_strides, world=self.world, rank=self.rank, seq_local=self.ls)
             ev = torch.cuda.Event()
             ev.record(main)
-            freed[slot] = ev
+            freed[g % 2] = ev
             if g + 2 < self.groups:
                 scatter(g + 2)
         w.barrier(main)                         # every routed row of every group has landed

@@ -437,6 +437,58 @@ def test_dual_model_cfg_split_across_gpus():
     _spawn(_dual_cfg_case, 2)
 
 
+def _cond_dispatch_case(rank, world, dev):
+    """Per-conditioning CFG dispatch (adapters/cfg_dispatch.py:209-271) over
+    real cfg ranks: conditionings that do not batch (7, 11 and 13 text tokens)
+    are spread over the ranks, each rank runs only its group, and the
+    NVLink gather hands every rank the one-GPU output list in cond order,
+    call after call."""
+    from dgx_monarch_b200 import _lib
+    from dgx_monarch_b200.cfg import CfgGather
+    from dgx_monarch_b200.cfg_dispatch import CondDispatch
+
+    class Tokens:
+        def __init__(self, n):
+            self.cond = torch.zeros(1, n, 4)
+
+        def process_cond(self, batch_size, area):
+            return self
+
+        def can_concat(self, other):
+            a, b = sorted((self.cond.shape[1], other.cond.shape[1]))
+            return a == b or (a > 0 and math.lcm(a, b) // a <= 4)
+
+    def executor(conds, x):
+        out = [torch.zeros_like(x) for _ in conds]
+        for i, slot in enumerate(conds):
+            for item in slot or []:
+                out[i] = out[i] + x * item["weight"] + float(item["model_conds"]["c"].cond.shape[1])
+        return out
+
+    check = Checks(rank)
+    conds = [[{"model_conds": {"c": Tokens(n)}, "weight": float(w)}] for n, w in ((7, 2), (11, 5), (13, 9))]
+    x = torch.arange(2 * 16 * 64 * 64, device=dev, dtype=torch.float32).reshape(2, 16, 64, 64) / 1e5
+    size = -(-len(conds) // world)
+    gather = CfgGather(size * x.numel() * x.element_size(), device=dev, generation=23)
+    dispatch = CondDispatch(world=world, rank=rank, gather=gather)
+    for step in range(3):
+        xs = x + step
+        got = dispatch(executor, conds, xs)
+        want = executor(conds, xs)
+        torch.cuda.synchronize()
+        check(dispatch.last_path == "dispatch", f"path {dispatch.last_path}")
+        check(len(got) == 3 and all(torch.equal(a, b) for a, b in zip(got, want)),
+              f"call {step}: the gathered outputs differ from the one-GPU list")
+    gather.close()
+    check(_lib.device_error() == 0, f"device error word {_lib.device_error()}")
+    check.close()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
+def test_per_cond_cfg_dispatch_across_gpus():
+    _spawn(_cond_dispatch_case, 2)
+
+
 def _graph_case(rank, world, dev):
     """A Ulysses step (scatter, barrier, routed attention, barrier) captured in
     a CUDA graph and replayed with new inputs: the barrier epochs advance on
@@ -560,9 +612,9 @@ def _overlapped_case(rank, world, dev):
     heads, ls = 4 * world, 300
     plain = UlyssesAttention(world=world, rank=rank, batch=1, seq_local=ls, heads=heads, head_dim=128,
                              device=dev, generation=19)
-    for groups in (4, 2):
+    for n, groups in enumerate((4, 2, [world, 3 * world], [world, world, 2 * world])):
         over = OverlappedUlysses(world=world, rank=rank, batch=1, seq_local=ls, heads=heads, head_dim=128,
-                                 device=dev, groups=groups, generation=20 + groups)
+                                 device=dev, groups=groups, generation=20 + n)
         for step in range(3):
             g = torch.Generator(device=dev).manual_seed(110 + step + rank)
             q, k, v = (torch.randn(1, ls, heads, 128, device=dev, generator=g).bfloat16() for _ in range(3))
