@@ -520,44 +520,90 @@ def run_full_context(world: int, rank: int, dev, steps: int, warmup: int) -> dic
 
 
 def run_cfg_fp8(world: int, rank: int, dev, steps: int, warmup: int) -> dict:
+    """C3: the cond/uncond pair in e4m3.  At N > 1 the pair maps to GPU pairs
+    (cfg2 x Ulysses-N/2: each cfg rank attends its batch row's sequence shard,
+    then the predictions are all-gathered over the pair); at N = 1 one call
+    attends both rows.  Also measures the output against fp32 attention of the
+    e4m3 inputs and of the bf16 activations (max over ranks)."""
     import torch
+    import torch.distributed as dist
 
     from dgx_monarch_b200.cfg import CfgGather
     from dgx_monarch_b200.usp import make_b200_usp_attention
 
-    sp = world // 2
-    # sequence parallel fastest, then cfg: ranks r and r + sp form a cond/uncond pair
-    import torch.distributed as dist
-
-    sp_groups = [list(range(c * sp, (c + 1) * sp)) for c in range(2)]
-    cfg_groups = [[r, r + sp] for r in range(sp)]
-    mine_sp = mine_cfg = None
-    for ranks in sp_groups:
-        gsp = dist.new_group(ranks)
-        if rank in ranks:
-            mine_sp = gsp
-    for ranks in cfg_groups:
-        gc = dist.new_group(ranks)
-        if rank in ranks:
-            mine_cfg = gc
-    attn = make_b200_usp_attention(ulysses_group=mine_sp if sp > 1 else None, generation=41,
-                                   device=dev, fp8=True)
-    s = CFG["img"] + CFG["txt"]
+    s, h = CFG["img"] + CFG["txt"], CFG["heads"]
+    if world == 1:
+        sp, rows, seeds = 1, 2, [700, 701]
+        attn = make_b200_usp_attention(generation=41, device=dev, fp8=True)
+        gather = None
+    else:
+        sp = world // 2
+        # sequence parallel fastest, then cfg: ranks r and r + sp form a cond/uncond pair
+        mine_sp = mine_cfg = None
+        for ranks in [list(range(c * sp, (c + 1) * sp)) for c in range(2)]:
+            gsp = dist.new_group(ranks)
+            if rank in ranks:
+                mine_sp = gsp
+        for ranks in [[r, r + sp] for r in range(sp)]:
+            gc = dist.new_group(ranks)
+            if rank in ranks:
+                mine_cfg = gc
+        attn = make_b200_usp_attention(ulysses_group=mine_sp if sp > 1 else None, generation=41,
+                                       device=dev, fp8=True)
+        rows, seeds = 1, [700 + rank]
     ls = s // sp
-    h = CFG["heads"]
-    g = torch.Generator(device=dev).manual_seed(700 + rank)
-    q, k, v = (torch.randn(1, ls, h * DIM, device=dev, generator=g, dtype=torch.bfloat16) for _ in range(3))
-    gather = CfgGather(ls * h * DIM * 2, device=dev, group=mine_cfg, generation=41)
+
+    def inputs(seed_list):
+        qkv = []
+        for seed in seed_list:
+            g = torch.Generator(device=dev).manual_seed(seed)
+            qkv.append([torch.randn(1, ls, h * DIM, device=dev, generator=g, dtype=torch.bfloat16)
+                        for _ in range(3)])
+        return [torch.cat([x[t] for x in qkv]) for t in range(3)]
+
+    q, k, v = inputs(seeds)
+    if world > 1:
+        gather = CfgGather(ls * h * DIM * 2, device=dev, group=mine_cfg, generation=41)
 
     def step():
-        out = attn(q, k, v, heads=h)          # this cfg rank's batch row, its sequence shard
-        return gather(out)                    # predictions of the pair, in cfg-rank order
+        out = attn(q, k, v, heads=h)          # this cfg rank's batch row(s), its sequence shard
+        return out if gather is None else gather(out)
 
     ms_eager = time_steps(step, steps, warmup)
-    ms = time_steps(step, steps, warmup, graph=True)
-    gather.close()
+    ms = time_steps(step, steps, warmup, graph=world > 1)
+    out = attn(q, k, v, heads=h).float().view(rows, ls, h, DIM)
+    # This rank's rows against fp32 attention over its batch row's whole
+    # sequence, rebuilt from the seeds of the ranks holding that row.
+    row_seeds = seeds if world == 1 else [700 + (rank // sp) * sp + r for r in range(sp)]
+    full = [x.view(-1, s if world == 1 else ls, h, DIM) for x in inputs(row_seeds)]
+    if world > 1:
+        full = [x.reshape(1, s, h, DIM) for x in full]
+    mine = slice(0, s) if world == 1 else slice((rank % sp) * ls, (rank % sp + 1) * ls)
+
+    def attend(qf, kf, vf):
+        logits = torch.einsum("bqhd,bkhd->bhqk", qf, kf) / math.sqrt(DIM)
+        return torch.einsum("bhqk,bkhd->bqhd", torch.softmax(logits, dim=-1), vf)
+
+    def e4m3(x):
+        scale = x.float().abs().amax(dim=(0, 1, 3)).clamp_min(1e-12) / 448.0
+        return (x.float() / scale.view(1, 1, -1, 1)).to(torch.float8_e4m3fn).float() * scale.view(1, 1, -1, 1)
+
+    ref_act = attend(*(x.float() for x in full))[:, mine]
+    ref_deq = attend(*(e4m3(x) for x in full))[:, mine]
+    rel = lambda a, b: ((a - b).norm() / b.norm()).item()
+    acc = torch.tensor([rel(out, ref_deq), rel(out, ref_act), rel(ref_deq, ref_act)], device=dev,
+                       dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(acc, op=dist.ReduceOp.MAX)
+        gather.close()
     attn.impl.invalidate()
-    return {"ms": ms, "ms_eager": ms_eager, "layout": f"cfg2xulysses{sp}"}
+    vs_inputs, vs_act, floor = acc.tolist()
+    return {"ms": ms, "ms_eager": ms_eager, "layout": f"cfg2xulysses{sp}" if world > 1 else "one GPU, both rows",
+            "accuracy": {"rel_l2_vs_sdpa_of_e4m3_inputs": vs_inputs, "bound": 3e-2,
+                         "rel_l2_vs_sdpa_of_bf16_activations": vs_act,
+                         "e4m3_input_floor_vs_activations": floor,
+                         "note": "the configuration's attention inputs are the e4m3 tensors; against the "
+                                 "unquantized activations the three e4m3 roundings alone give the floor"}}
 
 
 def time_scatter(uly, steps: int = 5) -> dict:
@@ -729,13 +775,13 @@ def main() -> None:
     dit = run_dit_layer(world, rank, dev, max(5, args.steps), args.warmup)
     extra = [dit["ms"], 0.0, 0.0, 0.0, 0.0, 0.0, dit["ms_eager"], 0.0, dit["ms_qkv_split"], dit["ms_qkv_fused"]]
     a2a = ring_res = cfg_res = fc_res = None
+    cfg_res = run_cfg_fp8(world, rank, dev, 5, 3)
+    extra[3], extra[7] = cfg_res["ms"], cfg_res["ms_eager"]
     if world > 1:
         a2a = time_scatter(uly)
         ring_res = run_ring(world, rank, dev, 2, 1)
-        cfg_res = run_cfg_fp8(world, rank, dev, 5, 3)
         fc_res = run_full_context(world, rank, dev, 3, 3)
-        extra[1:6] = [a2a["ms"], ring_res["ms"], cfg_res["ms"], a2a["gbs_per_direction"], fc_res["ms"]]
-        extra[7] = cfg_res["ms_eager"]
+        extra[1], extra[2], extra[4], extra[5] = a2a["ms"], ring_res["ms"], a2a["gbs_per_direction"], fc_res["ms"]
     td = torch.tensor(extra, device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(td, op=dist.ReduceOp.MAX)
@@ -815,17 +861,18 @@ def main() -> None:
             line["ring"] = {"workload": RING_WORKLOAD, "layout": ring_res["layout"], "ms_per_layer": ring_ms,
                             "tflops": rflops / (ring_ms * 1e-3) / 1e12,
                             "tokens_per_s": RING["seq"] / (ring_ms * 1e-3)}
-            cflops = attn_flops(CFG["batch"], CFG["heads"], CFG["img"] + CFG["txt"], DIM)
-            line["cfg_fp8"] = {"workload": CFG_WORKLOAD, "layout": cfg_res["layout"], "ms_per_step": cfg_ms,
-                               "ms_per_step_eager": cfg_ms_eager,
-                               "launch": "one CUDA graph per step (ms_per_step_eager: the same calls from Python)",
-                               "tflops": cflops / (cfg_ms * 1e-3) / 1e12}
             line["wan_ring2_full_context"] = {
                 "workload": WORKLOAD + "; pure ring-2 full context: K/V gathered over NVLink, "
                             "local Q x full K/V in one call",
                 "layout": f"{fc_res['pairs']} independent ring2 pairs", "ms_per_layer": fc_ms,
                 "tflops_per_pair": flops / (fc_ms * 1e-3) / 1e12,
                 "tflops_total": fc_res["pairs"] * flops / (fc_ms * 1e-3) / 1e12}
+        cflops = attn_flops(CFG["batch"], CFG["heads"], CFG["img"] + CFG["txt"], DIM)
+        line["cfg_fp8"] = {"workload": CFG_WORKLOAD, "layout": cfg_res["layout"], "ms_per_step": cfg_ms,
+                           "ms_per_step_eager": cfg_ms_eager,
+                           "launch": ("one CUDA graph per step (ms_per_step_eager: the same calls from Python)"
+                                      if world > 1 else "the drop-in called from Python"),
+                           "tflops": cflops / (cfg_ms * 1e-3) / 1e12, "accuracy": cfg_res["accuracy"]}
         if world == 1 and not args.no_cpu_baseline:
             from oracle.cpu_baseline import time_ulysses_sample
 

@@ -35,12 +35,16 @@
 // Softmax instruction choices (all compute the same function):
 //   DGXM_SM_MAX3      three-input max for the row reduction
 //   DGXM_SM_POLY_MOD  every N-th pair of exponentials on the FMA pipe
-//                     (exp2_poly2) instead of MUFU; 0 disables
+//                     (exp2_poly2) instead of MUFU; 0 (the default) runs
+//                     every exponential on MUFU.  With P released in 4
+//                     chunks the MUFU-only loop is the fastest: the per-block
+//                     period at 75,600 keys is 3749 clocks against 3802 (1/16
+//                     on the FMA pipe), 3839 (1/8) and 4002 (1/4).
 #ifndef DGXM_SM_MAX3
 #define DGXM_SM_MAX3 1
 #endif
 #ifndef DGXM_SM_POLY_MOD
-#define DGXM_SM_POLY_MOD 8
+#define DGXM_SM_POLY_MOD 0
 #endif
 #ifndef DGXM_SM_PAIR_BARRIER
 #define DGXM_SM_PAIR_BARRIER 1  // exchange row halves over a 64-thread barrier per warp pair
