@@ -108,6 +108,16 @@ def quantize_e4m3_per_head(x):
     return q8, scale
 
 
+def fp8_references(q, k, v):
+    """(SDPA over the per-head e4m3 rounding of q, k, v; the rel-L2 of that
+    against SDPA over q, k, v themselves): the reference an e4m3 kernel is held
+    to, and the floor its input format alone sets against the activations."""
+    deq = [x.float() * s.view(1, 1, -1, 1) for x, s in (quantize_e4m3_per_head(t) for t in (q, k, v))]
+    ref_deq, _ = reference_attention(*deq)
+    ref_act, _ = reference_attention(q, k, v)
+    return ref_deq, rel_l2(ref_deq, ref_act)
+
+
 @pytest.mark.parametrize("shape", [(1, 256, 256, 2, 2), (2, 4608, 4608, 3, 3), (1, 1000, 333, 4, 2)])
 def test_fp8_matches_sdpa_within_3e2(lib, shape):
     from dgx_monarch_b200.ops import attention_fwd
@@ -129,10 +139,11 @@ def test_fp8_matches_sdpa_within_3e2(lib, shape):
     assert out.dtype == torch.bfloat16
     assert rel_l2(out, ref) <= FP8_REL_L2
     assert (lse - ref_lse).abs().max().item() <= 5 * LSE_ABS
-    # Against the unquantized bf16 activations the input quantization adds
-    # about 5% for N(0,1) data (3 mantissa bits on q, k and v).
+    # Against the unquantized bf16 activations the three e4m3 roundings alone
+    # set a floor (about 4-5 % for N(0,1) data); the kernel adds at most its own 3e-2.
     ref_bf16, _ = reference_attention(q, k, v)
-    assert rel_l2(out, ref_bf16) <= 8e-2
+    floor = rel_l2(ref, ref_bf16)
+    assert rel_l2(out, ref_bf16) <= floor + FP8_REL_L2
 
 
 def test_lse_merge_reconstructs_full_attention(lib):

@@ -178,8 +178,12 @@ def test_fp8_callable_on_one_rank(lib):
     q, k, v = _qkv(2, 640, 4, 4, 21)
     for _ in range(2):  # the second call reuses the e4m3 buffers
         out = attn(*(t.reshape(2, 640, -1) for t in (q, k, v)), heads=4).reshape(2, 640, 4, 128)
+    from tests.test_attn_gpu import FP8_REL_L2, fp8_references
+
     ref, _ = reference_attention(q, k, v)
-    assert rel_l2(out, ref) <= 8e-2  # e4m3 inputs against bf16 activations
+    ref_deq, floor = fp8_references(q, k, v)  # per-head scales over both batch rows, as the drop-in takes
+    assert rel_l2(out, ref_deq) <= FP8_REL_L2
+    assert rel_l2(out, ref) <= floor + FP8_REL_L2  # e4m3 inputs against bf16 activations
     attn.impl.invalidate()
 
 
