@@ -172,3 +172,36 @@ def test_store_halves_refuse_bad_destinations(lib):
     k = torch.zeros(1, 4, 1, 128, device="cuda", dtype=torch.float32)
     with pytest.raises(DgxmError, match="bf16 or f16"):
         kv_gather_store(k, k, [k.data_ptr()], [k.data_ptr()], world=1, rank=0)
+
+
+def test_ring_entry_refuses_layouts_it_cannot_merge(lib):
+    """At any ring degree (here a one-rank ring) the ring entry refuses a
+    strided LSE -- the merge writes (B, H, L) contiguously -- and a
+    non-contiguous output, before any launch."""
+    import ctypes
+
+    from dgx_monarch_b200 import _lib as L
+    from dgx_monarch_b200.ops import attn_desc
+    from dgx_monarch_b200.ring import RingAttention
+
+    q = torch.randn(1, 256, 2, 128, device="cuda").bfloat16()
+    ring = RingAttention(world=1, rank=0, batch=1, q_len=256, kv_len=256, heads=2, kv_heads=2, head_dim=128,
+                         device=q.device, generation=31)
+    try:
+        out = torch.empty_like(q)
+        lse_t = torch.empty(1, 256, 2, device="cuda").transpose(1, 2)   # (B, H, L) view, strided
+        desc = attn_desc(q, q, q, out, lse_t)
+        stream = torch.cuda.current_stream().cuda_stream
+        for entry in ("dgxm_ring_attn_fwd", "dgxm_ring_attn_fwd_noalloc"):
+            fn = getattr(L.load(), entry)
+            args = [ring.windows._handle, ctypes.byref(desc), q.data_ptr(), q.data_ptr(), q.data_ptr(),
+                    out.data_ptr(), lse_t.data_ptr()]
+            if entry == "dgxm_ring_attn_fwd":
+                args += [ring.workspace.data_ptr(), ring.workspace_bytes]
+            rc = fn(*args, stream)
+            assert rc == L.DGXM_ERR_INVALID and b"contiguous (B, H, L) lse" in L.load().dgxm_last_error_message()
+        wide = torch.empty(1, 256, 4, 128, device="cuda", dtype=torch.bfloat16)[:, :, :2]
+        with pytest.raises(L.DgxmError, match="contiguous"):
+            ring.forward(q, q, q, out=wide)
+    finally:
+        ring.close()

@@ -153,13 +153,20 @@ def _ring_case(rank, world, dev):
     sl = slice(rank * rows, (rank + 1) * rows)
     ring = RingAttention(world=world, rank=rank, batch=1, q_len=rows, kv_len=rows, heads=heads,
                          kv_heads=heads, head_dim=128, device=dev, generation=2)
-    lse = torch.empty(1, heads, rows, device=dev, dtype=torch.float32)
-    for _ in range(3):
-        out, _ = ring.forward(q[:, sl].contiguous(), k[:, sl].contiguous(), v[:, sl].contiguous(), lse=lse)
+    # Several calls back to back with different inputs and no host sync in
+    # between: the closing barrier keeps a call's first rotation from
+    # overwriting a block a neighbour still attends in the previous call.
+    calls = []
+    for n in range(4):
+        qn, kn, vn = (t * (1.0 + 0.25 * n) for t in (q, k, v))
+        lse = torch.empty(1, heads, rows, device=dev, dtype=torch.float32)
+        out, _ = ring.forward(qn[:, sl].contiguous(), kn[:, sl].contiguous(), vn[:, sl].contiguous(), lse=lse)
+        calls.append((qn, kn, vn, out, lse))
     torch.cuda.synchronize()
-    ref, ref_lse = reference_attention(q, k, v)
-    check.le(rel_l2(out, ref[:, sl]), BF16_REL_L2, "ring rel l2")
-    check.le((lse - ref_lse[:, :, sl]).abs().max().item(), 2e-3, "ring lse")
+    for n, (qn, kn, vn, out, lse) in enumerate(calls):
+        ref, ref_lse = reference_attention(qn, kn, vn)
+        check.le(rel_l2(out, ref[:, sl]), BF16_REL_L2, f"ring call {n} rel l2")
+        check.le((lse - ref_lse[:, :, sl]).abs().max().item(), 2e-3, f"ring call {n} lse")
     check(_lib.device_error() == 0, f"device error word {_lib.device_error()}")
     ring.close()
     check.close()
