@@ -58,6 +58,36 @@ def ulysses_scatter(tensors: list[torch.Tensor], dst_ptrs: list[list[int]], *, w
                "dgxm_ulysses_scatter")
 
 
+def ulysses_scatter_copy(tensors: list[torch.Tensor], dst_ptrs: list[list[int]], *, world: int,
+                         rank: int, stream=None) -> None:
+    """The rank-major sequence->head scatter of ulysses_scatter as copy-engine
+    transfers (dgxm_copy_2d): for each tensor and destination rank r, the head
+    slice [r*H/P, (r+1)*H/P) of every local row is one strided copy into rows
+    [rank*Ls, (rank+1)*Ls) of rank r's (B, P*Ls, H/P, D) receive tensor (one
+    copy per batch item).  The same bytes as the kernel, but no SM is used, so
+    it can run beside an attention launch without taking SM slots from it.
+    Each row's heads must be contiguous (stride(2) == D)."""
+    _require_cuda(*tensors)
+    b, ls, h, d = tensors[0].shape
+    if h % world:
+        raise ValueError(f"{h} heads do not divide the Ulysses degree {world}")
+    hl = h // world
+    elt = tensors[0].element_size()
+    for t in tensors:
+        if t.shape != tensors[0].shape or t.dtype != tensors[0].dtype or t.stride(3) != 1 or t.stride(2) != d:
+            raise ValueError("the copy-engine scatter needs (B, Ls, H, D) tensors with contiguous heads per row")
+    from .ops import copy_2d
+
+    stream = stream or torch.cuda.current_stream(tensors[0].device)
+    row = hl * d * elt
+    for t, dsts in zip(tensors, dst_ptrs):
+        for r in range(world):
+            for bi in range(b):
+                src = t.data_ptr() + (bi * t.stride(0) + r * hl * d) * elt
+                dst = dsts[r] + (bi * world * ls + rank * ls) * row
+                copy_2d(dst, row, src, t.stride(1) * elt, row, ls, stream)
+
+
 def ulysses_gather(src: torch.Tensor, dst_ptrs: list[int], *, world: int, rank: int,
                    seq_local: int, heads: int, seg0: int = 0, stream=None) -> None:
     """Return (B, S, Hl, D) rows to the owning ranks' (B, Ls, H, D) tensors."""
@@ -415,6 +445,9 @@ class OverlappedUlysses:
     [8, 32] exposes 8/40 of the all-to-all behind which one head per rank of
     attention hides the other 32.
 
+    The group scatters run on copy engines (ulysses_scatter_copy), so they
+    take no SM from the attention launch they run beside.
+
     Receive slots: two groups use one slot each.  With more groups two slots
     alternate, and a rank refills a slot in its peers' windows only after a
     barrier that every rank reaches after its own attention from that slot, so
@@ -482,9 +515,11 @@ class OverlappedUlysses:
                 side.wait_event(freed[slot])   # this rank attended group g - 2 from the slot
                 w.barrier(side)                 # ... and so has every other rank
             sl = slice(self.first[g], self.first[g] + self.sizes[g])
-            ulysses_scatter([q[:, :, sl], k[:, :, sl], v[:, :, sl]],
-                            [[w.peer_ptr(r, off) for r in range(self.world)] for off in self.off_recv[slot]],
-                            world=self.world, rank=self.rank, stream=side)
+            # Copy engines move the group beside the attention of the group
+            # before it, taking no SM from that launch.
+            ulysses_scatter_copy([q[:, :, sl], k[:, :, sl], v[:, :, sl]],
+                                 [[w.peer_ptr(r, off) for r in range(self.world)] for off in self.off_recv[slot]],
+                                 world=self.world, rank=self.rank, stream=side)
             w.barrier(side)                     # every rank's rows of group g have landed
             ev = torch.cuda.Event()
             ev.record(side)

@@ -347,11 +347,14 @@ def _full_context_case(rank, world, dev):
             except UnsupportedModelError:
                 refused += 1
         check(refused == 5, f"{refused} of 5 unsupported surfaces refused")
-        try:
-            fn(ql.half(), kl.half(), vl.half())
-            check(False, "fp16 accepted")
-        except UnsupportedModelError:
-            pass
+        # fp16 shards run in fp16, as the reference's flash path takes them
+        # (adapters/wan_ring_full_context.py:10), and are held to the fp16 bound.
+        from tests.test_attn_gpu import F16_REL_L2
+
+        out16 = fn(ql.half(), kl.half(), vl.half())
+        ref16, _ = reference_attention(q.half(), k.half(), v.half())
+        check(out16.dtype == torch.float16, f"fp16 shards gave {out16.dtype}")
+        check.le(rel_l2(out16, ref16[:, sl]), F16_REL_L2, "fp16 reference-signature function rel l2")
         out = fn(ql, kl, vl, group=group)
         check.le(rel_l2(out, ref[:, sl]), BF16_REL_L2, "reference-signature function rel l2")
         fn.invalidate()

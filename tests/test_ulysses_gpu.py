@@ -43,6 +43,29 @@ def test_scatter_is_bit_exact_rank_major(lib, world, batch, seq_local, heads):
             assert np.array_equal(_bits(recv[t][r]), want[r])
 
 
+@pytest.mark.parametrize("world,batch,seq_local,heads", [(2, 1, 64, 4), (4, 2, 33, 8), (8, 1, 17, 40)])
+def test_copy_engine_scatter_is_bit_exact_rank_major(lib, world, batch, seq_local, heads):
+    """The copy-engine scatter (strided 2-D copies per tensor and destination)
+    writes the same bytes as the kernel, including from a head-group slice."""
+    from dgx_monarch_b200.ulysses import ulysses_scatter_copy
+
+    g = torch.Generator(device="cuda").manual_seed(world + 50)
+    wide = [[torch.randn(batch, seq_local, 2 * heads, 128, device="cuda", generator=g).bfloat16()
+             for _ in range(3)] for _ in range(world)]
+    local = [[t[:, :, heads:] for t in ts] for ts in wide]  # a group's head slice: strided rows
+    hl = heads // world
+    recv = [[torch.full((batch, seq_local * world, hl, 128), float("nan"), device="cuda",
+                        dtype=torch.bfloat16) for _ in range(world)] for _ in range(3)]
+    for src in range(world):
+        ulysses_scatter_copy(local[src], [[recv[t][r].data_ptr() for r in range(world)] for t in range(3)],
+                             world=world, rank=src)
+    torch.cuda.synchronize()
+    for t in range(3):
+        want = usp.seq_all_to_all_4d([_bits(local[s][t]) for s in range(world)], 2, 1)
+        for r in range(world):
+            assert np.array_equal(_bits(recv[t][r]), want[r])
+
+
 def test_scatter_reads_strided_projection_views(lib):
     """q/k/v as views of one packed (B, L, 3, H, D) projection output."""
     from dgx_monarch_b200.ulysses import ulysses_scatter
