@@ -48,9 +48,10 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--e2e-groups", type=int, default=5,
+    p.add_argument("--e2e-groups", type=int, default=0,
                    help="head groups the host-streamed e2e step pipelines (must divide the "
-                        "40 heads, with a multiple of the GPU count per group)")
+                        "40 heads, with a multiple of the GPU count per group); 0: one head per "
+                        "GPU per group, 40 / N groups")
     p.add_argument("--p-chunks", type=int, choices=[0, 1, 4], default=0,
                    help="release each block's probabilities to the tensor core in this many "
                         "chunks (0: the library default, 4; 1: the single release)")
@@ -642,6 +643,8 @@ def main() -> None:
         return
     if args.warmup < 3:
         raise SystemExit("--warmup must be at least 3")
+    if args.e2e_groups == 0 and args.gpus >= 1 and HEADS % args.gpus == 0:
+        args.e2e_groups = HEADS // args.gpus
     if args.e2e_groups < 1 or HEADS % args.e2e_groups or (HEADS // args.e2e_groups) % args.gpus:
         raise SystemExit(f"--e2e-groups {args.e2e_groups}: groups must divide the {HEADS} heads into "
                          f"groups whose size is a multiple of {args.gpus} GPUs")
