@@ -49,6 +49,9 @@
 #ifndef DGXM_SM_PAIR_BARRIER
 #define DGXM_SM_PAIR_BARRIER 1  // exchange row halves over a 64-thread barrier per warp pair
 #endif
+#ifndef DGXM_SM_WARP_ARRIVE
+#define DGXM_SM_WARP_ARRIVE 1  // one P-release arrival per softmax warp (0: one per thread)
+#endif
 #ifndef DGXM_SM_THR_BF16
 #define DGXM_SM_THR_BF16 8.0f  // stale-max threshold of the bf16 kernel (log2 units)
 #endif
@@ -269,6 +272,19 @@ __device__ __forceinline__ bool issue_pv_chunks(uint64_t* bars, uint32_t d_tmem,
   return true;
 }
 
+// Release one P chunk of a softmax warp.  Every thread has waited for its
+// own TMEM stores and fenced them; the warp then meets, and one arrival per
+// warp (or per thread) goes to the chunk's barrier.  Fewer arrivals mean
+// fewer shared-memory atomics on the barrier the MMA issuer is testing.
+__device__ __forceinline__ void release_p(uint32_t b, int lane) {
+  if (DGXM_SM_WARP_ARRIVE) {
+    __syncwarp();
+    if (lane == 0) mbar_arrive(b);
+  } else {
+    mbar_arrive(b);
+  }
+}
+
 __device__ __forceinline__ void raise_abort(volatile int* abort_flag, int bits) {
   report_device_error(bits);
   *abort_flag = 1;
@@ -304,7 +320,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(bar(B::kSFull + t), 1);
-      for (int ch = 0; ch < kPChunks; ++ch) mbar_init(bar(B::kPFull + t * kPChunks + ch), 256);
+      for (int ch = 0; ch < kPChunks; ++ch)
+        mbar_init(bar(B::kPFull + t * kPChunks + ch), DGXM_SM_WARP_ARRIVE ? 8 : 256);
       mbar_init(bar(B::kOFull + t), 1);
       mbar_init(bar(B::kPvDone + t), 1);
     }
@@ -660,7 +677,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
           }
           tmem_wait_st();
           tc_fence_before();
-          mbar_arrive(bar(B::kPFull + t * kPChunks + ch));
+          release_p(bar(B::kPFull + t * kPChunks + ch), lane);
         }
         float a0, a1, b0, b1;
         upk2(sum_a, a0, a1);
@@ -722,7 +739,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
         }
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(bar(B::kPFull + t));
+        release_p(bar(B::kPFull + t), lane);
       }
     }
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar(B::kOFull + t), 0, abort_flag));
