@@ -189,10 +189,15 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                                  _P, _P, _P, ctypes.POINTER(_P), _P]),
     "dgxm_quantize_e4m3_per_head": (ctypes.c_int, [_I32, _I32, _I32, _I32, _P,
                                                    ctypes.POINTER(ctypes.c_int64), _P, _P, _P]),
+    "dgxm_quantize_e4m3_per_head_masked": (ctypes.c_int, [_I32, _I32, _I32, _I32, _P,
+                                                          ctypes.POINTER(ctypes.c_int64), _P,
+                                                          ctypes.c_int64, _P, _P, _P]),
     "dgxm_ring_window_bytes": (ctypes.c_int64, [ctypes.POINTER(AttnDesc)]),
     "dgxm_ring_workspace_bytes": (ctypes.c_int64, [ctypes.POINTER(AttnDesc), _I32]),
     "dgxm_ring_attn_fwd": (ctypes.c_int, [_P, ctypes.POINTER(AttnDesc), _P, _P, _P, _P, _P, _P,
                                           ctypes.c_int64, _P]),
+    "dgxm_ring_attn_fwd_fp8": (ctypes.c_int, [_P, ctypes.POINTER(AttnDesc), _P, _P, _P, _P, _P, _P, _P,
+                                              _P, _P, ctypes.c_int64, _P]),
     "dgxm_ring_noalloc_max_bytes": (ctypes.c_int64, []),
     "dgxm_ring_attn_fwd_noalloc": (ctypes.c_int, [_P, ctypes.POINTER(AttnDesc), _P, _P, _P, _P, _P,
                                                   _P]),

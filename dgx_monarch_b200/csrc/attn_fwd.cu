@@ -506,9 +506,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
     if constexpr (FP8) sl2 *= p.q_descale[h] * p.k_descale[hk];
     float m_run = -INFINITY;  // running max of the scaled logits, log2 units
     float l_run = 0.f;        // this half's running sum of exp2(s * sl2 - m_run)
-    // EXTRA: this row's bias group (if any).
+    // EXTRA: this row's bias group (if any).  A bias is in logit units and is
+    // added to the raw dot products before they are scaled: divided by the
+    // softmax scale, and for e4m3 inputs also by the q and k descales the raw
+    // products leave out.
     const float* bias_row = nullptr;
     int bias_len = 0;
+    float bias_mul = p.inv_scale;
+    if constexpr (FP8 && EXTRA) bias_mul /= p.q_descale[h] * p.k_descale[hk];
     if constexpr (EXTRA) {
       const int qrow = row0 + t * kTileRows + r;
       for (int g = 0; g < p.n_bias; ++g) {
@@ -547,7 +552,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
         if (bias_row != nullptr) {
 #pragma unroll
           for (int i = 0; i < 64; ++i)
-            if (key0 + i < bias_len) s[i] += __ldg(bias_row + key0 + i) * p.inv_scale;
+            if (key0 + i < bias_len) s[i] += __ldg(bias_row + key0 + i) * bias_mul;
         }
         if (p.kmask != nullptr) {
           const uint32_t* km = p.kmask + static_cast<int64_t>(b) * p.kmask_sb;

@@ -237,6 +237,8 @@ struct QuantParams {
   int64_t sb, sl, sh;  // bytes
   uint8_t* out;        // contiguous (B, L, H, D) e4m3
   float* amax;         // per head: accumulated absmax, then rewritten as descale
+  const uint32_t* keep;  // optional row keep bits (bit l % 32 of word l / 32); cleared rows skip the absmax
+  int64_t keep_sb;       // words between batch rows of `keep` (0: one mask for every batch row)
   int batch, rows, heads;
 };
 
@@ -254,6 +256,9 @@ __global__ void __launch_bounds__(1024) absmax_kernel(const __grid_constant__ Qu
     for (int64_t br = blockIdx.x; br < rows; br += gridDim.x) {
       const int b = static_cast<int>(br / p.rows);
       const int l = static_cast<int>(br - static_cast<int64_t>(b) * p.rows);
+      // A pad row the attention will exclude does not set its head's scale:
+      // the scale is the one the real rows alone would give.
+      if (p.keep != nullptr && !((__ldg(p.keep + b * p.keep_sb + (l >> 5)) >> (l & 31)) & 1u)) continue;
       const uint4 raw = __ldg(reinterpret_cast<const uint4*>(p.x + b * p.sb + l * p.sl + h * p.sh) + part);
       const __nv_bfloat162* pr = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
@@ -372,10 +377,34 @@ extern "C" int dgxm_qkv_prologue_scatter(const dgxm_prologue_desc* d, const void
   return DGXM_OK;
 }
 
+namespace dgxm {
+static int quantize_e4m3_impl(int32_t batch, int32_t rows, int32_t heads, int32_t head_dim,
+                              const void* x, const int64_t* stride, const uint32_t* keep,
+                              int64_t keep_batch_stride, void* out, float* descale, void* stream);
+}  // namespace dgxm
+
 extern "C" int dgxm_quantize_e4m3_per_head(int32_t batch, int32_t rows, int32_t heads,
                                            int32_t head_dim, const void* x, const int64_t* stride,
                                            void* out, float* descale, void* stream) {
-  using namespace dgxm;
+  return dgxm::quantize_e4m3_impl(batch, rows, heads, head_dim, x, stride, nullptr, 0, out, descale,
+                                  stream);
+}
+
+extern "C" int dgxm_quantize_e4m3_per_head_masked(int32_t batch, int32_t rows, int32_t heads,
+                                                  int32_t head_dim, const void* x,
+                                                  const int64_t* stride, const uint32_t* keep,
+                                                  int64_t keep_batch_stride, void* out,
+                                                  float* descale, void* stream) {
+  if (keep == nullptr) return dgxm::fail(DGXM_ERR_INVALID, "NULL keep bits");
+  if (keep_batch_stride < 0) return dgxm::fail(DGXM_ERR_INVALID, "negative keep-bit batch stride");
+  return dgxm::quantize_e4m3_impl(batch, rows, heads, head_dim, x, stride, keep, keep_batch_stride,
+                                  out, descale, stream);
+}
+
+namespace dgxm {
+static int quantize_e4m3_impl(int32_t batch, int32_t rows, int32_t heads, int32_t head_dim,
+                              const void* x, const int64_t* stride, const uint32_t* keep,
+                              int64_t keep_batch_stride, void* out, float* descale, void* stream) {
   if (x == nullptr || out == nullptr || descale == nullptr || stride == nullptr)
     return fail(DGXM_ERR_INVALID, "NULL quantisation argument");
   if (head_dim != 128) return fail(DGXM_ERR_UNSUPPORTED, "quantisation head_dim must be 128");
@@ -393,6 +422,8 @@ extern "C" int dgxm_quantize_e4m3_per_head(int32_t batch, int32_t rows, int32_t 
   p.sh = stride[2] * 2;
   p.out = static_cast<uint8_t*>(out);
   p.amax = descale;
+  p.keep = keep;
+  p.keep_sb = keep_batch_stride;
   p.batch = batch;
   p.rows = rows;
   p.heads = heads;
@@ -410,3 +441,4 @@ extern "C" int dgxm_quantize_e4m3_per_head(int32_t batch, int32_t rows, int32_t 
   DGXM_CUDA_TRY(cudaGetLastError());
   return DGXM_OK;
 }
+}  // namespace dgxm

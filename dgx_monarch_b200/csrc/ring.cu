@@ -29,6 +29,13 @@ static int64_t ring_block_bytes(const dgxm_attn_desc* d) {
 
 static int64_t round256(int64_t x) { return (x + 255) / 256 * 256; }
 
+// One window slot holds a K or V block; an e4m3 block carries its per-head
+// fp32 descales right behind it, so they rotate with the block.
+static int64_t ring_slot_bytes(const dgxm_attn_desc* d) {
+  const int64_t descales = d->in_dtype == DGXM_DTYPE_E4M3 ? round256(int64_t(d->kv_heads) * 4) : 0;
+  return round256(ring_block_bytes(d)) + descales;
+}
+
 static int64_t ring_part_bytes(const dgxm_attn_desc* d) {
   return round256(static_cast<int64_t>(d->batch) * d->q_len * d->q_heads * d->head_dim * 4);
 }
@@ -64,7 +71,7 @@ static int check_comm_device(const dgxm_comm* c) {
 
 extern "C" int64_t dgxm_ring_window_bytes(const dgxm_attn_desc* d) {
   if (d == nullptr) return -1;
-  return 4 * dgxm::round256(dgxm::ring_block_bytes(d));
+  return 4 * dgxm::ring_slot_bytes(d);
 }
 
 extern "C" int64_t dgxm_ring_workspace_bytes(const dgxm_attn_desc* d, int32_t ring_world) {
@@ -75,9 +82,12 @@ extern "C" int64_t dgxm_ring_workspace_bytes(const dgxm_attn_desc* d, int32_t ri
 namespace dgxm {
 
 // The ring loop, partial results in `workspace` (any device memory of at
-// least dgxm_ring_workspace_bytes, 256-byte aligned).
+// least dgxm_ring_workspace_bytes, 256-byte aligned).  e4m3 inputs take
+// per-head fp32 descales: q's for the local rows, k's and v's for this
+// rank's block (each block keeps the scales it was quantised with).
 static int ring_attn_impl(dgxm_comm* c, const dgxm_attn_desc* d, const void* q, const void* k,
-                          const void* v, void* o, float* lse, void* workspace,
+                          const void* v, const float* q_descale, const float* k_descale,
+                          const float* v_descale, void* o, float* lse, void* workspace,
                           int64_t workspace_bytes, void* stream) {
   if (c == nullptr || d == nullptr) return fail(DGXM_ERR_INVALID, "NULL comm or descriptor");
   if (int rc0 = check_comm_device(c)) return rc0;
@@ -93,11 +103,18 @@ static int ring_attn_impl(dgxm_comm* c, const dgxm_attn_desc* d, const void* q, 
     return fail(DGXM_ERR_INVALID, "ring attention needs a contiguous (B, L, H, D) output");
   if (lse != nullptr && !contiguous_bhl(d->lse_stride, d))
     return fail(DGXM_ERR_INVALID, "ring attention needs a contiguous (B, H, L) lse");
-  if (world == 1) return dgxm_attn_fwd(d, q, k, v, nullptr, nullptr, nullptr, o, lse, stream);
-  if (d->in_dtype != DGXM_DTYPE_BF16 && d->in_dtype != DGXM_DTYPE_F16)
-    return fail(DGXM_ERR_UNSUPPORTED, "ring attention runs bf16 or f16 inputs");
+  const bool fp8 = d->in_dtype == DGXM_DTYPE_E4M3;
+  if (fp8 && (q_descale == nullptr || k_descale == nullptr || v_descale == nullptr))
+    return fail(DGXM_ERR_INVALID, "e4m3 ring attention takes q, k and v descales (dgxm_ring_attn_fwd_fp8)");
+  if (!fp8 && (q_descale != nullptr || k_descale != nullptr || v_descale != nullptr))
+    return fail(DGXM_ERR_INVALID, "descales belong to e4m3 inputs only");
+  if (world == 1) return dgxm_attn_fwd(d, q, k, v, q_descale, k_descale, v_descale, o, lse, stream);
+  if (d->in_dtype != DGXM_DTYPE_BF16 && d->in_dtype != DGXM_DTYPE_F16 && !fp8)
+    return fail(DGXM_ERR_UNSUPPORTED, "ring attention runs bf16, f16 or e4m3 inputs");
   const int64_t block = ring_block_bytes(d);
-  const int64_t slot = round256(block);
+  const int64_t slot = ring_slot_bytes(d);
+  const int64_t scales_at = round256(block);                       // descales inside a slot
+  const int64_t scale_bytes = int64_t(d->kv_heads) * 4;
   if (4 * slot > c->bytes)
     return fail(DGXM_ERR_INVALID, "comm window of %lld bytes is smaller than the %lld the ring needs",
                 (long long)c->bytes, (long long)(4 * slot));
@@ -131,6 +148,8 @@ static int ring_attn_impl(dgxm_comm* c, const dgxm_attn_desc* d, const void* q, 
 
   const char* cur_k = static_cast<const char*>(k);
   const char* cur_v = static_cast<const char*>(v);
+  const float* cur_kd = k_descale;
+  const float* cur_vd = v_descale;
   DGXM_CUDA_TRY(cudaEventRecord(c->ev_main, main));
   for (int t = 0; t < world; ++t) {
     const bool send = t < world - 1;
@@ -139,13 +158,19 @@ static int ring_attn_impl(dgxm_comm* c, const dgxm_attn_desc* d, const void* q, 
       DGXM_CUDA_TRY(cudaStreamWaitEvent(c->side, c->ev_main, 0));
       DGXM_CUDA_TRY(cudaMemcpyAsync(theirs + (2 * buf) * slot, cur_k, block, cudaMemcpyDefault, c->side));
       DGXM_CUDA_TRY(cudaMemcpyAsync(theirs + (2 * buf + 1) * slot, cur_v, block, cudaMemcpyDefault, c->side));
+      if (fp8) {
+        DGXM_CUDA_TRY(cudaMemcpyAsync(theirs + (2 * buf) * slot + scales_at, cur_kd, scale_bytes,
+                                      cudaMemcpyDefault, c->side));
+        DGXM_CUDA_TRY(cudaMemcpyAsync(theirs + (2 * buf + 1) * slot + scales_at, cur_vd, scale_bytes,
+                                      cudaMemcpyDefault, c->side));
+      }
       DGXM_CUDA_TRY(cudaEventRecord(c->ev_side, c->side));
     }
     void* po = parts_out + t * ring_part_bytes(d);
     float* pl = reinterpret_cast<float*>(parts_lse + t * ring_lse_bytes(d));
     outs[t] = po;
     lses[t] = pl;
-    rc = dgxm_attn_fwd(&step, q, cur_k, cur_v, nullptr, nullptr, nullptr, po, pl, main);
+    rc = dgxm_attn_fwd(&step, q, cur_k, cur_v, q_descale, cur_kd, cur_vd, po, pl, main);
     if (rc) return rc;
     if (send) {
       DGXM_CUDA_TRY(cudaStreamWaitEvent(main, c->ev_side, 0));
@@ -154,6 +179,10 @@ static int ring_attn_impl(dgxm_comm* c, const dgxm_attn_desc* d, const void* q, 
       DGXM_CUDA_TRY(cudaEventRecord(c->ev_main, main));
       cur_k = mine + (2 * buf) * slot;
       cur_v = mine + (2 * buf + 1) * slot;
+      if (fp8) {
+        cur_kd = reinterpret_cast<const float*>(mine + (2 * buf) * slot + scales_at);
+        cur_vd = reinterpret_cast<const float*>(mine + (2 * buf + 1) * slot + scales_at);
+      }
     }
   }
   // The last step attends the block in this rank's buffer (R - 2) % 2, and the
@@ -171,7 +200,19 @@ static int ring_attn_impl(dgxm_comm* c, const dgxm_attn_desc* d, const void* q, 
 extern "C" int dgxm_ring_attn_fwd(dgxm_comm* c, const dgxm_attn_desc* d, const void* q,
                                   const void* k, const void* v, void* o, float* lse,
                                   void* workspace, int64_t workspace_bytes, void* stream) {
-  return dgxm::ring_attn_impl(c, d, q, k, v, o, lse, workspace, workspace_bytes, stream);
+  return dgxm::ring_attn_impl(c, d, q, k, v, nullptr, nullptr, nullptr, o, lse, workspace,
+                              workspace_bytes, stream);
+}
+
+extern "C" int dgxm_ring_attn_fwd_fp8(dgxm_comm* c, const dgxm_attn_desc* d, const void* q,
+                                      const void* k, const void* v, const float* q_descale,
+                                      const float* k_descale, const float* v_descale, void* o,
+                                      float* lse, void* workspace, int64_t workspace_bytes,
+                                      void* stream) {
+  if (d != nullptr && d->in_dtype != DGXM_DTYPE_E4M3)
+    return dgxm::fail(DGXM_ERR_INVALID, "dgxm_ring_attn_fwd_fp8 takes e4m3 inputs");
+  return dgxm::ring_attn_impl(c, d, q, k, v, q_descale, k_descale, v_descale, o, lse, workspace,
+                              workspace_bytes, stream);
 }
 
 // ---------------------------------------------------------------- without allocation
@@ -215,7 +256,8 @@ extern "C" int dgxm_ring_attn_fwd_noalloc(dgxm_comm* c, const dgxm_attn_desc* d,
   if (c == nullptr || d == nullptr) return fail(DGXM_ERR_INVALID, "NULL comm or descriptor");
   if (int rc0 = check_comm_device(c)) return rc0;
   // One rank attends its own block: no partial results, so no scratch.
-  if (c->world == 1) return ring_attn_impl(c, d, q, k, v, o, lse, nullptr, 0, stream);
+  if (c->world == 1)
+    return ring_attn_impl(c, d, q, k, v, nullptr, nullptr, nullptr, o, lse, nullptr, 0, stream);
   const int64_t need = dgxm_ring_workspace_bytes(d, c->world);
   if (need < 0 || need > kRingStaticScratchBytes)
     return fail(DGXM_ERR_INVALID,
@@ -225,5 +267,6 @@ extern "C" int dgxm_ring_attn_fwd_noalloc(dgxm_comm* c, const dgxm_attn_desc* d,
   void* scratch = nullptr;
   const int rc = ring_static_scratch(&scratch);
   if (rc != DGXM_OK) return rc;
-  return ring_attn_impl(c, d, q, k, v, o, lse, scratch, kRingStaticScratchBytes, stream);
+  return ring_attn_impl(c, d, q, k, v, nullptr, nullptr, nullptr, o, lse, scratch,
+                        kRingStaticScratchBytes, stream);
 }

@@ -100,9 +100,14 @@ def qkv_gemm_prologue_scatter(x: torch.Tensor, w_qkv: torch.Tensor, dst_ptrs: li
 
 
 def quantize_e4m3_per_head(x: torch.Tensor, out: torch.Tensor | None = None,
-                           descale: torch.Tensor | None = None, stream=None):
-    """(e4m3 values, fp32 per-head descale = absmax / 448) of a bf16 (B, L, H, 128) tensor."""
-    _require_cuda(x, out, descale)
+                           descale: torch.Tensor | None = None, stream=None,
+                           keep: torch.Tensor | None = None):
+    """(e4m3 values, fp32 per-head descale = absmax / 448) of a bf16 (B, L, H, 128) tensor.
+
+    keep: optional row keep bits (ops.keep_bits: int32 words, (W,) for every
+    batch row or (B, W)); a cleared row does not count toward the absmax, so
+    the scale is the one the real rows alone give."""
+    _require_cuda(x, out, descale, keep)
     b, l, h, d = x.shape
     if x.dtype != torch.bfloat16 or x.stride(3) != 1:
         raise ValueError("quantisation input must be bf16 with contiguous head_dim")
@@ -116,7 +121,17 @@ def quantize_e4m3_per_head(x: torch.Tensor, out: torch.Tensor | None = None,
         raise ValueError(f"descale must be a contiguous fp32 vector of {h} heads")
     stride = (ctypes.c_int64 * 3)(x.stride(0), x.stride(1), x.stride(2))
     stream = stream or torch.cuda.current_stream(x.device)
-    _lib.check(_lib.load().dgxm_quantize_e4m3_per_head(b, l, h, d, x.data_ptr(), stride, out.data_ptr(),
-                                                       descale.data_ptr(), stream.cuda_stream),
-               "dgxm_quantize_e4m3_per_head")
+    if keep is None:
+        _lib.check(_lib.load().dgxm_quantize_e4m3_per_head(b, l, h, d, x.data_ptr(), stride,
+                                                           out.data_ptr(), descale.data_ptr(),
+                                                           stream.cuda_stream),
+                   "dgxm_quantize_e4m3_per_head")
+        return out, descale
+    words = (l + 31) // 32
+    if (keep.dtype != torch.int32 or keep.stride(-1) != 1 or keep.shape[-1] != words
+            or keep.ndim not in (1, 2) or (keep.ndim == 2 and keep.shape[0] != b)):
+        raise ValueError(f"keep must be int32 keep bits of shape ({words},) or ({b}, {words})")
+    _lib.check(_lib.load().dgxm_quantize_e4m3_per_head_masked(
+        b, l, h, d, x.data_ptr(), stride, keep.data_ptr(), keep.stride(0) if keep.ndim == 2 else 0,
+        out.data_ptr(), descale.data_ptr(), stream.cuda_stream), "dgxm_quantize_e4m3_per_head_masked")
     return out, descale

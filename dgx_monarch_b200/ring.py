@@ -16,7 +16,7 @@ import torch
 
 from . import _lib
 from .comm import PeerWindows
-from .ops import _ptr, _require_on, attn_desc, check_attn_buffers
+from .ops import _ptr, _require_on, attn_desc, check_attn_buffers, out16_dtype
 
 
 class RingAttention:
@@ -44,21 +44,35 @@ class RingAttention:
 
     def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
                 out: torch.Tensor | None = None, lse: torch.Tensor | None = None,
-                softmax_scale: float | None = None) -> tuple[torch.Tensor, torch.Tensor | None]:
+                softmax_scale: float | None = None, q_descale: torch.Tensor | None = None,
+                k_descale: torch.Tensor | None = None,
+                v_descale: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor | None]:
+        """e4m3 inputs (a ring planned with dtype float8_e4m3fn) take per-head
+        fp32 descales: q's for the local rows, k's and v's for this rank's
+        block; the output is bf16."""
         b, lq, h, d = q.shape
         if (b, lq, k.shape[1], h, k.shape[2], d) != self.shape or v.shape != k.shape:
             raise ValueError(f"ring planned for {self.shape}, called with q {tuple(q.shape)} k {tuple(k.shape)}")
-        _require_on(self.device, q, k, v)
-        check_attn_buffers(q, k, out=out, lse=lse)
+        _require_on(self.device, q, k, v, q_descale, k_descale, v_descale)
+        check_attn_buffers(q, k, out=out, lse=lse, q_descale=q_descale, k_descale=k_descale,
+                           v_descale=v_descale)
         k, v = k.contiguous(), v.contiguous()
         if out is None:
-            out = torch.empty(b, lq, h, d, device=self.device, dtype=q.dtype)
+            out = torch.empty(b, lq, h, d, device=self.device, dtype=out16_dtype(q.dtype))
         desc = attn_desc(q, k, v, out, lse, softmax_scale)
         stream = torch.cuda.current_stream(self.device)
-        _lib.check(_lib.load().dgxm_ring_attn_fwd(
-            self.windows._handle, ctypes.byref(desc), q.data_ptr(), k.data_ptr(), v.data_ptr(),
-            out.data_ptr(), _ptr(lse), self.workspace.data_ptr(), self.workspace_bytes,
-            stream.cuda_stream), "dgxm_ring_attn_fwd")
+        lib = _lib.load()
+        if q.dtype == torch.float8_e4m3fn:
+            _lib.check(lib.dgxm_ring_attn_fwd_fp8(
+                self.windows._handle, ctypes.byref(desc), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                _ptr(q_descale), _ptr(k_descale), _ptr(v_descale), out.data_ptr(), _ptr(lse),
+                self.workspace.data_ptr(), self.workspace_bytes, stream.cuda_stream),
+                "dgxm_ring_attn_fwd_fp8")
+        else:
+            _lib.check(lib.dgxm_ring_attn_fwd(
+                self.windows._handle, ctypes.byref(desc), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                out.data_ptr(), _ptr(lse), self.workspace.data_ptr(), self.workspace_bytes,
+                stream.cuda_stream), "dgxm_ring_attn_fwd")
         return out, lse
 
     def close(self) -> None:

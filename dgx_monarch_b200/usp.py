@@ -180,13 +180,14 @@ class B200SequenceParallelAttention:
         _check_pad_rows(k_l.shape[1] * p, kv_drop_rows)
         if p == 1 and g.ring_world == 1 and not self.fp8:
             return self._local(q_l, k_l, v_l, drop_rows, kv_drop_rows, bias_groups, softmax_scale)
-        if p == 1 and g.ring_world == 1 and not (drop_rows or kv_drop_rows or bias_groups):
-            return self._local_fp8(q_l, k_l, v_l, softmax_scale)
-        if self.fp8 and (g.ring_world > 1 or drop_rows or kv_drop_rows or bias_groups):
-            raise UnsupportedModelError(
-                "the B200 FP8 attention path runs pure Ulysses without pad rows; use the bf16 "
-                "kernel for ring topologies or padded sequences")
+        if p == 1 and g.ring_world == 1:
+            return self._local_fp8(q_l, k_l, v_l, drop_rows, kv_drop_rows, bias_groups, softmax_scale)
         if g.ring_world > 1:
+            if self.fp8 and self.full_context_ring and p == 1:
+                # adapters/wan_ring_full_context.py:10 admits fp16 and bf16 blocks only.
+                raise UnsupportedModelError(
+                    "the Wan Ring2 full-context path attends fp16 or bf16 blocks; run the FP8 "
+                    "kernel on the rotating ring or a Ulysses topology")
             return self._hybrid(q_l, k_l, v_l, softmax_scale)
         plan = self._ulysses_plan(b, ls, h, hkv, d, q_l.dtype)
         win, offs = plan["win"], plan["offs"]
@@ -204,12 +205,26 @@ class B200SequenceParallelAttention:
         if self.fp8:
             from .prologue import quantize_e4m3_per_head
 
-            for src, dst, ds in zip((qg, kg, vg), (plan["q8"], plan["k8"], plan["v8"]), plan["ds"]):
-                quantize_e4m3_per_head(src, out=dst, descale=ds)
-            attention_routed(plan["q8"], plan["k8"], plan["v8"], out_ptrs, (ls * h * d, h * d, d),
-                             world=p, rank=g.uly_rank, seq_local=ls, seg0=seg0,
-                             q_descale=plan["ds"][0], k_descale=plan["ds"][1], v_descale=plan["ds"][2],
-                             softmax_scale=softmax_scale)
+            # Pad rows neither attend nor set a head's scale, as when the
+            # reference hands its inner FP8 kernel the real rows only.
+            q_keep = keep_bits(qg.shape[1], drop_rows, qg.device)
+            k_keep = keep_bits(kg.shape[1], kv_drop_rows, qg.device)
+            for src, dst, ds, keep in zip((qg, kg, vg), (plan["q8"], plan["k8"], plan["v8"]), plan["ds"],
+                                          (q_keep, k_keep, k_keep)):
+                quantize_e4m3_per_head(src, out=dst, descale=ds, keep=keep)
+            descales = {"q_descale": plan["ds"][0], "k_descale": plan["ds"][1], "v_descale": plan["ds"][2]}
+            if not drop_rows and not kv_drop_rows and not bias_groups:
+                attention_routed(plan["q8"], plan["k8"], plan["v8"], out_ptrs, (ls * h * d, h * d, d),
+                                 world=p, rank=g.uly_rank, seq_local=ls, seg0=seg0,
+                                 softmax_scale=softmax_scale, **descales)
+            else:
+                attention_fwd_ext(plan["q8"], plan["k8"], plan["v8"], key_keep=k_keep, query_keep=q_keep,
+                                  bias_groups=_rank_bias(bias_groups, g.uly_rank, h // p,
+                                                         kg.shape[1], kv_drop_rows),
+                                  route={"o_peers": out_ptrs, "world": p, "rank": g.uly_rank,
+                                         "seq_local": ls, "seg0": seg0},
+                                  out_strides=(ls * h * d, h * d, d), softmax_scale=softmax_scale,
+                                  **descales)
         elif not drop_rows and not kv_drop_rows and not bias_groups:
             attention_routed(qg, kg, vg, out_ptrs, (ls * h * d, h * d, d), world=p, rank=g.uly_rank,
                              seq_local=ls, seg0=seg0, softmax_scale=softmax_scale)
@@ -237,9 +252,11 @@ class B200SequenceParallelAttention:
         out, _ = attention_fwd(q, k, v, return_lse=False, softmax_scale=softmax_scale)
         return out
 
-    def _local_fp8(self, q, k, v, softmax_scale=None):
+    def _local_fp8(self, q, k, v, drop_rows=None, kv_drop_rows=None, bias_groups=None,
+                   softmax_scale=None):
         """One rank, e4m3: quantise the caller's heads in place of a scatter
-        and attend into a fresh output (no window copy, no barrier)."""
+        and attend into a fresh output (no window copy, no barrier).  Pad rows
+        neither attend nor set a head's scale."""
         from .prologue import quantize_e4m3_per_head
 
         b, ls, h, d = q.shape
@@ -251,11 +268,20 @@ class B200SequenceParallelAttention:
                     "v8": torch.empty(v.shape, device=self.device, dtype=torch.float8_e4m3fn),
                     "ds": [torch.empty(x.shape[2], device=self.device, dtype=torch.float32) for x in (q, k, v)]}
             self._plans[key] = bufs
-        for src, dst, ds in zip((q, k, v), (bufs["q8"], bufs["k8"], bufs["v8"]), bufs["ds"]):
-            quantize_e4m3_per_head(src, out=dst, descale=ds)
-        out, _ = attention_fwd(bufs["q8"], bufs["k8"], bufs["v8"], q_descale=bufs["ds"][0],
-                               k_descale=bufs["ds"][1], v_descale=bufs["ds"][2], return_lse=False,
-                               softmax_scale=softmax_scale)
+        q_keep = keep_bits(q.shape[1], drop_rows, q.device)
+        k_keep = keep_bits(k.shape[1], kv_drop_rows, q.device)
+        for src, dst, ds, keep in zip((q, k, v), (bufs["q8"], bufs["k8"], bufs["v8"]), bufs["ds"],
+                                      (q_keep, k_keep, k_keep)):
+            quantize_e4m3_per_head(src, out=dst, descale=ds, keep=keep)
+        descales = {"q_descale": bufs["ds"][0], "k_descale": bufs["ds"][1], "v_descale": bufs["ds"][2]}
+        if drop_rows or kv_drop_rows or bias_groups:
+            out, _ = attention_fwd_ext(bufs["q8"], bufs["k8"], bufs["v8"], key_keep=k_keep, query_keep=q_keep,
+                                       bias_groups=_rank_bias(bias_groups, 0, q.shape[2], k.shape[1],
+                                                              kv_drop_rows),
+                                       softmax_scale=softmax_scale, **descales)
+            return out
+        out, _ = attention_fwd(bufs["q8"], bufs["k8"], bufs["v8"], return_lse=False,
+                               softmax_scale=softmax_scale, **descales)
         return out
 
     def _hybrid(self, q_l, k_l, v_l, softmax_scale=None):
@@ -274,8 +300,21 @@ class B200SequenceParallelAttention:
             qg, kg, vg = plan["recv"]
         else:
             qg, kg, vg = q_l, k_l, v_l
-        ring = self._ring_plan(b, qg.shape[1], kg.shape[1], qg.shape[2], kg.shape[2], d, q_l.dtype)
-        out_g, _ = ring.forward(qg, kg, vg, softmax_scale=softmax_scale)
+        if self.fp8:
+            # Each rank quantises its query rows and its own K/V block with
+            # per-head scales over exactly those rows; a block rotates with its
+            # scales, so every ring step attends under the scales an inner FP8
+            # kernel called on that block would take.
+            from .prologue import quantize_e4m3_per_head
+
+            ring = self._ring_plan(b, qg.shape[1], kg.shape[1], qg.shape[2], kg.shape[2], d,
+                                   torch.float8_e4m3fn)
+            (q8, qs), (k8, ks), (v8, vs) = (quantize_e4m3_per_head(t) for t in (qg, kg, vg))
+            out_g, _ = ring.forward(q8, k8, v8, softmax_scale=softmax_scale, q_descale=qs, k_descale=ks,
+                                    v_descale=vs)
+        else:
+            ring = self._ring_plan(b, qg.shape[1], kg.shape[1], qg.shape[2], kg.shape[2], d, q_l.dtype)
+            out_g, _ = ring.forward(qg, kg, vg, softmax_scale=softmax_scale)
         if p == 1:
             return out_g
         ulysses_gather(out_g, [win.peer_ptr(r, offs[3]) for r in range(p)], world=p, rank=g.uly_rank,

@@ -371,6 +371,20 @@ int dgxm_quantize_e4m3_per_head(int32_t batch, int32_t rows, int32_t heads, int3
                                 const void* x, const int64_t* stride, void* out, float* descale,
                                 void* stream);
 
+/*
+ * The same with row keep bits (int32 words, bit l % 32 of word l / 32 keeps
+ * row l; `keep_batch_stride` words between batch rows, 0 for one mask shared
+ * by every batch row): rows whose bit is clear do not count toward a head's
+ * absmax, and are still written (saturated to +-448 where they exceed it).
+ * The scale is then the one an attention over the real rows alone would
+ * quantise with -- the rows the reference's pad exclusion hands its inner
+ * kernel (adapters/usp_pad_exclusion.py:112-137).
+ */
+int dgxm_quantize_e4m3_per_head_masked(int32_t batch, int32_t rows, int32_t heads,
+                                       int32_t head_dim, const void* x, const int64_t* stride,
+                                       const uint32_t* keep, int64_t keep_batch_stride, void* out,
+                                       float* descale, void* stream);
+
 /* ------------------------------------------------------------ ring attention */
 /*
  * Ring attention over the ranks of `comm` (the ring group): every rank holds
@@ -381,7 +395,7 @@ int dgxm_quantize_e4m3_per_head(int32_t batch, int32_t rows, int32_t heads, int3
  * lse (may be NULL) is contiguous fp32 (B, H, Lq).  The comm window needs
  * dgxm_ring_window_bytes(desc); `workspace` (scratch owned by the caller,
  * 256-byte aligned) needs dgxm_ring_workspace_bytes(desc, R).  bf16 or f16
- * inputs.
+ * inputs; e4m3 inputs go through dgxm_ring_attn_fwd_fp8.
  *
  * Replaces the ring loop of xfuser/yunchang that adapters/base.py:320 reaches
  * when the ring degree exceeds one (block contract:
@@ -392,6 +406,21 @@ int64_t dgxm_ring_workspace_bytes(const dgxm_attn_desc* desc, int32_t ring_world
 int dgxm_ring_attn_fwd(dgxm_comm* comm, const dgxm_attn_desc* desc, const void* q, const void* k,
                        const void* v, void* o, float* lse, void* workspace,
                        int64_t workspace_bytes, void* stream);
+
+/*
+ * The same over e4m3 inputs (desc->in_dtype DGXM_DTYPE_E4M3, bf16 output):
+ * q_descale are the per-head fp32 descales of this rank's query rows,
+ * k_descale / v_descale those of this rank's key/value block.  Each block
+ * rotates with the descales it was quantised with (they ride behind it in
+ * the window slot), so every ring step attends one block under its own
+ * per-head scales -- what an inner FP8 kernel that quantises its own inputs
+ * sees when the reference's ring loop calls it block by block.  The partial
+ * results stay fp32 and merge by LSE as in dgxm_ring_attn_fwd.
+ */
+int dgxm_ring_attn_fwd_fp8(dgxm_comm* comm, const dgxm_attn_desc* desc, const void* q,
+                           const void* k, const void* v, const float* q_descale,
+                           const float* k_descale, const float* v_descale, void* o, float* lse,
+                           void* workspace, int64_t workspace_bytes, void* stream);
 
 /*
  * Ring attention that allocates nothing, for callers that cannot call

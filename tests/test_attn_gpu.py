@@ -245,6 +245,42 @@ def test_query_group_bias_matches_sdpa_with_additive_mask(lib):
         assert rel_l2(out[:, start:end], ref) <= BF16_REL_L2
 
 
+def test_fp8_extras_bias_groups_and_keep_masks(lib):
+    """The e4m3 extras kernel: a bias is in logit units, so it is added to
+    the raw e4m3 products divided by the softmax scale and the q and k
+    descales; key pads drop out and query pads come back as zeros.  Held to
+    fp32 attention over the dequantized inputs with the same biases."""
+    from dgx_monarch_b200.ops import attention_fwd_ext, keep_bits
+
+    g = torch.Generator(device="cuda").manual_seed(43)
+    rows, heads = 520, 2
+    q, k, v = (torch.randn(1, rows, heads, 128, device="cuda", generator=g).bfloat16() for _ in range(3))
+    (q8, qs), (k8, ks), (v8, vs) = (quantize_e4m3_per_head(t) for t in (q, k, v))
+    b0 = torch.randn(1, 1, 1, 300, device="cuda", generator=g) * 2.0
+    b2 = torch.randn(1, heads, 1, rows, device="cuda", generator=g)
+    groups = [(0, 200, b0), (200, 300, None), (300, rows, b2)]
+    drop = [5, 77, 519]
+    keep = keep_bits(rows, drop, q.device)
+    out, _ = attention_fwd_ext(q8, k8, v8, bias_groups=groups, key_keep=keep, query_keep=keep,
+                               q_descale=qs, k_descale=ks, v_descale=vs)
+    torch.cuda.synchronize()
+    deq = [x.float() * sc.view(1, 1, -1, 1) for x, sc in ((q8, qs), (k8, ks), (v8, vs))]
+    qf, kf, vf = (t.transpose(1, 2) for t in deq)
+    live = torch.ones(rows, dtype=torch.bool, device="cuda")
+    live[drop] = False
+    for start, end, bias in groups:
+        logits = qf[:, :, start:end] @ kf.transpose(-1, -2) / math.sqrt(128)
+        if bias is not None:
+            full = torch.zeros(1, bias.shape[1], bias.shape[2], rows, device="cuda")
+            full[..., :bias.shape[3]] = bias
+            logits = logits + full
+        logits[..., ~live] = float("-inf")
+        ref = (torch.softmax(logits, -1) @ vf).transpose(1, 2)
+        ref[:, ~live[start:end]] = 0
+        assert rel_l2(out[:, start:end], ref) <= FP8_REL_L2
+    assert torch.count_nonzero(out[:, drop]).item() == 0
+
+
 def test_row_with_only_excluded_keys_in_leading_blocks(lib):
     """One query row whose first 384 keys are excluded by its bias, beside
     rows that see every key: the row must attend the remaining keys (its

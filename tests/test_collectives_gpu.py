@@ -100,6 +100,70 @@ def test_emulated_ring_follows_the_oracle_block_order(lib):
         assert np.abs(lse.double().cpu().numpy() - want[r][1]).max() <= 2e-3
 
 
+def test_emulated_fp8_ring_with_per_block_scales(lib):
+    """The e4m3 ring's arithmetic on one GPU: every block quantised over its
+    own rows, each step an e4m3 attention with fp32 partials under the
+    block's descales, then the LSE merge; against fp32 attention over the
+    per-block dequantized axis."""
+    from dgx_monarch_b200.ops import attention_fwd, lse_merge
+    from tests.test_attn_gpu import FP8_REL_L2, quantize_e4m3_per_head, reference_attention
+
+    world, rows, heads = 3, 300, 2
+    g = torch.Generator(device="cuda").manual_seed(5)
+    q, k, v = ([torch.randn(1, rows, heads, 128, device="cuda", generator=g).bfloat16() for _ in range(world)]
+               for _ in range(3))
+    q8, k8, v8 = ([quantize_e4m3_per_head(t) for t in ts] for ts in (q, k, v))
+    deq = lambda qs: torch.cat([x.float() * sc.view(1, 1, -1, 1) for x, sc in qs], dim=1)
+    kd, vd = deq(k8), deq(v8)
+    for r in range(world):
+        parts = [attention_fwd(q8[r][0], k8[(r - t) % world][0], v8[(r - t) % world][0], q_descale=q8[r][1],
+                               k_descale=k8[(r - t) % world][1], v_descale=v8[(r - t) % world][1],
+                               out_dtype=torch.float32) for t in range(world)]
+        out, lse = lse_merge([p[0] for p in parts], [p[1] for p in parts])
+        torch.cuda.synchronize()
+        ref, ref_lse = reference_attention(deq([q8[r]]), kd, vd)
+        assert rel_l2(out, ref) <= FP8_REL_L2
+        assert (lse - ref_lse).abs().max().item() <= 5e-3
+
+
+def test_fp8_ring_entry_at_world_one_and_its_refusals(lib):
+    """A one-rank e4m3 ring is one e4m3 attention (bit-identical); e4m3
+    inputs without descales, descales with 16-bit inputs, and 16-bit inputs
+    through the e4m3 entry are refused before any launch."""
+    import ctypes
+
+    from dgx_monarch_b200 import _lib as L
+    from dgx_monarch_b200.ops import attention_fwd, attn_desc
+    from dgx_monarch_b200.ring import RingAttention
+    from tests.test_attn_gpu import quantize_e4m3_per_head
+
+    g = torch.Generator(device="cuda").manual_seed(6)
+    q, k, v = (torch.randn(1, 256, 2, 128, device="cuda", generator=g).bfloat16() for _ in range(3))
+    (q8, qs), (k8, ks), (v8, vs) = (quantize_e4m3_per_head(t) for t in (q, k, v))
+    ring = RingAttention(world=1, rank=0, batch=1, q_len=256, kv_len=256, heads=2, kv_heads=2, head_dim=128,
+                         device=q.device, generation=32, dtype=torch.float8_e4m3fn)
+    try:
+        out, _ = ring.forward(q8, k8, v8, q_descale=qs, k_descale=ks, v_descale=vs)
+        want, _ = attention_fwd(q8, k8, v8, q_descale=qs, k_descale=ks, v_descale=vs)
+        torch.cuda.synchronize()
+        assert out.dtype == torch.bfloat16 and torch.equal(out, want)
+        lib_ = L.load()
+        stream = torch.cuda.current_stream().cuda_stream
+        o = torch.empty_like(q)
+        d8 = attn_desc(q8, k8, v8, o, None)
+        rc = lib_.dgxm_ring_attn_fwd(ring.windows._handle, ctypes.byref(d8), q8.data_ptr(), k8.data_ptr(),
+                                     v8.data_ptr(), o.data_ptr(), None, ring.workspace.data_ptr(),
+                                     ring.workspace_bytes, stream)
+        assert rc == L.DGXM_ERR_INVALID and b"descales" in lib_.dgxm_last_error_message()
+        d16 = attn_desc(q, k, v, o, None)
+        rc = lib_.dgxm_ring_attn_fwd_fp8(ring.windows._handle, ctypes.byref(d16), q.data_ptr(), k.data_ptr(),
+                                         v.data_ptr(), qs.data_ptr(), ks.data_ptr(), vs.data_ptr(), o.data_ptr(),
+                                         None, ring.workspace.data_ptr(), ring.workspace_bytes, stream)
+        assert rc == L.DGXM_ERR_INVALID and b"e4m3" in lib_.dgxm_last_error_message()
+    finally:
+        ring.close()
+
+
 @pytest.mark.parametrize("dtype,rows,cols,stride", [
     (torch.bfloat16, 9728, 9216, 9216),   # the Flux/Krea2 activation, 16-byte rows
     (torch.float16, 1000, 1000, 1003),    # rows that break 16-byte alignment

@@ -177,6 +177,87 @@ def test_ring_across_gpus_matches_unsharded_attention():
     _spawn(_ring_case, min(torch.cuda.device_count(), 4))
 
 
+def _per_block_e4m3(t, world):
+    """(e4m3 blocks, descales, the dequantized whole axis) of a (1, world*L, H, D)
+    tensor cut into `world` row blocks, each quantised over its own rows."""
+    from tests.test_attn_gpu import quantize_e4m3_per_head
+
+    blocks = t.chunk(world, dim=1)
+    quant = [quantize_e4m3_per_head(b) for b in blocks]
+    deq = torch.cat([x.float() * sc.view(1, 1, -1, 1) for x, sc in quant], dim=1)
+    return quant, deq
+
+
+def _ring_fp8_case(rank, world, dev):
+    """e4m3 ring: every rank quantises its query rows and its K/V block with
+    per-head scales over those rows; the blocks rotate with their descales.
+    Held to fp32 attention over the per-block dequantized axis."""
+    check = Checks(rank)
+    from dgx_monarch_b200 import _lib
+    from dgx_monarch_b200.ring import RingAttention
+    from tests.test_attn_gpu import FP8_REL_L2, reference_attention, rel_l2
+
+    rows, heads = 500, 3
+    g = torch.Generator(device=dev).manual_seed(8)
+    q, k, v = (torch.randn(1, rows * world, heads, 128, device=dev, generator=g).bfloat16() for _ in range(3))
+    (qq, qd), (kq, kd), (vq, vd) = (_per_block_e4m3(t, world) for t in (q, k, v))
+    ring = RingAttention(world=world, rank=rank, batch=1, q_len=rows, kv_len=rows, heads=heads,
+                         kv_heads=heads, head_dim=128, device=dev, generation=3, dtype=torch.float8_e4m3fn)
+    for n in range(2):
+        lse = torch.empty(1, heads, rows, device=dev, dtype=torch.float32)
+        out, _ = ring.forward(qq[rank][0], kq[rank][0], vq[rank][0], lse=lse, q_descale=qq[rank][1],
+                              k_descale=kq[rank][1], v_descale=vq[rank][1])
+        torch.cuda.synchronize()
+        sl = slice(rank * rows, (rank + 1) * rows)
+        ref, ref_lse = reference_attention(qd[:, sl], kd, vd)
+        check(out.dtype == torch.bfloat16, f"output dtype {out.dtype}")
+        check.le(rel_l2(out, ref), FP8_REL_L2, f"fp8 ring call {n} rel l2")
+        check.le((lse - ref_lse).abs().max().item(), 5e-3, f"fp8 ring call {n} lse")
+    check(_lib.device_error() == 0, f"device error word {_lib.device_error()}")
+    ring.close()
+    check.close()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
+def test_fp8_ring_across_gpus_with_per_block_scales():
+    _spawn(_ring_fp8_case, min(torch.cuda.device_count(), 4))
+
+
+def _usp_fp8_ring_case(rank, world, dev):
+    """The FP8 drop-in over a pure ring group: each rank's rows and block are
+    quantised where they live, as the reference's ring loop hands an inner FP8
+    kernel one block at a time."""
+    from dgx_monarch_b200 import _lib
+    from dgx_monarch_b200.usp import make_b200_usp_attention
+    from tests.test_attn_gpu import FP8_REL_L2, reference_attention, rel_l2
+
+    check = Checks(rank)
+    attn = make_b200_usp_attention(ring_group=dist_world_group(), generation=43, device=dev, fp8=True)
+    heads, ls = 4, 384
+    g = torch.Generator(device=dev).manual_seed(79)
+    q, k, v = (torch.randn(1, ls * world, heads, 128, device=dev, generator=g).bfloat16() for _ in range(3))
+    rows = slice(rank * ls, (rank + 1) * ls)
+    (_, qd), (_, kd), (_, vd) = (_per_block_e4m3(t, world) for t in (q, k, v))
+    out = attn(*(t[:, rows].reshape(1, ls, -1) for t in (q, k, v)), heads=heads)
+    torch.cuda.synchronize()
+    ref, _ = reference_attention(qd[:, rows], kd, vd)
+    check.le(rel_l2(out.reshape(1, ls, heads, 128), ref), FP8_REL_L2, "fp8 ring drop-in rel l2")
+    check(_lib.device_error() == 0, f"device error word {_lib.device_error()}")
+    attn.impl.invalidate()
+    check.close()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
+def test_fp8_drop_in_over_a_ring_group():
+    _spawn(_usp_fp8_ring_case, min(torch.cuda.device_count(), 4))
+
+
+def dist_world_group():
+    import torch.distributed as dist
+
+    return dist.group.WORLD
+
+
 def _callable_case(rank, world, dev):
     """The drop-in usp_attention on a Ulysses group: plain, joint order with
     pad rows, and native GQA, against unsharded attention."""

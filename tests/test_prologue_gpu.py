@@ -146,6 +146,40 @@ def test_quantize_is_bit_exact_against_torch(lib, shape):
     assert torch.equal(q8.view(torch.uint8), want.view(torch.uint8))
 
 
+@pytest.mark.parametrize("shape,drop,per_batch", [
+    ((1, 333, 3), [7, 40, 331, 332], False),     # scattered pads and a tail
+    ((2, 4608, 24), list(range(4600, 4608)), False),
+    ((2, 96, 2), None, True),                    # one mask per batch row, one row all pads
+])
+def test_quantize_with_keep_bits_skips_pad_rows(lib, shape, drop, per_batch):
+    """Rows whose keep bit is clear do not set their head's scale: the
+    scale is the absmax over the kept rows / 448, and every row (pads
+    included, saturated) is written with it."""
+    from dgx_monarch_b200.ops import keep_bits
+    from dgx_monarch_b200.prologue import quantize_e4m3_per_head
+
+    b, l, h = shape
+    g = torch.Generator(device="cuda").manual_seed(l)
+    x = torch.randn(b, l, h, 128, device="cuda", generator=g).bfloat16()
+    if per_batch:
+        keep = torch.stack([keep_bits(l, list(range(0, l, 3)), x.device), keep_bits(l, list(range(l)), x.device)])
+        kept = torch.ones(b, l, dtype=torch.bool, device="cuda")
+        kept[0, 0::3] = False
+        kept[1] = False
+    else:
+        keep = keep_bits(l, drop, x.device)
+        kept = torch.ones(b, l, dtype=torch.bool, device="cuda")
+        kept[:, drop] = False
+    x[~kept] = x[~kept] * 50  # pads far above the real rows' range
+    q8, descale = quantize_e4m3_per_head(x, keep=keep)
+    torch.cuda.synchronize()
+    amax = (x.float().abs() * kept.view(b, l, 1, 1)).amax(dim=(0, 1, 3)).clamp_min(1e-12)
+    want_scale = amax / torch.full_like(amax, 448.0)
+    want = (x.float() / want_scale.view(1, 1, -1, 1)).clamp(-448, 448).to(torch.float8_e4m3fn)
+    assert torch.equal(descale, want_scale)
+    assert torch.equal(q8.view(torch.uint8), want.view(torch.uint8))
+
+
 def _within_ulps(got, want, ulps):
     g, w = got.float(), want.float()
     tol = ulps * 2.0 ** -7 * torch.maximum(g.abs(), w.abs()) + 1e-5

@@ -187,6 +187,28 @@ def test_fp8_callable_on_one_rank(lib):
     attn.impl.invalidate()
 
 
+def test_fp8_callable_excludes_pad_rows(lib):
+    """FP8 with divisibility pads at Ulysses degree 1: as the reference hands
+    its inner kernel the real rows only (adapters/usp_pad_exclusion.py:112-137),
+    pad rows neither attend nor set a head's e4m3 scale, and come back as
+    zeros."""
+    from dgx_monarch_b200.usp import make_b200_usp_attention
+    from tests.test_attn_gpu import FP8_REL_L2, fp8_references
+
+    attn = make_b200_usp_attention(fp8=True)
+    q, k, v = _qkv(1, 640, 4, 4, 22)
+    drop = list(range(632, 640))
+    q, k, v = (t.clone() for t in (q, k, v))
+    for t in (q, k, v):
+        t[:, drop] = 40.0  # pad content far outside the real rows' range
+    out = attn(*(t.reshape(1, 640, -1) for t in (q, k, v)), heads=4, drop_rows=drop).reshape(1, 640, 4, 128)
+    real = slice(0, 632)
+    ref_deq, _ = fp8_references(q[:, real], k[:, real], v[:, real])
+    assert rel_l2(out[:, real], ref_deq) <= FP8_REL_L2
+    assert torch.count_nonzero(out[:, drop]).item() == 0
+    attn.impl.invalidate()
+
+
 @pytest.mark.parametrize("head_dim", [64, 96])
 def test_small_head_dims_run_zero_padded(attn, head_dim):
     """Heads below 128 (LTX-Video's 64) run zero-padded with the scale of their
