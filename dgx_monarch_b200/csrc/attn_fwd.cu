@@ -78,16 +78,18 @@ constexpr int kHeadDim = 128;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
-template <bool FP8, bool F16 = false>
+// HD: the head dimension, 128 or (16-bit inputs) 64.
+template <bool FP8, bool F16 = false, int HD = kHeadDim>
 struct AttnCfg {
+  static_assert(HD == 128 || (HD == 64 && !FP8), "head dimension 128, or 64 for 16-bit inputs");
   static constexpr int kEltBytes = FP8 ? 1 : 2;
   static constexpr int kBoxCols = 128 / kEltBytes;          // elements in one 128-byte row
-  static constexpr int kBoxes = kHeadDim / kBoxCols;        // 128-byte column blocks per tile
+  static constexpr int kBoxes = HD / kBoxCols;              // 128-byte column blocks per tile
   static constexpr int kBoxBytes = kTileRows * 128;         // 16 KB
-  static constexpr int kTileBytes = kBoxes * kBoxBytes;     // one 128 x 128 tile
-  static constexpr int kStages = FP8 ? 8 : 4;
+  static constexpr int kTileBytes = kBoxes * kBoxBytes;     // one 128-row tile
+  static constexpr int kStages = (FP8 || HD == 64) ? 8 : 4;
   static constexpr int kMmaK = FP8 ? 32 : 16;               // K extent of one MMA
-  static constexpr int kKSteps = kHeadDim / kMmaK;          // MMAs per 128-deep product
+  static constexpr int kKSteps = HD / kMmaK;                // MMAs per Q K^T product
   static constexpr int kPCols = kTileRows * kEltBytes / 4;  // TMEM columns holding P
   // Stale-max threshold (log2 units) below which the running max is kept and
   // O is not rescaled; P values then stay below 2^kThr.
@@ -100,7 +102,7 @@ struct AttnCfg {
   // P takes the inputs' 16-bit format, so A and B of P.V always match.
   static constexpr uint32_t kFmt = FP8 ? 0u : (F16 ? 0u : 1u);
   static constexpr uint32_t kIdescQK = idesc_make(128, 128, kFmt, false);
-  static constexpr uint32_t kIdescPV = idesc_make(128, 128, kFmt, true);
+  static constexpr uint32_t kIdescPV = idesc_make(128, HD, kFmt, true);
   static constexpr int kSmemBytes = 1024 /*align slack*/ + 2 * kTileBytes + kStages * kTileBytes +
                                     1024 /*barriers + slots*/ + 12 * 128 * 4 /*row exchange*/;
 };
@@ -192,9 +194,9 @@ __device__ __forceinline__ uint64_t sdesc_join(uint32_t lo, uint32_t hi) {
 
 // S = Q K^T: both operands K-major, one 128-byte swizzle atom per 64 (bf16)
 // or 128 (e4m3) head-dim columns.  q_lo / k_lo are the tiles' low words.
-template <bool FP8, bool F16>
+template <bool FP8, bool F16, int HD>
 __device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_lo, uint32_t k_lo) {
-  using C = AttnCfg<FP8, F16>;
+  using C = AttnCfg<FP8, F16, HD>;
   constexpr uint32_t hi = sdesc_hi(1024);
 #pragma unroll
   for (int kk = 0; kk < C::kKSteps; ++kk) {
@@ -212,10 +214,10 @@ __device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_lo, uint32_
 // O += P V: P from tensor memory, V MN-major (head_dim along the 128-byte
 // rows, keys down the rows; the second 128-byte column block of bf16 sits
 // kBoxBytes further, the leading byte offset).
-template <bool FP8, bool F16>
+template <bool FP8, bool F16, int HD>
 __device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_lo,
                                          bool accumulate) {
-  using C = AttnCfg<FP8, F16>;
+  using C = AttnCfg<FP8, F16, HD>;
   constexpr uint32_t hi = sdesc_hi(1024);
 #pragma unroll
   for (int kk = 0; kk < C::kKSteps; ++kk) {
@@ -233,10 +235,10 @@ __device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint3
 // both column halves c, K = 64 / kPChunks -- the probabilities one chunk of
 // every softmax thread has stored.  The first step of chunk 0 starts the
 // accumulation when `accumulate` is false.
-template <bool FP8, bool F16, int kPChunks>
+template <bool FP8, bool F16, int HD, int kPChunks>
 __device__ __forceinline__ void issue_pv_chunk(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_lo,
                                                bool accumulate, int ch) {
-  using C = AttnCfg<FP8, F16>;
+  using C = AttnCfg<FP8, F16, HD>;
   constexpr uint32_t hi = sdesc_hi(1024);
   constexpr int kKeys = 64 / kPChunks;         // keys of one column half in one chunk
   constexpr int kSteps = kKeys / C::kMmaK;     // MMAs per column half per chunk
@@ -259,7 +261,7 @@ __device__ __forceinline__ void issue_pv_chunk(uint32_t d_tmem, uint32_t p_tmem,
 
 // O += P V of one tile, chunk by chunk as the softmax releases P: each chunk
 // waits for its own barrier.  Returns false when a wait gave up.
-template <bool FP8, bool F16, int kPChunks, int kBarPFull>
+template <bool FP8, bool F16, int HD, int kPChunks, int kBarPFull>
 __device__ __forceinline__ bool issue_pv_chunks(uint64_t* bars, uint32_t d_tmem, uint32_t p_tmem,
                                                 uint32_t v_lo, bool accumulate, int parity,
                                                 volatile int* abort_flag) {
@@ -267,7 +269,7 @@ __device__ __forceinline__ bool issue_pv_chunks(uint64_t* bars, uint32_t d_tmem,
   for (int ch = 0; ch < kPChunks; ++ch) {
     if (!mbar_wait(smem_u32(&bars[kBarPFull + ch]), parity, abort_flag)) return false;
     tc_fence_after();
-    issue_pv_chunk<FP8, F16, kPChunks>(d_tmem, p_tmem, v_lo, accumulate, ch);
+    issue_pv_chunk<FP8, F16, HD, kPChunks>(d_tmem, p_tmem, v_lo, accumulate, ch);
   }
   return true;
 }
@@ -292,9 +294,9 @@ __device__ __forceinline__ void raise_abort(volatile int* abort_flag, int bits) 
 
 // F16: 16-bit inputs (and P) are fp16 instead of bf16; a 16-bit output is
 // then fp16 too.
-template <bool FP8, bool OUT_F32, bool EXTRA, int NCH, bool F16>
+template <bool FP8, bool OUT_F32, bool EXTRA, int NCH, bool F16, int HD>
 __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_constant__ AttnParams p) {
-  using C = AttnCfg<FP8, F16>;
+  using C = AttnCfg<FP8, F16, HD>;
   constexpr int kPChunks = p_chunks<FP8, NCH>();
   using B = Bars<C::kStages, kPChunks>;
   extern __shared__ uint8_t smem_raw[];
@@ -415,19 +417,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
           if (!(ok = mbar_wait(bar(B::kPvDone + 0), (j - 1) & 1, abort_flag))) break;
           tc_fence_after();
         }
-        issue_qk<FP8, F16>(tS0, q0_lo, kv_lo_k + ks * kStageLo);
+        issue_qk<FP8, F16, HD>(tS0, q0_lo, kv_lo_k + ks * kStageLo);
         umma_commit(bar(B::kSFull + 0));
         // O1 += P1 V_{j-1}
         if (j > 0) {
           const int vs = (2 * j - 1) % C::kStages;
           if constexpr (kPChunks > 1) {
-            if (!(ok = issue_pv_chunks<FP8, F16, kPChunks, B::kPFull + kPChunks>(
+            if (!(ok = issue_pv_chunks<FP8, F16, HD, kPChunks, B::kPFull + kPChunks>(
                       bars, tO1, tS1, kv_lo_v + vs * kStageLo, j - 1 > 0, (j - 1) & 1, abort_flag)))
               break;
           } else {
             if (!(ok = mbar_wait(bar(B::kPFull + 1), (j - 1) & 1, abort_flag))) break;
             tc_fence_after();
-            issue_pv<FP8, F16>(tO1, tS1, kv_lo_v + vs * kStageLo, j - 1 > 0);
+            issue_pv<FP8, F16, HD>(tO1, tS1, kv_lo_v + vs * kStageLo, j - 1 > 0);
           }
           umma_commit(bar(B::kKvEmpty + vs));
           if (safe_order) {
@@ -437,7 +439,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
           }
         }
         // S1 = Q1 K_j^T
-        issue_qk<FP8, F16>(tS1, q1_lo, kv_lo_k + ks * kStageLo);
+        issue_qk<FP8, F16, HD>(tS1, q1_lo, kv_lo_k + ks * kStageLo);
         umma_commit(bar(B::kSFull + 1));
         umma_commit(bar(B::kKvEmpty + ks));
         // O0 += P0 V_j
@@ -445,13 +447,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
         const int vs = vi % C::kStages;
         if (!(ok = mbar_wait(bar(B::kKvFull + vs), (vi / C::kStages) & 1, abort_flag))) break;
         if constexpr (kPChunks > 1) {
-          if (!(ok = issue_pv_chunks<FP8, F16, kPChunks, B::kPFull>(bars, tO0, tS0, kv_lo_v + vs * kStageLo, j > 0,
+          if (!(ok = issue_pv_chunks<FP8, F16, HD, kPChunks, B::kPFull>(bars, tO0, tS0, kv_lo_v + vs * kStageLo, j > 0,
                                                      j & 1, abort_flag)))
             break;
         } else {
           if (!(ok = mbar_wait(bar(B::kPFull + 0), j & 1, abort_flag))) break;
           tc_fence_after();
-          issue_pv<FP8, F16>(tO0, tS0, kv_lo_v + vs * kStageLo, j > 0);
+          issue_pv<FP8, F16, HD>(tO0, tS0, kv_lo_v + vs * kStageLo, j > 0);
         }
         if (safe_order) umma_commit(bar(B::kPvDone + 0));
         if (j == nkv - 1) umma_commit(bar(B::kOFull + 0));
@@ -460,13 +462,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
         // O1 += P1 V_{n-1}
         const int vs = (2 * nkv - 1) % C::kStages;
         if constexpr (kPChunks > 1) {
-          ok = issue_pv_chunks<FP8, F16, kPChunks, B::kPFull + kPChunks>(bars, tO1, tS1, kv_lo_v + vs * kStageLo,
+          ok = issue_pv_chunks<FP8, F16, HD, kPChunks, B::kPFull + kPChunks>(bars, tO1, tS1, kv_lo_v + vs * kStageLo,
                                                             nkv - 1 > 0, (nkv - 1) & 1, abort_flag);
         } else {
           ok = mbar_wait(bar(B::kPFull + 1), (nkv - 1) & 1, abort_flag);
           if (ok) {
             tc_fence_after();
-            issue_pv<FP8, F16>(tO1, tS1, kv_lo_v + vs * kStageLo, nkv - 1 > 0);
+            issue_pv<FP8, F16, HD>(tO1, tS1, kv_lo_v + vs * kStageLo, nkv - 1 > 0);
           }
         }
         if (ok) {
@@ -500,7 +502,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
     const int xbar_threads = DGXM_SM_PAIR_BARRIER ? 64 : 256;
     const uint32_t tS = tmem + lane_off + t * 128 + c * 64;
     const uint32_t tP = tmem + lane_off + t * 128 + c * (C::kPCols / 2);
-    const uint32_t tO = tmem + lane_off + 256 + t * 128 + c * 64;
+    const uint32_t tO = tmem + lane_off + 256 + t * 128 + c * (HD / 2);  // this half's output columns
     float* xmax = reinterpret_cast<float*>(ctrl + kCtrlXmaxOffset);  // [2 parity][2 tile][2 half][128]
     float sl2 = p.scale_log2;
     if constexpr (FP8) sl2 *= p.q_descale[h] * p.k_descale[hk];
@@ -670,7 +672,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
             // P_t V product.  Eight columns at a time, because the later
             // chunks' logits are still held in registers.
 #pragma unroll
-            for (int h8 = 0; h8 < 8; ++h8) {
+            for (int h8 = 0; h8 < HD / 16; ++h8) {
               uint32_t o[8];
               tmem_ld8(tO + h8 * 8, o);
               tmem_wait_ld();
@@ -732,7 +734,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
           // O_t is quiescent here: the commit behind this S_t also covered the
           // previous P_t V product.
 #pragma unroll
-          for (int h2 = 0; h2 < 2; ++h2) {
+          for (int h2 = 0; h2 < HD / 64; ++h2) {
             uint32_t o[32];
             tmem_ld32(tO + h2 * 32, o);
             tmem_wait_ld();
@@ -818,9 +820,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
       const int64_t ooff = (static_cast<int64_t>(b) * osb + static_cast<int64_t>(orow_idx) * p.o_sl +
                             static_cast<int64_t>(ohead) * p.o_sh) *
                                (OUT_F32 ? 4 : 2) +
-                           c * 64 * (OUT_F32 ? 4 : 2);
+                           c * (HD / 2) * (OUT_F32 ? 4 : 2);
 #pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
+      for (int h2 = 0; h2 < HD / 64; ++h2) {
         uint32_t o[32];
         tmem_ld32(tO + h2 * 32, o);
         tmem_wait_ld();
@@ -870,11 +872,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
   }
 }
 
-template <bool FP8, bool OUT_F32, bool EXTRA, int NCH, bool F16 = false>
+template <bool FP8, bool OUT_F32, bool EXTRA, int NCH, bool F16 = false, int HD = kHeadDim>
 static int launch_attn(const AttnParams& prm, dim3 grid, cudaStream_t stream) {
-  using C = AttnCfg<FP8, F16>;
+  using C = AttnCfg<FP8, F16, HD>;
   static std::atomic<uint64_t> configured{0};  // one bit per device ordinal
-  auto kern = attn_fwd_kernel<FP8, OUT_F32, EXTRA, NCH, F16>;
+  auto kern = attn_fwd_kernel<FP8, OUT_F32, EXTRA, NCH, F16, HD>;
   DGXM_CUDA_TRY(set_smem_limit_once(kern, C::kSmemBytes, configured));
   kern<<<grid, kAttnThreads, C::kSmemBytes, stream>>>(prm);
   DGXM_CUDA_TRY(cudaGetLastError());
@@ -896,8 +898,9 @@ static int prepare_attn(const dgxm_attn_desc* d, const void* q, const void* k, c
   if (d->batch < 0 || d->q_len < 0 || d->kv_len < 0 || d->q_heads <= 0 || d->kv_heads <= 0)
     return fail(DGXM_ERR_INVALID, "negative or zero attention extent (batch=%d q_len=%d kv_len=%d "
                 "q_heads=%d kv_heads=%d)", d->batch, d->q_len, d->kv_len, d->q_heads, d->kv_heads);
-  if (d->head_dim != kHeadDim)
-    return fail(DGXM_ERR_UNSUPPORTED, "head_dim %d is not supported (this build runs 128)",
+  if (d->head_dim != kHeadDim && !(d->head_dim == 64 && d->in_dtype != DGXM_DTYPE_E4M3))
+    return fail(DGXM_ERR_UNSUPPORTED,
+                "head_dim %d is not supported (this build runs 128, and 64 for 16-bit inputs)",
                 d->head_dim);
   if (d->q_heads % d->kv_heads != 0)
     return fail(DGXM_ERR_INVALID, "query heads (%d) must be divisible by key/value heads (%d)",
@@ -940,13 +943,13 @@ static int prepare_attn(const dgxm_attn_desc* d, const void* q, const void* k, c
   const int eb = fp8 ? 1 : 2;
   const int box_cols = 128 / eb;
   int rc;
-  if ((rc = encode_map_4d(&prm.tmap_q, q, dt, eb, kHeadDim, d->q_heads, d->q_len, d->batch,
+  if ((rc = encode_map_4d(&prm.tmap_q, q, dt, eb, d->head_dim, d->q_heads, d->q_len, d->batch,
                           d->q_stride[2], d->q_stride[1], d->q_stride[0], box_cols, kTileRows)))
     return rc;
-  if ((rc = encode_map_4d(&prm.tmap_k, k, dt, eb, kHeadDim, d->kv_heads, d->kv_len, d->batch,
+  if ((rc = encode_map_4d(&prm.tmap_k, k, dt, eb, d->head_dim, d->kv_heads, d->kv_len, d->batch,
                           d->k_stride[2], d->k_stride[1], d->k_stride[0], box_cols, kTileRows)))
     return rc;
-  if ((rc = encode_map_4d(&prm.tmap_v, v, dt, eb, kHeadDim, d->kv_heads, d->kv_len, d->batch,
+  if ((rc = encode_map_4d(&prm.tmap_v, v, dt, eb, d->head_dim, d->kv_heads, d->kv_len, d->batch,
                           d->v_stride[2], d->v_stride[1], d->v_stride[0], box_cols, kTileRows)))
     return rc;
   prm.o = o;
@@ -992,6 +995,15 @@ static int dispatch_attn_t(const dgxm_attn_desc* d, const AttnParams& prm, dim3 
   int nch = (d->flags & DGXM_ATTN_P_CHUNKS_MASK) >> DGXM_ATTN_P_CHUNKS_SHIFT;
   if (nch != 0 && nch != 1 && nch != 2 && nch != 4)
     return fail(DGXM_ERR_INVALID, "%d P chunks per block (1, 2 or 4)", nch);
+  if (d->head_dim == 64) {
+    // Head dimension 64 (16-bit inputs): the library's default release of P.
+    const bool f32 = d->out_dtype == DGXM_DTYPE_F32;
+    if (d->in_dtype == DGXM_DTYPE_F16)
+      return f32 ? launch_attn<false, true, EXTRA, DGXM_SM_P_CHUNKS, true, 64>(prm, grid, st)
+                 : launch_attn<false, false, EXTRA, DGXM_SM_P_CHUNKS, true, 64>(prm, grid, st);
+    return f32 ? launch_attn<false, true, EXTRA, DGXM_SM_P_CHUNKS, false, 64>(prm, grid, st)
+               : launch_attn<false, false, EXTRA, DGXM_SM_P_CHUNKS, false, 64>(prm, grid, st);
+  }
   if (d->in_dtype == DGXM_DTYPE_F16) {
     // fp16 inputs run the library's default release of P.
     if (d->out_dtype == DGXM_DTYPE_F32)

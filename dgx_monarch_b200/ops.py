@@ -67,6 +67,14 @@ def _require_on(device: torch.device, *tensors: torch.Tensor | None) -> None:
         raise RuntimeError(f"a tensor on {dev} was passed to an operation set up on cuda:{want}")
 
 
+def kernel_head_dim(head_dim: int, *, fp8: bool = False, ring: bool = False) -> int:
+    """The head dimension a caller's head_dim runs at: 64 for head
+    dimensions up to 64 on 16-bit inputs (a native kernel), else 128.  A
+    smaller head_dim is zero-padded up to it, which is exact.  The e4m3
+    kernel and the ring's merge run 128 only."""
+    return 64 if head_dim <= 64 and not fp8 and not ring else 128
+
+
 def check_attn_buffers(q: torch.Tensor, k: torch.Tensor, *, out: torch.Tensor | None = None,
                        lse: torch.Tensor | None = None, q_descale: torch.Tensor | None = None,
                        k_descale: torch.Tensor | None = None,

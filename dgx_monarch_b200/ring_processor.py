@@ -7,8 +7,9 @@ processor for this because the stock flash path rounds the block LSE to the
 query dtype (adapters/cudnn_ring_attention.py:61-89); `B200RingBlockProcessor`
 is the same contract on the tcgen05 kernel: (q, k, v) blocks of (B, L, H, D)
 fp16 or bf16 in, the block output in the inputs' dtype and its natural-log
-LSE in fp32 (B, H, L) out.  Head dimensions below 128 (multiples of 8) run
-zero-padded with the scale of their own head dimension.
+LSE in fp32 (B, H, L) out.  Head dimensions up to 64 run on the head-dim-64
+kernel, larger ones below 128 (multiples of 8) zero-padded to 128, with the
+scale of their own head dimension.
 
 The reference admits a processor only after two live checks, restated here on
 this kernel:
@@ -35,7 +36,7 @@ import torch
 from .usp import UnsupportedModelError
 
 KERNEL_NAME = "B200_SP"
-KERNEL_HEAD_DIM = 128           # the kernel's head dimension; smaller ones are zero-padded
+KERNEL_HEAD_DIM = 128           # the largest head dimension; smaller ones run at 64 or 128
 HEAD_DIM_LIMIT = {KERNEL_NAME: KERNEL_HEAD_DIM}  # the capability-table entry this kernel adds
 PROBE_SHAPE = (1, 128, 2)       # batch, tokens, heads of the capability probe
 _DTYPES = (torch.float16, torch.bfloat16)
@@ -121,13 +122,14 @@ class B200RingBlockProcessor:
         if head_dim > KERNEL_HEAD_DIM or head_dim % 8:
             raise _refuse(f"{KERNEL_NAME} carries head dimensions up to {KERNEL_HEAD_DIM} in multiples of "
                           f"8, and this block has {head_dim}. Run this workflow on a cfg or single topology.")
-        from .ops import attention_fwd
+        from .ops import attention_fwd, kernel_head_dim
 
         scale = float(softmax_scale) if softmax_scale is not None else 1.0 / math.sqrt(head_dim)
-        if head_dim < KERNEL_HEAD_DIM:
+        dk = kernel_head_dim(head_dim)
+        if head_dim < dk:
             # Zero columns add exact zeros to every logit and give zero output
             # columns, which are dropped.
-            pad = (0, KERNEL_HEAD_DIM - head_dim)
+            pad = (0, dk - head_dim)
             q, k, v = (torch.nn.functional.pad(t, pad) for t in (q, k, v))
         elif any(t.stride(-1) != 1 for t in (q, k, v)):
             q, k, v = (t.contiguous() for t in (q, k, v))

@@ -22,7 +22,8 @@ import torch
 
 from . import _lib
 from .comm import PeerWindows
-from .ops import _dtype_code, _ptr, _require_cuda, attention_fwd, attn_flags, out16_dtype
+from .ops import (_dtype_code, _ptr, _require_cuda, attention_fwd, attn_flags, kernel_head_dim,
+                  out16_dtype)
 
 
 def a2a_desc(n_tensors, world, rank, batch, seq_local, heads, head_dim, dtype, strides, seg0=0):
@@ -269,9 +270,10 @@ class JointUlyssesAttention:
     The step computes in `compute_dtype` (bf16, or fp16 for fp16 models):
     inputs of any float dtype are rounded to it and the outputs are returned
     in the inputs' own dtype, so an fp32 caller gets attention over its inputs
-    rounded to bf16.  A head_dim below 128 (a multiple of 8) runs zero-padded to 128:
-    the padded columns add exact zeros to every logit and give zero output
-    columns, which are dropped; the softmax scale stays 1/sqrt(head_dim).
+    rounded to bf16.  Head dimensions up to 64 run on the head-dim-64 kernel,
+    larger ones below 128 (multiples of 8) zero-padded to 128: padded columns
+    add exact zeros to every logit and give zero output columns, which are
+    dropped; the softmax scale stays 1/sqrt(head_dim).
     """
 
     KERNEL_HEAD_DIM = 128
@@ -296,7 +298,7 @@ class JointUlyssesAttention:
         self.hl = heads // world
         self.text_first = text_first
         self.scale = softmax_scale or 1.0 / math.sqrt(head_dim)
-        dk = self.KERNEL_HEAD_DIM
+        self.dk = dk = kernel_head_dim(head_dim)
         self.rows = txt_rows + world * seq_local
         self.dt = dt = compute_dtype
         recv_bytes = batch * self.rows * self.hl * dk * 2
@@ -343,7 +345,7 @@ class JointUlyssesAttention:
         w.barrier()
         from .ops import attention_fwd_ext
 
-        dk = self.KERNEL_HEAD_DIM
+        dk = self.dk
         route = {"o_peers": [w.peer_ptr(r, self.off_img) for r in range(p)], "world": p,
                  "rank": self.rank, "seq_local": self.ls,
                  "txt_rows": self.t, "txt_front": self.text_first,

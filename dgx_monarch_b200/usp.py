@@ -33,7 +33,7 @@ import torch
 
 from ._lib import MAX_BIAS_GROUPS
 from .comm import PeerWindows
-from .ops import attention_fwd, attention_fwd_ext, keep_bits
+from .ops import attention_fwd, attention_fwd_ext, keep_bits, kernel_head_dim
 from .ring import FullContextRingAttention, RingAttention
 from .ulysses import attention_routed, ulysses_gather, ulysses_scatter
 
@@ -487,9 +487,10 @@ def make_b200_usp_attention(*, ulysses_group=None, ring_group=None, generation: 
             if h % kv_heads:
                 raise UnsupportedModelError(
                     f"GQA query heads ({h}) must be divisible by K/V heads ({kv_heads})")
-            if kv_heads % impl.groups.uly_world or impl.groups.ring_world > 1:
-                # The kernel maps query heads to shared K/V heads natively; only a
-                # K/V head count the Ulysses degree cannot split is expanded.
+            if kv_heads % impl.groups.uly_world:
+                # The kernel maps query heads to shared K/V heads natively, and
+                # the ring rotates the shared K/V heads alone; only a K/V head
+                # count the Ulysses degree cannot split is expanded.
                 rep = h // kv_heads
                 k_l = k_l.repeat_interleave(rep, dim=2)
                 v_l = v_l.repeat_interleave(rep, dim=2)
@@ -537,16 +538,16 @@ def make_b200_usp_attention(*, ulysses_group=None, ring_group=None, generation: 
             compute = torch.bfloat16
         if q_l.dtype != compute or k_l.dtype != compute or v_l.dtype != compute:
             q_l, k_l, v_l = (t.to(compute) for t in (q_l, k_l, v_l))
-        if head_dim < KERNEL_HEAD_DIM:
+        dk = kernel_head_dim(head_dim, fp8=impl.fp8, ring=impl.groups.ring_world > 1)
+        if head_dim < dk:
             # Zero columns add exact zeros to every logit and give zero output
             # columns; the scale stays that of the real head dimension.
-            q_l, k_l, v_l = (torch.nn.functional.pad(t, (0, KERNEL_HEAD_DIM - head_dim))
-                             for t in (q_l, k_l, v_l))
+            q_l, k_l, v_l = (torch.nn.functional.pad(t, (0, dk - head_dim)) for t in (q_l, k_l, v_l))
         q_l, k_l, v_l = (t if t.stride(-1) == 1 else t.contiguous() for t in (q_l, k_l, v_l))
         kv_rows = drop_rows if kv_drop_rows is None else kv_drop_rows
         out = impl.attend(q_l, k_l, v_l, drop_rows, kv_rows, sequence_order, query_bias_groups,
                           softmax_scale=1.0 / math.sqrt(head_dim))
-        if head_dim < KERNEL_HEAD_DIM:
+        if head_dim < dk:
             out = out[..., :head_dim]
         out = out.to(q.dtype)
         if skip_output_reshape:

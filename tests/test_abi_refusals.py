@@ -45,7 +45,8 @@ def _status(lib, rc, code, needle):
 
 
 @pytest.mark.parametrize("kw,code,needle", [
-    ({"head_dim": 64}, 2, "head_dim 64"),
+    ({"head_dim": 96}, 2, "head_dim 96"),
+    ({"head_dim": 64, "in_dtype": 2}, 2, "head_dim 64"),   # e4m3 runs 128 only
     ({"q_heads": 3}, 1, "divisible"),
     ({"kv_len": 0}, 1, "empty key axis"),
     ({"q_len": -1}, 1, "negative"),

@@ -168,7 +168,7 @@ def test_invalid_arguments_raise_before_launch(lib):
     from dgx_monarch_b200._lib import DgxmError
     from dgx_monarch_b200.ops import attention_fwd
 
-    q = torch.randn(1, 64, 2, 64, device="cuda").bfloat16()
+    q = torch.randn(1, 64, 2, 96, device="cuda").bfloat16()
     with pytest.raises(DgxmError, match="head_dim"):
         attention_fwd(q, q, q)
     q = torch.randn(1, 64, 3, 128, device="cuda").bfloat16()
@@ -473,3 +473,60 @@ def test_mixed_16bit_formats_are_refused(lib):
     parts = [torch.zeros(1, 64, 2, 128, device="cuda", dtype=torch.float16)]
     with pytest.raises(DgxmError, match="f16 parts into a bf16"):
         lse_merge(parts, [torch.zeros(1, 2, 64, device="cuda")], out_dtype=torch.bfloat16)
+
+
+@pytest.mark.parametrize("dtype,shape,out_f32", [
+    (torch.bfloat16, (1, 256, 256, 2, 2), False),
+    (torch.bfloat16, (2, 1000, 777, 4, 2), True),     # ragged tiles, GQA, fp32 out
+    (torch.float16, (1, 4096, 4096, 3, 3), False),
+    (torch.bfloat16, (1, 9000, 9000, 2, 1), False),   # 71 key blocks, MQA
+])
+def test_head_dim_64_matches_fp32_reference(lib, dtype, shape, out_f32):
+    """The head-dim-64 kernel (16-bit inputs): Q·Kᵀ over 64 dims, O of 64
+    columns, 8 K/V stages of 16 KB; against fp32 attention, out and LSE."""
+    from dgx_monarch_b200.ops import attention_fwd
+
+    b, lq, lk, h, hkv = shape
+    g = torch.Generator(device="cuda").manual_seed(lq + 64)
+    q = torch.randn(b, lq, h, 64, device="cuda", generator=g).to(dtype)
+    k = torch.randn(b, lk, hkv, 64, device="cuda", generator=g).to(dtype)
+    v = torch.randn(b, lk, hkv, 64, device="cuda", generator=g).to(dtype)
+    out, lse = attention_fwd(q, k, v, out_dtype=torch.float32 if out_f32 else None)
+    torch.cuda.synchronize()
+    ref, ref_lse = reference_attention(q, k, v)
+    tol = BF16_REL_L2 if dtype == torch.bfloat16 else 2e-3
+    assert out.shape == (b, lq, h, 64)
+    assert out.dtype == (torch.float32 if out_f32 else dtype)
+    assert rel_l2(out, ref) <= tol
+    assert (out.float() - ref).abs().max().item() <= BF16_MAX_ABS
+    assert (lse - ref_lse).abs().max().item() <= LSE_ABS
+
+
+def test_head_dim_64_extras_and_padding_agree(lib):
+    """Keep masks and a bias group on the head-dim-64 kernel, and the same
+    heads zero-padded to 128 on the 128 kernel: both against fp32 attention."""
+    from dgx_monarch_b200.ops import attention_fwd, attention_fwd_ext, keep_bits
+
+    g = torch.Generator(device="cuda").manual_seed(640)
+    rows, heads = 700, 2
+    q, k, v = (torch.randn(1, rows, heads, 64, device="cuda", generator=g).bfloat16() for _ in range(3))
+    bias = torch.randn(1, heads, 1, rows, device="cuda", generator=g)
+    drop = [3, 350, 699]
+    keep = keep_bits(rows, drop, q.device)
+    out, _ = attention_fwd_ext(q, k, v, key_keep=keep, query_keep=keep, bias_groups=[(100, 400, bias)])
+    torch.cuda.synchronize()
+    live = torch.ones(rows, dtype=torch.bool, device="cuda")
+    live[drop] = False
+    qf, kf, vf = (t.float().transpose(1, 2) for t in (q, k, v))
+    logits = qf @ kf.transpose(-1, -2) / math.sqrt(64)
+    logits[:, :, 100:400] += bias
+    logits[..., ~live] = float("-inf")
+    ref = (torch.softmax(logits, -1) @ vf).transpose(1, 2)
+    ref[:, ~live] = 0
+    assert rel_l2(out, ref) <= BF16_REL_L2
+    assert torch.count_nonzero(out[:, drop]).item() == 0
+    pad = [torch.nn.functional.pad(t, (0, 64)) for t in (q, k, v)]
+    padded, _ = attention_fwd(*pad, softmax_scale=1.0 / math.sqrt(64))
+    native, _ = attention_fwd(q, k, v)
+    torch.cuda.synchronize()
+    assert rel_l2(native, padded[..., :64]) <= BF16_REL_L2

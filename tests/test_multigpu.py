@@ -252,6 +252,35 @@ def test_fp8_drop_in_over_a_ring_group():
     _spawn(_usp_fp8_ring_case, min(torch.cuda.device_count(), 4))
 
 
+def _usp_gqa_ring_case(rank, world, dev):
+    """GQA over a ring group: the ring rotates the shared K/V heads alone (no
+    expansion), and the result equals attention with K/V repeated per group."""
+    from dgx_monarch_b200 import _lib
+    from dgx_monarch_b200.usp import make_b200_usp_attention
+    from tests.test_attn_gpu import BF16_REL_L2, reference_attention, rel_l2
+
+    check = Checks(rank)
+    attn = make_b200_usp_attention(ring_group=dist_world_group(), generation=44, device=dev)
+    heads, kv_heads, ls = 4, 2, 320
+    g = torch.Generator(device=dev).manual_seed(81)
+    q = torch.randn(1, ls * world, heads, 128, device=dev, generator=g).bfloat16()
+    k, v = (torch.randn(1, ls * world, kv_heads, 128, device=dev, generator=g).bfloat16() for _ in range(2))
+    rows = slice(rank * ls, (rank + 1) * ls)
+    out = attn(q[:, rows].reshape(1, ls, -1), k[:, rows].reshape(1, ls, -1), v[:, rows].reshape(1, ls, -1),
+               heads=heads, enable_gqa=True)
+    torch.cuda.synchronize()
+    ref, _ = reference_attention(q, k.repeat_interleave(2, dim=2), v.repeat_interleave(2, dim=2))
+    check.le(rel_l2(out.reshape(1, ls, heads, 128), ref[:, rows]), BF16_REL_L2, "gqa ring rel l2")
+    check(_lib.device_error() == 0, f"device error word {_lib.device_error()}")
+    attn.impl.invalidate()
+    check.close()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
+def test_gqa_drop_in_over_a_ring_group_without_expansion():
+    _spawn(_usp_gqa_ring_case, min(torch.cuda.device_count(), 4))
+
+
 def dist_world_group():
     import torch.distributed as dist
 

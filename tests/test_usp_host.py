@@ -36,8 +36,11 @@ def _callable_with_oracle_attend(seen, head_dim):
     return attn
 
 
-@pytest.mark.parametrize("head_dim,heads,kv_heads", [(64, 4, 4), (72, 3, 3), (96, 4, 2), (128, 2, 2)])
-def test_small_heads_are_padded_with_their_own_scale(head_dim, heads, kv_heads):
+@pytest.mark.parametrize("head_dim,heads,kv_heads,runs_at", [
+    (40, 2, 2, 64), (64, 4, 4, 64), (72, 3, 3, 128), (96, 4, 2, 128), (128, 2, 2, 128)])
+def test_small_heads_are_padded_with_their_own_scale(head_dim, heads, kv_heads, runs_at):
+    """Head dimensions up to 64 run at the kernel's 64, larger ones at 128;
+    the padding is zeros and the scale stays that of the caller's head_dim."""
     seen = []
     attn = _callable_with_oracle_attend(seen, head_dim)
     g = torch.Generator().manual_seed(head_dim)
@@ -46,8 +49,8 @@ def test_small_heads_are_padded_with_their_own_scale(head_dim, heads, kv_heads):
     v = torch.randn(1, 40, kv_heads * head_dim, generator=g)
     out = attn(q, k, v, heads=heads, enable_gqa=kv_heads != heads)
     (call,) = seen
-    assert call["shape"] == (1, 40, heads, 128)
-    assert call["kv_shape"][-1] == 128
+    assert call["shape"] == (1, 40, heads, runs_at)
+    assert call["kv_shape"][-1] == runs_at
     assert call["dtype"] == torch.bfloat16
     assert call["pad_max"] == 0.0
     assert call["scale"] == pytest.approx(1.0 / math.sqrt(head_dim))
