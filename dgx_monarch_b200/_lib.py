@@ -137,6 +137,21 @@ class QkvGemmDesc(ctypes.Structure):
 NORM_NONE, NORM_HIDDEN, NORM_HEAD = 0, 1, 2
 
 
+class QuantItem(ctypes.Structure):
+    _fields_ = [
+        ("batch", ctypes.c_int32),
+        ("rows", ctypes.c_int32),
+        ("heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("x", ctypes.c_void_p),
+        ("stride", ctypes.c_int64 * 3),
+        ("keep", ctypes.c_void_p),
+        ("keep_batch_stride", ctypes.c_int64),
+        ("out", ctypes.c_void_p),
+        ("descale", ctypes.c_void_p),
+    ]
+
+
 class PrologueDesc(ctypes.Structure):
     _fields_ = [
         ("world", ctypes.c_int32),
@@ -189,6 +204,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                                  _P, _P, _P, ctypes.POINTER(_P), _P]),
     "dgxm_quantize_e4m3_per_head": (ctypes.c_int, [_I32, _I32, _I32, _I32, _P,
                                                    ctypes.POINTER(ctypes.c_int64), _P, _P, _P]),
+    "dgxm_quantize_e4m3_per_head_batch": (ctypes.c_int, [_I32, ctypes.POINTER(QuantItem), _P]),
     "dgxm_quantize_e4m3_per_head_masked": (ctypes.c_int, [_I32, _I32, _I32, _I32, _P,
                                                           ctypes.POINTER(ctypes.c_int64), _P,
                                                           ctypes.c_int64, _P, _P, _P]),

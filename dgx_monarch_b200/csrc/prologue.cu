@@ -242,12 +242,21 @@ struct QuantParams {
   int batch, rows, heads;
 };
 
+// Up to three tensors (q, k, v) quantised by the same launches: blockIdx.y
+// picks the tensor, so one call fills the GPU with all three.
+constexpr int kMaxQuantItems = 3;
+struct QuantBatch {
+  QuantParams t[kMaxQuantItems];
+  int n;
+};
+
 // Per-head absmax.  Thread (h, part) of a block owns 16 bytes of head h in
 // every row the block visits, keeps a running max in a register, reduces it
 // over the head's 16 lanes with shuffles, and issues one atomicMax per head
 // per block -- not one per 16 bytes, which would serialise on 'heads'
 // addresses.  Non-negative floats order like their bit patterns.
-__global__ void __launch_bounds__(1024) absmax_kernel(const __grid_constant__ QuantParams p) {
+__global__ void __launch_bounds__(1024) absmax_kernel(const __grid_constant__ QuantBatch pb) {
+  const QuantParams& p = pb.t[blockIdx.y];
   const int slot = threadIdx.x;         // h * 16 + part
   const int h = slot / 16, part = slot % 16;
   float m = 0.f;
@@ -276,7 +285,8 @@ __global__ void __launch_bounds__(1024) absmax_kernel(const __grid_constant__ Qu
 
 // Blocks stride over (batch, row); threads over the row's (head, 16-byte
 // part) vectors, so the index math is a shift and a mask per vector.
-__global__ void __launch_bounds__(256) quantize_e4m3_kernel(const __grid_constant__ QuantParams p) {
+__global__ void __launch_bounds__(256) quantize_e4m3_kernel(const __grid_constant__ QuantBatch pb) {
+  const QuantParams& p = pb.t[blockIdx.y];
   const int per_row = p.heads * 16;
   for (int64_t row = blockIdx.x; row < static_cast<int64_t>(p.batch) * p.rows; row += gridDim.x) {
     const int b = static_cast<int>(row / p.rows);
@@ -301,9 +311,10 @@ __global__ void __launch_bounds__(256) quantize_e4m3_kernel(const __grid_constan
   }
 }
 
-__global__ void descale_kernel(float* amax, int heads) {
+__global__ void descale_kernel(const __grid_constant__ QuantBatch pb) {
+  const QuantParams& p = pb.t[blockIdx.y];
   const int h = blockIdx.x * blockDim.x + threadIdx.x;
-  if (h < heads) amax[h] = fmaxf(amax[h], 1e-12f) / 448.f;
+  if (h < p.heads) p.amax[h] = fmaxf(p.amax[h], 1e-12f) / 448.f;
 }
 
 }  // namespace dgxm
@@ -378,16 +389,73 @@ extern "C" int dgxm_qkv_prologue_scatter(const dgxm_prologue_desc* d, const void
 }
 
 namespace dgxm {
-static int quantize_e4m3_impl(int32_t batch, int32_t rows, int32_t heads, int32_t head_dim,
-                              const void* x, const int64_t* stride, const uint32_t* keep,
-                              int64_t keep_batch_stride, void* out, float* descale, void* stream);
+// Checks of one quantisation item; fills its kernel parameters.
+static int quant_item(const dgxm_quant_item& it, QuantParams* p) {
+  if (it.x == nullptr || it.out == nullptr || it.descale == nullptr)
+    return fail(DGXM_ERR_INVALID, "NULL quantisation argument");
+  if (it.head_dim != 128) return fail(DGXM_ERR_UNSUPPORTED, "quantisation head_dim must be 128");
+  if (it.batch < 0 || it.rows < 0 || it.heads <= 0) return fail(DGXM_ERR_INVALID, "bad extents");
+  if (it.heads > 64)
+    return fail(DGXM_ERR_UNSUPPORTED, "quantisation supports up to 64 heads, got %d", it.heads);
+  if (reinterpret_cast<uintptr_t>(it.x) % 16 || reinterpret_cast<uintptr_t>(it.out) % 16 ||
+      (it.stride[0] * 2) % 16 || (it.stride[1] * 2) % 16 || (it.stride[2] * 2) % 16)
+    return fail(DGXM_ERR_INVALID, "quantisation tensors must be 16-byte aligned");
+  if (it.keep_batch_stride < 0) return fail(DGXM_ERR_INVALID, "negative keep-bit batch stride");
+  p->x = static_cast<const char*>(it.x);
+  p->sb = it.stride[0] * 2;
+  p->sl = it.stride[1] * 2;
+  p->sh = it.stride[2] * 2;
+  p->out = static_cast<uint8_t*>(it.out);
+  p->amax = it.descale;
+  p->keep = it.keep;
+  p->keep_sb = it.keep_batch_stride;
+  p->batch = it.batch;
+  p->rows = it.rows;
+  p->heads = it.heads;
+  return DGXM_OK;
+}
+
+// Every item is checked before anything is launched; then one memset per
+// descale vector and three launches cover all items.
+static int quantize_e4m3_batch(int32_t n, const dgxm_quant_item* items, void* stream) {
+  if (items == nullptr || n < 1 || n > kMaxQuantItems)
+    return fail(DGXM_ERR_INVALID, "quantisation batches take 1 to %d items, got %d", kMaxQuantItems, n);
+  QuantBatch pb;
+  memset(&pb, 0, sizeof(pb));
+  int64_t max_rows = 0;
+  int max_heads = 1;
+  for (int i = 0; i < n; ++i) {
+    if (int rc = quant_item(items[i], &pb.t[i])) return rc;
+    max_rows = std::max<int64_t>(max_rows, static_cast<int64_t>(items[i].batch) * items[i].rows);
+    max_heads = std::max(max_heads, static_cast<int>(items[i].heads));
+  }
+  pb.n = n;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  for (int i = 0; i < n; ++i)
+    DGXM_CUDA_TRY(cudaMemsetAsync(items[i].descale, 0, sizeof(float) * items[i].heads, st));
+  if (max_rows == 0) return DGXM_OK;
+  int dev = 0, sms = 148;
+  DGXM_CUDA_TRY(cudaGetDevice(&dev));
+  DGXM_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  // Blocks beyond an item's rows find no work in their stride loop.
+  const int amax_blocks = static_cast<int>(std::min<int64_t>(max_rows, int64_t(sms) * 4));
+  const int amax_threads = (max_heads * 16 + 31) / 32 * 32;
+  absmax_kernel<<<dim3(amax_blocks, n), amax_threads, 0, st>>>(pb);
+  const int qblocks = static_cast<int>(std::min<int64_t>(max_rows, int64_t(sms) * 8));
+  quantize_e4m3_kernel<<<dim3(qblocks, n), 256, 0, st>>>(pb);
+  descale_kernel<<<dim3(1, n), 64, 0, st>>>(pb);
+  DGXM_CUDA_TRY(cudaGetLastError());
+  return DGXM_OK;
+}
 }  // namespace dgxm
 
 extern "C" int dgxm_quantize_e4m3_per_head(int32_t batch, int32_t rows, int32_t heads,
                                            int32_t head_dim, const void* x, const int64_t* stride,
                                            void* out, float* descale, void* stream) {
-  return dgxm::quantize_e4m3_impl(batch, rows, heads, head_dim, x, stride, nullptr, 0, out, descale,
-                                  stream);
+  if (stride == nullptr) return dgxm::fail(DGXM_ERR_INVALID, "NULL quantisation argument");
+  dgxm_quant_item it{batch, rows, heads, head_dim, x, {stride[0], stride[1], stride[2]},
+                     nullptr, 0, out, descale};
+  return dgxm::quantize_e4m3_batch(1, &it, stream);
 }
 
 extern "C" int dgxm_quantize_e4m3_per_head_masked(int32_t batch, int32_t rows, int32_t heads,
@@ -396,49 +464,13 @@ extern "C" int dgxm_quantize_e4m3_per_head_masked(int32_t batch, int32_t rows, i
                                                   int64_t keep_batch_stride, void* out,
                                                   float* descale, void* stream) {
   if (keep == nullptr) return dgxm::fail(DGXM_ERR_INVALID, "NULL keep bits");
-  if (keep_batch_stride < 0) return dgxm::fail(DGXM_ERR_INVALID, "negative keep-bit batch stride");
-  return dgxm::quantize_e4m3_impl(batch, rows, heads, head_dim, x, stride, keep, keep_batch_stride,
-                                  out, descale, stream);
+  if (stride == nullptr) return dgxm::fail(DGXM_ERR_INVALID, "NULL quantisation argument");
+  dgxm_quant_item it{batch, rows, heads, head_dim, x, {stride[0], stride[1], stride[2]},
+                     keep, keep_batch_stride, out, descale};
+  return dgxm::quantize_e4m3_batch(1, &it, stream);
 }
 
-namespace dgxm {
-static int quantize_e4m3_impl(int32_t batch, int32_t rows, int32_t heads, int32_t head_dim,
-                              const void* x, const int64_t* stride, const uint32_t* keep,
-                              int64_t keep_batch_stride, void* out, float* descale, void* stream) {
-  if (x == nullptr || out == nullptr || descale == nullptr || stride == nullptr)
-    return fail(DGXM_ERR_INVALID, "NULL quantisation argument");
-  if (head_dim != 128) return fail(DGXM_ERR_UNSUPPORTED, "quantisation head_dim must be 128");
-  if (batch < 0 || rows < 0 || heads <= 0) return fail(DGXM_ERR_INVALID, "bad extents");
-  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(out) % 16 ||
-      (stride[0] * 2) % 16 || (stride[1] * 2) % 16 || (stride[2] * 2) % 16)
-    return fail(DGXM_ERR_INVALID, "quantisation tensors must be 16-byte aligned");
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  DGXM_CUDA_TRY(cudaMemsetAsync(descale, 0, sizeof(float) * heads, st));
-  if (batch == 0 || rows == 0) return DGXM_OK;
-  QuantParams p;
-  p.x = static_cast<const char*>(x);
-  p.sb = stride[0] * 2;
-  p.sl = stride[1] * 2;
-  p.sh = stride[2] * 2;
-  p.out = static_cast<uint8_t*>(out);
-  p.amax = descale;
-  p.keep = keep;
-  p.keep_sb = keep_batch_stride;
-  p.batch = batch;
-  p.rows = rows;
-  p.heads = heads;
-  int dev = 0, sms = 148;
-  DGXM_CUDA_TRY(cudaGetDevice(&dev));
-  DGXM_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-  if (heads > 64) return fail(DGXM_ERR_UNSUPPORTED, "quantisation supports up to 64 heads, got %d", heads);
-  const int64_t nrows = static_cast<int64_t>(batch) * rows;
-  const int amax_blocks = static_cast<int>(nrows < int64_t(sms) * 4 ? nrows : int64_t(sms) * 4);
-  const int amax_threads = (heads * 16 + 31) / 32 * 32;
-  absmax_kernel<<<amax_blocks, amax_threads, 0, st>>>(p);
-  const int qblocks = static_cast<int>(nrows < int64_t(sms) * 8 ? nrows : int64_t(sms) * 8);
-  quantize_e4m3_kernel<<<qblocks, 256, 0, st>>>(p);
-  descale_kernel<<<(heads + 127) / 128, 128, 0, st>>>(descale, heads);
-  DGXM_CUDA_TRY(cudaGetLastError());
-  return DGXM_OK;
+extern "C" int dgxm_quantize_e4m3_per_head_batch(int32_t n, const dgxm_quant_item* items,
+                                                 void* stream) {
+  return dgxm::quantize_e4m3_batch(n, items, stream);
 }
-}  // namespace dgxm

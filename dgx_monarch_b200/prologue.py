@@ -135,3 +135,48 @@ def quantize_e4m3_per_head(x: torch.Tensor, out: torch.Tensor | None = None,
         b, l, h, d, x.data_ptr(), stride, keep.data_ptr(), keep.stride(0) if keep.ndim == 2 else 0,
         out.data_ptr(), descale.data_ptr(), stream.cuda_stream), "dgxm_quantize_e4m3_per_head_masked")
     return out, descale
+
+
+def quantize_e4m3_per_head_many(items, stream=None):
+    """Quantise up to three bf16 (B, L, H, 128) tensors in the same launches
+    (dgxm_quantize_e4m3_per_head_batch): items are (x, out, descale, keep)
+    tuples as quantize_e4m3_per_head takes them (out, descale and keep may be
+    None).  Returns [(e4m3 values, fp32 descale)] in item order."""
+    items = list(items)
+    if not 1 <= len(items) <= 3:
+        raise ValueError("quantisation batches take 1 to 3 tensors")
+    arr = (_lib.QuantItem * len(items))()
+    results = []
+    dev = None
+    for slot, (x, out, descale, keep) in zip(arr, items):
+        d = _require_cuda(x, out, descale, keep)
+        if dev is not None and d != dev:
+            raise RuntimeError("every tensor of one quantisation batch must live on one device")
+        dev = d
+        b, l, h, hd = x.shape
+        if x.dtype != torch.bfloat16 or x.stride(3) != 1:
+            raise ValueError("quantisation input must be bf16 with contiguous head_dim")
+        if out is None:
+            out = torch.empty(b, l, h, hd, device=x.device, dtype=torch.float8_e4m3fn)
+        elif tuple(out.shape) != (b, l, h, hd) or out.dtype != torch.float8_e4m3fn or not out.is_contiguous():
+            raise ValueError(f"out must be a contiguous float8_e4m3fn tensor of shape {(b, l, h, hd)}")
+        if descale is None:
+            descale = torch.empty(h, device=x.device, dtype=torch.float32)
+        elif descale.numel() != h or descale.dtype != torch.float32 or not descale.is_contiguous():
+            raise ValueError(f"descale must be a contiguous fp32 vector of {h} heads")
+        words = (l + 31) // 32
+        if keep is not None and (keep.dtype != torch.int32 or keep.stride(-1) != 1 or keep.shape[-1] != words
+                                 or keep.ndim not in (1, 2) or (keep.ndim == 2 and keep.shape[0] != b)):
+            raise ValueError(f"keep must be int32 keep bits of shape ({words},) or ({b}, {words})")
+        slot.batch, slot.rows, slot.heads, slot.head_dim = b, l, h, hd
+        slot.x = x.data_ptr()
+        slot.stride[:] = [x.stride(0), x.stride(1), x.stride(2)]
+        slot.keep = None if keep is None else keep.data_ptr()
+        slot.keep_batch_stride = keep.stride(0) if keep is not None and keep.ndim == 2 else 0
+        slot.out = out.data_ptr()
+        slot.descale = descale.data_ptr()
+        results.append((out, descale))
+    stream = stream or torch.cuda.current_stream(dev)
+    _lib.check(_lib.load().dgxm_quantize_e4m3_per_head_batch(len(items), arr, stream.cuda_stream),
+               "dgxm_quantize_e4m3_per_head_batch")
+    return results

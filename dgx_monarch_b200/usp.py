@@ -203,15 +203,14 @@ class B200SequenceParallelAttention:
         qg, kg, vg = plan["recv"]
         out_ptrs = [win.peer_ptr(r, offs[3]) for r in range(p)]
         if self.fp8:
-            from .prologue import quantize_e4m3_per_head
+            from .prologue import quantize_e4m3_per_head_many
 
             # Pad rows neither attend nor set a head's scale, as when the
             # reference hands its inner FP8 kernel the real rows only.
             q_keep = keep_bits(qg.shape[1], drop_rows, qg.device)
             k_keep = keep_bits(kg.shape[1], kv_drop_rows, qg.device)
-            for src, dst, ds, keep in zip((qg, kg, vg), (plan["q8"], plan["k8"], plan["v8"]), plan["ds"],
-                                          (q_keep, k_keep, k_keep)):
-                quantize_e4m3_per_head(src, out=dst, descale=ds, keep=keep)
+            quantize_e4m3_per_head_many(zip((qg, kg, vg), (plan["q8"], plan["k8"], plan["v8"]), plan["ds"],
+                                            (q_keep, k_keep, k_keep)))
             descales = {"q_descale": plan["ds"][0], "k_descale": plan["ds"][1], "v_descale": plan["ds"][2]}
             if not drop_rows and not kv_drop_rows and not bias_groups:
                 attention_routed(plan["q8"], plan["k8"], plan["v8"], out_ptrs, (ls * h * d, h * d, d),
@@ -257,7 +256,7 @@ class B200SequenceParallelAttention:
         """One rank, e4m3: quantise the caller's heads in place of a scatter
         and attend into a fresh output (no window copy, no barrier).  Pad rows
         neither attend nor set a head's scale."""
-        from .prologue import quantize_e4m3_per_head
+        from .prologue import quantize_e4m3_per_head_many
 
         b, ls, h, d = q.shape
         key = ("fp8_local", b, ls, k.shape[1], h, k.shape[2], d)
@@ -270,9 +269,8 @@ class B200SequenceParallelAttention:
             self._plans[key] = bufs
         q_keep = keep_bits(q.shape[1], drop_rows, q.device)
         k_keep = keep_bits(k.shape[1], kv_drop_rows, q.device)
-        for src, dst, ds, keep in zip((q, k, v), (bufs["q8"], bufs["k8"], bufs["v8"]), bufs["ds"],
-                                      (q_keep, k_keep, k_keep)):
-            quantize_e4m3_per_head(src, out=dst, descale=ds, keep=keep)
+        quantize_e4m3_per_head_many(zip((q, k, v), (bufs["q8"], bufs["k8"], bufs["v8"]), bufs["ds"],
+                                        (q_keep, k_keep, k_keep)))
         descales = {"q_descale": bufs["ds"][0], "k_descale": bufs["ds"][1], "v_descale": bufs["ds"][2]}
         if drop_rows or kv_drop_rows or bias_groups:
             out, _ = attention_fwd_ext(bufs["q8"], bufs["k8"], bufs["v8"], key_keep=k_keep, query_keep=q_keep,
@@ -305,11 +303,11 @@ class B200SequenceParallelAttention:
             # per-head scales over exactly those rows; a block rotates with its
             # scales, so every ring step attends under the scales an inner FP8
             # kernel called on that block would take.
-            from .prologue import quantize_e4m3_per_head
+            from .prologue import quantize_e4m3_per_head_many
 
             ring = self._ring_plan(b, qg.shape[1], kg.shape[1], qg.shape[2], kg.shape[2], d,
                                    torch.float8_e4m3fn)
-            (q8, qs), (k8, ks), (v8, vs) = (quantize_e4m3_per_head(t) for t in (qg, kg, vg))
+            (q8, qs), (k8, ks), (v8, vs) = quantize_e4m3_per_head_many((t, None, None, None) for t in (qg, kg, vg))
             out_g, _ = ring.forward(q8, k8, v8, softmax_scale=softmax_scale, q_descale=qs, k_descale=ks,
                                     v_descale=vs)
         else:

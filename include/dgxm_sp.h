@@ -385,6 +385,23 @@ int dgxm_quantize_e4m3_per_head_masked(int32_t batch, int32_t rows, int32_t head
                                        const uint32_t* keep, int64_t keep_batch_stride, void* out,
                                        float* descale, void* stream);
 
+/*
+ * Up to three tensors (q, k and v of one attention) quantised by the same
+ * launches, each item as in dgxm_quantize_e4m3_per_head_masked (keep may be
+ * NULL).  Every item is checked before anything is launched.
+ */
+typedef struct dgxm_quant_item {
+  int32_t batch, rows, heads, head_dim;
+  const void* x;
+  int64_t stride[3];             /* elements: batch, row, head */
+  const uint32_t* keep;          /* NULL: every row counts toward the scale */
+  int64_t keep_batch_stride;     /* words; 0 shares one mask over the batch */
+  void* out;                     /* contiguous (batch, rows, heads, 128) e4m3 */
+  float* descale;                /* heads fp32 */
+} dgxm_quant_item;
+
+int dgxm_quantize_e4m3_per_head_batch(int32_t n, const dgxm_quant_item* items, void* stream);
+
 /* ------------------------------------------------------------ ring attention */
 /*
  * Ring attention over the ranks of `comm` (the ring group): every rank holds

@@ -857,3 +857,48 @@ def _hybrid_case(rank, world, dev):
 @pytest.mark.skipif(torch.cuda.device_count() < 4, reason="needs four or more GPUs")
 def test_hybrid_ulysses_ring_across_gpus():
     _spawn(_hybrid_case, 4)
+
+
+def _hybrid_fp8_case(rank, world, dev):
+    """FP8 over Ulysses-2 x ring-2 (ulysses-low): after the scatter a rank holds
+    its Ulysses group's rows (half the sequence) for half the heads, quantises
+    them per head and rotates its K/V block with its scales.  So q, k and v are
+    quantised per head over each half of the sequence; held to fp32 attention
+    over those dequantized halves."""
+    import torch.distributed as dist
+
+    from dgx_monarch_b200 import _lib
+    from dgx_monarch_b200.groups import hybrid_layout
+    from dgx_monarch_b200.usp import make_b200_usp_attention
+    from tests.test_attn_gpu import FP8_REL_L2, reference_attention, rel_l2
+
+    check = Checks(rank)
+    uly, ring = 2, world // 2
+    ulysses_groups, ring_groups = hybrid_layout(world, uly, ring)
+    mine_u = mine_r = None
+    for ranks in ulysses_groups:
+        grp = dist.new_group(ranks)
+        if rank in ranks:
+            mine_u = grp
+    for ranks in ring_groups:
+        grp = dist.new_group(ranks)
+        if rank in ranks:
+            mine_r = grp
+    attn = make_b200_usp_attention(ulysses_group=mine_u, ring_group=mine_r, generation=45, device=dev, fp8=True)
+    heads, ls = 4, 256
+    g = torch.Generator(device=dev).manual_seed(83)
+    q, k, v = (torch.randn(1, ls * world, heads, 128, device=dev, generator=g).bfloat16() for _ in range(3))
+    rows = slice(rank * ls, (rank + 1) * ls)
+    (_, qd), (_, kd), (_, vd) = (_per_block_e4m3(t, ring) for t in (q, k, v))
+    out = attn(*(t[:, rows].reshape(1, ls, -1) for t in (q, k, v)), heads=heads)
+    torch.cuda.synchronize()
+    ref, _ = reference_attention(qd, kd, vd)
+    check.le(rel_l2(out.reshape(1, ls, heads, 128), ref[:, rows]), FP8_REL_L2, "hybrid fp8 rel l2")
+    check(_lib.device_error() == 0, f"device error word {_lib.device_error()}")
+    attn.impl.invalidate()
+    check.close()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 4, reason="needs four or more GPUs")
+def test_hybrid_ulysses_ring_fp8_across_gpus():
+    _spawn(_hybrid_fp8_case, 4)

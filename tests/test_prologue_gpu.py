@@ -180,6 +180,25 @@ def test_quantize_with_keep_bits_skips_pad_rows(lib, shape, drop, per_batch):
     assert torch.equal(q8.view(torch.uint8), want.view(torch.uint8))
 
 
+def test_batched_quantisation_equals_one_tensor_at_a_time(lib):
+    """q, k and v of different rows and head counts (GQA), pads on k and v,
+    quantised by one batch of launches: every byte and descale equals the
+    one-tensor calls."""
+    from dgx_monarch_b200.ops import keep_bits
+    from dgx_monarch_b200.prologue import quantize_e4m3_per_head, quantize_e4m3_per_head_many
+
+    g = torch.Generator(device="cuda").manual_seed(303)
+    q = torch.randn(2, 700, 6, 128, device="cuda", generator=g).bfloat16()
+    k, v = (torch.randn(2, 333, 2, 128, device="cuda", generator=g).bfloat16() for _ in range(2))
+    keep = keep_bits(333, [0, 100, 332], q.device)
+    got = quantize_e4m3_per_head_many([(q, None, None, None), (k, None, None, keep), (v, None, None, keep)])
+    want = [quantize_e4m3_per_head(q), quantize_e4m3_per_head(k, keep=keep), quantize_e4m3_per_head(v, keep=keep)]
+    torch.cuda.synchronize()
+    for (g8, gs), (w8, ws) in zip(got, want):
+        assert torch.equal(gs, ws)
+        assert torch.equal(g8.view(torch.uint8), w8.view(torch.uint8))
+
+
 def _within_ulps(got, want, ulps):
     g, w = got.float(), want.float()
     tol = ulps * 2.0 ** -7 * torch.maximum(g.abs(), w.abs()) + 1e-5
