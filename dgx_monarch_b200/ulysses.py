@@ -447,8 +447,9 @@ class OverlappedUlysses:
     [8, 32] exposes 8/40 of the all-to-all behind which one head per rank of
     attention hides the other 32.
 
-    The group scatters run on copy engines (ulysses_scatter_copy), so they
-    take no SM from the attention launch they run beside.
+    The first group's scatter, with nothing beside it, runs the SM kernel; the
+    later ones run on copy engines (ulysses_scatter_copy), so they take no SM
+    from the attention launch they run beside.
 
     Receive slots: two groups use one slot each.  With more groups two slots
     alternate, and a rank refills a slot in its peers' windows only after a
@@ -517,11 +518,17 @@ class OverlappedUlysses:
                 side.wait_event(freed[slot])   # this rank attended group g - 2 from the slot
                 w.barrier(side)                 # ... and so has every other rank
             sl = slice(self.first[g], self.first[g] + self.sizes[g])
-            # Copy engines move the group beside the attention of the group
-            # before it, taking no SM from that launch.
-            ulysses_scatter_copy([q[:, :, sl], k[:, :, sl], v[:, :, sl]],
-                                 [[w.peer_ptr(r, off) for r in range(self.world)] for off in self.off_recv[slot]],
-                                 world=self.world, rank=self.rank, stream=side)
+            xs = [q[:, :, sl], k[:, :, sl], v[:, :, sl]]
+            dst = [[w.peer_ptr(r, off) for r in range(self.world)] for off in self.off_recv[slot]]
+            if g == 0:
+                # Nothing runs beside the first group's scatter, so the SM
+                # kernel moves it: copy engines take one strided copy per
+                # peer and tensor, slow for its one-head rows.
+                ulysses_scatter(xs, dst, world=self.world, rank=self.rank, stream=side)
+            else:
+                # Copy engines move the group beside the attention of the
+                # group before it, taking no SM from that launch.
+                ulysses_scatter_copy(xs, dst, world=self.world, rank=self.rank, stream=side)
             w.barrier(side)                     # every rank's rows of group g have landed
             ev = torch.cuda.Event()
             ev.record(side)
