@@ -10,12 +10,14 @@
 // variant with a norm over the whole hidden size keeps the separate prologue
 // kernel (a row's norm spans 40 head tiles).
 //
-// Roles (6 warps): warp 0 issues TMA loads of x and W tiles into a 6-stage
-// ring, warp 1 issues the MMAs (one thread), warps 2-5 run the epilogue with
-// one thread per output row.  Tiles are 128 tokens x 128 output features,
-// i.e. exactly one head of q, k or v, so the per-head norm and the RoPE pairs
-// never leave a thread.  Two TMEM accumulators alternate so the epilogue of
-// one tile overlaps the MMAs of the next.
+// Roles (10 warps): warp 0 issues TMA loads of x and W tiles into a 4-stage
+// ring, warp 1 issues the MMAs (one thread), warps 2-5 and 6-9 run the
+// epilogue of the tile's first and second head with one thread per output
+// row.  Tiles are 128 tokens x 256 output features, i.e. two heads of q, k or
+// v (M128 N256 MMAs), so the per-head norm and the RoPE pairs never leave a
+// thread, and a K step reads 48 KB for 4 MFLOP where 128-wide tiles read
+// 32 KB for 2.  Two TMEM accumulators of 256 columns alternate so the
+// epilogue of one tile overlaps the MMAs of the next.
 //
 // Rounding follows the separate ops it fuses: the Linear output is rounded
 // to bf16 (bias added in fp32 first), the norm output is bf16(x * rsqrt) then
@@ -25,17 +27,19 @@
 
 namespace dgxm {
 
-constexpr int kQkvStages = 6;
-constexpr int kQkvThreads = 6 * 32;
-constexpr int kQkvTile = 128;                    // tokens x features per tile
+constexpr int kQkvStages = 4;
+constexpr int kQkvThreads = 10 * 32;
+constexpr int kQkvTile = 128;                    // tokens per tile, and features per head
+constexpr int kQkvTileN = 256;                   // features per tile: two heads
 constexpr int kQkvBk = 64;                       // K per stage (one 128-byte swizzle atom)
-constexpr int kQkvTileBytes = kQkvTile * 128;    // one operand tile per stage: 16 KB
-constexpr int kQkvStageBytes = 2 * kQkvTileBytes;
+constexpr int kQkvTileBytes = kQkvTile * 128;    // the x tile per stage: 16 KB
+constexpr int kQkvWBytes = kQkvTileN * 128;      // the W tile per stage: 32 KB
+constexpr int kQkvStageBytes = kQkvTileBytes + kQkvWBytes;
 constexpr int kQkvSmemBytes = 1024 + kQkvStages * kQkvStageBytes + 512;
 
 struct __align__(64) QkvGemmParams {
   CUtensorMap tmap_x;  // dims (K, 1, M, 1), box (64, 1, 128, 1)
-  CUtensorMap tmap_w;  // dims (K, 1, N, 1), box (64, 1, 128, 1)
+  CUtensorMap tmap_w;  // dims (K, 1, N, 1), box (64, 1, 256, 1)
   int m, k_tiles, heads, n_tiles, m_tiles;
   const __nv_bfloat16* bias;     // N entries or NULL
   const __nv_bfloat16* norm_w[2];
@@ -82,7 +86,7 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_gemm_prologue_kernel(const
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(bar(B::kAccFull + a), 1);
-      mbar_init(bar(B::kAccEmpty + a), 128);
+      mbar_init(bar(B::kAccEmpty + a), 256);  // every epilogue thread
     }
     mbar_init(bar(B::kDrain), 1);
     *abort_flag = 0;
@@ -93,7 +97,7 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_gemm_prologue_kernel(const
     tma_prefetch_desc(&p.tmap_w);
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), 256);
+    tmem_alloc(smem_u32(tmem_slot), 2 * kQkvTileN);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -117,7 +121,7 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_gemm_prologue_kernel(const
           const uint32_t dst = base + s * kQkvStageBytes;
           mbar_expect_tx(bar(B::kFull + s), kQkvStageBytes);
           tma_load_4d(dst, &p.tmap_x, bar(B::kFull + s), kt * kQkvBk, 0, mt * kQkvTile, 0);
-          tma_load_4d(dst + kQkvTileBytes, &p.tmap_w, bar(B::kFull + s), kt * kQkvBk, 0, nt * kQkvTile, 0);
+          tma_load_4d(dst + kQkvTileBytes, &p.tmap_w, bar(B::kFull + s), kt * kQkvBk, 0, nt * kQkvTileN, 0);
         }
       }
       if (!ok) {
@@ -132,14 +136,14 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_gemm_prologue_kernel(const
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_make(kQkvTile, kQkvTile, 1u, false);
+      constexpr uint32_t idesc = idesc_make(kQkvTile, kQkvTileN, 1u, false);
       int it = 0, u = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x, ++u) {
         const int a = u & 1;
         if (!(ok = mbar_wait(bar(B::kAccEmpty + a), ((u >> 1) & 1) ^ 1, abort_flag))) break;
         tc_fence_after();
-        const uint32_t acc = tmem + a * kQkvTile;
+        const uint32_t acc = tmem + a * kQkvTileN;
         for (int kt = 0; kt < p.k_tiles; ++kt, ++it) {
           const int s = it % kQkvStages;
           if (!(ok = mbar_wait(bar(B::kFull + s), (it / kQkvStages) & 1, abort_flag))) break;
@@ -167,6 +171,7 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_gemm_prologue_kernel(const
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;                      // TMEM lane quarter of this warp
+    const int hs = (warp - 2) >> 2;              // which of the tile's two heads (warps 2-5, 6-9)
     const int row = q * 32 + lane;               // row within the tile
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
     const int hl = p.heads / p.world;
@@ -181,75 +186,81 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_gemm_prologue_kernel(const
       }
       tc_fence_after();
       const int mt = tile / p.n_tiles, nt = tile % p.n_tiles;
-      const int which = nt / p.heads;            // 0 q, 1 k, 2 v
-      const int head = nt - which * p.heads;
-      // Linear output: fp32 accumulator + bias, rounded to bf16, kept packed.
-      uint32_t y[64];
-      float ss = 0.f;
+      // This warp group's head of the tile (q, k and v each span a whole
+      // number of tiles, the head count being even).
+      {
+        const int gh = nt * (kQkvTileN / kQkvTile) + hs;  // head over q | k | v
+        const int which = gh / p.heads;            // 0 q, 1 k, 2 v
+        const int head = gh - which * p.heads;
+        // Linear output: fp32 accumulator + bias, rounded to bf16, kept packed.
+        uint32_t y[64];
+        float ss = 0.f;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tmem + lane_off + a * kQkvTile + c * 32, r);
-        tmem_wait_ld();
-        reg_fence32(r);
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tmem + lane_off + a * kQkvTileN + hs * kQkvTile + c * 32, r);
+          tmem_wait_ld();
+          reg_fence32(r);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float v0 = __uint_as_float(r[2 * i]), v1 = __uint_as_float(r[2 * i + 1]);
-          if (p.bias != nullptr) {
-            const int n = nt * kQkvTile + c * 32 + 2 * i;
-            v0 += __bfloat162float(p.bias[n]);
-            v1 += __bfloat162float(p.bias[n + 1]);
+          for (int i = 0; i < 16; ++i) {
+            float v0 = __uint_as_float(r[2 * i]), v1 = __uint_as_float(r[2 * i + 1]);
+            if (p.bias != nullptr) {
+              const int n = gh * kQkvTile + c * 32 + 2 * i;
+              v0 += __bfloat162float(p.bias[n]);
+              v1 += __bfloat162float(p.bias[n + 1]);
+            }
+            const uint32_t packed = pack_bf16x2(v0, v1);
+            y[c * 16 + i] = packed;
+            const float b0 = __uint_as_float(packed << 16), b1 = __uint_as_float(packed & 0xFFFF0000u);
+            ss = fmaf(b0, b0, ss);
+            ss = fmaf(b1, b1, ss);
           }
-          const uint32_t packed = pack_bf16x2(v0, v1);
-          y[c * 16 + i] = packed;
-          const float b0 = __uint_as_float(packed << 16), b1 = __uint_as_float(packed & 0xFFFF0000u);
-          ss = fmaf(b0, b0, ss);
-          ss = fmaf(b1, b1, ss);
         }
-      }
-      // The accumulator is in registers: the MMA may refill it.
-      tc_fence_before();
-      mbar_arrive(bar(B::kAccEmpty + a));
-      const int m = mt * kQkvTile + row;
-      if (m < p.m) {
-        const int l = p.row0 + m;                // local row in this rank's joint order
-        const int64_t grow = qkv_gathered_row(p.rank, l, p.seq_local, p.world, p.seg0);
-        const int owner = head / hl, hh = head - owner * hl;
-        uint4* dst = reinterpret_cast<uint4*>(p.dst[which][owner] + (grow * hl + hh) * 256);
-        if (which < 2 && (p.norm_head || p.rope != nullptr)) {
-          const float sc = rsqrtf(ss / 128.f + p.eps);
-          const __nv_bfloat16* w = p.norm_w[which];
-          const float* rope_row = p.rope == nullptr ? nullptr : p.rope + static_cast<int64_t>(l) * 128;
+        // This warp's half of the accumulator is in registers; once both
+        // halves are, the MMA may refill it.
+        tc_fence_before();
+        mbar_arrive(bar(B::kAccEmpty + a));
+        const int m = mt * kQkvTile + row;
+        if (m < p.m) {
+          const int l = p.row0 + m;                // local row in this rank's joint order
+          const int64_t grow = qkv_gathered_row(p.rank, l, p.seq_local, p.world, p.seg0);
+          const int owner = head / hl, hh = head - owner * hl;
+          uint4* dst = reinterpret_cast<uint4*>(p.dst[which][owner] + (grow * hl + hh) * 256);
+          if (which < 2 && (p.norm_head || p.rope != nullptr)) {
+            const float sc = rsqrtf(ss / 128.f + p.eps);
+            const __nv_bfloat16* w = p.norm_w[which];
+            const float* rope_row = p.rope == nullptr ? nullptr : p.rope + static_cast<int64_t>(l) * 128;
 #pragma unroll
-          for (int i = 0; i < 64; ++i) {
-            float x0 = __uint_as_float(y[i] << 16), x1 = __uint_as_float(y[i] & 0xFFFF0000u);
-            if (p.norm_head) {
-              x0 = __bfloat162float(__float2bfloat16(x0 * sc));
-              x1 = __bfloat162float(__float2bfloat16(x1 * sc));
-              if (w != nullptr) {
-                x0 = __bfloat162float(__float2bfloat16(x0 * __bfloat162float(w[2 * i])));
-                x1 = __bfloat162float(__float2bfloat16(x1 * __bfloat162float(w[2 * i + 1])));
+            for (int i = 0; i < 64; ++i) {
+              float x0 = __uint_as_float(y[i] << 16), x1 = __uint_as_float(y[i] & 0xFFFF0000u);
+              if (p.norm_head) {
+                x0 = __bfloat162float(__float2bfloat16(x0 * sc));
+                x1 = __bfloat162float(__float2bfloat16(x1 * sc));
+                if (w != nullptr) {
+                  x0 = __bfloat162float(__float2bfloat16(x0 * __bfloat162float(w[2 * i])));
+                  x1 = __bfloat162float(__float2bfloat16(x1 * __bfloat162float(w[2 * i + 1])));
+                }
               }
+              if (rope_row != nullptr) {
+                const float cs = rope_row[2 * i], sn = rope_row[2 * i + 1];
+                const float r0 = fmaf(-sn, x1, cs * x0);
+                const float r1 = fmaf(cs, x1, sn * x0);
+                x0 = r0;
+                x1 = r1;
+              }
+              y[i] = pack_bf16x2(x0, x1);
             }
-            if (rope_row != nullptr) {
-              const float cs = rope_row[2 * i], sn = rope_row[2 * i + 1];
-              const float r0 = fmaf(-sn, x1, cs * x0);
-              const float r1 = fmaf(cs, x1, sn * x0);
-              x0 = r0;
-              x1 = r1;
-            }
-            y[i] = pack_bf16x2(x0, x1);
           }
-        }
 #pragma unroll
-        for (int v = 0; v < 16; ++v) dst[v] = make_uint4(y[4 * v], y[4 * v + 1], y[4 * v + 2], y[4 * v + 3]);
+          for (int v = 0; v < 16; ++v) dst[v] = make_uint4(y[4 * v], y[4 * v + 1], y[4 * v + 2], y[4 * v + 3]);
+        }
       }
     }
   }
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 2 * kQkvTileN);
   }
 }
 
@@ -266,6 +277,9 @@ extern "C" int dgxm_qkv_gemm_prologue_scatter(const dgxm_qkv_gemm_desc* d, const
     return fail(DGXM_ERR_INVALID, "rank %d / world %d out of range", d->rank, d->world);
   if (d->heads <= 0 || d->heads % d->world)
     return fail(DGXM_ERR_INVALID, "%d heads are not divisible by the Ulysses degree %d", d->heads, d->world);
+  if (d->heads % (kQkvTileN / kQkvTile))
+    return fail(DGXM_ERR_UNSUPPORTED, "the fused QKV kernel takes an even head count (two heads per tile), got %d",
+                d->heads);
   if (d->m < 0 || d->k <= 0 || d->k % 8 || d->x_row_stride % 8 || d->x_row_stride < d->k)
     return fail(DGXM_ERR_INVALID, "m %d / k %d / row stride %lld: k and the stride must be multiples of 8",
                 d->m, d->k, (long long)d->x_row_stride);
@@ -288,12 +302,12 @@ extern "C" int dgxm_qkv_gemm_prologue_scatter(const dgxm_qkv_gemm_desc* d, const
                           d->x_row_stride, d->x_row_stride * d->m, kQkvBk, kQkvTile)))
     return rc;
   if ((rc = encode_map_4d(&p.tmap_w, w_qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, d->k, 1, n, 1, d->k, d->k,
-                          d->k * n, kQkvBk, kQkvTile)))
+                          d->k * n, kQkvBk, kQkvTileN)))
     return rc;
   p.m = d->m;
   p.k_tiles = (d->k + kQkvBk - 1) / kQkvBk;
   p.heads = d->heads;
-  p.n_tiles = 3 * d->heads;
+  p.n_tiles = 3 * d->heads * kQkvTile / kQkvTileN;
   p.m_tiles = (d->m + kQkvTile - 1) / kQkvTile;
   p.bias = static_cast<const __nv_bfloat16*>(bias);
   p.norm_w[0] = static_cast<const __nv_bfloat16*>(norm_q_w);
