@@ -288,10 +288,10 @@ def run_reference(args) -> None:
 DIT = {"hidden": 3072, "heads": 24, "img": 9216, "txt": 512, "latent": (96, 96)}
 DIT_WORKLOAD = ("Flux/Krea2-style joint-attention DiT double block (attention sub-layer): "
                 "1536x1536 image -> 96x96 patch grid = 9216 tokens + 512 text tokens, hidden 3072, "
-                "24 heads x 128, bf16, random-init weights N(0, 0.02); QKV projection with bias (cuBLAS), "
-                "per-head RMSNorm on Q/K + 2-axis RoPE + sequence->head scatter in one kernel, joint "
-                "[text, image] attention with the inverse all-to-all in its epilogue, out projection "
-                "(cuBLAS)")
+                "24 heads x 128, bf16, random-init weights N(0, 0.02); QKV projection with bias, "
+                "per-head RMSNorm on Q/K, 2-axis RoPE and the sequence->head scatter in one tcgen05 GEMM "
+                "per stream, joint [text, image] attention with the inverse all-to-all in its epilogue, "
+                "out projection (cuBLAS)")
 
 
 def time_steps(step, steps: int, warmup: int, graph: bool = False) -> float:
@@ -418,7 +418,7 @@ def run_dit_layer(world: int, rank: int, dev, steps: int, warmup: int, group=Non
                              norm_mode=_lib.NORM_HEAD, norm_q_w=nq, norm_k_w=nk, rope=table, seg0=t_loc)
 
     def step():
-        qkv_split()
+        qkv_fused()
         win.barrier()
         attention_routed(recv[0], recv[1], recv[2], [win.peer_ptr(r, offs[3]) for r in range(world)],
                          (ls * h * DIM, h * DIM, DIM), world=world, rank=rank, seq_local=ls, seg0=t_loc)
@@ -437,7 +437,7 @@ def run_dit_layer(world: int, rank: int, dev, steps: int, warmup: int, group=Non
         torch.cuda.synchronize()
     win.close()
     return {"ms": ms, "ms_eager": ms_eager, "ms_qkv_split": ms_split, "ms_qkv_fused": ms_fused,
-            "my_launches": 6 if world > 1 else 4}
+            "my_launches": 7 if world > 1 else 5}
 
 
 # ----------------------------------------------------------------- ring / CFG workloads (N > 1)
@@ -836,7 +836,7 @@ def main() -> None:
                           "launch": "one CUDA graph per layer (ms_per_layer_eager: the same calls from Python)",
                           "qkv_stage_ms": {"cublas_addmm_plus_prologue_scatter": qkv_split_ms,
                                            "fused_tcgen05_gemm_prologue_scatter": qkv_fused_ms,
-                                           "in_layer": "cublas_addmm_plus_prologue_scatter"},
+                                           "in_layer": "fused_tcgen05_gemm_prologue_scatter"},
                           "tflops": dit_layer_flops() / (dit_ms * 1e-3) / 1e12,
                           "frac_of_bf16_peak": dit_layer_flops() / (dit_ms * 1e-3) / 1e12 / (world * peaks["bf16_tflops"]),
                           "parallelism": f"ulysses{world}"},

@@ -1,8 +1,9 @@
 // Thin inline-PTX wrappers for the sm_100a features the attention path uses:
 // mbarriers, TMA tile loads (no cluster fan-out of any kind), tcgen05 MMA with
-// TMEM accumulators, and TMEM loads/stores.  Every wait in this file is
-// bounded: a wait that runs past its budget reports failure to the caller,
-// which records an error word and unwinds instead of spinning forever.
+// TMEM accumulators (one CTA, or a CTA pair of one TPC), and TMEM loads and
+// stores.  Every wait in this file is bounded: a wait that runs past its
+// budget reports failure to the caller, which records an error word and
+// unwinds instead of spinning forever.
 #pragma once
 
 #include <cuda.h>
@@ -91,6 +92,14 @@ __device__ __forceinline__ void tma_load_4d_hint(uint32_t dst, const void* map, 
       "l"(policy)
       : "memory");
 }
+
+// 16 bytes global -> this CTA's shared memory, asynchronously (L2 only).
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+
+// Wait for every cp_async16 this thread issued.
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 __device__ __forceinline__ uint64_t l2_policy_evict_last() {
   uint64_t p;
@@ -184,6 +193,88 @@ __device__ __forceinline__ void umma_f8_ts(uint32_t d_tmem, uint32_t a_tmem, uin
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// ---------------------------------------------------------------- CTA pairs
+// A cluster of two CTAs on the two SMs of one TPC works as one tcgen05 pair:
+// the even CTA issues M256 MMAs that read the A rows and the B half each CTA
+// holds at the same shared-memory offset and write each CTA's own TMEM.  The
+// loads stay per CTA (each CTA fetches its own operands; nothing is fanned
+// out), and only their completion is reported on the even CTA's barrier.
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// The shared::cluster address of the object at shared::cta address `addr`
+// in the cluster's CTA `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+// Every thread of both CTAs: an execution barrier over the cluster with
+// release/acquire ordering of shared-memory writes.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile(
+      "barrier.cluster.arrive.release.aligned;\n\t"
+      "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Arrive on a barrier given by its shared::cluster address (own or peer CTA).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
+               : "memory");
+}
+
+// 4-D tiled load into this CTA's shared memory whose transaction bytes are
+// reported on `pair_bar`, a shared::cluster address in either CTA of the pair.
+__device__ __forceinline__ void tma_load_4d_pair(uint32_t dst, const void* map, uint32_t pair_bar,
+                                                 int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(pair_bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+               "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+// D[tmem of both CTAs] (+)= A[smem of both] * B[smem of both]^T: M256, each
+// CTA holding 128 A rows and N/2 B rows at the descriptors' offsets.
+__device__ __forceinline__ void umma_f16_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                 uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive once on the barrier at offset `bar` in every CTA of `cta_mask` when
+// the pair MMAs this thread issued so far have completed.
+__device__ __forceinline__ void umma_commit_pair_to(uint32_t bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(bar),
+      "h"(cta_mask)
       : "memory");
 }
 

@@ -10,14 +10,21 @@
 // variant with a norm over the whole hidden size keeps the separate prologue
 // kernel (a row's norm spans 40 head tiles).
 //
-// Roles (10 warps): warp 0 issues TMA loads of x and W tiles into a 4-stage
-// ring, warp 1 issues the MMAs (one thread), warps 2-5 and 6-9 run the
-// epilogue of the tile's first and second head with one thread per output
-// row.  Tiles are 128 tokens x 256 output features, i.e. two heads of q, k or
-// v (M128 N256 MMAs), so the per-head norm and the RoPE pairs never leave a
-// thread, and a K step reads 48 KB for 4 MFLOP where 128-wide tiles read
-// 32 KB for 2.  Two TMEM accumulators of 256 columns alternate so the
-// epilogue of one tile overlaps the MMAs of the next.
+// The kernel runs as clusters of two CTAs, one tcgen05 pair on the two SMs of
+// a TPC.  A pair tile is 256 tokens x 256 output features (two heads of q, k
+// or v): each CTA loads its own 128 token rows of x and its own 128 rows of W
+// (one head), and the even CTA issues M256 N256 MMAs that read both CTAs'
+// operands and leave each CTA's 128 token rows x 256 features in its own
+// TMEM.  A K step costs each SM 32 KB of operand loads for 512 MMA clocks,
+// where a one-CTA 128 x 256 tile loads 48 KB for the same clocks.
+//
+// Roles per CTA (10 warps): warp 0 issues this CTA's TMA loads into a 5-stage
+// ring (their completion counted on the even CTA's barrier), warp 1 of the
+// even CTA issues the MMAs (one thread), warps 2-5 and 6-9 run the epilogue of
+// the tile's first and second head, one thread per token row.  Two TMEM
+// accumulators of 256 columns alternate so the epilogue of one tile overlaps
+// the MMAs of the next.  The epilogue stages each warp's 32 finished head rows
+// in shared memory and stores them two whole 256-byte rows per instruction.
 //
 // Rounding follows the separate ops it fuses: the Linear output is rounded
 // to bf16 (bias added in fp32 first), the norm output is bf16(x * rsqrt) then
@@ -27,19 +34,21 @@
 
 namespace dgxm {
 
-constexpr int kQkvStages = 4;
+constexpr int kQkvStages = 5;
 constexpr int kQkvThreads = 10 * 32;
-constexpr int kQkvTile = 128;                    // tokens per tile, and features per head
-constexpr int kQkvTileN = 256;                   // features per tile: two heads
-constexpr int kQkvBk = 64;                       // K per stage (one 128-byte swizzle atom)
-constexpr int kQkvTileBytes = kQkvTile * 128;    // the x tile per stage: 16 KB
-constexpr int kQkvWBytes = kQkvTileN * 128;      // the W tile per stage: 32 KB
-constexpr int kQkvStageBytes = kQkvTileBytes + kQkvWBytes;
-constexpr int kQkvSmemBytes = 1024 + kQkvStages * kQkvStageBytes + 512;
+constexpr int kQkvTile = 128;                        // token rows per CTA, and features per head
+constexpr int kQkvPairM = 2 * kQkvTile;              // token rows per pair tile
+constexpr int kQkvTileN = 256;                       // features per tile: two heads
+constexpr int kQkvBk = 64;                           // K per stage (one 128-byte swizzle atom)
+constexpr int kQkvHalfBytes = kQkvTile * 128;        // 128 rows x 64 bf16: 16 KB
+constexpr int kQkvStageBytes = 2 * kQkvHalfBytes;    // this CTA's x rows and W rows
+constexpr int kQkvPairStageBytes = 2 * kQkvStageBytes;
+constexpr int kQkvStagingBytes = 8 * 32 * 256;       // per epilogue warp: 32 head rows
+constexpr int kQkvSmemBytes = 1024 + kQkvStages * kQkvStageBytes + kQkvStagingBytes + 512;
 
 struct __align__(64) QkvGemmParams {
   CUtensorMap tmap_x;  // dims (K, 1, M, 1), box (64, 1, 128, 1)
-  CUtensorMap tmap_w;  // dims (K, 1, N, 1), box (64, 1, 256, 1)
+  CUtensorMap tmap_w;  // dims (K, 1, N, 1), box (64, 1, 128, 1)
   int m, k_tiles, heads, n_tiles, m_tiles;
   const __nv_bfloat16* bias;     // N entries or NULL
   const __nv_bfloat16* norm_w[2];
@@ -50,6 +59,8 @@ struct __align__(64) QkvGemmParams {
   int world, rank, seq_local, row0, seg0;
 };
 
+// Barriers of each CTA.  The even CTA's Full and AccEmpty count for the pair;
+// Empty and AccFull are signalled in both CTAs by the even CTA's commits.
 struct QkvBars {
   static constexpr int kFull = 0;
   static constexpr int kEmpty = kFull + kQkvStages;
@@ -65,18 +76,51 @@ __device__ __forceinline__ int64_t qkv_gathered_row(int r, int l, int seq_local,
   return static_cast<int64_t>(world) * seg0 + static_cast<int64_t>(r) * (seq_local - seg0) + (l - seg0);
 }
 
+// Pair tiles run in groups of kQkvGroupM token-tile rows, feature tiles
+// outermost within a group, so the pairs resident at one time share a few x
+// panels and a few W panels (about 13 + 14 MB at the C2 width) instead of
+// sweeping all of W for every two token-tile rows.
+constexpr int kQkvGroupM = 8;
+
+__device__ __forceinline__ void qkv_tile_coords(int tile, int m_tiles, int n_tiles, int& mt, int& nt) {
+  const int per_group = kQkvGroupM * n_tiles;
+  const int g = tile / per_group, r = tile - g * per_group;
+  const int rows = min(kQkvGroupM, m_tiles - g * kQkvGroupM);  // token-tile rows in this group
+  mt = g * kQkvGroupM + r % rows;
+  nt = r / rows;
+}
+
+// One half of a warp's 32 RoPE rows (pairs 32h .. 32h + 31 of each row: 256
+// contiguous bytes) into its staging rows, two rows per instruction; 16-byte
+// chunk c of row r goes to chunk c ^ (r & 15), as the output rows do.
+__device__ __forceinline__ void qkv_stage_rope(const QkvGemmParams& p, uint8_t* stage_rows, int m0, int lane,
+                                               int h) {
+  const int cc = lane & 15;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int rr = 2 * j + (lane >> 4);
+    const int mr = m0 + rr;
+    if (mr < p.m)
+      cp_async16(smem_u32(stage_rows + rr * 256 + ((cc ^ (rr & 15)) << 4)),
+                 p.rope + static_cast<int64_t>(p.row0 + mr) * 128 + h * 64 + cc * 4);
+  }
+}
+
 __global__ void __launch_bounds__(kQkvThreads, 1) qkv_gemm_prologue_kernel(const __grid_constant__ QkvGemmParams p) {
   using B = QkvBars;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* smem = smem_raw + (base - raw);
-  uint8_t* ctrl = smem + kQkvStages * kQkvStageBytes;
+  uint8_t* staging = smem + kQkvStages * kQkvStageBytes;
+  uint8_t* ctrl = staging + kQkvStagingBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(ctrl);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ctrl + B::kCount * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t cta = cluster_ctarank();     // 0: issues the pair's MMAs
+  const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
   const int tiles = p.m_tiles * p.n_tiles;
 
   if (threadIdx.x == 0) {
@@ -86,7 +130,7 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_gemm_prologue_kernel(const
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(bar(B::kAccFull + a), 1);
-      mbar_init(bar(B::kAccEmpty + a), 256);  // every epilogue thread
+      mbar_init(bar(B::kAccEmpty + a), 16);  // every epilogue warp of both CTAs
     }
     mbar_init(bar(B::kDrain), 1);
     *abort_flag = 0;
@@ -97,11 +141,11 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_gemm_prologue_kernel(const
     tma_prefetch_desc(&p.tmap_w);
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), 2 * kQkvTileN);
-    tmem_relinquish();
+    tmem_alloc_pair(smem_u32(tmem_slot), 2 * kQkvTileN);
+    tmem_relinquish_pair();
   }
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();  // both CTAs' barriers initialised and TMEM allocated
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
@@ -110,8 +154,9 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_gemm_prologue_kernel(const
     if (lane == 0) {
       int it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
-        const int mt = tile / p.n_tiles, nt = tile % p.n_tiles;
+      for (int tile = pair; ok && tile < tiles; tile += pairs) {
+        int mt, nt;
+        qkv_tile_coords(tile, p.m_tiles, p.n_tiles, mt, nt);
         for (int kt = 0; kt < p.k_tiles; ++kt, ++it) {
           const int s = it % kQkvStages;
           if (!mbar_wait(bar(B::kEmpty + s), ((it / kQkvStages) & 1) ^ 1, abort_flag)) {
@@ -119,27 +164,32 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_gemm_prologue_kernel(const
             break;
           }
           const uint32_t dst = base + s * kQkvStageBytes;
-          mbar_expect_tx(bar(B::kFull + s), kQkvStageBytes);
-          tma_load_4d(dst, &p.tmap_x, bar(B::kFull + s), kt * kQkvBk, 0, mt * kQkvTile, 0);
-          tma_load_4d(dst + kQkvTileBytes, &p.tmap_w, bar(B::kFull + s), kt * kQkvBk, 0, nt * kQkvTileN, 0);
+          const uint32_t full = mapa_shared(bar(B::kFull + s), 0);
+          if (cta == 0) mbar_expect_tx(bar(B::kFull + s), kQkvPairStageBytes);
+          tma_load_4d_pair(dst, &p.tmap_x, full, kt * kQkvBk, 0, mt * kQkvPairM + cta * kQkvTile, 0);
+          tma_load_4d_pair(dst + kQkvHalfBytes, &p.tmap_w, full, kt * kQkvBk, 0,
+                           nt * kQkvTileN + cta * kQkvTile, 0);
         }
       }
       if (!ok) {
         report_device_error(kErrProducerTimeout);
         *abort_flag = 1;
-        // Let the loads already issued land before the CTA can exit.
-        const int first = it > kQkvStages ? it - kQkvStages : 0;
-        for (int i = first; i < it; ++i) mbar_wait(bar(B::kFull + i % kQkvStages), (i / kQkvStages) & 1, nullptr);
+        // Let the loads already issued land before the pair can exit (both
+        // CTAs' loads report on the even CTA's barriers).
+        if (cta == 0) {
+          const int first = it > kQkvStages ? it - kQkvStages : 0;
+          for (int i = first; i < it; ++i) mbar_wait(bar(B::kFull + i % kQkvStages), (i / kQkvStages) & 1, nullptr);
+        }
       }
     }
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_make(kQkvTile, kQkvTileN, 1u, false);
+    if (lane == 0 && cta == 0) {
+      constexpr uint32_t idesc = idesc_make(kQkvPairM, kQkvTileN, 1u, false);
       int it = 0, u = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x, ++u) {
+      for (int tile = pair; ok && tile < tiles; tile += pairs, ++u) {
         const int a = u & 1;
         if (!(ok = mbar_wait(bar(B::kAccEmpty + a), ((u >> 1) & 1) ^ 1, abort_flag))) break;
         tc_fence_after();
@@ -152,19 +202,19 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_gemm_prologue_kernel(const
 #pragma unroll
           for (int kk = 0; kk < kQkvBk / 16; ++kk) {
             const uint64_t da = sdesc_sw128(sa + kk * 32, 16, 1024);
-            const uint64_t db = sdesc_sw128(sa + kQkvTileBytes + kk * 32, 16, 1024);
-            umma_f16_ss(acc, da, db, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
+            const uint64_t db = sdesc_sw128(sa + kQkvHalfBytes + kk * 32, 16, 1024);
+            umma_f16_ss_pair(acc, da, db, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
           }
-          umma_commit(bar(B::kEmpty + s));
+          umma_commit_pair_to(bar(B::kEmpty + s), 0x3);
         }
-        if (ok) umma_commit(bar(B::kAccFull + a));
+        if (ok) umma_commit_pair_to(bar(B::kAccFull + a), 0x3);
       }
       if (!ok) {
         report_device_error(kErrMmaTimeout);
         *abort_flag = 1;
       }
-      // Every MMA issued has completed before TMEM is released.
-      umma_commit(bar(B::kDrain));
+      // Every MMA issued has completed before either CTA releases its TMEM.
+      umma_commit_pair_to(bar(B::kDrain), 0x1);
       mbar_wait(bar(B::kDrain), 0, nullptr);
     }
     __syncwarp();
@@ -172,95 +222,128 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_gemm_prologue_kernel(const
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;                      // TMEM lane quarter of this warp
     const int hs = (warp - 2) >> 2;              // which of the tile's two heads (warps 2-5, 6-9)
-    const int row = q * 32 + lane;               // row within the tile
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    const uint32_t acc_empty = mapa_shared(bar(B::kAccEmpty), 0);
+    uint8_t* stage_rows = staging + (warp - 2) * (32 * 256);
     const int hl = p.heads / p.world;
     int u = 0;
-    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++u) {
+    for (int tile = pair; tile < tiles; tile += pairs, ++u) {
       const int a = u & 1;
+      int mt, nt;
+      qkv_tile_coords(tile, p.m_tiles, p.n_tiles, mt, nt);
+      // This warp group's head of the tile (q, k and v each span a whole
+      // number of tiles, the head count being even).
+      const int gh = nt * (kQkvTileN / kQkvTile) + hs;  // head over q | k | v
+      const int which = gh / p.heads;                  // 0 q, 1 k, 2 v
+      const int head = gh - which * p.heads;
+      const int m0 = mt * kQkvPairM + static_cast<int>(cta) * kQkvTile + q * 32;  // this warp's first row
+      const int m = m0 + lane;
+      const bool rope = which < 2 && p.rope != nullptr;
+      // The first half of the warp's 32 RoPE rows is fetched while the MMAs run.
+      if (rope) qkv_stage_rope(p, stage_rows, m0, lane, 0);
       const bool got = __all_sync(0xffffffffu, mbar_wait(bar(B::kAccFull + a), (u >> 1) & 1, abort_flag));
       if (!got) {
+        cp_async_wait_all();
         report_device_error(kErrEpilogueTimeout);
         *abort_flag = 1;
         break;
       }
       tc_fence_after();
-      const int mt = tile / p.n_tiles, nt = tile % p.n_tiles;
-      // This warp group's head of the tile (q, k and v each span a whole
-      // number of tiles, the head count being even).
-      {
-        const int gh = nt * (kQkvTileN / kQkvTile) + hs;  // head over q | k | v
-        const int which = gh / p.heads;            // 0 q, 1 k, 2 v
-        const int head = gh - which * p.heads;
-        // Linear output: fp32 accumulator + bias, rounded to bf16, kept packed.
-        uint32_t y[64];
-        float ss = 0.f;
+      // Linear output: fp32 accumulator + bias, rounded to bf16, kept packed.
+      uint32_t y[64];
+      float ss = 0.f;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t r[32];
-          tmem_ld32(tmem + lane_off + a * kQkvTileN + hs * kQkvTile + c * 32, r);
-          tmem_wait_ld();
-          reg_fence32(r);
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_off + a * kQkvTileN + hs * kQkvTile + c * 32, r);
+        tmem_wait_ld();
+        reg_fence32(r);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            float v0 = __uint_as_float(r[2 * i]), v1 = __uint_as_float(r[2 * i + 1]);
-            if (p.bias != nullptr) {
-              const int n = gh * kQkvTile + c * 32 + 2 * i;
-              v0 += __bfloat162float(p.bias[n]);
-              v1 += __bfloat162float(p.bias[n + 1]);
-            }
-            const uint32_t packed = pack_bf16x2(v0, v1);
-            y[c * 16 + i] = packed;
-            const float b0 = __uint_as_float(packed << 16), b1 = __uint_as_float(packed & 0xFFFF0000u);
-            ss = fmaf(b0, b0, ss);
-            ss = fmaf(b1, b1, ss);
+        for (int i = 0; i < 16; ++i) {
+          float v0 = __uint_as_float(r[2 * i]), v1 = __uint_as_float(r[2 * i + 1]);
+          if (p.bias != nullptr) {
+            const int n = gh * kQkvTile + c * 32 + 2 * i;
+            v0 += __bfloat162float(p.bias[n]);
+            v1 += __bfloat162float(p.bias[n + 1]);
           }
-        }
-        // This warp's half of the accumulator is in registers; once both
-        // halves are, the MMA may refill it.
-        tc_fence_before();
-        mbar_arrive(bar(B::kAccEmpty + a));
-        const int m = mt * kQkvTile + row;
-        if (m < p.m) {
-          const int l = p.row0 + m;                // local row in this rank's joint order
-          const int64_t grow = qkv_gathered_row(p.rank, l, p.seq_local, p.world, p.seg0);
-          const int owner = head / hl, hh = head - owner * hl;
-          uint4* dst = reinterpret_cast<uint4*>(p.dst[which][owner] + (grow * hl + hh) * 256);
-          if (which < 2 && (p.norm_head || p.rope != nullptr)) {
-            const float sc = rsqrtf(ss / 128.f + p.eps);
-            const __nv_bfloat16* w = p.norm_w[which];
-            const float* rope_row = p.rope == nullptr ? nullptr : p.rope + static_cast<int64_t>(l) * 128;
-#pragma unroll
-            for (int i = 0; i < 64; ++i) {
-              float x0 = __uint_as_float(y[i] << 16), x1 = __uint_as_float(y[i] & 0xFFFF0000u);
-              if (p.norm_head) {
-                x0 = __bfloat162float(__float2bfloat16(x0 * sc));
-                x1 = __bfloat162float(__float2bfloat16(x1 * sc));
-                if (w != nullptr) {
-                  x0 = __bfloat162float(__float2bfloat16(x0 * __bfloat162float(w[2 * i])));
-                  x1 = __bfloat162float(__float2bfloat16(x1 * __bfloat162float(w[2 * i + 1])));
-                }
-              }
-              if (rope_row != nullptr) {
-                const float cs = rope_row[2 * i], sn = rope_row[2 * i + 1];
-                const float r0 = fmaf(-sn, x1, cs * x0);
-                const float r1 = fmaf(cs, x1, sn * x0);
-                x0 = r0;
-                x1 = r1;
-              }
-              y[i] = pack_bf16x2(x0, x1);
-            }
-          }
-#pragma unroll
-          for (int v = 0; v < 16; ++v) dst[v] = make_uint4(y[4 * v], y[4 * v + 1], y[4 * v + 2], y[4 * v + 3]);
+          const uint32_t packed = pack_bf16x2(v0, v1);
+          y[c * 16 + i] = packed;
+          const float b0 = __uint_as_float(packed << 16), b1 = __uint_as_float(packed & 0xFFFF0000u);
+          ss = fmaf(b0, b0, ss);
+          ss = fmaf(b1, b1, ss);
         }
       }
+      // This warp's rows of the accumulator are in registers; once every
+      // epilogue warp of both CTAs has arrived, the MMAs may refill it.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc_empty + a * 8);
+      if (which < 2 && p.norm_head) {
+        const float sc = rsqrtf(ss / 128.f + p.eps);
+        const __nv_bfloat16* w = p.norm_w[which];
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          float x0 = __uint_as_float(y[i] << 16), x1 = __uint_as_float(y[i] & 0xFFFF0000u);
+          x0 = __bfloat162float(__float2bfloat16(x0 * sc));
+          x1 = __bfloat162float(__float2bfloat16(x1 * sc));
+          if (w != nullptr) {
+            x0 = __bfloat162float(__float2bfloat16(x0 * __bfloat162float(w[2 * i])));
+            x1 = __bfloat162float(__float2bfloat16(x1 * __bfloat162float(w[2 * i + 1])));
+          }
+          y[i] = pack_bf16x2(x0, x1);
+        }
+      }
+      if (rope) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          if (h == 1) qkv_stage_rope(p, stage_rows, m0, lane, 1);
+          cp_async_wait_all();
+          __syncwarp();
+          // Row `lane`'s pairs 32h + 2c and 32h + 2c + 1: (cos, sin, cos, sin).
+          const float4* mine = reinterpret_cast<const float4*>(stage_rows + lane * 256);
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            const float4 t = mine[c ^ (lane & 15)];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int i = 32 * h + 2 * c + e;
+              const float cs = e ? t.z : t.x, sn = e ? t.w : t.y;
+              const float x0 = __uint_as_float(y[i] << 16), x1 = __uint_as_float(y[i] & 0xFFFF0000u);
+              y[i] = pack_bf16x2(fmaf(-sn, x1, cs * x0), fmaf(cs, x1, sn * x0));
+            }
+          }
+          __syncwarp();
+        }
+      }
+      // Stage the warp's 32 rows (16-byte chunk c of row r at chunk c ^ (r & 15),
+      // so that both the row-wise writes and the chunk-wise reads below are free
+      // of bank conflicts), then store two whole rows per instruction.
+      uint4* mine = reinterpret_cast<uint4*>(stage_rows + lane * 256);
+#pragma unroll
+      for (int c = 0; c < 16; ++c)
+        mine[c ^ (lane & 15)] = make_uint4(y[4 * c], y[4 * c + 1], y[4 * c + 2], y[4 * c + 3]);
+      __syncwarp();
+      const int owner = head / hl, hh = head - owner * hl;
+      char* const dst_base = p.dst[which][owner];
+      const int cc = lane & 15;
+#pragma unroll 4
+      for (int j = 0; j < 16; ++j) {
+        const int rr = 2 * j + (lane >> 4);
+        const int mr = m0 + rr;
+        if (mr < p.m) {
+          const uint4 v = reinterpret_cast<const uint4*>(stage_rows + rr * 256)[cc ^ (rr & 15)];
+          const int64_t grow = qkv_gathered_row(p.rank, p.row0 + mr, p.seq_local, p.world, p.seg0);
+          reinterpret_cast<uint4*>(dst_base + (grow * hl + hh) * 256)[cc] = v;
+        }
+      }
+      __syncwarp();
     }
   }
-  __syncthreads();
+  tc_fence_before();
+  cluster_sync();  // the pair's MMAs drained and every TMEM read done in both CTAs
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 2 * kQkvTileN);
+    tmem_dealloc_pair(tmem, 2 * kQkvTileN);
   }
 }
 
@@ -288,8 +371,8 @@ extern "C" int dgxm_qkv_gemm_prologue_scatter(const dgxm_qkv_gemm_desc* d, const
                 d->row0 + d->m, d->seq_local, d->seg0);
   if (d->norm_mode != DGXM_NORM_NONE && d->norm_mode != DGXM_NORM_HEAD)
     return fail(DGXM_ERR_UNSUPPORTED, "the fused QKV kernel applies per-head norms only (mode %d)", d->norm_mode);
-  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w_qkv)) % 16)
-    return fail(DGXM_ERR_INVALID, "x and w_qkv must be 16-byte aligned");
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w_qkv) | reinterpret_cast<uintptr_t>(rope)) % 16)
+    return fail(DGXM_ERR_INVALID, "x, w_qkv and rope must be 16-byte aligned");
   for (int i = 0; i < 3 * d->world; ++i)
     if (dst[i] == nullptr || reinterpret_cast<uintptr_t>(dst[i]) % 16)
       return fail(DGXM_ERR_INVALID, "destination %d is NULL or not 16-byte aligned", i);
@@ -302,13 +385,13 @@ extern "C" int dgxm_qkv_gemm_prologue_scatter(const dgxm_qkv_gemm_desc* d, const
                           d->x_row_stride, d->x_row_stride * d->m, kQkvBk, kQkvTile)))
     return rc;
   if ((rc = encode_map_4d(&p.tmap_w, w_qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, d->k, 1, n, 1, d->k, d->k,
-                          d->k * n, kQkvBk, kQkvTileN)))
+                          d->k * n, kQkvBk, kQkvTile)))
     return rc;
   p.m = d->m;
   p.k_tiles = (d->k + kQkvBk - 1) / kQkvBk;
   p.heads = d->heads;
   p.n_tiles = 3 * d->heads * kQkvTile / kQkvTileN;
-  p.m_tiles = (d->m + kQkvTile - 1) / kQkvTile;
+  p.m_tiles = (d->m + kQkvPairM - 1) / kQkvPairM;
   p.bias = static_cast<const __nv_bfloat16*>(bias);
   p.norm_w[0] = static_cast<const __nv_bfloat16*>(norm_q_w);
   p.norm_w[1] = static_cast<const __nv_bfloat16*>(norm_k_w);
@@ -322,14 +405,34 @@ extern "C" int dgxm_qkv_gemm_prologue_scatter(const dgxm_qkv_gemm_desc* d, const
   p.seq_local = d->seq_local;
   p.row0 = d->row0;
   p.seg0 = d->seg0;
-  int dev = 0, sms = 148;
+  int dev = 0;
   DGXM_CUDA_TRY(cudaGetDevice(&dev));
-  DGXM_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   static std::atomic<uint64_t> configured{0};  // bit per device
   DGXM_CUDA_TRY(set_smem_limit_once(qkv_gemm_prologue_kernel, kQkvSmemBytes, configured));
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kQkvThreads);
+  cfg.dynamicSmemBytes = kQkvSmemBytes;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // Pairs resident at once (one per TPC when nothing else runs), cached per device.
+  static std::atomic<int> max_pairs[64];
+  int pairs = dev < 64 ? max_pairs[dev].load() : 0;
+  if (pairs <= 0) {
+    cfg.gridDim = dim3(2);
+    DGXM_CUDA_TRY(cudaOccupancyMaxActiveClusters(&pairs, qkv_gemm_prologue_kernel, &cfg));
+    if (pairs <= 0) return fail(DGXM_ERR_CUDA, "no CTA pair of the fused QKV kernel fits on device %d", dev);
+    if (dev < 64) max_pairs[dev].store(pairs);
+  }
   const int tiles = p.m_tiles * p.n_tiles;
-  const int grid = tiles < sms ? tiles : sms;
-  qkv_gemm_prologue_kernel<<<grid, kQkvThreads, kQkvSmemBytes, static_cast<cudaStream_t>(stream)>>>(p);
+  cfg.gridDim = dim3(2 * (tiles < pairs ? tiles : pairs));
+  DGXM_CUDA_TRY(cudaLaunchKernelEx(&cfg, qkv_gemm_prologue_kernel, p));
   DGXM_CUDA_TRY(cudaGetLastError());
   return DGXM_OK;
 }

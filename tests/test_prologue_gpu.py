@@ -206,9 +206,10 @@ def _within_ulps(got, want, ulps):
 
 
 @pytest.mark.parametrize("hidden,heads,t_loc,i_loc,rope,bias", [
-    (512, 4, 40, 300, True, True),       # tails below and above one 128-row tile
-    (3072, 24, 64, 300, True, False),    # the C2 block width: 216 tiles over 148 SMs, 48-stage ring wrap
-    (512, 4, 0, 129, False, True),       # image stream only, no RoPE
+    (512, 4, 40, 300, True, True),       # tails below and above one 256-row pair tile (odd CTA idle)
+    (3072, 24, 64, 300, True, False),    # the C2 block width: 72 pair tiles, 48-step K over a 5-stage ring
+    (512, 4, 0, 129, False, True),       # image stream only, no RoPE, one row in the odd CTA
+    (1024, 8, 100, 4000, True, True),    # 192 pair tiles: every pair alternates its two accumulators
 ])
 def test_fused_qkv_gemm_prologue_matches_separate_ops(lib, hidden, heads, t_loc, i_loc, rope, bias):
     """The QKV Linear + per-head QKNorm + RoPE + sequence->head scatter in one
