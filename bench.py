@@ -55,6 +55,9 @@ def parse_args():
     p.add_argument("--p-chunks", type=int, choices=[0, 1, 4], default=0,
                    help="release each block's probabilities to the tensor core in this many "
                         "chunks (0: the library default, 4; 1: the single release)")
+    p.add_argument("--one-cta", action="store_true",
+                   help="run 16-bit attention on single CTAs instead of CTA pairs (the library "
+                        "default), as a cross-check")
     p.add_argument("--profile-case", choices=["attn", "fp8", "f16", "kernels"], default=None,
                    help="instead of the bench: a few launches of one kernel family on one GPU, "
                         "sized for a profiler capture (attn / fp8 / f16: three attention launches "
@@ -76,6 +79,10 @@ def run_profile_case(args) -> None:
     from dgx_monarch_b200.ops import attention_fwd, set_p_chunks
 
     set_p_chunks(args.p_chunks)
+    if args.one_cta:
+        from dgx_monarch_b200.ops import set_cta_pair
+
+        set_cta_pair(False)
     dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev).manual_seed(0)
     shape = (args.case_batch, args.case_seq, args.case_heads, DIM)
@@ -662,6 +669,10 @@ def main() -> None:
         from dgx_monarch_b200.ops import set_p_chunks
 
         set_p_chunks(args.p_chunks)
+    if args.one_cta:
+        from dgx_monarch_b200.ops import set_cta_pair
+
+        set_cta_pair(False)
     if world > 1:
         from datetime import timedelta
 
@@ -801,7 +812,8 @@ def main() -> None:
         value = flops / (ms * 1e-3) / 1e12
         per_rank_flops = flops / world
         achieved = per_rank_flops / (attn_ms * 1e-3) / 1e12
-        traffic = profiled_traffic("attn_fwd_bf16", f"s{SEQ}_h{HEADS // world}")
+        pair = not args.one_cta and args.p_chunks != 1
+        traffic = profiled_traffic("attn_fwd_bf16_pair" if pair else "attn_fwd_bf16", f"s{SEQ}_h{HEADS // world}")
         line = {
             "metric": METRIC,
             "value": value,
@@ -823,7 +835,7 @@ def main() -> None:
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
                          "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
                          "traffic": traffic, "peak_source": peaks["source"] + " burst bf16",
-                         "kernel": "attn_fwd_kernel<bf16>"},
+                         "kernel": "attn_fwd_kernel<bf16>" + (" on CTA pairs" if pair else " on single CTAs")},
             "e2e": {"value": flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                     "h2d_bytes_per_step": 3 * q.numel() * q.element_size(),
                     "d2h_bytes_per_step": out.numel() * out.element_size(),

@@ -25,6 +25,7 @@ DTYPE_E4M3 = 2
 DTYPE_F32 = 3
 
 ATTN_SAFE_ORDER = 1
+ATTN_ONE_CTA = 2  # DGXM_ATTN_ONE_CTA
 ATTN_P_CHUNKS_SHIFT = 4  # DGXM_ATTN_P_CHUNKS(n) = n << 4
 
 

@@ -103,6 +103,9 @@ struct AttnCfg {
   static constexpr uint32_t kFmt = FP8 ? 0u : (F16 ? 0u : 1u);
   static constexpr uint32_t kIdescQK = idesc_make(128, 128, kFmt, false);
   static constexpr uint32_t kIdescPV = idesc_make(128, HD, kFmt, true);
+  // CTA-pair products: M256, each CTA holding 128 of the rows.
+  static constexpr uint32_t kIdescQK2 = idesc_make(256, 128, kFmt, false);
+  static constexpr uint32_t kIdescPV2 = idesc_make(256, HD, kFmt, true);
   static constexpr int kSmemBytes = 1024 /*align slack*/ + 2 * kTileBytes + kStages * kTileBytes +
                                     1024 /*barriers + slots*/ + 12 * 128 * 4 /*row exchange*/;
 };
@@ -211,6 +214,31 @@ __device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_lo, uint32_
   }
 }
 
+// The CTA-pair S = Q K^T: each CTA holds its own Q tile and 64 of the
+// block's 128 keys (64-row boxes, kBoxBytes / 2 apart), and the even CTA's
+// M256 N128 products write both CTAs' S tiles.
+template <bool F16, int HD>
+__device__ __forceinline__ void issue_qk_pair(uint32_t d_tmem, uint32_t q_lo, uint32_t k_lo) {
+  using C = AttnCfg<false, F16, HD>;
+  constexpr uint32_t hi = sdesc_hi(1024);
+#pragma unroll
+  for (int kk = 0; kk < C::kKSteps; ++kk) {
+    const uint32_t byte = kk * 32;
+    const uint32_t off_q = ((byte / 128) * C::kBoxBytes + (byte % 128)) >> 4;
+    const uint32_t off_k = ((byte / 128) * (C::kBoxBytes / 2) + (byte % 128)) >> 4;
+    umma_f16_ss_pair(d_tmem, sdesc_join(q_lo + off_q, hi), sdesc_join(k_lo + off_k, hi), C::kIdescQK2,
+                     kk > 0 ? 1u : 0u);
+  }
+}
+
+template <bool FP8, bool F16, int HD, bool PAIR>
+__device__ __forceinline__ void issue_qk_any(uint32_t d_tmem, uint32_t q_lo, uint32_t k_lo) {
+  if constexpr (PAIR)
+    issue_qk_pair<F16, HD>(d_tmem, q_lo, k_lo);
+  else
+    issue_qk<FP8, F16, HD>(d_tmem, q_lo, k_lo);
+}
+
 // O += P V: P from tensor memory, V MN-major (head_dim along the 128-byte
 // rows, keys down the rows; the second 128-byte column block of bf16 sits
 // kBoxBytes further, the leading byte offset).
@@ -235,7 +263,10 @@ __device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint3
 // both column halves c, K = 64 / kPChunks -- the probabilities one chunk of
 // every softmax thread has stored.  The first step of chunk 0 starts the
 // accumulation when `accumulate` is false.
-template <bool FP8, bool F16, int HD, int kPChunks>
+// PAIR: the CTA-pair product, each CTA's P in its own TMEM and 64 of the head
+// dimensions of V (one 128-byte column block of all 128 keys) in its own
+// shared memory.
+template <bool FP8, bool F16, int HD, int kPChunks, bool PAIR = false>
 __device__ __forceinline__ void issue_pv_chunk(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_lo,
                                                bool accumulate, int ch) {
   using C = AttnCfg<FP8, F16, HD>;
@@ -251,7 +282,9 @@ __device__ __forceinline__ void issue_pv_chunk(uint32_t d_tmem, uint32_t p_tmem,
       const uint64_t b = sdesc_join(v_lo + ((kk * C::kMmaK * 128) >> 4), hi);
       const uint32_t a = p_tmem + kk * (C::kMmaK * C::kEltBytes / 4);
       const uint32_t acc = (accumulate || ch > 0 || c > 0 || q > 0) ? 1u : 0u;
-      if constexpr (FP8)
+      if constexpr (PAIR)
+        umma_f16_ts_pair(d_tmem, a, b, C::kIdescPV2, acc);
+      else if constexpr (FP8)
         umma_f8_ts(d_tmem, a, b, C::kIdescPV, acc);
       else
         umma_f16_ts(d_tmem, a, b, C::kIdescPV, acc);
@@ -261,7 +294,7 @@ __device__ __forceinline__ void issue_pv_chunk(uint32_t d_tmem, uint32_t p_tmem,
 
 // O += P V of one tile, chunk by chunk as the softmax releases P: each chunk
 // waits for its own barrier.  Returns false when a wait gave up.
-template <bool FP8, bool F16, int HD, int kPChunks, int kBarPFull>
+template <bool FP8, bool F16, int HD, int kPChunks, int kBarPFull, bool PAIR = false>
 __device__ __forceinline__ bool issue_pv_chunks(uint64_t* bars, uint32_t d_tmem, uint32_t p_tmem,
                                                 uint32_t v_lo, bool accumulate, int parity,
                                                 volatile int* abort_flag) {
@@ -269,7 +302,7 @@ __device__ __forceinline__ bool issue_pv_chunks(uint64_t* bars, uint32_t d_tmem,
   for (int ch = 0; ch < kPChunks; ++ch) {
     if (!mbar_wait(smem_u32(&bars[kBarPFull + ch]), parity, abort_flag)) return false;
     tc_fence_after();
-    issue_pv_chunk<FP8, F16, HD, kPChunks>(d_tmem, p_tmem, v_lo, accumulate, ch);
+    issue_pv_chunk<FP8, F16, HD, kPChunks, PAIR>(d_tmem, p_tmem, v_lo, accumulate, ch);
   }
   return true;
 }
@@ -287,6 +320,31 @@ __device__ __forceinline__ void release_p(uint32_t b, int lane) {
   }
 }
 
+// The CTA-pair release: one arrival per warp of either CTA on the even CTA's
+// chunk barrier (a shared::cluster address).  The arrival is relaxed: what it
+// hands over is P in this CTA's TMEM, whose stores every thread of the warp
+// has completed (tcgen05.wait::st) and fenced (tcgen05.fence::before_thread_
+// sync) before the warp meets, and the issuer orders its products after its
+// wait with tcgen05.fence::after_thread_sync; the issuer reads nothing the
+// softmax writes through generic memory.  A release at cluster scope would
+// make every softmax warp wait for its earlier shared-memory traffic to
+// become visible to the peer SM at each of the 8 hand-offs per block: that
+// measured 740 against 1188 TFLOP/s at 75,600 keys.
+__device__ __forceinline__ void release_p_pair(uint32_t leader_bar, int lane) {
+  __syncwarp();
+  if (lane == 0) mbar_arrive_cluster_relaxed(leader_bar);
+}
+
+// Commit of the MMA issuer: to this CTA's barrier, or for a CTA pair to the
+// barrier at the same offset in both CTAs.
+template <bool PAIR>
+__device__ __forceinline__ void attn_commit(uint32_t bar) {
+  if constexpr (PAIR)
+    umma_commit_pair_to(bar, 0x3);
+  else
+    umma_commit(bar);
+}
+
 __device__ __forceinline__ void raise_abort(volatile int* abort_flag, int bits) {
   report_device_error(bits);
   *abort_flag = 1;
@@ -294,18 +352,31 @@ __device__ __forceinline__ void raise_abort(volatile int* abort_flag, int bits) 
 
 // F16: 16-bit inputs (and P) are fp16 instead of bf16; a 16-bit output is
 // then fp16 too.
-template <bool FP8, bool OUT_F32, bool EXTRA, int NCH, bool F16, int HD>
+//
+// PAIR: the kernel runs as clusters of two CTAs on the two SMs of a TPC, one
+// tcgen05 pair.  Each CTA keeps its two Q tiles, its S, P and O in its own
+// TMEM and its own softmax; a K/V stage holds half of a block (K: 64 of the
+// 128 keys; V: 64 of the head dimensions of all keys), so each SM loads half
+// the K/V bytes.  The even CTA issues M256 products over both CTAs' operands
+// -- half the MMAs per FLOP of one CTA -- and its commits signal both CTAs;
+// the loads of both CTAs and the P releases of both CTAs' softmax warps are
+// counted on the even CTA's barriers.
+template <bool FP8, bool OUT_F32, bool EXTRA, int NCH, bool F16, int HD, bool PAIR>
 __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_constant__ AttnParams p) {
   using C = AttnCfg<FP8, F16, HD>;
   constexpr int kPChunks = p_chunks<FP8, NCH>();
-  using B = Bars<C::kStages, kPChunks>;
+  static_assert(!PAIR || (!FP8 && HD == kHeadDim && kPChunks > 1 && DGXM_SM_WARP_ARRIVE),
+                "CTA pairs: 16-bit inputs, head dim 128, chunked P release, one arrival per warp");
+  constexpr int kStageBytes = PAIR ? C::kTileBytes / 2 : C::kTileBytes;
+  constexpr int kStages = PAIR ? 2 * C::kStages : C::kStages;  // the same ring bytes
+  using B = Bars<kStages, kPChunks>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* smem = smem_raw + (base - raw);
   const uint32_t sQ = base;
   const uint32_t sKV = base + 2 * C::kTileBytes;
-  uint8_t* ctrl = smem + 2 * C::kTileBytes + C::kStages * C::kTileBytes;
+  uint8_t* ctrl = smem + 2 * C::kTileBytes + kStages * kStageBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(ctrl);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ctrl + B::kCount * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -316,14 +387,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
 
   if (threadIdx.x == 0) {
     mbar_init(bar(B::kQ), 1);
-    for (int s = 0; s < C::kStages; ++s) {
+    for (int s = 0; s < kStages; ++s) {
       mbar_init(bar(B::kKvFull + s), 1);
       mbar_init(bar(B::kKvEmpty + s), 1);
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(bar(B::kSFull + t), 1);
       for (int ch = 0; ch < kPChunks; ++ch)
-        mbar_init(bar(B::kPFull + t * kPChunks + ch), DGXM_SM_WARP_ARRIVE ? 8 : 256);
+        mbar_init(bar(B::kPFull + t * kPChunks + ch), PAIR ? 16 : (DGXM_SM_WARP_ARRIVE ? 8 : 256));
       mbar_init(bar(B::kOFull + t), 1);
       mbar_init(bar(B::kPvDone + t), 1);
     }
@@ -337,13 +408,22 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
     tma_prefetch_desc(&p.tmap_v);
   }
   if (warp == kMmaWarp) {
-    tmem_alloc(smem_u32(tmem_slot), 512);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(smem_u32(tmem_slot), 512);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(smem_u32(tmem_slot), 512);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR)
+    cluster_sync();  // both CTAs' barriers initialised and TMEM allocated
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const uint32_t cta = PAIR ? cluster_ctarank() : 0u;  // 0 issues a pair's MMAs
 
   const int qtile = blockIdx.x;
   const int h = blockIdx.y;
@@ -360,34 +440,65 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
       bool ok = true;
       const uint64_t keep = l2_policy_evict_last();   // K/V are re-read by every Q tile
       const uint64_t once = l2_policy_evict_first();  // Q is read by this CTA only
-      mbar_expect_tx(bar(B::kQ), 2 * C::kTileBytes);
-      for (int t = 0; t < 2; ++t)
-        for (int c = 0; c < C::kBoxes; ++c)
-          tma_load_4d_hint(sQ + t * C::kTileBytes + c * C::kBoxBytes, &p.tmap_q, bar(B::kQ),
-                           c * C::kBoxCols, h, row0 + t * kTileRows, b, once);
+      if constexpr (PAIR) {
+        // Both CTAs' loads count on the even CTA's barriers.
+        if (cta == 0) mbar_expect_tx(bar(B::kQ), 4 * C::kTileBytes);
+        const uint32_t qbar = mapa_shared(bar(B::kQ), 0);
+        for (int t = 0; t < 2; ++t)
+          for (int c = 0; c < C::kBoxes; ++c)
+            tma_load_4d_pair_hint(sQ + t * C::kTileBytes + c * C::kBoxBytes, &p.tmap_q, qbar,
+                                  c * C::kBoxCols, h, row0 + t * kTileRows, b, once);
+      } else {
+        mbar_expect_tx(bar(B::kQ), 2 * C::kTileBytes);
+        for (int t = 0; t < 2; ++t)
+          for (int c = 0; c < C::kBoxes; ++c)
+            tma_load_4d_hint(sQ + t * C::kTileBytes + c * C::kBoxBytes, &p.tmap_q, bar(B::kQ),
+                             c * C::kBoxCols, h, row0 + t * kTileRows, b, once);
+      }
       for (int idx = 0; idx < 2 * nkv; ++idx) {
-        const int s = idx % C::kStages;
-        const int ph = (idx / C::kStages) & 1;
+        const int s = idx % kStages;
+        const int ph = (idx / kStages) & 1;
         if (!mbar_wait(bar(B::kKvEmpty + s), ph ^ 1, abort_flag)) {
           ok = false;
           break;
         }
-        mbar_expect_tx(bar(B::kKvFull + s), C::kTileBytes);
-        const void* map = (idx & 1) ? static_cast<const void*>(&p.tmap_v)
-                                    : static_cast<const void*>(&p.tmap_k);
-        for (int c = 0; c < C::kBoxes; ++c)
-          tma_load_4d_hint(sKV + s * C::kTileBytes + c * C::kBoxBytes, map,
-                           bar(B::kKvFull + s), c * C::kBoxCols, hk, (idx >> 1) * kTileRows, b,
-                           keep);
+        if constexpr (PAIR) {
+          // K: this CTA's 64 keys of the block, both 128-byte column blocks
+          // (tmap_k has 64-row boxes); V: this CTA's 128-byte column block of
+          // all 128 keys.
+          if (cta == 0) mbar_expect_tx(bar(B::kKvFull + s), 2 * kStageBytes);
+          const uint32_t fbar = mapa_shared(bar(B::kKvFull + s), 0);
+          const uint32_t dst = sKV + s * kStageBytes;
+          if (idx & 1) {
+            tma_load_4d_pair_hint(dst, &p.tmap_v, fbar, static_cast<int>(cta) * C::kBoxCols, hk,
+                                  (idx >> 1) * kTileRows, b, keep);
+          } else {
+            for (int c = 0; c < C::kBoxes; ++c)
+              tma_load_4d_pair_hint(dst + c * (C::kBoxBytes / 2), &p.tmap_k, fbar, c * C::kBoxCols, hk,
+                                    (idx >> 1) * kTileRows + static_cast<int>(cta) * (kTileRows / 2), b,
+                                    keep);
+          }
+        } else {
+          mbar_expect_tx(bar(B::kKvFull + s), C::kTileBytes);
+          const void* map = (idx & 1) ? static_cast<const void*>(&p.tmap_v)
+                                      : static_cast<const void*>(&p.tmap_k);
+          for (int c = 0; c < C::kBoxes; ++c)
+            tma_load_4d_hint(sKV + s * C::kTileBytes + c * C::kBoxBytes, map,
+                             bar(B::kKvFull + s), c * C::kBoxCols, hk, (idx >> 1) * kTileRows, b,
+                             keep);
+        }
         issued_count = idx + 1;
       }
       if (!ok) {
         raise_abort(abort_flag, kErrProducerTimeout);
-        // Let the copies already in flight land before the CTA can exit.
-        mbar_wait(bar(B::kQ), 0, nullptr);
-        const int first = issued_count > C::kStages ? issued_count - C::kStages : 0;
-        for (int idx = first; idx < issued_count; ++idx)
-          mbar_wait(bar(B::kKvFull + idx % C::kStages), (idx / C::kStages) & 1, nullptr);
+        // Let the copies already in flight land before the CTA can exit (a
+        // pair's loads all report on the even CTA's barriers).
+        if (cta == 0) {
+          mbar_wait(bar(B::kQ), 0, nullptr);
+          const int first = issued_count > kStages ? issued_count - kStages : 0;
+          for (int idx = first; idx < issued_count; ++idx)
+            mbar_wait(bar(B::kKvFull + idx % kStages), (idx / kStages) & 1, nullptr);
+        }
       }
     }
     __syncwarp();
@@ -399,31 +510,31 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
     // products.  P_t sits in S_t's tensor memory, so S_t of the next block is
     // issued only after the P_t V that reads it (tcgen05 operations of one
     // thread execute in issue order; DGXM_ATTN_SAFE_ORDER drains instead).
-    if (lane == 0) {
+    if (lane == 0 && cta == 0) {
       const uint32_t tS0 = tmem, tS1 = tmem + 128, tO0 = tmem + 256, tO1 = tmem + 384;
       const uint32_t q0_lo = sdesc_lo(sQ, 16), q1_lo = sdesc_lo(sQ + C::kTileBytes, 16);
       const uint32_t kv_lo_k = sdesc_lo(sKV, 16);             // stage 0, K-major view
       const uint32_t kv_lo_v = sdesc_lo(sKV, C::kBoxBytes);   // stage 0, MN-major view
-      constexpr uint32_t kStageLo = C::kTileBytes >> 4;       // low-word step per stage
+      constexpr uint32_t kStageLo = kStageBytes >> 4;        // low-word step per stage
       bool ok = mbar_wait(bar(B::kQ), 0, abort_flag);
       tc_fence_after();
       for (int j = 0; ok && j < nkv; ++j) {
         const int ki = 2 * j;
-        const int ks = ki % C::kStages;
-        if (!(ok = mbar_wait(bar(B::kKvFull + ks), (ki / C::kStages) & 1, abort_flag))) break;
+        const int ks = ki % kStages;
+        if (!(ok = mbar_wait(bar(B::kKvFull + ks), (ki / kStages) & 1, abort_flag))) break;
         tc_fence_after();
         // S0 = Q0 K_j^T
         if (safe_order && j > 0) {
           if (!(ok = mbar_wait(bar(B::kPvDone + 0), (j - 1) & 1, abort_flag))) break;
           tc_fence_after();
         }
-        issue_qk<FP8, F16, HD>(tS0, q0_lo, kv_lo_k + ks * kStageLo);
-        umma_commit(bar(B::kSFull + 0));
+        issue_qk_any<FP8, F16, HD, PAIR>(tS0, q0_lo, kv_lo_k + ks * kStageLo);
+        attn_commit<PAIR>(bar(B::kSFull + 0));
         // O1 += P1 V_{j-1}
         if (j > 0) {
-          const int vs = (2 * j - 1) % C::kStages;
+          const int vs = (2 * j - 1) % kStages;
           if constexpr (kPChunks > 1) {
-            if (!(ok = issue_pv_chunks<FP8, F16, HD, kPChunks, B::kPFull + kPChunks>(
+            if (!(ok = issue_pv_chunks<FP8, F16, HD, kPChunks, B::kPFull + kPChunks, PAIR>(
                       bars, tO1, tS1, kv_lo_v + vs * kStageLo, j - 1 > 0, (j - 1) & 1, abort_flag)))
               break;
           } else {
@@ -431,23 +542,23 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
             tc_fence_after();
             issue_pv<FP8, F16, HD>(tO1, tS1, kv_lo_v + vs * kStageLo, j - 1 > 0);
           }
-          umma_commit(bar(B::kKvEmpty + vs));
+          attn_commit<PAIR>(bar(B::kKvEmpty + vs));
           if (safe_order) {
-            umma_commit(bar(B::kPvDone + 1));
+            attn_commit<PAIR>(bar(B::kPvDone + 1));
             if (!(ok = mbar_wait(bar(B::kPvDone + 1), (j - 1) & 1, abort_flag))) break;
             tc_fence_after();
           }
         }
         // S1 = Q1 K_j^T
-        issue_qk<FP8, F16, HD>(tS1, q1_lo, kv_lo_k + ks * kStageLo);
-        umma_commit(bar(B::kSFull + 1));
-        umma_commit(bar(B::kKvEmpty + ks));
+        issue_qk_any<FP8, F16, HD, PAIR>(tS1, q1_lo, kv_lo_k + ks * kStageLo);
+        attn_commit<PAIR>(bar(B::kSFull + 1));
+        attn_commit<PAIR>(bar(B::kKvEmpty + ks));
         // O0 += P0 V_j
         const int vi = 2 * j + 1;
-        const int vs = vi % C::kStages;
-        if (!(ok = mbar_wait(bar(B::kKvFull + vs), (vi / C::kStages) & 1, abort_flag))) break;
+        const int vs = vi % kStages;
+        if (!(ok = mbar_wait(bar(B::kKvFull + vs), (vi / kStages) & 1, abort_flag))) break;
         if constexpr (kPChunks > 1) {
-          if (!(ok = issue_pv_chunks<FP8, F16, HD, kPChunks, B::kPFull>(bars, tO0, tS0, kv_lo_v + vs * kStageLo, j > 0,
+          if (!(ok = issue_pv_chunks<FP8, F16, HD, kPChunks, B::kPFull, PAIR>(bars, tO0, tS0, kv_lo_v + vs * kStageLo, j > 0,
                                                      j & 1, abort_flag)))
             break;
         } else {
@@ -455,14 +566,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
           tc_fence_after();
           issue_pv<FP8, F16, HD>(tO0, tS0, kv_lo_v + vs * kStageLo, j > 0);
         }
-        if (safe_order) umma_commit(bar(B::kPvDone + 0));
-        if (j == nkv - 1) umma_commit(bar(B::kOFull + 0));
+        if (safe_order) attn_commit<PAIR>(bar(B::kPvDone + 0));
+        if (j == nkv - 1) attn_commit<PAIR>(bar(B::kOFull + 0));
       }
       if (ok) {
         // O1 += P1 V_{n-1}
-        const int vs = (2 * nkv - 1) % C::kStages;
+        const int vs = (2 * nkv - 1) % kStages;
         if constexpr (kPChunks > 1) {
-          ok = issue_pv_chunks<FP8, F16, HD, kPChunks, B::kPFull + kPChunks>(bars, tO1, tS1, kv_lo_v + vs * kStageLo,
+          ok = issue_pv_chunks<FP8, F16, HD, kPChunks, B::kPFull + kPChunks, PAIR>(bars, tO1, tS1, kv_lo_v + vs * kStageLo,
                                                             nkv - 1 > 0, (nkv - 1) & 1, abort_flag);
         } else {
           ok = mbar_wait(bar(B::kPFull + 1), (nkv - 1) & 1, abort_flag);
@@ -472,14 +583,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
           }
         }
         if (ok) {
-          umma_commit(bar(B::kKvEmpty + vs));
-          umma_commit(bar(B::kOFull + 1));
+          attn_commit<PAIR>(bar(B::kKvEmpty + vs));
+          attn_commit<PAIR>(bar(B::kOFull + 1));
         }
       }
       if (!ok) {
         raise_abort(abort_flag, kErrMmaTimeout);
         // Wait for the MMAs already issued before TMEM is released.
-        umma_commit(bar(B::kDrain));
+        if constexpr (PAIR)
+          umma_commit_pair_to(bar(B::kDrain), 0x1);
+        else
+          umma_commit(bar(B::kDrain));
         mbar_wait(bar(B::kDrain), 0, nullptr);
       }
     }
@@ -504,6 +618,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
     const uint32_t tP = tmem + lane_off + t * 128 + c * (C::kPCols / 2);
     const uint32_t tO = tmem + lane_off + 256 + t * 128 + c * (HD / 2);  // this half's output columns
     float* xmax = reinterpret_cast<float*>(ctrl + kCtrlXmaxOffset);  // [2 parity][2 tile][2 half][128]
+    const uint32_t pfull_leader = PAIR ? mapa_shared(bar(B::kPFull), 0) : 0u;  // the even CTA's chunk barriers
     float sl2 = p.scale_log2;
     if constexpr (FP8) sl2 *= p.q_descale[h] * p.k_descale[hk];
     float m_run = -INFINITY;  // running max of the scaled logits, log2 units
@@ -684,7 +799,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
           }
           tmem_wait_st();
           tc_fence_before();
-          release_p(bar(B::kPFull + t * kPChunks + ch), lane);
+          if constexpr (PAIR)
+            release_p_pair(pfull_leader + (t * kPChunks + ch) * 8, lane);
+          else
+            release_p(bar(B::kPFull + t * kPChunks + ch), lane);
         }
         float a0, a1, b0, b1;
         upk2(sum_a, a0, a1);
@@ -865,21 +983,48 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
       }
     }
   }
-  __syncthreads();
-  if (warp == kMmaWarp) {
-    tc_fence_after();
-    tmem_dealloc(tmem, 512);
+  if constexpr (PAIR) {
+    tc_fence_before();
+    cluster_sync();  // the pair's products complete and every TMEM read done in both CTAs
+    if (warp == kMmaWarp) {
+      tc_fence_after();
+      tmem_dealloc_pair(tmem, 512);
+    }
+  } else {
+    __syncthreads();
+    if (warp == kMmaWarp) {
+      tc_fence_after();
+      tmem_dealloc(tmem, 512);
+    }
   }
 }
 
-template <bool FP8, bool OUT_F32, bool EXTRA, int NCH, bool F16 = false, int HD = kHeadDim>
+template <bool FP8, bool OUT_F32, bool EXTRA, int NCH, bool F16 = false, int HD = kHeadDim, bool PAIR = false>
 static int launch_attn(const AttnParams& prm, dim3 grid, cudaStream_t stream) {
   using C = AttnCfg<FP8, F16, HD>;
   static std::atomic<uint64_t> configured{0};  // one bit per device ordinal
-  auto kern = attn_fwd_kernel<FP8, OUT_F32, EXTRA, NCH, F16, HD>;
+  auto kern = attn_fwd_kernel<FP8, OUT_F32, EXTRA, NCH, F16, HD, PAIR>;
   DGXM_CUDA_TRY(set_smem_limit_once(kern, C::kSmemBytes, configured));
-  kern<<<grid, kAttnThreads, C::kSmemBytes, stream>>>(prm);
-  DGXM_CUDA_TRY(cudaGetLastError());
+  if constexpr (PAIR) {
+    // Clusters of two along the Q tiles (the grid's x extent is even).
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof(cfg));
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kAttnThreads);
+    cfg.dynamicSmemBytes = C::kSmemBytes;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    DGXM_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, prm));
+  } else {
+    kern<<<grid, kAttnThreads, C::kSmemBytes, stream>>>(prm);
+    DGXM_CUDA_TRY(cudaGetLastError());
+  }
   return DGXM_OK;
 }
 
@@ -888,6 +1033,14 @@ static bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 1
 }  // namespace dgxm
 
 namespace dgxm {
+
+// Whether a call runs the CTA-pair kernel: built for 16-bit inputs at head
+// dim 128 with the chunked P release, and not turned off by DGXM_ATTN_ONE_CTA.
+static bool attn_uses_pair(const dgxm_attn_desc* d) {
+  const int nch = (d->flags & DGXM_ATTN_P_CHUNKS_MASK) >> DGXM_ATTN_P_CHUNKS_SHIFT;
+  return (d->flags & DGXM_ATTN_ONE_CTA) == 0 && d->in_dtype != DGXM_DTYPE_E4M3 &&
+         d->head_dim == kHeadDim && nch != 1;
+}
 
 // Validate the descriptor and fill the kernel parameters (everything but
 // the output routing, which the caller sets).
@@ -946,8 +1099,11 @@ static int prepare_attn(const dgxm_attn_desc* d, const void* q, const void* k, c
   if ((rc = encode_map_4d(&prm.tmap_q, q, dt, eb, d->head_dim, d->q_heads, d->q_len, d->batch,
                           d->q_stride[2], d->q_stride[1], d->q_stride[0], box_cols, kTileRows)))
     return rc;
+  // A CTA pair loads K in 64-key halves.
+  const bool pair = attn_uses_pair(d);
   if ((rc = encode_map_4d(&prm.tmap_k, k, dt, eb, d->head_dim, d->kv_heads, d->kv_len, d->batch,
-                          d->k_stride[2], d->k_stride[1], d->k_stride[0], box_cols, kTileRows)))
+                          d->k_stride[2], d->k_stride[1], d->k_stride[0], box_cols,
+                          pair ? kTileRows / 2 : kTileRows)))
     return rc;
   if ((rc = encode_map_4d(&prm.tmap_v, v, dt, eb, d->head_dim, d->kv_heads, d->kv_len, d->batch,
                           d->v_stride[2], d->v_stride[1], d->v_stride[0], box_cols, kTileRows)))
@@ -972,7 +1128,8 @@ static int prepare_attn(const dgxm_attn_desc* d, const void* q, const void* k, c
   prm.scale_log2 = scale * kLog2e;
   prm.flags = d->flags;
 
-  *out_grid = dim3((d->q_len + 2 * kTileRows - 1) / (2 * kTileRows), d->q_heads, d->batch);
+  const unsigned qtiles = (d->q_len + 2 * kTileRows - 1) / (2 * kTileRows);
+  *out_grid = dim3(pair ? (qtiles + 1) & ~1u : qtiles, d->q_heads, d->batch);
   return DGXM_OK;
 }
 
@@ -1003,6 +1160,14 @@ static int dispatch_attn_t(const dgxm_attn_desc* d, const AttnParams& prm, dim3 
                  : launch_attn<false, false, EXTRA, DGXM_SM_P_CHUNKS, true, 64>(prm, grid, st);
     return f32 ? launch_attn<false, true, EXTRA, DGXM_SM_P_CHUNKS, false, 64>(prm, grid, st)
                : launch_attn<false, false, EXTRA, DGXM_SM_P_CHUNKS, false, 64>(prm, grid, st);
+  }
+  if (attn_uses_pair(d)) {
+    const bool f32 = d->out_dtype == DGXM_DTYPE_F32;
+    if (d->in_dtype == DGXM_DTYPE_F16)
+      return f32 ? launch_attn<false, true, EXTRA, DGXM_SM_P_CHUNKS, true, kHeadDim, true>(prm, grid, st)
+                 : launch_attn<false, false, EXTRA, DGXM_SM_P_CHUNKS, true, kHeadDim, true>(prm, grid, st);
+    return f32 ? launch_attn<false, true, EXTRA, DGXM_SM_P_CHUNKS, false, kHeadDim, true>(prm, grid, st)
+               : launch_attn<false, false, EXTRA, DGXM_SM_P_CHUNKS, false, kHeadDim, true>(prm, grid, st);
   }
   if (d->in_dtype == DGXM_DTYPE_F16) {
     // fp16 inputs run the library's default release of P.

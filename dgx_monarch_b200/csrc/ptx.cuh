@@ -230,6 +230,13 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
                : "memory");
 }
 
+// The same without release semantics: for hand-offs whose data is ordered by
+// other means (tcgen05 waits and fences around the barrier).
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
+               : "memory");
+}
+
 // 4-D tiled load into this CTA's shared memory whose transaction bytes are
 // reported on `pair_bar`, a shared::cluster address in either CTA of the pair.
 __device__ __forceinline__ void tma_load_4d_pair(uint32_t dst, const void* map, uint32_t pair_bar,
@@ -238,6 +245,16 @@ __device__ __forceinline__ void tma_load_4d_pair(uint32_t dst, const void* map, 
       "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(pair_bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d_pair_hint(uint32_t dst, const void* map, uint32_t pair_bar,
+                                                      int c0, int c1, int c2, int c3, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%3, %4, %5, %6}], [%2], %7;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(pair_bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
+      "l"(policy)
       : "memory");
 }
 
@@ -265,6 +282,18 @@ __device__ __forceinline__ void umma_f16_ss_pair(uint32_t d_tmem, uint64_t a_des
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// D[tmem of both CTAs] (+)= A[tmem of both] * B[smem of both]: each CTA's
+// TMEM holding its 128 A rows at the same address.
+__device__ __forceinline__ void umma_f16_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                                 uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 

@@ -110,9 +110,24 @@ def set_p_chunks(chunks: int) -> None:
     _P_CHUNKS = chunks
 
 
+_CTA_PAIR = True  # 16-bit head-dim-128 attention on CTA pairs (False: DGXM_ATTN_ONE_CTA)
+
+
+def set_cta_pair(on: bool) -> None:
+    """Run the 16-bit, head-dim-128 attention calls this process makes from
+    now on as CTA pairs (the library default: clusters of two CTAs on one
+    TPC, each loading half of every K/V block, one thread issuing the M256
+    tensor-core products of both) or, with False, on single CTAs
+    (DGXM_ATTN_ONE_CTA, kept as a cross-check).  e4m3, head dim 64 and the
+    single P release always run on single CTAs."""
+    global _CTA_PAIR
+    _CTA_PAIR = bool(on)
+
+
 def attn_flags(safe_order: bool = False) -> int:
     """The descriptor flags of one attention call."""
-    return (_lib.ATTN_SAFE_ORDER if safe_order else 0) | (_P_CHUNKS << _lib.ATTN_P_CHUNKS_SHIFT)
+    return ((_lib.ATTN_SAFE_ORDER if safe_order else 0) | (_P_CHUNKS << _lib.ATTN_P_CHUNKS_SHIFT)
+            | (0 if _CTA_PAIR else _lib.ATTN_ONE_CTA))
 
 
 def attn_desc(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor,

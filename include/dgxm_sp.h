@@ -41,6 +41,13 @@ extern "C" {
 /* Drain each P.V product before the next Q.K^T product reuses its tensor
  * memory columns (slower; kept as a cross-check of the fast ordering). */
 #define DGXM_ATTN_SAFE_ORDER 1
+/* 16-bit attention at head dim 128 runs on CTA pairs: clusters of two CTAs
+ * on the two SMs of a TPC, each loading half of every K/V block, with one
+ * thread of the pair issuing M256 tensor-core products for both.  This flag
+ * runs it on single CTAs instead (a cross-check; results agree within the
+ * attention tolerance).  e4m3, head dim 64 and the single P release always
+ * run on single CTAs. */
+#define DGXM_ATTN_ONE_CTA 2
 /* Release the probabilities of each 128-key block to the tensor core in
  * chunks, so P.V starts on the first chunk while the softmax computes the
  * rest: 0 keeps the library default (4 chunks; 2 for e4m3 inputs, whose
