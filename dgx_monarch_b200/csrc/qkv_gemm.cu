@@ -179,6 +179,8 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_gemm_prologue_kernel(const
         if (cta == 0) {
           const int first = it > kQkvStages ? it - kQkvStages : 0;
           for (int i = first; i < it; ++i) mbar_wait(bar(B::kFull + i % kQkvStages), (i / kQkvStages) & 1, nullptr);
+        } else {
+          for (int i = 0; i < 50; ++i) __nanosleep(1000);  // the odd CTA cannot test those barriers
         }
       }
     }
