@@ -46,9 +46,6 @@
 #ifndef DGXM_SM_POLY_MOD
 #define DGXM_SM_POLY_MOD 0
 #endif
-#ifndef DGXM_SM_EX2_PACKED
-#define DGXM_SM_EX2_PACKED 0  // 16-bit kernels: exponentials as packed 16-bit pairs
-#endif
 #ifndef DGXM_SM_PAIR_BARRIER
 #define DGXM_SM_PAIR_BARRIER 1  // exchange row halves over a 64-thread barrier per warp pair
 #endif
@@ -757,15 +754,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
             const int i = ch * kPairs + q;
             uint64_t x = ffma2(pk2(s[2 * i], s[2 * i + 1]), sl2x2, biasx2);
             float p0, p1;
-            uint32_t pp = 0;  // the packed P pair of the packed path
-            if (!FP8 && DGXM_SM_EX2_PACKED) {
-              // The exponent pair rounded to the 16-bit format, one packed
-              // MUFU operation, and the sum taken over the rounded P.
-              upk2(x, p0, p1);
-              pp = ex2_packed16<F16>(pack16<F16>(p0, p1));
-              unpack16<F16>(pp, p0, p1);
-              x = pk2(p0, p1);
-            } else if (DGXM_SM_POLY_MOD > 0 && (i % (DGXM_SM_POLY_MOD > 0 ? DGXM_SM_POLY_MOD : 1)) == 0) {
+            if (DGXM_SM_POLY_MOD > 0 && (i % (DGXM_SM_POLY_MOD > 0 ? DGXM_SM_POLY_MOD : 1)) == 0) {
               x = exp2_poly2(x);
               upk2(x, p0, p1);
             } else {
@@ -779,7 +768,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
               s[2 * i] = p0;
               s[2 * i + 1] = p1;
             } else {
-              pk[q] = DGXM_SM_EX2_PACKED ? pp : pack16<F16>(p0, p1);
+              pk[q] = pack16<F16>(p0, p1);
             }
           }
           if constexpr (FP8) {

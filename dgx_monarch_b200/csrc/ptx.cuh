@@ -526,31 +526,6 @@ __device__ __forceinline__ uint32_t pack16(float lo, float hi) {
     return pack_bf16x2(lo, hi);
 }
 
-// 2^x of both halves of a 16-bit pair in the kernel's format (MUFU, packed):
-// bf16 flushes subnormal results to zero.
-template <bool F16>
-__device__ __forceinline__ uint32_t ex2_packed16(uint32_t x) {
-  uint32_t y;
-  if constexpr (F16)
-    asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
-  else
-    asm("ex2.approx.ftz.bf16x2 %0, %1;" : "=r"(y) : "r"(x));
-  return y;
-}
-
-// A 16-bit pair of the kernel's format -> two floats (exact).
-template <bool F16>
-__device__ __forceinline__ void unpack16(uint32_t v, float& lo, float& hi) {
-  if constexpr (F16) {
-    const __half2 h = *reinterpret_cast<const __half2*>(&v);
-    lo = __low2float(h);
-    hi = __high2float(h);
-  } else {
-    lo = __uint_as_float(v << 16);
-    hi = __uint_as_float(v & 0xFFFF0000u);
-  }
-}
-
 // Four floats -> four e4m3 bytes (saturating), first value in the low byte.
 __device__ __forceinline__ uint32_t pack_e4m3x4(float a, float b, float c, float d) {
   const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
