@@ -296,9 +296,10 @@ DIT = {"hidden": 3072, "heads": 24, "img": 9216, "txt": 512, "latent": (96, 96)}
 DIT_WORKLOAD = ("Flux/Krea2-style joint-attention DiT double block (attention sub-layer): "
                 "1536x1536 image -> 96x96 patch grid = 9216 tokens + 512 text tokens, hidden 3072, "
                 "24 heads x 128, bf16, random-init weights N(0, 0.02); QKV projection with bias, "
-                "per-head RMSNorm on Q/K, 2-axis RoPE and the sequence->head scatter in one tcgen05 GEMM "
-                "per stream, joint [text, image] attention with the inverse all-to-all in its epilogue, "
-                "out projection (cuBLAS)")
+                "per-head RMSNorm on Q/K, 2-axis RoPE and the sequence->head scatter (one fused tcgen05 "
+                "GEMM per stream, or cuBLAS + the prologue kernel, whichever this run timed faster: "
+                "qkv_stage_ms.in_layer), joint [text, image] attention with the inverse all-to-all in its "
+                "epilogue, out projection (cuBLAS)")
 
 
 def time_steps(step, steps: int, warmup: int, graph: bool = False) -> float:
@@ -424,8 +425,22 @@ def run_dit_layer(world: int, rank: int, dev, steps: int, warmup: int, group=Non
         qkv_prologue_scatter(qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2], dst, world=world, rank=rank,
                              norm_mode=_lib.NORM_HEAD, norm_q_w=nq, norm_k_w=nk, rope=table, seg0=t_loc)
 
+    # The QKV stage alone, both ways (rank-local work; peers are not waited for).
+    # The layer runs the faster one, the same on every rank (max over ranks): the
+    # fused GEMM wins at 1-4 ranks, cuBLAS + the prologue kernel at 8, where a
+    # rank projects only 1216 rows.
+    ms_split = time_steps(qkv_split, steps, warmup, graph=True)
+    ms_fused = time_steps(qkv_fused, steps, warmup, graph=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([ms_split, ms_fused], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+        ms_split, ms_fused = t.tolist()
+    qkv_stage = qkv_fused if ms_fused <= ms_split else qkv_split
+
     def step():
-        qkv_fused()
+        qkv_stage()
         win.barrier()
         attention_routed(recv[0], recv[1], recv[2], [win.peer_ptr(r, offs[3]) for r in range(world)],
                          (ls * h * DIM, h * DIM, DIM), world=world, rank=rank, seq_local=ls, seg0=t_loc)
@@ -436,15 +451,14 @@ def run_dit_layer(world: int, rank: int, dev, steps: int, warmup: int, group=Non
 
     ms_eager = time_steps(step, steps, warmup)
     ms = time_steps(step, steps, warmup, graph=True)  # the same work, launched from one graph
-    # The QKV stage alone, both ways (rank-local work; peers are not waited for).
-    ms_split = time_steps(qkv_split, steps, warmup, graph=True)
-    ms_fused = time_steps(qkv_fused, steps, warmup, graph=True)
     if world > 1:
         win.barrier()
         torch.cuda.synchronize()
     win.close()
+    fused = qkv_stage is qkv_fused
     return {"ms": ms, "ms_eager": ms_eager, "ms_qkv_split": ms_split, "ms_qkv_fused": ms_fused,
-            "my_launches": 7 if world > 1 else 5}
+            "qkv_fused_in_layer": fused,
+            "my_launches": (7 if world > 1 else 5) if fused else (6 if world > 1 else 4)}
 
 
 # ----------------------------------------------------------------- ring / CFG workloads (N > 1)
@@ -848,7 +862,8 @@ def main() -> None:
                           "launch": "one CUDA graph per layer (ms_per_layer_eager: the same calls from Python)",
                           "qkv_stage_ms": {"cublas_addmm_plus_prologue_scatter": qkv_split_ms,
                                            "fused_tcgen05_gemm_prologue_scatter": qkv_fused_ms,
-                                           "in_layer": "fused_tcgen05_gemm_prologue_scatter"},
+                                           "in_layer": ("fused_tcgen05_gemm_prologue_scatter" if qkv_fused_ms <= qkv_split_ms
+                                                        else "cublas_addmm_plus_prologue_scatter")},
                           "tflops": dit_layer_flops() / (dit_ms * 1e-3) / 1e12,
                           "frac_of_bf16_peak": dit_layer_flops() / (dit_ms * 1e-3) / 1e12 / (world * peaks["bf16_tflops"]),
                           "parallelism": f"ulysses{world}"},
