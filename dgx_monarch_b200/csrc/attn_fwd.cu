@@ -1037,12 +1037,53 @@ static bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 1
 
 namespace dgxm {
 
+// Whether the current device can hold a cluster of two attention CTAs (both
+// SMs of one TPC free for a 576-thread CTA with about 200 KB of shared
+// memory), asked once per device.  Where it cannot -- a partition without
+// whole TPCs, say -- 16-bit attention runs on single CTAs.
+static bool pair_fits() {
+  static std::atomic<int> state[64];  // 0 not asked, 1 fits, 2 does not
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  if (dev < 64) {
+    const int known = state[dev].load(std::memory_order_acquire);
+    if (known != 0) return known == 1;
+  }
+  using C = AttnCfg<false, false, kHeadDim>;
+  auto kern = attn_fwd_kernel<false, false, false, DGXM_SM_P_CHUNKS, false, kHeadDim, true>;
+  static std::atomic<uint64_t> configured{0};
+  bool fits = false;
+  if (set_smem_limit_once(kern, C::kSmemBytes, configured) == cudaSuccess) {
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof(cfg));
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2);
+    cfg.blockDim = dim3(kAttnThreads);
+    cfg.dynamicSmemBytes = C::kSmemBytes;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    fits = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) == cudaSuccess && clusters > 0;
+  }
+  if (!fits) cudaGetLastError();  // a failed query leaves no error for the next call
+  if (dev < 64) state[dev].store(fits ? 1 : 2, std::memory_order_release);
+  return fits;
+}
+
 // Whether a call runs the CTA-pair kernel: built for 16-bit inputs at head
-// dim 128 with the chunked P release, and not turned off by DGXM_ATTN_ONE_CTA.
+// dim 128 with the chunked P release, not turned off by DGXM_ATTN_ONE_CTA,
+// and the device holds a pair.
 static bool attn_uses_pair(const dgxm_attn_desc* d) {
   const int nch = (d->flags & DGXM_ATTN_P_CHUNKS_MASK) >> DGXM_ATTN_P_CHUNKS_SHIFT;
   return (d->flags & DGXM_ATTN_ONE_CTA) == 0 && d->in_dtype != DGXM_DTYPE_E4M3 &&
-         d->head_dim == kHeadDim && nch != 1;
+         d->head_dim == kHeadDim && nch != 1 && pair_fits();
 }
 
 // Validate the descriptor and fill the kernel parameters (everything but

@@ -45,8 +45,8 @@ extern "C" {
  * on the two SMs of a TPC, each loading half of every K/V block, with one
  * thread of the pair issuing M256 tensor-core products for both.  This flag
  * runs it on single CTAs instead (a cross-check; results agree within the
- * attention tolerance).  e4m3, head dim 64 and the single P release always
- * run on single CTAs. */
+ * attention tolerance).  e4m3, head dim 64, the single P release and devices
+ * that cannot hold a cluster of two such CTAs always run on single CTAs. */
 #define DGXM_ATTN_ONE_CTA 2
 /* Release the probabilities of each 128-key block to the tensor core in
  * chunks, so P.V starts on the first chunk while the softmax computes the
