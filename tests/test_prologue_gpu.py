@@ -210,6 +210,7 @@ def _within_ulps(got, want, ulps):
     (3072, 24, 64, 300, True, False),    # the C2 block width: 72 pair tiles, 48-step K over a 5-stage ring
     (512, 4, 0, 129, False, True),       # image stream only, no RoPE, one row in the odd CTA
     (1024, 8, 100, 4000, True, True),    # 192 pair tiles: every pair alternates its two accumulators
+    (200, 2, 10, 70, True, True),        # K tail (200 = 3 x 64 + 8, zero-filled) and one pair tile of 2 heads
 ])
 def test_fused_qkv_gemm_prologue_matches_separate_ops(lib, hidden, heads, t_loc, i_loc, rope, bias):
     """The QKV Linear + per-head QKNorm + RoPE + sequence->head scatter in one
