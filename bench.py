@@ -58,11 +58,13 @@ def parse_args():
     p.add_argument("--one-cta", action="store_true",
                    help="run 16-bit attention on single CTAs instead of CTA pairs (the library "
                         "default), as a cross-check")
-    p.add_argument("--profile-case", choices=["attn", "fp8", "f16", "kernels"], default=None,
-                   help="instead of the bench: a few launches of one kernel family on one GPU, "
-                        "sized for a profiler capture (attn / fp8 / f16: three attention launches "
-                        "of --case-seq tokens x --case-heads heads; kernels: every support kernel "
-                        "at the Flux/Krea2 block shapes)")
+    p.add_argument("--profile-case", choices=["attn", "fp8", "f16", "kernels", "nvlink"], default=None,
+                   help="instead of the bench: a few launches of one kernel family, sized for a "
+                        "profiler capture (attn / fp8 / f16: three attention launches of --case-seq "
+                        "tokens x --case-heads heads on one GPU; kernels: every support kernel at the "
+                        "Flux/Krea2 block shapes on one GPU; nvlink: rank 0's Ulysses scatter at the "
+                        "Wan layer's P = 2 shapes from one process over two GPUs, its peer half "
+                        "stored over NVLink)")
     p.add_argument("--case-seq", type=int, default=32768)
     p.add_argument("--case-heads", type=int, default=8)
     p.add_argument("--case-batch", type=int, default=1)
@@ -89,6 +91,9 @@ def run_profile_case(args) -> None:
     if args.profile_case == "kernels":
         profile_support_kernels(dev, g)
         return
+    if args.profile_case == "nvlink":
+        profile_nvlink_scatter(g)
+        return
     if args.profile_case == "fp8":
         from dgx_monarch_b200.prologue import quantize_e4m3_per_head
 
@@ -105,6 +110,43 @@ def run_profile_case(args) -> None:
         for _ in range(3):
             attention_fwd(q, k, v, out=out, return_lse=False)
     torch.cuda.synchronize()
+
+
+def profile_nvlink_scatter(g) -> None:
+    """Rank 0's sequence->head scatter of the Wan layer at P = 2, in one process
+    over two GPUs: q/k/v (37,800 local rows x 40 heads x 128, bf16) on cuda:0,
+    head slice [0, 20) stored into rank 0's receive tensors on cuda:0 and head
+    slice [20, 40) into rank 1's on cuda:1 through peer access -- 580.6 MB over
+    NVLink per launch, for the launching GPU's NVLink byte counters.  Three
+    launches, the last timed with CUDA events."""
+    import torch
+    from cuda.bindings import runtime as cudart
+
+    from dgx_monarch_b200.ulysses import ulysses_scatter
+
+    if torch.cuda.device_count() < 2:
+        raise SystemExit("the nvlink case needs two GPUs in this process")
+    torch.cuda.set_device(0)
+    (err,) = cudart.cudaDeviceEnablePeerAccess(1, 0)
+    if err not in (cudart.cudaError_t.cudaSuccess, cudart.cudaError_t.cudaErrorPeerAccessAlreadyEnabled):
+        raise SystemExit(f"peer access from GPU 0 to GPU 1: {err}")
+    ls, h = SEQ // 2, HEADS
+    x = [torch.randn(1, ls, h, DIM, device="cuda:0", generator=g).bfloat16() for _ in range(3)]
+    recv = [[torch.empty(1, 2 * ls, h // 2, DIM, device=f"cuda:{r}", dtype=torch.bfloat16) for r in range(2)]
+            for _ in range(3)]
+    dst = [[recv[t][r].data_ptr() for r in range(2)] for t in range(3)]
+    for _ in range(2):
+        ulysses_scatter(x, dst, world=2, rank=0)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    ulysses_scatter(x, dst, world=2, rank=0)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    peer_bytes = 3 * ls * (h // 2) * DIM * 2
+    print(f"scatter {ms:.3f} ms, {peer_bytes / 1e6:.1f} MB to the peer: {peer_bytes / ms / 1e6:.1f} GB/s per direction")
+    # The peer half arrived: rank 1's receive rows [0, ls) hold heads [20, 40).
+    assert torch.equal(recv[0][1][0, :ls].to("cuda:0"), x[0][0, :, h // 2:])
 
 
 def profile_support_kernels(dev, g) -> None:
