@@ -117,8 +117,10 @@ def profile_nvlink_scatter(g) -> None:
     over two GPUs: q/k/v (37,800 local rows x 40 heads x 128, bf16) on cuda:0,
     head slice [0, 20) stored into rank 0's receive tensors on cuda:0 and head
     slice [20, 40) into rank 1's on cuda:1 through peer access -- 580.6 MB over
-    NVLink per launch, for the launching GPU's NVLink byte counters.  Three
-    launches, the last timed with CUDA events."""
+    NVLink per launch; then the store half of the ring-2 full-context K/V
+    gather, rank 0's K and V into both ranks' full K/V -- 774.1 MB over NVLink
+    per launch.  For the launching GPU's NVLink byte counters; three launches
+    of each, the last timed with CUDA events."""
     import torch
     from cuda.bindings import runtime as cudart
 
@@ -147,6 +149,26 @@ def profile_nvlink_scatter(g) -> None:
     print(f"scatter {ms:.3f} ms, {peer_bytes / 1e6:.1f} MB to the peer: {peer_bytes / ms / 1e6:.1f} GB/s per direction")
     # The peer half arrived: rank 1's receive rows [0, ls) hold heads [20, 40).
     assert torch.equal(recv[0][1][0, :ls].to("cuda:0"), x[0][0, :, h // 2:])
+    del recv
+    # The store half of the Wan ring-2 full-context gather: rank 0's K/V block
+    # (37,800 rows x 40 heads x 128) into rows [0, ls) of both ranks' full K/V.
+    from dgx_monarch_b200.ring import kv_gather_store
+
+    k, v = x[1], x[2]
+    full = [[torch.empty(1, 2 * ls, h, DIM, device=f"cuda:{r}", dtype=torch.bfloat16) for r in range(2)]
+            for _ in range(2)]
+    dk, dv = [t.data_ptr() for t in full[0]], [t.data_ptr() for t in full[1]]
+    for _ in range(2):
+        kv_gather_store(k, v, dk, dv, world=2, rank=0)
+    e0.record()
+    kv_gather_store(k, v, dk, dv, world=2, rank=0)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    peer_bytes = 2 * ls * h * DIM * 2
+    print(f"kv gather store {ms:.3f} ms, {peer_bytes / 1e6:.1f} MB to the peer: "
+          f"{peer_bytes / ms / 1e6:.1f} GB/s per direction")
+    assert torch.equal(full[1][1][0, :ls].to("cuda:0"), v[0])
 
 
 def profile_support_kernels(dev, g) -> None:
