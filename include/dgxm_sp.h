@@ -548,7 +548,9 @@ int dgxm_shared_amax_scale(dgxm_comm* comm, const void* x, int64_t rows, int64_t
  * (norm_mode DGXM_NORM_HEAD: bf16(y * rsqrt(mean(y^2) + eps)) then
  * bf16(n * w), weights of 128 bf16 or NULL) and RoPE (rope: (seq_local, 64, 2)
  * fp32 cos/sin by local row, or NULL; x, W and rope 16-byte aligned; heads
- * even, two heads per tile), and every 128-wide head row stored into
+ * even, two heads per tile; the kernel runs as clusters of two CTAs, and a
+ * device that cannot hold one returns DGXM_ERR_CUDA), and every 128-wide
+ * head row stored into
  * dst[t * world + r] -- rank r's contiguous (world * seq_local, heads/world,
  * 128) bf16 receive tensor t (0 q, 1 k, 2 v) -- at the gathered row of local
  * row row0 + i (joint order seg0 as in dgxm_a2a_desc).  One tcgen05 kernel:
