@@ -350,6 +350,21 @@ __device__ __forceinline__ void raise_abort(volatile int* abort_flag, int bits) 
   *abort_flag = 1;
 }
 
+// K/V ring stages of a CTA-pair kernel (16 KB each: half a block of K or V);
+// 8 holds the same bytes as the single-CTA ring.
+#ifndef DGXM_PAIR_STAGES
+#define DGXM_PAIR_STAGES 8
+#endif
+constexpr int kPairStages = DGXM_PAIR_STAGES;
+
+// Dynamic shared memory of a kernel variant: a pair's ring of kPairStages
+// half-tile stages in place of the single-CTA ring.
+template <bool FP8, bool F16, int HD, bool PAIR>
+__host__ __device__ constexpr int attn_smem_bytes() {
+  using C = AttnCfg<FP8, F16, HD>;
+  return PAIR ? C::kSmemBytes - C::kStages * C::kTileBytes + kPairStages * (C::kTileBytes / 2) : C::kSmemBytes;
+}
+
 // F16: 16-bit inputs (and P) are fp16 instead of bf16; a 16-bit output is
 // then fp16 too.
 //
@@ -368,7 +383,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_fwd_kernel(const __grid_
   static_assert(!PAIR || (!FP8 && HD == kHeadDim && kPChunks > 1 && DGXM_SM_WARP_ARRIVE),
                 "CTA pairs: 16-bit inputs, head dim 128, chunked P release, one arrival per warp");
   constexpr int kStageBytes = PAIR ? C::kTileBytes / 2 : C::kTileBytes;
-  constexpr int kStages = PAIR ? 2 * C::kStages : C::kStages;  // the same ring bytes
+  constexpr int kStages = PAIR ? kPairStages : C::kStages;
+  static_assert(attn_smem_bytes<FP8, F16, HD, PAIR>() <= 227 * 1024, "shared memory of one CTA");
   using B = Bars<kStages, kPChunks>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -1007,7 +1023,8 @@ static int launch_attn(const AttnParams& prm, dim3 grid, cudaStream_t stream) {
   using C = AttnCfg<FP8, F16, HD>;
   static std::atomic<uint64_t> configured{0};  // one bit per device ordinal
   auto kern = attn_fwd_kernel<FP8, OUT_F32, EXTRA, NCH, F16, HD, PAIR>;
-  DGXM_CUDA_TRY(set_smem_limit_once(kern, C::kSmemBytes, configured));
+  constexpr int kSmem = attn_smem_bytes<FP8, F16, HD, PAIR>();
+  DGXM_CUDA_TRY(set_smem_limit_once(kern, kSmem, configured));
   if constexpr (PAIR) {
     // Clusters of two along the Q tiles (the grid's x extent is even).
     cudaLaunchConfig_t cfg;
@@ -1019,13 +1036,13 @@ static int launch_attn(const AttnParams& prm, dim3 grid, cudaStream_t stream) {
     attr[0].val.clusterDim.z = 1;
     cfg.gridDim = grid;
     cfg.blockDim = dim3(kAttnThreads);
-    cfg.dynamicSmemBytes = C::kSmemBytes;
+    cfg.dynamicSmemBytes = kSmem;
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     DGXM_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, prm));
   } else {
-    kern<<<grid, kAttnThreads, C::kSmemBytes, stream>>>(prm);
+    kern<<<grid, kAttnThreads, kSmem, stream>>>(prm);
     DGXM_CUDA_TRY(cudaGetLastError());
   }
   return DGXM_OK;
@@ -1052,11 +1069,11 @@ static bool pair_fits() {
     const int known = state[dev].load(std::memory_order_acquire);
     if (known != 0) return known == 1;
   }
-  using C = AttnCfg<false, false, kHeadDim>;
   auto kern = attn_fwd_kernel<false, false, false, DGXM_SM_P_CHUNKS, false, kHeadDim, true>;
   static std::atomic<uint64_t> configured{0};
   bool fits = false;
-  if (set_smem_limit_once(kern, C::kSmemBytes, configured) == cudaSuccess) {
+  constexpr int kSmem = attn_smem_bytes<false, false, kHeadDim, true>();
+  if (set_smem_limit_once(kern, kSmem, configured) == cudaSuccess) {
     cudaLaunchConfig_t cfg;
     memset(&cfg, 0, sizeof(cfg));
     cudaLaunchAttribute attr[1];
@@ -1066,7 +1083,7 @@ static bool pair_fits() {
     attr[0].val.clusterDim.z = 1;
     cfg.gridDim = dim3(2);
     cfg.blockDim = dim3(kAttnThreads);
-    cfg.dynamicSmemBytes = C::kSmemBytes;
+    cfg.dynamicSmemBytes = kSmem;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int clusters = 0;

@@ -239,7 +239,6 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_gemm_prologue_kernel(const
       const int which = gh / p.heads;                  // 0 q, 1 k, 2 v
       const int head = gh - which * p.heads;
       const int m0 = mt * kQkvPairM + static_cast<int>(cta) * kQkvTile + q * 32;  // this warp's first row
-      const int m = m0 + lane;
       const bool rope = which < 2 && p.rope != nullptr;
       // The first half of the warp's 32 RoPE rows is fetched while the MMAs run.
       if (rope) qkv_stage_rope(p, stage_rows, m0, lane, 0);
