@@ -361,7 +361,7 @@ DIT_WORKLOAD = ("Flux/Krea2-style joint-attention DiT double block (attention su
                 "1536x1536 image -> 96x96 patch grid = 9216 tokens + 512 text tokens, hidden 3072, "
                 "24 heads x 128, bf16, random-init weights N(0, 0.02); QKV projection with bias, "
                 "per-head RMSNorm on Q/K, 2-axis RoPE and the sequence->head scatter (one fused tcgen05 "
-                "GEMM per stream, or cuBLAS + the prologue kernel, whichever this run timed faster: "
+                "GEMM launch for both streams, or cuBLAS + the prologue kernel, whichever this run timed faster: "
                 "qkv_stage_ms.in_layer), joint [text, image] attention with the inverse all-to-all in its "
                 "epilogue, out projection (cuBLAS)")
 
@@ -441,7 +441,7 @@ def run_dit_layer(world: int, rank: int, dev, steps: int, warmup: int, group=Non
 
     from dgx_monarch_b200 import _lib
     from dgx_monarch_b200.comm import PeerWindows
-    from dgx_monarch_b200.prologue import qkv_gemm_prologue_scatter, qkv_prologue_scatter, rope_table
+    from dgx_monarch_b200.prologue import qkv_gemm_prologue_scatter_streams, qkv_prologue_scatter, rope_table
     from dgx_monarch_b200.ulysses import attention_routed
 
     hid, h = DIT["hidden"], DIT["heads"]
@@ -476,11 +476,11 @@ def run_dit_layer(world: int, rank: int, dev, steps: int, warmup: int, group=Non
     dst = [[win.peer_ptr(r, o) for r in range(world)] for o in offs[:3]]
 
     def qkv_fused():
-        # QKV Linear + QKNorm + RoPE + sequence->head scatter, one kernel per stream.
-        for x, wq, bq, row0 in ((x_txt, w_qkv_txt, b_qkv_txt, 0), (x_img, w_qkv_img, b_qkv_img, t_loc)):
-            qkv_gemm_prologue_scatter(x, wq, dst, world=world, rank=rank, seq_local=ls, row0=row0,
-                                      seg0=t_loc, bias=bq, norm_mode=_lib.NORM_HEAD, norm_q_w=nq,
-                                      norm_k_w=nk, rope=table)
+        # QKV Linear + QKNorm + RoPE + sequence->head scatter of both streams, one launch.
+        qkv_gemm_prologue_scatter_streams(
+            [dict(x=x_txt, w_qkv=w_qkv_txt, bias=b_qkv_txt, norm_q_w=nq, norm_k_w=nk, row0=0),
+             dict(x=x_img, w_qkv=w_qkv_img, bias=b_qkv_img, norm_q_w=nq, norm_k_w=nk, row0=t_loc)],
+            dst, world=world, rank=rank, seq_local=ls, seg0=t_loc, norm_mode=_lib.NORM_HEAD, rope=table)
 
     def qkv_split():
         # cuBLAS QKV Linear per stream, then the fused norm + RoPE + scatter kernel.
@@ -522,7 +522,7 @@ def run_dit_layer(world: int, rank: int, dev, steps: int, warmup: int, group=Non
     fused = qkv_stage is qkv_fused
     return {"ms": ms, "ms_eager": ms_eager, "ms_qkv_split": ms_split, "ms_qkv_fused": ms_fused,
             "qkv_fused_in_layer": fused,
-            "my_launches": (7 if world > 1 else 5) if fused else (6 if world > 1 else 4)}
+            "my_launches": 6 if world > 1 else 4}
 
 
 # ----------------------------------------------------------------- ring / CFG workloads (N > 1)

@@ -135,6 +135,19 @@ class QkvGemmDesc(ctypes.Structure):
     ]
 
 
+class QkvStream(ctypes.Structure):
+    _fields_ = [
+        ("x", ctypes.c_void_p),
+        ("w_qkv", ctypes.c_void_p),
+        ("bias", ctypes.c_void_p),
+        ("norm_q_w", ctypes.c_void_p),
+        ("norm_k_w", ctypes.c_void_p),
+        ("x_row_stride", ctypes.c_int64),
+        ("m", ctypes.c_int32),
+        ("row0", ctypes.c_int32),
+    ]
+
+
 NORM_NONE, NORM_HIDDEN, NORM_HEAD = 0, 1, 2
 
 
@@ -221,6 +234,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "dgxm_full_context_window_bytes": (ctypes.c_int64, [ctypes.POINTER(AttnDesc), _I32]),
     "dgxm_qkv_gemm_prologue_scatter": (ctypes.c_int, [ctypes.POINTER(QkvGemmDesc), _P, _P, _P, _P, _P, _P,
                                                       _P, _P]),
+    "dgxm_qkv_gemm_prologue_scatter_streams": (ctypes.c_int, [ctypes.POINTER(QkvGemmDesc), _I32,
+                                                              ctypes.POINTER(QkvStream), _P, _P, _P]),
     "dgxm_copy_2d": (ctypes.c_int, [_P, ctypes.c_int64, _P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _P]),
     "dgxm_cfg_combine": (ctypes.c_int, [_P, _P, ctypes.c_int64, _I32, ctypes.c_double, _P, _P]),
     "dgxm_seq_allgather": (ctypes.c_int, [_P, ctypes.POINTER(SeqGatherDesc), _P, ctypes.c_int64, _P]),

@@ -46,18 +46,37 @@ constexpr int kQkvPairStageBytes = 2 * kQkvStageBytes;
 constexpr int kQkvStagingBytes = 8 * 32 * 256;       // per epilogue warp: 32 head rows
 constexpr int kQkvSmemBytes = 1024 + kQkvStages * kQkvStageBytes + kQkvStagingBytes + 512;
 
-struct __align__(64) QkvGemmParams {
+// One token stream's projection: its rows, weight, bias and QKNorm weights.
+struct __align__(64) QkvProblem {
   CUtensorMap tmap_x;  // dims (K, 1, M, 1), box (64, 1, 128, 1)
   CUtensorMap tmap_w;  // dims (K, 1, N, 1), box (64, 1, 128, 1)
-  int m, k_tiles, heads, n_tiles, m_tiles;
   const __nv_bfloat16* bias;     // N entries or NULL
   const __nv_bfloat16* norm_w[2];
+  int m, m_tiles, tiles, row0;   // rows, pair-tile rows, pair tiles, local row of the first row
+};
+
+// Up to two streams (a joint block's text and image) in one launch: their
+// pair tiles are numbered one stream after the other.  The streams share the
+// input width, the heads, the RoPE table and the receive tensors.
+struct __align__(64) QkvGemmParams {
+  QkvProblem prob[2];
+  int n_prob, k_tiles, heads, n_tiles;
   int norm_head;                 // per-head RMSNorm on q and k
   float eps;
   const float* rope;             // (seq_local, 64, 2) cos/sin by local row, or NULL
   char* dst[3][DGXM_MAX_WORLD];  // (S, heads/world, 128) bf16 receive tensors
-  int world, rank, seq_local, row0, seg0;
+  int world, rank, seq_local, seg0;
 };
+
+// The stream of pair tile `tile` and the tile's index within it.
+__device__ __forceinline__ const QkvProblem& qkv_problem(const QkvGemmParams& p, int tile, int& local) {
+  if (tile < p.prob[0].tiles) {
+    local = tile;
+    return p.prob[0];
+  }
+  local = tile - p.prob[0].tiles;
+  return p.prob[1];
+}
 
 // Barriers of each CTA.  The even CTA's Full and AccEmpty count for the pair;
 // Empty and AccFull are signalled in both CTAs by the even CTA's commits.
@@ -93,16 +112,16 @@ __device__ __forceinline__ void qkv_tile_coords(int tile, int m_tiles, int n_til
 // One half of a warp's 32 RoPE rows (pairs 32h .. 32h + 31 of each row: 256
 // contiguous bytes) into its staging rows, two rows per instruction; 16-byte
 // chunk c of row r goes to chunk c ^ (r & 15), as the output rows do.
-__device__ __forceinline__ void qkv_stage_rope(const QkvGemmParams& p, uint8_t* stage_rows, int m0, int lane,
-                                               int h) {
+__device__ __forceinline__ void qkv_stage_rope(const float* rope, const QkvProblem& pr, uint8_t* stage_rows,
+                                               int m0, int lane, int h) {
   const int cc = lane & 15;
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
     const int rr = 2 * j + (lane >> 4);
     const int mr = m0 + rr;
-    if (mr < p.m)
+    if (mr < pr.m)
       cp_async16(smem_u32(stage_rows + rr * 256 + ((cc ^ (rr & 15)) << 4)),
-                 p.rope + static_cast<int64_t>(p.row0 + mr) * 128 + h * 64 + cc * 4);
+                 rope + static_cast<int64_t>(pr.row0 + mr) * 128 + h * 64 + cc * 4);
   }
 }
 
@@ -121,7 +140,7 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_gemm_prologue_kernel(const
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t cta = cluster_ctarank();     // 0: issues the pair's MMAs
   const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
-  const int tiles = p.m_tiles * p.n_tiles;
+  const int tiles = p.prob[0].tiles + (p.n_prob > 1 ? p.prob[1].tiles : 0);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kQkvStages; ++s) {
@@ -137,8 +156,10 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_gemm_prologue_kernel(const
     mbar_fence_init();
   }
   if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&p.tmap_x);
-    tma_prefetch_desc(&p.tmap_w);
+    for (int i = 0; i < p.n_prob; ++i) {
+      tma_prefetch_desc(&p.prob[i].tmap_x);
+      tma_prefetch_desc(&p.prob[i].tmap_w);
+    }
   }
   if (warp == 1) {
     tmem_alloc_pair(smem_u32(tmem_slot), 2 * kQkvTileN);
@@ -155,8 +176,9 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_gemm_prologue_kernel(const
       int it = 0;
       bool ok = true;
       for (int tile = pair; ok && tile < tiles; tile += pairs) {
-        int mt, nt;
-        qkv_tile_coords(tile, p.m_tiles, p.n_tiles, mt, nt);
+        int lt, mt, nt;
+        const QkvProblem& pr = qkv_problem(p, tile, lt);
+        qkv_tile_coords(lt, pr.m_tiles, p.n_tiles, mt, nt);
         for (int kt = 0; kt < p.k_tiles; ++kt, ++it) {
           const int s = it % kQkvStages;
           if (!mbar_wait(bar(B::kEmpty + s), ((it / kQkvStages) & 1) ^ 1, abort_flag)) {
@@ -166,8 +188,8 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_gemm_prologue_kernel(const
           const uint32_t dst = base + s * kQkvStageBytes;
           const uint32_t full = mapa_shared(bar(B::kFull + s), 0);
           if (cta == 0) mbar_expect_tx(bar(B::kFull + s), kQkvPairStageBytes);
-          tma_load_4d_pair(dst, &p.tmap_x, full, kt * kQkvBk, 0, mt * kQkvPairM + cta * kQkvTile, 0);
-          tma_load_4d_pair(dst + kQkvHalfBytes, &p.tmap_w, full, kt * kQkvBk, 0,
+          tma_load_4d_pair(dst, &pr.tmap_x, full, kt * kQkvBk, 0, mt * kQkvPairM + cta * kQkvTile, 0);
+          tma_load_4d_pair(dst + kQkvHalfBytes, &pr.tmap_w, full, kt * kQkvBk, 0,
                            nt * kQkvTileN + cta * kQkvTile, 0);
         }
       }
@@ -231,8 +253,9 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_gemm_prologue_kernel(const
     int u = 0;
     for (int tile = pair; tile < tiles; tile += pairs, ++u) {
       const int a = u & 1;
-      int mt, nt;
-      qkv_tile_coords(tile, p.m_tiles, p.n_tiles, mt, nt);
+      int lt, mt, nt;
+      const QkvProblem& pr = qkv_problem(p, tile, lt);
+      qkv_tile_coords(lt, pr.m_tiles, p.n_tiles, mt, nt);
       // This warp group's head of the tile (q, k and v each span a whole
       // number of tiles, the head count being even).
       const int gh = nt * (kQkvTileN / kQkvTile) + hs;  // head over q | k | v
@@ -241,7 +264,7 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_gemm_prologue_kernel(const
       const int m0 = mt * kQkvPairM + static_cast<int>(cta) * kQkvTile + q * 32;  // this warp's first row
       const bool rope = which < 2 && p.rope != nullptr;
       // The first half of the warp's 32 RoPE rows is fetched while the MMAs run.
-      if (rope) qkv_stage_rope(p, stage_rows, m0, lane, 0);
+      if (rope) qkv_stage_rope(p.rope, pr, stage_rows, m0, lane, 0);
       const bool got = __all_sync(0xffffffffu, mbar_wait(bar(B::kAccFull + a), (u >> 1) & 1, abort_flag));
       if (!got) {
         cp_async_wait_all();
@@ -262,10 +285,10 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_gemm_prologue_kernel(const
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           float v0 = __uint_as_float(r[2 * i]), v1 = __uint_as_float(r[2 * i + 1]);
-          if (p.bias != nullptr) {
+          if (pr.bias != nullptr) {
             const int n = gh * kQkvTile + c * 32 + 2 * i;
-            v0 += __bfloat162float(p.bias[n]);
-            v1 += __bfloat162float(p.bias[n + 1]);
+            v0 += __bfloat162float(pr.bias[n]);
+            v1 += __bfloat162float(pr.bias[n + 1]);
           }
           const uint32_t packed = pack_bf16x2(v0, v1);
           y[c * 16 + i] = packed;
@@ -281,7 +304,7 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_gemm_prologue_kernel(const
       if (lane == 0) mbar_arrive_cluster(acc_empty + a * 8);
       if (which < 2 && p.norm_head) {
         const float sc = rsqrtf(ss / 128.f + p.eps);
-        const __nv_bfloat16* w = p.norm_w[which];
+        const __nv_bfloat16* w = pr.norm_w[which];
 #pragma unroll
         for (int i = 0; i < 64; ++i) {
           float x0 = __uint_as_float(y[i] << 16), x1 = __uint_as_float(y[i] & 0xFFFF0000u);
@@ -297,7 +320,7 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_gemm_prologue_kernel(const
       if (rope) {
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          if (h == 1) qkv_stage_rope(p, stage_rows, m0, lane, 1);
+          if (h == 1) qkv_stage_rope(p.rope, pr, stage_rows, m0, lane, 1);
           cp_async_wait_all();
           __syncwarp();
           // Row `lane`'s pairs 32h + 2c and 32h + 2c + 1: (cos, sin, cos, sin).
@@ -331,9 +354,9 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_gemm_prologue_kernel(const
       for (int j = 0; j < 16; ++j) {
         const int rr = 2 * j + (lane >> 4);
         const int mr = m0 + rr;
-        if (mr < p.m) {
+        if (mr < pr.m) {
           const uint4 v = reinterpret_cast<const uint4*>(stage_rows + rr * 256)[cc ^ (rr & 15)];
-          const int64_t grow = qkv_gathered_row(p.rank, p.row0 + mr, p.seq_local, p.world, p.seg0);
+          const int64_t grow = qkv_gathered_row(p.rank, pr.row0 + mr, p.seq_local, p.world, p.seg0);
           reinterpret_cast<uint4*>(dst_base + (grow * hl + hh) * 256)[cc] = v;
         }
       }
@@ -350,13 +373,14 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_gemm_prologue_kernel(const
 
 }  // namespace dgxm
 
-extern "C" int dgxm_qkv_gemm_prologue_scatter(const dgxm_qkv_gemm_desc* d, const void* x,
-                                              const void* w_qkv, const void* bias,
-                                              const void* norm_q_w, const void* norm_k_w,
-                                              const float* rope, void* const* dst, void* stream) {
-  using namespace dgxm;
-  if (d == nullptr || x == nullptr || w_qkv == nullptr || dst == nullptr)
-    return fail(DGXM_ERR_INVALID, "NULL descriptor, input, weight or destination");
+namespace dgxm {
+
+// Check and launch the grouped projection of n (1 or 2) streams.
+static int qkv_launch(const dgxm_qkv_gemm_desc* d, int n, const dgxm_qkv_stream* st, const float* rope,
+                      void* const* dst, void* stream) {
+  if (d == nullptr || st == nullptr || dst == nullptr)
+    return fail(DGXM_ERR_INVALID, "NULL descriptor, streams or destination");
+  if (n < 1 || n > 2) return fail(DGXM_ERR_INVALID, "%d streams (1 or 2)", n);
   if (d->world < 1 || d->world > DGXM_MAX_WORLD || d->rank < 0 || d->rank >= d->world)
     return fail(DGXM_ERR_INVALID, "rank %d / world %d out of range", d->rank, d->world);
   if (d->heads <= 0 || d->heads % d->world)
@@ -364,38 +388,58 @@ extern "C" int dgxm_qkv_gemm_prologue_scatter(const dgxm_qkv_gemm_desc* d, const
   if (d->heads % (kQkvTileN / kQkvTile))
     return fail(DGXM_ERR_UNSUPPORTED, "the fused QKV kernel takes an even head count (two heads per tile), got %d",
                 d->heads);
-  if (d->m < 0 || d->k <= 0 || d->k % 8 || d->x_row_stride % 8 || d->x_row_stride < d->k)
-    return fail(DGXM_ERR_INVALID, "m %d / k %d / row stride %lld: k and the stride must be multiples of 8",
-                d->m, d->k, (long long)d->x_row_stride);
-  if (d->seq_local <= 0 || d->row0 < 0 || d->row0 + d->m > d->seq_local || d->seg0 < 0 || d->seg0 >= d->seq_local)
-    return fail(DGXM_ERR_INVALID, "rows [%d, %d) do not fit the %d local rows (seg0 %d)", d->row0,
-                d->row0 + d->m, d->seq_local, d->seg0);
+  if (d->k <= 0 || d->k % 8)
+    return fail(DGXM_ERR_INVALID, "k %d must be a positive multiple of 8", d->k);
+  if (d->seq_local <= 0 || d->seg0 < 0 || d->seg0 >= d->seq_local)
+    return fail(DGXM_ERR_INVALID, "seg0 %d does not split the %d local rows", d->seg0, d->seq_local);
   if (d->norm_mode != DGXM_NORM_NONE && d->norm_mode != DGXM_NORM_HEAD)
     return fail(DGXM_ERR_UNSUPPORTED, "the fused QKV kernel applies per-head norms only (mode %d)", d->norm_mode);
-  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w_qkv) | reinterpret_cast<uintptr_t>(rope)) % 16)
-    return fail(DGXM_ERR_INVALID, "x, w_qkv and rope must be 16-byte aligned");
+  if (reinterpret_cast<uintptr_t>(rope) % 16) return fail(DGXM_ERR_INVALID, "rope must be 16-byte aligned");
+  for (int i = 0; i < n; ++i) {
+    const dgxm_qkv_stream& s = st[i];
+    if (s.m == 0) continue;  // an empty stream may pass NULL pointers
+    if (s.x == nullptr || s.w_qkv == nullptr)
+      return fail(DGXM_ERR_INVALID, "stream %d: NULL input or weight", i);
+    if (s.m < 0 || s.x_row_stride % 8 || s.x_row_stride < d->k)
+      return fail(DGXM_ERR_INVALID, "stream %d: m %d / row stride %lld (a multiple of 8, at least k %d)", i, s.m,
+                  (long long)s.x_row_stride, d->k);
+    if (s.row0 < 0 || s.row0 + s.m > d->seq_local)
+      return fail(DGXM_ERR_INVALID, "stream %d: rows [%d, %d) do not fit the %d local rows", i, s.row0,
+                  s.row0 + s.m, d->seq_local);
+    if ((reinterpret_cast<uintptr_t>(s.x) | reinterpret_cast<uintptr_t>(s.w_qkv)) % 16)
+      return fail(DGXM_ERR_INVALID, "stream %d: x and w_qkv must be 16-byte aligned", i);
+  }
   for (int i = 0; i < 3 * d->world; ++i)
     if (dst[i] == nullptr || reinterpret_cast<uintptr_t>(dst[i]) % 16)
       return fail(DGXM_ERR_INVALID, "destination %d is NULL or not 16-byte aligned", i);
-  if (d->m == 0) return DGXM_OK;
   QkvGemmParams p;
   memset(&p, 0, sizeof(p));
-  const int64_t n = 3LL * d->heads * 128;
-  int rc;
-  if ((rc = encode_map_4d(&p.tmap_x, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, d->k, 1, d->m, 1, d->k,
-                          d->x_row_stride, d->x_row_stride * d->m, kQkvBk, kQkvTile)))
-    return rc;
-  if ((rc = encode_map_4d(&p.tmap_w, w_qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, d->k, 1, n, 1, d->k, d->k,
-                          d->k * n, kQkvBk, kQkvTile)))
-    return rc;
-  p.m = d->m;
+  const int64_t nw = 3LL * d->heads * 128;
   p.k_tiles = (d->k + kQkvBk - 1) / kQkvBk;
   p.heads = d->heads;
   p.n_tiles = 3 * d->heads * kQkvTile / kQkvTileN;
-  p.m_tiles = (d->m + kQkvPairM - 1) / kQkvPairM;
-  p.bias = static_cast<const __nv_bfloat16*>(bias);
-  p.norm_w[0] = static_cast<const __nv_bfloat16*>(norm_q_w);
-  p.norm_w[1] = static_cast<const __nv_bfloat16*>(norm_k_w);
+  int tiles = 0;
+  for (int i = 0; i < n; ++i) {
+    const dgxm_qkv_stream& s = st[i];
+    if (s.m == 0) continue;  // no rows, no tiles
+    QkvProblem& pr = p.prob[p.n_prob++];
+    int rc;
+    if ((rc = encode_map_4d(&pr.tmap_x, s.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, d->k, 1, s.m, 1, d->k,
+                            s.x_row_stride, s.x_row_stride * s.m, kQkvBk, kQkvTile)))
+      return rc;
+    if ((rc = encode_map_4d(&pr.tmap_w, s.w_qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, d->k, 1, nw, 1, d->k, d->k,
+                            d->k * nw, kQkvBk, kQkvTile)))
+      return rc;
+    pr.bias = static_cast<const __nv_bfloat16*>(s.bias);
+    pr.norm_w[0] = static_cast<const __nv_bfloat16*>(s.norm_q_w);
+    pr.norm_w[1] = static_cast<const __nv_bfloat16*>(s.norm_k_w);
+    pr.m = s.m;
+    pr.m_tiles = (s.m + kQkvPairM - 1) / kQkvPairM;
+    pr.tiles = pr.m_tiles * p.n_tiles;
+    pr.row0 = s.row0;
+    tiles += pr.tiles;
+  }
+  if (tiles == 0) return DGXM_OK;
   p.norm_head = d->norm_mode == DGXM_NORM_HEAD;
   p.eps = d->eps;
   p.rope = rope;
@@ -404,7 +448,6 @@ extern "C" int dgxm_qkv_gemm_prologue_scatter(const dgxm_qkv_gemm_desc* d, const
   p.world = d->world;
   p.rank = d->rank;
   p.seq_local = d->seq_local;
-  p.row0 = d->row0;
   p.seg0 = d->seg0;
   int dev = 0;
   DGXM_CUDA_TRY(cudaGetDevice(&dev));
@@ -431,9 +474,41 @@ extern "C" int dgxm_qkv_gemm_prologue_scatter(const dgxm_qkv_gemm_desc* d, const
     if (pairs <= 0) return fail(DGXM_ERR_CUDA, "no CTA pair of the fused QKV kernel fits on device %d", dev);
     if (dev < 64) max_pairs[dev].store(pairs);
   }
-  const int tiles = p.m_tiles * p.n_tiles;
   cfg.gridDim = dim3(2 * (tiles < pairs ? tiles : pairs));
   DGXM_CUDA_TRY(cudaLaunchKernelEx(&cfg, qkv_gemm_prologue_kernel, p));
   DGXM_CUDA_TRY(cudaGetLastError());
   return DGXM_OK;
+}
+
+}  // namespace dgxm
+
+extern "C" int dgxm_qkv_gemm_prologue_scatter(const dgxm_qkv_gemm_desc* d, const void* x,
+                                              const void* w_qkv, const void* bias,
+                                              const void* norm_q_w, const void* norm_k_w,
+                                              const float* rope, void* const* dst, void* stream) {
+  using namespace dgxm;
+  if (d == nullptr || x == nullptr || w_qkv == nullptr || dst == nullptr)
+    return fail(DGXM_ERR_INVALID, "NULL descriptor, input, weight or destination");
+  if (d->m < 0 || d->k <= 0 || d->k % 8 || d->x_row_stride % 8 || d->x_row_stride < d->k)
+    return fail(DGXM_ERR_INVALID, "m %d / k %d / row stride %lld: k and the stride must be multiples of 8",
+                d->m, d->k, (long long)d->x_row_stride);
+  if (d->seq_local <= 0 || d->row0 < 0 || d->row0 + d->m > d->seq_local || d->seg0 < 0 || d->seg0 >= d->seq_local)
+    return fail(DGXM_ERR_INVALID, "rows [%d, %d) do not fit the %d local rows (seg0 %d)", d->row0,
+                d->row0 + d->m, d->seq_local, d->seg0);
+  dgxm_qkv_stream s;
+  s.x = x;
+  s.w_qkv = w_qkv;
+  s.bias = bias;
+  s.norm_q_w = norm_q_w;
+  s.norm_k_w = norm_k_w;
+  s.x_row_stride = d->x_row_stride;
+  s.m = d->m;
+  s.row0 = d->row0;
+  return qkv_launch(d, 1, &s, rope, dst, stream);
+}
+
+extern "C" int dgxm_qkv_gemm_prologue_scatter_streams(const dgxm_qkv_gemm_desc* d, int32_t n_streams,
+                                                      const dgxm_qkv_stream* streams, const float* rope,
+                                                      void* const* dst, void* stream) {
+  return dgxm::qkv_launch(d, n_streams, streams, rope, dst, stream);
 }

@@ -99,6 +99,56 @@ def qkv_gemm_prologue_scatter(x: torch.Tensor, w_qkv: torch.Tensor, dst_ptrs: li
         ptr(rope), dst, stream.cuda_stream), "dgxm_qkv_gemm_prologue_scatter")
 
 
+def qkv_gemm_prologue_scatter_streams(streams: list[dict], dst_ptrs: list[list[int]], *, world: int,
+                                      rank: int, seq_local: int, seg0: int = 0,
+                                      norm_mode: int = _lib.NORM_NONE, eps: float = 1e-6,
+                                      rope: torch.Tensor | None = None, stream=None) -> None:
+    """qkv_gemm_prologue_scatter for one or two token streams in one launch
+    (dgxm_qkv_gemm_prologue_scatter_streams): a joint block's text and image
+    projections share one grid of pair tiles.  Each stream is a dict with
+    x, w_qkv, row0 and optionally bias, norm_q_w and norm_k_w, as the
+    single-stream call takes them; every head row comes out as that call
+    writes it."""
+    if not 1 <= len(streams) <= 2:
+        raise ValueError(f"{len(streams)} streams (1 or 2)")
+    if rope is not None and (rope.dtype != torch.float32 or not rope.is_contiguous()
+                             or tuple(rope.shape) != (seq_local, 64, 2)):
+        raise ValueError("rope must be a contiguous fp32 (seq_local, 64, 2) table")
+    arr = (_lib.QkvStream * len(streams))()
+    ptr = lambda t: None if t is None else t.data_ptr()
+    k = n = None
+    keep = []  # the 2-D views passed by pointer stay alive until the launch
+    for i, st in enumerate(streams):
+        x, w_qkv = st["x"], st["w_qkv"]
+        bias, nq, nk = st.get("bias"), st.get("norm_q_w"), st.get("norm_k_w")
+        _require_cuda(x, w_qkv, bias, nq, nk, rope)
+        x2 = x.reshape(-1, x.shape[-1]) if x.ndim == 3 else x
+        if x.ndim == 3 and x.shape[0] != 1:
+            raise ValueError("the fused QKV kernel takes one batch item per stream")
+        if x2.dtype != torch.bfloat16 or w_qkv.dtype != torch.bfloat16 or x2.stride(1) != 1 \
+                or not w_qkv.is_contiguous():
+            raise ValueError("x and w_qkv must be bf16 with contiguous features")
+        if k is None:
+            k, n = x2.shape[1], w_qkv.shape[0]
+        if x2.shape[1] != k or tuple(w_qkv.shape) != (n, k) or n % 384:
+            raise ValueError("the streams' inputs and Linear weights must share (3 * heads * 128, k)")
+        if bias is not None and (bias.dtype != torch.bfloat16 or bias.numel() != n or not bias.is_contiguous()):
+            raise ValueError("bias must be a contiguous bf16 vector of the Linear's outputs")
+        keep.append(x2)
+        arr[i].x, arr[i].w_qkv, arr[i].bias = x2.data_ptr(), w_qkv.data_ptr(), ptr(bias)
+        arr[i].norm_q_w, arr[i].norm_k_w = ptr(nq), ptr(nk)
+        arr[i].x_row_stride, arr[i].m, arr[i].row0 = x2.stride(0), x2.shape[0], int(st.get("row0", 0))
+    desc = _lib.QkvGemmDesc()
+    desc.world, desc.rank, desc.k = world, rank, k
+    desc.heads, desc.seq_local, desc.seg0 = n // 384, seq_local, seg0
+    desc.norm_mode, desc.eps = norm_mode, eps
+    dst = (ctypes.c_void_p * (3 * world))(*[p for row in dst_ptrs for p in row])
+    stream = stream or torch.cuda.current_stream(streams[0]["x"].device)
+    _lib.check(_lib.load().dgxm_qkv_gemm_prologue_scatter_streams(
+        ctypes.byref(desc), len(streams), arr, ptr(rope), dst, stream.cuda_stream),
+        "dgxm_qkv_gemm_prologue_scatter_streams")
+
+
 def quantize_e4m3_per_head(x: torch.Tensor, out: torch.Tensor | None = None,
                            descale: torch.Tensor | None = None, stream=None,
                            keep: torch.Tensor | None = None):

@@ -578,6 +578,37 @@ int dgxm_qkv_gemm_prologue_scatter(const dgxm_qkv_gemm_desc* desc, const void* x
                                    const void* bias, const void* norm_q_w, const void* norm_k_w,
                                    const float* rope, void* const* dst, void* stream);
 
+/*
+ * One token stream of dgxm_qkv_gemm_prologue_scatter_streams: its m rows of
+ * x (row stride x_row_stride elements, a multiple of 8) at local row row0,
+ * its Linear weight and bias, and its own per-head QKNorm weights (a joint
+ * block's text and image streams each have theirs).
+ */
+typedef struct dgxm_qkv_stream {
+  const void* x;
+  const void* w_qkv;     /* (3 * heads * 128, k) bf16 */
+  const void* bias;      /* 3 * heads * 128 bf16, or NULL */
+  const void* norm_q_w;  /* 128 bf16, or NULL */
+  const void* norm_k_w;
+  int64_t x_row_stride;
+  int32_t m;
+  int32_t row0;
+} dgxm_qkv_stream;
+
+/*
+ * dgxm_qkv_gemm_prologue_scatter for the text and image streams of a joint
+ * block (n_streams 1 or 2) in one launch: the pair tiles of both projections
+ * share one grid, so neither stream's partial last wave of tiles idles the
+ * GPU.  desc gives what the streams share (world, rank, k, heads, seq_local,
+ * seg0, norm_mode, eps); its m, row0 and x_row_stride are not read.  Each
+ * head row is computed exactly as by one dgxm_qkv_gemm_prologue_scatter call
+ * per stream.  Replaces the same reference calls (adapters/usp_full_axis.py:27-29
+ * after the blocks' QKV Linear, QKNorm and RoPE).
+ */
+int dgxm_qkv_gemm_prologue_scatter_streams(const dgxm_qkv_gemm_desc* desc, int32_t n_streams,
+                                           const dgxm_qkv_stream* streams, const float* rope,
+                                           void* const* dst, void* stream);
+
 /* ------------------------------------------------------------ CFG combine */
 /*
  * out = uncond + (cond - uncond) * cfg_scale over n contiguous elements of

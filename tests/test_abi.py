@@ -24,6 +24,7 @@ STRUCTS = {
     "PrologueDesc": "dgxm_prologue_desc",
     "SeqGatherDesc": "dgxm_seq_gather_desc",
     "QkvGemmDesc": "dgxm_qkv_gemm_desc",
+    "QkvStream": "dgxm_qkv_stream",
     "QuantItem": "dgxm_quant_item",
 }
 

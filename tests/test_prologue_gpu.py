@@ -285,3 +285,53 @@ def test_fused_qkv_gemm_prologue_matches_separate_ops(lib, hidden, heads, t_loc,
             diff = (recv[t][r].float() - want).abs().max().item()
             assert diff <= 2.0 ** -6 * want.abs().max().item() + 1e-3, f"tensor {t} rank {r}: max-abs {diff}"
     assert order.text_rows == t_loc
+
+
+@pytest.mark.parametrize("t_loc,i_loc", [(64, 700), (0, 300), (128, 256)])
+def test_grouped_streams_equal_one_call_per_stream(lib, t_loc, i_loc):
+    """dgxm_qkv_gemm_prologue_scatter_streams runs a joint block's text and
+    image projections (their own weights, biases and QKNorm weights) in one
+    launch; every receive row must hold exactly the bits one single-stream
+    call per stream writes -- the same tile arithmetic, only the grid is
+    shared.  Two ranks emulated on one GPU, joint order, an empty stream."""
+    from dgx_monarch_b200 import _lib
+    from dgx_monarch_b200.prologue import (qkv_gemm_prologue_scatter, qkv_gemm_prologue_scatter_streams,
+                                           rope_table)
+
+    world, heads, hidden, eps = 2, 8, 1024, 1e-6
+    ls = t_loc + i_loc
+    g = torch.Generator(device="cuda").manual_seed(61)
+    w = lambda *shape, s=0.02: (s * torch.randn(*shape, device="cuda", generator=g)).bfloat16()
+    n = 3 * heads * 128
+    w_t, w_i, b_t, b_i = w(n, hidden), w(n, hidden), w(n, s=0.5), w(n, s=0.5)
+    nq_t, nk_t, nq_i, nk_i = ((1 + w(128, s=0.1)).contiguous() for _ in range(4))
+    hl = heads // world
+    outs = []
+    for grouped in (False, True):
+        recv = [[torch.full((world * ls, hl, 128), float("nan"), device="cuda", dtype=torch.bfloat16)
+                 for _ in range(world)] for _ in range(3)]
+        ptrs = [[recv[t][r].data_ptr() for r in range(world)] for t in range(3)]
+        gx = torch.Generator(device="cuda").manual_seed(62)
+        for r in range(world):
+            x_t = torch.randn(t_loc, hidden, device="cuda", generator=gx).bfloat16()
+            x_i = torch.randn(i_loc, hidden, device="cuda", generator=gx).bfloat16()
+            rows = torch.arange(r * ls, (r + 1) * ls, device="cuda")
+            table = rope_table(torch.stack((rows // 100, (rows // 10) % 10, rows % 10), dim=1), [16, 56, 56])
+            common = dict(world=world, rank=r, seq_local=ls, seg0=t_loc, norm_mode=_lib.NORM_HEAD, eps=eps,
+                          rope=table)
+            streams = [dict(x=x_t, w_qkv=w_t, bias=b_t, norm_q_w=nq_t, norm_k_w=nk_t, row0=0),
+                       dict(x=x_i, w_qkv=w_i, bias=b_i, norm_q_w=nq_i, norm_k_w=nk_i, row0=t_loc)]
+            if grouped:
+                qkv_gemm_prologue_scatter_streams(streams, ptrs, **common)
+            else:
+                for st in streams:
+                    if st["x"].shape[0]:
+                        qkv_gemm_prologue_scatter(st["x"], st["w_qkv"], ptrs, row0=st["row0"], bias=st["bias"],
+                                                  norm_q_w=st["norm_q_w"], norm_k_w=st["norm_k_w"], **common)
+        torch.cuda.synchronize()
+        assert _lib.device_error() == 0
+        outs.append(recv)
+    for t in range(3):
+        for r in range(world):
+            assert not torch.isnan(outs[1][t][r].float()).any(), f"tensor {t} rank {r}: rows left unwritten"
+            assert torch.equal(outs[0][t][r], outs[1][t][r]), f"tensor {t} rank {r}"
